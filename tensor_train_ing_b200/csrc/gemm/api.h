@@ -1,0 +1,31 @@
+// C++ entry points of the GEMM family (no torch types; the bindings translate tensors).
+#pragma once
+
+#include <cuda_runtime.h>
+#include <cstdint>
+
+namespace ttb {
+
+// One bf16 matrix operand in global memory.
+//  A operand (M x K):  mn_major=false -> stored [M][K] with row stride ld;  true -> stored [K][M].
+//  B operand (N x K):  mn_major=false -> stored [N][K];                     true -> stored [K][N].
+struct Operand {
+  const void* ptr;
+  long long ld;
+  bool mn_major;
+};
+
+// D[M,N] = alpha * (A B^T + bias) + beta * C
+void gemm_linear(const Operand& a, const Operand& b, int M, int N, int K, void* D, long long ldd, bool d_f32,
+                 const void* C, long long ldc, bool c_f32, float alpha, float beta, const float* bias,
+                 cudaStream_t stream);
+
+// l = x Wl^T (+bl), r = x Wr^T (+br), H = l*r (mode 0) or silu(l)*r (mode 1); all [M, N] bf16 with row stride ld.
+void gemm_bilinear(const Operand& x, const Operand& wl, const Operand& wr, int M, int N, int K, void* H, void* Lo,
+                   void* Ro, long long ld, const float* bias_l, const float* bias_r, int mode, cudaStream_t stream);
+
+// dH = dY Wd (B operand = Wd^T view), fused with the bilinear backward: writes dl, dr [M, N] bf16.
+void gemm_bilinear_grad(const Operand& dy, const Operand& wd, int M, int N, int K, const void* Lin, const void* Rin,
+                        void* dL, void* dR, long long ld, int mode, cudaStream_t stream);
+
+}  // namespace ttb

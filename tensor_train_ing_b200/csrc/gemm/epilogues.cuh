@@ -1,0 +1,232 @@
+// Epilogue functors for the sm_100a GEMM.  Each thread owns one accumulator row (TMEM lane)
+// and walks the tile's columns 32 at a time with tcgen05.ld.
+#pragma once
+
+#include "gemm_sm100.cuh"
+
+namespace ttb {
+namespace gemm {
+
+__device__ __forceinline__ void load_row32_bf16(const __nv_bfloat16* p, bool full, int n_valid, float (&v)[32]) {
+  if (full) {
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      uint4 u = *reinterpret_cast<const uint4*>(p + q * 8);
+      const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        v[q * 8 + 2 * j] = bf16_lo(w[j]);
+        v[q * 8 + 2 * j + 1] = bf16_hi(w[j]);
+      }
+    }
+  } else {
+#pragma unroll
+    for (int j = 0; j < 32; ++j) v[j] = j < n_valid ? __bfloat162float(p[j]) : 0.f;
+  }
+}
+
+__device__ __forceinline__ void load_row32_f32(const float* p, bool full, int n_valid, float (&v)[32]) {
+  if (full) {
+#pragma unroll
+    for (int q = 0; q < 8; ++q) {
+      float4 u = *reinterpret_cast<const float4*>(p + q * 4);
+      v[q * 4 + 0] = u.x;
+      v[q * 4 + 1] = u.y;
+      v[q * 4 + 2] = u.z;
+      v[q * 4 + 3] = u.w;
+    }
+  } else {
+#pragma unroll
+    for (int j = 0; j < 32; ++j) v[j] = j < n_valid ? p[j] : 0.f;
+  }
+}
+
+__device__ __forceinline__ void store_row32_bf16(__nv_bfloat16* p, bool full, int n_valid, const float (&v)[32]) {
+  if (full) {
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      uint4 u;
+      u.x = pack_bf16(v[q * 8 + 0], v[q * 8 + 1]);
+      u.y = pack_bf16(v[q * 8 + 2], v[q * 8 + 3]);
+      u.z = pack_bf16(v[q * 8 + 4], v[q * 8 + 5]);
+      u.w = pack_bf16(v[q * 8 + 6], v[q * 8 + 7]);
+      *reinterpret_cast<uint4*>(p + q * 8) = u;
+    }
+  } else {
+#pragma unroll
+    for (int j = 0; j < 32; ++j)
+      if (j < n_valid) p[j] = __float2bfloat16_rn(v[j]);
+  }
+}
+
+__device__ __forceinline__ void store_row32_f32(float* p, bool full, int n_valid, const float (&v)[32]) {
+  if (full) {
+#pragma unroll
+    for (int q = 0; q < 8; ++q)
+      *reinterpret_cast<float4*>(p + q * 4) = make_float4(v[q * 4], v[q * 4 + 1], v[q * 4 + 2], v[q * 4 + 3]);
+  } else {
+#pragma unroll
+    for (int j = 0; j < 32; ++j)
+      if (j < n_valid) p[j] = v[j];
+  }
+}
+
+// D = alpha * acc + beta * C   (C optional, may alias D; D and C bf16 or fp32).
+// Optionally also adds a per-column bias (fp32) before scaling by alpha.
+template <int NB>
+struct EpiLinear {
+  void* D;
+  long long ldd;
+  int d_f32;
+  const void* C;
+  long long ldc;
+  int c_f32;
+  float alpha, beta;
+  const float* bias;
+  int M, N;
+
+  __device__ __forceinline__ void operator()(uint32_t taddr, int row, int n0, int, int) const {
+#pragma unroll 1
+    for (int c = 0; c < NB / 32; ++c) {
+      uint32_t r[32];
+      tmem_ld32(taddr + c * 32, r);
+      tmem_ld_wait();
+      const int col0 = n0 + c * 32;
+      if (row >= M || col0 >= N) continue;
+      const int nv = min(32, N - col0);
+      const bool full = nv == 32;
+      const bool d_vec = full && (d_f32 ? (ldd % 4 == 0) : (ldd % 8 == 0)) &&
+                         (reinterpret_cast<uintptr_t>(D) & 15) == 0;
+      const bool c_vec = full && (c_f32 ? (ldc % 4 == 0) : (ldc % 8 == 0)) &&
+                         (reinterpret_cast<uintptr_t>(C) & 15) == 0;
+      float v[32];
+#pragma unroll
+      for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
+      if (bias != nullptr) {
+#pragma unroll
+        for (int j = 0; j < 32; ++j) v[j] += (j < nv) ? bias[col0 + j] : 0.f;
+      }
+#pragma unroll
+      for (int j = 0; j < 32; ++j) v[j] *= alpha;
+      if (C != nullptr && beta != 0.f) {
+        float cv[32];
+        if (c_f32)
+          load_row32_f32(static_cast<const float*>(C) + row * ldc + col0, c_vec, nv, cv);
+        else
+          load_row32_bf16(static_cast<const __nv_bfloat16*>(C) + row * ldc + col0, c_vec, nv, cv);
+#pragma unroll
+        for (int j = 0; j < 32; ++j) v[j] += beta * cv[j];
+      }
+      if (d_f32)
+        store_row32_f32(static_cast<float*>(D) + row * ldd + col0, d_vec, nv, v);
+      else
+        store_row32_bf16(static_cast<__nv_bfloat16*>(D) + row * ldd + col0, d_vec, nv, v);
+    }
+  }
+};
+
+// Bilinear / gated MLP hidden layer from a DUAL GEMM:
+//   l = acc1 (+bl), r = acc2 (+br);  H = l * r  (mode 0)  or  silu(l) * r  (mode 1)
+// H is written in bf16; l and r are also written (bf16) when pointers are given, for backward.
+template <int NB>
+struct EpiBilinear {
+  __nv_bfloat16* H;
+  __nv_bfloat16* Lo;
+  __nv_bfloat16* Ro;
+  long long ld;
+  const float* bias_l;
+  const float* bias_r;
+  int mode;
+  int M, N;
+
+  __device__ __forceinline__ void operator()(uint32_t taddr, int row, int n0, int, int) const {
+#pragma unroll 1
+    for (int c = 0; c < NB / 32; ++c) {
+      uint32_t a[32], b[32];
+      tmem_ld32(taddr + c * 32, a);
+      tmem_ld32(taddr + NB + c * 32, b);
+      tmem_ld_wait();
+      const int col0 = n0 + c * 32;
+      if (row >= M || col0 >= N) continue;
+      const int nv = min(32, N - col0);
+      const bool full = nv == 32 && (ld % 8 == 0);
+      float l[32], r[32], h[32];
+#pragma unroll
+      for (int j = 0; j < 32; ++j) {
+        l[j] = __uint_as_float(a[j]);
+        r[j] = __uint_as_float(b[j]);
+      }
+      if (bias_l != nullptr) {
+#pragma unroll
+        for (int j = 0; j < 32; ++j) {
+          l[j] += (j < nv) ? bias_l[col0 + j] : 0.f;
+          r[j] += (j < nv) ? bias_r[col0 + j] : 0.f;
+        }
+      }
+      // The reference rounds l and r to bf16 before multiplying; do the same so that the
+      // saved factors and the product agree exactly with what backward sees.
+#pragma unroll
+      for (int j = 0; j < 32; ++j) {
+        l[j] = __bfloat162float(__float2bfloat16_rn(l[j]));
+        r[j] = __bfloat162float(__float2bfloat16_rn(r[j]));
+        const float g = mode == 1 ? l[j] / (1.f + __expf(-l[j])) : l[j];
+        h[j] = g * r[j];
+      }
+      const long long off = row * ld + col0;
+      store_row32_bf16(H + off, full, nv, h);
+      if (Lo != nullptr) store_row32_bf16(Lo + off, full, nv, l);
+      if (Ro != nullptr) store_row32_bf16(Ro + off, full, nv, r);
+    }
+  }
+};
+
+// Backward of the bilinear hidden layer, fused into dH = dY @ D:
+//   dl = dH * r            dr = dH * l          (mode 0)
+//   dl = dH * r * silu'(l) dr = dH * silu(l)    (mode 1)
+// l, r are the bf16 factors saved by the forward; dl/dr written bf16.
+template <int NB>
+struct EpiBilinearGrad {
+  const __nv_bfloat16* Lin;
+  const __nv_bfloat16* Rin;
+  __nv_bfloat16* dL;
+  __nv_bfloat16* dR;
+  long long ld;
+  int mode;
+  int M, N;
+
+  __device__ __forceinline__ void operator()(uint32_t taddr, int row, int n0, int, int) const {
+#pragma unroll 1
+    for (int c = 0; c < NB / 32; ++c) {
+      uint32_t a[32];
+      tmem_ld32(taddr + c * 32, a);
+      tmem_ld_wait();
+      const int col0 = n0 + c * 32;
+      if (row >= M || col0 >= N) continue;
+      const int nv = min(32, N - col0);
+      const bool full = nv == 32 && (ld % 8 == 0);
+      const long long off = row * ld + col0;
+      float l[32], r[32], dl[32], dr[32];
+      load_row32_bf16(Lin + off, full, nv, l);
+      load_row32_bf16(Rin + off, full, nv, r);
+#pragma unroll
+      for (int j = 0; j < 32; ++j) {
+        // the reference's autograd sees dH rounded to bf16 (output grad of a bf16 product)
+        const float dh = __bfloat162float(__float2bfloat16_rn(__uint_as_float(a[j])));
+        if (mode == 1) {
+          const float sg = 1.f / (1.f + __expf(-l[j]));
+          const float silu = l[j] * sg;
+          dr[j] = dh * silu;
+          dl[j] = dh * r[j] * (sg * (1.f + l[j] * (1.f - sg)));
+        } else {
+          dl[j] = dh * r[j];
+          dr[j] = dh * l[j];
+        }
+      }
+      store_row32_bf16(dL + off, full, nv, dl);
+      store_row32_bf16(dR + off, full, nv, dr);
+    }
+  }
+};
+
+}  // namespace gemm
+}  // namespace ttb

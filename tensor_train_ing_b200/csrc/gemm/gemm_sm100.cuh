@@ -1,0 +1,251 @@
+// Persistent, warp-specialised bf16 GEMM for sm_100a on the 5th-generation tensor cores.
+//
+//   D[M, N] = epilogue( sum_k A[m, k] * B[n, k] )
+//
+// Roles (192 threads = 6 warps, one CTA per SM, grid = #SMs):
+//   warp 0     : TMA producer (one elected lane) filling a STAGES-deep shared-memory ring
+//   warp 1     : tcgen05.mma issuer (one elected lane); also owns the TMEM allocation
+//   warps 2..5 : epilogue; drain an fp32 accumulator from TMEM (tcgen05.ld) and apply the functor
+// Two TMEM accumulators (2 x BN columns) let the epilogue of tile i overlap the mainloop of
+// tile i+1.  Operands may be K-major or MN-major in global memory; both are staged with TMA
+// into 128-byte-swizzled shared memory and described to the tensor core with UMMA descriptors.
+// DUAL=true runs two B operands against the same A tile (two accumulators of BN/2 columns),
+// which the bilinear MLP uses to form (x L^T) and (x R^T) from one read of x.
+//
+// The epilogue is a functor with
+//   __device__ void operator()(uint32_t taddr, int row, int n0, int tile_m, int tile_n) const
+// where taddr addresses this thread's TMEM lane at column 0 of the tile's accumulator.
+#pragma once
+
+#include "../common/sm100.cuh"
+
+namespace ttb {
+namespace gemm {
+
+constexpr int BM = 128;
+constexpr int BK = 64;            // one 128-byte swizzle row of bf16
+constexpr int kThreads = 192;
+constexpr int kGroupM = 8;        // tile raster: groups of kGroupM row-tiles sweep all column-tiles
+
+struct Shape {
+  int M, N, K;
+  uint32_t* status;  // device error word (bounded-wait timeouts)
+};
+
+template <int BN, int STAGES, bool DUAL>
+struct Layout {
+  static constexpr int kBNMma = DUAL ? BN / 2 : BN;            // N of each UMMA
+  static constexpr int kABytes = BM * BK * 2;
+  static constexpr int kBBytes = kBNMma * BK * 2;              // per B operand
+  static constexpr int kStageBytes = kABytes + (DUAL ? 2 : 1) * kBBytes;
+  static constexpr int kAccCols = BN;                          // per accumulator buffer
+  static constexpr int kTmemCols = 2 * BN;                     // double buffered
+  static constexpr int kBarOffset = STAGES * kStageBytes;
+  // full[STAGES], empty[STAGES], tfull[2], tempty[2], mma_done, tmem holder
+  static constexpr int kSmemBytes = kBarOffset + (2 * STAGES + 5) * 8 + 16 + 1024;  // +1024 alignment slack
+};
+
+__device__ __forceinline__ void tile_coords(int tile, int m_tiles, int n_tiles, int& tm, int& tn) {
+  const int per_group = kGroupM * n_tiles;
+  const int group = tile / per_group;
+  const int first_m = group * kGroupM;
+  const int gsize = min(m_tiles - first_m, kGroupM);
+  const int in_group = tile - group * per_group;
+  tm = first_m + in_group % gsize;
+  tn = in_group / gsize;
+}
+
+template <int BN, int STAGES, bool A_MN, bool B_MN, bool DUAL, class Epi>
+__global__ void __launch_bounds__(kThreads, 1)
+    gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                const __grid_constant__ CUtensorMap tmB2, Shape s, Epi epi) {
+  using L = Layout<BN, STAGES, DUAL>;
+  constexpr int NB = L::kBNMma;
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + L::kBarOffset);
+  uint64_t* empty = full + STAGES;
+  uint64_t* tfull = empty + STAGES;
+  uint64_t* tempty = tfull + 2;
+  uint64_t* mma_done = tempty + 2;
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(mma_done + 1);
+
+  const int warp = threadIdx.x / 32;
+  const int lane = threadIdx.x % 32;
+  const int m_tiles = (s.M + BM - 1) / BM;
+  const int n_tiles = (s.N + NB - 1) / NB;  // output columns per tile: NB (BN/2 when DUAL)
+  const int num_tiles = m_tiles * n_tiles;
+  const int k_blocks = (s.K + BK - 1) / BK;
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < STAGES; ++i) {
+      mbar_init(&full[i], 1);
+      mbar_init(&empty[i], 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&tfull[i], 1);
+      mbar_init(&tempty[i], 128);
+    }
+    mbar_init(mma_done, 1);
+    fence_mbar_init();
+  }
+  if (warp == 0 && lane == 0) {
+    prefetch_tmap(&tmA);
+    prefetch_tmap(&tmB);
+    if (DUAL) prefetch_tmap(&tmB2);
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_holder, L::kTmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_holder;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------------ TMA producer
+    if (elect_one()) {
+      int stage = 0;
+      uint32_t phase = 0;
+      uint32_t issued = 0, issued_parity = 0;  // per stage: a load was issued / parity of its phase
+      bool ok = true;
+      for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
+        int tm, tn;
+        tile_coords(tile, m_tiles, n_tiles, tm, tn);
+        const int m0 = tm * BM;
+        const int n0 = tn * NB;
+        for (int kb = 0; kb < k_blocks; ++kb) {
+          if (!mbar_wait(&empty[stage], phase ^ 1, s.status, kErrTimeoutProducer)) {
+            ok = false;
+            break;
+          }
+          uint8_t* sa = smem + stage * L::kStageBytes;
+          uint8_t* sb = sa + L::kABytes;
+          mbar_arrive_expect_tx(&full[stage], L::kStageBytes);
+          issued |= 1u << stage;
+          issued_parity = (issued_parity & ~(1u << stage)) | (phase << stage);
+          const int k0 = kb * BK;
+          if (A_MN) {
+#pragma unroll
+            for (int i = 0; i < BM / 64; ++i) tma_load_2d(sa + i * 64 * BK * 2, &tmA, &full[stage], m0 + 64 * i, k0);
+          } else {
+            tma_load_2d(sa, &tmA, &full[stage], k0, m0);
+          }
+          if (B_MN) {
+#pragma unroll
+            for (int i = 0; i < NB / 64; ++i) tma_load_2d(sb + i * 64 * BK * 2, &tmB, &full[stage], n0 + 64 * i, k0);
+            if (DUAL) {
+#pragma unroll
+              for (int i = 0; i < NB / 64; ++i)
+                tma_load_2d(sb + L::kBBytes + i * 64 * BK * 2, &tmB2, &full[stage], n0 + 64 * i, k0);
+            }
+          } else {
+            if (DUAL) {
+              tma_load_2d(sb, &tmB, &full[stage], k0, n0);
+              tma_load_2d(sb + L::kBBytes, &tmB2, &full[stage], k0, n0);
+            } else {
+              tma_load_2d(sb, &tmB, &full[stage], k0, n0);
+            }
+          }
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+      }
+      if (!ok) {
+        // Let copies that may still be in flight land before the CTA exits (bounded waits).
+        for (int i = 0; i < STAGES; ++i)
+          if (issued & (1u << i)) mbar_wait(&full[i], (issued_parity >> i) & 1u, s.status, kErrTimeoutProducer);
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------------ MMA issuer
+    if (elect_one()) {
+      constexpr uint32_t idesc = idesc_bf16_f32(BM, NB, A_MN ? 1 : 0, B_MN ? 1 : 0);
+      int stage = 0;
+      uint32_t phase = 0;
+      int acc = 0;
+      uint32_t acc_phase = 0;
+      bool ok = true;
+      for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
+        if (!mbar_wait(&tempty[acc], acc_phase ^ 1, s.status, kErrTimeoutMma)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + acc * L::kAccCols;
+        for (int kb = 0; kb < k_blocks; ++kb) {
+          if (!mbar_wait(&full[stage], phase, s.status, kErrTimeoutMma)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t sa = smem_u32(smem + stage * L::kStageBytes);
+          const uint32_t sb = sa + L::kABytes;
+#pragma unroll
+          for (int k = 0; k < BK / 16; ++k) {
+            // K-major: advance 16 elements = 32 bytes inside the swizzled row.
+            // MN-major: advance 16 K-rows = 2048 bytes; MN atoms are 64*BK*2 bytes apart.
+            const uint64_t adesc = A_MN ? smem_desc(sa + k * 2048, 64 * BK * 2, 1024) : smem_desc(sa + k * 32, 16, 1024);
+            const uint64_t bdesc = B_MN ? smem_desc(sb + k * 2048, 64 * BK * 2, 1024) : smem_desc(sb + k * 32, 16, 1024);
+            const uint32_t accumulate = (kb > 0 || k > 0) ? 1u : 0u;
+            umma_ss(d_tmem, adesc, bdesc, idesc, accumulate);
+            if (DUAL) {
+              const uint32_t sb2 = sb + L::kBBytes;
+              const uint64_t bdesc2 =
+                  B_MN ? smem_desc(sb2 + k * 2048, 64 * BK * 2, 1024) : smem_desc(sb2 + k * 32, 16, 1024);
+              umma_ss(d_tmem + NB, adesc, bdesc2, idesc, accumulate);
+            }
+          }
+          umma_commit(&empty[stage]);
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+        if (!ok) break;
+        umma_commit(&tfull[acc]);
+        if (++acc == 2) {
+          acc = 0;
+          acc_phase ^= 1;
+        }
+      }
+      // No tcgen05.mma may still be writing TMEM when it is released.
+      umma_commit(mma_done);
+      mbar_wait(mma_done, 0, s.status, kErrTimeoutMma);
+    }
+  } else {
+    // ------------------------------------------------------------------ epilogue (warps 2..5)
+    const int sub = warp & 3;  // TMEM sub-partition this warp may access
+    int acc = 0;
+    uint32_t acc_phase = 0;
+    for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x) {
+      int tm, tn;
+      tile_coords(tile, m_tiles, n_tiles, tm, tn);
+      if (!mbar_wait(&tfull[acc], acc_phase, s.status, kErrTimeoutEpilogue)) break;
+      tc_fence_after();
+      const uint32_t taddr = tmem_base + (static_cast<uint32_t>(sub * 32) << 16) + acc * L::kAccCols;
+      const int row = tm * BM + sub * 32 + lane;
+      epi(taddr, row, tn * NB, tm, tn);
+      tc_fence_before();
+      mbar_arrive(&tempty[acc]);
+      if (++acc == 2) {
+        acc = 0;
+        acc_phase ^= 1;
+      }
+    }
+  }
+
+  __syncwarp();  // reconverge the producer / issuer warps (only one lane of each looped)
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, L::kTmemCols);
+  }
+}
+
+}  // namespace gemm
+}  // namespace ttb
