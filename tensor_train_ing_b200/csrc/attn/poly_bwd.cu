@@ -1,0 +1,650 @@
+// Polynomial attention backward on the tcgen05 tensor cores: two deterministic kernels.
+//
+//   dP = dO V^T,  H = C * dP  (C = visible * row_scale)
+//   signed_product:   dS1 = H * S2,             dS2 = H * S1
+//   offset_square:    dS1 = 2 H (S1 + b)                          db  = sum dS1
+//   lower_degree_mix: dS1 = H (c1 + c12 S2),    dS2 = H (c2 + c12 S1)
+//                     dc0 = sum H, dc1 = sum H S1, dc2 = sum H S2, dc12 = sum H S1 S2
+//   dQ = sm * dS K,   dK = sm * dS^T Q,   dV = P^T dO   with P = C * A(S1, S2)
+//
+// dq kernel  (one CTA per 128 queries): S1, S2, dP tiles of 64 keys in TMEM, dS written to
+//            swizzled SMEM as the A operand of dQ1 += dS1 K1 and dQ2 += dS2 K2 (TMEM accumulators).
+// dkv kernel (one CTA per 128 keys): the transposed scores S1^T, S2^T, dP^T of 32 queries in TMEM,
+//            P^T and dS^T written to 64B-swizzled SMEM, accumulating dV, dK1, dK2 in TMEM (480 of
+//            the 512 columns at head dim 128).  Learned kind parameters get per-key-block partial
+//            sums reduced later in a fixed order.  Reference: tnlm/kernels/poly_attn.py:78-202.
+#include "../common/host.h"
+#include "attn_api.h"
+#include "poly_common.cuh"
+
+namespace ttb {
+namespace attn {
+
+constexpr int kBwdThreads = 192;
+
+// ============================================================================ dQ kernel
+constexpr int DQ_BM = 128;  // queries per CTA
+constexpr int DQ_BN = 64;   // keys per block
+
+template <int DK, int DV>
+struct DqSmem {
+  static constexpr int kQ = DK / 64 * DQ_BM * 128;
+  static constexpr int kDO = DV / 64 * DQ_BM * 128;
+  static constexpr int kK = DK / 64 * DQ_BN * 128;
+  static constexpr int kV = DV / 64 * DQ_BN * 128;
+  static constexpr int kStage = 2 * kK + kV;
+  static constexpr int kDS = DQ_BM * 128;  // 128 rows x 64 keys bf16
+  static constexpr int kOffQ1 = 0, kOffQ2 = kQ, kOffDO = 2 * kQ;
+  static constexpr int kOffStage = 2 * kQ + kDO;
+  static constexpr int kOffDS = kOffStage + 2 * kStage;
+  static constexpr int kOffBar = kOffDS + 2 * kDS;
+  static constexpr int kBytes = (kOffBar + 256 + 1024) > 120 * 1024 ? (kOffBar + 256 + 1024) : 120 * 1024;
+};
+
+template <int DK, int DV, int KIND>
+__global__ void __launch_bounds__(kBwdThreads, 1)
+    poly_bwd_dq_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmKV,
+                       const __grid_constant__ CUtensorMap tmDO, Params p) {
+  using S = DqSmem<DK, DV>;
+  constexpr bool kTwo = KIND != 1;
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* bar = reinterpret_cast<uint64_t*>(smem + S::kOffBar);
+  uint64_t* q_full = bar + 0;
+  uint64_t* kv_full = bar + 1;   // [2]
+  uint64_t* kv_empty = bar + 3;  // [2]
+  uint64_t* sc_full = bar + 5;
+  uint64_t* sc_empty = bar + 6;
+  uint64_t* ds_full = bar + 7;
+  uint64_t* ds_empty = bar + 8;
+  uint64_t* acc_full = bar + 9;
+  uint64_t* mma_done = bar + 10;
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(bar + 12);
+
+  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+  const int nqb = (p.T + DQ_BM - 1) / DQ_BM;
+  const int qb = nqb - 1 - static_cast<int>(blockIdx.x);
+  const int bh = blockIdx.y;
+  const int b = bh / p.H, h = bh % p.H;
+  const int q0 = qb * DQ_BM;
+  const long long row0 = static_cast<long long>(b) * p.T;
+  const int lo = q0 - p.pos[row0 + q0];
+  const int kstart = (lo / DQ_BN) * DQ_BN;
+  const int kend = min(q0 + DQ_BM, p.T);
+  const int nkb = (kend - kstart + DQ_BN - 1) / DQ_BN;
+
+  if (threadIdx.x == 0) {
+    mbar_init(q_full, 1);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&kv_full[i], 1);
+      mbar_init(&kv_empty[i], 1);
+    }
+    mbar_init(sc_full, 1);
+    mbar_init(sc_empty, 128);
+    mbar_init(ds_full, 128);
+    mbar_init(ds_empty, 1);
+    mbar_init(acc_full, 1);
+    mbar_init(mma_done, 1);
+    fence_mbar_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_holder, 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_holder;
+  const uint32_t tS1 = tmem, tS2 = tmem + 64, tDP = tmem + 128, tDQ1 = tmem + 256, tDQ2 = tmem + 256 + DK;
+
+  if (warp == 0) {
+    if (elect_one()) {
+      prefetch_tmap(&tmQ);
+      prefetch_tmap(&tmKV);
+      prefetch_tmap(&tmDO);
+      const int qrow = static_cast<int>(row0 + q0);
+      mbar_arrive_expect_tx(q_full, (kTwo ? 2 : 1) * S::kQ + S::kDO);
+      for (int i = 0; i < DK / 64; ++i) {
+        tma_load_2d(smem + S::kOffQ1 + i * DQ_BM * 128, &tmQ, q_full, p.cq1 + h * DK + 64 * i, qrow);
+        if (kTwo) tma_load_2d(smem + S::kOffQ2 + i * DQ_BM * 128, &tmQ, q_full, p.cq2 + h * DK + 64 * i, qrow);
+      }
+      for (int i = 0; i < DV / 64; ++i)
+        tma_load_2d(smem + S::kOffDO + i * DQ_BM * 128, &tmDO, q_full, h * DV + 64 * i, qrow);
+      bool ok = true;
+      for (int j = 0; j < nkb && ok; ++j) {
+        const int st = j & 1;
+        if (!mbar_wait(&kv_empty[st], ((j >> 1) & 1) ^ 1, p.status, kErrTimeoutProducer)) {
+          ok = false;
+          break;
+        }
+        uint8_t* sk = smem + S::kOffStage + st * S::kStage;
+        const int krow = static_cast<int>(row0 + kstart + j * DQ_BN);
+        mbar_arrive_expect_tx(&kv_full[st], (kTwo ? 2 : 1) * S::kK + S::kV);
+        for (int i = 0; i < DK / 64; ++i) {
+          tma_load_2d(sk + i * DQ_BN * 128, &tmKV, &kv_full[st], p.ck1 + h * DK + 64 * i, krow);
+          if (kTwo) tma_load_2d(sk + S::kK + i * DQ_BN * 128, &tmKV, &kv_full[st], p.ck2 + h * DK + 64 * i, krow);
+        }
+        for (int i = 0; i < DV / 64; ++i)
+          tma_load_2d(sk + 2 * S::kK + i * DQ_BN * 128, &tmKV, &kv_full[st], p.cv + h * DV + 64 * i, krow);
+      }
+      mbar_wait(q_full, 0, p.status, kErrTimeoutProducer);
+      if (!ok)
+        for (int j = max(0, nkb - 2); j < nkb; ++j) mbar_wait(&kv_full[j & 1], (j >> 1) & 1, p.status, kErrTimeoutProducer);
+    }
+  } else if (warp == 1) {
+    if (elect_one()) {
+      constexpr uint32_t idS = idesc_bf16_f32(128, DQ_BN, 0, 0);
+      constexpr uint32_t idAcc = idesc_bf16_f32(128, DK, 0, 1);
+      const uint32_t sQ1 = smem_u32(smem + S::kOffQ1), sQ2 = smem_u32(smem + S::kOffQ2);
+      const uint32_t sDO = smem_u32(smem + S::kOffDO);
+      const uint32_t sDS1 = smem_u32(smem + S::kOffDS), sDS2 = sDS1 + S::kDS;
+      bool ok = mbar_wait(q_full, 0, p.status, kErrTimeoutMma);
+      auto accumulate = [&](int i) -> bool {
+        if (!mbar_wait(ds_full, i & 1, p.status, kErrTimeoutMma)) return false;
+        tc_fence_after();
+        const uint32_t sK1 = smem_u32(smem + S::kOffStage + (i & 1) * S::kStage);
+        const uint32_t sK2 = sK1 + S::kK;
+#pragma unroll
+        for (int k = 0; k < DQ_BN / 16; ++k) {
+          const uint32_t acc = (i > 0 || k > 0) ? 1u : 0u;
+          umma_ss(tDQ1, kmajor_desc(sDS1, DQ_BM, k), mnmajor_desc(sK1, DQ_BN, k), idAcc, acc);
+          if (kTwo) umma_ss(tDQ2, kmajor_desc(sDS2, DQ_BM, k), mnmajor_desc(sK2, DQ_BN, k), idAcc, acc);
+        }
+        umma_commit(ds_empty);
+        umma_commit(&kv_empty[i & 1]);
+        return true;
+      };
+      for (int j = 0; j < nkb && ok; ++j) {
+        const int st = j & 1;
+        if (!mbar_wait(&kv_full[st], (j >> 1) & 1, p.status, kErrTimeoutMma)) { ok = false; break; }
+        if (!mbar_wait(sc_empty, (j & 1) ^ 1, p.status, kErrTimeoutMma)) { ok = false; break; }
+        tc_fence_after();
+        const uint32_t sK1 = smem_u32(smem + S::kOffStage + st * S::kStage);
+        const uint32_t sK2 = sK1 + S::kK;
+        const uint32_t sV = sK1 + 2 * S::kK;
+#pragma unroll
+        for (int k = 0; k < DK / 16; ++k) {
+          umma_ss(tS1, kmajor_desc(sQ1, DQ_BM, k), kmajor_desc(sK1, DQ_BN, k), idS, k > 0 ? 1u : 0u);
+          if (kTwo) umma_ss(tS2, kmajor_desc(sQ2, DQ_BM, k), kmajor_desc(sK2, DQ_BN, k), idS, k > 0 ? 1u : 0u);
+        }
+#pragma unroll
+        for (int k = 0; k < DV / 16; ++k)
+          umma_ss(tDP, kmajor_desc(sDO, DQ_BM, k), kmajor_desc(sV, DQ_BN, k), idS, k > 0 ? 1u : 0u);
+        umma_commit(sc_full);
+        if (j > 0 && !accumulate(j - 1)) { ok = false; break; }
+      }
+      if (ok && accumulate(nkb - 1)) umma_commit(acc_full);
+      umma_commit(mma_done);
+      mbar_wait(mma_done, 0, p.status, kErrTimeoutMma);
+    }
+  } else {
+    const int sub = warp & 3;
+    const int r = sub * 32 + lane;
+    const int t = q0 + r;
+    const bool valid = t < p.T;
+    const long long grow = row0 + (valid ? t : q0);
+    const int dq = valid ? p.doc[grow] : -1;
+    const int dstart = valid ? t - p.pos[grow] : 0;
+    const float rs = valid ? p.row_scale[grow] : 0.f;
+    float c[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) c[i] = p.par[h * 4 + i];
+    const uint32_t lane_off = static_cast<uint32_t>(sub * 32) << 16;
+    bool ok = true;
+    for (int j = 0; j < nkb && ok; ++j) {
+      if (!mbar_wait(sc_full, j & 1, p.status, kErrTimeoutEpilogue)) { ok = false; break; }
+      tc_fence_after();
+      uint32_t d1[32], d2[32];  // 64 bf16 each: rows of dS1 / dS2
+      const int kb0 = kstart + j * DQ_BN;
+#pragma unroll
+      for (int cc = 0; cc < DQ_BN / 32; ++cc) {
+        uint32_t a[32], bb[32], g[32];
+        tmem_ld32(tS1 + lane_off + cc * 32, a);
+        if (kTwo) tmem_ld32(tS2 + lane_off + cc * 32, bb);
+        tmem_ld32(tDP + lane_off + cc * 32, g);
+        tmem_ld_wait();
+#pragma unroll
+        for (int jj = 0; jj < 32; jj += 2) {
+          float o1[2], o2[2];
+#pragma unroll
+          for (int e = 0; e < 2; ++e) {
+            const int kt = kb0 + cc * 32 + jj + e;
+            const bool vis = valid && dq >= 0 && kt <= t && kt >= dstart;
+            const float s1 = __uint_as_float(a[jj + e]) * p.sm;
+            const float s2 = kTwo ? __uint_as_float(bb[jj + e]) * p.sm : s1;
+            const float hh = vis ? __uint_as_float(g[jj + e]) * rs : 0.f;
+            if (KIND == 0) {
+              o1[e] = hh * s2;
+              o2[e] = hh * s1;
+            } else if (KIND == 1) {
+              o1[e] = 2.f * hh * (s1 + c[0]);
+              o2[e] = 0.f;
+            } else {
+              o1[e] = hh * (c[1] + c[3] * s2);
+              o2[e] = hh * (c[2] + c[3] * s1);
+            }
+          }
+          d1[cc * 16 + jj / 2] = pack_bf16(o1[0], o1[1]);
+          d2[cc * 16 + jj / 2] = pack_bf16(o2[0], o2[1]);
+        }
+      }
+      tc_fence_before();
+      mbar_arrive(sc_empty);
+      if (!mbar_wait(ds_empty, (j & 1) ^ 1, p.status, kErrTimeoutEpilogue)) { ok = false; break; }
+      uint8_t* row1 = smem + S::kOffDS;
+      uint8_t* row2 = row1 + S::kDS;
+#pragma unroll
+      for (int ch = 0; ch < 8; ++ch) {
+        *reinterpret_cast<uint4*>(row1 + sw128_offset(r, ch)) =
+            make_uint4(d1[ch * 4], d1[ch * 4 + 1], d1[ch * 4 + 2], d1[ch * 4 + 3]);
+        if (kTwo)
+          *reinterpret_cast<uint4*>(row2 + sw128_offset(r, ch)) =
+              make_uint4(d2[ch * 4], d2[ch * 4 + 1], d2[ch * 4 + 2], d2[ch * 4 + 3]);
+      }
+      fence_proxy_async_smem();
+      mbar_arrive(ds_full);
+    }
+    if (ok && mbar_wait(acc_full, 0, p.status, kErrTimeoutEpilogue)) {
+      tc_fence_after();
+#pragma unroll 1
+      for (int which = 0; which < (kTwo ? 2 : 1); ++which) {
+        const uint32_t tacc = (which == 0 ? tDQ1 : tDQ2) + lane_off;
+        const int col = (which == 0 ? p.cq1 : p.cq2) + h * DK;
+#pragma unroll 1
+        for (int cc = 0; cc < DK / 32; ++cc) {
+          uint32_t a[32];
+          tmem_ld32(tacc + cc * 32, a);
+          tmem_ld_wait();
+          if (valid) {
+            __nv_bfloat16* dst = p.dq + grow * p.ldd + col + cc * 32;
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+              uint4 u;
+              u.x = pack_bf16(__uint_as_float(a[q * 8 + 0]) * p.sm, __uint_as_float(a[q * 8 + 1]) * p.sm);
+              u.y = pack_bf16(__uint_as_float(a[q * 8 + 2]) * p.sm, __uint_as_float(a[q * 8 + 3]) * p.sm);
+              u.z = pack_bf16(__uint_as_float(a[q * 8 + 4]) * p.sm, __uint_as_float(a[q * 8 + 5]) * p.sm);
+              u.w = pack_bf16(__uint_as_float(a[q * 8 + 6]) * p.sm, __uint_as_float(a[q * 8 + 7]) * p.sm);
+              *reinterpret_cast<uint4*>(dst + q * 8) = u;
+            }
+          }
+        }
+      }
+    }
+  }
+  __syncwarp();
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+}
+
+// ============================================================================ dK/dV kernel
+constexpr int KV_BN = 128;  // keys per CTA
+constexpr int KV_BM = 32;   // queries per block
+constexpr int KV_STAGES = 3;
+
+template <int DK, int DV>
+struct DkvSmem {
+  static constexpr int kK = DK / 64 * KV_BN * 128;
+  static constexpr int kV = DV / 64 * KV_BN * 128;
+  static constexpr int kQ = DK / 64 * KV_BM * 128;
+  static constexpr int kDO = DV / 64 * KV_BM * 128;
+  static constexpr int kStage = 2 * kQ + kDO;
+  static constexpr int kT = KV_BN * 64;  // 128 rows x 32 queries bf16 (64-byte rows)
+  static constexpr int kTile = 3 * kT;   // P^T, dS1^T, dS2^T
+  static constexpr int kOffK1 = 0, kOffK2 = kK, kOffV = 2 * kK;
+  static constexpr int kOffStage = 2 * kK + kV;
+  static constexpr int kOffT = kOffStage + KV_STAGES * kStage;
+  static constexpr int kOffRed = kOffT + 2 * kTile;        // 4 warps x 4 floats
+  static constexpr int kOffBar = kOffRed + 256;
+  static constexpr int kBytes = (kOffBar + 256 + 1024) > 120 * 1024 ? (kOffBar + 256 + 1024) : 120 * 1024;
+};
+
+// 64-byte swizzle (Swizzle<2,4,3>): 16-byte chunk c of row r
+__device__ __forceinline__ uint32_t sw64_offset(uint32_t row, uint32_t chunk) {
+  return row * 64u + ((chunk ^ ((row >> 1) & 3u)) << 4);
+}
+
+template <int DK, int DV, int KIND>
+__global__ void __launch_bounds__(kBwdThreads, 1)
+    poly_bwd_dkv_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant__ CUtensorMap tmQ,
+                        const __grid_constant__ CUtensorMap tmDO, const int* __restrict__ doc_end, Params p) {
+  using S = DkvSmem<DK, DV>;
+  constexpr bool kTwo = KIND != 1;
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* bar = reinterpret_cast<uint64_t*>(smem + S::kOffBar);
+  uint64_t* k_full = bar + 0;
+  uint64_t* q_full = bar + 1;    // [3]
+  uint64_t* q_empty = bar + 4;   // [3]
+  uint64_t* sc_full = bar + 7;
+  uint64_t* sc_empty = bar + 8;
+  uint64_t* t_full = bar + 9;    // [2]
+  uint64_t* t_empty = bar + 11;  // [2]
+  uint64_t* acc_full = bar + 13;
+  uint64_t* mma_done = bar + 14;
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(bar + 16);
+  float* red = reinterpret_cast<float*>(smem + S::kOffRed);
+
+  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+  const int kb = blockIdx.x;
+  const int bh = blockIdx.y;
+  const int b = bh / p.H, h = bh % p.H;
+  const int k0 = kb * KV_BN;
+  const long long row0 = static_cast<long long>(b) * p.T;
+  const int klast = min(k0 + KV_BN, p.T) - 1;
+  const int hi = doc_end[row0 + klast];  // exclusive end of the last key's document
+  const int nqb = (hi - k0 + KV_BM - 1) / KV_BM;
+
+  if (threadIdx.x == 0) {
+    mbar_init(k_full, 1);
+    for (int i = 0; i < KV_STAGES; ++i) {
+      mbar_init(&q_full[i], 1);
+      mbar_init(&q_empty[i], 1);
+    }
+    mbar_init(sc_full, 1);
+    mbar_init(sc_empty, 128);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&t_full[i], 128);
+      mbar_init(&t_empty[i], 1);
+    }
+    mbar_init(acc_full, 1);
+    mbar_init(mma_done, 1);
+    fence_mbar_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_holder, 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_holder;
+  // TMEM: S1^T 0, S2^T 32, dP^T 64, dV at 128, dK1 at 128+DV, dK2 at 128+DV+DK
+  const uint32_t tS1 = tmem, tS2 = tmem + 32, tDP = tmem + 64;
+  const uint32_t tDV = tmem + 128, tDK1 = tmem + 128 + DV, tDK2 = tmem + 128 + DV + DK;
+
+  if (warp == 0) {
+    if (elect_one()) {
+      prefetch_tmap(&tmK);
+      prefetch_tmap(&tmQ);
+      prefetch_tmap(&tmDO);
+      const int krow = static_cast<int>(row0 + k0);
+      mbar_arrive_expect_tx(k_full, (kTwo ? 2 : 1) * S::kK + S::kV);
+      for (int i = 0; i < DK / 64; ++i) {
+        tma_load_2d(smem + S::kOffK1 + i * KV_BN * 128, &tmK, k_full, p.ck1 + h * DK + 64 * i, krow);
+        if (kTwo) tma_load_2d(smem + S::kOffK2 + i * KV_BN * 128, &tmK, k_full, p.ck2 + h * DK + 64 * i, krow);
+      }
+      for (int i = 0; i < DV / 64; ++i)
+        tma_load_2d(smem + S::kOffV + i * KV_BN * 128, &tmK, k_full, p.cv + h * DV + 64 * i, krow);
+      bool ok = true;
+      for (int i = 0; i < nqb && ok; ++i) {
+        const int st = i % KV_STAGES;
+        if (!mbar_wait(&q_empty[st], ((i / KV_STAGES) & 1) ^ 1, p.status, kErrTimeoutProducer)) {
+          ok = false;
+          break;
+        }
+        uint8_t* sq = smem + S::kOffStage + st * S::kStage;
+        const int qrow = static_cast<int>(row0 + k0 + i * KV_BM);
+        mbar_arrive_expect_tx(&q_full[st], (kTwo ? 2 : 1) * S::kQ + S::kDO);
+        for (int c = 0; c < DK / 64; ++c) {
+          tma_load_2d(sq + c * KV_BM * 128, &tmQ, &q_full[st], p.cq1 + h * DK + 64 * c, qrow);
+          if (kTwo) tma_load_2d(sq + S::kQ + c * KV_BM * 128, &tmQ, &q_full[st], p.cq2 + h * DK + 64 * c, qrow);
+        }
+        for (int c = 0; c < DV / 64; ++c)
+          tma_load_2d(sq + 2 * S::kQ + c * KV_BM * 128, &tmDO, &q_full[st], h * DV + 64 * c, qrow);
+      }
+      mbar_wait(k_full, 0, p.status, kErrTimeoutProducer);
+      if (!ok)
+        for (int i = max(0, nqb - KV_STAGES); i < nqb; ++i)
+          mbar_wait(&q_full[i % KV_STAGES], (i / KV_STAGES) & 1, p.status, kErrTimeoutProducer);
+    }
+  } else if (warp == 1) {
+    if (elect_one()) {
+      constexpr uint32_t idS = idesc_bf16_f32(128, KV_BM, 0, 0);
+      constexpr uint32_t idDV = idesc_bf16_f32(128, DV, 0, 1);
+      constexpr uint32_t idDK = idesc_bf16_f32(128, DK, 0, 1);
+      const uint32_t sK1 = smem_u32(smem + S::kOffK1), sK2 = smem_u32(smem + S::kOffK2);
+      const uint32_t sV = smem_u32(smem + S::kOffV);
+      bool ok = mbar_wait(k_full, 0, p.status, kErrTimeoutMma);
+      auto accumulate = [&](int i) -> bool {
+        const int tb = i & 1;
+        if (!mbar_wait(&t_full[tb], (i >> 1) & 1, p.status, kErrTimeoutMma)) return false;
+        tc_fence_after();
+        const uint32_t sq = smem_u32(smem + S::kOffStage + (i % KV_STAGES) * S::kStage);
+        const uint32_t sT = smem_u32(smem + S::kOffT + tb * S::kTile);
+#pragma unroll
+        for (int k = 0; k < KV_BM / 16; ++k) {
+          const uint32_t acc = (i > 0 || k > 0) ? 1u : 0u;
+          // A tiles (128 keys x 32 queries, 64-byte swizzle): P^T, dS1^T, dS2^T
+          const uint64_t aP = smem_desc(sT + k * 32, 16, 512, 4);
+          const uint64_t a1 = smem_desc(sT + S::kT + k * 32, 16, 512, 4);
+          const uint64_t a2 = smem_desc(sT + 2 * S::kT + k * 32, 16, 512, 4);
+          umma_ss(tDV, aP, mnmajor_desc(sq + 2 * S::kQ, KV_BM, k), idDV, acc);
+          umma_ss(tDK1, a1, mnmajor_desc(sq, KV_BM, k), idDK, acc);
+          if (kTwo) umma_ss(tDK2, a2, mnmajor_desc(sq + S::kQ, KV_BM, k), idDK, acc);
+        }
+        umma_commit(&t_empty[tb]);
+        umma_commit(&q_empty[i % KV_STAGES]);
+        return true;
+      };
+      for (int i = 0; i < nqb && ok; ++i) {
+        const int st = i % KV_STAGES;
+        if (!mbar_wait(&q_full[st], (i / KV_STAGES) & 1, p.status, kErrTimeoutMma)) { ok = false; break; }
+        if (!mbar_wait(sc_empty, (i & 1) ^ 1, p.status, kErrTimeoutMma)) { ok = false; break; }
+        tc_fence_after();
+        const uint32_t sq = smem_u32(smem + S::kOffStage + st * S::kStage);
+#pragma unroll
+        for (int k = 0; k < DK / 16; ++k) {
+          umma_ss(tS1, kmajor_desc(sK1, KV_BN, k), kmajor_desc(sq, KV_BM, k), idS, k > 0 ? 1u : 0u);
+          if (kTwo) umma_ss(tS2, kmajor_desc(sK2, KV_BN, k), kmajor_desc(sq + S::kQ, KV_BM, k), idS, k > 0 ? 1u : 0u);
+        }
+#pragma unroll
+        for (int k = 0; k < DV / 16; ++k)
+          umma_ss(tDP, kmajor_desc(sV, KV_BN, k), kmajor_desc(sq + 2 * S::kQ, KV_BM, k), idS, k > 0 ? 1u : 0u);
+        umma_commit(sc_full);
+        if (i > 0 && !accumulate(i - 1)) { ok = false; break; }
+      }
+      if (ok && nqb > 0 && accumulate(nqb - 1)) umma_commit(acc_full);
+      umma_commit(mma_done);
+      mbar_wait(mma_done, 0, p.status, kErrTimeoutMma);
+    }
+  } else {
+    const int sub = warp & 3;
+    const int r = sub * 32 + lane;  // key row
+    const int kt = k0 + r;
+    const bool kvalid = kt < p.T;
+    const long long krow = row0 + (kvalid ? kt : k0);
+    const bool kreal = kvalid && p.doc[krow] >= 0;
+    const int kend = kreal ? doc_end[krow] : kt;  // queries of the same document: [kt, kend)
+    float c[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) c[i] = p.par[h * 4 + i];
+    float g0 = 0.f, g1 = 0.f, g2 = 0.f, g12 = 0.f;
+    const uint32_t lane_off = static_cast<uint32_t>(sub * 32) << 16;
+    bool ok = true;
+    for (int i = 0; i < nqb && ok; ++i) {
+      if (!mbar_wait(sc_full, i & 1, p.status, kErrTimeoutEpilogue)) { ok = false; break; }
+      tc_fence_after();
+      uint32_t a[32], bb[32], g[32];
+      tmem_ld32(tS1 + lane_off, a);
+      if (kTwo) tmem_ld32(tS2 + lane_off, bb);
+      tmem_ld32(tDP + lane_off, g);
+      tmem_ld_wait();
+      tc_fence_before();
+      mbar_arrive(sc_empty);
+      const int qb0 = k0 + i * KV_BM;
+      uint32_t pp[16], d1[16], d2[16];
+#pragma unroll
+      for (int jj = 0; jj < 32; jj += 2) {
+        float vp[2], o1[2], o2[2];
+#pragma unroll
+        for (int e = 0; e < 2; ++e) {
+          const int qt = qb0 + jj + e;
+          const bool vis = kreal && qt >= kt && qt < kend;
+          const float rs = vis ? p.row_scale[row0 + qt] : 0.f;
+          const float s1 = __uint_as_float(a[jj + e]) * p.sm;
+          const float s2 = kTwo ? __uint_as_float(bb[jj + e]) * p.sm : s1;
+          const float hh = __uint_as_float(g[jj + e]) * rs;
+          vp[e] = rs * poly<KIND>(s1, s2, c);
+          if (KIND == 0) {
+            o1[e] = hh * s2;
+            o2[e] = hh * s1;
+          } else if (KIND == 1) {
+            o1[e] = 2.f * hh * (s1 + c[0]);
+            o2[e] = 0.f;
+            g0 += o1[e];
+          } else {
+            o1[e] = hh * (c[1] + c[3] * s2);
+            o2[e] = hh * (c[2] + c[3] * s1);
+            g0 += hh;
+            g1 += hh * s1;
+            g2 += hh * s2;
+            g12 += hh * s1 * s2;
+          }
+        }
+        pp[jj / 2] = pack_bf16(vp[0], vp[1]);
+        d1[jj / 2] = pack_bf16(o1[0], o1[1]);
+        d2[jj / 2] = pack_bf16(o2[0], o2[1]);
+      }
+      const int tb = i & 1;
+      if (!mbar_wait(&t_empty[tb], ((i >> 1) & 1) ^ 1, p.status, kErrTimeoutEpilogue)) { ok = false; break; }
+      uint8_t* tp = smem + S::kOffT + tb * S::kTile;
+#pragma unroll
+      for (int ch = 0; ch < 4; ++ch) {
+        const uint32_t off = sw64_offset(r, ch);
+        *reinterpret_cast<uint4*>(tp + off) = make_uint4(pp[ch * 4], pp[ch * 4 + 1], pp[ch * 4 + 2], pp[ch * 4 + 3]);
+        *reinterpret_cast<uint4*>(tp + S::kT + off) =
+            make_uint4(d1[ch * 4], d1[ch * 4 + 1], d1[ch * 4 + 2], d1[ch * 4 + 3]);
+        if (kTwo)
+          *reinterpret_cast<uint4*>(tp + 2 * S::kT + off) =
+              make_uint4(d2[ch * 4], d2[ch * 4 + 1], d2[ch * 4 + 2], d2[ch * 4 + 3]);
+      }
+      fence_proxy_async_smem();
+      mbar_arrive(&t_full[tb]);
+    }
+    // kind-parameter partials: fixed-order reduction over the 128 key rows of this block
+    if (KIND != 0 && p.dpar != nullptr) {
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) {
+        g0 += __shfl_xor_sync(0xffffffffu, g0, o);
+        g1 += __shfl_xor_sync(0xffffffffu, g1, o);
+        g2 += __shfl_xor_sync(0xffffffffu, g2, o);
+        g12 += __shfl_xor_sync(0xffffffffu, g12, o);
+      }
+      if (lane == 0) {
+        red[sub * 4 + 0] = g0;
+        red[sub * 4 + 1] = g1;
+        red[sub * 4 + 2] = g2;
+        red[sub * 4 + 3] = g12;
+      }
+      asm volatile("bar.sync 1, 128;" ::: "memory");
+      if (r < 4) {
+        const float s = red[0 * 4 + r] + red[1 * 4 + r] + red[2 * 4 + r] + red[3 * 4 + r];
+        p.dpar[(static_cast<long long>(bh) * p.dpar_blocks + kb) * 4 + r] = s;
+      }
+    }
+    if (ok && nqb > 0 && mbar_wait(acc_full, 0, p.status, kErrTimeoutEpilogue)) {
+      tc_fence_after();
+#pragma unroll 1
+      for (int which = 0; which < (kTwo ? 3 : 2); ++which) {
+        const uint32_t tacc = (which == 0 ? tDV : (which == 1 ? tDK1 : tDK2)) + lane_off;
+        const int width = which == 0 ? DV : DK;
+        const int col = (which == 0 ? p.cv + h * DV : (which == 1 ? p.ck1 : p.ck2) + h * DK);
+        const float scale = which == 0 ? 1.f : p.sm;
+#pragma unroll 1
+        for (int cc = 0; cc < width / 32; ++cc) {
+          uint32_t a[32];
+          tmem_ld32(tacc + cc * 32, a);
+          tmem_ld_wait();
+          if (kvalid) {
+            __nv_bfloat16* dst = p.dq + krow * p.ldd + col + cc * 32;
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+              uint4 u;
+              u.x = pack_bf16(__uint_as_float(a[q * 8 + 0]) * scale, __uint_as_float(a[q * 8 + 1]) * scale);
+              u.y = pack_bf16(__uint_as_float(a[q * 8 + 2]) * scale, __uint_as_float(a[q * 8 + 3]) * scale);
+              u.z = pack_bf16(__uint_as_float(a[q * 8 + 4]) * scale, __uint_as_float(a[q * 8 + 5]) * scale);
+              u.w = pack_bf16(__uint_as_float(a[q * 8 + 6]) * scale, __uint_as_float(a[q * 8 + 7]) * scale);
+              *reinterpret_cast<uint4*>(dst + q * 8) = u;
+            }
+          }
+        }
+      }
+    } else if (kvalid && ok && nqb == 0) {
+      // no visible query: gradients are zero
+      for (int which = 0; which < (kTwo ? 3 : 2); ++which) {
+        const int width = which == 0 ? DV : DK;
+        const int col = (which == 0 ? p.cv + h * DV : (which == 1 ? p.ck1 : p.ck2) + h * DK);
+        for (int cc = 0; cc < width; ++cc) p.dq[krow * p.ldd + col + cc] = __float2bfloat16_rn(0.f);
+      }
+    }
+  }
+  __syncwarp();
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+}
+
+template <int DK, int DV, int KIND>
+void launch_bwd(const void* qkv, long long ld, const void* dout, long long ldo, const int* doc_end, long long rows,
+                const Params& p, cudaStream_t stream) {
+  {
+    using S = DqSmem<DK, DV>;
+    const CUtensorMap tq = make_tmap_2d(qkv, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, ld, rows, ld, 64, DQ_BM);
+    const CUtensorMap tkv = make_tmap_2d(qkv, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, ld, rows, ld, 64, DQ_BN);
+    const CUtensorMap tdo = make_tmap_2d(dout, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, ldo, rows, ldo, 64, DQ_BM);
+    auto kern = poly_bwd_dq_kernel<DK, DV, KIND>;
+    static bool configured = false;
+    if (!configured) {
+      TTB_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, S::kBytes));
+      configured = true;
+    }
+    dim3 grid((p.T + DQ_BM - 1) / DQ_BM, p.B * p.H);
+    kern<<<grid, kBwdThreads, S::kBytes, stream>>>(tq, tkv, tdo, p);
+    TTB_CUDA_CHECK(cudaGetLastError());
+  }
+  {
+    using S = DkvSmem<DK, DV>;
+    const CUtensorMap tk = make_tmap_2d(qkv, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, ld, rows, ld, 64, KV_BN);
+    const CUtensorMap tq = make_tmap_2d(qkv, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, ld, rows, ld, 64, KV_BM);
+    const CUtensorMap tdo = make_tmap_2d(dout, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, ldo, rows, ldo, 64, KV_BM);
+    auto kern = poly_bwd_dkv_kernel<DK, DV, KIND>;
+    static bool configured = false;
+    if (!configured) {
+      TTB_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, S::kBytes));
+      configured = true;
+    }
+    dim3 grid((p.T + KV_BN - 1) / KV_BN, p.B * p.H);
+    kern<<<grid, kBwdThreads, S::kBytes, stream>>>(tk, tq, tdo, doc_end, p);
+    TTB_CUDA_CHECK(cudaGetLastError());
+  }
+}
+
+}  // namespace attn
+
+int poly_attention_dpar_blocks(int T) { return (T + attn::KV_BN - 1) / attn::KV_BN; }
+
+void poly_attention_bwd(int kind, int dk, int dv, const void* qkv, long long ld, const void* dout, long long ldo,
+                        const int* doc_end, attn::Params p, cudaStream_t stream) {
+  TTB_CHECK((dk == 64 || dk == 128) && (dv == 64 || dv == 128), "poly attention: head dims must be 64 or 128");
+  const long long rows = static_cast<long long>(p.B) * p.T;
+  p.status = status_ptr();
+  p.dpar_blocks = poly_attention_dpar_blocks(p.T);
+#define TTB_BWD(DK_, DV_, K_)                                                                         \
+  if (dk == DK_ && dv == DV_ && kind == K_)                                                          \
+    return attn::launch_bwd<DK_, DV_, K_>(qkv, ld, dout, ldo, doc_end, rows, p, stream);
+  TTB_BWD(64, 64, 0) TTB_BWD(64, 64, 1) TTB_BWD(64, 64, 2)
+  TTB_BWD(128, 128, 0) TTB_BWD(128, 128, 1) TTB_BWD(128, 128, 2)
+  TTB_BWD(64, 128, 0) TTB_BWD(64, 128, 1) TTB_BWD(64, 128, 2)
+  TTB_BWD(128, 64, 0) TTB_BWD(128, 64, 1) TTB_BWD(128, 64, 2)
+#undef TTB_BWD
+  TTB_CHECK(false, "poly attention backward: unsupported configuration");
+}
+
+}  // namespace ttb

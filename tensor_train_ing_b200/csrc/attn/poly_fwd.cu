@@ -1,0 +1,289 @@
+// Polynomial attention forward on the 5th-generation tensor cores (sm_100a).
+//
+// One CTA per (batch, head, block of 128 queries).  Warp roles:
+//   warp 0    TMA producer: Q1/Q2 once, then K1/K2/V tiles of 64 keys through a 2-stage ring
+//   warp 1    tcgen05.mma issuer: S1 = Q1 K1^T, S2 = Q2 K2^T into a double-buffered TMEM pair,
+//             then O += P V once the poly warps have produced P
+//   warps 2-5 "poly" warps, one query row per thread: tcgen05.ld the S1/S2 row, form
+//             P = visible * row_scale * A(S1, S2) (fp32), round to bf16 and write it into a
+//             128B-swizzled K-major shared tile; finally drain O from TMEM to global memory.
+// S of key block j+1 is computed while the poly warps work on block j, and P V of block j runs
+// after it, so the tensor pipe stays busy.  Key blocks before the start of the first query's
+// document are skipped (documents are contiguous).  Reference: tnlm/kernels/poly_attn.py:38-74.
+#include "../common/host.h"
+#include "attn_api.h"
+#include "poly_common.cuh"
+
+namespace ttb {
+namespace attn {
+
+constexpr int BMQ = 128;  // queries per CTA
+constexpr int BNK = 64;   // keys per block
+constexpr int kThreads = 192;
+
+template <int DK, int DV>
+struct FwdSmem {
+  static constexpr int kQ = DK / 64 * BMQ * 128;          // one of Q1/Q2
+  static constexpr int kK = DK / 64 * BNK * 128;          // one of K1/K2
+  static constexpr int kV = DV / 64 * BNK * 128;
+  static constexpr int kStage = 2 * kK + kV;
+  static constexpr int kP = BMQ * 128;                     // 128 rows x 64 keys bf16
+  static constexpr int kOffQ1 = 0;
+  static constexpr int kOffQ2 = kQ;
+  static constexpr int kOffStage = 2 * kQ;
+  static constexpr int kOffP = kOffStage + 2 * kStage;
+  static constexpr int kOffBar = kOffP + 2 * kP;
+  // >= 120 KB keeps one CTA per SM, so the 512-column TMEM allocation never waits on a neighbour
+  static constexpr int kBytes = (kOffBar + 256 + 1024) > 120 * 1024 ? (kOffBar + 256 + 1024) : 120 * 1024;
+};
+
+template <int DK, int DV, int KIND>
+__global__ void __launch_bounds__(kThreads, 1)
+    poly_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmKV, Params p) {
+  using S = FwdSmem<DK, DV>;
+  constexpr bool kTwo = KIND != 1;  // kinds with a second score S2
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* bar = reinterpret_cast<uint64_t*>(smem + S::kOffBar);
+  uint64_t* q_full = bar + 0;
+  uint64_t* kv_full = bar + 1;    // [2]
+  uint64_t* kv_empty = bar + 3;   // [2]
+  uint64_t* s_full = bar + 5;     // [2]
+  uint64_t* s_empty = bar + 7;    // [2]
+  uint64_t* p_full = bar + 9;     // [2]
+  uint64_t* p_empty = bar + 11;   // [2]
+  uint64_t* o_full = bar + 13;
+  uint64_t* mma_done = bar + 14;
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(bar + 16);
+
+  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+  const int nqb = (p.T + BMQ - 1) / BMQ;
+  const int qb = nqb - 1 - static_cast<int>(blockIdx.x);  // heaviest blocks first
+  const int bh = blockIdx.y;
+  const int b = bh / p.H, h = bh % p.H;
+  const int q0 = qb * BMQ;
+  const long long row0 = static_cast<long long>(b) * p.T;
+  const int lo = q0 - p.pos[row0 + q0];  // start of the first query's document
+  const int kstart = (lo / BNK) * BNK;
+  const int kend = min(q0 + BMQ, p.T);
+  const int nkb = (kend - kstart + BNK - 1) / BNK;
+
+  if (threadIdx.x == 0) {
+    mbar_init(q_full, 1);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&kv_full[i], 1);
+      mbar_init(&kv_empty[i], 1);
+      mbar_init(&s_full[i], 1);
+      mbar_init(&s_empty[i], 128);
+      mbar_init(&p_full[i], 128);
+      mbar_init(&p_empty[i], 1);
+    }
+    mbar_init(o_full, 1);
+    mbar_init(mma_done, 1);
+    fence_mbar_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_holder, 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_holder;
+  // TMEM columns: S1[2] at 0/64, S2[2] at 128/192, O at 256
+  const uint32_t tS1 = tmem, tS2 = tmem + 128, tO = tmem + 256;
+
+  if (warp == 0) {
+    if (elect_one()) {
+      prefetch_tmap(&tmQ);
+      prefetch_tmap(&tmKV);
+      const int qrow = static_cast<int>(row0 + q0);
+      mbar_arrive_expect_tx(q_full, (kTwo ? 2 : 1) * S::kQ);
+      for (int i = 0; i < DK / 64; ++i) {
+        tma_load_2d(smem + S::kOffQ1 + i * BMQ * 128, &tmQ, q_full, p.cq1 + h * DK + 64 * i, qrow);
+        if (kTwo) tma_load_2d(smem + S::kOffQ2 + i * BMQ * 128, &tmQ, q_full, p.cq2 + h * DK + 64 * i, qrow);
+      }
+      bool ok = true;
+      for (int j = 0; j < nkb && ok; ++j) {
+        const int st = j & 1;
+        if (!mbar_wait(&kv_empty[st], ((j >> 1) & 1) ^ 1, p.status, kErrTimeoutProducer)) {
+          ok = false;
+          break;
+        }
+        uint8_t* sk = smem + S::kOffStage + st * S::kStage;
+        const int krow = static_cast<int>(row0 + kstart + j * BNK);
+        mbar_arrive_expect_tx(&kv_full[st], (kTwo ? 2 : 1) * S::kK + S::kV);
+        for (int i = 0; i < DK / 64; ++i) {
+          tma_load_2d(sk + i * BNK * 128, &tmKV, &kv_full[st], p.ck1 + h * DK + 64 * i, krow);
+          if (kTwo) tma_load_2d(sk + S::kK + i * BNK * 128, &tmKV, &kv_full[st], p.ck2 + h * DK + 64 * i, krow);
+        }
+        for (int i = 0; i < DV / 64; ++i)
+          tma_load_2d(sk + 2 * S::kK + i * BNK * 128, &tmKV, &kv_full[st], p.cv + h * DV + 64 * i, krow);
+      }
+      // let in-flight copies land before exit (bounded)
+      mbar_wait(q_full, 0, p.status, kErrTimeoutProducer);
+      if (!ok) {
+        for (int j = max(0, nkb - 2); j < nkb; ++j) mbar_wait(&kv_full[j & 1], (j >> 1) & 1, p.status, kErrTimeoutProducer);
+      }
+    }
+  } else if (warp == 1) {
+    if (elect_one()) {
+      constexpr uint32_t idS = idesc_bf16_f32(128, BNK, 0, 0);
+      constexpr uint32_t idPV = idesc_bf16_f32(128, DV, 0, 1);
+      const uint32_t sQ1 = smem_u32(smem + S::kOffQ1), sQ2 = smem_u32(smem + S::kOffQ2);
+      bool ok = mbar_wait(q_full, 0, p.status, kErrTimeoutMma);
+      auto issue_pv = [&](int i) -> bool {
+        const int pb = i & 1;
+        if (!mbar_wait(&p_full[pb], (i >> 1) & 1, p.status, kErrTimeoutMma)) return false;
+        tc_fence_after();
+        const uint32_t sP = smem_u32(smem + S::kOffP + pb * S::kP);
+        const uint32_t sV = smem_u32(smem + S::kOffStage + pb * S::kStage + 2 * S::kK);
+#pragma unroll
+        for (int k = 0; k < BNK / 16; ++k)
+          umma_ss(tO, kmajor_desc(sP, BMQ, k), mnmajor_desc(sV, BNK, k), idPV, (i > 0 || k > 0) ? 1u : 0u);
+        umma_commit(&p_empty[pb]);
+        umma_commit(&kv_empty[pb]);
+        return true;
+      };
+      for (int j = 0; j < nkb && ok; ++j) {
+        const int st = j & 1;
+        const uint32_t ph = (j >> 1) & 1;
+        if (!mbar_wait(&kv_full[st], ph, p.status, kErrTimeoutMma)) { ok = false; break; }
+        if (!mbar_wait(&s_empty[st], ph ^ 1, p.status, kErrTimeoutMma)) { ok = false; break; }
+        tc_fence_after();
+        const uint32_t sK1 = smem_u32(smem + S::kOffStage + st * S::kStage);
+        const uint32_t sK2 = sK1 + S::kK;
+#pragma unroll
+        for (int k = 0; k < DK / 16; ++k)
+          umma_ss(tS1 + st * BNK, kmajor_desc(sQ1, BMQ, k), kmajor_desc(sK1, BNK, k), idS, k > 0 ? 1u : 0u);
+        if (kTwo) {
+#pragma unroll
+          for (int k = 0; k < DK / 16; ++k)
+            umma_ss(tS2 + st * BNK, kmajor_desc(sQ2, BMQ, k), kmajor_desc(sK2, BNK, k), idS, k > 0 ? 1u : 0u);
+        }
+        umma_commit(&s_full[st]);
+        if (j > 0 && !issue_pv(j - 1)) { ok = false; break; }
+      }
+      if (ok && issue_pv(nkb - 1)) umma_commit(o_full);
+      umma_commit(mma_done);
+      mbar_wait(mma_done, 0, p.status, kErrTimeoutMma);
+    }
+  } else {
+    // ------------------------------------------------------------- poly warps (2..5)
+    const int sub = warp & 3;
+    const int r = sub * 32 + lane;  // query row inside the block == TMEM lane
+    const int t = q0 + r;
+    const bool valid = t < p.T;
+    const long long grow = row0 + (valid ? t : q0);
+    const int dq = valid ? p.doc[grow] : -1;
+    const int dstart = valid ? t - p.pos[grow] : 0;  // documents are contiguous: keys [dstart, t]
+    const float rs = valid ? p.row_scale[grow] : 0.f;
+    float c[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) c[i] = p.par[h * 4 + i];
+    const uint32_t lane_off = static_cast<uint32_t>(sub * 32) << 16;
+    bool ok = true;
+    for (int j = 0; j < nkb && ok; ++j) {
+      const int st = j & 1;
+      const uint32_t ph = (j >> 1) & 1;
+      if (!mbar_wait(&s_full[st], ph, p.status, kErrTimeoutEpilogue)) { ok = false; break; }
+      tc_fence_after();
+      uint32_t pk[32];  // 64 bf16 of this row of P
+      const int kb0 = kstart + j * BNK;
+#pragma unroll
+      for (int cc = 0; cc < BNK / 32; ++cc) {
+        uint32_t a[32], bb[32];
+        tmem_ld32(tS1 + lane_off + st * BNK + cc * 32, a);
+        if (kTwo) tmem_ld32(tS2 + lane_off + st * BNK + cc * 32, bb);
+        tmem_ld_wait();
+#pragma unroll
+        for (int jj = 0; jj < 32; jj += 2) {
+          float v[2];
+#pragma unroll
+          for (int e = 0; e < 2; ++e) {
+            const int kt = kb0 + cc * 32 + jj + e;
+            const float s1 = __uint_as_float(a[jj + e]) * p.sm;
+            const float s2 = kTwo ? __uint_as_float(bb[jj + e]) * p.sm : s1;
+            const bool vis = valid && dq >= 0 && kt <= t && kt >= dstart;
+            v[e] = vis ? poly<KIND>(s1, s2, c) * rs : 0.f;
+          }
+          pk[cc * 16 + jj / 2] = pack_bf16(v[0], v[1]);
+        }
+      }
+      tc_fence_before();
+      mbar_arrive(&s_empty[st]);
+      // P buffer st is free once P V of block j-2 has completed
+      if (!mbar_wait(&p_empty[st], ph ^ 1, p.status, kErrTimeoutEpilogue)) { ok = false; break; }
+      uint8_t* prow = smem + S::kOffP + st * S::kP;
+#pragma unroll
+      for (int ch = 0; ch < 8; ++ch) {
+        uint4 u = make_uint4(pk[ch * 4], pk[ch * 4 + 1], pk[ch * 4 + 2], pk[ch * 4 + 3]);
+        *reinterpret_cast<uint4*>(prow + sw128_offset(r, ch)) = u;
+      }
+      fence_proxy_async_smem();
+      mbar_arrive(&p_full[st]);
+    }
+    if (ok && mbar_wait(o_full, 0, p.status, kErrTimeoutEpilogue)) {
+      tc_fence_after();
+#pragma unroll 1
+      for (int cc = 0; cc < DV / 32; ++cc) {
+        uint32_t a[32];
+        tmem_ld32(tO + lane_off + cc * 32, a);
+        tmem_ld_wait();
+        if (valid) {
+          __nv_bfloat16* dst = p.y + grow * p.ldy + h * DV + cc * 32;
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            uint4 u;
+            u.x = pack_bf16(__uint_as_float(a[q * 8 + 0]), __uint_as_float(a[q * 8 + 1]));
+            u.y = pack_bf16(__uint_as_float(a[q * 8 + 2]), __uint_as_float(a[q * 8 + 3]));
+            u.z = pack_bf16(__uint_as_float(a[q * 8 + 4]), __uint_as_float(a[q * 8 + 5]));
+            u.w = pack_bf16(__uint_as_float(a[q * 8 + 6]), __uint_as_float(a[q * 8 + 7]));
+            *reinterpret_cast<uint4*>(dst + q * 8) = u;
+          }
+        }
+      }
+    }
+  }
+  __syncwarp();
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+}
+
+template <int DK, int DV, int KIND>
+void launch_fwd(const void* qkv, long long ld, long long rows, const Params& p, cudaStream_t stream) {
+  using S = FwdSmem<DK, DV>;
+  const CUtensorMap tq = make_tmap_2d(qkv, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, ld, rows, ld, 64, BMQ);
+  const CUtensorMap tkv = make_tmap_2d(qkv, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, ld, rows, ld, 64, BNK);
+  auto kern = poly_fwd_kernel<DK, DV, KIND>;
+  static bool configured = false;
+  if (!configured) {
+    TTB_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, S::kBytes));
+    configured = true;
+  }
+  dim3 grid((p.T + BMQ - 1) / BMQ, p.B * p.H);
+  kern<<<grid, kThreads, S::kBytes, stream>>>(tq, tkv, p);
+  TTB_CUDA_CHECK(cudaGetLastError());
+}
+
+}  // namespace attn
+
+void poly_attention_fwd(int kind, int dk, int dv, const void* qkv, long long ld, attn::Params p, cudaStream_t stream) {
+  TTB_CHECK((dk == 64 || dk == 128) && (dv == 64 || dv == 128), "poly attention: head dims must be 64 or 128");
+  TTB_CHECK(kind >= 0 && kind <= 2, "poly attention: bad kind");
+  const long long rows = static_cast<long long>(p.B) * p.T;
+  p.status = status_ptr();
+#define TTB_FWD(DK_, DV_, K_) \
+  if (dk == DK_ && dv == DV_ && kind == K_) return attn::launch_fwd<DK_, DV_, K_>(qkv, ld, rows, p, stream);
+  TTB_FWD(64, 64, 0) TTB_FWD(64, 64, 1) TTB_FWD(64, 64, 2)
+  TTB_FWD(128, 128, 0) TTB_FWD(128, 128, 1) TTB_FWD(128, 128, 2)
+  TTB_FWD(64, 128, 0) TTB_FWD(64, 128, 1) TTB_FWD(64, 128, 2)
+  TTB_FWD(128, 64, 0) TTB_FWD(128, 64, 1) TTB_FWD(128, 64, 2)
+#undef TTB_FWD
+}
+
+}  // namespace ttb

@@ -4,8 +4,14 @@
 #include <c10/cuda/CUDAGuard.h>
 #include <torch/extension.h>
 
+#include <cmath>
+#include <vector>
+
 #include "common/host.h"
+#include "attn/attn_api.h"
 #include "gemm/api.h"
+#include "gemm/ce_api.h"
+#include "misc/rowops.h"
 
 namespace {
 
@@ -117,6 +123,166 @@ void bilinear_grad(const Tensor& dy, const Tensor& wd, const Tensor& l, const Te
                           static_cast<int>(mode), cur_stream());
 }
 
+
+// ------------------------------------------------------------------ row ops
+std::vector<Tensor> rmsnorm_fwd(const Tensor& x, const Tensor& w, int64_t groups, double eps) {
+  const c10::cuda::CUDAGuard guard(x.device());
+  TORCH_CHECK(x.scalar_type() == torch::kFloat32 && x.is_contiguous() && x.dim() == 2, "x: contiguous fp32 [N, d]");
+  TORCH_CHECK(w.scalar_type() == torch::kFloat32 && w.is_contiguous() && w.numel() == x.size(1), "w");
+  const int N = x.size(0), d = x.size(1);
+  auto y = torch::empty({N, d}, x.options().dtype(torch::kBFloat16));
+  auto rstd = torch::empty({N, groups}, x.options());
+  if (N > 0)
+    ttb::rmsnorm_fwd(x.data_ptr<float>(), w.data_ptr<float>(), y.data_ptr(), rstd.data_ptr<float>(), N, d, groups,
+                     static_cast<float>(eps), cur_stream());
+  return {y, rstd};
+}
+
+// dres (+)= dx; returns dw
+Tensor rmsnorm_bwd(const Tensor& dy, const Tensor& x, const Tensor& w, const Tensor& rstd, Tensor& dres,
+                   bool accumulate, int64_t groups) {
+  const c10::cuda::CUDAGuard guard(x.device());
+  TORCH_CHECK(dy.is_contiguous() && dy.sizes() == x.sizes(), "dy");
+  TORCH_CHECK(dy.scalar_type() == torch::kFloat32 || dy.scalar_type() == torch::kBFloat16, "dy dtype");
+  TORCH_CHECK(dres.scalar_type() == torch::kFloat32 && dres.is_contiguous() && dres.sizes() == x.sizes(), "dres");
+  const int N = x.size(0), d = x.size(1);
+  auto dw = torch::zeros({d}, x.options());
+  if (N == 0) return dw;
+  auto part = torch::empty({ttb::rmsnorm_bwd_partials(N), d}, x.options());
+  ttb::rmsnorm_bwd(dy.data_ptr(), dy.scalar_type() == torch::kFloat32, x.data_ptr<float>(), w.data_ptr<float>(),
+                   rstd.data_ptr<float>(), dres.data_ptr<float>(), accumulate, part.data_ptr<float>(),
+                   dw.data_ptr<float>(), false, N, d, groups, cur_stream());
+  return dw;
+}
+
+void rope_(Tensor& buf, int64_t rope_cols, int64_t dk, const Tensor& pos, const Tensor& inv_freq, bool inverse) {
+  const c10::cuda::CUDAGuard guard(buf.device());
+  check_bf16(buf, "buf");
+  TORCH_CHECK(buf.dim() == 2 && buf.stride(1) == 1, "buf rows");
+  TORCH_CHECK(pos.scalar_type() == torch::kInt32 && pos.is_contiguous() && pos.numel() == buf.size(0), "pos");
+  TORCH_CHECK(inv_freq.scalar_type() == torch::kFloat32 && inv_freq.numel() == dk / 2, "inv_freq");
+  if (buf.size(0) == 0) return;
+  ttb::rope_apply(buf.data_ptr(), buf.stride(0), buf.size(0), rope_cols, dk, pos.data_ptr<int>(),
+                  inv_freq.data_ptr<float>(), inverse, cur_stream());
+}
+
+Tensor embed_fwd(const Tensor& idx, const Tensor& W) {
+  const c10::cuda::CUDAGuard guard(W.device());
+  TORCH_CHECK(idx.scalar_type() == torch::kInt64 && idx.is_contiguous(), "idx: int64");
+  TORCH_CHECK(W.scalar_type() == torch::kFloat32 && W.is_contiguous(), "W: fp32");
+  auto x = torch::empty({idx.numel(), W.size(1)}, W.options());
+  if (idx.numel() > 0)
+    ttb::embed_fwd(reinterpret_cast<const long long*>(idx.data_ptr<int64_t>()), W.data_ptr<float>(), x.data_ptr<float>(), idx.numel(), W.size(1),
+                   cur_stream());
+  return x;
+}
+
+// dW += scatter of dx rows by idx, deterministic (stable sort by id)
+void embed_bwd(const Tensor& idx, const Tensor& dx, Tensor& dW) {
+  const c10::cuda::CUDAGuard guard(dW.device());
+  TORCH_CHECK(dx.scalar_type() == torch::kFloat32 && dx.is_contiguous(), "dx: fp32");
+  TORCH_CHECK(dW.scalar_type() == torch::kFloat32 && dW.is_contiguous(), "dW: fp32");
+  if (idx.numel() == 0) return;
+  auto sorted = torch::sort(idx.reshape({-1}), /*stable=*/true, 0, false);
+  auto ids = std::get<0>(sorted).contiguous();
+  auto order = std::get<1>(sorted).contiguous();
+  ttb::embed_bwd(reinterpret_cast<const long long*>(ids.data_ptr<int64_t>()), reinterpret_cast<const long long*>(order.data_ptr<int64_t>()), dx.data_ptr<float>(), dW.data_ptr<float>(),
+                 idx.numel(), dW.size(1), cur_stream());
+}
+
+// ------------------------------------------------------------------ fused linear + CE
+// returns (loss_rows [M] fp32, lse [M] fp32)
+std::vector<Tensor> ce_fwd(const Tensor& x, const Tensor& w, int64_t V, double alpha, const Tensor& targets) {
+  const c10::cuda::CUDAGuard guard(x.device());
+  const auto X = a_operand(x);
+  const auto W = b_operand(w.t());
+  const int M = x.size(0), K = x.size(1);
+  TORCH_CHECK(w.size(1) == K && w.size(0) >= V, "w: [>=V, d]");
+  TORCH_CHECK(targets.scalar_type() == torch::kInt64 && targets.is_contiguous() && targets.numel() == M, "targets");
+  const int tiles = ttb::ce_num_tiles(V);
+  auto opts = x.options().dtype(torch::kFloat32);
+  auto pmax = torch::empty({M, tiles}, opts);
+  auto psum = torch::empty({M, tiles}, opts);
+  auto tlogit = torch::zeros({M}, opts);
+  auto lse = torch::empty({M}, opts);
+  auto loss = torch::empty({M}, opts);
+  ttb::ce_forward(X, W, M, V, K, static_cast<float>(alpha), reinterpret_cast<const long long*>(targets.data_ptr<int64_t>()), pmax.data_ptr<float>(),
+                  psum.data_ptr<float>(), tlogit.data_ptr<float>(), lse.data_ptr<float>(), loss.data_ptr<float>(),
+                  cur_stream());
+  return {loss, lse};
+}
+
+void ce_bwd_logits(const Tensor& x, const Tensor& w, int64_t V, double alpha, const Tensor& targets, const Tensor& lse,
+                   const Tensor& grad, Tensor& dlogits) {
+  const c10::cuda::CUDAGuard guard(x.device());
+  const auto X = a_operand(x);
+  const auto W = b_operand(w.t());
+  const int M = x.size(0), K = x.size(1);
+  check_bf16(dlogits, "dlogits");
+  TORCH_CHECK(dlogits.dim() == 2 && dlogits.size(0) == M && dlogits.stride(1) == 1, "dlogits");
+  TORCH_CHECK(grad.scalar_type() == torch::kFloat32 && grad.numel() == 1, "grad: fp32 scalar");
+  const int Npad = dlogits.size(1);
+  TORCH_CHECK(w.size(0) >= Npad, "w rows must cover the padded logits");
+  ttb::ce_backward_logits(X, W, M, Npad, V, K, static_cast<float>(alpha), reinterpret_cast<const long long*>(targets.data_ptr<int64_t>()),
+                          lse.data_ptr<float>(), grad.data_ptr<float>(), dlogits.data_ptr(), dlogits.stride(0),
+                          cur_stream());
+}
+
+// ------------------------------------------------------------------ polynomial attention
+ttb::attn::Params attn_params(const std::vector<int64_t>& cols, const Tensor& pos, const Tensor& doc,
+                              const Tensor& row_scale, const Tensor& par, int64_t B, int64_t T, int64_t H, int64_t dk) {
+  TORCH_CHECK(cols.size() == 5, "cols: q1,k1,q2,k2,v offsets");
+  TORCH_CHECK(pos.scalar_type() == torch::kInt32 && pos.is_contiguous() && pos.numel() == B * T, "pos int32 [B*T]");
+  TORCH_CHECK(doc.scalar_type() == torch::kInt32 && doc.is_contiguous() && doc.numel() == B * T, "doc int32 [B*T]");
+  TORCH_CHECK(row_scale.scalar_type() == torch::kFloat32 && row_scale.is_contiguous() && row_scale.numel() == B * T,
+              "row_scale fp32 [B*T]");
+  TORCH_CHECK(par.scalar_type() == torch::kFloat32 && par.is_contiguous() && par.numel() == H * 4, "par fp32 [H,4]");
+  for (auto c : cols) TORCH_CHECK(c % 64 == 0, "projection column offsets must be multiples of 64");
+  ttb::attn::Params p{};
+  p.B = B; p.T = T; p.H = H;
+  p.cq1 = cols[0]; p.ck1 = cols[1]; p.cq2 = cols[2]; p.ck2 = cols[3]; p.cv = cols[4];
+  p.pos = pos.data_ptr<int>();
+  p.doc = doc.data_ptr<int>();
+  p.row_scale = row_scale.data_ptr<float>();
+  p.par = par.data_ptr<float>();
+  p.sm = static_cast<float>(1.0 / std::sqrt(static_cast<double>(dk)));
+  return p;
+}
+
+Tensor poly_fwd(int64_t kind, int64_t dk, int64_t dv, const Tensor& qkv, std::vector<int64_t> cols, const Tensor& pos,
+                const Tensor& doc, const Tensor& row_scale, const Tensor& par, int64_t B, int64_t T, int64_t H) {
+  const c10::cuda::CUDAGuard guard(qkv.device());
+  check_bf16(qkv, "qkv");
+  TORCH_CHECK(qkv.dim() == 2 && qkv.stride(1) == 1 && qkv.size(0) == B * T, "qkv [B*T, ld]");
+  auto p = attn_params(cols, pos, doc, row_scale, par, B, T, H, dk);
+  auto y = torch::empty({B * T, H * dv}, qkv.options());
+  p.y = static_cast<__nv_bfloat16*>(y.data_ptr());
+  p.ldy = y.stride(0);
+  ttb::poly_attention_fwd(kind, dk, dv, qkv.data_ptr(), qkv.stride(0), p, cur_stream());
+  return y;
+}
+
+// returns (dqkv [B*T, ld] bf16 in the qkv layout, dpar [B*H, blocks, 4] fp32)
+std::vector<Tensor> poly_bwd(int64_t kind, int64_t dk, int64_t dv, const Tensor& qkv, std::vector<int64_t> cols,
+                             const Tensor& dout, const Tensor& pos, const Tensor& doc, const Tensor& doc_end,
+                             const Tensor& row_scale, const Tensor& par, int64_t B, int64_t T, int64_t H) {
+  const c10::cuda::CUDAGuard guard(qkv.device());
+  check_bf16(qkv, "qkv");
+  check_bf16(dout, "dout");
+  TORCH_CHECK(dout.dim() == 2 && dout.stride(1) == 1 && dout.size(0) == B * T && dout.size(1) == H * dv, "dout");
+  TORCH_CHECK(doc_end.scalar_type() == torch::kInt32 && doc_end.is_contiguous() && doc_end.numel() == B * T, "doc_end");
+  auto p = attn_params(cols, pos, doc, row_scale, par, B, T, H, dk);
+  auto dqkv = torch::zeros_like(qkv);
+  const int blocks = ttb::poly_attention_dpar_blocks(T);
+  auto dpar = torch::zeros({B * H, blocks, 4}, qkv.options().dtype(torch::kFloat32));
+  p.dq = static_cast<__nv_bfloat16*>(dqkv.data_ptr());
+  p.ldd = dqkv.stride(0);
+  p.dpar = dpar.data_ptr<float>();
+  ttb::poly_attention_bwd(kind, dk, dv, qkv.data_ptr(), qkv.stride(0), dout.data_ptr(), dout.stride(0),
+                          doc_end.data_ptr<int>(), p, cur_stream());
+  return {dqkv, dpar};
+}
+
 int64_t status() { return static_cast<int64_t>(ttb::status_read_and_reset()); }
 
 }  // namespace
@@ -129,4 +295,13 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("bilinear", &bilinear, "dual-B GEMM forming the bilinear hidden layer");
   m.def("bilinear_grad", &bilinear_grad, "dH GEMM fused with the bilinear backward");
   m.def("status", &status, "read and clear the device error word (bounded-wait timeouts)");
+  m.def("rmsnorm_fwd", &rmsnorm_fwd, "(group) RMSNorm: fp32 x -> bf16 y, fp32 rstd");
+  m.def("rmsnorm_bwd", &rmsnorm_bwd, "(group) RMSNorm backward; adds dx into the residual grad, returns dw");
+  m.def("rope_", &rope_, "in-place rotary embedding (or its inverse) on a bf16 [N, ld] buffer");
+  m.def("embed_fwd", &embed_fwd, "fp32 embedding gather");
+  m.def("embed_bwd", &embed_bwd, "deterministic embedding backward (accumulates into dW)");
+  m.def("ce_fwd", &ce_fwd, "fused linear + cross-entropy forward: per-row loss and lse");
+  m.def("ce_bwd_logits", &ce_bwd_logits, "fused logits recompute + softmax-grad epilogue");
+  m.def("poly_fwd", &poly_fwd, "tcgen05 polynomial attention forward");
+  m.def("poly_bwd", &poly_bwd, "tcgen05 polynomial attention backward (dq and dkv kernels)");
 }

@@ -1,0 +1,305 @@
+// Row-wise and elementwise kernels: (group) RMSNorm forward/backward with a fused residual-grad
+// accumulation, rotary embedding (forward / inverse) on the fused QKV buffer, deterministic
+// embedding backward, and the small reductions that finish them.
+#include <cuda_bf16.h>
+
+#include "../common/host.h"
+#include "../common/sm100.cuh"
+#include "rowops.h"
+
+namespace ttb {
+namespace {
+
+constexpr int kRowThreads = 256;
+constexpr int kVec = 4;
+constexpr int kMaxChunks = 8;  // d <= 8192
+constexpr int kMaxGroups = 8;
+
+__device__ __forceinline__ float block_sum(float v, float* red) {
+  // red: >= 32 floats of shared memory
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+  __syncthreads();
+  if (lane == 0) red[warp] = v;
+  __syncthreads();
+  float t = 0.f;
+  const int nw = blockDim.x / 32;
+  for (int i = 0; i < nw; ++i) t += red[i];
+  return t;
+}
+
+__device__ __forceinline__ void load4(const float* p, float (&v)[4]) {
+  const float4 u = *reinterpret_cast<const float4*>(p);
+  v[0] = u.x; v[1] = u.y; v[2] = u.z; v[3] = u.w;
+}
+__device__ __forceinline__ void load4(const __nv_bfloat16* p, float (&v)[4]) {
+  const uint2 u = *reinterpret_cast<const uint2*>(p);
+  v[0] = bf16_lo(u.x); v[1] = bf16_hi(u.x); v[2] = bf16_lo(u.y); v[3] = bf16_hi(u.y);
+}
+
+// y = bf16(x * rstd_g * w),  rstd_g = 1/sqrt(mean_{group}(x^2) + eps).  One CTA per row.
+__global__ void __launch_bounds__(kRowThreads) rmsnorm_fwd_kernel(const float* __restrict__ x,
+                                                                 const float* __restrict__ w,
+                                                                 __nv_bfloat16* __restrict__ y,
+                                                                 float* __restrict__ rstd, int N, int d, int G,
+                                                                 float eps) {
+  __shared__ float red[32];
+  const int gsize = d / G;
+  for (int row = blockIdx.x; row < N; row += gridDim.x) {
+    const float* xr = x + static_cast<long long>(row) * d;
+    float v[kMaxChunks][4];
+    float part[kMaxGroups];
+#pragma unroll
+    for (int g = 0; g < kMaxGroups; ++g) part[g] = 0.f;
+#pragma unroll
+    for (int c = 0; c < kMaxChunks; ++c) {
+      const int j = (c * kRowThreads + threadIdx.x) * kVec;
+      if (j < d) {
+        load4(xr + j, v[c]);
+        const float s = v[c][0] * v[c][0] + v[c][1] * v[c][1] + v[c][2] * v[c][2] + v[c][3] * v[c][3];
+        const int g = j / gsize;
+#pragma unroll
+        for (int q = 0; q < kMaxGroups; ++q)
+          if (q == g) part[q] += s;
+      }
+    }
+    float inv[kMaxGroups];
+    for (int g = 0; g < G; ++g) {
+      const float tot = block_sum(part[g], red);
+      inv[g] = rsqrtf(tot / gsize + eps);
+    }
+    if (threadIdx.x < G) rstd[static_cast<long long>(row) * G + threadIdx.x] = inv[threadIdx.x];
+    __nv_bfloat16* yr = y + static_cast<long long>(row) * d;
+#pragma unroll
+    for (int c = 0; c < kMaxChunks; ++c) {
+      const int j = (c * kRowThreads + threadIdx.x) * kVec;
+      if (j < d) {
+        const int g = j / gsize;
+        float r = inv[0];
+#pragma unroll
+        for (int q = 1; q < kMaxGroups; ++q)
+          if (q == g) r = inv[q];
+        float wv[4];
+        load4(w + j, wv);
+        uint2 o;
+        o.x = pack_bf16(v[c][0] * r * wv[0], v[c][1] * r * wv[1]);
+        o.y = pack_bf16(v[c][2] * r * wv[2], v[c][3] * r * wv[3]);
+        *reinterpret_cast<uint2*>(yr + j) = o;
+      }
+    }
+  }
+}
+
+// Backward of y = x * rstd * w (rstd depends on x):
+//   g = dy * w;  dx = rstd * (g - xhat * mean_group(g * xhat));  dw += dy * xhat
+// dx is added into dres (the fp32 residual-stream gradient) when accumulate != 0, else written.
+// dw partial sums per CTA go to dw_part[blockIdx.x][d] (reduced by dw_reduce_kernel).
+template <typename TDY>
+__global__ void __launch_bounds__(kRowThreads) rmsnorm_bwd_kernel(const TDY* __restrict__ dy,
+                                                                 const float* __restrict__ x,
+                                                                 const float* __restrict__ w,
+                                                                 const float* __restrict__ rstd,
+                                                                 float* __restrict__ dres, int accumulate,
+                                                                 float* __restrict__ dw_part, int N, int d, int G) {
+  __shared__ float red[32];
+  const int gsize = d / G;
+  float dw[kMaxChunks][4];
+#pragma unroll
+  for (int c = 0; c < kMaxChunks; ++c)
+#pragma unroll
+    for (int k = 0; k < 4; ++k) dw[c][k] = 0.f;
+  for (int row = blockIdx.x; row < N; row += gridDim.x) {
+    const long long base = static_cast<long long>(row) * d;
+    float xh[kMaxChunks][4], gg[kMaxChunks][4];
+    float part[kMaxGroups];
+#pragma unroll
+    for (int g = 0; g < kMaxGroups; ++g) part[g] = 0.f;
+#pragma unroll
+    for (int c = 0; c < kMaxChunks; ++c) {
+      const int j = (c * kRowThreads + threadIdx.x) * kVec;
+      if (j < d) {
+        const int g = j / gsize;
+        const float r = rstd[static_cast<long long>(row) * G + g];
+        float xv[4], dv[4], wv[4];
+        load4(x + base + j, xv);
+        load4(dy + base + j, dv);
+        load4(w + j, wv);
+        float s = 0.f;
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          xh[c][k] = xv[k] * r;
+          gg[c][k] = dv[k] * wv[k];
+          dw[c][k] += dv[k] * xh[c][k];
+          s += gg[c][k] * xh[c][k];
+        }
+#pragma unroll
+        for (int q = 0; q < kMaxGroups; ++q)
+          if (q == g) part[q] += s;
+      }
+    }
+    float mean[kMaxGroups];
+    for (int g = 0; g < G; ++g) mean[g] = block_sum(part[g], red) / gsize;
+#pragma unroll
+    for (int c = 0; c < kMaxChunks; ++c) {
+      const int j = (c * kRowThreads + threadIdx.x) * kVec;
+      if (j < d) {
+        const int g = j / gsize;
+        const float r = rstd[static_cast<long long>(row) * G + g];
+        float m = mean[0];
+#pragma unroll
+        for (int q = 1; q < kMaxGroups; ++q)
+          if (q == g) m = mean[q];
+        float4 o;
+        o.x = r * (gg[c][0] - xh[c][0] * m);
+        o.y = r * (gg[c][1] - xh[c][1] * m);
+        o.z = r * (gg[c][2] - xh[c][2] * m);
+        o.w = r * (gg[c][3] - xh[c][3] * m);
+        float4* dst = reinterpret_cast<float4*>(dres + base + j);
+        if (accumulate) {
+          const float4 prev = *dst;
+          o.x += prev.x; o.y += prev.y; o.z += prev.z; o.w += prev.w;
+        }
+        *dst = o;
+      }
+    }
+  }
+#pragma unroll
+  for (int c = 0; c < kMaxChunks; ++c) {
+    const int j = (c * kRowThreads + threadIdx.x) * kVec;
+    if (j < d)
+      *reinterpret_cast<float4*>(dw_part + static_cast<long long>(blockIdx.x) * d + j) =
+          make_float4(dw[c][0], dw[c][1], dw[c][2], dw[c][3]);
+  }
+}
+
+// out[j] (+)= sum_p part[p][j]   (fixed order over p: deterministic)
+__global__ void colsum_kernel(const float* __restrict__ part, int P, int d, float* __restrict__ out, int accumulate) {
+  const int j = blockIdx.x * blockDim.x + threadIdx.x;
+  if (j >= d) return;
+  float s = 0.f;
+  for (int p = 0; p < P; ++p) s += part[static_cast<long long>(p) * d + j];
+  out[j] = accumulate ? out[j] + s : s;
+}
+
+// Rotary embedding on the leading `rope_cols` columns of a [N, ld] bf16 buffer, in place.
+// Heads of width dk; pair (i, i + dk/2) of a head is rotated by angle pos * inv_freq[i].
+// inverse != 0 rotates by the negative angle (the backward of the forward rotation).
+__global__ void rope_kernel(__nv_bfloat16* __restrict__ buf, long long ld, int N, int rope_cols, int dk,
+                            const int* __restrict__ pos, const float* __restrict__ inv_freq, int inverse) {
+  const int half = dk / 2;
+  const long long pairs_per_row = rope_cols / 2;
+  const long long total = static_cast<long long>(N) * pairs_per_row;
+  for (long long t = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; t < total;
+       t += static_cast<long long>(gridDim.x) * blockDim.x) {
+    const int row = static_cast<int>(t / pairs_per_row);
+    const int pr = static_cast<int>(t % pairs_per_row);
+    const int head = pr / half;
+    const int i = pr % half;
+    const float ang = static_cast<float>(pos[row]) * inv_freq[i];
+    float s, c;
+    sincosf(ang, &s, &c);
+    if (inverse) s = -s;
+    __nv_bfloat16* p = buf + row * ld + static_cast<long long>(head) * dk + i;
+    const float a = __bfloat162float(p[0]);
+    const float b = __bfloat162float(p[half]);
+    p[0] = __float2bfloat16_rn(a * c - b * s);
+    p[half] = __float2bfloat16_rn(a * s + b * c);
+  }
+}
+
+// x[t, :] = W[idx[t], :]   (fp32 rows; d multiple of 4)
+__global__ void embed_fwd_kernel(const long long* __restrict__ idx, const float* __restrict__ W,
+                                 float* __restrict__ x, int N, int d) {
+  const int warps = blockDim.x / 32;
+  const int lane = threadIdx.x % 32;
+  for (int t = blockIdx.x * warps + threadIdx.x / 32; t < N; t += gridDim.x * warps) {
+    const float4* src = reinterpret_cast<const float4*>(W + idx[t] * static_cast<long long>(d));
+    float4* dst = reinterpret_cast<float4*>(x + static_cast<long long>(t) * d);
+    for (int j = lane; j < d / 4; j += 32) dst[j] = src[j];
+  }
+}
+
+// Deterministic embedding backward over tokens sorted by id (stable sort, so equal ids keep
+// their original order): the first position of each run sums the run's gradient rows in order.
+__global__ void embed_bwd_kernel(const long long* __restrict__ sorted_ids, const long long* __restrict__ order,
+                                 const float* __restrict__ dx, float* __restrict__ dW, int N, int d) {
+  const int warps = blockDim.x / 32;
+  const int lane = threadIdx.x % 32;
+  for (int s = blockIdx.x * warps + threadIdx.x / 32; s < N; s += gridDim.x * warps) {
+    const long long id = sorted_ids[s];
+    if (s > 0 && sorted_ids[s - 1] == id) continue;
+    int e = s + 1;
+    while (e < N && sorted_ids[e] == id) ++e;
+    float* dst = dW + id * static_cast<long long>(d);
+    for (int j = lane * 4; j < d; j += 128) {
+      float4 acc = *reinterpret_cast<float4*>(dst + j);
+      for (int q = s; q < e; ++q) {
+        const float4 g = *reinterpret_cast<const float4*>(dx + order[q] * static_cast<long long>(d) + j);
+        acc.x += g.x; acc.y += g.y; acc.z += g.z; acc.w += g.w;
+      }
+      *reinterpret_cast<float4*>(dst + j) = acc;
+    }
+  }
+}
+
+}  // namespace
+
+int rmsnorm_bwd_partials(int N) {
+  const int g = 2 * num_sms();
+  return N < g ? N : g;
+}
+
+void rmsnorm_fwd(const float* x, const float* w, void* y, float* rstd, int N, int d, int G, float eps,
+                 cudaStream_t stream) {
+  TTB_CHECK(d % 4 == 0 && d <= kRowThreads * kVec * kMaxChunks, "rmsnorm: d must be a multiple of 4 and <= 8192");
+  TTB_CHECK(G >= 1 && G <= kMaxGroups && d % G == 0 && (d / G) % 4 == 0, "rmsnorm: bad group count");
+  const int grid = N < 8 * num_sms() ? N : 8 * num_sms();
+  rmsnorm_fwd_kernel<<<grid, kRowThreads, 0, stream>>>(x, w, static_cast<__nv_bfloat16*>(y), rstd, N, d, G, eps);
+  TTB_CUDA_CHECK(cudaGetLastError());
+}
+
+void rmsnorm_bwd(const void* dy, bool dy_f32, const float* x, const float* w, const float* rstd, float* dres,
+                 bool accumulate, float* dw_part, float* dw, bool dw_accumulate, int N, int d, int G,
+                 cudaStream_t stream) {
+  TTB_CHECK(d % 4 == 0 && d <= kRowThreads * kVec * kMaxChunks, "rmsnorm: d must be a multiple of 4 and <= 8192");
+  const int grid = rmsnorm_bwd_partials(N);
+  if (dy_f32)
+    rmsnorm_bwd_kernel<float><<<grid, kRowThreads, 0, stream>>>(static_cast<const float*>(dy), x, w, rstd, dres,
+                                                                accumulate, dw_part, N, d, G);
+  else
+    rmsnorm_bwd_kernel<__nv_bfloat16><<<grid, kRowThreads, 0, stream>>>(
+        static_cast<const __nv_bfloat16*>(dy), x, w, rstd, dres, accumulate, dw_part, N, d, G);
+  TTB_CUDA_CHECK(cudaGetLastError());
+  colsum_kernel<<<(d + 255) / 256, 256, 0, stream>>>(dw_part, grid, d, dw, dw_accumulate);
+  TTB_CUDA_CHECK(cudaGetLastError());
+}
+
+void rope_apply(void* buf, long long ld, int N, int rope_cols, int dk, const int* pos, const float* inv_freq,
+                bool inverse, cudaStream_t stream) {
+  TTB_CHECK(dk % 2 == 0 && rope_cols % dk == 0, "rope: bad head layout");
+  const long long total = static_cast<long long>(N) * (rope_cols / 2);
+  long long blocks = (total + 255) / 256;
+  if (blocks > 16LL * num_sms()) blocks = 16LL * num_sms();
+  if (blocks < 1) blocks = 1;
+  rope_kernel<<<static_cast<int>(blocks), 256, 0, stream>>>(static_cast<__nv_bfloat16*>(buf), ld, N, rope_cols, dk,
+                                                             pos, inv_freq, inverse ? 1 : 0);
+  TTB_CUDA_CHECK(cudaGetLastError());
+}
+
+void embed_fwd(const long long* idx, const float* W, float* x, int N, int d, cudaStream_t stream) {
+  TTB_CHECK(d % 4 == 0, "embedding: d must be a multiple of 4");
+  const int grid = (N + 7) / 8 < 4 * num_sms() ? (N + 7) / 8 : 4 * num_sms();
+  embed_fwd_kernel<<<grid, 256, 0, stream>>>(idx, W, x, N, d);
+  TTB_CUDA_CHECK(cudaGetLastError());
+}
+
+void embed_bwd(const long long* sorted_ids, const long long* order, const float* dx, float* dW, int N, int d,
+               cudaStream_t stream) {
+  TTB_CHECK(d % 4 == 0, "embedding: d must be a multiple of 4");
+  const int grid = (N + 7) / 8 < 4 * num_sms() ? (N + 7) / 8 : 4 * num_sms();
+  embed_bwd_kernel<<<grid, 256, 0, stream>>>(sorted_ids, order, dx, dW, N, d);
+  TTB_CUDA_CHECK(cudaGetLastError());
+}
+
+}  // namespace ttb

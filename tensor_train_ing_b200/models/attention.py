@@ -50,10 +50,14 @@ def row_scale_vector(doc_ids: torch.Tensor, power: float) -> torch.Tensor:
     return torch.where(doc_ids >= 0, n.pow(-power), torch.zeros_like(n))
 
 
+def rope_inv_freq(dim: int, base: float, device=None) -> torch.Tensor:
+    """Rotation frequencies 1 / base^(2i/dim), i < dim/2 (fp32, the rounding the reference uses)."""
+    return 1.0 / (base ** (torch.arange(0, dim, 2, device=device, dtype=torch.float32) / dim))
+
+
 def rope_tables(positions: torch.Tensor, dim: int, base: float):
     """cos/sin tables of shape (B, 1, T, dim/2) for the half-split rotary embedding."""
-    freqs = base ** (-torch.arange(0, dim, 2, device=positions.device, dtype=torch.float32) / dim)
-    angle = positions.float().unsqueeze(-1) * freqs
+    angle = positions.float().unsqueeze(-1) * rope_inv_freq(dim, base, positions.device)
     return angle.cos().unsqueeze(1), angle.sin().unsqueeze(1)
 
 

@@ -1,0 +1,130 @@
+"""Fused (sm_100a) execution of ``TensorLM``: context tables, block forward and model forward.
+
+Per block (reference tnlm/model.py:137-144, 67-101):
+  h   = norm_in(x)                       RMSNorm / GroupRMSNorm kernel -> bf16 (other norms: module math)
+  qkv = h [q1|k1|q2|k2|v]^T              one tcgen05 GEMM over the concatenated bf16 weights, RoPE in place
+  y   = PolyAttention(qkv)               tcgen05 attention kernels
+  x   = x + alpha * o(y)                 GEMM with the residual add in its epilogue (fp32 stream)
+  x   = x + alpha * D(L h' * R h')       dual-B bilinear GEMM, then the down GEMM with fused residual
+With an output norm (branch_rms / sandwich_rms) the branch stays bf16 and the norm module and the
+residual add run as in the reference.  Spectral layers use their effective weights every step.
+"""
+from __future__ import annotations
+
+import torch
+import torch.nn as nn
+
+from ..models.attention import rope_inv_freq, row_scale_vector
+from ..models.normalization import GroupRMSNorm, RMSNorm, SpectralLinear
+from . import fused
+from .weights import ComputedWeights, group_for
+
+
+def _weights(owner, name, linears):
+    if any(isinstance(l, SpectralLinear) for l in linears):
+        return ComputedWeights([l.effective_weight() for l in linears])
+    return group_for(owner, name, [l.weight for l in linears])
+
+
+def fused_context(model, doc_ids, pos):
+    cfg = model.cfg
+    tables = fused.attention_tables(doc_ids)
+    row_scale = {p: row_scale_vector(doc_ids, p).contiguous().view(-1) for p in model._row_powers()}
+    return {"fused": True, "tables": tables, "row_scale": row_scale,
+            "pos32": tables["pos32"], "inv_freq": rope_inv_freq(cfg.d_key, cfg.rope_base, doc_ids.device)}
+
+
+def norm_to_bf16(norm: nn.Module, x: torch.Tensor) -> torch.Tensor:
+    """Apply an input norm to the fp32 stream and return the bf16 GEMM operand."""
+    if isinstance(norm, nn.Identity):
+        return x.to(torch.bfloat16)
+    if isinstance(norm, (RMSNorm, GroupRMSNorm)) and norm.denom_mode is None:
+        groups = norm.groups if isinstance(norm, GroupRMSNorm) else 1
+        return fused.rms_norm(x, norm.weight, groups, norm.eps)
+    return norm(x).to(torch.bfloat16)
+
+
+def _record_bound(attn, qkv, cols, N):
+    cfg = attn.cfg
+    H, dk = cfg.heads, cfg.d_key
+    bounds = {}
+    pairs = (("S1", cols[0], cols[1]),) + ((("S2", cols[2], cols[3]),) if attn.kind != "offset_square" else ())
+    with torch.no_grad():
+        for name, cq, ck in pairs:
+            qn = qkv[:, cq:cq + H * dk].float().view(N, H, dk).norm(dim=-1).amax(0)
+            kn = qkv[:, ck:ck + H * dk].float().view(N, H, dk).norm(dim=-1).amax(0)
+            bounds[name] = qn * kn / dk ** 0.5
+    attn.last_score_bound = bounds
+
+
+def attention_branch(blk, h, ctx):
+    a = blk.attn
+    cfg = a.cfg
+    H, dk, dv = cfg.heads, cfg.d_key, cfg.d_value
+    projs = a.projections()
+    grp = _weights(a, "qkv", projs)
+    two = a.kind != "offset_square"
+    n_qk = 4 if two else 2
+    qkv = fused.qkv_rope(h, grp, n_qk * H * dk, dk, ctx["pos32"], ctx["inv_freq"])
+    if two:
+        cols = [0, H * dk, 2 * H * dk, 3 * H * dk, 4 * H * dk]
+    else:
+        cols = [0, H * dk, 0, H * dk, 2 * H * dk]
+    if a.record_score_bound:
+        _record_bound(a, qkv, cols, h.shape[0])
+    kpar = getattr(a, "b", None) if a.kind == "offset_square" else getattr(a, "coef", None)
+    return fused.poly_attention(qkv, kpar, a.kind, dk, dv, H, cols, ctx["tables"], ctx["row_scale"][a.row_power])
+
+
+def block_forward(blk, x, ctx):
+    """x: fp32 [N, d] residual stream."""
+    a, m = blk.attn, blk.mlp
+    if "attn" not in blk.ablate:
+        y = attention_branch(blk, norm_to_bf16(blk.attn_in, x), ctx)
+        og = _weights(a, "o", [a.o])
+        if isinstance(blk.attn_out, nn.Identity):
+            x = fused.linear(y, og, residual=x, alpha=blk.alpha, bias=a.o.bias)
+        else:
+            x = x + blk.alpha * blk.attn_out(fused.linear(y, og, bias=a.o.bias))
+    if "mlp" not in blk.ablate:
+        h = norm_to_bf16(blk.mlp_in, x)
+        gl, gr, gd = _weights(m, "l", [m.l]), _weights(m, "r", [m.r]), _weights(m, "d", [m.d])
+        mode = 1 if m.kind == "swiglu" else 0
+        if isinstance(blk.mlp_out, nn.Identity):
+            x = fused.bilinear_mlp(h, gl, gr, gd, residual=x, alpha=blk.alpha, mode=mode,
+                                   bl=m.l.bias, br=m.r.bias, bd=m.d.bias)
+        else:
+            branch = fused.bilinear_mlp(h, gl, gr, gd, mode=mode, bl=m.l.bias, br=m.r.bias, bd=m.d.bias)
+            x = x + blk.alpha * blk.mlp_out(branch)
+    return x
+
+
+def model_forward(model, idx, ctx, targets, reduction):
+    cfg = model.cfg
+    B, T = idx.shape
+    x = fused.embedding(idx.reshape(-1), group_for(model, "embed", [model.embed.weight]))
+    ckpt = cfg.activation_checkpointing and model.training and torch.is_grad_enabled()
+    for blk in model.blocks:
+        if ckpt:
+            x = torch.utils.checkpoint.checkpoint(block_forward, blk, x, ctx, use_reentrant=False)
+        else:
+            x = blk(x, ctx)
+    h = norm_to_bf16(model.final_norm, x)
+    V = cfg.vocab_size
+    ug = group_for(model, "unembed", [model.unembed.weight])
+    alpha = model.logit_multiplier
+    if targets is not None and cfg.loss_chunk_tokens > 0:
+        loss = fused.linear_cross_entropy(h, targets.reshape(-1), ug, V, alpha, cfg.loss_chunk_tokens)
+        logits = None
+    else:
+        logits = fused.linear(h, ug)[:, :V].view(B, T, V)
+        if alpha != 1.0:
+            logits = logits * alpha
+        if targets is None:
+            return logits
+        loss = torch.nn.functional.cross_entropy(logits.float().flatten(0, 1), targets.flatten(),
+                                                 ignore_index=-100, reduction="sum")
+    n = (targets != -100).sum()
+    if reduction == "sum":
+        return logits, loss, n
+    return logits, loss / n.clamp_min(1)

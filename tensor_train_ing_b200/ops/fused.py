@@ -1,0 +1,301 @@
+"""Autograd functions over the sm_100a kernels (tcgen05 GEMMs, polynomial attention, norms,
+fused linear-CE, embedding).  Every function here runs only on the compiled library; there is
+no PyTorch fallback inside (see ``ops._ext``).
+
+Conventions: the residual stream is fp32 [N, d]; GEMM operands are bf16; weight gradients are
+accumulated through ``WeightGroup.sink_grad`` (fp32, in the GEMM epilogue).
+"""
+from __future__ import annotations
+
+import torch
+
+from ._ext import lib
+
+
+def _mm(a, b, out, c=None, alpha=1.0, beta=0.0, bias=None):
+    lib().mm(a, b, out, c, float(alpha), float(beta), bias)
+    return out
+
+
+# ============================================================================ RMSNorm
+class RMSNormFn(torch.autograd.Function):
+    """y = bf16(x / rms_g(x) * w) for fp32 x [N, d]; groups > 1 = GroupRMSNorm."""
+
+    @staticmethod
+    def forward(ctx, x, w, groups, eps):
+        y, rstd = lib().rmsnorm_fwd(x, w, int(groups), float(eps))
+        ctx.save_for_backward(x, w, rstd)
+        ctx.groups = int(groups)
+        return y
+
+    @staticmethod
+    def backward(ctx, dy):
+        x, w, rstd = ctx.saved_tensors
+        dx = torch.empty_like(x)
+        dw = lib().rmsnorm_bwd(dy.contiguous(), x, w, rstd, dx, False, ctx.groups)
+        return dx, dw, None, None
+
+
+def rms_norm(x, w, groups=1, eps=1e-6):
+    return RMSNormFn.apply(x.contiguous(), w.contiguous(), groups, eps)
+
+
+# ============================================================================ linear
+class LinearFn(torch.autograd.Function):
+    """out = residual + alpha * (x W^T + b)  (fp32, residual given)  or  bf16(x W^T + b).
+
+    x: bf16 [N, d_in]; ``group`` provides the bf16 weight and the gradient sink."""
+
+    @staticmethod
+    def forward(ctx, x, residual, bias, group, alpha, *weights):
+        w16 = group.bf16()
+        N = x.shape[0]
+        if residual is not None:
+            out = torch.empty(N, w16.shape[0], device=x.device, dtype=torch.float32)
+            _mm(x, w16.t(), out, c=residual, alpha=alpha, beta=1.0, bias=bias)
+        else:
+            out = torch.empty(N, w16.shape[0], device=x.device, dtype=torch.bfloat16)
+            _mm(x, w16.t(), out, alpha=alpha, bias=bias)
+        ctx.save_for_backward(x)
+        ctx.group, ctx.alpha, ctx.has_res, ctx.has_bias = group, alpha, residual is not None, bias is not None
+        return out
+
+    @staticmethod
+    def backward(ctx, dout):
+        (x,) = ctx.saved_tensors
+        group, alpha = ctx.group, ctx.alpha
+        # gradient of the branch output, as the bf16 operand of the backward GEMMs
+        g = (dout * alpha).to(torch.bfloat16) if (alpha != 1.0 or dout.dtype != torch.bfloat16) else dout
+        g = g.contiguous()
+        w16 = group.bf16()
+        dx = torch.empty_like(x)
+        _mm(g, w16, dx)
+        grads = group.sink_grad(lambda out, beta: _mm(g.t(), x, out, c=out, beta=beta))
+        dres = dout if ctx.has_res else None
+        dbias = g.float().sum(0) if ctx.has_bias else None
+        return (dx, dres, dbias, None, None, *grads)
+
+
+def linear(x, group, residual=None, alpha=1.0, bias=None):
+    return LinearFn.apply(x, residual, bias, group, float(alpha), *group.params)
+
+
+# ============================================================================ QKV + RoPE
+class QKVRopeFn(torch.autograd.Function):
+    """qkv = x W_cat^T (bf16 [N, sum rows]) with RoPE applied in place to the first rope_cols columns."""
+
+    @staticmethod
+    def forward(ctx, x, group, rope_cols, dk, pos32, inv_freq, *weights):
+        w16 = group.bf16()
+        qkv = torch.empty(x.shape[0], w16.shape[0], device=x.device, dtype=torch.bfloat16)
+        _mm(x, w16.t(), qkv)
+        if rope_cols:
+            lib().rope_(qkv, int(rope_cols), int(dk), pos32, inv_freq, False)
+        ctx.save_for_backward(x, pos32, inv_freq)
+        ctx.group, ctx.rope_cols, ctx.dk = group, rope_cols, dk
+        return qkv
+
+    @staticmethod
+    def backward(ctx, dqkv):
+        x, pos32, inv_freq = ctx.saved_tensors
+        # the attention backward hands over a fresh buffer it owns: undo RoPE in place there
+        owned = getattr(dqkv, "_ttb_owned", False) and dqkv.is_contiguous()
+        g = dqkv if owned else dqkv.contiguous().clone()
+        if ctx.rope_cols:
+            lib().rope_(g, int(ctx.rope_cols), int(ctx.dk), pos32, inv_freq, True)
+        w16 = ctx.group.bf16()
+        dx = torch.empty(x.shape[0], x.shape[1], device=x.device, dtype=torch.float32)
+        _mm(g, w16, dx)
+        grads = ctx.group.sink_grad(lambda out, beta: _mm(g.t(), x, out, c=out, beta=beta))
+        return (dx, None, None, None, None, None, *grads)
+
+
+def qkv_rope(x, group, rope_cols, dk, pos32, inv_freq):
+    return QKVRopeFn.apply(x, group, rope_cols, dk, pos32, inv_freq, *group.params)
+
+
+# ============================================================================ polynomial attention
+KIND_ID = {"signed_product": 0, "offset_square": 1, "lower_degree_mix": 2}
+
+
+def attention_tables(doc_ids: torch.Tensor):
+    """int32 position-in-document, document id and exclusive document end for every token."""
+    from ..models.attention import doc_positions
+    B, T = doc_ids.shape
+    pos = doc_positions(doc_ids)
+    t = torch.arange(T, device=doc_ids.device).expand(B, T)
+    last = torch.ones_like(doc_ids, dtype=torch.bool)
+    last[:, :-1] = doc_ids[:, 1:] != doc_ids[:, :-1]
+    end_here = torch.where(last, t + 1, torch.full_like(t, T))
+    doc_end = end_here.flip(-1).cummin(-1).values.flip(-1)
+    return {"pos": pos, "pos32": pos.to(torch.int32).contiguous().view(-1),
+            "doc32": doc_ids.to(torch.int32).contiguous().view(-1),
+            "doc_end32": doc_end.to(torch.int32).contiguous().view(-1), "B": B, "T": T}
+
+
+class PolyAttentionFn(torch.autograd.Function):
+    """y [N, H*dv] = polynomial attention of the fused qkv buffer (see csrc/attn)."""
+
+    @staticmethod
+    def forward(ctx, qkv, kpar, kind, dk, dv, H, cols, tables, row_scale):
+        kid = KIND_ID[kind]
+        par = torch.zeros(H, 4, device=qkv.device, dtype=torch.float32)
+        if kind == "offset_square":
+            par[:, 0] = kpar.detach().float()
+        elif kind == "lower_degree_mix":
+            par.copy_(kpar.detach().float())
+        y = lib().poly_fwd(kid, dk, dv, qkv, list(cols), tables["pos32"], tables["doc32"], row_scale, par,
+                           tables["B"], tables["T"], H)
+        ctx.save_for_backward(qkv, par, row_scale)
+        ctx.meta = (kind, kid, dk, dv, H, list(cols), tables, kpar is not None)
+        return y
+
+    @staticmethod
+    def backward(ctx, dy):
+        qkv, par, row_scale = ctx.saved_tensors
+        kind, kid, dk, dv, H, cols, tables, has_par = ctx.meta
+        dqkv, dpar = lib().poly_bwd(kid, dk, dv, qkv, cols, dy.contiguous(), tables["pos32"], tables["doc32"],
+                                    tables["doc_end32"], row_scale, par, tables["B"], tables["T"], H)
+        dqkv._ttb_owned = True
+        dk_par = None
+        if has_par:
+            g = dpar.view(tables["B"], H, -1, 4).sum(dim=(0, 2))  # fixed-order reduction
+            dk_par = g[:, 0].clone() if kind == "offset_square" else g
+        return dqkv, dk_par, None, None, None, None, None, None, None
+
+
+def poly_attention(qkv, kpar, kind, dk, dv, H, cols, tables, row_scale):
+    return PolyAttentionFn.apply(qkv, kpar, kind, dk, dv, H, cols, tables, row_scale)
+
+
+# ============================================================================ bilinear MLP
+class BilinearMLPFn(torch.autograd.Function):
+    """out = residual + alpha * D((x L^T + bl) * (x R^T + br)) + alpha*bd  (mode 0)
+    or with silu on the left factor (mode 1, the SwiGLU control).  x: bf16 [N, d]."""
+
+    @staticmethod
+    def forward(ctx, x, residual, bl, br, bd, g_l, g_r, g_d, alpha, mode, *weights):
+        wl, wr = g_l.bf16(), g_r.bf16()
+        wd = g_d.bf16()
+        N, F_ = x.shape[0], wl.shape[0]
+        h = torch.empty(N, F_, device=x.device, dtype=torch.bfloat16)
+        l = torch.empty_like(h)
+        r = torch.empty_like(h)
+        lib().bilinear(x, wl, wr, bl, br, int(mode), h, l, r)
+        if residual is not None:
+            out = torch.empty(N, wd.shape[0], device=x.device, dtype=torch.float32)
+            _mm(h, wd.t(), out, c=residual, alpha=alpha, beta=1.0, bias=bd)
+        else:
+            out = torch.empty(N, wd.shape[0], device=x.device, dtype=torch.bfloat16)
+            _mm(h, wd.t(), out, alpha=alpha, bias=bd)
+        ctx.save_for_backward(x, h, l, r)
+        ctx.groups = (g_l, g_r, g_d)
+        ctx.alpha, ctx.mode, ctx.has_res = alpha, mode, residual is not None
+        ctx.has_bias = bl is not None
+        return out
+
+    @staticmethod
+    def backward(ctx, dout):
+        x, h, l, r = ctx.saved_tensors
+        g_l, g_r, g_d = ctx.groups
+        g = (dout * ctx.alpha).to(torch.bfloat16).contiguous()
+        wd = g_d.bf16()
+        dl = torch.empty_like(l)
+        dr = torch.empty_like(r)
+        lib().bilinear_grad(g, wd, l, r, dl, dr, int(ctx.mode))
+        grads_d = g_d.sink_grad(lambda out, beta: _mm(g.t(), h, out, c=out, beta=beta))
+        dx = torch.empty(x.shape[0], x.shape[1], device=x.device, dtype=torch.float32)
+        _mm(dl, g_l.bf16(), dx)
+        _mm(dr, g_r.bf16(), dx, c=dx, beta=1.0)
+        grads_l = g_l.sink_grad(lambda out, beta: _mm(dl.t(), x, out, c=out, beta=beta))
+        grads_r = g_r.sink_grad(lambda out, beta: _mm(dr.t(), x, out, c=out, beta=beta))
+        dres = dout if ctx.has_res else None
+        dbl = dbr = dbd = None
+        if ctx.has_bias:
+            dbl, dbr, dbd = dl.float().sum(0), dr.float().sum(0), g.float().sum(0)
+        return (dx, dres, dbl, dbr, dbd, None, None, None, None, None, *grads_l, *grads_r, *grads_d)
+
+
+def bilinear_mlp(x, g_l, g_r, g_d, residual=None, alpha=1.0, mode=0, bl=None, br=None, bd=None):
+    return BilinearMLPFn.apply(x, residual, bl, br, bd, g_l, g_r, g_d, float(alpha), int(mode),
+                               *g_l.params, *g_r.params, *g_d.params)
+
+
+# ============================================================================ embedding
+class EmbeddingFn(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, idx, group, weight):
+        ctx.save_for_backward(idx)
+        ctx.group = group
+        return lib().embed_fwd(idx.contiguous().view(-1), weight.detach().contiguous())
+
+    @staticmethod
+    def backward(ctx, dx):
+        (idx,) = ctx.saved_tensors
+        dx = dx.contiguous().float()
+
+        def compute(out, beta):
+            if beta == 0.0:
+                out.zero_()
+            lib().embed_bwd(idx.contiguous().view(-1), dx, out)
+
+        (g,) = ctx.group.sink_grad(compute)
+        return None, None, g
+
+
+def embedding(idx, group):
+    return EmbeddingFn.apply(idx, group, group.params[0])
+
+
+# ============================================================================ fused linear + CE
+class LinearCEFn(torch.autograd.Function):
+    """Summed cross-entropy of (alpha * x W[:V]^T) against targets (-100 ignored), chunked over rows.
+
+    Forward keeps only the per-row log-sum-exp; backward recomputes each chunk's logits in the
+    GEMM and writes bf16 dlogits (padded to W's rows), then dx = dlogits W, dW += dlogits^T x."""
+
+    @staticmethod
+    def forward(ctx, x, targets, group, V, alpha, chunk, weight):
+        w16 = group.bf16()
+        N = x.shape[0]
+        lse = torch.empty(N, device=x.device, dtype=torch.float32)
+        total = torch.zeros((), device=x.device, dtype=torch.float32)
+        for s in range(0, N, chunk):
+            e = min(N, s + chunk)
+            loss_rows, l = lib().ce_fwd(x[s:e], w16, int(V), float(alpha), targets[s:e])
+            lse[s:e] = l
+            total += loss_rows.sum()
+        ctx.save_for_backward(x, targets, lse)
+        ctx.group, ctx.V, ctx.alpha, ctx.chunk = group, V, alpha, chunk
+        return total
+
+    @staticmethod
+    def backward(ctx, g):
+        x, targets, lse = ctx.saved_tensors
+        group, V, alpha, chunk = ctx.group, ctx.V, ctx.alpha, ctx.chunk
+        w16 = group.bf16()
+        Vp = w16.shape[0]
+        g32 = g.detach().float().reshape(1).contiguous()
+        N = x.shape[0]
+        dx = torch.empty(N, x.shape[1], device=x.device, dtype=torch.float32)
+        dlog = torch.empty(min(chunk, N), Vp, device=x.device, dtype=torch.bfloat16)
+        acc = None
+        for s in range(0, N, chunk):
+            e = min(N, s + chunk)
+            d = dlog[: e - s]
+            lib().ce_bwd_logits(x[s:e], w16, int(V), float(alpha), targets[s:e], lse[s:e], g32, d)
+            _mm(d, w16, dx[s:e])
+
+            def compute(out, beta, d=d, s=s, e=e):
+                _mm(d.t(), x[s:e], out, c=out, beta=beta)
+
+            # each chunk goes through the sink: the first may overwrite, later ones accumulate
+            (gw,) = group.sink_grad(compute)
+            if gw is not None:  # not accumulated in place: keep a running sum for autograd
+                acc = gw if acc is None else acc + gw
+        return dx, None, None, None, None, None, acc
+
+
+def linear_cross_entropy(x, targets, group, V, alpha=1.0, chunk=8192):
+    return LinearCEFn.apply(x.contiguous(), targets.contiguous().view(-1), group, int(V), float(alpha), int(chunk),
+                            group.params[0])

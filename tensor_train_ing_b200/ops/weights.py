@@ -1,0 +1,107 @@
+"""Weight groups: bf16 operand caches and fused fp32 gradient accumulation for the sm_100a ops.
+
+Parameters stay fp32 masters (as under the reference's bf16 autocast).  A ``WeightGroup`` is a
+list of parameters that one GEMM consumes together (e.g. q1, k1, q2, k2, v of a layer):
+
+* ``bf16()`` returns the row-concatenated bf16 copy, rebuilt only when a parameter changed
+  (tracked through the tensors' version counters), i.e. once per optimizer step rather than
+  once per micro-batch as autocast would;
+* ``sink_grad(compute)`` runs the weight-gradient GEMM straight into one fp32 buffer
+  ([rows, d_in]) whose row blocks are attached as the parameters' ``.grad`` views: the first
+  micro-batch of a step overwrites (beta = 0), later ones accumulate in the GEMM epilogue
+  (beta = 1), so no separate gradient-accumulation kernel runs.  If the parameters' grads are
+  not this group's views (set by someone else), the gradient is returned to autograd instead.
+"""
+from __future__ import annotations
+
+import torch
+
+
+class WeightGroup:
+    def __init__(self, params: list[torch.Tensor]):
+        self.params = list(params)
+        d_in = {p.shape[-1] for p in self.params}
+        if len(d_in) != 1:
+            raise ValueError("a weight group needs a common input dimension")
+        self.rows = [p.shape[0] for p in self.params]
+        self.d_in = d_in.pop()
+        self._cache = None
+        self._key = None
+        self._grad = None
+
+    # ------------------------------------------------------------------ forward operand
+    def _version_key(self):
+        return tuple((p.data_ptr(), p._version) for p in self.params)
+
+    def bf16(self) -> torch.Tensor:
+        key = self._version_key()
+        if self._cache is None or key != self._key:
+            with torch.no_grad():
+                if self._cache is None or self._cache.device != self.params[0].device:
+                    self._cache = torch.empty(sum(self.rows), self.d_in, device=self.params[0].device,
+                                              dtype=torch.bfloat16)
+                row = 0
+                for p, n in zip(self.params, self.rows):
+                    self._cache[row:row + n].copy_(p.detach())
+                    row += n
+            self._key = key
+        return self._cache
+
+    # ------------------------------------------------------------------ backward sink
+    def _grad_buffer(self):
+        dev = self.params[0].device
+        if self._grad is None or self._grad.device != dev:
+            self._grad = torch.empty(sum(self.rows), self.d_in, device=dev, dtype=torch.float32)
+        return self._grad
+
+    def _views(self, buf):
+        return list(buf.split(self.rows, dim=0))
+
+    def sink_grad(self, compute):
+        """compute(out_fp32 [rows, d_in], beta) writes (beta=0) or adds (beta=1) the weight grad.
+
+        Returns the list of gradients to hand to autograd (None where accumulated in place)."""
+        leafs = all(p.is_leaf and p.requires_grad for p in self.params)
+        if leafs:
+            buf = self._grad_buffer()
+            views = self._views(buf)
+            if all(p.grad is None for p in self.params):
+                compute(buf, 0.0)
+                for p, v in zip(self.params, views):
+                    p.grad = v
+                return [None] * len(self.params)
+            if all(p.grad is not None and p.grad.data_ptr() == v.data_ptr() and p.grad.shape == v.shape
+                   for p, v in zip(self.params, views)):
+                compute(buf, 1.0)
+                return [None] * len(self.params)
+        out = torch.empty(sum(self.rows), self.d_in, device=self.params[0].device, dtype=torch.float32)
+        compute(out, 0.0)
+        return [g.to(p.dtype) for g, p in zip(self._views(out), self.params)]
+
+
+class ComputedWeights:
+    """Same interface for weights that are computed every forward (e.g. spectral effective
+    weights): no caching, gradients always go back through autograd."""
+
+    def __init__(self, tensors: list[torch.Tensor]):
+        self.params = list(tensors)
+        self.rows = [t.shape[0] for t in self.params]
+        self.d_in = self.params[0].shape[-1]
+
+    def bf16(self) -> torch.Tensor:
+        return torch.cat([t.detach() for t in self.params], dim=0).to(torch.bfloat16)
+
+    def sink_grad(self, compute):
+        out = torch.empty(sum(self.rows), self.d_in, device=self.params[0].device, dtype=torch.float32)
+        compute(out, 0.0)
+        return [g.to(t.dtype) for g, t in zip(out.split(self.rows, dim=0), self.params)]
+
+
+def group_for(owner, name: str, params: list[torch.Tensor]):
+    """Cached WeightGroup stored on ``owner`` (rebuilt if the parameter objects changed)."""
+    attr = f"_ttb_group_{name}"
+    grp = getattr(owner, attr, None)
+    if grp is None or len(grp.params) != len(params) or any(a is not b for a, b in zip(grp.params, params)):
+        grp = WeightGroup(params)
+        object.__setattr__(owner, attr, grp)
+    return grp

@@ -1,0 +1,155 @@
+"""sm_100a kernels vs plain PyTorch fp32/fp64 references of the same op (tolerances fixed up
+front, as in the reference's kernel acceptance tests: bf16 relative error < 3e-2)."""
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+from tensor_train_ing_b200.models.attention import (apply_rope, polynomial_attention, rope_tables, row_scale_mask,
+                                                    row_scale_vector, visible_mask, doc_positions)
+from tensor_train_ing_b200.ops import fused
+from tensor_train_ing_b200.ops._ext import lib
+
+
+def rel(a, b):
+    a, b = a.double(), b.double()
+    return ((a - b).norm() / b.norm().clamp_min(1e-30)).item()
+
+
+def make_docs(B, T, seed=0, pad=True):
+    g = torch.Generator().manual_seed(seed)
+    docs = torch.empty(B, T, dtype=torch.long)
+    for b in range(B):
+        t, d = 0, 0
+        while t < T:
+            n = int(torch.randint(5, max(6, T // 2), (1,), generator=g))
+            docs[b, t:t + n] = d
+            t += n
+            d += 1
+        if pad and b == B - 1:
+            docs[b, T - 7:] = -torch.arange(1, 8)  # unique negative ids = padding
+    return docs
+
+
+def dense_attention(kind, qkv, cols, B, T, H, dk, dv, docs, power, kpar):
+    def head(c, d):
+        return qkv[:, c:c + H * d].double().view(B, T, H, d).transpose(1, 2)
+    q1, k1 = head(cols[0], dk), head(cols[1], dk)
+    q2, k2 = (head(cols[2], dk), head(cols[3], dk)) if kind != "offset_square" else (None, None)
+    v = head(cols[4], dv)
+    C = row_scale_mask(visible_mask(docs), power, dtype=torch.float64)
+    coef = kpar.double() if kind == "lower_degree_mix" else None
+    b = kpar.double() if kind == "offset_square" else None
+    y = polynomial_attention(kind, q1, k1, q2, k2, v, C, coef=coef, b=b)
+    return y.transpose(1, 2).reshape(B * T, H * dv)
+
+
+@pytest.mark.parametrize("kind", ["signed_product", "offset_square", "lower_degree_mix"])
+@pytest.mark.parametrize("dk", [64, 128])
+@pytest.mark.parametrize("B,T", [(2, 200), (1, 77), (1, 384)])
+def test_poly_attention_fwd_bwd(kind, dk, B, T):
+    torch.manual_seed(0)
+    H, dv = 2, dk
+    dev = "cuda"
+    nqk = 4 if kind != "offset_square" else 2
+    cols = [0, H * dk, 2 * H * dk, 3 * H * dk, 4 * H * dk] if nqk == 4 else [0, H * dk, 0, H * dk, 2 * H * dk]
+    width = nqk * H * dk + H * dv
+    qkv = (torch.randn(B * T, width, device=dev) * 0.7).bfloat16().requires_grad_()
+    docs = make_docs(B, T).to(dev)
+    power = 1.0 if kind == "offset_square" else 0.5
+    tables = fused.attention_tables(docs)
+    rs = row_scale_vector(docs, power).contiguous().view(-1)
+    if kind == "offset_square":
+        kpar = torch.full((H,), 0.7, device=dev, requires_grad=True)
+    elif kind == "lower_degree_mix":
+        kpar = torch.tensor([[0.1, 0.3, -0.2, 1.0]], device=dev).repeat(H, 1).requires_grad_()
+    else:
+        kpar = None
+    y = fused.poly_attention(qkv, kpar, kind, dk, dv, H, cols, tables, rs)
+    gy = torch.randn_like(y)
+    y.backward(gy)
+    torch.cuda.synchronize()
+    assert lib().status() == 0
+    qkv_ref = qkv.detach().double().requires_grad_()
+    kpar_ref = kpar.detach().double().requires_grad_() if kpar is not None else None
+    y_ref = dense_attention(kind, qkv_ref, cols, B, T, H, dk, dv, docs, power, kpar_ref)
+    y_ref.backward(gy.double())
+    assert rel(y.float(), y_ref) < 3e-2
+    assert rel(qkv.grad.float(), qkv_ref.grad) < 3e-2
+    if kpar is not None:
+        assert rel(kpar.grad, kpar_ref.grad) < 3e-2
+
+
+def test_rmsnorm_fwd_bwd_groups():
+    torch.manual_seed(1)
+    for groups, d in ((1, 512), (4, 2048), (1, 6144)):
+        x = torch.randn(300, d, device="cuda", requires_grad=True)
+        w = (1 + 0.1 * torch.randn(d, device="cuda")).requires_grad_()
+        y = fused.rms_norm(x, w, groups, 1e-6)
+        gy = torch.randn(300, d, device="cuda").bfloat16()
+        y.backward(gy)
+        xr, wr = x.detach().double().requires_grad_(), w.detach().double().requires_grad_()
+        xg = xr.unflatten(-1, (groups, -1))
+        r = (xg.square().mean(-1, keepdim=True) + 1e-6).sqrt()
+        yr = (xg / r).flatten(-2) * wr
+        yr.backward(gy.double())
+        assert rel(y.float(), yr) < 1e-2
+        assert rel(x.grad, xr.grad) < 1e-2
+        assert rel(w.grad, wr.grad) < 1e-2
+
+
+def test_rope_roundtrip():
+    torch.manual_seed(2)
+    B, T, H, dk = 2, 100, 3, 64
+    docs = make_docs(B, T, pad=False).cuda()
+    pos = doc_positions(docs)
+    qk = torch.randn(B * T, 2 * H * dk, device="cuda").bfloat16()
+    buf = qk.clone()
+    from tensor_train_ing_b200.models.attention import rope_inv_freq
+    inv = rope_inv_freq(dk, 10000.0, "cuda")
+    lib().rope_(buf, 2 * H * dk, dk, pos.to(torch.int32).contiguous().view(-1), inv, False)
+    cos, sin = rope_tables(pos, dk, 10000.0)
+    ref = apply_rope(qk.float().view(B, T, 2 * H, dk).transpose(1, 2), cos, sin).transpose(1, 2).reshape(B * T, -1)
+    assert rel(buf.float(), ref) < 1e-2
+    lib().rope_(buf, 2 * H * dk, dk, pos.to(torch.int32).contiguous().view(-1), inv, True)
+    assert rel(buf.float(), qk.float()) < 2e-2
+
+
+def test_linear_ce_matches_torch():
+    torch.manual_seed(3)
+    N, d, V, Vp = 700, 256, 1000, 1024
+    from tensor_train_ing_b200.ops.weights import WeightGroup
+    w = torch.nn.Parameter(torch.randn(Vp, d, device="cuda") * 0.05)
+    x = torch.randn(N, d, device="cuda").bfloat16().requires_grad_()
+    tgt = torch.randint(0, V, (N,), device="cuda")
+    tgt[::7] = -100
+    grp = WeightGroup([w])
+    loss = fused.linear_cross_entropy(x, tgt, grp, V, alpha=0.5, chunk=256)
+    loss.backward()
+    xr = x.detach().double().requires_grad_()
+    wr = w.detach().double().requires_grad_()
+    logits = 0.5 * (xr @ wr[:V].t())
+    lr = torch.nn.functional.cross_entropy(logits, tgt, ignore_index=-100, reduction="sum")
+    lr.backward()
+    assert abs(loss.item() - lr.item()) / abs(lr.item()) < 5e-3
+    assert rel(x.grad.float(), xr.grad) < 3e-2
+    assert rel(w.grad, wr.grad) < 3e-2
+    assert w.grad[V:].abs().max().item() == 0.0
+
+
+def test_embedding_deterministic_backward():
+    torch.manual_seed(4)
+    from tensor_train_ing_b200.ops.weights import WeightGroup
+    W = torch.nn.Parameter(torch.randn(500, 128, device="cuda"))
+    idx = torch.randint(0, 50, (4000,), device="cuda")
+    grp = WeightGroup([W])
+    x = fused.embedding(idx, grp)
+    assert torch.equal(x, W.detach()[idx])
+    g = torch.randn_like(x)
+    x.backward(g)
+    ref = torch.zeros_like(W).index_add_(0, idx, g)
+    assert rel(W.grad, ref) < 1e-6
+    first = W.grad.clone()
+    W.grad = None
+    fused.embedding(idx, grp).backward(g)
+    assert torch.equal(W.grad, first)  # bitwise run-to-run determinism

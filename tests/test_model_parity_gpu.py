@@ -1,0 +1,52 @@
+"""The fused sm_100a model path against the PyTorch reference path of the same model (GPU)."""
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+from tensor_train_ing_b200.config import ModelConfig
+from tensor_train_ing_b200.models.model import TensorLM
+
+
+def rel(a, b):
+    return ((a.double() - b.double()).norm() / b.double().norm().clamp_min(1e-30)).item()
+
+
+@pytest.mark.parametrize("kind", ["signed_product", "offset_square", "lower_degree_mix"])
+@pytest.mark.parametrize("norm", ["pre_rms", "group_rms", "sandwich_rms", "spectral_rms"])
+def test_fused_matches_reference(kind, norm):
+    torch.manual_seed(0)
+    cfg = ModelConfig(layers=2, d_model=256, heads=2, d_key=64, d_value=64, d_mlp=512, vocab_size=1000,
+                      padded_vocab=1024, attention=kind, normalization=norm, loss_chunk_tokens=256,
+                      qk_init_scale=0.5)
+    model = TensorLM(cfg).cuda()
+    B, T = 2, 160
+    idx = torch.randint(0, 1000, (B, T), device="cuda")
+    docs = torch.zeros(B, T, dtype=torch.long, device="cuda")
+    docs[:, 90:] = 1
+    tgt = torch.roll(idx, -1, 1)
+    tgt[:, -1] = -100
+    _, loss, n = model(idx, docs, tgt, reduction="sum")
+    loss.backward()
+    grads = {k: p.grad.detach().clone() for k, p in model.named_parameters() if p.grad is not None}
+    model.zero_grad(set_to_none=True)
+    ref_cfg = ModelConfig(**{**cfg.__dict__, "attention_backend": "reference"})
+    ref = TensorLM(ref_cfg).cuda()
+    ref.load_state_dict(model.state_dict())
+    with torch.autocast("cuda", dtype=torch.bfloat16):
+        _, loss_r, n_r = ref(idx, docs, tgt, reduction="sum")
+    loss_r.backward()
+    exact = TensorLM(ref_cfg).cuda().double()
+    exact.load_state_dict(model.state_dict())
+    _, loss_x, _ = exact(idx, docs, tgt, reduction="sum")
+    loss_x.backward()
+    assert int(n) == int(n_r)
+    assert abs(loss.item() - loss_x.item()) / abs(loss_x.item()) < 1e-2
+    ref_grads = dict(ref.named_parameters())
+    for k, p in exact.named_parameters():
+        if p.grad is None:
+            continue
+        # the fused bf16 path must be about as close to fp64 as the reference's own bf16 autocast path
+        err_fused = rel(grads[k], p.grad)
+        err_ref = rel(ref_grads[k].grad, p.grad)
+        assert err_fused < max(2.0 * err_ref, 3e-2), (k, err_fused, err_ref)
