@@ -23,6 +23,10 @@ struct Params {
   float* dpar;                 // [B*H, nblocks, 4] per-key-block partials of the kind-parameter grads
   int dpar_blocks;
   uint32_t* status;
+  // rotary tables [positions, dk/2] fp32: when set, the backward writes dq/dk with the rotary
+  // embedding undone (gradients w.r.t. the pre-rotation projections)
+  const float* rope_cos;
+  const float* rope_sin;
 };
 
 }  // namespace attn

@@ -20,7 +20,8 @@
 namespace ttb {
 namespace attn {
 
-constexpr int kBwdThreads = 192;
+constexpr int kBwdThreads = 320;  // 2 control warps + 8 poly warps (two per TMEM lane quadrant)
+constexpr int kBwdPoly = 256;
 
 // ============================================================================ dQ kernel
 constexpr int DQ_BM = 128;  // queries per CTA
@@ -80,8 +81,8 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       mbar_init(&kv_empty[i], 1);
     }
     mbar_init(sc_full, 1);
-    mbar_init(sc_empty, 128);
-    mbar_init(ds_full, 128);
+    mbar_init(sc_empty, kBwdPoly);
+    mbar_init(ds_full, kBwdPoly);
     mbar_init(ds_empty, 1);
     mbar_init(acc_full, 1);
     mbar_init(mma_done, 1);
@@ -179,37 +180,50 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
     }
   } else {
     const int sub = warp & 3;
+    const int half = (warp - 2) >> 2;  // which 32 keys of the 64-key block
     const int r = sub * 32 + lane;
     const int t = q0 + r;
     const bool valid = t < p.T;
     const long long grow = row0 + (valid ? t : q0);
     const int dq = valid ? p.doc[grow] : -1;
     const int dstart = valid ? t - p.pos[grow] : 0;
-    const float rs = valid ? p.row_scale[grow] : 0.f;
+    const float rs = (valid && dq >= 0) ? p.row_scale[grow] : 0.f;
     float c[4];
 #pragma unroll
     for (int i = 0; i < 4; ++i) c[i] = p.par[h * 4 + i];
+    const float k0scale = p.sm * p.sm * rs;  // signed_product: dS1 = dP rs (s2 sm) etc., sm folded
     const uint32_t lane_off = static_cast<uint32_t>(sub * 32) << 16;
     bool ok = true;
     for (int j = 0; j < nkb && ok; ++j) {
       if (!mbar_wait(sc_full, j & 1, p.status, kErrTimeoutEpilogue)) { ok = false; break; }
       tc_fence_after();
-      uint32_t d1[32], d2[32];  // 64 bf16 each: rows of dS1 / dS2
-      const int kb0 = kstart + j * DQ_BN;
+      uint32_t a[32], bb[32], g[32];
+      tmem_ld32(tS1 + lane_off + half * 32, a);
+      if (kTwo) tmem_ld32(tS2 + lane_off + half * 32, bb);
+      tmem_ld32(tDP + lane_off + half * 32, g);
+      tmem_ld_wait();
+      tc_fence_before();
+      mbar_arrive(sc_empty);
+      const int kb0 = kstart + j * DQ_BN + half * 32;
+      const bool full_vis = rs != 0.f && kb0 >= dstart && kb0 + 31 <= t;
+      uint32_t d1[16], d2[16];
+      if (KIND == 0 && full_vis) {
+        // dS1 = H S2 = dP rs sm s2_raw ; the second sm of S2 is folded with the first: scale = sm^2 rs / sm
+        const float sc = k0scale / p.sm;
 #pragma unroll
-      for (int cc = 0; cc < DQ_BN / 32; ++cc) {
-        uint32_t a[32], bb[32], g[32];
-        tmem_ld32(tS1 + lane_off + cc * 32, a);
-        if (kTwo) tmem_ld32(tS2 + lane_off + cc * 32, bb);
-        tmem_ld32(tDP + lane_off + cc * 32, g);
-        tmem_ld_wait();
+        for (int jj = 0; jj < 32; jj += 2) {
+          const float h0 = __uint_as_float(g[jj]) * sc, h1 = __uint_as_float(g[jj + 1]) * sc;
+          d1[jj / 2] = pack_bf16(h0 * __uint_as_float(bb[jj]), h1 * __uint_as_float(bb[jj + 1]));
+          d2[jj / 2] = pack_bf16(h0 * __uint_as_float(a[jj]), h1 * __uint_as_float(a[jj + 1]));
+        }
+      } else {
 #pragma unroll
         for (int jj = 0; jj < 32; jj += 2) {
           float o1[2], o2[2];
 #pragma unroll
           for (int e = 0; e < 2; ++e) {
-            const int kt = kb0 + cc * 32 + jj + e;
-            const bool vis = valid && dq >= 0 && kt <= t && kt >= dstart;
+            const int kt = kb0 + jj + e;
+            const bool vis = full_vis || (rs != 0.f && kt <= t && kt >= dstart);
             const float s1 = __uint_as_float(a[jj + e]) * p.sm;
             const float s2 = kTwo ? __uint_as_float(bb[jj + e]) * p.sm : s1;
             const float hh = vis ? __uint_as_float(g[jj + e]) * rs : 0.f;
@@ -224,21 +238,19 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
               o2[e] = hh * (c[2] + c[3] * s1);
             }
           }
-          d1[cc * 16 + jj / 2] = pack_bf16(o1[0], o1[1]);
-          d2[cc * 16 + jj / 2] = pack_bf16(o2[0], o2[1]);
+          d1[jj / 2] = pack_bf16(o1[0], o1[1]);
+          d2[jj / 2] = pack_bf16(o2[0], o2[1]);
         }
       }
-      tc_fence_before();
-      mbar_arrive(sc_empty);
       if (!mbar_wait(ds_empty, (j & 1) ^ 1, p.status, kErrTimeoutEpilogue)) { ok = false; break; }
       uint8_t* row1 = smem + S::kOffDS;
       uint8_t* row2 = row1 + S::kDS;
 #pragma unroll
-      for (int ch = 0; ch < 8; ++ch) {
-        *reinterpret_cast<uint4*>(row1 + sw128_offset(r, ch)) =
+      for (int ch = 0; ch < 4; ++ch) {
+        *reinterpret_cast<uint4*>(row1 + sw128_offset(r, half * 4 + ch)) =
             make_uint4(d1[ch * 4], d1[ch * 4 + 1], d1[ch * 4 + 2], d1[ch * 4 + 3]);
         if (kTwo)
-          *reinterpret_cast<uint4*>(row2 + sw128_offset(r, ch)) =
+          *reinterpret_cast<uint4*>(row2 + sw128_offset(r, half * 4 + ch)) =
               make_uint4(d2[ch * 4], d2[ch * 4 + 1], d2[ch * 4 + 2], d2[ch * 4 + 3]);
       }
       fence_proxy_async_smem();
@@ -246,29 +258,13 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
     }
     if (ok && mbar_wait(acc_full, 0, p.status, kErrTimeoutEpilogue)) {
       tc_fence_after();
-#pragma unroll 1
-      for (int which = 0; which < (kTwo ? 2 : 1); ++which) {
-        const uint32_t tacc = (which == 0 ? tDQ1 : tDQ2) + lane_off;
-        const int col = (which == 0 ? p.cq1 : p.cq2) + h * DK;
-#pragma unroll 1
-        for (int cc = 0; cc < DK / 32; ++cc) {
-          uint32_t a[32];
-          tmem_ld32(tacc + cc * 32, a);
-          tmem_ld_wait();
-          if (valid) {
-            __nv_bfloat16* dst = p.dq + grow * p.ldd + col + cc * 32;
-#pragma unroll
-            for (int q = 0; q < 4; ++q) {
-              uint4 u;
-              u.x = pack_bf16(__uint_as_float(a[q * 8 + 0]) * p.sm, __uint_as_float(a[q * 8 + 1]) * p.sm);
-              u.y = pack_bf16(__uint_as_float(a[q * 8 + 2]) * p.sm, __uint_as_float(a[q * 8 + 3]) * p.sm);
-              u.z = pack_bf16(__uint_as_float(a[q * 8 + 4]) * p.sm, __uint_as_float(a[q * 8 + 5]) * p.sm);
-              u.w = pack_bf16(__uint_as_float(a[q * 8 + 6]) * p.sm, __uint_as_float(a[q * 8 + 7]) * p.sm);
-              *reinterpret_cast<uint4*>(dst + q * 8) = u;
-            }
-          }
-        }
-      }
+      const long long qp = valid ? p.pos[grow] : 0;
+      const float* ct = p.rope_cos ? p.rope_cos + qp * (DK / 2) : nullptr;
+      const float* st = p.rope_sin ? p.rope_sin + qp * (DK / 2) : nullptr;
+      if (half == 0)
+        store_row<DK>(tDQ1 + lane_off, p.dq + grow * p.ldd + p.cq1 + h * DK, valid, p.sm, ct, st);
+      else if (kTwo)
+        store_row<DK>(tDQ2 + lane_off, p.dq + grow * p.ldd + p.cq2 + h * DK, valid, p.sm, ct, st);
     }
   }
   __syncwarp();
@@ -297,7 +293,7 @@ struct DkvSmem {
   static constexpr int kOffK1 = 0, kOffK2 = kK, kOffV = 2 * kK;
   static constexpr int kOffStage = 2 * kK + kV;
   static constexpr int kOffT = kOffStage + KV_STAGES * kStage;
-  static constexpr int kOffRed = kOffT + 2 * kTile;        // 4 warps x 4 floats
+  static constexpr int kOffRed = kOffT + 2 * kTile;        // 8 poly warps x 4 floats
   static constexpr int kOffBar = kOffRed + 256;
   static constexpr int kBytes = (kOffBar + 256 + 1024) > 120 * 1024 ? (kOffBar + 256 + 1024) : 120 * 1024;
 };
@@ -345,9 +341,9 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       mbar_init(&q_empty[i], 1);
     }
     mbar_init(sc_full, 1);
-    mbar_init(sc_empty, 128);
+    mbar_init(sc_empty, kBwdPoly);
     for (int i = 0; i < 2; ++i) {
-      mbar_init(&t_full[i], 128);
+      mbar_init(&t_full[i], kBwdPoly);
       mbar_init(&t_empty[i], 1);
     }
     mbar_init(acc_full, 1);
@@ -453,7 +449,9 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
     }
   } else {
     const int sub = warp & 3;
-    const int r = sub * 32 + lane;  // key row
+    const int half = (warp - 2) >> 2;  // which 16 queries of the 32-query block
+    const int pw = warp - 2;           // poly warp index 0..7
+    const int r = sub * 32 + lane;     // key row
     const int kt = k0 + r;
     const bool kvalid = kt < p.T;
     const long long krow = row0 + (kvalid ? kt : k0);
@@ -468,22 +466,23 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
     for (int i = 0; i < nqb && ok; ++i) {
       if (!mbar_wait(sc_full, i & 1, p.status, kErrTimeoutEpilogue)) { ok = false; break; }
       tc_fence_after();
-      uint32_t a[32], bb[32], g[32];
-      tmem_ld32(tS1 + lane_off, a);
-      if (kTwo) tmem_ld32(tS2 + lane_off, bb);
-      tmem_ld32(tDP + lane_off, g);
+      uint32_t a[16], bb[16], g[16];
+      tmem_ld16(tS1 + lane_off + half * 16, a);
+      if (kTwo) tmem_ld16(tS2 + lane_off + half * 16, bb);
+      tmem_ld16(tDP + lane_off + half * 16, g);
       tmem_ld_wait();
       tc_fence_before();
       mbar_arrive(sc_empty);
-      const int qb0 = k0 + i * KV_BM;
-      uint32_t pp[16], d1[16], d2[16];
+      const int qb0 = k0 + i * KV_BM + half * 16;
+      const bool full_vis = kreal && qb0 >= kt && qb0 + 15 < kend;
+      uint32_t pp[8], d1[8], d2[8];
 #pragma unroll
-      for (int jj = 0; jj < 32; jj += 2) {
+      for (int jj = 0; jj < 16; jj += 2) {
         float vp[2], o1[2], o2[2];
 #pragma unroll
         for (int e = 0; e < 2; ++e) {
           const int qt = qb0 + jj + e;
-          const bool vis = kreal && qt >= kt && qt < kend;
+          const bool vis = full_vis || (kreal && qt >= kt && qt < kend);
           const float rs = vis ? p.row_scale[row0 + qt] : 0.f;
           const float s1 = __uint_as_float(a[jj + e]) * p.sm;
           const float s2 = kTwo ? __uint_as_float(bb[jj + e]) * p.sm : s1;
@@ -513,8 +512,8 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       if (!mbar_wait(&t_empty[tb], ((i >> 1) & 1) ^ 1, p.status, kErrTimeoutEpilogue)) { ok = false; break; }
       uint8_t* tp = smem + S::kOffT + tb * S::kTile;
 #pragma unroll
-      for (int ch = 0; ch < 4; ++ch) {
-        const uint32_t off = sw64_offset(r, ch);
+      for (int ch = 0; ch < 2; ++ch) {
+        const uint32_t off = sw64_offset(r, half * 2 + ch);
         *reinterpret_cast<uint4*>(tp + off) = make_uint4(pp[ch * 4], pp[ch * 4 + 1], pp[ch * 4 + 2], pp[ch * 4 + 3]);
         *reinterpret_cast<uint4*>(tp + S::kT + off) =
             make_uint4(d1[ch * 4], d1[ch * 4 + 1], d1[ch * 4 + 2], d1[ch * 4 + 3]);
@@ -525,7 +524,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       fence_proxy_async_smem();
       mbar_arrive(&t_full[tb]);
     }
-    // kind-parameter partials: fixed-order reduction over the 128 key rows of this block
+    // kind-parameter partials: fixed-order reduction over the 256 poly threads of this key block
     if (KIND != 0 && p.dpar != nullptr) {
 #pragma unroll
       for (int o = 16; o > 0; o >>= 1) {
@@ -535,50 +534,28 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
         g12 += __shfl_xor_sync(0xffffffffu, g12, o);
       }
       if (lane == 0) {
-        red[sub * 4 + 0] = g0;
-        red[sub * 4 + 1] = g1;
-        red[sub * 4 + 2] = g2;
-        red[sub * 4 + 3] = g12;
+        red[pw * 4 + 0] = g0;
+        red[pw * 4 + 1] = g1;
+        red[pw * 4 + 2] = g2;
+        red[pw * 4 + 3] = g12;
       }
-      asm volatile("bar.sync 1, 128;" ::: "memory");
-      if (r < 4) {
-        const float s = red[0 * 4 + r] + red[1 * 4 + r] + red[2 * 4 + r] + red[3 * 4 + r];
-        p.dpar[(static_cast<long long>(bh) * p.dpar_blocks + kb) * 4 + r] = s;
+      asm volatile("bar.sync 1, 256;" ::: "memory");
+      if (pw == 0 && lane < 4) {
+        float sum = 0.f;
+        for (int w8 = 0; w8 < 8; ++w8) sum += red[w8 * 4 + lane];
+        p.dpar[(static_cast<long long>(bh) * p.dpar_blocks + kb) * 4 + lane] = sum;
       }
     }
     if (ok && nqb > 0 && mbar_wait(acc_full, 0, p.status, kErrTimeoutEpilogue)) {
       tc_fence_after();
-#pragma unroll 1
-      for (int which = 0; which < (kTwo ? 3 : 2); ++which) {
-        const uint32_t tacc = (which == 0 ? tDV : (which == 1 ? tDK1 : tDK2)) + lane_off;
-        const int width = which == 0 ? DV : DK;
-        const int col = (which == 0 ? p.cv + h * DV : (which == 1 ? p.ck1 : p.ck2) + h * DK);
-        const float scale = which == 0 ? 1.f : p.sm;
-#pragma unroll 1
-        for (int cc = 0; cc < width / 32; ++cc) {
-          uint32_t a[32];
-          tmem_ld32(tacc + cc * 32, a);
-          tmem_ld_wait();
-          if (kvalid) {
-            __nv_bfloat16* dst = p.dq + krow * p.ldd + col + cc * 32;
-#pragma unroll
-            for (int q = 0; q < 4; ++q) {
-              uint4 u;
-              u.x = pack_bf16(__uint_as_float(a[q * 8 + 0]) * scale, __uint_as_float(a[q * 8 + 1]) * scale);
-              u.y = pack_bf16(__uint_as_float(a[q * 8 + 2]) * scale, __uint_as_float(a[q * 8 + 3]) * scale);
-              u.z = pack_bf16(__uint_as_float(a[q * 8 + 4]) * scale, __uint_as_float(a[q * 8 + 5]) * scale);
-              u.w = pack_bf16(__uint_as_float(a[q * 8 + 6]) * scale, __uint_as_float(a[q * 8 + 7]) * scale);
-              *reinterpret_cast<uint4*>(dst + q * 8) = u;
-            }
-          }
-        }
-      }
-    } else if (kvalid && ok && nqb == 0) {
-      // no visible query: gradients are zero
-      for (int which = 0; which < (kTwo ? 3 : 2); ++which) {
-        const int width = which == 0 ? DV : DK;
-        const int col = (which == 0 ? p.cv + h * DV : (which == 1 ? p.ck1 : p.ck2) + h * DK);
-        for (int cc = 0; cc < width; ++cc) p.dq[krow * p.ldd + col + cc] = __float2bfloat16_rn(0.f);
+      const long long kp = kvalid ? p.pos[krow] : 0;
+      const float* ct = p.rope_cos ? p.rope_cos + kp * (DK / 2) : nullptr;
+      const float* st = p.rope_sin ? p.rope_sin + kp * (DK / 2) : nullptr;
+      if (half == 0) {
+        store_row<DV>(tDV + lane_off, p.dq + krow * p.ldd + p.cv + h * DV, kvalid, 1.f, nullptr, nullptr);
+        if (kTwo) store_row<DK>(tDK2 + lane_off, p.dq + krow * p.ldd + p.ck2 + h * DK, kvalid, p.sm, ct, st);
+      } else {
+        store_row<DK>(tDK1 + lane_off, p.dq + krow * p.ldd + p.ck1 + h * DK, kvalid, p.sm, ct, st);
       }
     }
   }

@@ -34,5 +34,66 @@ __device__ __forceinline__ uint64_t mnmajor_desc(uint32_t base, int rows, int k)
   return smem_desc(base + k * 2048, rows * 128, 1024, 2);
 }
 
+__device__ __forceinline__ void store32_scaled(__nv_bfloat16* dst, const float (&v)[32]) {
+#pragma unroll
+  for (int q = 0; q < 4; ++q) {
+    uint4 u;
+    u.x = pack_bf16(v[q * 8 + 0], v[q * 8 + 1]);
+    u.y = pack_bf16(v[q * 8 + 2], v[q * 8 + 3]);
+    u.z = pack_bf16(v[q * 8 + 4], v[q * 8 + 5]);
+    u.w = pack_bf16(v[q * 8 + 6], v[q * 8 + 7]);
+    *reinterpret_cast<uint4*>(dst + q * 8) = u;
+  }
+}
+
+// Drain one accumulator row of width W from TMEM (columns tacc..tacc+W) to global bf16 memory,
+// scaled by `scale`.  With rotary tables (ct/st = the row's table entries, W/2 each) the pairs
+// (i, i + W/2) are rotated back: g1 = a cos + b sin, g2 = -a sin + b cos.
+template <int W>
+__device__ __forceinline__ void store_row(uint32_t tacc, __nv_bfloat16* dst, bool valid, float scale,
+                                          const float* ct, const float* st) {
+  if (ct == nullptr) {
+#pragma unroll 1
+    for (int cc = 0; cc < W / 32; ++cc) {
+      uint32_t a[32];
+      tmem_ld32(tacc + cc * 32, a);
+      tmem_ld_wait();
+      if (valid) {
+        float v[32];
+#pragma unroll
+        for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(a[j]) * scale;
+        store32_scaled(dst + cc * 32, v);
+      }
+    }
+    return;
+  }
+#pragma unroll 1
+  for (int cc = 0; cc < W / 64; ++cc) {
+    uint32_t a[32], b[32];
+    tmem_ld32(tacc + cc * 32, a);
+    tmem_ld32(tacc + W / 2 + cc * 32, b);
+    tmem_ld_wait();
+    if (valid) {
+      float g1[32], g2[32], cs[32], sn[32];
+#pragma unroll
+      for (int q = 0; q < 8; ++q) {
+        const float4 c4 = *reinterpret_cast<const float4*>(ct + cc * 32 + q * 4);
+        const float4 s4 = *reinterpret_cast<const float4*>(st + cc * 32 + q * 4);
+        cs[q * 4 + 0] = c4.x; cs[q * 4 + 1] = c4.y; cs[q * 4 + 2] = c4.z; cs[q * 4 + 3] = c4.w;
+        sn[q * 4 + 0] = s4.x; sn[q * 4 + 1] = s4.y; sn[q * 4 + 2] = s4.z; sn[q * 4 + 3] = s4.w;
+      }
+#pragma unroll
+      for (int j = 0; j < 32; ++j) {
+        const float c = cs[j], s = sn[j];
+        const float x1 = __uint_as_float(a[j]) * scale, x2 = __uint_as_float(b[j]) * scale;
+        g1[j] = x1 * c + x2 * s;
+        g2[j] = x2 * c - x1 * s;
+      }
+      store32_scaled(dst + cc * 32, g1);
+      store32_scaled(dst + W / 2 + cc * 32, g2);
+    }
+  }
+}
+
 }  // namespace attn
 }  // namespace ttb

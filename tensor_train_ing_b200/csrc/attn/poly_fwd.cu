@@ -4,9 +4,11 @@
 //   warp 0    TMA producer: Q1/Q2 once, then K1/K2/V tiles of 64 keys through a 2-stage ring
 //   warp 1    tcgen05.mma issuer: S1 = Q1 K1^T, S2 = Q2 K2^T into a double-buffered TMEM pair,
 //             then O += P V once the poly warps have produced P
-//   warps 2-5 "poly" warps, one query row per thread: tcgen05.ld the S1/S2 row, form
-//             P = visible * row_scale * A(S1, S2) (fp32), round to bf16 and write it into a
-//             128B-swizzled K-major shared tile; finally drain O from TMEM to global memory.
+//   warps 2-9 "poly" warps: warp w owns TMEM lane quadrant w%4 (32 query rows) and one half
+//             (32 keys) of the key block; it tcgen05.ld's its S1/S2 slice, forms
+//             P = visible * row_scale * A(S1, S2) in fp32 (no per-element mask when the slice is
+//             fully visible), rounds to bf16 and writes it into a 128B-swizzled K-major shared
+//             tile; finally the eight warps drain O from TMEM to global memory.
 // S of key block j+1 is computed while the poly warps work on block j, and P V of block j runs
 // after it, so the tensor pipe stays busy.  Key blocks before the start of the first query's
 // document are skipped (documents are contiguous).  Reference: tnlm/kernels/poly_attn.py:38-74.
@@ -19,7 +21,8 @@ namespace attn {
 
 constexpr int BMQ = 128;  // queries per CTA
 constexpr int BNK = 64;   // keys per block
-constexpr int kThreads = 192;
+constexpr int kThreads = 320;   // 2 control warps + 8 poly warps
+constexpr int kPolyThreads = 256;
 
 template <int DK, int DV>
 struct FwdSmem {
@@ -74,8 +77,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&kv_full[i], 1);
       mbar_init(&kv_empty[i], 1);
       mbar_init(&s_full[i], 1);
-      mbar_init(&s_empty[i], 128);
-      mbar_init(&p_full[i], 128);
+      mbar_init(&s_empty[i], kPolyThreads);
+      mbar_init(&p_full[i], kPolyThreads);
       mbar_init(&p_empty[i], 1);
     }
     mbar_init(o_full, 1);
@@ -169,18 +172,21 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_wait(mma_done, 0, p.status, kErrTimeoutMma);
     }
   } else {
-    // ------------------------------------------------------------- poly warps (2..5)
+    // ------------------------------------------------------------- poly warps (2..9)
     const int sub = warp & 3;
-    const int r = sub * 32 + lane;  // query row inside the block == TMEM lane
+    const int half = (warp - 2) >> 2;  // which 32 keys of the 64-key block
+    const int r = sub * 32 + lane;     // query row inside the block == TMEM lane
     const int t = q0 + r;
     const bool valid = t < p.T;
     const long long grow = row0 + (valid ? t : q0);
     const int dq = valid ? p.doc[grow] : -1;
     const int dstart = valid ? t - p.pos[grow] : 0;  // documents are contiguous: keys [dstart, t]
-    const float rs = valid ? p.row_scale[grow] : 0.f;
+    const float rs = (valid && dq >= 0) ? p.row_scale[grow] : 0.f;
     float c[4];
 #pragma unroll
     for (int i = 0; i < 4; ++i) c[i] = p.par[h * 4 + i];
+    // signed_product fast path: P = (s1 sm)(s2 sm) rs = s1 s2 (sm^2 rs)
+    const float k0scale = p.sm * p.sm * rs;
     const uint32_t lane_off = static_cast<uint32_t>(sub * 32) << 16;
     bool ok = true;
     for (int j = 0; j < nkb && ok; ++j) {
@@ -188,59 +194,58 @@ __global__ void __launch_bounds__(kThreads, 1)
       const uint32_t ph = (j >> 1) & 1;
       if (!mbar_wait(&s_full[st], ph, p.status, kErrTimeoutEpilogue)) { ok = false; break; }
       tc_fence_after();
-      uint32_t pk[32];  // 64 bf16 of this row of P
-      const int kb0 = kstart + j * BNK;
+      uint32_t a[32], bb[32];
+      const uint32_t col = st * BNK + half * 32;
+      tmem_ld32(tS1 + lane_off + col, a);
+      if (kTwo) tmem_ld32(tS2 + lane_off + col, bb);
+      tmem_ld_wait();
+      tc_fence_before();
+      mbar_arrive(&s_empty[st]);
+      const int kb0 = kstart + j * BNK + half * 32;
+      const bool full_vis = rs != 0.f && kb0 >= dstart && kb0 + 31 <= t;
+      uint32_t pk[16];
+      if (full_vis && KIND == 0) {
 #pragma unroll
-      for (int cc = 0; cc < BNK / 32; ++cc) {
-        uint32_t a[32], bb[32];
-        tmem_ld32(tS1 + lane_off + st * BNK + cc * 32, a);
-        if (kTwo) tmem_ld32(tS2 + lane_off + st * BNK + cc * 32, bb);
-        tmem_ld_wait();
+        for (int jj = 0; jj < 32; jj += 2)
+          pk[jj / 2] = pack_bf16(__uint_as_float(a[jj]) * __uint_as_float(bb[jj]) * k0scale,
+                                 __uint_as_float(a[jj + 1]) * __uint_as_float(bb[jj + 1]) * k0scale);
+      } else {
 #pragma unroll
         for (int jj = 0; jj < 32; jj += 2) {
           float v[2];
 #pragma unroll
           for (int e = 0; e < 2; ++e) {
-            const int kt = kb0 + cc * 32 + jj + e;
+            const int kt = kb0 + jj + e;
             const float s1 = __uint_as_float(a[jj + e]) * p.sm;
             const float s2 = kTwo ? __uint_as_float(bb[jj + e]) * p.sm : s1;
-            const bool vis = valid && dq >= 0 && kt <= t && kt >= dstart;
+            const bool vis = full_vis || (kt <= t && kt >= dstart);
             v[e] = vis ? poly<KIND>(s1, s2, c) * rs : 0.f;
           }
-          pk[cc * 16 + jj / 2] = pack_bf16(v[0], v[1]);
+          pk[jj / 2] = pack_bf16(v[0], v[1]);
         }
       }
-      tc_fence_before();
-      mbar_arrive(&s_empty[st]);
       // P buffer st is free once P V of block j-2 has completed
       if (!mbar_wait(&p_empty[st], ph ^ 1, p.status, kErrTimeoutEpilogue)) { ok = false; break; }
       uint8_t* prow = smem + S::kOffP + st * S::kP;
 #pragma unroll
-      for (int ch = 0; ch < 8; ++ch) {
-        uint4 u = make_uint4(pk[ch * 4], pk[ch * 4 + 1], pk[ch * 4 + 2], pk[ch * 4 + 3]);
-        *reinterpret_cast<uint4*>(prow + sw128_offset(r, ch)) = u;
-      }
+      for (int ch = 0; ch < 4; ++ch)
+        *reinterpret_cast<uint4*>(prow + sw128_offset(r, half * 4 + ch)) =
+            make_uint4(pk[ch * 4], pk[ch * 4 + 1], pk[ch * 4 + 2], pk[ch * 4 + 3]);
       fence_proxy_async_smem();
       mbar_arrive(&p_full[st]);
     }
     if (ok && mbar_wait(o_full, 0, p.status, kErrTimeoutEpilogue)) {
       tc_fence_after();
 #pragma unroll 1
-      for (int cc = 0; cc < DV / 32; ++cc) {
+      for (int cc = half * (DV / 64); cc < (half + 1) * (DV / 64); ++cc) {
         uint32_t a[32];
         tmem_ld32(tO + lane_off + cc * 32, a);
         tmem_ld_wait();
         if (valid) {
-          __nv_bfloat16* dst = p.y + grow * p.ldy + h * DV + cc * 32;
+          float v[32];
 #pragma unroll
-          for (int q = 0; q < 4; ++q) {
-            uint4 u;
-            u.x = pack_bf16(__uint_as_float(a[q * 8 + 0]), __uint_as_float(a[q * 8 + 1]));
-            u.y = pack_bf16(__uint_as_float(a[q * 8 + 2]), __uint_as_float(a[q * 8 + 3]));
-            u.z = pack_bf16(__uint_as_float(a[q * 8 + 4]), __uint_as_float(a[q * 8 + 5]));
-            u.w = pack_bf16(__uint_as_float(a[q * 8 + 6]), __uint_as_float(a[q * 8 + 7]));
-            *reinterpret_cast<uint4*>(dst + q * 8) = u;
-          }
+          for (int q = 0; q < 32; ++q) v[q] = __uint_as_float(a[q]);
+          store32_scaled(p.y + grow * p.ldy + h * DV + cc * 32, v);
         }
       }
     }

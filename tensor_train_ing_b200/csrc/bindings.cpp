@@ -76,6 +76,24 @@ void mm(const Tensor& a, const Tensor& b, Tensor& out, const c10::optional<Tenso
                    c_f32, static_cast<float>(alpha), static_cast<float>(beta), bp, cur_stream());
 }
 
+// qkv = x w^T with the rotary embedding applied to the first rope_cols columns
+Tensor qkv_rope(const Tensor& x, const Tensor& w, int64_t rope_cols, int64_t dk, const Tensor& pos,
+                const Tensor& cos_t, const Tensor& sin_t) {
+  const c10::cuda::CUDAGuard guard(x.device());
+  const auto X = a_operand(x);
+  const auto W = b_operand(w.t());
+  const int M = x.size(0), K = x.size(1), N = w.size(0);
+  TORCH_CHECK(w.size(1) == K, "w shape");
+  TORCH_CHECK(pos.scalar_type() == torch::kInt32 && pos.is_contiguous() && pos.numel() == M, "pos int32 [M]");
+  TORCH_CHECK(cos_t.scalar_type() == torch::kFloat32 && cos_t.is_contiguous() && cos_t.size(-1) == dk / 2, "cos table");
+  TORCH_CHECK(sin_t.scalar_type() == torch::kFloat32 && sin_t.is_contiguous() && sin_t.sizes() == cos_t.sizes(),
+              "sin table");
+  auto out = torch::empty({M, N}, x.options());
+  ttb::gemm_qkv_rope(X, W, M, N, K, out.data_ptr(), out.stride(0), rope_cols, dk, pos.data_ptr<int>(),
+                     cos_t.data_ptr<float>(), sin_t.data_ptr<float>(), cur_stream());
+  return out;
+}
+
 // h = l*r (mode 0) / silu(l)*r (mode 1) with l = x wl^T (+bl), r = x wr^T (+br)
 void bilinear(const Tensor& x, const Tensor& wl, const Tensor& wr, const c10::optional<Tensor>& bl,
               const c10::optional<Tensor>& br, int64_t mode, Tensor& h, const c10::optional<Tensor>& lo,
@@ -265,15 +283,25 @@ Tensor poly_fwd(int64_t kind, int64_t dk, int64_t dv, const Tensor& qkv, std::ve
 // returns (dqkv [B*T, ld] bf16 in the qkv layout, dpar [B*H, blocks, 4] fp32)
 std::vector<Tensor> poly_bwd(int64_t kind, int64_t dk, int64_t dv, const Tensor& qkv, std::vector<int64_t> cols,
                              const Tensor& dout, const Tensor& pos, const Tensor& doc, const Tensor& doc_end,
-                             const Tensor& row_scale, const Tensor& par, int64_t B, int64_t T, int64_t H) {
+                             const Tensor& row_scale, const Tensor& par, int64_t B, int64_t T, int64_t H,
+                             const c10::optional<Tensor>& rope_cos, const c10::optional<Tensor>& rope_sin) {
   const c10::cuda::CUDAGuard guard(qkv.device());
   check_bf16(qkv, "qkv");
   check_bf16(dout, "dout");
   TORCH_CHECK(dout.dim() == 2 && dout.stride(1) == 1 && dout.size(0) == B * T && dout.size(1) == H * dv, "dout");
   TORCH_CHECK(doc_end.scalar_type() == torch::kInt32 && doc_end.is_contiguous() && doc_end.numel() == B * T, "doc_end");
   auto p = attn_params(cols, pos, doc, row_scale, par, B, T, H, dk);
-  auto dqkv = torch::zeros_like(qkv);
+  // every element of dqkv is written by the two kernels (all rows < B*T, all five column groups)
+  auto dqkv = torch::empty_like(qkv);
   const int blocks = ttb::poly_attention_dpar_blocks(T);
+  if (rope_cos.has_value()) {
+    TORCH_CHECK(rope_sin.has_value(), "rope tables come in pairs");
+    TORCH_CHECK(rope_cos->scalar_type() == torch::kFloat32 && rope_cos->is_contiguous() && rope_cos->size(-1) == dk / 2,
+                "rope cos table [positions, dk/2]");
+    TORCH_CHECK(rope_sin->sizes() == rope_cos->sizes() && rope_sin->is_contiguous(), "rope sin table");
+    p.rope_cos = rope_cos->data_ptr<float>();
+    p.rope_sin = rope_sin->data_ptr<float>();
+  }
   auto dpar = torch::zeros({B * H, blocks, 4}, qkv.options().dtype(torch::kFloat32));
   p.dq = static_cast<__nv_bfloat16*>(dqkv.data_ptr());
   p.ldd = dqkv.stride(0);
@@ -303,5 +331,9 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("ce_fwd", &ce_fwd, "fused linear + cross-entropy forward: per-row loss and lse");
   m.def("ce_bwd_logits", &ce_bwd_logits, "fused logits recompute + softmax-grad epilogue");
   m.def("poly_fwd", &poly_fwd, "tcgen05 polynomial attention forward");
-  m.def("poly_bwd", &poly_bwd, "tcgen05 polynomial attention backward (dq and dkv kernels)");
+  m.def("poly_bwd", &poly_bwd, "tcgen05 polynomial attention backward (dq and dkv kernels)", py::arg("kind"),
+        py::arg("dk"), py::arg("dv"), py::arg("qkv"), py::arg("cols"), py::arg("dout"), py::arg("pos"), py::arg("doc"),
+        py::arg("doc_end"), py::arg("row_scale"), py::arg("par"), py::arg("B"), py::arg("T"), py::arg("H"),
+        py::arg("rope_cos") = py::none(), py::arg("rope_sin") = py::none());
+  m.def("qkv_rope", &qkv_rope, "QKV projection GEMM with the rotary embedding in its epilogue");
 }

@@ -29,7 +29,18 @@ using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t
                                    const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
                                    CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
 
+// Driver-API calls need a current context on the calling thread (autograd runs backward on its
+// own worker threads): touch the runtime once per thread so the primary context is bound.
+inline void ensure_context() {
+  thread_local bool bound = false;
+  if (!bound) {
+    TTB_CUDA_CHECK(cudaFree(nullptr));
+    bound = true;
+  }
+}
+
 inline EncodeTiledFn encode_tiled_fn() {
+  ensure_context();
   static EncodeTiledFn fn = nullptr;
   if (fn == nullptr) {
     void* ptr = nullptr;

@@ -28,4 +28,9 @@ void gemm_bilinear(const Operand& x, const Operand& wl, const Operand& wr, int M
 void gemm_bilinear_grad(const Operand& dy, const Operand& wd, int M, int N, int K, const void* Lin, const void* Rin,
                         void* dL, void* dR, long long ld, int mode, cudaStream_t stream);
 
+// qkv[M, N] = x W^T (bf16) with the rotary embedding applied to the first rope_cols columns
+// (heads of width dk; cos/sin tables [positions, dk/2] fp32; pos [M] int32).
+void gemm_qkv_rope(const Operand& x, const Operand& w, int M, int N, int K, void* D, long long ldd, int rope_cols,
+                   int dk, const int* pos, const float* cos_t, const float* sin_t, cudaStream_t stream);
+
 }  // namespace ttb

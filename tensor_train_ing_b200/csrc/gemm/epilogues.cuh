@@ -228,5 +228,61 @@ struct EpiBilinearGrad {
   }
 };
 
+// Projection GEMM for the fused QKV buffer with the rotary embedding in the epilogue:
+// columns < rope_cols hold heads of width dk whose pairs (i, i + dk/2) are rotated by the angle of
+// the row's position, using cos/sin tables [positions, dk/2] (fp32) built once per forward.
+// The tile width NB is a multiple of dk, so a thread sees both halves of every head it stores.
+template <int NB>
+struct EpiRope {
+  __nv_bfloat16* D;
+  long long ldd;
+  int rope_cols, dk;
+  const int* pos;
+  const float* cos_t;
+  const float* sin_t;
+  int M, N;
+
+  __device__ __forceinline__ void operator()(uint32_t taddr, int row, int n0, int, int) const {
+    const bool vec = (ldd % 8 == 0);
+    const int half = dk / 2;
+    const int p = row < M ? pos[row] : 0;
+#pragma unroll 1
+    for (int c = 0; c < NB / 32; ++c) {
+      const int col0 = n0 + c * 32;
+      if (col0 < rope_cols) {
+        const int o = col0 % dk;  // offset inside the head
+        if (o >= half) continue;  // second half: stored together with its first-half partner
+        const int cb = c + half / 32;
+        uint32_t ra[32], rb[32];
+        tmem_ld32(taddr + c * 32, ra);
+        tmem_ld32(taddr + cb * 32, rb);
+        tmem_ld_wait();
+        if (row >= M || col0 >= N) continue;
+        float cs[32], sn[32], a[32], b[32];
+        load_row32_f32(cos_t + static_cast<long long>(p) * half + o, (half % 4 == 0), 32, cs);
+        load_row32_f32(sin_t + static_cast<long long>(p) * half + o, (half % 4 == 0), 32, sn);
+#pragma unroll
+        for (int j = 0; j < 32; ++j) {
+          const float x1 = __uint_as_float(ra[j]), x2 = __uint_as_float(rb[j]);
+          a[j] = x1 * cs[j] - x2 * sn[j];
+          b[j] = x1 * sn[j] + x2 * cs[j];
+        }
+        store_row32_bf16(D + row * ldd + col0, vec, 32, a);
+        store_row32_bf16(D + row * ldd + col0 + half, vec, 32, b);
+      } else {
+        uint32_t r[32];
+        tmem_ld32(taddr + c * 32, r);
+        tmem_ld_wait();
+        if (row >= M || col0 >= N) continue;
+        const int nv = min(32, N - col0);
+        float v[32];
+#pragma unroll
+        for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
+        store_row32_bf16(D + row * ldd + col0, vec && nv == 32, nv, v);
+      }
+    }
+  }
+};
+
 }  // namespace gemm
 }  // namespace ttb

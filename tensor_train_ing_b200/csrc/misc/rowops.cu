@@ -7,6 +7,8 @@
 #include "../common/sm100.cuh"
 #include "rowops.h"
 
+#include <type_traits>
+
 namespace ttb {
 namespace {
 
@@ -173,6 +175,183 @@ __global__ void __launch_bounds__(kRowThreads) rmsnorm_bwd_kernel(const TDY* __r
   }
 }
 
+// ---------------------------------------------------------------------------------------------
+// Warp-per-row variants for d <= 4096: each lane keeps CH float4 of the row in registers, so the
+// row is read once and reduced with shuffles only.  GROUPED=false is plain RMSNorm (one group).
+template <bool GROUPED>
+__device__ __forceinline__ int group_of(int j, int gsize) {
+  return GROUPED ? j / gsize : 0;
+}
+
+template <int CH, bool GROUPED>
+__global__ void __launch_bounds__(256) rmsnorm_fwd_warp_kernel(const float* __restrict__ x, const float* __restrict__ w,
+                                                              __nv_bfloat16* __restrict__ y, float* __restrict__ rstd,
+                                                              int N, int d, int G, float eps) {
+  constexpr int NG = GROUPED ? kMaxGroups : 1;
+  const int lane = threadIdx.x % 32;
+  const int row = blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32;
+  if (row >= N) return;
+  const int gsize = d / G;
+  const bool whole = (CH * 128 == d);
+  const float* xr = x + static_cast<long long>(row) * d;
+  float v[CH][4];
+#pragma unroll
+  for (int c = 0; c < CH; ++c) {
+    const int j = (c * 32 + lane) * 4;
+    if (whole || j < d)
+      load4(xr + j, v[c]);
+    else
+      v[c][0] = v[c][1] = v[c][2] = v[c][3] = 0.f;
+  }
+  float part[NG];
+#pragma unroll
+  for (int g = 0; g < NG; ++g) part[g] = 0.f;
+#pragma unroll
+  for (int c = 0; c < CH; ++c) {
+    const int j = (c * 32 + lane) * 4;
+    const float sq = v[c][0] * v[c][0] + v[c][1] * v[c][1] + v[c][2] * v[c][2] + v[c][3] * v[c][3];
+    const int g = group_of<GROUPED>(j, gsize);
+#pragma unroll
+    for (int q = 0; q < NG; ++q)
+      if (q == g) part[q] += sq;
+  }
+  float inv[NG];
+#pragma unroll
+  for (int g = 0; g < NG; ++g) {
+    float t = part[g];
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) t += __shfl_xor_sync(0xffffffffu, t, o);
+    inv[g] = rsqrtf(t / gsize + eps);
+  }
+#pragma unroll
+  for (int g = 0; g < NG; ++g)
+    if (lane == g && g < G) rstd[static_cast<long long>(row) * G + g] = inv[g];
+  __nv_bfloat16* yr = y + static_cast<long long>(row) * d;
+#pragma unroll
+  for (int c = 0; c < CH; ++c) {
+    const int j = (c * 32 + lane) * 4;
+    if (whole || j < d) {
+      const int g = group_of<GROUPED>(j, gsize);
+      float r = inv[0];
+#pragma unroll
+      for (int q = 1; q < NG; ++q)
+        if (q == g) r = inv[q];
+      float wv[4];
+      load4(w + j, wv);
+      uint2 o;
+      o.x = pack_bf16(v[c][0] * r * wv[0], v[c][1] * r * wv[1]);
+      o.y = pack_bf16(v[c][2] * r * wv[2], v[c][3] * r * wv[3]);
+      *reinterpret_cast<uint2*>(yr + j) = o;
+    }
+  }
+}
+
+// Two passes over the row (the second re-reads x and dy, which are still in L1) keep the register
+// footprint at one row of partial weight gradients, so several CTAs stay resident per SM.
+template <int CH, bool GROUPED, typename TDY>
+__global__ void __launch_bounds__(256) rmsnorm_bwd_warp_kernel(const TDY* __restrict__ dy, const float* __restrict__ x,
+                                                              const float* __restrict__ w,
+                                                              const float* __restrict__ rstd, float* __restrict__ dres,
+                                                              int accumulate, float* __restrict__ dw_part, int N,
+                                                              int d, int G) {
+  constexpr int NG = GROUPED ? kMaxGroups : 1;
+  extern __shared__ float acc[];  // d floats
+  const int lane = threadIdx.x % 32, wid = threadIdx.x / 32, nw = blockDim.x / 32;
+  const int gsize = d / G;
+  const bool whole = (CH * 128 == d);
+  float dwl[CH][4];
+#pragma unroll
+  for (int c = 0; c < CH; ++c)
+#pragma unroll
+    for (int k = 0; k < 4; ++k) dwl[c][k] = 0.f;
+  for (int row = blockIdx.x * nw + wid; row < N; row += gridDim.x * nw) {
+    const long long base = static_cast<long long>(row) * d;
+    float rg[NG];
+#pragma unroll
+    for (int g = 0; g < NG; ++g) rg[g] = (g < G) ? rstd[static_cast<long long>(row) * G + g] : 0.f;
+    float part[NG];
+#pragma unroll
+    for (int g = 0; g < NG; ++g) part[g] = 0.f;
+    // pass 1: sum of (dy w) xhat per group; weight-gradient partials
+#pragma unroll
+    for (int c = 0; c < CH; ++c) {
+      const int j = (c * 32 + lane) * 4;
+      if (whole || j < d) {
+        const int g = group_of<GROUPED>(j, gsize);
+        float r = rg[0];
+#pragma unroll
+        for (int q = 1; q < NG; ++q)
+          if (q == g) r = rg[q];
+        float xv[4], dv[4], wv[4];
+        load4(x + base + j, xv);
+        load4(dy + base + j, dv);
+        load4(w + j, wv);
+        float sacc = 0.f;
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          const float xh = xv[k] * r;
+          dwl[c][k] += dv[k] * xh;
+          sacc += dv[k] * wv[k] * xh;
+        }
+#pragma unroll
+        for (int q = 0; q < NG; ++q)
+          if (q == g) part[q] += sacc;
+      }
+    }
+    float mean[NG];
+#pragma unroll
+    for (int g = 0; g < NG; ++g) {
+      float t = part[g];
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) t += __shfl_xor_sync(0xffffffffu, t, o);
+      mean[g] = t / gsize;
+    }
+    // pass 2: dx = rstd (dy w - xhat mean)
+#pragma unroll
+    for (int c = 0; c < CH; ++c) {
+      const int j = (c * 32 + lane) * 4;
+      if (whole || j < d) {
+        const int g = group_of<GROUPED>(j, gsize);
+        float r = rg[0], m = mean[0];
+#pragma unroll
+        for (int q = 1; q < NG; ++q)
+          if (q == g) {
+            r = rg[q];
+            m = mean[q];
+          }
+        float xv[4], dv[4], wv[4];
+        load4(x + base + j, xv);
+        load4(dy + base + j, dv);
+        load4(w + j, wv);
+        float4 o = make_float4(r * (dv[0] * wv[0] - xv[0] * r * m), r * (dv[1] * wv[1] - xv[1] * r * m),
+                               r * (dv[2] * wv[2] - xv[2] * r * m), r * (dv[3] * wv[3] - xv[3] * r * m));
+        float4* dst = reinterpret_cast<float4*>(dres + base + j);
+        if (accumulate) {
+          const float4 prev = *dst;
+          o.x += prev.x; o.y += prev.y; o.z += prev.z; o.w += prev.w;
+        }
+        *dst = o;
+      }
+    }
+  }
+  // deterministic CTA reduction: warps add their partials into shared memory in warp order
+  for (int ww = 0; ww < nw; ++ww) {
+    __syncthreads();
+    if (wid == ww) {
+#pragma unroll
+      for (int c = 0; c < CH; ++c) {
+        const int j = (c * 32 + lane) * 4;
+        if (whole || j < d) {
+#pragma unroll
+          for (int k = 0; k < 4; ++k) acc[j + k] = (ww == 0 ? 0.f : acc[j + k]) + dwl[c][k];
+        }
+      }
+    }
+  }
+  __syncthreads();
+  for (int j = threadIdx.x; j < d; j += blockDim.x) dw_part[static_cast<long long>(blockIdx.x) * d + j] = acc[j];
+}
+
 // out[j] (+)= sum_p part[p][j]   (fixed order over p: deterministic)
 __global__ void colsum_kernel(const float* __restrict__ part, int P, int d, float* __restrict__ out, int accumulate) {
   const int j = blockIdx.x * blockDim.x + threadIdx.x;
@@ -246,16 +425,47 @@ __global__ void embed_bwd_kernel(const long long* __restrict__ sorted_ids, const
 }  // namespace
 
 int rmsnorm_bwd_partials(int N) {
-  const int g = 2 * num_sms();
-  return N < g ? N : g;
+  const int g = 4 * num_sms();
+  const int warp_ctas = (N + 7) / 8;
+  return warp_ctas < g ? warp_ctas : g;  // one partial row per CTA (8 rows per CTA pass)
 }
+
+namespace {
+template <typename F>
+bool with_chunks(int d, int max_ch, F&& f) {
+  const int need = (d + 127) / 128;
+  if (need > max_ch) return false;
+  if (need <= 1) return f(std::integral_constant<int, 1>{});
+  if (need <= 2) return f(std::integral_constant<int, 2>{});
+  if (need <= 4) return f(std::integral_constant<int, 4>{});
+  if (need <= 6) return f(std::integral_constant<int, 6>{});
+  if (need <= 8) return f(std::integral_constant<int, 8>{});
+  if (need <= 12) return f(std::integral_constant<int, 12>{});
+  if (need <= 16) return f(std::integral_constant<int, 16>{});
+  if (need <= 24) return f(std::integral_constant<int, 24>{});
+  if (need <= 32) return f(std::integral_constant<int, 32>{});
+  return false;
+}
+}  // namespace
 
 void rmsnorm_fwd(const float* x, const float* w, void* y, float* rstd, int N, int d, int G, float eps,
                  cudaStream_t stream) {
   TTB_CHECK(d % 4 == 0 && d <= kRowThreads * kVec * kMaxChunks, "rmsnorm: d must be a multiple of 4 and <= 8192");
   TTB_CHECK(G >= 1 && G <= kMaxGroups && d % G == 0 && (d / G) % 4 == 0, "rmsnorm: bad group count");
-  const int grid = N < 8 * num_sms() ? N : 8 * num_sms();
-  rmsnorm_fwd_kernel<<<grid, kRowThreads, 0, stream>>>(x, w, static_cast<__nv_bfloat16*>(y), rstd, N, d, G, eps);
+  const bool done = with_chunks(d, 32, [&](auto ch) {
+    constexpr int CH = decltype(ch)::value;
+    if (G == 1)
+      rmsnorm_fwd_warp_kernel<CH, false><<<(N + 7) / 8, 256, 0, stream>>>(x, w, static_cast<__nv_bfloat16*>(y), rstd,
+                                                                          N, d, G, eps);
+    else
+      rmsnorm_fwd_warp_kernel<CH, true><<<(N + 7) / 8, 256, 0, stream>>>(x, w, static_cast<__nv_bfloat16*>(y), rstd,
+                                                                         N, d, G, eps);
+    return true;
+  });
+  if (!done) {
+    const int grid = N < 8 * num_sms() ? N : 8 * num_sms();
+    rmsnorm_fwd_kernel<<<grid, kRowThreads, 0, stream>>>(x, w, static_cast<__nv_bfloat16*>(y), rstd, N, d, G, eps);
+  }
   TTB_CUDA_CHECK(cudaGetLastError());
 }
 
@@ -264,12 +474,32 @@ void rmsnorm_bwd(const void* dy, bool dy_f32, const float* x, const float* w, co
                  cudaStream_t stream) {
   TTB_CHECK(d % 4 == 0 && d <= kRowThreads * kVec * kMaxChunks, "rmsnorm: d must be a multiple of 4 and <= 8192");
   const int grid = rmsnorm_bwd_partials(N);
-  if (dy_f32)
-    rmsnorm_bwd_kernel<float><<<grid, kRowThreads, 0, stream>>>(static_cast<const float*>(dy), x, w, rstd, dres,
-                                                                accumulate, dw_part, N, d, G);
-  else
-    rmsnorm_bwd_kernel<__nv_bfloat16><<<grid, kRowThreads, 0, stream>>>(
-        static_cast<const __nv_bfloat16*>(dy), x, w, rstd, dres, accumulate, dw_part, N, d, G);
+  const bool done = with_chunks(d, 32, [&](auto ch) {
+    constexpr int CH = decltype(ch)::value;
+    const size_t smem = static_cast<size_t>(d) * sizeof(float);
+    auto launch = [&](auto grouped) {
+      constexpr bool GR = decltype(grouped)::value;
+      if (dy_f32)
+        rmsnorm_bwd_warp_kernel<CH, GR, float><<<grid, 256, smem, stream>>>(static_cast<const float*>(dy), x, w, rstd,
+                                                                            dres, accumulate, dw_part, N, d, G);
+      else
+        rmsnorm_bwd_warp_kernel<CH, GR, __nv_bfloat16><<<grid, 256, smem, stream>>>(
+            static_cast<const __nv_bfloat16*>(dy), x, w, rstd, dres, accumulate, dw_part, N, d, G);
+    };
+    if (G == 1)
+      launch(std::false_type{});
+    else
+      launch(std::true_type{});
+    return true;
+  });
+  if (!done) {
+    if (dy_f32)
+      rmsnorm_bwd_kernel<float><<<grid, kRowThreads, 0, stream>>>(static_cast<const float*>(dy), x, w, rstd, dres,
+                                                                  accumulate, dw_part, N, d, G);
+    else
+      rmsnorm_bwd_kernel<__nv_bfloat16><<<grid, kRowThreads, 0, stream>>>(
+          static_cast<const __nv_bfloat16*>(dy), x, w, rstd, dres, accumulate, dw_part, N, d, G);
+  }
   TTB_CUDA_CHECK(cudaGetLastError());
   colsum_kernel<<<(d + 255) / 256, 256, 0, stream>>>(dw_part, grid, d, dw, dw_accumulate);
   TTB_CUDA_CHECK(cudaGetLastError());

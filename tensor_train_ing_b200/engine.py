@@ -1,0 +1,81 @@
+"""The training-step engine: the public call a user (or a trainer) makes for one optimizer update.
+
+``TrainEngine.step(idx, doc_ids, targets)`` takes this rank's share of a global batch (CPU --
+ideally pinned -- or CUDA tensors), splits it into micro-batches, copies each to the device
+(non-blocking), runs forward/backward on the fused sm_100a path with the reference's
+loss-normalization contract (every rank back-propagates ``local_sum / global_valid_targets``),
+sums gradients across ranks, clips the global norm and steps the optimizer.  It returns the
+step's summed loss and valid-target count as device tensors (no host synchronisation).
+"""
+from __future__ import annotations
+
+import torch
+import torch.distributed as dist
+
+from .config import Config
+from .models.model import TensorLM
+from .optim import make_optimizer
+from .parallel.data_parallel import DataParallel
+
+
+class TrainEngine:
+    def __init__(self, cfg: Config, device="cuda", micro_batch: int = 8, model: TensorLM | None = None,
+                 optimizer=None, group=None, grad_clip: float | None = None):
+        self.cfg = cfg
+        self.device = torch.device(device)
+        self.micro_batch = int(micro_batch)
+        self.model = model if model is not None else TensorLM(cfg.model).to(self.device)
+        self.model.train()
+        self.optimizer = optimizer if optimizer is not None else make_optimizer(self.model, cfg.train)
+        self.group = group
+        self.world = dist.get_world_size(group) if dist.is_available() and dist.is_initialized() else 1
+        self.grad_clip = cfg.train.grad_clip if grad_clip is None else grad_clip
+        self.fused = self.device.type == "cuda" and self.model.fused_path_supported()[0]
+        self.dp = DataParallel(self.model, self.device, group) if self.fused else None
+        self.last_grad_norm = None
+
+    def _to_device(self, t):
+        if t.device == self.device:
+            return t
+        return t.to(self.device, non_blocking=True)
+
+    def zero_grad(self):
+        if self.dp is not None:
+            self.dp.zero_grad()
+        else:
+            self.optimizer.zero_grad(set_to_none=True)
+
+    def forward_backward(self, idx, doc_ids, targets, inv_count):
+        """Accumulate gradients of sum(loss) * inv_count over micro-batches; returns the loss sum."""
+        loss_total = torch.zeros((), device=self.device, dtype=torch.float32)
+        rows = idx.shape[0]
+        for s in range(0, rows, self.micro_batch):
+            e = min(rows, s + self.micro_batch)
+            i, d, t = (self._to_device(x[s:e]) for x in (idx, doc_ids, targets))
+            _, loss, _ = self.model(i, d, t, reduction="sum")
+            (loss * inv_count).backward()
+            loss_total += loss.detach().float()
+        return loss_total
+
+    def step(self, idx, doc_ids, targets, lr_multiplier: float | None = None):
+        """One optimizer update on this rank's rows.  Returns (loss_sum, global_count) on the device."""
+        if lr_multiplier is not None:
+            for g in self.optimizer.param_groups:
+                g["lr"] = g.get("base_lr", g["lr"]) * lr_multiplier
+        self.zero_grad()
+        # valid-target count: counted on the host side of the copy, summed over ranks on the device
+        local = (targets != -100).sum()
+        count = local.to(self.device, non_blocking=True).to(torch.int64)
+        if self.world > 1:
+            dist.all_reduce(count, group=self.group)
+        inv = 1.0 / count.clamp_min(1).to(torch.float32)
+        loss_sum = self.forward_backward(idx, doc_ids, targets, inv)
+        if self.dp is not None:
+            self.dp.reduce_gradients()
+        if self.world > 1:
+            dist.all_reduce(loss_sum, group=self.group)
+        params = [p for p in self.model.parameters() if p.grad is not None]
+        if self.grad_clip and self.grad_clip > 0:
+            self.last_grad_norm = torch.nn.utils.clip_grad_norm_(params, self.grad_clip, foreach=True)
+        self.optimizer.step()
+        return loss_sum, count

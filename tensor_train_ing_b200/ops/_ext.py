@@ -10,13 +10,61 @@ import importlib
 
 _C = None
 _ERR: Exception | None = None
+_PROXY = None
+
+# kernels launched by one call of each binding (used by the launch counter)
+KERNELS_PER_CALL = {"mm": 1, "bilinear": 1, "bilinear_grad": 1, "rmsnorm_fwd": 1, "rmsnorm_bwd": 2, "rope_": 1,
+                    "embed_fwd": 1, "embed_bwd": 1, "ce_fwd": 2, "ce_bwd_logits": 1, "poly_fwd": 1,
+                    "poly_bwd": 2, "qkv_rope": 1, "adamw_step": 1, "muon_prep": 1}
+
+
+class _Counting:
+    """Proxy over the extension that counts the kernels each binding launches while enabled."""
+
+    def __init__(self, mod):
+        self._mod = mod
+        self.enabled = False
+        self.count = 0
+        self.by_name: dict[str, int] = {}
+
+    def __getattr__(self, name):
+        fn = getattr(self._mod, name)
+        k = KERNELS_PER_CALL.get(name)
+        if k is None or not callable(fn):
+            return fn
+
+        def wrapped(*args, **kwargs):
+            if self.enabled:
+                self.count += k
+                self.by_name[name] = self.by_name.get(name, 0) + k
+            return fn(*args, **kwargs)
+
+        object.__setattr__(self, name, wrapped)
+        return wrapped
+
+
+class launch_counter:
+    """Context manager: ``with launch_counter() as c: ...; c.count`` = sm_100a kernels launched."""
+
+    def __enter__(self):
+        lib()
+        _PROXY.enabled = True
+        _PROXY.count = 0
+        _PROXY.by_name = {}
+        return self
+
+    def __exit__(self, *exc):
+        _PROXY.enabled = False
+        self.count = _PROXY.count
+        self.by_name = dict(_PROXY.by_name)
+        return False
 
 
 def lib():
     """Return the compiled extension module, raising a clear error if it cannot be loaded."""
-    global _C, _ERR
-    if _C is not None:
-        return _C
+    global _C, _ERR, _PROXY
+    if _PROXY is not None:
+        return _PROXY
     try:
         _C = importlib.import_module("tensor_train_ing_b200._C")
     except Exception as e:  # pragma: no cover - depends on the build
@@ -24,7 +72,8 @@ def lib():
         raise RuntimeError(
             "tensor_train_ing_b200._C (the sm_100a kernel library) is not built or failed to load: "
             f"{e!r}. Build it with `python setup.py build_ext --inplace`.") from e
-    return _C
+    _PROXY = _Counting(_C)
+    return _PROXY
 
 
 def available() -> bool:

@@ -26,12 +26,35 @@ def _weights(owner, name, linears):
     return group_for(owner, name, [l.weight for l in linears])
 
 
+def model_weight_groups(model):
+    """Every (owner, name, linears) weight group the fused path uses, in backward order
+    (unembed first, then blocks from last to first, embedding last).  Spectral layers are
+    excluded (their effective weights are recomputed every forward)."""
+    out = [(model, "unembed", [model.unembed])]
+    for blk in reversed(model.blocks):
+        a, m = blk.attn, blk.mlp
+        for owner, name, lins in ((m, "d", [m.d]), (m, "r", [m.r]), (m, "l", [m.l]), (a, "o", [a.o]),
+                                  (a, "qkv", a.projections())):
+            if not any(isinstance(l, SpectralLinear) for l in lins):
+                out.append((owner, name, lins))
+    out.append((model, "embed", [model.embed]))
+    return out
+
+
+def rope_context(pos32: torch.Tensor, T: int, dk: int, base: float) -> dict:
+    """cos/sin tables [T, dk/2] computed exactly as the reference's rope_tables (fp32 torch ops),
+    indexed by position-in-document inside the kernels."""
+    positions = torch.arange(T, device=pos32.device)
+    angle = positions.float().unsqueeze(-1) * rope_inv_freq(dk, base, pos32.device)
+    return {"pos32": pos32, "cos": angle.cos().contiguous(), "sin": angle.sin().contiguous()}
+
+
 def fused_context(model, doc_ids, pos):
     cfg = model.cfg
     tables = fused.attention_tables(doc_ids)
     row_scale = {p: row_scale_vector(doc_ids, p).contiguous().view(-1) for p in model._row_powers()}
-    return {"fused": True, "tables": tables, "row_scale": row_scale,
-            "pos32": tables["pos32"], "inv_freq": rope_inv_freq(cfg.d_key, cfg.rope_base, doc_ids.device)}
+    rope = rope_context(tables["pos32"], tables["T"], cfg.d_key, cfg.rope_base)
+    return {"fused": True, "tables": tables, "row_scale": row_scale, "rope": rope}
 
 
 def norm_to_bf16(norm: nn.Module, x: torch.Tensor) -> torch.Tensor:
@@ -65,7 +88,7 @@ def attention_branch(blk, h, ctx):
     grp = _weights(a, "qkv", projs)
     two = a.kind != "offset_square"
     n_qk = 4 if two else 2
-    qkv = fused.qkv_rope(h, grp, n_qk * H * dk, dk, ctx["pos32"], ctx["inv_freq"])
+    qkv = fused.qkv_rope(h, grp, n_qk * H * dk, dk, ctx["rope"])
     if two:
         cols = [0, H * dk, 2 * H * dk, 3 * H * dk, 4 * H * dk]
     else:
@@ -73,7 +96,8 @@ def attention_branch(blk, h, ctx):
     if a.record_score_bound:
         _record_bound(a, qkv, cols, h.shape[0])
     kpar = getattr(a, "b", None) if a.kind == "offset_square" else getattr(a, "coef", None)
-    return fused.poly_attention(qkv, kpar, a.kind, dk, dv, H, cols, ctx["tables"], ctx["row_scale"][a.row_power])
+    return fused.poly_attention(qkv, kpar, a.kind, dk, dv, H, cols, ctx["tables"], ctx["row_scale"][a.row_power],
+                                ctx["rope"])
 
 
 def block_forward(blk, x, ctx):

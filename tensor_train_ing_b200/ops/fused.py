@@ -82,36 +82,33 @@ def linear(x, group, residual=None, alpha=1.0, bias=None):
 
 # ============================================================================ QKV + RoPE
 class QKVRopeFn(torch.autograd.Function):
-    """qkv = x W_cat^T (bf16 [N, sum rows]) with RoPE applied in place to the first rope_cols columns."""
+    """qkv = x W_cat^T (bf16 [N, sum rows]) with RoPE on the first rope_cols columns, applied in the
+    GEMM epilogue.  The backward receives a gradient that the attention backward has already
+    rotated back (it writes dq/dk w.r.t. the pre-rotation projections), so only GEMMs remain."""
 
     @staticmethod
-    def forward(ctx, x, group, rope_cols, dk, pos32, inv_freq, *weights):
+    def forward(ctx, x, group, rope_cols, dk, rope, *weights):
         w16 = group.bf16()
-        qkv = torch.empty(x.shape[0], w16.shape[0], device=x.device, dtype=torch.bfloat16)
-        _mm(x, w16.t(), qkv)
-        if rope_cols:
-            lib().rope_(qkv, int(rope_cols), int(dk), pos32, inv_freq, False)
-        ctx.save_for_backward(x, pos32, inv_freq)
-        ctx.group, ctx.rope_cols, ctx.dk = group, rope_cols, dk
+        qkv = lib().qkv_rope(x, w16, int(rope_cols), int(dk), rope["pos32"], rope["cos"], rope["sin"])
+        ctx.save_for_backward(x)
+        ctx.group = group
         return qkv
 
     @staticmethod
     def backward(ctx, dqkv):
-        x, pos32, inv_freq = ctx.saved_tensors
-        # the attention backward hands over a fresh buffer it owns: undo RoPE in place there
-        owned = getattr(dqkv, "_ttb_owned", False) and dqkv.is_contiguous()
-        g = dqkv if owned else dqkv.contiguous().clone()
-        if ctx.rope_cols:
-            lib().rope_(g, int(ctx.rope_cols), int(ctx.dk), pos32, inv_freq, True)
+        (x,) = ctx.saved_tensors
+        if not getattr(dqkv, "_ttb_unrotated", False):
+            raise RuntimeError("QKVRopeFn expects the gradient produced by PolyAttentionFn (rotary already undone)")
+        g = dqkv.contiguous()
         w16 = ctx.group.bf16()
         dx = torch.empty(x.shape[0], x.shape[1], device=x.device, dtype=torch.float32)
         _mm(g, w16, dx)
         grads = ctx.group.sink_grad(lambda out, beta: _mm(g.t(), x, out, c=out, beta=beta))
-        return (dx, None, None, None, None, None, *grads)
+        return (dx, None, None, None, None, *grads)
 
 
-def qkv_rope(x, group, rope_cols, dk, pos32, inv_freq):
-    return QKVRopeFn.apply(x, group, rope_cols, dk, pos32, inv_freq, *group.params)
+def qkv_rope(x, group, rope_cols, dk, rope):
+    return QKVRopeFn.apply(x, group, rope_cols, dk, rope, *group.params)
 
 
 # ============================================================================ polynomial attention
@@ -137,7 +134,7 @@ class PolyAttentionFn(torch.autograd.Function):
     """y [N, H*dv] = polynomial attention of the fused qkv buffer (see csrc/attn)."""
 
     @staticmethod
-    def forward(ctx, qkv, kpar, kind, dk, dv, H, cols, tables, row_scale):
+    def forward(ctx, qkv, kpar, kind, dk, dv, H, cols, tables, row_scale, rope=None):
         kid = KIND_ID[kind]
         par = torch.zeros(H, 4, device=qkv.device, dtype=torch.float32)
         if kind == "offset_square":
@@ -147,25 +144,28 @@ class PolyAttentionFn(torch.autograd.Function):
         y = lib().poly_fwd(kid, dk, dv, qkv, list(cols), tables["pos32"], tables["doc32"], row_scale, par,
                            tables["B"], tables["T"], H)
         ctx.save_for_backward(qkv, par, row_scale)
-        ctx.meta = (kind, kid, dk, dv, H, list(cols), tables, kpar is not None)
+        ctx.meta = (kind, kid, dk, dv, H, list(cols), tables, kpar is not None, rope)
         return y
 
     @staticmethod
     def backward(ctx, dy):
         qkv, par, row_scale = ctx.saved_tensors
-        kind, kid, dk, dv, H, cols, tables, has_par = ctx.meta
+        kind, kid, dk, dv, H, cols, tables, has_par, rope = ctx.meta
         dqkv, dpar = lib().poly_bwd(kid, dk, dv, qkv, cols, dy.contiguous(), tables["pos32"], tables["doc32"],
-                                    tables["doc_end32"], row_scale, par, tables["B"], tables["T"], H)
-        dqkv._ttb_owned = True
+                                    tables["doc_end32"], row_scale, par, tables["B"], tables["T"], H,
+                                    rope["cos"] if rope else None, rope["sin"] if rope else None)
+        dqkv._ttb_unrotated = rope is not None
         dk_par = None
         if has_par:
             g = dpar.view(tables["B"], H, -1, 4).sum(dim=(0, 2))  # fixed-order reduction
             dk_par = g[:, 0].clone() if kind == "offset_square" else g
-        return dqkv, dk_par, None, None, None, None, None, None, None
+        return dqkv, dk_par, None, None, None, None, None, None, None, None
 
 
-def poly_attention(qkv, kpar, kind, dk, dv, H, cols, tables, row_scale):
-    return PolyAttentionFn.apply(qkv, kpar, kind, dk, dv, H, cols, tables, row_scale)
+def poly_attention(qkv, kpar, kind, dk, dv, H, cols, tables, row_scale, rope=None):
+    """``rope``: the rotary tables the projection used; the backward then returns gradients
+    w.r.t. the pre-rotation projections (the inverse rotation runs in its epilogues)."""
+    return PolyAttentionFn.apply(qkv, kpar, kind, dk, dv, H, cols, tables, row_scale, rope)
 
 
 # ============================================================================ bilinear MLP

@@ -98,6 +98,24 @@ def test_rmsnorm_fwd_bwd_groups():
         assert rel(w.grad, wr.grad) < 1e-2
 
 
+def test_qkv_rope_gemm_matches_reference_rope():
+    torch.manual_seed(5)
+    from tensor_train_ing_b200.ops.block import rope_context
+    B, T, H, dk = 2, 100, 2, 64
+    docs = make_docs(B, T, pad=False).cuda()
+    pos = doc_positions(docs)
+    x = torch.randn(B * T, 256, device="cuda").bfloat16()
+    w = (torch.randn(5 * H * dk, 256, device="cuda") / 16).bfloat16()
+    rope = rope_context(pos.to(torch.int32).contiguous().view(-1), T, dk, 10000.0)
+    out = lib().qkv_rope(x, w, 4 * H * dk, dk, rope["pos32"], rope["cos"], rope["sin"])
+    raw = (x.float() @ w.float().t())
+    cos, sin = rope_tables(pos, dk, 10000.0)
+    qk = raw[:, :4 * H * dk].view(B, T, 4 * H, dk).transpose(1, 2)
+    ref = apply_rope(qk, cos, sin).transpose(1, 2).reshape(B * T, -1)
+    assert rel(out[:, :4 * H * dk].float(), ref) < 1e-2
+    assert rel(out[:, 4 * H * dk:].float(), raw[:, 4 * H * dk:]) < 1e-2
+
+
 def test_rope_roundtrip():
     torch.manual_seed(2)
     B, T, H, dk = 2, 100, 3, 64
