@@ -1,0 +1,757 @@
+"""Frozen held-out evaluation, paired comparisons and exact-label mechanism probes
+(reference tnlm/evaluate.py:22-945).
+
+* ``evaluate_checkpoint``: CE on a context-independent validation target plan (source target
+  offsets 1..L-1 of documents in ``documents.jsonl`` order, up to a token cap), with a
+  document-bootstrap CI, proof that the model/buffers were not mutated, and an exact-document
+  overlap audit of the validation split against training data;
+* ``compare_evaluations``: paired per-document bootstrap of CE_right - CE_left on identical plans;
+* ``evaluate_mechanisms``: answer-token CE/accuracy on held-out task compositions, branch removal
+  and final-position activation transfer between same-task donors;
+* ``_training_descriptor`` / ``_training_comparison``: what a checkpoint says about its training.
+"""
+from __future__ import annotations
+
+import copy
+import hashlib
+import json
+import math
+import os
+import time
+from pathlib import Path
+
+import numpy as np
+import torch
+import torch.nn.functional as F
+
+from .budget import SpendLedger
+from .calibration import _check_lagged_divisor
+from .config import Config
+from .models.model import TensorLM
+from .models.normalization import lagged_modules
+from .runtime import evaluation_validator
+
+
+def _integer(v, minimum=0):
+    return v if type(v) is int and v >= minimum else None
+
+
+def _number(v, nonnegative=True):
+    return v if type(v) in (int, float) and math.isfinite(v) and (not nonnegative or v >= 0) else None
+
+
+def _history(progress, key, check_entry, fresh_source, fork_source, last_check):
+    history = progress.get(key)
+    if not isinstance(history, list) or not history:
+        return None, "unknown"
+    entries, complete = [], True
+    prev_tokens = prev_step = None
+    for i, e in enumerate(history):
+        if not isinstance(e, dict) or not check_entry(e, entries):
+            return None, "unknown"
+        tokens, step, source = e.get("start_tokens"), e.get("start_step"), e.get("source")
+        if i == 0 and source == "legacy_unknown" and tokens is None and step is None:
+            complete = False
+        else:
+            if any(type(v) is not int or v < 0 for v in (tokens, step)):
+                return None, "unknown"
+            if i == 0 and (source != fresh_source or tokens != 0 or step != 0):
+                return None, "unknown"
+            if i > 0 and (source != fork_source or (prev_tokens is not None and tokens < prev_tokens)
+                          or (prev_step is not None and step < prev_step)):
+                return None, "unknown"
+            if (type(progress.get("tokens")) is not int or tokens > progress["tokens"]
+                    or type(progress.get("steps")) is not int or step > progress["steps"]):
+                return None, "unknown"
+        entries.append(e)
+        prev_tokens, prev_step = tokens, step
+    if not last_check(entries[-1]):
+        return None, "unknown"
+    return entries, "complete" if complete else "partial"
+
+
+def _context_history_descriptor(progress, context):
+    def check(e, prior):
+        ctx = e.get("context")
+        return type(ctx) is int and ctx > 0 and (not prior or e.get("source") == "legacy_unknown"
+                                                 or ctx > prior[-1]["context"])
+    entries, status = _history(progress, "context_history", check, "fresh", "context_fork",
+                               lambda last: last["context"] == context)
+    if entries is None:
+        return None, status
+    return [{k: e.get(k) for k in ("context", "start_tokens", "start_step", "source")} for e in entries], status
+
+
+def _batch_history_descriptor(progress, train):
+    rate = lambda v: type(v) in (int, float) and math.isfinite(v) and v >= 0  # noqa: E731
+
+    def check(e, prior):
+        batch, scale = e.get("batch_tokens"), e.get("lr_scale", 1.0)
+        ok = (type(batch) is int and batch > 0 and rate(e.get("lr")) and "aux_adamw_lr" in e
+              and (e["aux_adamw_lr"] is None or rate(e["aux_adamw_lr"])) and rate(scale) and scale > 0)
+        if not prior and scale != 1:
+            return False
+        if prior and e.get("source") == "batch_branch" and "lr_scale" not in e:
+            return False
+        return ok
+
+    def last_ok(last):
+        return (last["batch_tokens"] == train.get("global_prediction_tokens_per_update")
+                and last["lr"] == train.get("lr") and last["aux_adamw_lr"] == train.get("aux_adamw_lr"))
+    entries, status = _history(progress, "batch_history", check, "fresh", "batch_branch", last_ok)
+    if entries is None:
+        return None, status
+    return [{"batch_tokens": e["batch_tokens"], "lr": e["lr"], "aux_adamw_lr": e["aux_adamw_lr"],
+             "start_tokens": e.get("start_tokens"), "start_step": e.get("start_step"), "source": e.get("source"),
+             "lr_scale": e.get("lr_scale", 1.0)} for e in entries], status
+
+
+def _training_descriptor(payload) -> dict:
+    """Training evidence recorded in a checkpoint payload (never evaluation overrides)."""
+    as_map = lambda v: v if isinstance(v, dict) else {}  # noqa: E731
+    config, progress, extra = (as_map(payload.get(k)) for k in ("config", "progress", "extra"))
+    train, model, data = (as_map(config.get(k)) for k in ("train", "model", "data"))
+    ctx_hist, ctx_status = _context_history_descriptor(progress, data.get("context", 512))
+    batch_hist, batch_status = _batch_history_descriptor(progress, train)
+    text = lambda v: v if isinstance(v, str) and v else None  # noqa: E731
+    schedule = as_map(progress.get("distributed_schedule"))
+    candidates = [(src, vals["cooldown_steps"]) for src, vals in (("progress.distributed_schedule", schedule),
+                                                                  ("extra", extra))
+                  if "cooldown_steps" in vals and (vals["cooldown_steps"] is None
+                                                   or _integer(vals["cooldown_steps"], 1) is not None)]
+    notes, cooldown_steps = [], None
+    start = _integer(progress.get("cooldown_start_tokens"))
+    if candidates and len({v for _, v in candidates}) > 1:
+        cooldown = "unknown"
+        notes.append("conflicting checkpoint cooldown metadata")
+    elif candidates:
+        cooldown_steps = candidates[0][1]
+        cooldown = "uncooled" if cooldown_steps is None else "cooled"
+        if cooldown == "uncooled" and start is not None:
+            cooldown = "unknown"
+            notes.append("cooldown start conflicts with explicit uncooled metadata")
+    elif start is not None:
+        cooldown = "cooled"
+        notes.append("cooldown branch start exists but its step horizon is missing")
+    else:
+        cooldown = "unknown"
+        notes.append("checkpoint has no explicit cooldown branch evidence")
+    tokens = _integer(progress.get("tokens"))
+    rung = _integer(train.get("rung_total_tokens"), 1)
+    batch = _integer(train.get("global_prediction_tokens_per_update"), 1)
+    sched = _integer(progress.get("scheduler_step"))
+    target = rung if cooldown == "uncooled" else None
+    if cooldown == "cooled" and None not in (start, cooldown_steps, batch):
+        target = start + cooldown_steps * batch
+    invalid_end = False
+    if "cooldown_end_tokens" in progress:
+        end = _integer(progress["cooldown_end_tokens"], 1)
+        if (cooldown != "cooled" or None in (end, start, cooldown_steps, batch)
+                or not start + (cooldown_steps - 1) * batch < end <= start + cooldown_steps * batch):
+            invalid_end, target = True, None
+            notes.append("invalid explicit cooldown token endpoint")
+        else:
+            target = end
+    completion = "unknown"
+    if target is not None and tokens is not None:
+        completion = "complete" if tokens >= target else "partial"
+        if cooldown == "cooled" and sched is not None and (tokens >= target) != (sched >= cooldown_steps):
+            completion = "unknown"
+            notes.append("cooldown token and scheduler-step completion evidence disagree")
+    elif not invalid_end and cooldown == "cooled" and cooldown_steps is not None and sched is not None:
+        completion = "complete" if sched >= cooldown_steps else "partial"
+    if train.get("schedule") == "cosine":
+        expected = (rung + batch - 1) // batch if rung is not None and batch is not None else None
+        if (cooldown != "uncooled" or None in (expected, sched, tokens) or sched > expected or tokens > rung
+                or (tokens == rung) != (sched == expected)):
+            completion = "unknown"
+            notes.append("cosine token and scheduler horizon evidence is missing or inconsistent")
+    disabled_or = lambda key: ("disabled" if key in model and model[key] is None  # noqa: E731
+                               else _integer(model.get(key), 1))
+    return {"version": 1, "source": "checkpoint_payload",
+            "config_compatibility": copy.deepcopy(payload.get("config_compatibility", {})),
+            "configuration": copy.deepcopy({k: v for k, v in config.items() if k != "project"}),
+            "optimizer": text(train.get("optimizer")), "seed": _integer(train.get("seed")),
+            "width": _integer(model.get("d_model"), 1), "depth": _integer(model.get("layers"), 1),
+            "train_context": _integer(data.get("context"), 1), "rung_total_tokens": rung,
+            "context_history": ctx_hist, "context_history_status": ctx_status,
+            "batch_history": batch_hist, "batch_history_status": batch_status,
+            "normalization": text(model.get("normalization")), "attention": text(model.get("attention")),
+            "width_scaling_base": disabled_or("width_scaling_base"),
+            "width_lr_exponent": _number(model.get("width_lr_exponent"), False),
+            "width_logit_exponent": _number(model.get("width_logit_exponent"), False),
+            "depth_scaling_base": disabled_or("depth_scaling_base"),
+            "depth_lr_exponent": _number(model.get("depth_lr_exponent"), False),
+            "depth_residual_base": disabled_or("depth_residual_base"),
+            "depth_residual_exponent": _number(model.get("depth_residual_exponent"), False),
+            "residual_alpha": _number(model.get("residual_alpha"), False),
+            "weight_decay_hidden": _number(train.get("weight_decay_hidden")),
+            "beta1": _number(train.get("beta1")), "beta2": _number(train.get("beta2")),
+            "aux_adamw_lr": ("default_to_lr" if "aux_adamw_lr" in train and train["aux_adamw_lr"] is None
+                             else _number(train.get("aux_adamw_lr"))),
+            "actual_prediction_tokens": tokens, "optimizer_steps": _integer(progress.get("steps")),
+            "global_prediction_tokens_per_update": batch, "lr": _number(train.get("lr")),
+            "schedule": text(train.get("schedule")), "scheduler_step": sched,
+            "warmup_steps": _integer(progress.get("warmup_steps"), 1), "cooldown_status": cooldown,
+            "cooldown_steps": cooldown_steps, "cooldown_start_tokens": start,
+            "segment_target_prediction_tokens": target, "completion_status": completion, "evidence_notes": notes,
+            "completion_scope": "declared training segment token/step endpoint only; no automatic experiment "
+                                "completion, fairness, or ranking claim"}
+
+
+_COMPARED = ("optimizer", "seed", "width", "depth", "train_context", "context_history", "batch_history",
+             "rung_total_tokens", "actual_prediction_tokens", "global_prediction_tokens_per_update", "lr",
+             "normalization", "attention", "width_scaling_base", "width_lr_exponent", "width_logit_exponent",
+             "aux_adamw_lr", "schedule", "cooldown_status", "cooldown_steps", "segment_target_prediction_tokens",
+             "completion_status", "warmup_steps", "depth_scaling_base", "depth_lr_exponent", "depth_residual_base",
+             "depth_residual_exponent", "residual_alpha", "weight_decay_hidden", "beta1", "beta2")
+
+
+def _training_comparison(left, right) -> dict:
+    def descriptor(report):
+        v = report.get("training_descriptor")
+        return v if isinstance(v, dict) and v.get("version") == 1 and v.get("source") == "checkpoint_payload" else {}
+    ds = descriptor(left), descriptor(right)
+    dims = {}
+    for f in _COMPARED:
+        vals = [d.get(f) for d in ds]
+        if f == "cooldown_steps":
+            vals = ["not_applicable" if d.get("cooldown_status") == "uncooled" and f in d and v is None else v
+                    for d, v in zip(ds, vals)]
+        known = all(v is not None and v != "unknown" for v in vals)
+        if f == "context_history":
+            known = known and all(d.get("context_history_status") == "complete" for d in ds)
+        if f == "batch_history":
+            known = known and all(d.get("batch_history_status") == "complete" for d in ds)
+        dims[f] = {"status": ("matched" if vals[0] == vals[1] else "different") if known else "unknown",
+                   "left": vals[0], "right": vals[1]}
+    return {"dimensions": dims, "matched_dimensions": [k for k, v in dims.items() if v["status"] == "matched"],
+            "different_dimensions": [k for k, v in dims.items() if v["status"] == "different"],
+            "unknown_dimensions": [k for k, v in dims.items() if v["status"] == "unknown"],
+            "automatic_ranking_eligible": False,
+            "scope": "training evidence summary only; equality of missing evidence is never inferred"}
+
+
+def _tensor_hash(items) -> str:
+    h = hashlib.sha256()
+    for name, value in sorted(items):
+        value = value.detach().cpu().contiguous()
+        h.update(json.dumps([name, str(value.dtype), list(value.shape)]).encode())
+        h.update(value.reshape(-1).view(torch.uint8).numpy().tobytes())
+    return h.hexdigest()
+
+
+def _file_hash(path, deadline=lambda: None) -> str:
+    h = hashlib.sha256()
+    with open(path, "rb") as fh:
+        for block in iter(lambda: fh.read(1 << 20), b""):
+            deadline()
+            h.update(block)
+    return h.hexdigest()
+
+
+def _ledger(project):
+    return SpendLedger(project.get("spend_ledger", "runs/spend.json"), project.get("total_budget_usd", 1000),
+                       project.get("reserve_usd", 150), stage_budgets=project.get("stage_budgets"))
+
+
+def evaluate_checkpoint(cfg, checkpoint, out_dir, *, context=None, max_prediction_tokens=1_000_000, max_seconds,
+                        device="cpu", bootstrap_samples=1000, run_budget_usd=None) -> dict:
+    from .checkpoint import load_checkpoint
+    from .data import PackedSampler, audit_validation_overlap, manifest_hash, validate_tokenizer_compatibility
+    if isinstance(cfg, (str, Path)):
+        cfg = Config.from_yaml(str(cfg))
+    project, data = cfg.raw.get("project", {}), cfg.raw.get("data", {})
+    probe_context = data.get("context", 512) if context is None else context
+    if project.get("dry_run", True):
+        return {"dry_run": True, "command": "evaluate", "checkpoint": str(checkpoint), "context": probe_context,
+                "max_prediction_tokens": max_prediction_tokens, "split": "val",
+                "target_policy": "canonical document order; source target offsets 1..L-1"}
+    if (type(probe_context) is not int or probe_context <= 0 or type(max_prediction_tokens) is not int
+            or max_prediction_tokens <= 0 or type(bootstrap_samples) is not int or not 0 <= bootstrap_samples <= 100_000
+            or not math.isfinite(max_seconds) or max_seconds <= 0):
+        raise ValueError("positive evaluation bounds and bootstrap_samples in [0, 100000] required")
+    dev = torch.device(device)
+    if dev.type == "cuda" and not torch.cuda.is_available():
+        raise RuntimeError("CUDA requested but unavailable")
+    rate = project.get("gpu_hourly_rate_usd")
+    if rate is None or (dev.type == "cuda" and rate <= 0):
+        raise ValueError("declare actual gpu_hourly_rate_usd (explicit 0 allowed for CPU)")
+    out_dir = Path(out_dir)
+    if out_dir.exists():
+        raise FileExistsError(f"evaluation directory already exists: {out_dir}")
+    ledger = _ledger(project)
+    run_id = str(out_dir.resolve())
+    ledger.begin(run_id, rate, max_seconds, run_budget_usd, parent_checkpoint=checkpoint,
+                 cost_margin_fraction=project.get("cost_margin_fraction", .1), stage=project.get("stage", "A"))
+    started, status = time.monotonic(), "failed"
+
+    def deadline():
+        if time.monotonic() - started >= max_seconds:
+            raise TimeoutError("evaluation runtime cap exhausted")
+
+    try:
+        out_dir.mkdir(parents=True, exist_ok=False)
+        train_hash = manifest_hash(data["manifest"])
+        val_path = cfg.raw.get("evaluation", {}).get("validation_manifest", data["manifest"])
+        tok_compat = validate_tokenizer_compatibility(data["manifest"], val_path, allow_test_only=dev.type == "cpu")
+        eval_seed = int(cfg.raw.get("evaluation", {}).get("seed", 0))
+        sampler = PackedSampler(val_path, split="val", batch_size=1, context=probe_context, seed=eval_seed)
+        ranges, remaining = [], max_prediction_tokens
+        for i in range(len(sampler.docs)):
+            doc = sampler.docs[i]
+            count = min(max(0, sampler.docs.length(i) - 1), remaining)
+            if count:
+                ranges.append({"document_id": doc["id"], "target_start": 1, "target_end": count + 1, "count": count})
+                remaining -= count
+            if not remaining:
+                break
+        if not ranges:
+            raise ValueError("validation split has no prediction targets")
+        audit = audit_validation_overlap(data["manifest"], val_path, document_ids=[r["document_id"] for r in ranges])
+        (out_dir / "data-overlap-audit.json").write_text(json.dumps(audit, indent=2) + "\n")
+        if audit["has_overlap"]:
+            raise ValueError("held-out validation has exact whole-document content overlap; see data-overlap-audit.json")
+        model = TensorLM(cfg.model)
+        payload = load_checkpoint(checkpoint, model, config_validator=evaluation_validator(cfg),
+                                  expected_manifest_hash=train_hash, restore_rng=False, map_location="cpu")
+        model.to(dev).eval()
+        ckpt_progress, ckpt_code = payload["progress"], payload["code"]
+        descriptor = _training_descriptor(payload)
+        del payload
+        for norm in lagged_modules(model):
+            norm.collecting = False
+            norm.set_valid_mask(None)
+            _check_lagged_divisor(norm)
+        before_model, before_buffers = _tensor_hash(model.state_dict().items()), _tensor_hash(model.named_buffers())
+        plan = {"version": 1, "validation_manifest_sha256": sampler.manifest_hash, "split": "val",
+                "ordering": "immutable documents.jsonl order",
+                "offset_semantics": "processed document stream; includes synthetic EOS if present", "ranges": ranges}
+        plan_hash = hashlib.sha256(json.dumps(plan, sort_keys=True, separators=(",", ":")).encode()).hexdigest()
+        selected = {r["document_id"]: r for r in ranges}
+        totals = {r["document_id"]: {"loss_sum": 0.0, "tokens": 0} for r in ranges}
+        prefixes, fwd_tokens, fwd_batches = {}, 0, 0
+        prefix_digest = hashlib.sha256()
+        initial = sampler.state_dict()
+        with torch.inference_mode():
+            for _ in range(sampler.epoch_row_count):
+                deadline()
+                idx, docs, orig = sampler.next_batch()
+                targets = torch.full_like(orig, -100)
+                positions = []
+                for m in sampler.batch_mappings()[0]["ranges"]:
+                    row = selected.get(m["document_id"])
+                    if row is None:
+                        continue
+                    s, e = m["packed_token_start"], m["packed_token_end"]
+                    for j in range(s, min(e - 1, probe_context)):
+                        off = m["source_token_start"] + j - s + 1
+                        if row["target_start"] <= off < row["target_end"]:
+                            if orig[0, j] == -100:
+                                raise ValueError("selected validation target was masked by sampler")
+                            targets[0, j] = orig[0, j]
+                            positions.append((j, m["document_id"], j - s + 1, off))
+                if not positions:
+                    continue
+                logits = model(idx.to(dev), doc_ids=docs.to(dev))
+                losses = F.cross_entropy(logits.float().flatten(0, 1), targets.to(dev).flatten(), reduction="none",
+                                         ignore_index=-100).cpu()
+                if not torch.isfinite(losses).all():
+                    raise FloatingPointError("nonfinite validation loss")
+                for j, doc_id, prefix, off in positions:
+                    if off != selected[doc_id]["target_start"] + totals[doc_id]["tokens"]:
+                        raise ValueError("duplicate or missing source target offset in evaluation")
+                    totals[doc_id]["loss_sum"] += float(losses[j])
+                    totals[doc_id]["tokens"] += 1
+                    prefixes[prefix] = prefixes.get(prefix, 0) + 1
+                    prefix_digest.update(json.dumps([doc_id, off, prefix], separators=(",", ":")).encode() + b"\n")
+                fwd_batches += 1
+                fwd_tokens += int((docs >= 0).sum())
+        for r in ranges:
+            if totals[r["document_id"]]["tokens"] != r["count"]:
+                raise ValueError("validation target plan was not evaluated exactly once")
+        after_model, after_buffers = _tensor_hash(model.state_dict().items()), _tensor_hash(model.named_buffers())
+        if before_model != after_model or before_buffers != after_buffers:
+            raise RuntimeError("evaluation changed checkpoint model or normalization buffers")
+        counts = np.asarray([r["tokens"] for r in totals.values()], dtype=np.int64)
+        sums = np.asarray([r["loss_sum"] for r in totals.values()], dtype=np.float64)
+        tokens, loss_sum = int(counts.sum()), float(sums.sum())
+        ci = None
+        if len(counts) >= 2 and bootstrap_samples:
+            rng = np.random.default_rng(eval_seed)
+            est = np.empty(bootstrap_samples)
+            for i in range(bootstrap_samples):
+                draw = rng.integers(0, len(counts), size=len(counts))
+                est[i] = sums[draw].sum() / counts[draw].sum()
+            ci = np.quantile(est, [.025, .975]).tolist()
+        pkg = Path(__file__).parent
+        runtime_sources = {f"{pkg.name}/{p.relative_to(pkg).as_posix()}": _file_hash(p) for p in sorted(pkg.rglob("*.py"))}
+        critical = ("models/model.py", "models/attention.py", "models/normalization.py", "config.py")
+        matches = {n: runtime_sources.get(f"{pkg.name}/{n}") == ckpt_code.get("source_sha256", {}).get(f"{pkg.name}/{n}")
+                   for n in critical}
+        ckpt = Path(checkpoint)
+        result = {"kind": "held_out_validation", "evaluation_protocol_version": 2, "data_overlap_audit": audit,
+                  "tokenizer_compatibility": tok_compat, "split": "val", "context": probe_context,
+                  "prediction_tokens": tokens, "loss_sum": loss_sum, "ce": loss_sum / tokens,
+                  "validation_below_one_million_targets": tokens < 1_000_000,
+                  "uncertainty": {"unit": "documents, not training seeds", "method": "token-weighted ratio document bootstrap",
+                                  "samples": bootstrap_samples, "seed": eval_seed, "ce_95_ci": ci, "documents": len(totals)},
+                  "target_plan": plan, "target_plan_sha256": plan_hash,
+                  "per_document": [{"document_id": k, **v} for k, v in totals.items()],
+                  "available_prefix_length_histogram": {str(k): v for k, v in sorted(prefixes.items())},
+                  "available_prefix_plan_sha256": prefix_digest.hexdigest(), "evaluation_seed": eval_seed,
+                  "training_manifest_sha256": train_hash, "validation_manifest_sha256": sampler.manifest_hash,
+                  "checkpoint": str(ckpt.resolve()), "checkpoint_manifest_sha256": _file_hash(ckpt / "manifest.json"),
+                  "checkpoint_state_sha256": _file_hash(ckpt / "state.pt"), "checkpoint_progress": ckpt_progress,
+                  "training_descriptor": descriptor, "operator_audit": model.operator_audit(),
+                  "model_sha256": before_model,
+                  "frozen_state": {"model_before": before_model, "model_after": after_model,
+                                   "buffers_before": before_buffers, "buffers_after": after_buffers, "unchanged": True},
+                  "sampler": {"initial": initial, "final": sampler.state_dict(), "rows_scanned": sampler.epoch_row_count,
+                              "forwarded_batches": fwd_batches},
+                  "probe": {"context_override": context, "batch_size": 1, "device": str(dev),
+                            "dtype": str(next(model.parameters()).dtype), "autocast": False,
+                            "checkpoint_code": ckpt_code, "runtime_source_sha256": runtime_sources,
+                            "critical_model_sources_match_checkpoint": all(matches.values()),
+                            "critical_model_source_matches": matches, "torch_version": str(torch.__version__),
+                            "deterministic_algorithms": torch.are_deterministic_algorithms_enabled()},
+                  "exposure": {"split": "val", "unique_prediction_tokens": tokens, "forward_input_tokens": fwd_tokens,
+                               "final_test_exposed": False}}
+        status = "complete"
+    finally:
+        ledger.finish(run_id, time.monotonic() - started, status)
+    result["billing"] = json.loads(ledger.path.read_text())["runs"][run_id]
+    (out_dir / "evaluation.json").write_text(json.dumps(result, indent=2, allow_nan=False) + "\n")
+    return result
+
+
+def _validated_report(value):
+    report = json.loads(Path(value).read_text()) if isinstance(value, (str, Path)) else value
+    if not isinstance(report, dict) or report.get("kind") != "held_out_validation" or report.get("split") != "val":
+        raise ValueError("comparison requires held_out_validation reports")
+    frozen = report.get("frozen_state", {})
+    if (frozen.get("unchanged") is not True or not frozen.get("model_before")
+            or frozen.get("model_before") != frozen.get("model_after")
+            or frozen.get("model_before") != report.get("model_sha256")
+            or not frozen.get("buffers_before") or frozen.get("buffers_before") != frozen.get("buffers_after")):
+        raise ValueError("evaluation lacks consistent frozen-state proof")
+    plan = report.get("target_plan")
+    if not isinstance(plan, dict) or plan.get("split") != "val":
+        raise ValueError("invalid validation target plan")
+    if hashlib.sha256(json.dumps(plan, sort_keys=True, separators=(",", ":")).encode()).hexdigest() != report.get("target_plan_sha256"):
+        raise ValueError("target-plan SHA256 mismatch")
+    if not plan.get("validation_manifest_sha256") or plan["validation_manifest_sha256"] != report.get("validation_manifest_sha256"):
+        raise ValueError("validation manifest identity mismatch")
+    ctx, ph = report.get("context"), report.get("available_prefix_plan_sha256")
+    if type(ctx) is not int or ctx <= 0 or not isinstance(ph, str) or len(ph) != 64:
+        raise ValueError("invalid context or prefix provenance")
+    audit = report.get("data_overlap_audit", {})
+    if (report.get("evaluation_protocol_version") != 2 or audit.get("has_overlap") is not False
+            or audit.get("training_manifest_hash") != report.get("training_manifest_sha256")
+            or audit.get("validation_manifest_hash") != report.get("validation_manifest_sha256")):
+        raise ValueError("evaluation lacks certified exact-document separation audit")
+    planned = {}
+    for r in plan.get("ranges") or []:
+        name, s, e, c = (r.get(k) for k in ("document_id", "target_start", "target_end", "count"))
+        if not isinstance(name, str) or name in planned or any(type(x) is not int for x in (s, e, c)) \
+                or s < 1 or e <= s or c != e - s:
+            raise ValueError("invalid or duplicate target range/count")
+        planned[name] = c
+    if not planned:
+        raise ValueError("empty target plan")
+    ids = hashlib.sha256(json.dumps(sorted(planned), separators=(",", ":"), ensure_ascii=True).encode()).hexdigest()
+    if audit.get("selected_validation_documents") != len(planned) or audit.get("selected_validation_ids_sha256") != ids:
+        raise ValueError("document separation audit differs from target plan")
+    by_doc = {}
+    for r in report.get("per_document") or []:
+        name, n, loss = r.get("document_id"), r.get("tokens"), r.get("loss_sum")
+        if (not isinstance(name, str) or name in by_doc or type(n) is not int or n <= 0
+                or isinstance(loss, bool) or not isinstance(loss, (int, float)) or not math.isfinite(loss) or loss < 0
+                or planned.get(name) != n):
+            raise ValueError("invalid per-document ID/count/loss")
+        by_doc[name] = (n, float(loss))
+    if set(by_doc) != set(planned):
+        raise ValueError("per-document IDs differ from target plan")
+    tt = sum(v[0] for v in by_doc.values())
+    tl = sum(v[1] for v in by_doc.values())
+    if (report.get("prediction_tokens") != tt or not math.isclose(report.get("loss_sum", -1), tl, rel_tol=1e-12, abs_tol=1e-10)
+            or not math.isclose(report.get("ce", -1), tl / tt, rel_tol=1e-12, abs_tol=1e-10)):
+        raise ValueError("aggregate losses/counts disagree with per-document state")
+    return report, by_doc
+
+
+def compare_evaluations(left, right, out_dir, *, bootstrap_samples=1000, seed=0) -> dict:
+    """Paired document bootstrap of CE_right - CE_left on identical target plans."""
+    if type(bootstrap_samples) is not int or not 0 <= bootstrap_samples <= 100_000:
+        raise ValueError("bootstrap_samples must be in [0, 100000]")
+    if type(seed) is not int or seed < 0:
+        raise ValueError("seed must be a nonnegative integer")
+    left, ld = _validated_report(left)
+    right, rd = _validated_report(right)
+    if left["target_plan"] != right["target_plan"] or left["validation_manifest_sha256"] != right["validation_manifest_sha256"]:
+        raise ValueError("evaluations have different target plans or validation manifests")
+    if set(ld) != set(rd) or any(ld[k][0] != rd[k][0] for k in ld):
+        raise ValueError("evaluations have different per-document targets/counts")
+    prefix_match = left["available_prefix_plan_sha256"] == right["available_prefix_plan_sha256"]
+    if left["context"] == right["context"] and not prefix_match:
+        raise ValueError("same-context evaluations have different available prefix plans")
+    names = sorted(ld)
+    counts = np.asarray([ld[k][0] for k in names], dtype=np.int64)
+    diffs = np.asarray([rd[k][1] - ld[k][1] for k in names], dtype=np.float64)
+    tokens = int(counts.sum())
+    ci = None
+    if len(names) >= 2 and bootstrap_samples:
+        rng = np.random.default_rng(seed)
+        est = np.empty(bootstrap_samples)
+        for i in range(bootstrap_samples):
+            draw = rng.integers(0, len(names), size=len(names))
+            est[i] = diffs[draw].sum() / counts[draw].sum()
+        ci = np.quantile(est, [.025, .975]).tolist()
+    ident = lambda r: {k: r.get(k) for k in (  # noqa: E731
+        "checkpoint", "checkpoint_manifest_sha256", "checkpoint_state_sha256", "checkpoint_progress",
+        "training_descriptor", "model_sha256", "operator_audit", "probe", "context", "evaluation_seed",
+        "available_prefix_plan_sha256", "available_prefix_length_histogram", "ce")}
+    result = {"kind": "matched_validation_comparison", "left": ident(left), "right": ident(right),
+              "validation_manifest_sha256": left["validation_manifest_sha256"],
+              "target_plan_sha256": left["target_plan_sha256"], "prediction_tokens": tokens, "documents": len(names),
+              "contexts_match": left["context"] == right["context"], "available_prefix_plans_match": prefix_match,
+              "training_comparison": _training_comparison(left, right), "automatic_ranking_eligible": False,
+              "prefix_comparison": ("identical available prefixes" if prefix_match
+                                    else "different available prefixes across contexts"),
+              "delta_ce_right_minus_left": float(diffs.sum() / tokens),
+              "uncertainty": {"method": "paired document bootstrap of token-weighted CE difference",
+                              "unit": "nominal document uncertainty; not training seeds or HPO correction",
+                              "bootstrap_samples": bootstrap_samples, "seed": seed, "delta_ce_95_ci": ci},
+              "interpretation": "matched-target predictive loss comparison; no automatic fair ranking"}
+    if out_dir is None:
+        return result
+    out_dir = Path(out_dir)
+    out_dir.mkdir(parents=True, exist_ok=False)
+    (out_dir / "comparison.json").write_text(json.dumps(result, indent=2, allow_nan=False) + "\n")
+    return result
+
+
+def _gpt2():
+    import tiktoken
+    tok = tiktoken.get_encoding("gpt2")
+    ranks = sorted((k.hex(), v) for k, v in tok._mergeable_ranks.items())
+    fp = hashlib.sha256(json.dumps({"ranks": ranks, "regex_pattern": tok._pat_str,
+                                    "special_tokens": tok._special_tokens}, sort_keys=True).encode()).hexdigest()
+    return tok, fp
+
+
+def evaluate_mechanisms(cfg, checkpoint, task_manifest, out_dir, *, max_examples=32, max_seconds=300, device="cpu",
+                        components=("0:attn", "0:mlp"), run_budget_usd=None, max_prompt_tokens=None, tokenizer=None):
+    """Answer-only exact-label probes with branch removal and final-position activation transfer.
+
+    ``tokenizer`` defaults to GPT-2 (tiktoken) and must match the training data's fingerprint; an
+    injected tokenizer (tests) must match an injected test-only training tokenizer by name."""
+    from .analysis import reference_path
+    from .checkpoint import load_checkpoint
+    from .data import manifest_hash
+    from .tasks import audit_mechanism_training, load_mechanism_tasks
+    if isinstance(cfg, (str, Path)):
+        cfg = Config.from_yaml(str(cfg))
+    project = cfg.raw.get("project", {})
+    components = tuple(components)
+    cap = cfg.raw.get("data", {}).get("context", 512) if max_prompt_tokens is None else max_prompt_tokens
+    if project.get("dry_run", True):
+        return {"dry_run": True, "command": "evaluate_mechanisms", "checkpoint": str(checkpoint),
+                "task_manifest": str(task_manifest), "max_examples": max_examples, "max_prompt_tokens": cap,
+                "components": list(components)}
+    if type(max_examples) is not int or max_examples <= 0 or type(cap) is not int or cap <= 0 \
+            or not math.isfinite(max_seconds) or max_seconds <= 0:
+        raise ValueError("positive bounded mechanism evaluation limits required")
+    parsed = []
+    for comp in components:
+        try:
+            layer, branch = comp.split(":")
+            layer = int(layer)
+        except (AttributeError, ValueError) as e:
+            raise ValueError("component must be layer:attn or layer:mlp") from e
+        if branch not in ("attn", "mlp") or not 0 <= layer < cfg.model.layers or comp in [c[0] for c in parsed]:
+            raise ValueError("invalid or duplicate branch-removal component")
+        parsed.append((comp, layer, branch))
+    dev = torch.device(device)
+    rate = project.get("gpu_hourly_rate_usd")
+    if rate is None or (dev.type == "cuda" and rate <= 0):
+        raise ValueError("declare actual gpu_hourly_rate_usd (explicit 0 allowed for CPU)")
+    out_dir = Path(out_dir)
+    if out_dir.exists():
+        raise FileExistsError(f"mechanism evaluation directory already exists: {out_dir}")
+    ledger = _ledger(project)
+    run_id = str(out_dir.resolve())
+    ledger.begin(run_id, rate, max_seconds, run_budget_usd, parent_checkpoint=checkpoint,
+                 cost_margin_fraction=project.get("cost_margin_fraction", .1), stage=project.get("stage", "A"))
+    started, status = time.monotonic(), "failed"
+
+    def deadline():
+        if time.monotonic() - started >= max_seconds:
+            raise TimeoutError("mechanism evaluation runtime cap exhausted")
+
+    try:
+        out_dir.mkdir(parents=True, exist_ok=False)
+        metadata, all_rows = load_mechanism_tasks(task_manifest, split="val")
+        rows = all_rows[:max_examples]
+        if not rows:
+            raise ValueError("mechanism validation split is empty")
+        task_hash = manifest_hash(task_manifest)
+        train_manifest = cfg.raw["data"]["manifest"]
+        training_hash = manifest_hash(train_manifest)
+        train_tok = json.loads(Path(train_manifest, "manifest.json").read_text() if Path(train_manifest).is_dir()
+                               else Path(train_manifest).read_text())["tokenizer"]
+        if tokenizer is None:
+            tokenizer, fp = _gpt2()
+            if train_tok.get("fingerprint_sha256") != fp:
+                raise ValueError("mechanism prompts require the checkpoint training GPT2 tokenizer fingerprint")
+        elif not (train_tok.get("test_only") and train_tok.get("name") == getattr(tokenizer, "name", None)):
+            raise ValueError("an injected tokenizer must match the test-only training tokenizer")
+        exposure = audit_mechanism_training(task_manifest, train_manifest)
+        encode = tokenizer.encode_ordinary if hasattr(tokenizer, "encode_ordinary") else tokenizer.encode
+        cand = {}
+        for task, digits in (("boolean_hierarchy", range(2)), ("associative_retrieval", range(4))):
+            ids = [encode(f" {d}") for d in digits]
+            if any(len(t) != 1 for t in ids):
+                raise ValueError("mechanism candidate answers must be exactly one token")
+            cand[task] = [t[0] for t in ids]
+        encoded = []
+        for r in rows:
+            prompt, answer = encode(r["prompt"]), encode(r["answer"])
+            if len(answer) != 1 or answer[0] not in cand[r["task"]]:
+                raise ValueError("mechanism answer must be exactly one task-candidate token")
+            if not prompt or len(prompt) > cap:
+                raise ValueError("mechanism prompt exceeds explicit context cap; no truncation permitted")
+            if max(prompt + answer) >= cfg.model.vocab_size:
+                raise ValueError("mechanism tokens exceed checkpoint vocabulary")
+            encoded.append((r, prompt, answer[0]))
+        model = TensorLM(cfg.model)
+        payload = load_checkpoint(checkpoint, model, expected_manifest_hash=training_hash,
+                                  config_validator=evaluation_validator(cfg), restore_rng=False, map_location="cpu")
+        progress, code = payload["progress"], payload["code"]
+        descriptor = _training_descriptor(payload)
+        del payload
+        model.to(dev).eval()
+        for norm in lagged_modules(model):
+            _check_lagged_divisor(norm)
+        before_p, before_b = _tensor_hash(model.named_parameters()), _tensor_hash(model.named_buffers())
+        fwd_tokens = [0]
+
+        def score(prompt, answer, task):
+            deadline()
+            idx = torch.tensor([prompt], dtype=torch.long, device=dev)
+            logits = model(idx, doc_ids=torch.zeros_like(idx))[0, -1].float()
+            if not bool(torch.isfinite(logits).all()):
+                raise FloatingPointError("nonfinite mechanism logits")
+            ce = float(F.cross_entropy(logits[None], torch.tensor([answer], device=dev)))
+            pred = int(logits.argmax())
+            constrained = cand[task][int(logits[cand[task]].argmax())]
+            fwd_tokens[0] += len(prompt)
+            return {"answer_ce": ce, "full_vocab_prediction_token": pred, "full_vocab_correct": pred == answer,
+                    "candidate_prediction_token": constrained, "candidate_correct": constrained == answer}
+
+        def delta(measured, base):
+            measured["delta_answer_ce"] = measured["answer_ce"] - base["answer_ce"]
+            measured["delta_full_vocab_correct"] = int(measured["full_vocab_correct"]) - int(base["full_vocab_correct"])
+            measured["delta_candidate_correct"] = int(measured["candidate_correct"]) - int(base["candidate_correct"])
+            return measured
+
+        examples, cached, reuse_count = [], {}, 0
+        with reference_path(model), torch.inference_mode():
+            for r, prompt, answer in encoded:
+                caps, handles = {}, []
+                for name, layer, branch in parsed:
+                    def hook(module, inputs, output, name=name):
+                        caps[name] = output[0, -1].detach().cpu().clone()
+                    handles.append(getattr(model.blocks[layer], branch).register_forward_hook(hook))
+                try:
+                    base = score(prompt, answer, r["task"])
+                finally:
+                    for h in handles:
+                        h.remove()
+                cached[r["id"]] = caps
+                contrasts = {}
+                for name, layer, branch in parsed:
+                    model.blocks[layer].ablate = frozenset({branch})
+                    try:
+                        contrasts[name] = delta(score(prompt, answer, r["task"]), base)
+                    finally:
+                        model.blocks[layer].ablate = frozenset()
+                examples.append({"id": r["id"], "task": r["task"], "composition_id": r["composition_id"],
+                                 "prompt": r["prompt"], "answer": r["answer"], "answer_token": answer,
+                                 "prompt_tokens": len(prompt), "baseline": base, "branch_removal": contrasts})
+            for target, (r, prompt, answer) in zip(examples, encoded):
+                target["branch_reuse"] = {}
+                for name, layer, branch in parsed:
+                    transfers = {}
+                    for donor_class in ("same_answer", "different_answer"):
+                        eligible = [c for c in rows if c["task"] == r["task"] and c["composition_id"] != r["composition_id"]
+                                    and ((c["answer"] == r["answer"]) == (donor_class == "same_answer"))]
+                        if not eligible:
+                            transfers[donor_class] = {"status": "skipped", "reason": "no eligible donor"}
+                            continue
+                        donor = min(eligible, key=lambda c: c["id"])
+                        vec = cached[donor["id"]][name]
+
+                        def patch(module, inputs, output, vec=vec):
+                            out = output.clone()
+                            out[0, -1] = vec.to(device=output.device, dtype=output.dtype)
+                            return out
+                        h = getattr(model.blocks[layer], branch).register_forward_hook(patch)
+                        try:
+                            m = delta(score(prompt, answer, r["task"]), target["baseline"])
+                        finally:
+                            h.remove()
+                        reuse_count += 1
+                        m.update(status="patched", donor_id=donor["id"], donor_composition_id=donor["composition_id"],
+                                 donor_answer=donor["answer"])
+                        transfers[donor_class] = m
+                    target["branch_reuse"][name] = transfers
+        if (before_p, before_b) != (_tensor_hash(model.named_parameters()), _tensor_hash(model.named_buffers())):
+            raise RuntimeError("mechanism evaluation mutated checkpoint parameters/buffers")
+
+        def summarize(sel):
+            n = len(sel)
+            met = lambda vals: {"answer_ce": sum(v["answer_ce"] for v in vals) / n,  # noqa: E731
+                                "full_vocab_accuracy": sum(v["full_vocab_correct"] for v in vals) / n,
+                                "candidate_accuracy": sum(v["candidate_correct"] for v in vals) / n}
+            out = {"examples": n, "baseline": met([s["baseline"] for s in sel]), "branch_removal": {}, "branch_reuse": {}}
+            for name in components:
+                vals = [s["branch_removal"][name] for s in sel]
+                out["branch_removal"][name] = {**met(vals),
+                                               "paired_mean_delta_answer_ce": sum(v["delta_answer_ce"] for v in vals) / n}
+                out["branch_reuse"][name] = {}
+                for dc in ("same_answer", "different_answer"):
+                    patched = [s["branch_reuse"][name][dc] for s in sel if s["branch_reuse"][name][dc]["status"] == "patched"]
+                    summ = {"patched_examples": len(patched), "skipped_examples": n - len(patched)}
+                    if patched:
+                        summ["paired_mean_delta_answer_ce"] = sum(v["delta_answer_ce"] for v in patched) / len(patched)
+                        summ["candidate_accuracy"] = sum(v["candidate_correct"] for v in patched) / len(patched)
+                    out["branch_reuse"][name][dc] = summ
+            return out
+
+        ckpt = Path(checkpoint)
+        result = {"kind": "known_mechanism_evaluation", "split": "val", "examples": examples,
+                  "summary": summarize(examples),
+                  "per_task": {t: summarize([e for e in examples if e["task"] == t]) for t in sorted({e["task"] for e in examples})},
+                  "probe_ids": [e["id"] for e in examples], "task_manifest_sha256": task_hash, "task_metadata": metadata,
+                  "training_manifest_sha256": training_hash, "checkpoint": str(ckpt.resolve()),
+                  "checkpoint_manifest_sha256": _file_hash(ckpt / "manifest.json"),
+                  "checkpoint_state_sha256": _file_hash(ckpt / "state.pt"), "checkpoint_progress": progress,
+                  "training_descriptor": descriptor, "checkpoint_code": code, "operator_audit": model.operator_audit(),
+                  "probe": {"device": str(dev), "max_examples": max_examples, "max_prompt_tokens": cap,
+                            "components": list(components), "autocast": False, "candidate_token_ids": cand},
+                  "frozen_state": {"unchanged": True, "parameters": before_p, "buffers": before_b},
+                  "exposure": {"answer_prediction_tokens": len(examples) * (1 + len(components)),
+                               "reuse_answer_prediction_tokens": reuse_count, "forward_input_tokens": fwd_tokens[0],
+                               "final_test_exposed": False},
+                  "generator_composition_holdout_verified": True,
+                  "benchmark_training_exposure_verified": exposure["verified"], "training_exposure_audit": exposure,
+                  "interpretation": "exact-label task evidence, not an LM-quality proxy or unique causal mediation claim"}
+        status = "complete"
+    finally:
+        ledger.finish(run_id, time.monotonic() - started, status)
+    result["billing"] = json.loads(ledger.path.read_text())["runs"][run_id]
+    tmp = out_dir / ".mechanism_evaluation.json.tmp"
+    tmp.write_text(json.dumps(result, indent=2, allow_nan=False) + "\n")
+    os.replace(tmp, out_dir / "mechanism_evaluation.json")
+    return result

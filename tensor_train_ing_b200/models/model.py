@@ -243,6 +243,8 @@ class TensorLM(nn.Module):
 
     def uses_fused_path(self, idx: torch.Tensor) -> bool:
         backend = self.cfg.attention_backend
+        if getattr(self, "_force_reference", False):  # analysis hooks need the module-level path
+            return False
         if not (idx.is_cuda and backend in ("auto", "cuda", "triton")):
             return False
         ok, why = self.fused_path_supported()
