@@ -1,0 +1,119 @@
+"""Full-state checkpoint format: integrity, atomic publish, preflight before mutation."""
+import json
+
+import pytest
+import torch
+
+from helpers import TINY_MODEL
+from tensor_train_ing_b200.checkpoint import load_checkpoint, read_manifest, save_checkpoint
+from tensor_train_ing_b200.config import ModelConfig, TrainConfig
+from tensor_train_ing_b200.models.model import TensorLM
+from tensor_train_ing_b200.optim import MuonAdamW
+from tensor_train_ing_b200.optim import make_optimizer as make_opt
+
+
+def _model(seed=0):
+    torch.manual_seed(seed)
+    return TensorLM(ModelConfig(**TINY_MODEL))
+
+
+def _save(path, model, optimizer=None, **kw):
+    return save_checkpoint(path, model, optimizer, None, config={"model": {}}, progress={"steps": 0},
+                           manifest_hash="m" * 64, **kw)
+
+
+def _clone_state(m):
+    return {k: v.clone() for k, v in m.state_dict().items()}
+
+
+def test_full_state_roundtrip(tmp_path):
+    m = _model(1)
+    manifest = _save(tmp_path / "c", m)
+    assert manifest["files"]["state.pt"]["bytes"] > 0
+    other = _model(2)
+    load_checkpoint(tmp_path / "c", other, restore_rng=False)
+    for k, v in m.state_dict().items():
+        assert torch.equal(v, other.state_dict()[k])
+
+
+def test_reject_corrupt_incomplete_and_overwrite(tmp_path):
+    m = _model()
+    _save(tmp_path / "c", m)
+    with pytest.raises(FileExistsError):
+        _save(tmp_path / "c", m)
+    state = tmp_path / "c" / "state.pt"
+    raw = bytearray(state.read_bytes())
+    raw[len(raw) // 2] ^= 0xFF
+    state.write_bytes(bytes(raw))
+    before = _clone_state(m)
+    with pytest.raises(ValueError):
+        load_checkpoint(tmp_path / "c", m)
+    assert all(torch.equal(v, m.state_dict()[k]) for k, v in before.items())
+    (tmp_path / "d").mkdir()
+    with pytest.raises(ValueError):
+        read_manifest(tmp_path / "d")
+
+
+def test_shape_mismatch_preflight_does_not_mutate(tmp_path):
+    _save(tmp_path / "c", _model())
+    other = TensorLM(ModelConfig(**{**TINY_MODEL, "d_mlp": 64}))
+    before = _clone_state(other)
+    with pytest.raises(ValueError):
+        load_checkpoint(tmp_path / "c", other, restore_rng=False)
+    assert all(torch.equal(v, other.state_dict()[k]) for k, v in before.items())
+
+
+def test_nonfinite_state_not_published(tmp_path):
+    m = _model()
+    with torch.no_grad():
+        next(m.parameters()).view(-1)[0] = float("nan")
+    with pytest.raises(Exception):
+        _save(tmp_path / "c", m)
+    assert not (tmp_path / "c").exists()
+    assert not any(p.name.startswith(".c.tmp") for p in tmp_path.iterdir())
+
+
+def test_failed_write_is_not_published(tmp_path, monkeypatch):
+    import tensor_train_ing_b200.checkpoint as ck
+
+    def boom(*a, **k):
+        raise OSError("disk full")
+    monkeypatch.setattr(ck.torch, "save", boom)
+    with pytest.raises(OSError):
+        _save(tmp_path / "c", _model())
+    assert list(tmp_path.iterdir()) == []
+
+
+def test_optimizer_state_roundtrip_and_mismatch(tmp_path):
+    tc = TrainConfig(optimizer="muon", lr=0.01)
+    m = _model()
+    opt = make_opt(m, tc)
+    assert isinstance(opt, MuonAdamW)
+    idx = torch.randint(0, 97, (2, 5))
+    _, loss = m(idx, targets=torch.roll(idx, -1, 1))
+    loss.backward()
+    opt.step()
+    _save(tmp_path / "c", m, opt)
+    m2 = _model(3)
+    opt2 = make_opt(m2, tc)
+    load_checkpoint(tmp_path / "c", m2, opt2, restore_rng=False)
+    a, b = opt.state_dict(), opt2.state_dict()
+    for part in ("muon", "adamw"):
+        sa, sb = a[part]["state"], b[part]["state"]
+        assert sa.keys() == sb.keys()
+        for k in sa:
+            for name, v in sa[k].items():
+                assert torch.equal(torch.as_tensor(v), torch.as_tensor(sb[k][name]))
+    adam = torch.optim.AdamW(m2.parameters())
+    with pytest.raises(ValueError):
+        load_checkpoint(tmp_path / "c", m2, adam, restore_rng=False)
+
+
+def test_unfinished_stat_collection_rejected(tmp_path):
+    m = TensorLM(ModelConfig(**{**TINY_MODEL, "normalization": "lagged", "final_normalization": "lagged"}))
+    from tensor_train_ing_b200.models.normalization import lagged_modules
+    norm = lagged_modules(m)[0]
+    norm.collecting = True
+    m(torch.randint(0, 97, (1, 4)))
+    with pytest.raises(ValueError):
+        _save(tmp_path / "c", m)

@@ -1,0 +1,93 @@
+"""Serial trainer integration on CPU (tiny model, fixture dataset)."""
+import copy
+import json
+
+import pytest
+import torch
+
+from helpers import state
+from tensor_train_ing_b200.budget import SpendLedger
+from tensor_train_ing_b200.checkpoint import load_checkpoint
+from tensor_train_ing_b200.models.model import TensorLM
+from tensor_train_ing_b200.train import train_run
+
+
+def _cfg(config, **train):
+    cfg = copy.deepcopy(config)
+    for k, v in train.items():
+        setattr(cfg.train, k, v)
+    return cfg
+
+
+def test_interrupted_training_exact_replay(config, tmp_path):
+    cfg = _cfg(config, deterministic=True)
+    full = train_run(cfg, tmp_path / "full", max_steps=4, max_seconds=120, device="cpu")
+    first = train_run(cfg, tmp_path / "a", max_steps=2, max_seconds=120, device="cpu")
+    resumed = train_run(cfg, tmp_path / "b", max_steps=2, max_seconds=120, device="cpu", resume=first["checkpoint"])
+    assert resumed["progress"]["steps"] == full["progress"]["steps"] == 4
+    a, b = state(tmp_path / "full" / "final"), state(tmp_path / "b" / "final")
+    for k, v in a["model"].items():
+        assert torch.equal(v, b["model"][k]), k
+    assert a["progress"]["tokens"] == b["progress"]["tokens"]
+
+
+def test_dry_run_returns_plan_without_writing(config, tmp_path):
+    cfg = copy.deepcopy(config)
+    cfg.raw["project"]["dry_run"] = True
+    plan = train_run(cfg, tmp_path / "dry", max_steps=1, max_seconds=1, device="cpu")
+    assert plan["dry_run"] is True
+    assert not (tmp_path / "dry").exists()
+
+
+def test_result_records_progress_metrics_and_billing(config, tmp_path):
+    r = train_run(config, tmp_path / "run", max_steps=3, max_seconds=120, device="cpu")
+    assert r["progress"]["steps"] == 3
+    assert r["progress"]["tokens"] == 3 * config.train.global_prediction_tokens_per_update
+    rows = [json.loads(x) for x in (tmp_path / "run" / "metrics.jsonl").read_text().splitlines()]
+    assert len(rows) >= 3 and all("loss" in x for x in rows if x.get("kind", "train") == "train")
+    led = json.loads((tmp_path / "spend.json").read_text())
+    assert any(run["status"] == "complete" for run in led["runs"].values())
+
+
+def test_cooldown_forks_and_resumes_schedule(config, tmp_path):
+    parent = train_run(config, tmp_path / "p", max_steps=2, max_seconds=120, device="cpu")
+    cool = train_run(config, tmp_path / "c", max_steps=5, max_seconds=120, device="cpu",
+                     resume=parent["checkpoint"], cooldown_steps=3)
+    assert cool["training_descriptor"]["cooldown_status"] == "cooled"
+    assert cool["progress"]["steps"] == 5
+
+
+def test_resume_rejects_model_change(config, tmp_path):
+    parent = train_run(config, tmp_path / "p", max_steps=1, max_seconds=120, device="cpu")
+    other = copy.deepcopy(config)
+    other.model.d_mlp = 16
+    with pytest.raises(Exception):
+        train_run(other, tmp_path / "x", max_steps=1, max_seconds=120, device="cpu", resume=parent["checkpoint"])
+
+
+def test_checkpoint_loads_into_fresh_model(config, tmp_path):
+    r = train_run(config, tmp_path / "run", max_steps=2, max_seconds=120, device="cpu")
+    m = TensorLM(config.model)
+    payload = load_checkpoint(r["checkpoint"], m, restore_rng=False, map_location="cpu")
+    assert payload["progress"]["steps"] == 2
+    saved = state(tmp_path / "run" / "final")["model"]
+    for k, v in m.state_dict().items():
+        assert torch.equal(v, saved[k])
+
+
+def test_run_budget_cap_rejects_launch(config, tmp_path):
+    cfg = copy.deepcopy(config)
+    cfg.raw["project"]["gpu_hourly_rate_usd"] = 1000.0
+    with pytest.raises(Exception):
+        train_run(cfg, tmp_path / "run", max_steps=1, max_seconds=3600, device="cpu", run_budget_usd=0.01)
+
+
+def test_spend_ledger_reservations_and_reconcile(tmp_path):
+    led = SpendLedger(tmp_path / "l.json", 100.0, 10.0)
+    led.begin("a", 36.0, 3600.0, None)  # reserves $36 of the 90 usable dollars
+    led.finish("a", 1.0, "complete")  # charges one second
+    data = json.loads((tmp_path / "l.json").read_text())
+    assert data["runs"]["a"]["status"] == "complete"
+    assert data["runs"]["a"]["spent_usd"] == pytest.approx(0.01)
+    with pytest.raises(ValueError):
+        led.begin("b", 3600.0, 3600.0, None)  # $3600 exceeds the budget left
