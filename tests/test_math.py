@@ -15,8 +15,6 @@ from tensor_train_ing_b200.models.normalization import (GroupRMSNorm, LaggedRMS,
                                                         freeze_spectral, rms_jacobian)
 from tensor_train_ing_b200.ops.linear_ce import chunked_linear_cross_entropy_reference
 
-torch.set_default_dtype(torch.float64)
-
 
 @pytest.fixture(autouse=True)
 def _fp64():
