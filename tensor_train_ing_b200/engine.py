@@ -4,8 +4,9 @@
 ideally pinned -- or CUDA tensors), splits it into micro-batches, copies each to the device
 (non-blocking), runs forward/backward on the fused sm_100a path with the reference's
 loss-normalization contract (every rank back-propagates ``local_sum / global_valid_targets``),
-sums gradients across ranks, clips the global norm and steps the optimizer.  It returns the
-step's summed loss and valid-target count as device tensors (no host synchronisation).
+sums gradients across ranks (one reduce-scatter onto the owning ranks), clips the global norm,
+steps the optimizer on the owned parameters and all-gathers the updated parameters.  It returns
+the step's summed loss and valid-target count as device tensors (no host synchronisation).
 """
 from __future__ import annotations
 
@@ -15,7 +16,7 @@ import torch.distributed as dist
 from .config import Config
 from .models.model import TensorLM
 from .optim import make_optimizer
-from .parallel.data_parallel import DataParallel
+from .parallel.sharded import ShardedDataParallel
 
 
 class TrainEngine:
@@ -26,12 +27,17 @@ class TrainEngine:
         self.micro_batch = int(micro_batch)
         self.model = model if model is not None else TensorLM(cfg.model).to(self.device)
         self.model.train()
-        self.optimizer = optimizer if optimizer is not None else make_optimizer(self.model, cfg.train)
         self.group = group
         self.world = dist.get_world_size(group) if dist.is_available() and dist.is_initialized() else 1
         self.grad_clip = cfg.train.grad_clip if grad_clip is None else grad_clip
         self.fused = self.device.type == "cuda" and self.model.fused_path_supported()[0]
-        self.dp = DataParallel(self.model, self.device, group) if self.fused else None
+        # flat gradient/parameter buffers: needed by the fused path and by every multi-rank run
+        self.dp = (ShardedDataParallel(self.model, self.device, group, fused=self.fused)
+                   if self.fused or self.world > 1 else None)
+        if optimizer is None:
+            only = self.dp.owned_ids() if self.dp is not None and self.world > 1 else None
+            optimizer = make_optimizer(self.model, cfg.train, only=only)
+        self.optimizer = optimizer
         self.last_grad_norm = None
 
     def _to_device(self, t):
@@ -74,8 +80,13 @@ class TrainEngine:
             self.dp.reduce_gradients()
         if self.world > 1:
             dist.all_reduce(loss_sum, group=self.group)
-        params = [p for p in self.model.parameters() if p.grad is not None]
         if self.grad_clip and self.grad_clip > 0:
-            self.last_grad_norm = torch.nn.utils.clip_grad_norm_(params, self.grad_clip, foreach=True)
+            if self.dp is not None:
+                self.last_grad_norm = self.dp.clip_(self.grad_clip)
+            else:
+                params = [p for p in self.model.parameters() if p.grad is not None]
+                self.last_grad_norm = torch.nn.utils.clip_grad_norm_(params, self.grad_clip, foreach=True)
         self.optimizer.step()
+        if self.dp is not None:
+            self.dp.gather_params()
         return loss_sum, count

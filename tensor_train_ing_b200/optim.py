@@ -30,11 +30,13 @@ def hidden_matrix(name: str, p: torch.Tensor) -> bool:
     return p.ndim == 2 and name.startswith("blocks.") and name.endswith(".weight")
 
 
-def param_split(model):
+def param_split(model, only: set[int] | None = None):
+    """(hidden matrices, vocabulary matrices, small params); ``only`` restricts to parameter ids
+    (the parameters a rank owns under sharded data parallelism)."""
     vocab_ids = {id(model.embed.weight), id(model.unembed.weight)}
     hidden, vocab, small = [], [], []
     for name, p in model.named_parameters():
-        if not p.requires_grad:
+        if not p.requires_grad or (only is not None and id(p) not in only):
             continue
         if id(p) in vocab_ids:
             vocab.append(p)
@@ -142,15 +144,16 @@ class MuonAdamW(torch.optim.Optimizer):
     """Muon on hidden matrices plus AdamW on the rest, presented as one optimizer."""
 
     def __init__(self, model, *, lr, aux_lr, weight_decay, betas, momentum=0.95, nesterov=True,
-                 adjust_lr_fn="match_rms_adamw", vocab_weight_decay=0.0):
-        hidden, vocab, small = param_split(model)
+                 adjust_lr_fn="match_rms_adamw", vocab_weight_decay=0.0, only=None):
+        hidden, vocab, small = param_split(model, only)
         self.muon = Muon([{"params": hidden, "base_lr": lr, "kind": "muon"}], lr=lr, weight_decay=weight_decay,
                          momentum=momentum, nesterov=nesterov, adjust_lr_fn=adjust_lr_fn)
         groups = [{"params": vocab, "weight_decay": vocab_weight_decay, "base_lr": aux_lr, "kind": "adamw_vocab"},
                   {"params": small, "weight_decay": 0.0, "base_lr": aux_lr, "kind": "adamw_small"}]
         fused = torch.cuda.is_available() and all(p.is_cuda for g in groups for p in g["params"])
-        self.adamw = torch.optim.AdamW([g for g in groups if g["params"]], lr=aux_lr, betas=betas,
-                                       fused=fused or None)
+        # serial: only non-empty groups (the reference layout); sharded: every group on every rank
+        self.adamw = torch.optim.AdamW(groups if only is not None else [g for g in groups if g["params"]], lr=aux_lr,
+                                       betas=betas, fused=fused or None)
         # not calling Optimizer.__init__: the children own groups and state
         self.defaults = {}
         self._optimizer_step_pre_hooks, self._optimizer_step_post_hooks = {}, {}
@@ -192,12 +195,13 @@ def _scaling_multiplier(model) -> float:
     return mult
 
 
-def make_optimizer(model, cfg):
-    """cfg: TrainConfig.  'adamw' = the reference grouping; 'muon' = MuonAdamW."""
+def make_optimizer(model, cfg, only: set[int] | None = None):
+    """cfg: TrainConfig.  'adamw' = the reference grouping; 'muon' = MuonAdamW.  ``only``: build it
+    over these parameter ids (a rank's owned parameters); group hyper-parameters are unchanged."""
     betas = (cfg.beta1, cfg.beta2)
     mult = _scaling_multiplier(model)
     if cfg.optimizer == "adamw":
-        hidden, vocab, small = param_split(model)
+        hidden, vocab, small = param_split(model, only)
         groups = [{"params": hidden, "weight_decay": cfg.weight_decay_hidden / mult, "base_lr": cfg.lr * mult,
                    "lr": cfg.lr * mult},
                   {"params": vocab + small, "weight_decay": 0.0, "base_lr": cfg.lr}]
@@ -207,5 +211,5 @@ def make_optimizer(model, cfg):
         if mult != 1.0:
             raise NotImplementedError("width/depth LR scaling is defined for AdamW only; Muon uses its own shape scaling")
         return MuonAdamW(model, lr=cfg.lr, aux_lr=cfg.aux_adamw_lr or cfg.lr, weight_decay=cfg.weight_decay_hidden,
-                         betas=betas, momentum=cfg.muon_momentum, adjust_lr_fn=cfg.muon_adjust_lr)
+                         betas=betas, momentum=cfg.muon_momentum, adjust_lr_fn=cfg.muon_adjust_lr, only=only)
     raise ValueError(f"unknown optimizer {cfg.optimizer!r}")

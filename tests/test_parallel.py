@@ -1,0 +1,34 @@
+"""Multi-rank data parallelism on CPU (gloo): sharded engine steps == one process on the global batch."""
+import os
+import subprocess
+import sys
+
+import pytest
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+
+
+def _torchrun(worker, nproc, *args, timeout=300):
+    env = dict(os.environ, CUDA_VISIBLE_DEVICES="", OMP_NUM_THREADS="1")
+    cmd = [sys.executable, "-m", "torch.distributed.run", "--standalone", "--local-addr", "127.0.0.1",
+           "--nproc-per-node", str(nproc), os.path.join(HERE, "dist_workers", worker), *args]
+    return subprocess.run(cmd, capture_output=True, text=True, timeout=timeout, env=env)
+
+
+@pytest.mark.slow
+@pytest.mark.parametrize("optimizer", ["adamw", "muon"])
+@pytest.mark.parametrize("nproc", [2, 3])
+def test_sharded_steps_match_single_process(optimizer, nproc):
+    out = _torchrun("sharded_equivalence.py", nproc, optimizer)
+    assert out.returncode == 0, out.stdout[-3000:] + out.stderr[-3000:]
+    line = next(x for x in out.stdout.splitlines() if x.startswith("MAXERR"))
+    assert float(line.split()[1]) < 1e-10
+
+
+def test_unit_assignment_is_balanced_and_deterministic():
+    from tensor_train_ing_b200.parallel.sharded import assign_units
+    sizes = [100, 7, 50, 50, 3, 99, 1]
+    a = assign_units(sizes, 3)
+    assert a == assign_units(sizes, 3)
+    load = [sum(s for s, r in zip(sizes, a) if r == q) for q in range(3)]
+    assert max(load) - min(load) <= 100
