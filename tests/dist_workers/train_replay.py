@@ -1,0 +1,61 @@
+"""Worker: distributed trainer on gloo.  Checks that a resumed run replays an uninterrupted one
+bitwise and writes the final parameters for comparison with the serial trainer.
+
+argv: <shared tmp dir>.  Prints ``REPLAY_OK`` on rank 0."""
+import json
+import os
+import sys
+from pathlib import Path
+
+import torch
+import torch.distributed as dist
+
+ROOT = os.path.dirname(os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
+sys.path.insert(0, ROOT)
+sys.path.insert(0, os.path.join(ROOT, "tests"))
+
+from helpers import FixtureTokenizer  # noqa: E402
+from tensor_train_ing_b200.config import Config, ModelConfig, TrainConfig  # noqa: E402
+from tensor_train_ing_b200.data import prepare_data  # noqa: E402
+from tensor_train_ing_b200.distributed_train import distributed_train_run  # noqa: E402
+
+
+def config(tmp):
+    return Config(model=ModelConfig(layers=1, d_model=8, heads=1, d_key=4, d_value=4, d_mlp=12, padded_vocab=50257),
+                  train=TrainConfig(compile=False, bf16_compute=False, global_prediction_tokens_per_update=12,
+                                    rung_total_tokens=200, lr=.01),
+                  raw={"data": {"manifest": str(tmp / "data" / "manifest.json"), "context": 8, "micro_batch_size": 1},
+                       "project": {"dry_run": False, "gpu_hourly_rate_usd": 0, "spend_ledger": str(tmp / "spend.json")}})
+
+
+def main():
+    tmp = Path(sys.argv[1])
+    dist.init_process_group("gloo")
+    rank = dist.get_rank()
+    torch.set_num_threads(1)
+    if rank == 0 and not (tmp / "data").exists():
+        src = tmp / "source.jsonl"
+        src.write_text("".join(json.dumps({"id": str(i), "text": "abcdefghijklm" * (1 + i % 3)}) + "\n"
+                               for i in range(30)))
+        prepare_data(tmp / "data", source_jsonl=src, revision="offline-v1", tokenizer=FixtureTokenizer(),
+                     split_fractions={"train": 1., "val": 0., "test": 0., "calibration": 0.})
+    dist.barrier()
+    cfg = config(tmp)
+    full = distributed_train_run(cfg, tmp / "full", max_steps=4, max_seconds=300, device="cpu")
+    first = distributed_train_run(cfg, tmp / "a", max_steps=2, max_seconds=300, device="cpu")
+    second = distributed_train_run(cfg, tmp / "b", max_steps=2, max_seconds=300, device="cpu", resume=first["checkpoint"])
+    assert full["progress"]["steps"] == second["progress"]["steps"] == 4
+    assert full["progress"]["tokens"] == second["progress"]["tokens"] == 48
+    if rank == 0:
+        a = torch.load(tmp / "full" / "final" / "model.pt", weights_only=False)["model"]
+        b = torch.load(tmp / "b" / "final" / "model.pt", weights_only=False)["model"]
+        for k in a:
+            assert torch.equal(a[k], b[k]), k
+        losses = [json.loads(x)["loss"] for x in (tmp / "full" / "metrics.jsonl").read_text().splitlines()]
+        (tmp / "distributed_losses.json").write_text(json.dumps(losses))
+        print("REPLAY_OK", flush=True)
+    dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

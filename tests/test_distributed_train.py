@@ -1,0 +1,40 @@
+"""Distributed trainer on CPU ranks (gloo): exact resume replay and agreement with the serial trainer."""
+import json
+import os
+import subprocess
+import sys
+
+import pytest
+import torch
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+
+
+def _torchrun(worker, nproc, *args, timeout=600):
+    env = dict(os.environ, CUDA_VISIBLE_DEVICES="", OMP_NUM_THREADS="1")
+    cmd = [sys.executable, "-m", "torch.distributed.run", "--standalone", "--local-addr", "127.0.0.1",
+           "--nproc-per-node", str(nproc), os.path.join(HERE, "dist_workers", worker), *args]
+    return subprocess.run(cmd, capture_output=True, text=True, timeout=timeout, env=env)
+
+
+@pytest.mark.slow
+def test_two_rank_training_replays_and_matches_serial(tmp_path):
+    out = _torchrun("train_replay.py", 2, str(tmp_path))
+    assert out.returncode == 0, out.stdout[-3000:] + out.stderr[-4000:]
+    assert "REPLAY_OK" in out.stdout
+    sys.path.insert(0, os.path.join(HERE, "dist_workers"))
+    from train_replay import config  # noqa: E402
+
+    from tensor_train_ing_b200.train import train_run
+    torch.set_num_threads(1)
+    cfg = config(tmp_path)
+    cfg.raw["project"]["spend_ledger"] = str(tmp_path / "serial-spend.json")
+    serial = train_run(cfg, tmp_path / "serial", max_steps=4, max_seconds=300, device="cpu")
+    serial_losses = [json.loads(x)["loss"] for x in (tmp_path / "serial" / "metrics.jsonl").read_text().splitlines()]
+    dist_losses = json.loads((tmp_path / "distributed_losses.json").read_text())
+    assert serial["progress"]["tokens"] == 48
+    assert serial_losses == pytest.approx(dist_losses, rel=1e-5)
+    s = torch.load(tmp_path / "serial" / "final" / "state.pt", weights_only=False)["model"]
+    d = torch.load(tmp_path / "full" / "final" / "model.pt", weights_only=False)["model"]
+    for k in s:
+        torch.testing.assert_close(s[k], d[k], rtol=1e-4, atol=1e-5)
