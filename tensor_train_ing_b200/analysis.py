@@ -556,3 +556,126 @@ def analyze(model, batches, out_dir: str, rw_layer_window: int | None = None) ->
     result = json.loads(json.dumps(result, default=float).replace("NaN", "null"))
     (out / "analysis.json").write_text(json.dumps(result, indent=1))
     return result
+
+
+def analyze_checkpoint(cfg, checkpoint, out, *, batches=2, context=None, max_seconds=300.0, device="cpu",
+                       run_budget_usd=None, rw_layer_window=None) -> dict:
+    """Billed, frozen-state-checked ``analyze`` of a checkpoint on validation probe batches (the
+    reference's ``analyze`` command, tnlm/cli.py:117-270): the model, its buffers, module modes,
+    hooks and the probe batches must be unchanged afterwards; the probe plan, overlap audit and
+    source provenance are written beside the diagnostics."""
+    import hashlib
+    import json
+    import time
+
+    from .budget import SpendLedger
+    from .checkpoint import load_checkpoint
+    from .config import Config
+    from .data import (PackedSampler, audit_validation_overlap, batch_hash, manifest_hash,
+                       validate_tokenizer_compatibility)
+    from .evaluate import _training_descriptor
+    from .models.model import TensorLM
+    from .runtime import evaluation_validator
+    if isinstance(cfg, (str, Path)):
+        cfg = Config.from_yaml(str(cfg))
+    project, data = cfg.raw.get("project", {}), cfg.raw.get("data", {})
+    context = data.get("context", 512) if context is None else context
+    if rw_layer_window is not None and (type(rw_layer_window) is not int or rw_layer_window < 0):
+        raise ValueError("rw_layer_window must be a nonnegative integer")
+    if batches <= 0 or context <= 0 or max_seconds <= 0:
+        raise ValueError("analysis requires positive batches, context and runtime cap")
+    if project.get("dry_run", True):
+        return {"dry_run": True, "command": "analyze", "checkpoint": str(checkpoint), "context": context,
+                "batches": batches, "max_seconds": max_seconds, "rw_layer_window": rw_layer_window}
+    out = Path(out)
+    if out.exists():
+        raise FileExistsError(f"analysis output already exists: {out}")
+    dev = torch.device(device)
+    rate = project.get("gpu_hourly_rate_usd")
+    if rate is None or (dev.type == "cuda" and rate <= 0):
+        raise ValueError("declare actual gpu_hourly_rate_usd (explicit 0 allowed for CPU)")
+    ledger = SpendLedger(project.get("spend_ledger", "runs/spend.json"), project.get("total_budget_usd", 1000),
+                         project.get("reserve_usd", 150), stage_budgets=project.get("stage_budgets"))
+    run_id = str(out.resolve())
+    ledger.begin(run_id, rate, max_seconds, run_budget_usd, parent_checkpoint=str(checkpoint),
+                 cost_margin_fraction=project.get("cost_margin_fraction", .1), stage=project.get("stage", "A"))
+    started, status = time.monotonic(), "failed"
+    try:
+        evaluation = cfg.raw.get("evaluation", {})
+        manifest = evaluation.get("validation_manifest", data.get("manifest"))
+        tok_compat = validate_tokenizer_compatibility(data["manifest"], manifest, allow_test_only=dev.type == "cpu")
+        sampler = PackedSampler(manifest, split="val", context=context, batch_size=data.get("micro_batch_size", 1),
+                                seed=int(evaluation.get("seed", 0)))
+        model = TensorLM(cfg.model).to(dev)
+        payload = load_checkpoint(checkpoint, model, expected_manifest_hash=manifest_hash(data["manifest"]),
+                                  config_validator=evaluation_validator(cfg), restore_rng=False, map_location="cpu")
+        code, ckpt_progress = payload["code"], payload["progress"]
+        descriptor = _training_descriptor(payload)
+        del payload
+        model.eval()
+
+        def fingerprint():
+            h = hashlib.sha256()
+            for name, t in list(model.named_parameters()) + list(model.named_buffers()):
+                h.update(name.encode())
+                h.update(str((t.dtype, tuple(t.shape))).encode())
+                h.update(t.detach().cpu().contiguous().reshape(-1).view(torch.uint8).numpy().tobytes())
+            return h.hexdigest()
+
+        def lifecycle():
+            return ({n: (m.training, getattr(m, "collecting", None), getattr(m, "denom_mode", None),
+                         getattr(m, "ablate", None), tuple(m._forward_hooks), tuple(m._forward_pre_hooks))
+                     for n, m in model.named_modules()},
+                    {n: p.requires_grad for n, p in model.named_parameters()})
+        before_state, before_modes = fingerprint(), lifecycle()
+        initial = sampler.state_dict()
+        probe, mappings = [], []
+        for _ in range(batches):
+            if time.monotonic() - started >= max_seconds:
+                raise TimeoutError("analysis runtime cap during probe setup")
+            probe.append(tuple(t.to(dev) for t in sampler.next_batch()))
+            mappings.append(sampler.batch_mappings())
+        hashes = [batch_hash(b) for b in probe]
+        plan = {"version": 1, "validation_manifest_sha256": manifest_hash(manifest), "split": "val",
+                "context": context, "sampler_initial": initial, "batch_mappings": mappings, "batch_hashes": hashes}
+        plan_sha = hashlib.sha256(json.dumps(plan, sort_keys=True, separators=(",", ":")).encode()).hexdigest()
+        docs = {item["document_id"] for mapping in mappings for row in mapping for item in row["ranges"]
+                if item["packed_token_start"] < row["input_length"]}
+        audit = audit_validation_overlap(data["manifest"], manifest, document_ids=docs)
+        if audit["has_overlap"]:
+            raise ValueError("analysis validation has exact whole-document content overlap")
+        seed = int(evaluation.get("seed", 0))
+        devices = [dev.index if dev.index is not None else torch.cuda.current_device()] if dev.type == "cuda" else []
+        with torch.random.fork_rng(devices=devices):
+            torch.random.default_generator.manual_seed(seed)
+            if devices:
+                torch.cuda.default_generators[devices[0]].manual_seed(seed)
+            result = analyze(model, probe, str(out), **({} if rw_layer_window is None else
+                                                          {"rw_layer_window": rw_layer_window}))
+        if [batch_hash(b) for b in probe] != hashes:
+            raise RuntimeError("analysis changed probe batch inputs or targets")
+        after_state, after_modes = fingerprint(), lifecycle()
+        if before_state != after_state or before_modes != after_modes:
+            raise RuntimeError("analysis changed model state, modes, collection flags, gradient flags or hooks")
+        pkg = Path(__file__).parent
+        sources = {str(p.relative_to(pkg)): hashlib.sha256(p.read_bytes()).hexdigest() for p in sorted(pkg.rglob("*.py"))}
+        provenance = {"checkpoint": str(Path(checkpoint).resolve()), "training_descriptor": descriptor,
+                      "checkpoint_progress": ckpt_progress, "checkpoint_code": code,
+                      "checkpoint_manifest_sha256": hashlib.sha256((Path(checkpoint) / "manifest.json").read_bytes()).hexdigest(),
+                      "validation_manifest_sha256": manifest_hash(manifest), "split": "val", "batches": batches,
+                      "context": context, "rw_layer_window": rw_layer_window, "probe_seed": seed,
+                      "runtime_source_sha256": sources, "batch_hashes": hashes, "probe_plan": plan,
+                      "probe_plan_sha256": plan_sha, "data_overlap_audit": audit, "tokenizer_compatibility": tok_compat,
+                      "frozen_state": {"before": before_state, "after": after_state, "unchanged": True},
+                      "sampler": sampler.state_dict(), "runtime_cap_seconds": max_seconds}
+        result["training_descriptor"] = descriptor
+        result["evaluation_provenance"] = provenance
+        json.dumps(result, allow_nan=False)
+        out.mkdir(parents=True, exist_ok=True)
+        (out / "invocation.json").write_text(json.dumps(provenance, indent=2))
+        status = "complete"
+    finally:
+        ledger.finish(run_id, time.monotonic() - started, status)
+    result["billing"] = json.loads(ledger.path.read_text())["runs"][run_id]
+    (out / "analysis-invocation-result.json").write_text(json.dumps(result, indent=2, allow_nan=False))
+    return result

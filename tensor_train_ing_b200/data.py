@@ -155,7 +155,7 @@ def prepare_data(output_dir, *, source_jsonl=None, revision, max_tokens=50_000_0
     try:
         return _prepare(out, source_jsonl, revision, max_tokens, max_documents, tokenizer, split_fractions,
                         hf_dataset, hf_config, hf_data_files, hf_shard_checksums, hf_local_shards,
-                        exclude_validation_manifest, on_shard_scanned)
+                        exclude_validation_manifest, on_shard_scanned, workers, tokenization_batch_bytes)
     except BaseException:
         shutil.rmtree(out)
         raise
@@ -163,7 +163,7 @@ def prepare_data(output_dir, *, source_jsonl=None, revision, max_tokens=50_000_0
 
 def _prepare(out, source_jsonl, revision, max_tokens, max_documents, tokenizer, split_fractions, hf_dataset,
              hf_config, hf_data_files, hf_shard_checksums, hf_local_shards, exclude_validation_manifest,
-             on_shard_scanned):
+             on_shard_scanned, workers=1, tokenization_batch_bytes=1 << 20):
     if not revision or revision in ("main", "master", "latest"):
         raise ValueError("an immutable source revision is required")
     if any(type(v) is not int or v <= 0 for v in (max_tokens, max_documents)):
@@ -229,12 +229,10 @@ def _prepare(out, source_jsonl, revision, max_tokens, max_documents, tokenizer, 
     total = count = 0
     try:
         with (out / "documents.jsonl").open("w") as meta:
-            for rank, doc_id, text, offset, content in candidates:
-                processed_text = text.replace("\r\n", "\n").replace("\r", "\n")
-                encoded = np.asarray(tok.encode(processed_text, allowed_special=set(), disallowed_special=()),
-                                     dtype="<i8")
-                if len(encoded) and (encoded.min() < 0 or encoded.max() >= GPT2_VOCAB):
-                    raise ValueError("tokens must belong to the real GPT2 vocabulary")
+            from .data_preparation import ordered_tokenization
+            rows = ((doc_id, text, rank, offset, content) for rank, doc_id, text, offset, content in candidates)
+            for doc_id, processed_sha, encoded, rank, offset, content in ordered_tokenization(
+                    rows, tokenizer=tokenizer, workers=workers, batch_bytes=tokenization_batch_bytes):
                 remaining = max_tokens - total
                 eos_included = len(encoded) + 1 <= remaining
                 toks = encoded[:remaining].astype(TOKEN_DTYPE)
@@ -251,7 +249,7 @@ def _prepare(out, source_jsonl, revision, max_tokens, max_documents, tokenizer, 
                     streams[split].write(np.asarray([EOS], dtype=TOKEN_DTYPE).tobytes())
                 offsets[split] += n
                 doc = {"id": doc_id, "numeric_id": count, "split": split, "selection_sha256": rank,
-                       "content_sha256": content, "processed_sha256": _digest(processed_text),
+                       "content_sha256": content, "processed_sha256": processed_sha,
                        "source_offset": offset, "token_start": start, "token_end": offsets[split],
                        "source_token_start": 0, "source_token_end": n, "processed_token_start": 0,
                        "processed_token_end": min(n, len(encoded)),

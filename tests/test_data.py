@@ -95,3 +95,16 @@ def test_failed_preparation_cleans_output(tmp_path):
     with pytest.raises(ValueError):
         prepare_data(tmp_path / "out", source_jsonl=src, revision="main", tokenizer=FixtureTokenizer())
     assert not (tmp_path / "out").exists()
+
+
+def test_parallel_tokenization_is_byte_identical(tmp_path):
+    src = tmp_path / "src.jsonl"
+    src.write_text("".join(json.dumps({"id": f"d{i}", "text": ("word%d " % i) * (1 + i % 7)}) + "\n" for i in range(300)))
+    outs = []
+    for workers in (1, 3):
+        m = prepare_data(tmp_path / f"data{workers}", source_jsonl=src, revision="offline-v1",
+                         tokenizer=FixtureTokenizer(), workers=workers, tokenization_batch_bytes=256,
+                         split_fractions={"train": .7, "val": .1, "test": .1, "calibration": .1})
+        root = m.parent if m.is_file() else m
+        outs.append({p.name: p.read_bytes() for p in root.iterdir() if p.is_file() and p.name != "manifest.json"})
+    assert outs[0] == outs[1]
