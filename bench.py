@@ -66,7 +66,7 @@ def model_kwargs(name):
 
 def train_kwargs(opt):
     return dict(optimizer=opt, lr=6e-3 if opt == "muon" else 4.5e-4, aux_adamw_lr=4.5e-4, grad_clip=1.0,
-                compile=False, muon_adjust_lr="match_rms_adamw")
+                muon_adjust_lr="match_rms_adamw")
 
 
 def setup_dist(n):
@@ -192,6 +192,13 @@ def build_reference(args, device, world):
         mesh = init_device_mesh("cuda", (world,))
         model = shard_model(model, mesh)
     opt = make_optimizer(model, tcfg)
+    # the reference's serial trainer compiles the model when train.compile is set (its default;
+    # tnlm/train.py:353); its distributed trainer does not compile
+    forward = model
+    compile_note = "eager (the reference's distributed trainer does not compile)"
+    if world == 1 and tcfg.compile:
+        forward = torch.compile(model)
+        compile_note = "torch.compile(model), as the reference's serial trainer"
     n_params = sum(p.numel() for p in model.parameters())
     if world > 1:
         n_params = sum(p.full_tensor().numel() if hasattr(p, "full_tensor") else p.numel() for p in model.parameters())
@@ -205,7 +212,7 @@ def build_reference(args, device, world):
         for s in range(0, idx.shape[0], micro):
             i, d, t = (x[s:s + micro].to(device, non_blocking=True) for x in (idx, docs, tgt))
             with torch.autocast("cuda", dtype=torch.bfloat16):
-                _, loss, _ = model(i, doc_ids=d, targets=t, reduction="sum")
+                _, loss, _ = forward(i, doc_ids=d, targets=t, reduction="sum")
             (loss / count).backward()
             total += loss.detach().float()
         torch.nn.utils.clip_grad_norm_(model.parameters(), tcfg.grad_clip)
@@ -214,6 +221,7 @@ def build_reference(args, device, world):
             dist.all_reduce(total)
         return total, count
 
+    step.note = compile_note
     return step, mcfg, T, gb, n_params, None
 
 
@@ -295,10 +303,12 @@ def main():
         pass
 
     peaks_path = os.path.join(ROOT, "MEASURED_PEAKS.json")
-    peak_tflops = 1590.0
+    peak_tflops, sustained_tflops = 1590.0, 1400.0
     if os.path.exists(peaks_path):
         with open(peaks_path) as fh:
-            peak_tflops = float(json.load(fh).get("bf16_tflops", peak_tflops))
+            peaks = json.load(fh)
+        peak_tflops = float(peaks.get("bf16_tflops", peak_tflops))
+        sustained_tflops = float(peaks.get("bf16_tflops_sustained", sustained_tflops))
     if rank == 0:
         out = {
             "metric": METRIC, "value": round(value, 1), "unit": "tokens/s", "n_gpus": world,
@@ -312,11 +322,14 @@ def main():
                        "l2": "per-step working set >> 126 MB L2; no flush needed"},
             "mfu": round(6 * n_params * value / (world * peak_tflops * 1e12), 4),
             "mfu_peak_tflops": peak_tflops,
+            "mfu_of_sustained": round(6 * n_params * value / (world * sustained_tflops * 1e12), 4),
+            "mfu_sustained_tflops": sustained_tflops,
             "loss_first_last": [round(loss_vals[0], 4), round(loss_vals[-1], 4)],
             "clocks": clocks, "e2e": e2e,
         }
         if args.impl == "reference":
             out["impl"] = "reference"
+            out["config"]["reference_path"] = getattr(step, "note", None)
         else:
             out["gpu_launches"] = counter.count
             out["gpu_launches_by_binding"] = counter.by_name
