@@ -24,8 +24,15 @@ constexpr int kBwdThreads = 320;  // 2 control warps + 8 poly warps (two per TME
 constexpr int kBwdPoly = 256;
 
 // ============================================================================ dQ kernel
+// Warps: 0 = TMA producer of Q1/Q2/dO (once) and the K1/K2 ring (3 stages), 1 = MMA issuer,
+// 2 = TMA producer of the V ring (2 stages), 3..10 = poly warps.  dS1/dS2 go from the poly warps
+// straight into tensor memory and are the A operands of dQ1 += dS1 K1, dQ2 += dS2 K2.
 constexpr int DQ_BM = 128;  // queries per CTA
 constexpr int DQ_BN = 64;   // keys per block
+constexpr int kDqKStages = 3;
+constexpr int kDqVStages = 2;
+constexpr int kDqThreads = 352;
+constexpr int kDqFirstPoly = 3;
 
 template <int DK, int DV>
 struct DqSmem {
@@ -33,17 +40,16 @@ struct DqSmem {
   static constexpr int kDO = DV / 64 * DQ_BM * 128;
   static constexpr int kK = DK / 64 * DQ_BN * 128;
   static constexpr int kV = DV / 64 * DQ_BN * 128;
-  static constexpr int kStage = 2 * kK + kV;
-  static constexpr int kDS = DQ_BM * 128;  // 128 rows x 64 keys bf16
+  static constexpr int kKStage = 2 * kK;
   static constexpr int kOffQ1 = 0, kOffQ2 = kQ, kOffDO = 2 * kQ;
-  static constexpr int kOffStage = 2 * kQ + kDO;
-  static constexpr int kOffDS = kOffStage + 2 * kStage;
-  static constexpr int kOffBar = kOffDS + 2 * kDS;
+  static constexpr int kOffK = 2 * kQ + kDO;
+  static constexpr int kOffV = kOffK + kDqKStages * kKStage;
+  static constexpr int kOffBar = kOffV + kDqVStages * kV;
   static constexpr int kBytes = (kOffBar + 256 + 1024) > 120 * 1024 ? (kOffBar + 256 + 1024) : 120 * 1024;
 };
 
 template <int DK, int DV, int KIND>
-__global__ void __launch_bounds__(kBwdThreads, 1)
+__global__ void __launch_bounds__(kDqThreads, 1)
     poly_bwd_dq_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmKV,
                        const __grid_constant__ CUtensorMap tmDO, Params p) {
   using S = DqSmem<DK, DV>;
@@ -52,15 +58,17 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t* bar = reinterpret_cast<uint64_t*>(smem + S::kOffBar);
   uint64_t* q_full = bar + 0;
-  uint64_t* kv_full = bar + 1;   // [2]
-  uint64_t* kv_empty = bar + 3;  // [2]
-  uint64_t* sc_full = bar + 5;
-  uint64_t* sc_empty = bar + 6;
-  uint64_t* ds_full = bar + 7;
-  uint64_t* ds_empty = bar + 8;
-  uint64_t* acc_full = bar + 9;
-  uint64_t* mma_done = bar + 10;
-  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(bar + 12);
+  uint64_t* k_full = bar + 1;    // [3]
+  uint64_t* k_empty = bar + 4;   // [3]
+  uint64_t* v_full = bar + 7;    // [2]
+  uint64_t* v_empty = bar + 9;   // [2]
+  uint64_t* sc_full = bar + 11;
+  uint64_t* sc_empty = bar + 12;
+  uint64_t* ds_full = bar + 13;
+  uint64_t* ds_empty = bar + 14;
+  uint64_t* acc_full = bar + 15;
+  uint64_t* mma_done = bar + 16;
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(bar + 18);
 
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
   const int nqb = (p.T + DQ_BM - 1) / DQ_BM;
@@ -76,9 +84,13 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
 
   if (threadIdx.x == 0) {
     mbar_init(q_full, 1);
-    for (int i = 0; i < 2; ++i) {
-      mbar_init(&kv_full[i], 1);
-      mbar_init(&kv_empty[i], 1);
+    for (int i = 0; i < kDqKStages; ++i) {
+      mbar_init(&k_full[i], 1);
+      mbar_init(&k_empty[i], 1);
+    }
+    for (int i = 0; i < kDqVStages; ++i) {
+      mbar_init(&v_full[i], 1);
+      mbar_init(&v_empty[i], 1);
     }
     mbar_init(sc_full, 1);
     mbar_init(sc_empty, kBwdPoly);
@@ -96,7 +108,9 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_holder;
-  const uint32_t tS1 = tmem, tS2 = tmem + 64, tDP = tmem + 128, tDQ1 = tmem + 256, tDQ2 = tmem + 256 + DK;
+  // TMEM: S1 0, S2 64, dP 128, dS1 192 (bf16 pairs), dS2 224, dQ1 256, dQ2 256+DK
+  const uint32_t tS1 = tmem, tS2 = tmem + 64, tDP = tmem + 128, tDS1 = tmem + 192, tDS2 = tmem + 224;
+  const uint32_t tDQ1 = tmem + 256, tDQ2 = tmem + 256 + DK;
 
   if (warp == 0) {
     if (elect_one()) {
@@ -111,26 +125,38 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       }
       for (int i = 0; i < DV / 64; ++i)
         tma_load_2d(smem + S::kOffDO + i * DQ_BM * 128, &tmDO, q_full, h * DV + 64 * i, qrow);
-      bool ok = true;
-      for (int j = 0; j < nkb && ok; ++j) {
-        const int st = j & 1;
-        if (!mbar_wait(&kv_empty[st], ((j >> 1) & 1) ^ 1, p.status, kErrTimeoutProducer)) {
-          ok = false;
-          break;
-        }
-        uint8_t* sk = smem + S::kOffStage + st * S::kStage;
+      int issued = 0;
+      for (int j = 0; j < nkb; ++j) {
+        const int st = j % kDqKStages;
+        if (!mbar_wait(&k_empty[st], ((j / kDqKStages) & 1) ^ 1, p.status, kErrTimeoutProducer)) break;
+        uint8_t* sk = smem + S::kOffK + st * S::kKStage;
         const int krow = static_cast<int>(row0 + kstart + j * DQ_BN);
-        mbar_arrive_expect_tx(&kv_full[st], (kTwo ? 2 : 1) * S::kK + S::kV);
+        mbar_arrive_expect_tx(&k_full[st], (kTwo ? 2 : 1) * S::kK);
         for (int i = 0; i < DK / 64; ++i) {
-          tma_load_2d(sk + i * DQ_BN * 128, &tmKV, &kv_full[st], p.ck1 + h * DK + 64 * i, krow);
-          if (kTwo) tma_load_2d(sk + S::kK + i * DQ_BN * 128, &tmKV, &kv_full[st], p.ck2 + h * DK + 64 * i, krow);
+          tma_load_2d(sk + i * DQ_BN * 128, &tmKV, &k_full[st], p.ck1 + h * DK + 64 * i, krow);
+          if (kTwo) tma_load_2d(sk + S::kK + i * DQ_BN * 128, &tmKV, &k_full[st], p.ck2 + h * DK + 64 * i, krow);
         }
-        for (int i = 0; i < DV / 64; ++i)
-          tma_load_2d(sk + 2 * S::kK + i * DQ_BN * 128, &tmKV, &kv_full[st], p.cv + h * DV + 64 * i, krow);
+        issued = j + 1;
       }
       mbar_wait(q_full, 0, p.status, kErrTimeoutProducer);
-      if (!ok)
-        for (int j = max(0, nkb - 2); j < nkb; ++j) mbar_wait(&kv_full[j & 1], (j >> 1) & 1, p.status, kErrTimeoutProducer);
+      for (int j = max(0, issued - kDqKStages); j < issued; ++j)
+        mbar_wait(&k_full[j % kDqKStages], (j / kDqKStages) & 1, p.status, kErrTimeoutProducer);
+    }
+  } else if (warp == 2) {
+    if (elect_one()) {
+      int issued = 0;
+      for (int j = 0; j < nkb; ++j) {
+        const int st = j % kDqVStages;
+        if (!mbar_wait(&v_empty[st], ((j / kDqVStages) & 1) ^ 1, p.status, kErrTimeoutProducer)) break;
+        uint8_t* sv = smem + S::kOffV + st * S::kV;
+        const int krow = static_cast<int>(row0 + kstart + j * DQ_BN);
+        mbar_arrive_expect_tx(&v_full[st], S::kV);
+        for (int i = 0; i < DV / 64; ++i)
+          tma_load_2d(sv + i * DQ_BN * 128, &tmKV, &v_full[st], p.cv + h * DV + 64 * i, krow);
+        issued = j + 1;
+      }
+      for (int j = max(0, issued - kDqVStages); j < issued; ++j)
+        mbar_wait(&v_full[j % kDqVStages], (j / kDqVStages) & 1, p.status, kErrTimeoutProducer);
     }
   } else if (warp == 1) {
     if (elect_one()) {
@@ -138,31 +164,32 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       constexpr uint32_t idAcc = idesc_bf16_f32(128, DK, 0, 1);
       const uint32_t sQ1 = smem_u32(smem + S::kOffQ1), sQ2 = smem_u32(smem + S::kOffQ2);
       const uint32_t sDO = smem_u32(smem + S::kOffDO);
-      const uint32_t sDS1 = smem_u32(smem + S::kOffDS), sDS2 = sDS1 + S::kDS;
       bool ok = mbar_wait(q_full, 0, p.status, kErrTimeoutMma);
       auto accumulate = [&](int i) -> bool {
+        const int ks = i % kDqKStages;
         if (!mbar_wait(ds_full, i & 1, p.status, kErrTimeoutMma)) return false;
         tc_fence_after();
-        const uint32_t sK1 = smem_u32(smem + S::kOffStage + (i & 1) * S::kStage);
+        const uint32_t sK1 = smem_u32(smem + S::kOffK + ks * S::kKStage);
         const uint32_t sK2 = sK1 + S::kK;
 #pragma unroll
         for (int k = 0; k < DQ_BN / 16; ++k) {
           const uint32_t acc = (i > 0 || k > 0) ? 1u : 0u;
-          umma_ss(tDQ1, kmajor_desc(sDS1, DQ_BM, k), mnmajor_desc(sK1, DQ_BN, k), idAcc, acc);
-          if (kTwo) umma_ss(tDQ2, kmajor_desc(sDS2, DQ_BM, k), mnmajor_desc(sK2, DQ_BN, k), idAcc, acc);
+          umma_ts(tDQ1, tDS1 + k * 8, mnmajor_desc(sK1, DQ_BN, k), idAcc, acc);
+          if (kTwo) umma_ts(tDQ2, tDS2 + k * 8, mnmajor_desc(sK2, DQ_BN, k), idAcc, acc);
         }
         umma_commit(ds_empty);
-        umma_commit(&kv_empty[i & 1]);
+        umma_commit(&k_empty[ks]);
         return true;
       };
       for (int j = 0; j < nkb && ok; ++j) {
-        const int st = j & 1;
-        if (!mbar_wait(&kv_full[st], (j >> 1) & 1, p.status, kErrTimeoutMma)) { ok = false; break; }
+        const int ks = j % kDqKStages, vs = j % kDqVStages;
+        if (!mbar_wait(&k_full[ks], (j / kDqKStages) & 1, p.status, kErrTimeoutMma)) { ok = false; break; }
+        if (!mbar_wait(&v_full[vs], (j / kDqVStages) & 1, p.status, kErrTimeoutMma)) { ok = false; break; }
         if (!mbar_wait(sc_empty, (j & 1) ^ 1, p.status, kErrTimeoutMma)) { ok = false; break; }
         tc_fence_after();
-        const uint32_t sK1 = smem_u32(smem + S::kOffStage + st * S::kStage);
+        const uint32_t sK1 = smem_u32(smem + S::kOffK + ks * S::kKStage);
         const uint32_t sK2 = sK1 + S::kK;
-        const uint32_t sV = sK1 + 2 * S::kK;
+        const uint32_t sV = smem_u32(smem + S::kOffV + vs * S::kV);
 #pragma unroll
         for (int k = 0; k < DK / 16; ++k) {
           umma_ss(tS1, kmajor_desc(sQ1, DQ_BM, k), kmajor_desc(sK1, DQ_BN, k), idS, k > 0 ? 1u : 0u);
@@ -172,6 +199,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
         for (int k = 0; k < DV / 16; ++k)
           umma_ss(tDP, kmajor_desc(sDO, DQ_BM, k), kmajor_desc(sV, DQ_BN, k), idS, k > 0 ? 1u : 0u);
         umma_commit(sc_full);
+        umma_commit(&v_empty[vs]);
         if (j > 0 && !accumulate(j - 1)) { ok = false; break; }
       }
       if (ok && accumulate(nkb - 1)) umma_commit(acc_full);
@@ -180,7 +208,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
     }
   } else {
     const int sub = warp & 3;
-    const int half = (warp - 2) >> 2;  // which 32 keys of the 64-key block
+    const int half = (warp - kDqFirstPoly) >> 2;  // which 32 keys of the 64-key block
     const int r = sub * 32 + lane;
     const int t = q0 + r;
     const bool valid = t < p.T;
@@ -242,18 +270,12 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
           d2[jj / 2] = pack_bf16(o2[0], o2[1]);
         }
       }
+      // the dS buffers are free once dQ of block j-1 has completed
       if (!mbar_wait(ds_empty, (j & 1) ^ 1, p.status, kErrTimeoutEpilogue)) { ok = false; break; }
-      uint8_t* row1 = smem + S::kOffDS;
-      uint8_t* row2 = row1 + S::kDS;
-#pragma unroll
-      for (int ch = 0; ch < 4; ++ch) {
-        *reinterpret_cast<uint4*>(row1 + sw128_offset(r, half * 4 + ch)) =
-            make_uint4(d1[ch * 4], d1[ch * 4 + 1], d1[ch * 4 + 2], d1[ch * 4 + 3]);
-        if (kTwo)
-          *reinterpret_cast<uint4*>(row2 + sw128_offset(r, half * 4 + ch)) =
-              make_uint4(d2[ch * 4], d2[ch * 4 + 1], d2[ch * 4 + 2], d2[ch * 4 + 3]);
-      }
-      fence_proxy_async_smem();
+      tmem_st16(tDS1 + lane_off + half * 16, d1);
+      if (kTwo) tmem_st16(tDS2 + lane_off + half * 16, d2);
+      tmem_st_wait();
+      tc_fence_before();
       mbar_arrive(ds_full);
     }
     if (ok && mbar_wait(acc_full, 0, p.status, kErrTimeoutEpilogue)) {
@@ -463,7 +485,28 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
     float g0 = 0.f, g1 = 0.f, g2 = 0.f, g12 = 0.f;
     const uint32_t lane_off = static_cast<uint32_t>(sub * 32) << 16;
     bool ok = true;
+    // row scales of this thread's 16 queries, loaded for block i+1 while block i is processed
+    auto load_rs = [&](int i, float (&dst)[16]) {
+      const int q = k0 + i * KV_BM + half * 16;
+      const float* src = p.row_scale + row0 + q;
+      if (q + 15 < p.T && (reinterpret_cast<uintptr_t>(src) & 15u) == 0) {
+#pragma unroll
+        for (int v = 0; v < 4; ++v) {
+          const float4 f = __ldg(reinterpret_cast<const float4*>(src) + v);
+          dst[v * 4 + 0] = f.x; dst[v * 4 + 1] = f.y; dst[v * 4 + 2] = f.z; dst[v * 4 + 3] = f.w;
+        }
+      } else {
+#pragma unroll
+        for (int e = 0; e < 16; ++e) dst[e] = (q + e < p.T) ? __ldg(src + e) : 0.f;
+      }
+    };
+    float rs_next[16];
+    if (nqb > 0) load_rs(0, rs_next);
     for (int i = 0; i < nqb && ok; ++i) {
+      float rsv[16];
+#pragma unroll
+      for (int e = 0; e < 16; ++e) rsv[e] = rs_next[e];
+      if (i + 1 < nqb) load_rs(i + 1, rs_next);
       if (!mbar_wait(sc_full, i & 1, p.status, kErrTimeoutEpilogue)) { ok = false; break; }
       tc_fence_after();
       uint32_t a[16], bb[16], g[16];
@@ -483,7 +526,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
         for (int e = 0; e < 2; ++e) {
           const int qt = qb0 + jj + e;
           const bool vis = full_vis || (kreal && qt >= kt && qt < kend);
-          const float rs = vis ? p.row_scale[row0 + qt] : 0.f;
+          const float rs = vis ? rsv[jj + e] : 0.f;
           const float s1 = __uint_as_float(a[jj + e]) * p.sm;
           const float s2 = kTwo ? __uint_as_float(bb[jj + e]) * p.sm : s1;
           const float hh = __uint_as_float(g[jj + e]) * rs;
@@ -583,7 +626,7 @@ void launch_bwd(const void* qkv, long long ld, const void* dout, long long ldo, 
       configured = true;
     }
     dim3 grid((p.T + DQ_BM - 1) / DQ_BM, p.B * p.H);
-    kern<<<grid, kBwdThreads, S::kBytes, stream>>>(tq, tkv, tdo, p);
+    kern<<<grid, kDqThreads, S::kBytes, stream>>>(tq, tkv, tdo, p);
     TTB_CUDA_CHECK(cudaGetLastError());
   }
   {

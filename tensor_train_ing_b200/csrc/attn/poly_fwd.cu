@@ -1,17 +1,20 @@
 // Polynomial attention forward on the 5th-generation tensor cores (sm_100a).
 //
 // One CTA per (batch, head, block of 128 queries).  Warp roles:
-//   warp 0    TMA producer: Q1/Q2 once, then K1/K2/V tiles of 64 keys through a 2-stage ring
-//   warp 1    tcgen05.mma issuer: S1 = Q1 K1^T, S2 = Q2 K2^T into a double-buffered TMEM pair,
-//             then O += P V once the poly warps have produced P
-//   warps 2-9 "poly" warps: warp w owns TMEM lane quadrant w%4 (32 query rows) and one half
+//   warp 0    TMA producer for Q1/Q2 (once) and the K1/K2 ring (3 stages of 64 keys)
+//   warp 1    tcgen05.mma issuer: S1 = Q1 K1^T, S2 = Q2 K2^T into double-buffered TMEM, then
+//             O += P V with P read straight from TMEM (A operand in tensor memory)
+//   warp 2    TMA producer for the V ring (3 stages)
+//   warps 3-10 "poly" warps: warp w owns TMEM lane quadrant w%4 (32 query rows) and one half
 //             (32 keys) of the key block; it tcgen05.ld's its S1/S2 slice, forms
 //             P = visible * row_scale * A(S1, S2) in fp32 (no per-element mask when the slice is
-//             fully visible), rounds to bf16 and writes it into a 128B-swizzled K-major shared
-//             tile; finally the eight warps drain O from TMEM to global memory.
-// S of key block j+1 is computed while the poly warps work on block j, and P V of block j runs
-// after it, so the tensor pipe stays busy.  Key blocks before the start of the first query's
-// document are skipped (documents are contiguous).  Reference: tnlm/kernels/poly_attn.py:38-74.
+//             fully visible), rounds to bf16 and tcgen05.st's it into the P buffer in TMEM;
+//             finally the eight warps drain O from TMEM to global memory.
+// K and V have separate rings: a K stage is released as soon as its S MMAs complete and a V
+// stage when its P V completes, so the loads of later blocks are in flight long before they are
+// needed.  S of key block j+1 is computed while the poly warps work on block j.  Key blocks before
+// the start of the first query's document are skipped (documents are contiguous).
+// Reference: tnlm/kernels/poly_attn.py:38-74.
 #include "../common/host.h"
 #include "attn_api.h"
 #include "poly_common.cuh"
@@ -21,21 +24,23 @@ namespace attn {
 
 constexpr int BMQ = 128;  // queries per CTA
 constexpr int BNK = 64;   // keys per block
-constexpr int kThreads = 320;   // 2 control warps + 8 poly warps
+constexpr int kKStages = 3;
+constexpr int kVStages = 3;
+constexpr int kThreads = 352;   // 3 control warps + 8 poly warps
 constexpr int kPolyThreads = 256;
+constexpr int kFirstPoly = 3;
 
 template <int DK, int DV>
 struct FwdSmem {
   static constexpr int kQ = DK / 64 * BMQ * 128;          // one of Q1/Q2
   static constexpr int kK = DK / 64 * BNK * 128;          // one of K1/K2
   static constexpr int kV = DV / 64 * BNK * 128;
-  static constexpr int kStage = 2 * kK + kV;
-  static constexpr int kP = BMQ * 128;                     // 128 rows x 64 keys bf16
+  static constexpr int kKStage = 2 * kK;
   static constexpr int kOffQ1 = 0;
   static constexpr int kOffQ2 = kQ;
-  static constexpr int kOffStage = 2 * kQ;
-  static constexpr int kOffP = kOffStage + 2 * kStage;
-  static constexpr int kOffBar = kOffP + 2 * kP;
+  static constexpr int kOffK = 2 * kQ;
+  static constexpr int kOffV = kOffK + kKStages * kKStage;
+  static constexpr int kOffBar = kOffV + kVStages * kV;
   // >= 120 KB keeps one CTA per SM, so the 512-column TMEM allocation never waits on a neighbour
   static constexpr int kBytes = (kOffBar + 256 + 1024) > 120 * 1024 ? (kOffBar + 256 + 1024) : 120 * 1024;
 };
@@ -49,15 +54,17 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t* bar = reinterpret_cast<uint64_t*>(smem + S::kOffBar);
   uint64_t* q_full = bar + 0;
-  uint64_t* kv_full = bar + 1;    // [2]
-  uint64_t* kv_empty = bar + 3;   // [2]
-  uint64_t* s_full = bar + 5;     // [2]
-  uint64_t* s_empty = bar + 7;    // [2]
-  uint64_t* p_full = bar + 9;     // [2]
-  uint64_t* p_empty = bar + 11;   // [2]
-  uint64_t* o_full = bar + 13;
-  uint64_t* mma_done = bar + 14;
-  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(bar + 16);
+  uint64_t* k_full = bar + 1;     // [3]
+  uint64_t* k_empty = bar + 4;    // [3]
+  uint64_t* v_full = bar + 7;     // [3]
+  uint64_t* v_empty = bar + 10;   // [3]
+  uint64_t* s_full = bar + 13;    // [2]
+  uint64_t* s_empty = bar + 15;   // [2]
+  uint64_t* p_full = bar + 17;    // [2]
+  uint64_t* p_empty = bar + 19;   // [2]
+  uint64_t* o_full = bar + 21;
+  uint64_t* mma_done = bar + 22;
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(bar + 24);
 
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
   const int nqb = (p.T + BMQ - 1) / BMQ;
@@ -73,9 +80,15 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   if (threadIdx.x == 0) {
     mbar_init(q_full, 1);
+    for (int i = 0; i < kKStages; ++i) {
+      mbar_init(&k_full[i], 1);
+      mbar_init(&k_empty[i], 1);
+    }
+    for (int i = 0; i < kVStages; ++i) {
+      mbar_init(&v_full[i], 1);
+      mbar_init(&v_empty[i], 1);
+    }
     for (int i = 0; i < 2; ++i) {
-      mbar_init(&kv_full[i], 1);
-      mbar_init(&kv_empty[i], 1);
       mbar_init(&s_full[i], 1);
       mbar_init(&s_empty[i], kPolyThreads);
       mbar_init(&p_full[i], kPolyThreads);
@@ -93,8 +106,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_holder;
-  // TMEM columns: S1[2] at 0/64, S2[2] at 128/192, O at 256
-  const uint32_t tS1 = tmem, tS2 = tmem + 128, tO = tmem + 256;
+  // TMEM columns: S1[2] at 0/64, S2[2] at 128/192, P[2] (bf16 pairs) at 256/288, O at 320
+  const uint32_t tS1 = tmem, tS2 = tmem + 128, tP = tmem + 256, tO = tmem + 320;
 
   if (warp == 0) {
     if (elect_one()) {
@@ -106,28 +119,39 @@ __global__ void __launch_bounds__(kThreads, 1)
         tma_load_2d(smem + S::kOffQ1 + i * BMQ * 128, &tmQ, q_full, p.cq1 + h * DK + 64 * i, qrow);
         if (kTwo) tma_load_2d(smem + S::kOffQ2 + i * BMQ * 128, &tmQ, q_full, p.cq2 + h * DK + 64 * i, qrow);
       }
-      bool ok = true;
-      for (int j = 0; j < nkb && ok; ++j) {
-        const int st = j & 1;
-        if (!mbar_wait(&kv_empty[st], ((j >> 1) & 1) ^ 1, p.status, kErrTimeoutProducer)) {
-          ok = false;
-          break;
-        }
-        uint8_t* sk = smem + S::kOffStage + st * S::kStage;
+      int issued = 0;
+      for (int j = 0; j < nkb; ++j) {
+        const int st = j % kKStages;
+        if (!mbar_wait(&k_empty[st], ((j / kKStages) & 1) ^ 1, p.status, kErrTimeoutProducer)) break;
+        uint8_t* sk = smem + S::kOffK + st * S::kKStage;
         const int krow = static_cast<int>(row0 + kstart + j * BNK);
-        mbar_arrive_expect_tx(&kv_full[st], (kTwo ? 2 : 1) * S::kK + S::kV);
+        mbar_arrive_expect_tx(&k_full[st], (kTwo ? 2 : 1) * S::kK);
         for (int i = 0; i < DK / 64; ++i) {
-          tma_load_2d(sk + i * BNK * 128, &tmKV, &kv_full[st], p.ck1 + h * DK + 64 * i, krow);
-          if (kTwo) tma_load_2d(sk + S::kK + i * BNK * 128, &tmKV, &kv_full[st], p.ck2 + h * DK + 64 * i, krow);
+          tma_load_2d(sk + i * BNK * 128, &tmKV, &k_full[st], p.ck1 + h * DK + 64 * i, krow);
+          if (kTwo) tma_load_2d(sk + S::kK + i * BNK * 128, &tmKV, &k_full[st], p.ck2 + h * DK + 64 * i, krow);
         }
-        for (int i = 0; i < DV / 64; ++i)
-          tma_load_2d(sk + 2 * S::kK + i * BNK * 128, &tmKV, &kv_full[st], p.cv + h * DV + 64 * i, krow);
+        issued = j + 1;
       }
       // let in-flight copies land before exit (bounded)
       mbar_wait(q_full, 0, p.status, kErrTimeoutProducer);
-      if (!ok) {
-        for (int j = max(0, nkb - 2); j < nkb; ++j) mbar_wait(&kv_full[j & 1], (j >> 1) & 1, p.status, kErrTimeoutProducer);
+      for (int j = max(0, issued - kKStages); j < issued; ++j)
+        mbar_wait(&k_full[j % kKStages], (j / kKStages) & 1, p.status, kErrTimeoutProducer);
+    }
+  } else if (warp == 2) {
+    if (elect_one()) {
+      int issued = 0;
+      for (int j = 0; j < nkb; ++j) {
+        const int st = j % kVStages;
+        if (!mbar_wait(&v_empty[st], ((j / kVStages) & 1) ^ 1, p.status, kErrTimeoutProducer)) break;
+        uint8_t* sv = smem + S::kOffV + st * S::kV;
+        const int krow = static_cast<int>(row0 + kstart + j * BNK);
+        mbar_arrive_expect_tx(&v_full[st], S::kV);
+        for (int i = 0; i < DV / 64; ++i)
+          tma_load_2d(sv + i * BNK * 128, &tmKV, &v_full[st], p.cv + h * DV + 64 * i, krow);
+        issued = j + 1;
       }
+      for (int j = max(0, issued - kVStages); j < issued; ++j)
+        mbar_wait(&v_full[j % kVStages], (j / kVStages) & 1, p.status, kErrTimeoutProducer);
     }
   } else if (warp == 1) {
     if (elect_one()) {
@@ -136,25 +160,24 @@ __global__ void __launch_bounds__(kThreads, 1)
       const uint32_t sQ1 = smem_u32(smem + S::kOffQ1), sQ2 = smem_u32(smem + S::kOffQ2);
       bool ok = mbar_wait(q_full, 0, p.status, kErrTimeoutMma);
       auto issue_pv = [&](int i) -> bool {
-        const int pb = i & 1;
+        const int pb = i & 1, vs = i % kVStages;
         if (!mbar_wait(&p_full[pb], (i >> 1) & 1, p.status, kErrTimeoutMma)) return false;
+        if (!mbar_wait(&v_full[vs], (i / kVStages) & 1, p.status, kErrTimeoutMma)) return false;
         tc_fence_after();
-        const uint32_t sP = smem_u32(smem + S::kOffP + pb * S::kP);
-        const uint32_t sV = smem_u32(smem + S::kOffStage + pb * S::kStage + 2 * S::kK);
+        const uint32_t sV = smem_u32(smem + S::kOffV + vs * S::kV);
 #pragma unroll
         for (int k = 0; k < BNK / 16; ++k)
-          umma_ss(tO, kmajor_desc(sP, BMQ, k), mnmajor_desc(sV, BNK, k), idPV, (i > 0 || k > 0) ? 1u : 0u);
+          umma_ts(tO, tP + pb * (BNK / 2) + k * 8, mnmajor_desc(sV, BNK, k), idPV, (i > 0 || k > 0) ? 1u : 0u);
         umma_commit(&p_empty[pb]);
-        umma_commit(&kv_empty[pb]);
+        umma_commit(&v_empty[vs]);
         return true;
       };
       for (int j = 0; j < nkb && ok; ++j) {
-        const int st = j & 1;
-        const uint32_t ph = (j >> 1) & 1;
-        if (!mbar_wait(&kv_full[st], ph, p.status, kErrTimeoutMma)) { ok = false; break; }
-        if (!mbar_wait(&s_empty[st], ph ^ 1, p.status, kErrTimeoutMma)) { ok = false; break; }
+        const int st = j & 1, ks = j % kKStages;
+        if (!mbar_wait(&k_full[ks], (j / kKStages) & 1, p.status, kErrTimeoutMma)) { ok = false; break; }
+        if (!mbar_wait(&s_empty[st], ((j >> 1) & 1) ^ 1, p.status, kErrTimeoutMma)) { ok = false; break; }
         tc_fence_after();
-        const uint32_t sK1 = smem_u32(smem + S::kOffStage + st * S::kStage);
+        const uint32_t sK1 = smem_u32(smem + S::kOffK + ks * S::kKStage);
         const uint32_t sK2 = sK1 + S::kK;
 #pragma unroll
         for (int k = 0; k < DK / 16; ++k)
@@ -165,6 +188,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             umma_ss(tS2 + st * BNK, kmajor_desc(sQ2, BMQ, k), kmajor_desc(sK2, BNK, k), idS, k > 0 ? 1u : 0u);
         }
         umma_commit(&s_full[st]);
+        umma_commit(&k_empty[ks]);
         if (j > 0 && !issue_pv(j - 1)) { ok = false; break; }
       }
       if (ok && issue_pv(nkb - 1)) umma_commit(o_full);
@@ -172,10 +196,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_wait(mma_done, 0, p.status, kErrTimeoutMma);
     }
   } else {
-    // ------------------------------------------------------------- poly warps (2..9)
+    // ------------------------------------------------------------- poly warps (3..10)
     const int sub = warp & 3;
-    const int half = (warp - 2) >> 2;  // which 32 keys of the 64-key block
-    const int r = sub * 32 + lane;     // query row inside the block == TMEM lane
+    const int half = (warp - kFirstPoly) >> 2;  // which 32 keys of the 64-key block
+    const int r = sub * 32 + lane;              // query row inside the block == TMEM lane
     const int t = q0 + r;
     const bool valid = t < p.T;
     const long long grow = row0 + (valid ? t : q0);
@@ -226,12 +250,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       // P buffer st is free once P V of block j-2 has completed
       if (!mbar_wait(&p_empty[st], ph ^ 1, p.status, kErrTimeoutEpilogue)) { ok = false; break; }
-      uint8_t* prow = smem + S::kOffP + st * S::kP;
-#pragma unroll
-      for (int ch = 0; ch < 4; ++ch)
-        *reinterpret_cast<uint4*>(prow + sw128_offset(r, half * 4 + ch)) =
-            make_uint4(pk[ch * 4], pk[ch * 4 + 1], pk[ch * 4 + 2], pk[ch * 4 + 3]);
-      fence_proxy_async_smem();
+      tmem_st16(tP + lane_off + st * (BNK / 2) + half * 16, pk);
+      tmem_st_wait();
+      tc_fence_before();
       mbar_arrive(&p_full[st]);
     }
     if (ok && mbar_wait(o_full, 0, p.status, kErrTimeoutEpilogue)) {

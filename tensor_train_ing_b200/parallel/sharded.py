@@ -139,7 +139,8 @@ class ShardedDataParallel:
 
     def grad_norm_sq(self) -> torch.Tensor:
         """Global sum of squared (reduced) gradients: owned regions, summed over ranks."""
-        sq = self.region(self.grad_flat).double().square().sum()
+        # one fused reduction in the gradients' dtype (as torch's clip_grad_norm_); no upcast copy
+        sq = torch.linalg.vector_norm(self.region(self.grad_flat)).double().square()
         if self.world > 1:
             dist.all_reduce(sq, group=self.group)
         return sq
