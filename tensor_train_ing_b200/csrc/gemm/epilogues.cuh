@@ -194,36 +194,95 @@ struct EpiBilinearGrad {
   int mode;
   int M, N;
 
+  // Loads the saved bf16 factors of 32 columns as packed pairs (zero outside the matrix).
+  __device__ __forceinline__ void load_pairs(long long off, bool full, int nv, uint32_t (&lp)[16],
+                                             uint32_t (&rp)[16]) const {
+    if (full) {
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        const uint4 u = *reinterpret_cast<const uint4*>(Lin + off + q * 8);
+        const uint4 v = *reinterpret_cast<const uint4*>(Rin + off + q * 8);
+        lp[q * 4 + 0] = u.x; lp[q * 4 + 1] = u.y; lp[q * 4 + 2] = u.z; lp[q * 4 + 3] = u.w;
+        rp[q * 4 + 0] = v.x; rp[q * 4 + 1] = v.y; rp[q * 4 + 2] = v.z; rp[q * 4 + 3] = v.w;
+      }
+    } else {
+#pragma unroll
+      for (int j = 0; j < 16; ++j) {
+        const float l0 = 2 * j < nv ? __bfloat162float(Lin[off + 2 * j]) : 0.f;
+        const float l1 = 2 * j + 1 < nv ? __bfloat162float(Lin[off + 2 * j + 1]) : 0.f;
+        const float r0 = 2 * j < nv ? __bfloat162float(Rin[off + 2 * j]) : 0.f;
+        const float r1 = 2 * j + 1 < nv ? __bfloat162float(Rin[off + 2 * j + 1]) : 0.f;
+        lp[j] = pack_bf16(l0, l1);
+        rp[j] = pack_bf16(r0, r1);
+      }
+    }
+  }
+
+  // The saved factors of chunk c+1 are loaded while chunk c is computed and stored, so the
+  // global-load latency overlaps useful work instead of stalling every 32-column chunk.
   __device__ __forceinline__ void operator()(uint32_t taddr, int row, int n0, int, int) const {
+    constexpr int kChunks = NB / 32;
+    const bool vec_ok = (ld % 8 == 0);
+    const bool row_ok = row < M;
+    uint32_t lp[16], rp[16];
+    auto chunk_meta = [&](int c, long long& off, bool& full, int& nv) {
+      const int col0 = n0 + c * 32;
+      nv = max(0, min(32, N - col0));
+      full = nv == 32 && vec_ok;
+      off = static_cast<long long>(row) * ld + col0;
+    };
+    {
+      long long off;
+      bool full;
+      int nv;
+      chunk_meta(0, off, full, nv);
+      if (row_ok && nv > 0) load_pairs(off, full, nv, lp, rp);
+    }
 #pragma unroll 1
-    for (int c = 0; c < NB / 32; ++c) {
+    for (int c = 0; c < kChunks; ++c) {
       uint32_t a[32];
       tmem_ld32(taddr + c * 32, a);
+      long long off;
+      bool full;
+      int nv;
+      chunk_meta(c, off, full, nv);
+      uint32_t ln[16], rn[16];
+      if (c + 1 < kChunks) {
+        long long off2;
+        bool full2;
+        int nv2;
+        chunk_meta(c + 1, off2, full2, nv2);
+        if (row_ok && nv2 > 0) load_pairs(off2, full2, nv2, ln, rn);
+      }
       tmem_ld_wait();
-      const int col0 = n0 + c * 32;
-      if (row >= M || col0 >= N) continue;
-      const int nv = min(32, N - col0);
-      const bool full = nv == 32 && (ld % 8 == 0);
-      const long long off = row * ld + col0;
-      float l[32], r[32], dl[32], dr[32];
-      load_row32_bf16(Lin + off, full, nv, l);
-      load_row32_bf16(Rin + off, full, nv, r);
+      if (row_ok && nv > 0) {
+        float dl[32], dr[32];
 #pragma unroll
-      for (int j = 0; j < 32; ++j) {
-        // the reference's autograd sees dH rounded to bf16 (output grad of a bf16 product)
-        const float dh = __bfloat162float(__float2bfloat16_rn(__uint_as_float(a[j])));
-        if (mode == 1) {
-          const float sg = 1.f / (1.f + __expf(-l[j]));
-          const float silu = l[j] * sg;
-          dr[j] = dh * silu;
-          dl[j] = dh * r[j] * (sg * (1.f + l[j] * (1.f - sg)));
-        } else {
-          dl[j] = dh * r[j];
-          dr[j] = dh * l[j];
+        for (int j = 0; j < 32; ++j) {
+          const float l = (j & 1) ? bf16_hi(lp[j / 2]) : bf16_lo(lp[j / 2]);
+          const float r = (j & 1) ? bf16_hi(rp[j / 2]) : bf16_lo(rp[j / 2]);
+          // the reference's autograd sees dH rounded to bf16 (output grad of a bf16 product)
+          const float dh = __bfloat162float(__float2bfloat16_rn(__uint_as_float(a[j])));
+          if (mode == 1) {
+            const float sg = 1.f / (1.f + __expf(-l));
+            const float silu = l * sg;
+            dr[j] = dh * silu;
+            dl[j] = dh * r * (sg * (1.f + l * (1.f - sg)));
+          } else {
+            dl[j] = dh * r;
+            dr[j] = dh * l;
+          }
+        }
+        store_row32_bf16(dL + off, full, nv, dl);
+        store_row32_bf16(dR + off, full, nv, dr);
+      }
+      if (c + 1 < kChunks) {
+#pragma unroll
+        for (int j = 0; j < 16; ++j) {
+          lp[j] = ln[j];
+          rp[j] = rn[j];
         }
       }
-      store_row32_bf16(dL + off, full, nv, dl);
-      store_row32_bf16(dR + off, full, nv, dr);
     }
   }
 };
