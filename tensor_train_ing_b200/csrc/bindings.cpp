@@ -158,7 +158,7 @@ std::vector<Tensor> rmsnorm_fwd(const Tensor& x, const Tensor& w, int64_t groups
 
 // dres (+)= dx; returns dw
 Tensor rmsnorm_bwd(const Tensor& dy, const Tensor& x, const Tensor& w, const Tensor& rstd, Tensor& dres,
-                   bool accumulate, int64_t groups) {
+                   bool accumulate, int64_t groups, c10::optional<Tensor> out16, double scale16) {
   const c10::cuda::CUDAGuard guard(x.device());
   TORCH_CHECK(dy.is_contiguous() && dy.sizes() == x.sizes(), "dy");
   TORCH_CHECK(dy.scalar_type() == torch::kFloat32 || dy.scalar_type() == torch::kBFloat16, "dy dtype");
@@ -166,10 +166,16 @@ Tensor rmsnorm_bwd(const Tensor& dy, const Tensor& x, const Tensor& w, const Ten
   const int N = x.size(0), d = x.size(1);
   auto dw = torch::zeros({d}, x.options());
   if (N == 0) return dw;
+  void* o16 = nullptr;
+  if (out16.has_value()) {
+    check_bf16(*out16, "out16");
+    TORCH_CHECK(out16->is_contiguous() && out16->sizes() == x.sizes(), "out16: contiguous bf16 like x");
+    o16 = out16->data_ptr();
+  }
   auto part = torch::empty({ttb::rmsnorm_bwd_partials(N), d}, x.options());
-  ttb::rmsnorm_bwd(dy.data_ptr(), dy.scalar_type() == torch::kFloat32, x.data_ptr<float>(), w.data_ptr<float>(),
-                   rstd.data_ptr<float>(), dres.data_ptr<float>(), accumulate, part.data_ptr<float>(),
-                   dw.data_ptr<float>(), false, N, d, groups, cur_stream());
+  ttb::rmsnorm_bwd_ex(dy.data_ptr(), dy.scalar_type() == torch::kFloat32, x.data_ptr<float>(), w.data_ptr<float>(),
+                      rstd.data_ptr<float>(), dres.data_ptr<float>(), accumulate, part.data_ptr<float>(),
+                      dw.data_ptr<float>(), false, N, d, groups, o16, static_cast<float>(scale16), cur_stream());
   return dw;
 }
 
@@ -324,7 +330,9 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("bilinear_grad", &bilinear_grad, "dH GEMM fused with the bilinear backward");
   m.def("status", &status, "read and clear the device error word (bounded-wait timeouts)");
   m.def("rmsnorm_fwd", &rmsnorm_fwd, "(group) RMSNorm: fp32 x -> bf16 y, fp32 rstd");
-  m.def("rmsnorm_bwd", &rmsnorm_bwd, "(group) RMSNorm backward; adds dx into the residual grad, returns dw");
+  m.def("rmsnorm_bwd", &rmsnorm_bwd, "(group) RMSNorm backward; adds dx into the residual grad, returns dw",
+        py::arg("dy"), py::arg("x"), py::arg("w"), py::arg("rstd"), py::arg("dres"), py::arg("accumulate"),
+        py::arg("groups"), py::arg("out16") = py::none(), py::arg("scale16") = 1.0);
   m.def("rope_", &rope_, "in-place rotary embedding (or its inverse) on a bf16 [N, ld] buffer");
   m.def("embed_fwd", &embed_fwd, "fp32 embedding gather");
   m.def("embed_bwd", &embed_bwd, "deterministic embedding backward (accumulates into dW)");

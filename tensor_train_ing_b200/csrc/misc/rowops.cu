@@ -103,7 +103,8 @@ __global__ void __launch_bounds__(kRowThreads) rmsnorm_bwd_kernel(const TDY* __r
                                                                  const float* __restrict__ w,
                                                                  const float* __restrict__ rstd,
                                                                  float* __restrict__ dres, int accumulate,
-                                                                 float* __restrict__ dw_part, int N, int d, int G) {
+                                                                 float* __restrict__ dw_part, int N, int d, int G,
+                                                                 __nv_bfloat16* __restrict__ out16, float scale16) {
   __shared__ float red[32];
   const int gsize = d / G;
   float dw[kMaxChunks][4];
@@ -163,6 +164,9 @@ __global__ void __launch_bounds__(kRowThreads) rmsnorm_bwd_kernel(const TDY* __r
           o.x += prev.x; o.y += prev.y; o.z += prev.z; o.w += prev.w;
         }
         *dst = o;
+        if (out16 != nullptr)
+          *reinterpret_cast<uint2*>(out16 + base + j) =
+              make_uint2(pack_bf16(o.x * scale16, o.y * scale16), pack_bf16(o.z * scale16, o.w * scale16));
       }
     }
   }
@@ -253,7 +257,8 @@ __global__ void __launch_bounds__(256) rmsnorm_bwd_warp_kernel(const TDY* __rest
                                                               const float* __restrict__ w,
                                                               const float* __restrict__ rstd, float* __restrict__ dres,
                                                               int accumulate, float* __restrict__ dw_part, int N,
-                                                              int d, int G) {
+                                                              int d, int G, __nv_bfloat16* __restrict__ out16,
+                                                              float scale16) {
   constexpr int NG = GROUPED ? kMaxGroups : 1;
   extern __shared__ float acc[];  // d floats
   const int lane = threadIdx.x % 32, wid = threadIdx.x / 32, nw = blockDim.x / 32;
@@ -331,6 +336,9 @@ __global__ void __launch_bounds__(256) rmsnorm_bwd_warp_kernel(const TDY* __rest
           o.x += prev.x; o.y += prev.y; o.z += prev.z; o.w += prev.w;
         }
         *dst = o;
+        if (out16 != nullptr)
+          *reinterpret_cast<uint2*>(out16 + base + j) =
+              make_uint2(pack_bf16(o.x * scale16, o.y * scale16), pack_bf16(o.z * scale16, o.w * scale16));
       }
     }
   }
@@ -472,6 +480,13 @@ void rmsnorm_fwd(const float* x, const float* w, void* y, float* rstd, int N, in
 void rmsnorm_bwd(const void* dy, bool dy_f32, const float* x, const float* w, const float* rstd, float* dres,
                  bool accumulate, float* dw_part, float* dw, bool dw_accumulate, int N, int d, int G,
                  cudaStream_t stream) {
+  rmsnorm_bwd_ex(dy, dy_f32, x, w, rstd, dres, accumulate, dw_part, dw, dw_accumulate, N, d, G, nullptr, 1.f, stream);
+}
+
+void rmsnorm_bwd_ex(const void* dy, bool dy_f32, const float* x, const float* w, const float* rstd, float* dres,
+                    bool accumulate, float* dw_part, float* dw, bool dw_accumulate, int N, int d, int G,
+                    void* out16_, float scale16, cudaStream_t stream) {
+  __nv_bfloat16* out16 = static_cast<__nv_bfloat16*>(out16_);
   TTB_CHECK(d % 4 == 0 && d <= kRowThreads * kVec * kMaxChunks, "rmsnorm: d must be a multiple of 4 and <= 8192");
   const int grid = rmsnorm_bwd_partials(N);
   const bool done = with_chunks(d, 32, [&](auto ch) {
@@ -481,10 +496,10 @@ void rmsnorm_bwd(const void* dy, bool dy_f32, const float* x, const float* w, co
       constexpr bool GR = decltype(grouped)::value;
       if (dy_f32)
         rmsnorm_bwd_warp_kernel<CH, GR, float><<<grid, 256, smem, stream>>>(static_cast<const float*>(dy), x, w, rstd,
-                                                                            dres, accumulate, dw_part, N, d, G);
+                                                                            dres, accumulate, dw_part, N, d, G, out16, scale16);
       else
         rmsnorm_bwd_warp_kernel<CH, GR, __nv_bfloat16><<<grid, 256, smem, stream>>>(
-            static_cast<const __nv_bfloat16*>(dy), x, w, rstd, dres, accumulate, dw_part, N, d, G);
+            static_cast<const __nv_bfloat16*>(dy), x, w, rstd, dres, accumulate, dw_part, N, d, G, out16, scale16);
     };
     if (G == 1)
       launch(std::false_type{});
@@ -495,10 +510,10 @@ void rmsnorm_bwd(const void* dy, bool dy_f32, const float* x, const float* w, co
   if (!done) {
     if (dy_f32)
       rmsnorm_bwd_kernel<float><<<grid, kRowThreads, 0, stream>>>(static_cast<const float*>(dy), x, w, rstd, dres,
-                                                                  accumulate, dw_part, N, d, G);
+                                                                  accumulate, dw_part, N, d, G, out16, scale16);
     else
       rmsnorm_bwd_kernel<__nv_bfloat16><<<grid, kRowThreads, 0, stream>>>(
-          static_cast<const __nv_bfloat16*>(dy), x, w, rstd, dres, accumulate, dw_part, N, d, G);
+          static_cast<const __nv_bfloat16*>(dy), x, w, rstd, dres, accumulate, dw_part, N, d, G, out16, scale16);
   }
   TTB_CUDA_CHECK(cudaGetLastError());
   colsum_kernel<<<(d + 255) / 256, 256, 0, stream>>>(dw_part, grid, d, dw, dw_accumulate);

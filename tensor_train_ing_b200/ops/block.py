@@ -100,18 +100,50 @@ def attention_branch(blk, h, ctx):
                                 ctx["rope"])
 
 
+def _split_norm(norm) -> bool:
+    return isinstance(norm, (RMSNorm, GroupRMSNorm)) and norm.denom_mode is None
+
+
+def _norm_and_residual(norm, x, up_alpha):
+    """(residual stream, bf16 branch input).  Plain RMS / group norms go through ResidualNormFn,
+    whose backward folds the norm's dx into the residual gradient in place and emits the bf16
+    operand of the upstream branch's backward GEMM (``up_alpha`` = that branch's alpha, None when
+    the stream was not produced by a fused residual GEMM)."""
+    if _split_norm(norm):
+        groups = norm.groups if isinstance(norm, GroupRMSNorm) else 1
+        return fused.residual_norm(x, norm.weight, groups, norm.eps, up_alpha)
+    return x, norm_to_bf16(norm, x)
+
+
+def _fused_residual(blk, branch):
+    return branch not in blk.ablate and isinstance(getattr(blk, f"{branch}_out"), nn.Identity)
+
+
+def _output_alpha(blk, incoming):
+    """Alpha of the fused residual GEMM that produced the block's output stream (None if not fused)."""
+    if "mlp" not in blk.ablate:
+        return blk.alpha if _fused_residual(blk, "mlp") else None
+    if "attn" not in blk.ablate:
+        return blk.alpha if _fused_residual(blk, "attn") else None
+    return incoming
+
+
 def block_forward(blk, x, ctx):
     """x: fp32 [N, d] residual stream."""
     a, m = blk.attn, blk.mlp
+    up = getattr(blk, "_ttb_up_alpha", None)  # set per block by model_forward (structure only)
     if "attn" not in blk.ablate:
-        y = attention_branch(blk, norm_to_bf16(blk.attn_in, x), ctx)
+        x, h = _norm_and_residual(blk.attn_in, x, up)
+        y = attention_branch(blk, h, ctx)
         og = _weights(a, "o", [a.o])
         if isinstance(blk.attn_out, nn.Identity):
             x = fused.linear(y, og, residual=x, alpha=blk.alpha, bias=a.o.bias)
+            up = blk.alpha
         else:
             x = x + blk.alpha * blk.attn_out(fused.linear(y, og, bias=a.o.bias))
+            up = None
     if "mlp" not in blk.ablate:
-        h = norm_to_bf16(blk.mlp_in, x)
+        x, h = _norm_and_residual(blk.mlp_in, x, up)
         gl, gr, gd = _weights(m, "l", [m.l]), _weights(m, "r", [m.r]), _weights(m, "d", [m.d])
         mode = 1 if m.kind == "swiglu" else 0
         if isinstance(blk.mlp_out, nn.Identity):
@@ -127,6 +159,10 @@ def model_forward(model, idx, ctx, targets, reduction):
     cfg = model.cfg
     B, T = idx.shape
     x = fused.embedding(idx.reshape(-1), group_for(model, "embed", [model.embed.weight]))
+    up = None  # the embedding's backward takes the fp32 gradient directly
+    for blk in model.blocks:
+        object.__setattr__(blk, "_ttb_up_alpha", up)
+        up = _output_alpha(blk, up)
     ckpt = cfg.activation_checkpointing and model.training and torch.is_grad_enabled()
     for blk in model.blocks:
         if ckpt:

@@ -40,6 +40,53 @@ def rms_norm(x, w, groups=1, eps=1e-6):
     return RMSNormFn.apply(x.contiguous(), w.contiguous(), groups, eps)
 
 
+def _take_bf16(dout, alpha):
+    """The bf16 operand bf16(alpha * dout) for a backward GEMM: the copy the residual-norm backward
+    attached to ``dout`` when it matches, else a conversion."""
+    pre = getattr(dout, "_ttb_bf16", None)
+    if pre is not None and pre[1] == alpha and pre[0].shape == dout.shape:
+        return pre[0]
+    if alpha != 1.0 or dout.dtype != torch.bfloat16:
+        return (dout * alpha).to(torch.bfloat16).contiguous()
+    return dout.contiguous()
+
+
+class ResidualNormFn(torch.autograd.Function):
+    """(x, h): x passes through to the residual add, h = bf16(x / rms_g(x) * w) feeds the branch.
+
+    Backward: the fp32 residual gradient is updated in place with the norm's dx by the RMSNorm
+    backward kernel, which in the same pass writes bf16(up_alpha * dx_total), the operand the
+    producing branch's backward GEMM needs (attached to the gradient tensor)."""
+
+    @staticmethod
+    def forward(ctx, x, w, groups, eps, up_alpha):
+        h, rstd = lib().rmsnorm_fwd(x, w, int(groups), float(eps))
+        ctx.save_for_backward(x, w, rstd)
+        ctx.groups, ctx.up_alpha = int(groups), up_alpha
+        return x.view_as(x), h
+
+    @staticmethod
+    def backward(ctx, dres, dh):
+        x, w, rstd = ctx.saved_tensors
+        accumulate = dres is not None
+        if not accumulate or dres.dtype != torch.float32 or not dres.is_contiguous():
+            dres = torch.empty_like(x) if not accumulate else dres.float().contiguous().clone()
+        if dh is None:
+            dh = torch.zeros(x.shape, device=x.device, dtype=torch.bfloat16)
+        g16 = torch.empty(x.shape, device=x.device, dtype=torch.bfloat16) if ctx.up_alpha is not None else None
+        dw = lib().rmsnorm_bwd(dh.contiguous(), x, w, rstd, dres, accumulate, ctx.groups, g16,
+                               float(ctx.up_alpha) if ctx.up_alpha is not None else 1.0)
+        if g16 is not None:
+            dres._ttb_bf16 = (g16, ctx.up_alpha)
+        elif hasattr(dres, "_ttb_bf16"):
+            del dres._ttb_bf16
+        return dres, dw, None, None, None
+
+
+def residual_norm(x, w, groups=1, eps=1e-6, up_alpha=None):
+    return ResidualNormFn.apply(x.contiguous(), w.contiguous(), groups, eps, up_alpha)
+
+
 # ============================================================================ linear
 class LinearFn(torch.autograd.Function):
     """out = residual + alpha * (x W^T + b)  (fp32, residual given)  or  bf16(x W^T + b).
@@ -65,8 +112,7 @@ class LinearFn(torch.autograd.Function):
         (x,) = ctx.saved_tensors
         group, alpha = ctx.group, ctx.alpha
         # gradient of the branch output, as the bf16 operand of the backward GEMMs
-        g = (dout * alpha).to(torch.bfloat16) if (alpha != 1.0 or dout.dtype != torch.bfloat16) else dout
-        g = g.contiguous()
+        g = _take_bf16(dout, alpha)
         w16 = group.bf16()
         dx = torch.empty_like(x)
         _mm(g, w16, dx)
@@ -198,7 +244,7 @@ class BilinearMLPFn(torch.autograd.Function):
     def backward(ctx, dout):
         x, h, l, r = ctx.saved_tensors
         g_l, g_r, g_d = ctx.groups
-        g = (dout * ctx.alpha).to(torch.bfloat16).contiguous()
+        g = _take_bf16(dout, ctx.alpha)
         wd = g_d.bf16()
         dl = torch.empty_like(l)
         dr = torch.empty_like(r)

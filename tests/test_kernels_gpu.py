@@ -98,6 +98,33 @@ def test_rmsnorm_fwd_bwd_groups():
         assert rel(w.grad, wr.grad) < 1e-2
 
 
+def test_residual_norm_folds_dx_into_residual_grad_and_emits_bf16_copy():
+    torch.manual_seed(2)
+    for groups, d in ((1, 512), (4, 2048), (1, 6144)):
+        x = torch.randn(200, d, device="cuda", requires_grad=True)
+        w = (1 + 0.1 * torch.randn(d, device="cuda")).requires_grad_()
+        xr, h = fused.residual_norm(x, w, groups, 1e-6, up_alpha=0.5)
+        gres = torch.randn(200, d, device="cuda")
+        gh = torch.randn(200, d, device="cuda").bfloat16()
+        captured = {}
+
+        def hook(g):
+            captured["g"] = g
+        x.register_hook(hook)
+        torch.autograd.backward([xr, h], [gres.clone(), gh])
+        xd, wd = x.detach().double().requires_grad_(), w.detach().double().requires_grad_()
+        xg = xd.unflatten(-1, (groups, -1))
+        r = (xg.square().mean(-1, keepdim=True) + 1e-6).sqrt()
+        yr = (xg / r).flatten(-2) * wd
+        (yr * gh.double()).sum().backward()
+        expect = xd.grad + gres.double()
+        assert rel(x.grad, expect) < 1e-2
+        assert rel(w.grad, wd.grad) < 1e-2
+        g16, alpha = captured["g"]._ttb_bf16
+        assert alpha == 0.5 and g16.dtype == torch.bfloat16
+        assert rel(g16.float(), 0.5 * expect) < 1e-2
+
+
 def test_qkv_rope_gemm_matches_reference_rope():
     torch.manual_seed(5)
     from tensor_train_ing_b200.ops.block import rope_context
