@@ -6,6 +6,8 @@
 #include "api.h"
 #include "gemm_sm100.cuh"
 
+#include <cstdlib>
+
 namespace ttb {
 namespace gemm {
 
@@ -26,9 +28,59 @@ inline void launch_impl(const CUtensorMap& ta, const CUtensorMap& tb, const CUte
   TTB_CUDA_CHECK(cudaGetLastError());
 }
 
+constexpr int kPairStages = 6;
+
+// CTA-pair GEMM for plain (single-B) problems with 256-column tiles; off when TTB_GEMM_PAIR=0.
+inline bool pair_enabled() {
+  static const bool on = [] {
+    const char* v = std::getenv("TTB_GEMM_PAIR");
+    return v == nullptr || v[0] != '0';
+  }();
+  return on;
+}
+
+template <class Epi, bool A_MN, bool B_MN, bool DUAL>
+inline void launch_pair(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& tb2, Shape s, const Epi& epi,
+                        cudaStream_t stream) {
+  using L = PairLayout<kPairStages, DUAL>;
+  auto kern = gemm_pair_kernel<kPairStages, A_MN, B_MN, DUAL, Epi>;
+  static bool configured = false;
+  if (!configured) {
+    TTB_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kSmemBytes));
+    configured = true;
+  }
+  const int tiles = ((s.M + kPairBM - 1) / kPairBM) * ((s.N + L::kTileN - 1) / L::kTileN);
+  const int pairs = num_sms() / 2;
+  const int grid = 2 * (tiles < pairs ? tiles : pairs);
+  kern<<<grid, kThreads, L::kSmemBytes, stream>>>(ta, tb, tb2, s, epi);
+  TTB_CUDA_CHECK(cudaGetLastError());
+}
+
 template <int BN, int STAGES, bool DUAL, class Epi>
 inline void dispatch(const Operand& a, const Operand& b, const Operand* b2, Shape s, const Epi& epi,
                      cudaStream_t stream) {
+  if constexpr (BN == 256) {
+    if (pair_enabled() && s.M >= kPairBM) {
+      using L = PairLayout<kPairStages, DUAL>;
+      // per CTA: 128-row A boxes and kBCols-column B boxes (MN-major operands use 64-wide boxes)
+      const CUtensorMap ta = a.mn_major
+                                 ? make_tmap_2d(a.ptr, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, s.M, s.K, a.ld, 64, BK)
+                                 : make_tmap_2d(a.ptr, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, s.K, s.M, a.ld, BK, kPairHalf);
+      auto bmap = [&](const Operand& o) {
+        return o.mn_major ? make_tmap_2d(o.ptr, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, s.N, s.K, o.ld, 64, BK)
+                          : make_tmap_2d(o.ptr, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, s.K, s.N, o.ld, BK, L::kBCols);
+      };
+      const CUtensorMap tb = bmap(b);
+      const CUtensorMap tb2 = b2 != nullptr ? bmap(*b2) : tb;
+      TTB_CHECK(b2 == nullptr || b2->mn_major == b.mn_major, "dual GEMM operands must share a layout");
+      if (a.mn_major) {
+        if (b.mn_major) return launch_pair<Epi, true, true, DUAL>(ta, tb, tb2, s, epi, stream);
+        return launch_pair<Epi, true, false, DUAL>(ta, tb, tb2, s, epi, stream);
+      }
+      if (b.mn_major) return launch_pair<Epi, false, true, DUAL>(ta, tb, tb2, s, epi, stream);
+      return launch_pair<Epi, false, false, DUAL>(ta, tb, tb2, s, epi, stream);
+    }
+  }
   constexpr int NB = DUAL ? BN / 2 : BN;
   // A: rows = M, contraction = K.  K-major -> [M, K] rows; MN-major -> [K, M] rows.
   const CUtensorMap ta = a.mn_major

@@ -247,5 +247,219 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
 }
 
+// ============================================================================ CTA-pair GEMM
+// The same persistent, warp-specialised structure on a cluster of two CTAs (two SMs) that
+// computes 256 x 256 output tiles with M=256 tcgen05.mma (cta_group::2): CTA r of the pair stages
+// rows [128 r, 128 r + 128) of the A tile and columns [128 r, 128 r + 128) of the B tile, so each SM
+// streams half of the B tile instead of all of it, and the even CTA issues the MMAs for both.
+// Its full barriers count the TMA bytes of both CTAs; its commits arrive on the stage / accumulator
+// barriers of both CTAs (multicast commit); the epilogue warps of both CTAs release an accumulator
+// buffer by arriving on the even CTA's barrier.  Loads are never multicast.
+constexpr int kPairBM = 256;   // rows per pair tile (128 per CTA)
+constexpr int kPairBN = 256;   // columns per pair tile (128 of B staged per CTA)
+constexpr int kPairHalf = 128;
+
+// DUAL: two B operands of 128 columns each per pair tile (64 staged per CTA), as in the bilinear
+// MLP; the two accumulators sit side by side in tensor memory.
+template <int STAGES, bool DUAL>
+struct PairLayout {
+  static constexpr int kBCols = DUAL ? kPairHalf / 2 : kPairHalf;  // B columns staged per CTA, per operand
+  static constexpr int kTileN = DUAL ? kPairBN / 2 : kPairBN;       // output columns per pair tile
+  static constexpr int kABytes = kPairHalf * BK * 2;   // this CTA's 128 rows of A
+  static constexpr int kBBytes = kBCols * BK * 2;      // this CTA's columns of one B operand
+  static constexpr int kStageBytes = kABytes + (DUAL ? 2 : 1) * kBBytes;
+  static constexpr int kAccCols = kPairBN;
+  static constexpr int kTmemCols = 2 * kPairBN;        // double-buffered 256-column accumulators
+  static constexpr int kBarOffset = STAGES * kStageBytes;
+  static constexpr int kSmemBytes = kBarOffset + (2 * STAGES + 5) * 8 + 16 + 1024;
+};
+
+template <int STAGES, bool A_MN, bool B_MN, bool DUAL, class Epi>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
+    gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                     const __grid_constant__ CUtensorMap tmB2, Shape s, Epi epi) {
+  using L = PairLayout<STAGES, DUAL>;
+  constexpr int TN = L::kTileN;
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + L::kBarOffset);
+  uint64_t* empty = full + STAGES;
+  uint64_t* tfull = empty + STAGES;
+  uint64_t* tempty = tfull + 2;
+  uint64_t* mma_done = tempty + 2;
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(mma_done + 1);
+
+  const int warp = threadIdx.x / 32;
+  const int lane = threadIdx.x % 32;
+  const uint32_t rank = cluster_ctarank();
+  const bool leader = rank == 0;
+  const int pair = blockIdx.x >> 1;
+  const int npairs = gridDim.x >> 1;
+  const int m_tiles = (s.M + kPairBM - 1) / kPairBM;
+  const int n_tiles = (s.N + TN - 1) / TN;
+  const int num_tiles = m_tiles * n_tiles;
+  const int k_blocks = (s.K + BK - 1) / BK;
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < STAGES; ++i) {
+      mbar_init(&full[i], 1);   // the even CTA's producer arrival (+ both CTAs' bytes)
+      mbar_init(&empty[i], 1);  // the even CTA's multicast commit
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&tfull[i], 1);
+      mbar_init(&tempty[i], 2 * 128);  // epilogue threads of both CTAs
+    }
+    mbar_init(mma_done, 1);
+    fence_mbar_init();
+  }
+  if (warp == 0 && lane == 0) {
+    prefetch_tmap(&tmA);
+    prefetch_tmap(&tmB);
+    if (DUAL) prefetch_tmap(&tmB2);
+  }
+  if (warp == 1) {
+    tmem_alloc_pair(tmem_holder, L::kTmemCols);
+    tmem_relinquish_pair();
+  }
+  tc_fence_before();
+  cluster_sync();  // barriers of both CTAs are initialised before any remote arrival
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_holder;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------------ TMA producer (both CTAs)
+    if (elect_one()) {
+      int stage = 0;
+      uint32_t phase = 0;
+      int loaded = 0;
+      bool ok = true;
+      for (int tile = pair; tile < num_tiles && ok; tile += npairs) {
+        int tm, tn;
+        tile_coords(tile, m_tiles, n_tiles, tm, tn);
+        const int m0 = tm * kPairBM + static_cast<int>(rank) * kPairHalf;
+        const int n0 = tn * TN + static_cast<int>(rank) * L::kBCols;
+        for (int kb = 0; kb < k_blocks; ++kb) {
+          if (!mbar_wait(&empty[stage], phase ^ 1, s.status, kErrTimeoutProducer)) {
+            ok = false;
+            break;
+          }
+          uint8_t* sa = smem + stage * L::kStageBytes;
+          uint8_t* sb = sa + L::kABytes;
+          if (leader) mbar_arrive_expect_tx(&full[stage], 2 * L::kStageBytes);
+          const uint32_t bar = mapa_shared(smem_u32(&full[stage]), 0);
+          const int k0 = kb * BK;
+          if (A_MN) {
+#pragma unroll
+            for (int i = 0; i < kPairHalf / 64; ++i) tma_load_2d_pair(sa + i * 64 * BK * 2, &tmA, bar, m0 + 64 * i, k0);
+          } else {
+            tma_load_2d_pair(sa, &tmA, bar, k0, m0);
+          }
+          if (B_MN) {
+#pragma unroll
+            for (int i = 0; i < L::kBCols / 64; ++i) {
+              tma_load_2d_pair(sb + i * 64 * BK * 2, &tmB, bar, n0 + 64 * i, k0);
+              if (DUAL) tma_load_2d_pair(sb + L::kBBytes + i * 64 * BK * 2, &tmB2, bar, n0 + 64 * i, k0);
+            }
+          } else {
+            tma_load_2d_pair(sb, &tmB, bar, k0, n0);
+            if (DUAL) tma_load_2d_pair(sb + L::kBBytes, &tmB2, bar, k0, n0);
+          }
+          ++loaded;
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+      }
+      // Every stage this CTA filled must have been consumed before the pair tears down (the MMAs
+      // read this CTA's shared memory); bounded waits.
+      for (int i = 0; i < STAGES && i < loaded; ++i) {
+        const int idx = loaded - 1 - i;
+        mbar_wait(&empty[idx % STAGES], (idx / STAGES) & 1, s.status, kErrTimeoutProducer);
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------------ MMA issuer (even CTA)
+    if (leader && elect_one()) {
+      constexpr uint32_t idesc = idesc_bf16_f32(kPairBM, TN, A_MN ? 1 : 0, B_MN ? 1 : 0);
+      int stage = 0;
+      uint32_t phase = 0;
+      int acc = 0;
+      uint32_t acc_phase = 0;
+      bool ok = true;
+      for (int tile = pair; tile < num_tiles && ok; tile += npairs) {
+        if (!mbar_wait(&tempty[acc], acc_phase ^ 1, s.status, kErrTimeoutMma)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + acc * L::kAccCols;
+        for (int kb = 0; kb < k_blocks; ++kb) {
+          if (!mbar_wait(&full[stage], phase, s.status, kErrTimeoutMma)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t sa = smem_u32(smem + stage * L::kStageBytes);
+          const uint32_t sb = sa + L::kABytes;
+#pragma unroll
+          for (int k = 0; k < BK / 16; ++k) {
+            const uint64_t adesc = A_MN ? smem_desc(sa + k * 2048, 64 * BK * 2, 1024) : smem_desc(sa + k * 32, 16, 1024);
+            const uint64_t bdesc = B_MN ? smem_desc(sb + k * 2048, 64 * BK * 2, 1024) : smem_desc(sb + k * 32, 16, 1024);
+            umma_ss_pair(d_tmem, adesc, bdesc, idesc, (kb > 0 || k > 0) ? 1u : 0u);
+            if (DUAL) {
+              const uint32_t sb2 = sb + L::kBBytes;
+              const uint64_t bdesc2 =
+                  B_MN ? smem_desc(sb2 + k * 2048, 64 * BK * 2, 1024) : smem_desc(sb2 + k * 32, 16, 1024);
+              umma_ss_pair(d_tmem + TN, adesc, bdesc2, idesc, (kb > 0 || k > 0) ? 1u : 0u);
+            }
+          }
+          umma_commit_pair(&empty[stage], 0x3);
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+        if (!ok) break;
+        umma_commit_pair(&tfull[acc], 0x3);
+        if (++acc == 2) {
+          acc = 0;
+          acc_phase ^= 1;
+        }
+      }
+      umma_commit_pair(mma_done, 0x1);
+      mbar_wait(mma_done, 0, s.status, kErrTimeoutMma);
+    }
+  } else {
+    // ------------------------------------------------------------------ epilogue (warps 2..5, both CTAs)
+    const int sub = warp & 3;
+    int acc = 0;
+    uint32_t acc_phase = 0;
+    for (int tile = pair; tile < num_tiles; tile += npairs) {
+      int tm, tn;
+      tile_coords(tile, m_tiles, n_tiles, tm, tn);
+      if (!mbar_wait(&tfull[acc], acc_phase, s.status, kErrTimeoutEpilogue)) break;
+      tc_fence_after();
+      const uint32_t taddr = tmem_base + (static_cast<uint32_t>(sub * 32) << 16) + acc * L::kAccCols;
+      const int row = tm * kPairBM + static_cast<int>(rank) * kPairHalf + sub * 32 + lane;
+      epi(taddr, row, tn * TN, tm, tn);
+      tc_fence_before();
+      mbar_arrive_cluster(mapa_shared(smem_u32(&tempty[acc]), 0));
+      if (++acc == 2) {
+        acc = 0;
+        acc_phase ^= 1;
+      }
+    }
+  }
+
+  __syncwarp();
+  tc_fence_before();
+  cluster_sync();  // no MMA, commit or remote arrival of either CTA is still in flight
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc_pair(tmem_base, L::kTmemCols);
+  }
+}
+
 }  // namespace gemm
 }  // namespace ttb
