@@ -12,6 +12,7 @@
 #include "gemm/api.h"
 #include "gemm/ce_api.h"
 #include "misc/rowops.h"
+#include "comm/peer.h"
 
 namespace {
 
@@ -317,6 +318,40 @@ std::vector<Tensor> poly_bwd(int64_t kind, int64_t dk, int64_t dv, const Tensor&
   return {dqkv, dpar};
 }
 
+// ---------------------------------------------------------------------------- peer collectives
+ttb::PeerPtrs peer_ptrs(const std::vector<int64_t>& ptrs) {
+  TORCH_CHECK(!ptrs.empty() && static_cast<int>(ptrs.size()) <= ttb::kMaxPeers, "1..8 peer pointers");
+  ttb::PeerPtrs p{};
+  for (size_t i = 0; i < ptrs.size(); ++i) p.p[i] = reinterpret_cast<void*>(ptrs[i]);
+  return p;
+}
+
+void peer_barrier(const std::vector<int64_t>& pads, int64_t rank, int64_t epoch) {
+  ttb::peer_barrier(peer_ptrs(pads), static_cast<int>(pads.size()), static_cast<int>(rank),
+                    static_cast<uint32_t>(epoch), cur_stream());
+}
+
+// Pull-based reduce-scatter of the flat fp32 buffers: out (this rank's region of its own buffer)
+// = sum over ranks of their [off, off + n); returns the per-block partial sums of squares (fp64).
+Tensor rs_reduce_sq(const std::vector<int64_t>& bufs, int64_t off, Tensor& out) {
+  TORCH_CHECK(out.scalar_type() == torch::kFloat32 && out.is_contiguous(), "out: contiguous fp32");
+  TORCH_CHECK(reinterpret_cast<uintptr_t>(out.data_ptr()) % 16 == 0, "out: 16-byte aligned");
+  auto partial = torch::empty({ttb::rs_reduce_blocks()}, out.options().dtype(torch::kFloat64));
+  ttb::rs_reduce_sq(peer_ptrs(bufs), static_cast<int>(bufs.size()), off, out.numel(), out.data_ptr<float>(),
+                    partial.data_ptr<double>(), cur_stream());
+  return partial;
+}
+
+// segs: int64 [nseg, 4] rows (src, dst32, dst16, n) of device addresses (0 = absent), on the device.
+void ag_pull_cast(const Tensor& segs, int64_t max_n) {
+  TORCH_CHECK(segs.scalar_type() == torch::kInt64 && segs.is_cuda() && segs.is_contiguous() && segs.dim() == 2 &&
+                  segs.size(1) == 4,
+              "segs: int64 [nseg, 4] on the device");
+  static_assert(sizeof(ttb::CopySeg) == 32, "CopySeg layout");
+  ttb::ag_pull_cast(reinterpret_cast<const ttb::CopySeg*>(segs.data_ptr<int64_t>()), static_cast<int>(segs.size(0)),
+                    max_n, cur_stream());
+}
+
 int64_t status() { return static_cast<int64_t>(ttb::status_read_and_reset()); }
 
 }  // namespace
@@ -329,6 +364,9 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("bilinear", &bilinear, "dual-B GEMM forming the bilinear hidden layer");
   m.def("bilinear_grad", &bilinear_grad, "dH GEMM fused with the bilinear backward");
   m.def("status", &status, "read and clear the device error word (bounded-wait timeouts)");
+  m.def("peer_barrier", &peer_barrier, "cross-GPU barrier through symmetric signal pads (bounded wait)");
+  m.def("rs_reduce_sq", &rs_reduce_sq, "pull reduce-scatter over peer buffers with fused sum-of-squares partials");
+  m.def("ag_pull_cast", &ag_pull_cast, "pull all-gather over peer buffers with fused bf16 weight-cache writes");
   m.def("rmsnorm_fwd", &rmsnorm_fwd, "(group) RMSNorm: fp32 x -> bf16 y, fp32 rstd");
   m.def("rmsnorm_bwd", &rmsnorm_bwd, "(group) RMSNorm backward; adds dx into the residual grad, returns dw",
         py::arg("dy"), py::arg("x"), py::arg("w"), py::arg("rstd"), py::arg("dres"), py::arg("accumulate"),

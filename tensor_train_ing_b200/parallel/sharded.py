@@ -22,10 +22,19 @@ FSDP unshards:
   is 1 reduce-scatter + 1 all-gather of the model, where FSDP2 issues 2 all-gathers and a
   reduce-scatter per block per micro-batch.
 
+On CUDA with NCCL the two flat buffers live in symmetric memory (mapped into every rank's address
+space over NVLink) and both collectives are this framework's own kernels: the reduce-scatter pulls
+each peer's copy of the local region and sums it in rank order (deterministic) while emitting the
+sum of squares for the clip, and the all-gather pulls each owner's updated region while writing the
+bf16 operand caches of the GEMM weights in the same pass.  A bounded cross-GPU barrier through
+symmetric signal pads orders them.  ``TTB_PEER_COLLECTIVES=0`` selects NCCL instead.
+
 With the gloo backend (CPU tests) the reduce-scatter is an all-reduce and the all-gather a
 broadcast per rank region; the arithmetic is the same sum.
 """
 from __future__ import annotations
+
+import os
 
 import torch
 import torch.distributed as dist
@@ -83,8 +92,13 @@ class ShardedDataParallel:
         for i, n in enumerate(sizes):
             load[self.owner[i]] += _aligned(n)
         self.shard = _aligned(max(load) if load else 0)
-        self.grad_flat = torch.zeros(self.world * self.shard, device=device, dtype=dtype)
-        self.param_flat = torch.zeros(self.world * self.shard, device=device, dtype=dtype)
+        self.peer = (self.world > 1 and self.backend == "nccl" and device.type == "cuda" and fused
+                     and dtype == torch.float32 and os.environ.get("TTB_PEER_COLLECTIVES", "1") != "0")
+        if self.peer:
+            self._init_symmetric(device, dtype)
+        else:
+            self.grad_flat = torch.zeros(self.world * self.shard, device=device, dtype=dtype)
+            self.param_flat = torch.zeros(self.world * self.shard, device=device, dtype=dtype)
         cursor = [r * self.shard for r in range(self.world)]
         self.units = []
         with torch.no_grad():
@@ -102,6 +116,58 @@ class ShardedDataParallel:
                 self.units.append((kind, obj, params, off, n, r))
         self.layout = [{"kind": k, "params": [self._name(p) for p in ps], "offset": off, "numel": n, "owner": r}
                        for k, _, ps, off, n, r in self.units]
+        self._sq = None
+        if self.peer:
+            self._build_gather_plan()
+
+    # ------------------------------------------------------------------ symmetric memory
+    def _init_symmetric(self, device, dtype):
+        # plain peer mappings only: these kernels use ordinary loads and stores, never multimem
+        os.environ.setdefault("TORCH_SYMM_MEM_DISABLE_MULTICAST", "1")
+        import torch.distributed._symmetric_memory as symm_mem
+        group = self.group if self.group is not None else dist.group.WORLD
+        enable = getattr(symm_mem, "enable_symm_mem_for_group", None)
+        if enable is not None:
+            enable(group.group_name)
+        n = self.world * self.shard
+        self.grad_flat = symm_mem.empty(n, dtype=dtype, device=device)
+        self.param_flat = symm_mem.empty(n, dtype=dtype, device=device)
+        self.grad_flat.zero_()
+        self.param_flat.zero_()
+        hg = symm_mem.rendezvous(self.grad_flat, group)
+        hp = symm_mem.rendezvous(self.param_flat, group)
+        self._handles = (hg, hp)
+        self._gptrs = [int(x) for x in hg.buffer_ptrs]
+        self._pptrs = [int(x) for x in hp.buffer_ptrs]
+        self._pads = [int(x) for x in hg.signal_pad_ptrs]
+        self._epoch = 0
+
+    def _build_gather_plan(self):
+        """Copy segments of the fused all-gather: every unit from its owner's buffer into the local
+        one (own units are not copied), plus the bf16 cache of every weight group."""
+        from ..ops._ext import lib
+        rows, max_n = [], 0
+        local = self.param_flat.data_ptr()
+        for kind, obj, params, off, n, r in self.units:
+            n4 = (n + 3) // 4 * 4  # units are 64-element aligned, so the rounded tail stays in padding
+            src = self._pptrs[r] + 4 * off
+            dst32 = 0 if r == self.rank else local + 4 * off
+            dst16 = 0
+            if kind == "group":
+                cache = obj.bf16()  # allocates the cache; the gather refreshes it every step
+                assert cache.numel() == n
+                dst16 = cache.data_ptr()
+            if dst32 == 0 and dst16 == 0:
+                continue
+            rows.append((src, dst32, dst16, n4 if dst16 == 0 else n))
+            max_n = max(max_n, n4)
+        self._segs = torch.tensor(rows, dtype=torch.int64).to(self.param_flat.device) if rows else None
+        self._seg_max = max_n
+        self._lib = lib
+
+    def _barrier(self):
+        self._epoch += 1
+        self._lib().peer_barrier(self._pads, self.rank, self._epoch)
 
     def _name(self, p):
         if not hasattr(self, "_names"):
@@ -132,15 +198,23 @@ class ShardedDataParallel:
         """Sum gradients over ranks; afterwards this rank's region holds its owned units' sums."""
         if self.world == 1:
             return
-        if self.backend == "nccl":
+        self._sq = None
+        if self.peer:
+            self._barrier()  # every rank's backward has finished writing its buffer
+            partial = self._lib().rs_reduce_sq(self._gptrs, self.rank * self.shard, self.region(self.grad_flat))
+            self._sq = partial.sum()
+        elif self.backend == "nccl":
             dist.reduce_scatter_tensor(self.region(self.grad_flat), self.grad_flat, group=self.group)
         else:
             dist.all_reduce(self.grad_flat, group=self.group)
 
     def grad_norm_sq(self) -> torch.Tensor:
         """Global sum of squared (reduced) gradients: owned regions, summed over ranks."""
-        # one fused reduction in the gradients' dtype (as torch's clip_grad_norm_); no upcast copy
-        sq = torch.linalg.vector_norm(self.region(self.grad_flat)).double().square()
+        if self._sq is not None:  # emitted by the fused reduce-scatter
+            sq = self._sq.clone()
+        else:
+            # one fused reduction in the gradients' dtype (as torch's clip_grad_norm_); no upcast copy
+            sq = torch.linalg.vector_norm(self.region(self.grad_flat)).double().square()
         if self.world > 1:
             dist.all_reduce(sq, group=self.group)
         return sq
@@ -157,7 +231,14 @@ class ShardedDataParallel:
         """Bring every rank the owners' updated parameters."""
         if self.world == 1:
             return
-        if self.backend == "nccl":
+        if self.peer:
+            self._barrier()  # every owner has updated its region
+            if self._segs is not None:
+                self._lib().ag_pull_cast(self._segs, self._seg_max)
+            for kind, obj, *_ in self.units:
+                if kind == "group":
+                    obj._key = obj._version_key()  # the caches were written from the gathered values
+        elif self.backend == "nccl":
             dist.all_gather_into_tensor(self.param_flat, self.region(self.param_flat), group=self.group)
         else:
             ranks = dist.get_process_group_ranks(self.group) if self.group is not None else range(self.world)
