@@ -1,5 +1,6 @@
-"""Worker (NCCL, one GPU per rank): the peer-memory reduce-scatter / all-gather path of
-ShardedDataParallel against the NCCL path on identical training steps.  Prints PEER_OK on rank 0."""
+"""Worker (NCCL, one GPU per rank): the peer-memory reduce-scatter / all-gather of
+ShardedDataParallel against NCCL's collectives on the same buffers, then a few training steps of
+both paths.  Prints PEER_OK on rank 0."""
 import os
 import sys
 
@@ -24,41 +25,72 @@ def build(peer: bool):
     return eng
 
 
+def batch(g, world, rank):
+    idx = torch.randint(0, 1000, (4 * world, 256), generator=g)
+    doc = torch.zeros_like(idx)
+    doc[:, 100:] = 1
+    tgt = torch.roll(idx, -1, 1)
+    tgt[:, -1] = -100
+    sl = slice(4 * rank, 4 * rank + 4)
+    return idx[sl], doc[sl], tgt[sl]
+
+
+def rel(a, b):
+    return float((a - b).norm() / b.norm().clamp_min(1e-30))
+
+
 def main():
     dist.init_process_group("nccl")
     rank, world = dist.get_rank(), dist.get_world_size()
     torch.cuda.set_device(int(os.environ["LOCAL_RANK"]))
-    a, b = build(False), build(True)
+    b = build(True)
+    dp = b.dp
     g = torch.Generator().manual_seed(1)
-    for step in range(3):
-        idx = torch.randint(0, 1000, (4 * world, 256), generator=g)
-        doc = torch.zeros_like(idx)
-        doc[:, 100:] = 1
-        tgt = torch.roll(idx, -1, 1)
-        tgt[:, -1] = -100
-        sl = slice(4 * rank, 4 * rank + 4)
-        la, _ = a.step(idx[sl], doc[sl], tgt[sl])
-        lb, _ = b.step(idx[sl], doc[sl], tgt[sl])
-        torch.cuda.synchronize()
-        check_status()
-        assert abs(float(la) - float(lb)) <= 1e-3 * abs(float(la)), (float(la), float(lb))
-    worst = 0.0
-    for (n, pa), (_, pb) in zip(a.model.named_parameters(), b.model.named_parameters()):
-        worst = max(worst, float((pa.detach() - pb.detach()).abs().max() / pa.detach().abs().max().clamp_min(1e-12)))
-    assert worst < 2e-2, worst  # reduction order differs (NCCL ring vs rank order); Muon amplifies little
-    # replicas of the peer path are bitwise identical across ranks
+    # ---- the collectives themselves against NCCL on the same data
+    idx, doc, tgt = batch(g, world, rank)
+    b.zero_grad()
+    b.forward_backward(idx, doc, tgt, torch.ones((), device="cuda"))
+    full = dp.grad_flat.clone()
+    expect = torch.empty(dp.shard, device="cuda")
+    dist.reduce_scatter_tensor(expect, full)
+    dp.reduce_gradients()
+    got = dp.region(dp.grad_flat)
+    e_rs = rel(got, expect)
+    e_sq = abs(float(dp._sq) - float(expect.double().square().sum())) / float(expect.double().square().sum())
+    with torch.no_grad():
+        dp.region(dp.param_flat).add_(0.25 * (rank + 1))
+    pf = dp.param_flat.clone()
+    want = torch.empty_like(pf)
+    dist.all_gather_into_tensor(want, pf[rank * dp.shard:(rank + 1) * dp.shard].contiguous())
     for p in b.model.parameters():
-        mine = p.detach().clone()
-        dist.broadcast(p.detach(), src=0)
-        assert torch.equal(mine, p.detach()), "peer all-gather left replicas different"
-    # the fused all-gather wrote the bf16 operand caches from the gathered fp32 values
-    for kind, obj, *_ in b.dp.units:
+        p.data.add_(0.0)  # bump versions like an optimizer step
+    dp.gather_params()
+    torch.cuda.synchronize()
+    check_status()
+    for kind, obj, params, off, n, owner in dp.units:  # alignment padding is not gathered
+        assert torch.equal(dp.param_flat[off:off + n], want[off:off + n]), "peer all-gather differs from NCCL"
+    assert e_rs < 1e-6 and e_sq < 1e-5, (e_rs, e_sq)
+    for kind, obj, *_ in dp.units:
         if kind == "group":
             ref = torch.cat([p.detach().reshape(obj.rows[i], obj.d_in) for i, p in enumerate(obj.params)]).bfloat16()
             assert torch.equal(obj._cache, ref), "stale bf16 cache"
             assert obj._key == obj._version_key()
+    # ---- training steps: peer path vs NCCL path
+    del b
+    a, b = build(False), build(True)
+    for step in range(3):
+        batch_ = batch(g, world, rank)
+        la, _ = a.step(*batch_)
+        lb, _ = b.step(*batch_)
+        torch.cuda.synchronize()
+        check_status()
+        assert abs(float(la) - float(lb)) <= 1e-3 * abs(float(la)), (float(la), float(lb))
+    for p in b.model.parameters():
+        mine = p.detach().clone()
+        dist.broadcast(p.detach(), src=0)
+        assert torch.equal(mine, p.detach()), "peer all-gather left replicas different"
     if rank == 0:
-        print(f"PEER_OK worst_rel={worst:.3e}", flush=True)
+        print(f"PEER_OK rs_rel={e_rs:.2e} sq_rel={e_sq:.2e}", flush=True)
     dist.barrier()
     del a, b
     dist.destroy_process_group()
