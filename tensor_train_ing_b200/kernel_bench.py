@@ -1,0 +1,168 @@
+"""Kernel micro-benchmarks and profiling cases for the sm_100a library.
+
+    python -m tensor_train_ing_b200.kernel_bench time [CASE ...]      CUDA-event timings, TFLOP/s, GB/s
+    python -m tensor_train_ing_b200.kernel_bench profile CASE         three launches of one case (for ncu -k/-c)
+
+Cases (shapes of one 1B micro-batch, 8 x 2048 tokens, unless noted): gemm_qkv, gemm_dx, gemm_dw,
+bilinear, bilinear_grad, attn_fwd, attn_bwd, attn_case (B=2 for profiling), rmsnorm_fwd,
+rmsnorm_bwd, ce_fwd, ce_bwd.  Every input is larger than the 126 MB L2 or is flushed: ``time``
+writes a 256 MB buffer between timed launches.  ``TTB_GEMM_PAIR=0`` selects the one-CTA GEMM.
+The attention timings are the measurements the reference's kernel tuner makes for its Triton
+configurations (reference tnlm/kernels/tune.py:20-62); the tile shapes here are fixed per kernel.
+"""
+from __future__ import annotations
+
+import json
+import sys
+
+import torch
+
+B, T, H, DK, D, DMLP, V = 8, 2048, 16, 128, 2048, 8192, 50304
+N = B * T
+
+
+def _lib():
+    from .ops._ext import lib
+    return lib()
+
+
+class _Case:
+    def __init__(self, fn, flops=0.0, bytes_=0.0):
+        self.fn, self.flops, self.bytes = fn, flops, bytes_
+
+
+def _attn_inputs(b=B):
+    from .ops import fused
+    from .ops.block import rope_context
+    n = b * T
+    docs = torch.zeros(b, T, dtype=torch.long, device="cuda")
+    tables = fused.attention_tables(docs)
+    rs = torch.ones(n, device="cuda")
+    qkv = (torch.randn(n, 5 * H * DK, device="cuda") * 0.5).bfloat16()
+    par = torch.zeros(H, 4, device="cuda")
+    cols = [0, H * DK, 2 * H * DK, 3 * H * DK, 4 * H * DK]
+    dout = torch.randn(n, H * DK, device="cuda").bfloat16()
+    rope = rope_context(tables["pos32"], T, DK, 10000.0)
+    return tables, rs, qkv, par, cols, dout, rope
+
+
+def build(name: str) -> _Case:
+    C = _lib()
+    unit = B * H * (T * T / 2) * DK * 2  # one causal T x T x dk GEMM-equivalent
+    if name in ("gemm_qkv", "gemm_dx", "gemm_dw"):
+        if name == "gemm_qkv":
+            a = torch.randn(N, D, device="cuda").bfloat16()
+            b = torch.randn(5 * H * DK, D, device="cuda").bfloat16().t()
+            out = torch.empty(N, 5 * H * DK, device="cuda", dtype=torch.bfloat16)
+            return _Case(lambda: C.mm(a, b, out), 2.0 * N * D * 5 * H * DK)
+        if name == "gemm_dx":
+            a = torch.randn(N, DMLP, device="cuda").bfloat16()
+            b = torch.randn(DMLP, D, device="cuda").bfloat16()
+            out = torch.empty(N, D, device="cuda")
+            return _Case(lambda: C.mm(a, b, out), 2.0 * N * DMLP * D)
+        a = torch.randn(N, DMLP, device="cuda").bfloat16().t()
+        b = torch.randn(N, D, device="cuda").bfloat16()
+        out = torch.zeros(DMLP, D, device="cuda")
+        return _Case(lambda: C.mm(a, b, out, out, 1.0, 1.0), 2.0 * N * DMLP * D)
+    if name in ("bilinear", "bilinear_grad"):
+        x = torch.randn(N, D, device="cuda").bfloat16()
+        wl = torch.randn(DMLP, D, device="cuda").bfloat16()
+        wr = torch.randn(DMLP, D, device="cuda").bfloat16()
+        h = torch.empty(N, DMLP, device="cuda", dtype=torch.bfloat16)
+        l, r = torch.empty_like(h), torch.empty_like(h)
+        if name == "bilinear":
+            return _Case(lambda: C.bilinear(x, wl, wr, None, None, 0, h, l, r), 4.0 * N * D * DMLP)
+        C.bilinear(x, wl, wr, None, None, 0, h, l, r)
+        wd = torch.randn(D, DMLP, device="cuda").bfloat16()
+        dy = torch.randn(N, D, device="cuda").bfloat16()
+        dl, dr = torch.empty_like(h), torch.empty_like(h)
+        return _Case(lambda: C.bilinear_grad(dy, wd, l, r, dl, dr, 0), 2.0 * N * D * DMLP)
+    if name in ("attn_fwd", "attn_bwd", "attn_case"):
+        b = 2 if name == "attn_case" else B
+        tables, rs, qkv, par, cols, dout, rope = _attn_inputs(b)
+        u = unit * b / B
+        fwd = lambda: C.poly_fwd(0, DK, DK, qkv, cols, tables["pos32"], tables["doc32"], rs, par, b, T, H)  # noqa: E731
+        bwd = lambda: C.poly_bwd(0, DK, DK, qkv, cols, dout, tables["pos32"], tables["doc32"],  # noqa: E731
+                                 tables["doc_end32"], rs, par, b, T, H, rope["cos"], rope["sin"])
+        if name == "attn_fwd":
+            return _Case(fwd, 3 * u)
+        if name == "attn_bwd":
+            return _Case(bwd, 11 * u)
+        return _Case(lambda: (fwd(), bwd()), 14 * u)
+    if name in ("rmsnorm_fwd", "rmsnorm_bwd"):
+        x = torch.randn(N, D, device="cuda")
+        w = torch.ones(D, device="cuda")
+        if name == "rmsnorm_fwd":
+            return _Case(lambda: C.rmsnorm_fwd(x, w, 1, 1e-6), 0, N * D * (4 + 2))
+        y, rstd = C.rmsnorm_fwd(x, w, 1, 1e-6)
+        dres = torch.zeros_like(x)
+        g16 = torch.empty(N, D, device="cuda", dtype=torch.bfloat16)
+        return _Case(lambda: C.rmsnorm_bwd(y, x, w, rstd, dres, True, 1, g16, 1.0), 0, N * D * (4 + 2 + 8 + 2))
+    if name in ("ce_fwd", "ce_bwd"):
+        x = torch.randn(N // 2, D, device="cuda").bfloat16()
+        w = (torch.randn(V, D, device="cuda") * 0.02).bfloat16()
+        t = torch.randint(0, 50257, (N // 2,), device="cuda")
+        fl = 2.0 * (N // 2) * D * V
+        if name == "ce_fwd":
+            return _Case(lambda: C.ce_fwd(x, w, 50257, 1.0, t), fl)
+        _, lse = C.ce_fwd(x, w, 50257, 1.0, t)
+        g = torch.ones(1, device="cuda")
+        dl = torch.empty(N // 2, V, device="cuda", dtype=torch.bfloat16)
+        return _Case(lambda: C.ce_bwd_logits(x, w, 50257, 1.0, t, lse, g, dl), fl)
+    raise KeyError(name)
+
+
+CASES = ["gemm_qkv", "gemm_dx", "gemm_dw", "bilinear", "bilinear_grad", "attn_fwd", "attn_bwd", "rmsnorm_fwd",
+         "rmsnorm_bwd", "ce_fwd", "ce_bwd"]
+
+
+def time_case(name: str, reps: int = 10) -> dict:
+    case = build(name)
+    flush = torch.empty(64 << 20, device="cuda")  # 256 MB, twice the L2
+    for _ in range(3):
+        case.fn()
+    torch.cuda.synchronize()
+    total = 0.0
+    for _ in range(reps):
+        flush.zero_()
+        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s.record()
+        case.fn()
+        e.record()
+        torch.cuda.synchronize()
+        total += s.elapsed_time(e)
+    us = total / reps * 1e3
+    from .ops._ext import check_status
+    check_status()
+    out = {"case": name, "us": round(us, 1)}
+    if case.flops:
+        out["TFLOPs"] = round(case.flops / us / 1e6, 1)
+    if case.bytes:
+        out["GBps"] = round(case.bytes / us / 1e3, 1)
+    return out
+
+
+def profile_case(name: str):
+    case = build(name)
+    for _ in range(3):
+        case.fn()
+    torch.cuda.synchronize()
+    from .ops._ext import check_status
+    check_status()
+    print(json.dumps({"case": name, "profiled": True}))
+
+
+def main(argv=None):
+    argv = list(sys.argv[1:] if argv is None else argv)
+    mode = argv[0] if argv else "time"
+    names = argv[1:] or CASES
+    if mode == "profile":
+        for n in names:
+            profile_case(n)
+        return
+    for n in names:
+        print(json.dumps(time_case(n)), flush=True)
+
+
+if __name__ == "__main__":
+    main()
