@@ -252,7 +252,7 @@ __global__ void __launch_bounds__(256) rmsnorm_fwd_warp_kernel(const float* __re
 
 // Two passes over the row (the second re-reads x and dy, which are still in L1) keep the register
 // footprint at one row of partial weight gradients, so several CTAs stay resident per SM.
-template <int CH, bool GROUPED, typename TDY>
+template <int CH, bool GROUPED, typename TDY, bool WITH_DW>
 __global__ void __launch_bounds__(256) rmsnorm_bwd_warp_kernel(const TDY* __restrict__ dy, const float* __restrict__ x,
                                                               const float* __restrict__ w,
                                                               const float* __restrict__ rstd, float* __restrict__ dres,
@@ -295,7 +295,7 @@ __global__ void __launch_bounds__(256) rmsnorm_bwd_warp_kernel(const TDY* __rest
 #pragma unroll
         for (int k = 0; k < 4; ++k) {
           const float xh = xv[k] * r;
-          dwl[c][k] += dv[k] * xh;
+          if (WITH_DW) dwl[c][k] += dv[k] * xh;
           sacc += dv[k] * wv[k] * xh;
         }
 #pragma unroll
@@ -342,6 +342,7 @@ __global__ void __launch_bounds__(256) rmsnorm_bwd_warp_kernel(const TDY* __rest
       }
     }
   }
+  if (!WITH_DW) return;
   // deterministic CTA reduction: warps add their partials into shared memory in warp order
   for (int ww = 0; ww < nw; ++ww) {
     __syncthreads();
@@ -360,13 +361,52 @@ __global__ void __launch_bounds__(256) rmsnorm_bwd_warp_kernel(const TDY* __rest
   for (int j = threadIdx.x; j < d; j += blockDim.x) dw_part[static_cast<long long>(blockIdx.x) * d + j] = acc[j];
 }
 
-// out[j] (+)= sum_p part[p][j]   (fixed order over p: deterministic)
-__global__ void colsum_kernel(const float* __restrict__ part, int P, int d, float* __restrict__ out, int accumulate) {
-  const int j = blockIdx.x * blockDim.x + threadIdx.x;
-  if (j >= d) return;
+// out[j] (+)= sum_p part[p][j].  Block = 32 columns x 8 row groups: warp g sums rows p = g, g+8, ...
+// in order, then warp 0 adds the 8 group sums in order (a fixed tree: deterministic).
+__global__ void __launch_bounds__(256) colsum_kernel(const float* __restrict__ part, int P, int d,
+                                                     float* __restrict__ out, int accumulate) {
+  __shared__ float red[8][33];
+  const int lane = threadIdx.x % 32, g = threadIdx.x / 32;
+  const int j = blockIdx.x * 32 + lane;
   float s = 0.f;
-  for (int p = 0; p < P; ++p) s += part[static_cast<long long>(p) * d + j];
-  out[j] = accumulate ? out[j] + s : s;
+  if (j < d)
+    for (int p = g; p < P; p += 8) s += part[static_cast<long long>(p) * d + j];
+  red[g][lane] = s;
+  __syncthreads();
+  if (g == 0 && j < d) {
+    float t = 0.f;
+#pragma unroll
+    for (int q = 0; q < 8; ++q) t += red[q][lane];
+    out[j] = accumulate ? out[j] + t : t;
+  }
+}
+
+// Weight-gradient partials of the (group) RMSNorm backward: part[p][j] = sum over the rows of chunk
+// p of dy[row][j] * x[row][j] * rstd[row][group(j)].  Threads own 4 consecutive columns and walk
+// their chunk's rows in order (coalesced rows, deterministic sums).
+template <typename TDY>
+__global__ void __launch_bounds__(256) rmsnorm_dw_kernel(const TDY* __restrict__ dy, const float* __restrict__ x,
+                                                         const float* __restrict__ rstd, float* __restrict__ part,
+                                                         int N, int d, int G, int rows_per_chunk) {
+  const int j = (blockIdx.x * blockDim.x + threadIdx.x) * 4;
+  if (j >= d) return;
+  const int p = blockIdx.y;
+  const int r0 = p * rows_per_chunk;
+  const int r1 = min(N, r0 + rows_per_chunk);
+  const int g = j / (d / G);
+  float a0 = 0.f, a1 = 0.f, a2 = 0.f, a3 = 0.f;
+  for (int row = r0; row < r1; ++row) {
+    const long long base = static_cast<long long>(row) * d + j;
+    float xv[4], dv[4];
+    load4(x + base, xv);
+    load4(dy + base, dv);
+    const float r = rstd[static_cast<long long>(row) * G + g];
+    a0 += dv[0] * xv[0] * r;
+    a1 += dv[1] * xv[1] * r;
+    a2 += dv[2] * xv[2] * r;
+    a3 += dv[3] * xv[3] * r;
+  }
+  *reinterpret_cast<float4*>(part + static_cast<long long>(p) * d + j) = make_float4(a0, a1, a2, a3);
 }
 
 // Rotary embedding on the leading `rope_cols` columns of a [N, ld] bf16 buffer, in place.
@@ -492,14 +532,18 @@ void rmsnorm_bwd_ex(const void* dy, bool dy_f32, const float* x, const float* w,
   const bool done = with_chunks(d, 32, [&](auto ch) {
     constexpr int CH = decltype(ch)::value;
     const size_t smem = static_cast<size_t>(d) * sizeof(float);
+    // dx pass without weight-gradient accumulators (low register use, more warps per SM), then a
+    // coalesced column-reduction pass for dw into the same [grid, d] partials.
+    const int dx_grid = (N + 7) / 8 < 8 * num_sms() ? (N + 7) / 8 : 8 * num_sms();
     auto launch = [&](auto grouped) {
       constexpr bool GR = decltype(grouped)::value;
       if (dy_f32)
-        rmsnorm_bwd_warp_kernel<CH, GR, float><<<grid, 256, smem, stream>>>(static_cast<const float*>(dy), x, w, rstd,
-                                                                            dres, accumulate, dw_part, N, d, G, out16, scale16);
+        rmsnorm_bwd_warp_kernel<CH, GR, float, false><<<dx_grid, 256, 0, stream>>>(
+            static_cast<const float*>(dy), x, w, rstd, dres, accumulate, dw_part, N, d, G, out16, scale16);
       else
-        rmsnorm_bwd_warp_kernel<CH, GR, __nv_bfloat16><<<grid, 256, smem, stream>>>(
+        rmsnorm_bwd_warp_kernel<CH, GR, __nv_bfloat16, false><<<dx_grid, 256, 0, stream>>>(
             static_cast<const __nv_bfloat16*>(dy), x, w, rstd, dres, accumulate, dw_part, N, d, G, out16, scale16);
+      (void)smem;
     };
     if (G == 1)
       launch(std::false_type{});
@@ -516,7 +560,18 @@ void rmsnorm_bwd_ex(const void* dy, bool dy_f32, const float* x, const float* w,
           static_cast<const __nv_bfloat16*>(dy), x, w, rstd, dres, accumulate, dw_part, N, d, G, out16, scale16);
   }
   TTB_CUDA_CHECK(cudaGetLastError());
-  colsum_kernel<<<(d + 255) / 256, 256, 0, stream>>>(dw_part, grid, d, dw, dw_accumulate);
+  if (done) {
+    const int rows_per_chunk = (N + grid - 1) / grid;
+    const dim3 dgrid((d / 4 + 255) / 256, grid);
+    if (dy_f32)
+      rmsnorm_dw_kernel<float><<<dgrid, 256, 0, stream>>>(static_cast<const float*>(dy), x, rstd, dw_part, N, d, G,
+                                                          rows_per_chunk);
+    else
+      rmsnorm_dw_kernel<__nv_bfloat16><<<dgrid, 256, 0, stream>>>(static_cast<const __nv_bfloat16*>(dy), x, rstd,
+                                                                  dw_part, N, d, G, rows_per_chunk);
+    TTB_CUDA_CHECK(cudaGetLastError());
+  }
+  colsum_kernel<<<(d + 31) / 32, 256, 0, stream>>>(dw_part, grid, d, dw, dw_accumulate);
   TTB_CUDA_CHECK(cudaGetLastError());
 }
 
