@@ -48,13 +48,24 @@ ttb::Operand b_operand(const Tensor& b) {
 }
 
 // out = alpha * (a @ b + bias) + beta * c     (out/c: bf16 or fp32, row-major rows)
+// With b2: out = alpha * (a @ cat(b, b2) + bias) + beta * c, the contraction concatenated in one pass.
 void mm(const Tensor& a, const Tensor& b, Tensor& out, const c10::optional<Tensor>& c, double alpha, double beta,
-        const c10::optional<Tensor>& bias) {
+        const c10::optional<Tensor>& bias, const c10::optional<Tensor>& b2) {
   const c10::cuda::CUDAGuard guard(a.device());
   const auto A = a_operand(a);
   const auto B = b_operand(b);
   const int M = a.size(0), K = a.size(1), N = b.size(1);
-  TORCH_CHECK(b.size(0) == K, "inner dimensions differ");
+  ttb::Operand B2{};
+  int k_split = 0;
+  if (b2.has_value()) {
+    B2 = b_operand(*b2);
+    TORCH_CHECK(b2->size(1) == N && b.size(0) + b2->size(0) == K, "concatenated inner dimensions differ");
+    TORCH_CHECK(B2.mn_major == B.mn_major, "concatenated B operands must share a layout");
+    k_split = static_cast<int>(b.size(0));
+    TORCH_CHECK(k_split % 64 == 0, "the first B operand's rows must be a multiple of 64");
+  } else {
+    TORCH_CHECK(b.size(0) == K, "inner dimensions differ");
+  }
   TORCH_CHECK(out.dim() == 2 && out.size(0) == M && out.size(1) == N && out.stride(1) == 1, "bad output");
   TORCH_CHECK(out.scalar_type() == torch::kBFloat16 || out.scalar_type() == torch::kFloat32, "out dtype");
   const void* cp = nullptr;
@@ -74,7 +85,8 @@ void mm(const Tensor& a, const Tensor& b, Tensor& out, const c10::optional<Tenso
     bp = bias->data_ptr<float>();
   }
   ttb::gemm_linear(A, B, M, N, K, out.data_ptr(), out.stride(0), out.scalar_type() == torch::kFloat32, cp, ldc,
-                   c_f32, static_cast<float>(alpha), static_cast<float>(beta), bp, cur_stream());
+                   c_f32, static_cast<float>(alpha), static_cast<float>(beta), bp, cur_stream(),
+                   b2.has_value() ? &B2 : nullptr, k_split);
 }
 
 // qkv = x w^T with the rotary embedding applied to the first rope_cols columns
@@ -133,13 +145,15 @@ void bilinear_grad(const Tensor& dy, const Tensor& wd, const Tensor& l, const Te
   const auto WD = b_operand(wd);
   const int M = dy.size(0), K = dy.size(1), N = wd.size(1);
   TORCH_CHECK(wd.size(0) == K, "wd shape");
+  // l, r share one row stride, dl, dr another (dl, dr may be the two halves of one [M, 2N] buffer)
   for (const Tensor* t : std::initializer_list<const Tensor*>{&l, &r, &dl, &dr}) {
     check_bf16(*t, "bilinear factor");
-    TORCH_CHECK(t->is_contiguous() && t->size(0) == M && t->size(1) == N, "factor shape");
+    TORCH_CHECK(t->dim() == 2 && t->stride(1) == 1 && t->size(0) == M && t->size(1) == N, "factor shape");
     TORCH_CHECK(reinterpret_cast<uintptr_t>(t->data_ptr()) % 16 == 0, "bilinear factors must be 16-byte aligned");
   }
+  TORCH_CHECK(l.stride(0) == r.stride(0) && dl.stride(0) == dr.stride(0), "factor row strides");
   ttb::gemm_bilinear_grad(DY, WD, M, N, K, l.data_ptr(), r.data_ptr(), dl.data_ptr(), dr.data_ptr(), l.stride(0),
-                          static_cast<int>(mode), cur_stream());
+                          dl.stride(0), static_cast<int>(mode), cur_stream());
 }
 
 
@@ -360,7 +374,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.doc() = "tensor_train_ing_b200 sm_100a kernels (tcgen05 / TMEM / TMA)";
   m.def("mm", &mm, "out = alpha*(a@b + bias) + beta*c on the tcgen05 GEMM", py::arg("a"), py::arg("b"),
         py::arg("out"), py::arg("c") = py::none(), py::arg("alpha") = 1.0, py::arg("beta") = 0.0,
-        py::arg("bias") = py::none());
+        py::arg("bias") = py::none(), py::arg("b2") = py::none());
   m.def("bilinear", &bilinear, "dual-B GEMM forming the bilinear hidden layer");
   m.def("bilinear_grad", &bilinear_grad, "dH GEMM fused with the bilinear backward");
   m.def("status", &status, "read and clear the device error word (bounded-wait timeouts)");

@@ -15,18 +15,21 @@ struct Operand {
   bool mn_major;
 };
 
-// D[M,N] = alpha * (A B^T + bias) + beta * C
+// D[M,N] = alpha * (A B^T + bias) + beta * C.  With b2 the contraction is concatenated: B rows
+// [0, k_split) come from b and [k_split, K) from b2 (k_split a multiple of 64), so
+// A[:, :k_split] b^T + A[:, k_split:] b2^T accumulates in one pass.
 void gemm_linear(const Operand& a, const Operand& b, int M, int N, int K, void* D, long long ldd, bool d_f32,
                  const void* C, long long ldc, bool c_f32, float alpha, float beta, const float* bias,
-                 cudaStream_t stream);
+                 cudaStream_t stream, const Operand* b2 = nullptr, int k_split = 0);
 
 // l = x Wl^T (+bl), r = x Wr^T (+br), H = l*r (mode 0) or silu(l)*r (mode 1); all [M, N] bf16 with row stride ld.
 void gemm_bilinear(const Operand& x, const Operand& wl, const Operand& wr, int M, int N, int K, void* H, void* Lo,
                    void* Ro, long long ld, const float* bias_l, const float* bias_r, int mode, cudaStream_t stream);
 
-// dH = dY Wd (B operand = Wd^T view), fused with the bilinear backward: writes dl, dr [M, N] bf16.
+// dH = dY Wd (B operand = Wd^T view), fused with the bilinear backward: writes dl, dr [M, N] bf16
+// (row stride ldo; the saved factors Lin / Rin have row stride ld).
 void gemm_bilinear_grad(const Operand& dy, const Operand& wd, int M, int N, int K, const void* Lin, const void* Rin,
-                        void* dL, void* dR, long long ld, int mode, cudaStream_t stream);
+                        void* dL, void* dR, long long ld, long long ldo, int mode, cudaStream_t stream);
 
 // qkv[M, N] = x W^T (bf16) with the rotary embedding applied to the first rope_cols columns
 // (heads of width dk; cos/sin tables [positions, dk/2] fp32; pos [M] int32).

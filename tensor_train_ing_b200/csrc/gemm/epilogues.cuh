@@ -190,7 +190,8 @@ struct EpiBilinearGrad {
   const __nv_bfloat16* Rin;
   __nv_bfloat16* dL;
   __nv_bfloat16* dR;
-  long long ld;
+  long long ld;   // row stride of Lin / Rin
+  long long ldo;  // row stride of dL / dR
   int mode;
   int M, N;
 
@@ -222,7 +223,7 @@ struct EpiBilinearGrad {
   // global-load latency overlaps useful work instead of stalling every 32-column chunk.
   __device__ __forceinline__ void operator()(uint32_t taddr, int row, int n0, int, int) const {
     constexpr int kChunks = NB / 32;
-    const bool vec_ok = (ld % 8 == 0);
+    const bool vec_ok = (ld % 8 == 0) && (ldo % 8 == 0);
     const bool row_ok = row < M;
     uint32_t lp[16], rp[16];
     auto chunk_meta = [&](int c, long long& off, bool& full, int& nv) {
@@ -231,6 +232,7 @@ struct EpiBilinearGrad {
       full = nv == 32 && vec_ok;
       off = static_cast<long long>(row) * ld + col0;
     };
+    const long long out_base = static_cast<long long>(row) * ldo + n0;
     {
       long long off;
       bool full;
@@ -273,8 +275,8 @@ struct EpiBilinearGrad {
             dr[j] = dh * l;
           }
         }
-        store_row32_bf16(dL + off, full, nv, dl);
-        store_row32_bf16(dR + off, full, nv, dr);
+        store_row32_bf16(dL + out_base + c * 32, full, nv, dl);
+        store_row32_bf16(dR + out_base + c * 32, full, nv, dr);
       }
       if (c + 1 < kChunks) {
 #pragma unroll

@@ -11,14 +11,15 @@ namespace ttb {
 
 void gemm_linear(const Operand& a, const Operand& b, int M, int N, int K, void* D, long long ldd, bool d_f32,
                  const void* C, long long ldc, bool c_f32, float alpha, float beta, const float* bias,
-                 cudaStream_t stream) {
+                 cudaStream_t stream, const Operand* b2, int k_split) {
   TTB_CHECK(M > 0 && N > 0 && K > 0, "empty GEMM");
+  const gemm::Shape shape{M, N, K, status_ptr(), b2 != nullptr ? k_split : 0};
   if (N <= 128) {
     gemm::EpiLinear<128> epi{D, ldd, d_f32, C, ldc, c_f32, alpha, beta, bias, M, N};
-    gemm::dispatch<128, 6, false>(a, b, nullptr, gemm::Shape{M, N, K, status_ptr()}, epi, stream);
+    gemm::dispatch<128, 6, false>(a, b, b2, shape, epi, stream);
   } else {
     gemm::EpiLinear<256> epi{D, ldd, d_f32, C, ldc, c_f32, alpha, beta, bias, M, N};
-    gemm::dispatch<256, 4, false>(a, b, nullptr, gemm::Shape{M, N, K, status_ptr()}, epi, stream);
+    gemm::dispatch<256, 4, false>(a, b, b2, shape, epi, stream);
   }
 }
 
@@ -31,10 +32,11 @@ void gemm_bilinear(const Operand& x, const Operand& wl, const Operand& wr, int M
 }
 
 void gemm_bilinear_grad(const Operand& dy, const Operand& wd, int M, int N, int K, const void* Lin, const void* Rin,
-                        void* dL, void* dR, long long ld, int mode, cudaStream_t stream) {
+                        void* dL, void* dR, long long ld, long long ldo, int mode, cudaStream_t stream) {
   TTB_CHECK(M > 0 && N > 0 && K > 0, "empty GEMM");
   gemm::EpiBilinearGrad<256> epi{static_cast<const __nv_bfloat16*>(Lin), static_cast<const __nv_bfloat16*>(Rin),
-                                 static_cast<__nv_bfloat16*>(dL), static_cast<__nv_bfloat16*>(dR), ld, mode, M, N};
+                                 static_cast<__nv_bfloat16*>(dL), static_cast<__nv_bfloat16*>(dR), ld, ldo, mode,
+                                 M, N};
   gemm::dispatch<256, 4, false>(dy, wd, nullptr, gemm::Shape{M, N, K, status_ptr()}, epi, stream);
 }
 

@@ -59,6 +59,11 @@ inline void launch_pair(const CUtensorMap& ta, const CUtensorMap& tb, const CUte
 template <int BN, int STAGES, bool DUAL, class Epi>
 inline void dispatch(const Operand& a, const Operand& b, const Operand* b2, Shape s, const Epi& epi,
                      cudaStream_t stream) {
+  // contraction extents of the B operands: all of K, or the two parts of a K concatenation
+  TTB_CHECK(s.k_split == 0 || (!DUAL && b2 != nullptr && s.k_split % BK == 0 && s.k_split < s.K),
+            "K concatenation needs a second B operand and a split on a k-block boundary");
+  const int k1 = s.k_split > 0 ? s.k_split : s.K;
+  const int k2 = s.k_split > 0 ? s.K - s.k_split : s.K;
   if constexpr (BN == 256) {
     if (pair_enabled() && s.M >= kPairBM) {
       using L = PairLayout<kPairStages, DUAL>;
@@ -66,12 +71,12 @@ inline void dispatch(const Operand& a, const Operand& b, const Operand* b2, Shap
       const CUtensorMap ta = a.mn_major
                                  ? make_tmap_2d(a.ptr, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, s.M, s.K, a.ld, 64, BK)
                                  : make_tmap_2d(a.ptr, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, s.K, s.M, a.ld, BK, kPairHalf);
-      auto bmap = [&](const Operand& o) {
-        return o.mn_major ? make_tmap_2d(o.ptr, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, s.N, s.K, o.ld, 64, BK)
-                          : make_tmap_2d(o.ptr, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, s.K, s.N, o.ld, BK, L::kBCols);
+      auto bmap = [&](const Operand& o, int kx) {
+        return o.mn_major ? make_tmap_2d(o.ptr, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, s.N, kx, o.ld, 64, BK)
+                          : make_tmap_2d(o.ptr, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, kx, s.N, o.ld, BK, L::kBCols);
       };
-      const CUtensorMap tb = bmap(b);
-      const CUtensorMap tb2 = b2 != nullptr ? bmap(*b2) : tb;
+      const CUtensorMap tb = bmap(b, k1);
+      const CUtensorMap tb2 = b2 != nullptr ? bmap(*b2, k2) : tb;
       TTB_CHECK(b2 == nullptr || b2->mn_major == b.mn_major, "dual GEMM operands must share a layout");
       if (a.mn_major) {
         if (b.mn_major) return launch_pair<Epi, true, true, DUAL>(ta, tb, tb2, s, epi, stream);
@@ -86,12 +91,12 @@ inline void dispatch(const Operand& a, const Operand& b, const Operand* b2, Shap
   const CUtensorMap ta = a.mn_major
                              ? make_tmap_2d(a.ptr, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, s.M, s.K, a.ld, 64, BK)
                              : make_tmap_2d(a.ptr, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, s.K, s.M, a.ld, BK, BM);
-  auto bmap = [&](const Operand& o) {
-    return o.mn_major ? make_tmap_2d(o.ptr, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, s.N, s.K, o.ld, 64, BK)
-                      : make_tmap_2d(o.ptr, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, s.K, s.N, o.ld, BK, NB);
+  auto bmap = [&](const Operand& o, int kx) {
+    return o.mn_major ? make_tmap_2d(o.ptr, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, s.N, kx, o.ld, 64, BK)
+                      : make_tmap_2d(o.ptr, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, kx, s.N, o.ld, BK, NB);
   };
-  const CUtensorMap tb = bmap(b);
-  const CUtensorMap tb2 = b2 != nullptr ? bmap(*b2) : tb;
+  const CUtensorMap tb = bmap(b, k1);
+  const CUtensorMap tb2 = b2 != nullptr ? bmap(*b2, k2) : tb;
   TTB_CHECK(b2 == nullptr || b2->mn_major == b.mn_major, "dual GEMM operands must share a layout");
   if (a.mn_major) {
     if (b.mn_major)

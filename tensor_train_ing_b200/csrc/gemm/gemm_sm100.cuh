@@ -30,7 +30,22 @@ constexpr int kGroupM = 8;        // tile raster: groups of kGroupM row-tiles sw
 struct Shape {
   int M, N, K;
   uint32_t* status;  // device error word (bounded-wait timeouts)
+  // K concatenation (non-DUAL only): when k_split > 0 the contraction runs over two B operands,
+  // B rows [0, k_split) from tmB and [k_split, K) from tmB2 (a multiple of BK, so every k-block
+  // lies in one of them); A is one [M, K] operand.
+  int k_split;
 };
+
+// Tensor map and k coordinate of B for the k-block starting at k0.
+__device__ __forceinline__ const CUtensorMap* b_source(const CUtensorMap* b1, const CUtensorMap* b2, int k_split,
+                                                       int k0, int& kb) {
+  if (k_split > 0 && k0 >= k_split) {
+    kb = k0 - k_split;
+    return b2;
+  }
+  kb = k0;
+  return b1;
+}
 
 template <int BN, int STAGES, bool DUAL>
 struct Layout {
@@ -92,7 +107,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (warp == 0 && lane == 0) {
     prefetch_tmap(&tmA);
     prefetch_tmap(&tmB);
-    if (DUAL) prefetch_tmap(&tmB2);
+    if (DUAL || s.k_split > 0) prefetch_tmap(&tmB2);
   }
   if (warp == 1) {
     tmem_alloc(tmem_holder, L::kTmemCols);
@@ -132,9 +147,11 @@ __global__ void __launch_bounds__(kThreads, 1)
           } else {
             tma_load_2d(sa, &tmA, &full[stage], k0, m0);
           }
+          int kB;
+          const CUtensorMap* mB = b_source(&tmB, &tmB2, DUAL ? 0 : s.k_split, k0, kB);
           if (B_MN) {
 #pragma unroll
-            for (int i = 0; i < NB / 64; ++i) tma_load_2d(sb + i * 64 * BK * 2, &tmB, &full[stage], n0 + 64 * i, k0);
+            for (int i = 0; i < NB / 64; ++i) tma_load_2d(sb + i * 64 * BK * 2, mB, &full[stage], n0 + 64 * i, kB);
             if (DUAL) {
 #pragma unroll
               for (int i = 0; i < NB / 64; ++i)
@@ -145,7 +162,7 @@ __global__ void __launch_bounds__(kThreads, 1)
               tma_load_2d(sb, &tmB, &full[stage], k0, n0);
               tma_load_2d(sb + L::kBBytes, &tmB2, &full[stage], k0, n0);
             } else {
-              tma_load_2d(sb, &tmB, &full[stage], k0, n0);
+              tma_load_2d(sb, mB, &full[stage], kB, n0);
             }
           }
           if (++stage == STAGES) {
@@ -315,7 +332,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
   if (warp == 0 && lane == 0) {
     prefetch_tmap(&tmA);
     prefetch_tmap(&tmB);
-    if (DUAL) prefetch_tmap(&tmB2);
+    if (DUAL || s.k_split > 0) prefetch_tmap(&tmB2);
   }
   if (warp == 1) {
     tmem_alloc_pair(tmem_holder, L::kTmemCols);
@@ -354,14 +371,16 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
           } else {
             tma_load_2d_pair(sa, &tmA, bar, k0, m0);
           }
+          int kB;
+          const CUtensorMap* mB = b_source(&tmB, &tmB2, DUAL ? 0 : s.k_split, k0, kB);
           if (B_MN) {
 #pragma unroll
             for (int i = 0; i < L::kBCols / 64; ++i) {
-              tma_load_2d_pair(sb + i * 64 * BK * 2, &tmB, bar, n0 + 64 * i, k0);
+              tma_load_2d_pair(sb + i * 64 * BK * 2, mB, bar, n0 + 64 * i, kB);
               if (DUAL) tma_load_2d_pair(sb + L::kBBytes + i * 64 * BK * 2, &tmB2, bar, n0 + 64 * i, k0);
             }
           } else {
-            tma_load_2d_pair(sb, &tmB, bar, k0, n0);
+            tma_load_2d_pair(sb, mB, bar, kB, n0);
             if (DUAL) tma_load_2d_pair(sb + L::kBBytes, &tmB2, bar, k0, n0);
           }
           ++loaded;

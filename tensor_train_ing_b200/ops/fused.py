@@ -12,8 +12,9 @@ import torch
 from ._ext import lib
 
 
-def _mm(a, b, out, c=None, alpha=1.0, beta=0.0, bias=None):
-    lib().mm(a, b, out, c, float(alpha), float(beta), bias)
+def _mm(a, b, out, c=None, alpha=1.0, beta=0.0, bias=None, b2=None):
+    """out = alpha * (a @ b + bias) + beta * c; with ``b2``, a @ cat(b, b2) in one pass."""
+    lib().mm(a, b, out, c, float(alpha), float(beta), bias, b2)
     return out
 
 
@@ -147,7 +148,7 @@ class QKVRopeFn(torch.autograd.Function):
             raise RuntimeError("QKVRopeFn expects the gradient produced by PolyAttentionFn (rotary already undone)")
         g = dqkv.contiguous()
         w16 = ctx.group.bf16()
-        dx = torch.empty(x.shape[0], x.shape[1], device=x.device, dtype=torch.float32)
+        dx = torch.empty_like(x)  # bf16 like the input: no cast inserted by autograd
         _mm(g, w16, dx)
         grads = ctx.group.sink_grad(lambda out, beta: _mm(g.t(), x, out, c=out, beta=beta))
         return (dx, None, None, None, None, *grads)
@@ -246,13 +247,24 @@ class BilinearMLPFn(torch.autograd.Function):
         g_l, g_r, g_d = ctx.groups
         g = _take_bf16(dout, ctx.alpha)
         wd = g_d.bf16()
-        dl = torch.empty_like(l)
-        dr = torch.empty_like(r)
+        # dl and dr side by side in one [N, 2F] buffer, so that dx = [dl | dr] @ [L; R] is one
+        # GEMM over the concatenated contraction (F a multiple of the 64-wide k-block), written in
+        # bf16 like the input
+        F_ = l.shape[1]
+        concat = F_ % 64 == 0
+        if concat:
+            dlr = torch.empty(l.shape[0], 2 * F_, device=l.device, dtype=l.dtype)
+            dl, dr = dlr[:, :F_], dlr[:, F_:]
+        else:
+            dl, dr = torch.empty_like(l), torch.empty_like(r)
         lib().bilinear_grad(g, wd, l, r, dl, dr, int(ctx.mode))
         grads_d = g_d.sink_grad(lambda out, beta: _mm(g.t(), h, out, c=out, beta=beta))
-        dx = torch.empty(x.shape[0], x.shape[1], device=x.device, dtype=torch.float32)
-        _mm(dl, g_l.bf16(), dx)
-        _mm(dr, g_r.bf16(), dx, c=dx, beta=1.0)
+        dx = torch.empty_like(x)
+        if concat:
+            _mm(dlr, g_l.bf16(), dx, b2=g_r.bf16())
+        else:
+            part = _mm(dl, g_l.bf16(), torch.empty(dx.shape, device=dx.device, dtype=torch.float32))
+            _mm(dr, g_r.bf16(), dx, c=part, beta=1.0)
         grads_l = g_l.sink_grad(lambda out, beta: _mm(dl.t(), x, out, c=out, beta=beta))
         grads_r = g_r.sink_grad(lambda out, beta: _mm(dr.t(), x, out, c=out, beta=beta))
         dres = dout if ctx.has_res else None

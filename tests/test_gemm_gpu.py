@@ -79,3 +79,37 @@ def test_bilinear_and_grad():
     assert _rel(dl, dh * ro.float()) < 2e-2 and _rel(dr, dh * lo.float()) < 2e-2
     torch.cuda.synchronize()
     assert _C().status() == 0
+
+
+@pytest.mark.parametrize("M,N,K1,K2", [(512, 256, 128, 192), (4096, 2048, 1024, 1024), (300, 200, 64, 96)])
+@pytest.mark.parametrize("b_t", [False, True])
+def test_mm_concatenated_contraction(M, N, K1, K2, b_t):
+    """a @ cat(b1, b2) in one pass (the bilinear MLP's dx = [dl | dr] @ [L; R])."""
+    torch.manual_seed(3)
+    a = torch.randn(M, K1 + K2, device="cuda").bfloat16()
+    mk = (lambda k: torch.randn(N, k, device="cuda").bfloat16().t()) if b_t else \
+        (lambda k: torch.randn(k, N, device="cuda").bfloat16())
+    b1, b2 = mk(K1), mk(K2)
+    out = torch.empty(M, N, device="cuda", dtype=torch.bfloat16)
+    _C().mm(a, b1, out, b2=b2)
+    torch.cuda.synchronize()
+    assert _C().status() == 0
+    assert _rel(out, _ref(a, torch.cat([b1, b2], 0))) < 1e-2
+    with pytest.raises(RuntimeError):  # the split must fall on a 64-wide k-block
+        _C().mm(a[:, 1:], b1[1:], out, b2=b2)
+
+
+def test_bilinear_grad_strided_outputs():
+    """dl, dr written as the two halves of one [M, 2N] buffer."""
+    torch.manual_seed(4)
+    M, N, D = 640, 384, 256
+    lo = torch.randn(M, N, device="cuda").bfloat16()
+    ro = torch.randn(M, N, device="cuda").bfloat16()
+    wd = (torch.randn(D, N, device="cuda") / N ** 0.5).bfloat16()
+    dy = torch.randn(M, D, device="cuda").bfloat16()
+    dlr = torch.full((M, 2 * N), float("nan"), device="cuda", dtype=torch.bfloat16)
+    _C().bilinear_grad(dy, wd, lo, ro, dlr[:, :N], dlr[:, N:], 0)
+    dh = dy.float() @ wd.float()
+    assert _rel(dlr[:, :N], dh * ro.float()) < 2e-2 and _rel(dlr[:, N:], dh * lo.float()) < 2e-2
+    torch.cuda.synchronize()
+    assert _C().status() == 0
