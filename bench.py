@@ -37,6 +37,7 @@ PRESETS = {
     # name: (layers, d_model, heads, head_dim, d_mlp, T, global_batch, micro_batch, act_ckpt, loss_chunk)
     "1b": (24, 2048, 16, 128, 8192, 2048, 512, 8, False, 8192),
     "7b": (32, 4096, 32, 128, 16384, 4096, 256, 4, True, 8192),
+    "32b": (48, 6144, 48, 128, 24576, 4096, 256, 2, True, 8192),
     "100m": (12, 768, 12, 64, 3072, 2048, 256, 16, False, 8192),
     "tiny": (4, 256, 4, 64, 1024, 256, 8, 8, False, 0),
 }
@@ -53,6 +54,8 @@ def parse():
     p.add_argument("--micro-batch", type=int, default=None)
     p.add_argument("--optimizer", default="muon", choices=["muon", "adamw"])
     p.add_argument("--no-e2e", action="store_true")
+    p.add_argument("--shard-params", default="auto", choices=["auto", "on", "off"],
+                   help="fp32 weights/grads/optimizer state only on owner ranks (auto: when replicated does not fit)")
     return p.parse_args()
 
 
@@ -160,7 +163,13 @@ def build_ours(args, device, world):
     mk, T, gb, mb = model_kwargs(args.config)
     cfg = Config.from_dict({"model": mk, "train": train_kwargs(args.optimizer)})
     torch.manual_seed(101)
-    eng = TrainEngine(cfg, device=device, micro_batch=args.micro_batch or mb)
+    shard = {"auto": None, "on": True, "off": False}[args.shard_params]
+    if shard is None:
+        from tensor_train_ing_b200.models.shapes import needs_parameter_sharding
+        shard = needs_parameter_sharding(cfg.model, world, device)
+    # a sharded model is drawn on the device (the serial CPU initialisation of 33B weights takes minutes)
+    eng = TrainEngine(cfg, device=device, micro_batch=args.micro_batch or mb, shard_params=shard,
+                      init="device" if shard else "serial")
     if not eng.fused:
         raise SystemExit("the fused sm_100a path does not cover this configuration")
     n_params = sum(p.numel() for p in eng.model.parameters())
@@ -316,7 +325,8 @@ def main():
             "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
             "data": "synthetic uniform token ids (seed 0), next-token targets; random init weights",
             "config": {"model": f"tnlm-{args.config}", "global_batch": gb, "seq_len": T,
-                       "parallelism": f"dp{world}", "tokens_per_step": tokens_per_step,
+                       "parallelism": f"dp{world}" + ("-param-sharded" if eng is not None and eng.shard_params
+                                                       else ""), "tokens_per_step": tokens_per_step,
                        "optimizer": f"{args.optimizer} (hidden) + adamw", "micro_batch": args.micro_batch
                        or PRESETS[args.config][7], "params": n_params,
                        "l2": "per-step working set >> 126 MB L2; no flush needed"},

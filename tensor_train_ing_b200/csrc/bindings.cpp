@@ -340,9 +340,9 @@ ttb::PeerPtrs peer_ptrs(const std::vector<int64_t>& ptrs) {
   return p;
 }
 
-void peer_barrier(const std::vector<int64_t>& pads, int64_t rank, int64_t epoch) {
+void peer_barrier(const std::vector<int64_t>& pads, int64_t rank, int64_t epoch, int64_t limit_cycles) {
   ttb::peer_barrier(peer_ptrs(pads), static_cast<int>(pads.size()), static_cast<int>(rank),
-                    static_cast<uint32_t>(epoch), cur_stream());
+                    static_cast<uint32_t>(epoch), limit_cycles, cur_stream());
 }
 
 // Pull-based reduce-scatter of the flat fp32 buffers: out (this rank's region of its own buffer)
@@ -352,8 +352,16 @@ Tensor rs_reduce_sq(const std::vector<int64_t>& bufs, int64_t off, Tensor& out) 
   TORCH_CHECK(reinterpret_cast<uintptr_t>(out.data_ptr()) % 16 == 0, "out: 16-byte aligned");
   auto partial = torch::empty({ttb::rs_reduce_blocks()}, out.options().dtype(torch::kFloat64));
   ttb::rs_reduce_sq(peer_ptrs(bufs), static_cast<int>(bufs.size()), off, out.numel(), out.data_ptr<float>(),
-                    partial.data_ptr<double>(), cur_stream());
+                    partial.data_ptr<double>(), false, 0, cur_stream());
   return partial;
+}
+
+// out += sum over ranks of bufs[q][off : off + out.numel()] (rank order, deterministic).
+void rs_accumulate(const std::vector<int64_t>& bufs, int64_t off, Tensor& out, int64_t blocks) {
+  TORCH_CHECK(out.scalar_type() == torch::kFloat32 && out.is_contiguous(), "out: contiguous fp32");
+  TORCH_CHECK(reinterpret_cast<uintptr_t>(out.data_ptr()) % 16 == 0, "out: 16-byte aligned");
+  ttb::rs_reduce_sq(peer_ptrs(bufs), static_cast<int>(bufs.size()), off, out.numel(), out.data_ptr<float>(),
+                    nullptr, true, static_cast<int>(blocks), cur_stream());
 }
 
 // segs: int64 [nseg, 4] rows (src, dst32, dst16, n) of device addresses (0 = absent), on the device.
@@ -378,7 +386,10 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("bilinear", &bilinear, "dual-B GEMM forming the bilinear hidden layer");
   m.def("bilinear_grad", &bilinear_grad, "dH GEMM fused with the bilinear backward");
   m.def("status", &status, "read and clear the device error word (bounded-wait timeouts)");
-  m.def("peer_barrier", &peer_barrier, "cross-GPU barrier through symmetric signal pads (bounded wait)");
+  m.def("peer_barrier", &peer_barrier, "cross-GPU barrier through symmetric signal pads (bounded wait)",
+        py::arg("pads"), py::arg("rank"), py::arg("epoch"), py::arg("limit_cycles") = 2000000000LL);
+  m.def("rs_accumulate", &rs_accumulate, "pull reduction over peer buffers added into a local accumulator",
+        py::arg("bufs"), py::arg("off"), py::arg("out"), py::arg("blocks") = 0);
   m.def("rs_reduce_sq", &rs_reduce_sq, "pull reduce-scatter over peer buffers with fused sum-of-squares partials");
   m.def("ag_pull_cast", &ag_pull_cast, "pull all-gather over peer buffers with fused bf16 weight-cache writes");
   m.def("rmsnorm_fwd", &rmsnorm_fwd, "(group) RMSNorm: fp32 x -> bf16 y, fp32 rstd");

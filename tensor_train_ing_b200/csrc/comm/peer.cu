@@ -6,7 +6,9 @@
 //   rs_reduce_sq     reduce-scatter of the flat fp32 gradient buffer by pulling: rank r sums its own
 //                    region of every rank's buffer in rank order (deterministic) into its own buffer
 //                    and, in the same pass, emits per-CTA partial sums of squares for the global
-//                    gradient-norm clip.
+//                    gradient-norm clip.  With ``accumulate`` the sum is added to the output instead
+//                    (the per-layer gradient reduction of parameter-sharded training, which adds
+//                    every micro-batch's summed layer gradient into the owner's accumulator).
 //   ag_pull_cast     all-gather of the flat fp32 parameter buffer by pulling each owner's region, fused
 //                    with the bf16 operand caches of the GEMM weights (one pass writes both).
 //
@@ -21,7 +23,6 @@ namespace ttb {
 namespace {
 
 constexpr int kThreads = 256;
-constexpr long long kSpinLimit = 2000000000LL;  // clock cycles (about a second)
 
 __device__ __forceinline__ void st_release_sys(uint32_t* p, uint32_t v) {
   asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
@@ -33,7 +34,8 @@ __device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
 }
 
 // One block; thread q signals peer q and then waits for peer q's signal (epochs only grow).
-__global__ void peer_barrier_kernel(PeerPtrs pads, int world, int rank, uint32_t epoch, uint32_t* status) {
+__global__ void peer_barrier_kernel(PeerPtrs pads, int world, int rank, uint32_t epoch, long long limit,
+                                    uint32_t* status) {
   const int q = threadIdx.x;
   if (q < world) {
     __threadfence_system();  // this GPU's earlier writes (previous kernels) before the signal
@@ -42,7 +44,7 @@ __global__ void peer_barrier_kernel(PeerPtrs pads, int world, int rank, uint32_t
     const uint32_t* mine = reinterpret_cast<const uint32_t*>(pads.p[rank]) + q;
     const long long t0 = clock64();
     while (static_cast<int32_t>(ld_acquire_sys(mine) - epoch) < 0) {
-      if (clock64() - t0 > kSpinLimit) {
+      if (clock64() - t0 > limit) {
         atomicCAS(status, 0u, static_cast<uint32_t>(kErrTimeoutPeer));
         break;
       }
@@ -52,10 +54,11 @@ __global__ void peer_barrier_kernel(PeerPtrs pads, int world, int rank, uint32_t
   __syncthreads();
 }
 
-// out[i] = sum_q peers[q][off + i] for i < n (float4 granularity; n and off multiples of 4),
-// partial[blockIdx.x] = sum of out[i]^2 over this block's elements (fp32 tree inside the block).
+// out[i] = sum_q peers[q][off + i] (+ out[i] when accumulating) for i < n (float4 granularity; n and
+// off multiples of 4), partial[blockIdx.x] = sum of out[i]^2 over this block's elements (fp32 tree
+// inside the block; skipped when partial is null).
 __global__ void __launch_bounds__(kThreads) rs_reduce_sq_kernel(PeerPtrs peers, int world, long long off, long long n,
-                                                               float* out, double* partial) {
+                                                               float* out, double* partial, int accumulate) {
   __shared__ float red[kThreads / 32];
   float acc = 0.f;
   const long long n4 = n / 4;
@@ -67,6 +70,10 @@ __global__ void __launch_bounds__(kThreads) rs_reduce_sq_kernel(PeerPtrs peers, 
       const float4 v = __ldcg(reinterpret_cast<const float4*>(reinterpret_cast<const float*>(peers.p[q]) + off) + i);
       s.x += v.x; s.y += v.y; s.z += v.z; s.w += v.w;
     }
+    if (accumulate) {
+      const float4 o = reinterpret_cast<const float4*>(out)[i];
+      s.x += o.x; s.y += o.y; s.z += o.z; s.w += o.w;
+    }
     reinterpret_cast<float4*>(out)[i] = s;
     acc += s.x * s.x + s.y * s.y + s.z * s.z + s.w * s.w;
   }
@@ -74,7 +81,7 @@ __global__ void __launch_bounds__(kThreads) rs_reduce_sq_kernel(PeerPtrs peers, 
   for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
   if (threadIdx.x % 32 == 0) red[threadIdx.x / 32] = acc;
   __syncthreads();
-  if (threadIdx.x == 0) {
+  if (threadIdx.x == 0 && partial != nullptr) {
     double t = 0.0;
     for (int w = 0; w < kThreads / 32; ++w) t += red[w];
     partial[blockIdx.x] = t;
@@ -99,19 +106,24 @@ __global__ void __launch_bounds__(kThreads) ag_pull_cast_kernel(const CopySeg* _
 
 }  // namespace
 
-void peer_barrier(const PeerPtrs& pads, int world, int rank, uint32_t epoch, cudaStream_t stream) {
+void peer_barrier(const PeerPtrs& pads, int world, int rank, uint32_t epoch, long long limit_cycles,
+                  cudaStream_t stream) {
   TTB_CHECK(world >= 1 && world <= kMaxPeers && rank >= 0 && rank < world, "peer_barrier: bad world/rank");
-  peer_barrier_kernel<<<1, 32, 0, stream>>>(pads, world, rank, epoch, status_ptr());
+  TTB_CHECK(limit_cycles > 0, "peer_barrier: the wait needs a limit");
+  peer_barrier_kernel<<<1, 32, 0, stream>>>(pads, world, rank, epoch, limit_cycles, status_ptr());
   TTB_CUDA_CHECK(cudaGetLastError());
 }
 
 int rs_reduce_blocks() { return 4 * num_sms(); }
 
 void rs_reduce_sq(const PeerPtrs& peers, int world, long long off, long long n, float* out, double* partial,
-                  cudaStream_t stream) {
+                  bool accumulate, int blocks, cudaStream_t stream) {
   TTB_CHECK(world >= 1 && world <= kMaxPeers, "rs_reduce_sq: bad world");
   TTB_CHECK(n % 4 == 0 && off % 4 == 0, "rs_reduce_sq: region must be float4 aligned");
-  rs_reduce_sq_kernel<<<rs_reduce_blocks(), kThreads, 0, stream>>>(peers, world, off, n, out, partial);
+  TTB_CHECK(partial == nullptr || blocks == 0, "rs_reduce_sq: partial sums need the default grid");
+  if (n == 0) return;
+  const int grid = blocks > 0 && blocks < rs_reduce_blocks() ? blocks : rs_reduce_blocks();
+  rs_reduce_sq_kernel<<<grid, kThreads, 0, stream>>>(peers, world, off, n, out, partial, accumulate ? 1 : 0);
   TTB_CUDA_CHECK(cudaGetLastError());
 }
 

@@ -24,10 +24,15 @@ struct CopySeg {
   long long n;
 };
 
-void peer_barrier(const PeerPtrs& pads, int world, int rank, uint32_t epoch, cudaStream_t stream);
-int rs_reduce_blocks();
-void rs_reduce_sq(const PeerPtrs& peers, int world, long long off, long long n, float* out, double* partial,
+// Every rank's wait gives up after limit_cycles SM clock cycles and sets the timeout status word.
+void peer_barrier(const PeerPtrs& pads, int world, int rank, uint32_t epoch, long long limit_cycles,
                   cudaStream_t stream);
+int rs_reduce_blocks();
+// out[i] (+)= sum over ranks of peers[q][off + i]; partial (nullable) gets per-block sums of squares
+// (one per block of the default grid, rs_reduce_blocks()).  blocks > 0 caps the grid (a pull that
+// runs beside compute kernels on another stream should leave them most of the SMs).
+void rs_reduce_sq(const PeerPtrs& peers, int world, long long off, long long n, float* out, double* partial,
+                  bool accumulate, int blocks, cudaStream_t stream);
 void ag_pull_cast(const CopySeg* segs_device, int nseg, long long max_n, cudaStream_t stream);
 
 }  // namespace ttb

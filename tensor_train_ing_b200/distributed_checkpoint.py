@@ -4,8 +4,9 @@ tnlm/distributed_checkpoint.py:46-483, format ``tnlm-dcp-v1``; this framework wr
 Directory layout (published atomically with a no-replace rename, like the full-state format):
 
 * ``model.pt``        the model state (parameters are replicated between steps; rank 0 writes it);
+                      under parameter sharding only the replicated part;
 * ``rank-XXXXX.pt``   each rank's optimizer state (only the parameters it owns), RNG states and
-                      sampler cursor;
+                      sampler cursor, and under parameter sharding the fp32 masters it owns;
 * ``manifest.json``   format, world size, torch version, backend, the ownership layout, the
                       replicated-buffer digest, config / progress / data identity and the sha256
                       and size of every file.
@@ -74,9 +75,17 @@ def _tensor_digest(items) -> str:
     return h.hexdigest()
 
 
-def _replicated_digest(model) -> str:
+def _replicated_state(model, dp=None) -> dict:
+    """Everything every rank holds identically between steps (all of the model unless its
+    parameters are sharded)."""
+    if dp is not None and getattr(dp, "shard_params", False):
+        return dp.replicated_state()
+    return model.state_dict()
+
+
+def _replicated_digest(model, dp=None) -> str:
     """Digest of everything that must be identical on every rank: parameters and buffers."""
-    return _tensor_digest(model.state_dict().items())
+    return _tensor_digest(_replicated_state(model, dp).items())
 
 
 def _layout(dp, optimizer) -> dict:
@@ -117,14 +126,17 @@ def save_distributed_checkpoint(path, model, optimizer, sampler, dp, *, config, 
                 "config": _plain(config), "progress": _plain(progress), "manifest_hash": manifest_hash,
                 "parent": _plain(parent), "extra": _plain(extra)}
     shared = _agree("checkpoint request", _phase("checkpoint preflight", preflight))
-    digest = _agree("replicated state", _phase("replicated digest", lambda: _replicated_digest(model)))
+    digest = _agree("replicated state", _phase("replicated digest", lambda: _replicated_digest(model, dp)))
+    sharded = bool(getattr(dp, "shard_params", False))
     local = {"rank": rank, "world_size": world, "optimizer": optimizer.state_dict(),
              "optimizer_layout": _local_layout(optimizer),
-             "sampler": sampler.state_dict() if sampler is not None else None, "rng": _rng_state()}
+             "sampler": sampler.state_dict() if sampler is not None else None, "rng": _rng_state(),
+             "owned_params": ({k: v.cpu() for k, v in dp.owned_sharded_state().items()} if sharded else None)}
+    replicated = _replicated_state(model, dp)
 
     def staging():
         if rank == 0:
-            estimate = checkpoint_space_estimate({"local": local, "model": model.state_dict()}) * 2
+            estimate = checkpoint_space_estimate({"local": local, "model": replicated}) * (2 + world * sharded)
             require_checkpoint_space(path.parent, estimate)
             path.parent.mkdir(parents=True, exist_ok=True)
             return tempfile.mkdtemp(prefix=f".{path.name}.tmp-", dir=path.parent)
@@ -143,7 +155,7 @@ def save_distributed_checkpoint(path, model, optimizer, sampler, dp, *, config, 
             out[name] = {"sha256": _digest(stage / name), "bytes": (stage / name).stat().st_size}
             if rank == 0:
                 with (stage / "model.pt").open("wb") as fh:
-                    torch.save({"model": model.state_dict()}, fh)
+                    torch.save({"model": replicated}, fh)
                     fh.flush()
                     os.fsync(fh.fileno())
                 out["model.pt"] = {"sha256": _digest(stage / "model.pt"), "bytes": (stage / "model.pt").stat().st_size}
@@ -230,9 +242,15 @@ def load_distributed_checkpoint(path, model, optimizer, sampler, dp, *, expected
         _require_finite(local["optimizer"], "optimizer")
         if restore_rng:
             _validate_rng(local["rng"])
-        current = model.state_dict()
+        current = _replicated_state(model, dp)
         if current.keys() != state.keys() or any(current[k].shape != state[k].shape for k in current):
             raise ValueError("checkpoint model keys or shapes differ")
+        if getattr(dp, "shard_params", False):
+            owned = dp.owned_sharded_state()
+            mine = local.get("owned_params") or {}
+            if mine.keys() != owned.keys() or any(mine[k].shape != owned[k].shape for k in owned):
+                raise ValueError("this rank's sharded parameters differ from the checkpoint")
+            _require_finite(mine, "sharded parameters")
         if sampler is not None and local["sampler"] is None:
             raise ValueError("checkpoint has no sampler state")
         return state, local
@@ -240,16 +258,20 @@ def load_distributed_checkpoint(path, model, optimizer, sampler, dp, *, expected
 
     def install():
         with torch.no_grad():
-            current = model.state_dict()
+            current = _replicated_state(model, dp)
             for k, v in state.items():
                 current[k].copy_(v)  # in place: parameters stay views of the flat buffers
+            if getattr(dp, "shard_params", False):
+                dp.load_owned_sharded(local["owned_params"])
         optimizer.load_state_dict(local["optimizer"])
         if sampler is not None:
             sampler.load_state_dict(local["sampler"])
         if restore_rng:
             _restore_rng(local["rng"])
     _phase("checkpoint install", install)
-    digest = _replicated_digest(model)
+    if getattr(dp, "shard_params", False):
+        dp.gather_params()  # bf16 caches / compute copies from the restored masters
+    digest = _replicated_digest(model, dp)
     if digest != manifest["replicated_state_sha256"]:
         raise ValueError("restored replicated state digest differs from the manifest")
     out = dict(manifest)
@@ -259,19 +281,21 @@ def load_distributed_checkpoint(path, model, optimizer, sampler, dp, *, expected
 
 
 def export_distributed_weights(path, model, *, config, progress, manifest_hash, parent=None,
-                               max_state_bytes=4_000_000_000) -> dict:
-    """Collectively export the (replicated) model as a full-state checkpoint for serial evaluators.
+                               max_state_bytes=4_000_000_000, dp=None) -> dict:
+    """Collectively export the model as a full-state checkpoint for serial evaluators (with
+    parameter sharding, ``dp`` assembles the owners' masters on rank 0).
 
     Only rank 0 writes; the result has no optimizer or sampler state and does not resume training."""
     from .checkpoint import save_checkpoint
     rank, world = _group()
+    sharded = bool(getattr(dp, "shard_params", False))
 
     def preflight():
         if type(max_state_bytes) is not int or max_state_bytes <= 0:
             raise ValueError("positive integer export state-byte limit required")
         _check_boundary(model)
         state = model.state_dict()
-        _require_finite(state, "model")
+        _require_finite(_replicated_state(model, dp), "model")
         size = sum(v.numel() * v.element_size() for v in state.values())
         if size > max_state_bytes:
             raise ValueError(f"full export needs {size} tensor bytes, exceeds {max_state_bytes}")
@@ -279,12 +303,19 @@ def export_distributed_weights(path, model, *, config, progress, manifest_hash, 
             raise ValueError("export destination already exists")
         return {"path": str(Path(path).resolve()), "state_bytes": size}
     request = _agree("export request", _phase("export preflight", preflight))
-    _agree("export replicated state", _replicated_digest(model))
+    _agree("export replicated state", _replicated_digest(model, dp))
+    full = dp.full_state_dict(dst=0) if sharded else None
 
     def publish():
         if rank:
             return None
-        return save_checkpoint(request["path"], model, None, None, config=config, progress=progress,
+        source = model
+        if sharded:  # a CPU model holding the assembled state
+            with torch.device("meta"):
+                source = type(model)(model.cfg)
+            source.load_state_dict(full, assign=True)
+            _require_finite(full, "model")
+        return save_checkpoint(request["path"], source, None, None, config=config, progress=progress,
                                manifest_hash=manifest_hash, parent=parent,
                                extra={"artifact_kind": "distributed_evaluation_weights", "training_recovery": False,
                                       "source_world_size": world, "persistent_tensor_bytes": request["state_bytes"]})

@@ -34,6 +34,7 @@ from .distributed_checkpoint import (_agree, _phase, export_distributed_weights,
                                      load_distributed_checkpoint, read_distributed_manifest,
                                      save_distributed_checkpoint)
 from .models.model import TensorLM
+from .models.shapes import needs_parameter_sharding
 from .models.normalization import lagged_modules, spectral_step
 from .optim import make_optimizer
 from .optimizer_exposure import update_optimizer_exposure
@@ -148,9 +149,14 @@ def distributed_train_run(cfg, run_dir, *, max_steps, max_seconds, device="cuda"
             if tokenizer.get("test_only") and dev.type != "cpu":
                 raise ValueError("test-only tokenizer manifests are restricted to CPU fixtures")
             seed_all(cfg.train.seed)
-            model = TensorLM(cfg.model).to(dev)
+            shard = needs_parameter_sharding(cfg.model, world, dev)
+            if shard:  # built from the streamed serial initialisation: no rank holds all fp32 weights
+                with torch.device("meta"):
+                    model = TensorLM(cfg.model)
+            else:
+                model = TensorLM(cfg.model).to(dev)
             fused = dev.type == "cuda" and model.fused_path_supported()[0]
-            dp = ShardedDataParallel(model, dev, fused=fused)
+            dp = ShardedDataParallel(model, dev, fused=fused, shard_params=shard)
             optimizer = make_optimizer(model, cfg.train, only=dp.owned_ids())
             # the logical (unsharded) optimizer: never stepped, it carries the full group structure
             # for exposure bookkeeping, which must not depend on which rank owns what
@@ -162,8 +168,8 @@ def distributed_train_run(cfg, run_dir, *, max_steps, max_seconds, device="cuda"
         manifest_hash = hash_manifest(data["manifest"])
         _agree("data identity", manifest_hash)
         _agree("initial replicas", hashlib.sha256(b"".join(
-            p.detach().cpu().contiguous().view(-1).view(torch.uint8).numpy().tobytes()[:4096]
-            for p in model.parameters())).hexdigest())
+            v.detach().cpu().contiguous().view(-1).view(torch.uint8).numpy().tobytes()[:4096]
+            for _, v in sorted(dp.replicated_state().items()))).hexdigest())
         progress = {"steps": 0, "tokens": 0, "scheduler_step": 0, "input_tokens_seen": 0,
                     "discarded_prediction_targets": 0, "world_size": world,
                     "warmup_steps": validate_schedule(cfg.train.schedule, planned_total)}
@@ -306,6 +312,7 @@ def distributed_train_run(cfg, run_dir, *, max_steps, max_seconds, device="cuda"
                             objective = objective + taper.anchor_lambda * anchor * (selected / wanted)
                             extra = float(anchor.detach()) * selected
                         objective.backward()
+                        dp.after_backward()
                         return float(loss.detach()), extra
                     loss_value, anchor_value = _phase("forward/backward", forward_backward)
                 finally:
@@ -343,6 +350,8 @@ def distributed_train_run(cfg, run_dir, *, max_steps, max_seconds, device="cuda"
             clipping = None
             if clip_tau > 0 and progress["steps"] % clip_every == 0:
                 clipping = bounds.clip(clip_tau)
+                if dp.shard_params:
+                    dp.gather_params()  # owners rescaled their masters: refresh every rank's copies
             seconds = max_value(time.monotonic() - step_started)
             elapsed = max_value(time.monotonic() - started)
             record = {"step": progress["steps"], "tokens": progress["tokens"], "prediction_tokens": accumulated,
@@ -375,7 +384,7 @@ def distributed_train_run(cfg, run_dir, *, max_steps, max_seconds, device="cuda"
             export = export_distributed_weights(run_dir / "final-weights", model, config=full_config(cfg),
                                                 progress=progress, manifest_hash=manifest_hash,
                                                 parent={"path": str((run_dir / "final").resolve())},
-                                                max_state_bytes=export_max_state_bytes)
+                                                max_state_bytes=export_max_state_bytes, dp=dp)
         result = {"checkpoint": str((run_dir / "final").resolve()), "checkpoint_manifest": final,
                   "weights_export": export, "progress": progress, "history": history[-1000:],
                   "stop_reason": stop_reason, "world_size": world, "run_id": run_id,

@@ -21,21 +21,38 @@ from .parallel.sharded import ShardedDataParallel
 
 class TrainEngine:
     def __init__(self, cfg: Config, device="cuda", micro_batch: int = 8, model: TensorLM | None = None,
-                 optimizer=None, group=None, grad_clip: float | None = None):
+                 optimizer=None, group=None, grad_clip: float | None = None, shard_params: bool | None = None,
+                 init: str = "serial"):
+        """``shard_params``: keep fp32 weights, gradients and optimizer state only on their owner
+        rank (None: when ``TTB_SHARD_PARAMS=1`` or when the replicated layout would not fit the
+        device; see models.shapes.needs_parameter_sharding).  A sharded engine builds its model
+        itself from the streamed serial initialisation unless ``model`` is given (``init="device"``:
+        the same distributions drawn on the device, for throughput runs)."""
         self.cfg = cfg
         self.device = torch.device(device)
         self.micro_batch = int(micro_batch)
-        self.model = model if model is not None else TensorLM(cfg.model).to(self.device)
-        self.model.train()
         self.group = group
         self.world = dist.get_world_size(group) if dist.is_available() and dist.is_initialized() else 1
+        if shard_params is None:
+            from .models.shapes import needs_parameter_sharding
+            shard_params = needs_parameter_sharding(cfg.model, self.world, self.device)
+        self.shard_params = bool(shard_params)
+        if model is None:
+            if self.shard_params:
+                with torch.device("meta"):
+                    model = TensorLM(cfg.model)
+            else:
+                model = TensorLM(cfg.model).to(self.device)
+        self.model = model
+        self.model.train()
         self.grad_clip = cfg.train.grad_clip if grad_clip is None else grad_clip
         self.fused = self.device.type == "cuda" and self.model.fused_path_supported()[0]
         # flat gradient/parameter buffers: needed by the fused path and by every multi-rank run
-        self.dp = (ShardedDataParallel(self.model, self.device, group, fused=self.fused)
-                   if self.fused or self.world > 1 else None)
+        self.dp = (ShardedDataParallel(self.model, self.device, group, fused=self.fused,
+                                       shard_params=self.shard_params, init=init)
+                   if self.fused or self.world > 1 or self.shard_params else None)
         if optimizer is None:
-            only = self.dp.owned_ids() if self.dp is not None and self.world > 1 else None
+            only = self.dp.owned_ids() if self.dp is not None and (self.world > 1 or self.shard_params) else None
             optimizer = make_optimizer(self.model, cfg.train, only=only)
         self.optimizer = optimizer
         self.last_grad_norm = None
@@ -60,6 +77,8 @@ class TrainEngine:
             i, d, t = (self._to_device(x[s:e]) for x in (idx, doc_ids, targets))
             _, loss, _ = self.model(i, d, t, reduction="sum")
             (loss * inv_count).backward()
+            if self.dp is not None:
+                self.dp.after_backward()
             loss_total += loss.detach().float()
         return loss_total
 

@@ -166,6 +166,37 @@ class Block(nn.Module):
         return x
 
 
+# Initialisation of each top-level component, in the order TensorLM.reset_parameters draws them
+# (reference tnlm/model.py reset_parameters).  Kept per component so that a sharded model can stream
+# the serial initialisation one component at a time (models/init_stream.py).
+@torch.no_grad()
+def init_embedding(embed: nn.Module):
+    nn.init.normal_(embed.weight, std=1.0)
+
+
+@torch.no_grad()
+def init_block(blk: nn.Module, cfg: ModelConfig):
+    a, m = blk.attn, blk.mlp
+    for lin in [a.q1, a.k1, a.v, m.l, m.r] + ([a.q2, a.k2] if hasattr(a, "q2") else []):
+        nn.init.normal_(lin.weight, std=lin.weight.shape[1] ** -0.5)
+    if cfg.qk_init_scale != 1.0:
+        for lin in [a.q1, a.k1] + ([a.q2, a.k2] if hasattr(a, "q2") else []):
+            lin.weight.mul_(cfg.qk_init_scale)
+    depth = cfg.depth_residual_base or cfg.layers
+    for lin in (a.o, m.d):
+        nn.init.normal_(lin.weight, std=(2 * depth * lin.weight.shape[1]) ** -0.5)
+    for mod in blk.modules():
+        if isinstance(mod, (nn.Linear, SpectralLinear)) and mod.bias is not None:
+            mod.bias.zero_()
+        if isinstance(mod, SpectralLinear):
+            mod.reset_gamma()
+
+
+@torch.no_grad()
+def init_unembedding(unembed: nn.Module):
+    nn.init.normal_(unembed.weight, std=0.02)
+
+
 class TensorLM(nn.Module):
     def __init__(self, cfg: ModelConfig):
         super().__init__()
@@ -183,25 +214,11 @@ class TensorLM(nn.Module):
         """Fan-in init: embed N(0,1); Q/K/V/L/R std fan_in^-1/2 (Q/K times qk_init_scale);
         O/D std (2*depth*fan_in)^-1/2; unembed 0.02; biases 0; spectral gamma = sigma(W).
         The draw order matches the reference so a seed gives identical weights."""
-        cfg = self.cfg
-        nn.init.normal_(self.embed.weight, std=1.0)
+        init_embedding(self.embed)
         for blk in self.blocks:
-            a, m = blk.attn, blk.mlp
-            for lin in [a.q1, a.k1, a.v, m.l, m.r] + ([a.q2, a.k2] if hasattr(a, "q2") else []):
-                nn.init.normal_(lin.weight, std=lin.weight.shape[1] ** -0.5)
-            if cfg.qk_init_scale != 1.0:
-                for lin in [a.q1, a.k1] + ([a.q2, a.k2] if hasattr(a, "q2") else []):
-                    lin.weight.mul_(cfg.qk_init_scale)
-            depth = cfg.depth_residual_base or cfg.layers
-            for lin in (a.o, m.d):
-                nn.init.normal_(lin.weight, std=(2 * depth * lin.weight.shape[1]) ** -0.5)
-            for mod in blk.modules():
-                if isinstance(mod, (nn.Linear, SpectralLinear)) and mod.bias is not None:
-                    mod.bias.zero_()
-                if isinstance(mod, SpectralLinear):
-                    mod.reset_gamma()
-        if not cfg.tie_embeddings:
-            nn.init.normal_(self.unembed.weight, std=0.02)
+            init_block(blk, self.cfg)
+        if not self.cfg.tie_embeddings:
+            init_unembedding(self.unembed)
 
     @property
     def logit_multiplier(self) -> float:
@@ -287,6 +304,9 @@ class TensorLM(nn.Module):
         if ctx.get("fused"):
             from ..ops.block import model_forward
             return model_forward(self, idx, ctx, targets, reduction)
+        if getattr(self, "_ttb_weights_remote", False):
+            raise RuntimeError("this parameter-sharded model holds non-owned weights only as the fused path's bf16 "
+                               "caches; the PyTorch reference path cannot run it")
         x = self.embed(idx)
         ckpt = self.cfg.activation_checkpointing and self.training and torch.is_grad_enabled()
         for blk in self.blocks:

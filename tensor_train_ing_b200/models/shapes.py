@@ -90,17 +90,29 @@ def activation_bytes_per_token_layer(cfg: ModelConfig) -> float:
 
 
 def memory_plan(cfg: ModelConfig, *, gpus: int, micro_tokens_per_gpu: int, gpu_gb: float = 180.0,
-                checkpointing: bool | None = None, workspace_gb: float = 4.0, optimizer: str = "muon") -> dict:
-    """Per-GPU bytes of the owner-computes layout plus one micro-batch of activations."""
+                checkpointing: bool | None = None, workspace_gb: float = 4.0, optimizer: str = "muon",
+                shard_params: bool = False) -> dict:
+    """Per-GPU bytes of the owner-computes layout plus one micro-batch of activations.
+
+    Replicated layout: fp32 parameters and gradients and the bf16 GEMM caches on every rank, the
+    optimizer state sharded.  ``shard_params``: the block matrices and the unembedding keep fp32
+    master, gradient accumulator and optimizer state only on their owner (1/gpus each), every rank
+    holds their bf16 caches and two per-block fp32 staging slots; embedding and vectors replicated."""
     ckpt = cfg.activation_checkpointing if checkpointing is None else checkpointing
     c = count_params(cfg)
     n = c["total"]
     hidden = c["non_embedding"]
-    replicated = (4 + 4 + 2) * n
+    unembed = 0 if cfg.tie_embeddings else cfg.padded_vocab * cfg.d_model
     if optimizer == "muon":
         opt = (4 * hidden + 8 * (n - hidden)) / gpus
     else:
         opt = 8 * n / gpus
+    if shard_params:
+        sharded = hidden + unembed
+        staging = 2 * 4 * max(c["per_block"], unembed)
+        weights = 2 * sharded + 8 * sharded / gpus + 10 * (n - sharded) + staging
+    else:
+        weights = (4 + 4 + 2) * n
     per_layer = activation_bytes_per_token_layer(cfg)
     if ckpt:
         act = (4 * cfg.d_model * cfg.layers + per_layer) * micro_tokens_per_gpu
@@ -108,22 +120,44 @@ def memory_plan(cfg: ModelConfig, *, gpus: int, micro_tokens_per_gpu: int, gpu_g
         act = per_layer * cfg.layers * micro_tokens_per_gpu
     chunk = min(micro_tokens_per_gpu, cfg.loss_chunk_tokens or micro_tokens_per_gpu)
     loss = 2 * chunk * cfg.padded_vocab + 8 * micro_tokens_per_gpu
-    total = replicated + opt + act + loss + workspace_gb * 1e9
+    total = weights + opt + act + loss + workspace_gb * 1e9
+    layout = ("owner-computes, parameter-sharded: fp32 masters/grads/optimizer state on owners, bf16 caches "
+              "replicated" if shard_params else
+              "owner-computes: replicated fp32 params/grads + bf16 caches, sharded optimizer state")
     return {"params_B": round(n / 1e9, 3), "gpus": gpus, "micro_tokens_per_gpu": micro_tokens_per_gpu,
-            "checkpointing": ckpt, "replicated_state_GB": round(replicated / 1e9, 1),
+            "checkpointing": ckpt, "shard_params": shard_params, "replicated_state_GB": round(weights / 1e9, 1),
             "optimizer_state_GB": round(opt / 1e9, 1), "activations_GB": round(act / 1e9, 1),
             "loss_GB": round(loss / 1e9, 2), "total_GB": round(total / 1e9, 1), "fits": total < 0.92 * gpu_gb * 1e9,
-            "layout": "owner-computes: replicated fp32 params/grads + bf16 caches, sharded optimizer state"}
+            "layout": layout}
+
+
+def needs_parameter_sharding(cfg: ModelConfig, world: int, device=None) -> bool:
+    """Whether a data-parallel engine should shard the fp32 parameters: ``TTB_SHARD_PARAMS=1``/``0``
+    decides; otherwise yes when the replicated fp32 parameters, gradients and bf16 caches would
+    take more than 60% of the device's memory and there is more than one rank."""
+    import os
+    env = os.environ.get("TTB_SHARD_PARAMS")
+    if env is not None:
+        return env not in ("0", "")
+    if world <= 1:
+        return False
+    total = 180e9
+    if device is not None and torch.device(device).type == "cuda" and torch.cuda.is_available():
+        total = torch.cuda.get_device_properties(torch.device(device)).total_memory
+    return 10 * count_params(cfg)["total"] > 0.6 * total
 
 
 def min_gpus(cfg: ModelConfig, micro_tokens_per_gpu: int, gpu_gb: float = 180.0, checkpointing: bool = True,
              max_gpus: int = 1024) -> dict | None:
+    """Smallest power-of-two GPU count whose plan fits: the replicated layout first, then the
+    parameter-sharded one."""
     g = 1
     while g <= max_gpus:
-        plan = memory_plan(cfg, gpus=g, micro_tokens_per_gpu=micro_tokens_per_gpu, gpu_gb=gpu_gb,
-                           checkpointing=checkpointing)
-        if plan["fits"]:
-            return plan
+        for shard in (False, True) if g > 1 else (False,):
+            plan = memory_plan(cfg, gpus=g, micro_tokens_per_gpu=micro_tokens_per_gpu, gpu_gb=gpu_gb,
+                               checkpointing=checkpointing, shard_params=shard)
+            if plan["fits"]:
+                return plan
         g *= 2
     return None
 

@@ -337,21 +337,19 @@ class LinearCEFn(torch.autograd.Function):
         N = x.shape[0]
         dx = torch.empty(N, x.shape[1], device=x.device, dtype=torch.float32)
         dlog = torch.empty(min(chunk, N), Vp, device=x.device, dtype=torch.bfloat16)
-        acc = None
-        for s in range(0, N, chunk):
-            e = min(N, s + chunk)
-            d = dlog[: e - s]
-            lib().ce_bwd_logits(x[s:e], w16, int(V), float(alpha), targets[s:e], lse[s:e], g32, d)
-            _mm(d, w16, dx[s:e])
 
-            def compute(out, beta, d=d, s=s, e=e):
-                _mm(d.t(), x[s:e], out, c=out, beta=beta)
+        def compute(out, beta):
+            # one sink call per backward: the chunk loop runs inside it, the first chunk's dW GEMM
+            # may overwrite the buffer (beta = 0) and later chunks accumulate
+            for s in range(0, N, chunk):
+                e = min(N, s + chunk)
+                d = dlog[: e - s]
+                lib().ce_bwd_logits(x[s:e], w16, int(V), float(alpha), targets[s:e], lse[s:e], g32, d)
+                _mm(d, w16, dx[s:e])
+                _mm(d.t(), x[s:e], out, c=out, beta=beta if s == 0 else 1.0)
 
-            # each chunk goes through the sink: the first may overwrite, later ones accumulate
-            (gw,) = group.sink_grad(compute)
-            if gw is not None:  # not accumulated in place: keep a running sum for autograd
-                acc = gw if acc is None else acc + gw
-        return dx, None, None, None, None, None, acc
+        (gw,) = group.sink_grad(compute)
+        return dx, None, None, None, None, None, gw
 
 
 def linear_cross_entropy(x, targets, group, V, alpha=1.0, chunk=8192):

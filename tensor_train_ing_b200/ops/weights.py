@@ -11,6 +11,10 @@ list of parameters that one GEMM consumes together (e.g. q1, k1, q2, k2, v of a 
   micro-batch of a step overwrites (beta = 0), later ones accumulate in the GEMM epilogue
   (beta = 1), so no separate gradient-accumulation kernel runs.  If the parameters' grads are
   not this group's views (set by someone else), the gradient is returned to autograd instead.
+
+Under parameter-sharded data parallelism the group is attached to its sharding layer
+(``_shard``): the gradient then goes to the layer's per-layer staging buffer and the layer reduces
+it onto the owning rank.
 """
 from __future__ import annotations
 
@@ -28,12 +32,15 @@ class WeightGroup:
         self._cache = None
         self._key = None
         self._grad = None
+        self._shard = None  # (sharding layer, unit) under parameter-sharded data parallelism
 
     # ------------------------------------------------------------------ forward operand
     def _version_key(self):
         return tuple((p.data_ptr(), p._version) for p in self.params)
 
     def bf16(self) -> torch.Tensor:
+        if self._shard is not None and self._cache is not None:
+            return self._cache  # written by the sharding layer's gather, once per optimizer step
         key = self._version_key()
         if self._cache is None or key != self._key:
             with torch.no_grad():
@@ -61,6 +68,9 @@ class WeightGroup:
         """compute(out_fp32 [rows, d_in], beta) writes (beta=0) or adds (beta=1) the weight grad.
 
         Returns the list of gradients to hand to autograd (None where accumulated in place)."""
+        if self._shard is not None:
+            layer, unit = self._shard
+            return layer.sink(unit, compute)
         leafs = all(p.is_leaf and p.requires_grad for p in self.params)
         if leafs:
             buf = self._grad_buffer()

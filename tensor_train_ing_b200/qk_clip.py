@@ -23,7 +23,8 @@ def _rescale_heads_(blk, name: str, gamma: torch.Tensor, d_key: int):
     q, k = (blk.attn.q1, blk.attn.k1) if name == "S1" else (blk.attn.q2, blk.attn.k2)
     rows = gamma.sqrt().repeat_interleave(d_key).to(q.weight.dtype)
     for lin in (q, k):
-        lin.weight.mul_(rows[:, None])
+        if not getattr(lin.weight, "_ttb_remote", False):  # sharded: only the owner holds the master
+            lin.weight.mul_(rows[:, None])
         if lin.bias is not None:
             lin.bias.mul_(rows)
 

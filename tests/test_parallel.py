@@ -32,3 +32,15 @@ def test_unit_assignment_is_balanced_and_deterministic():
     assert a == assign_units(sizes, 3)
     load = [sum(s for s, r in zip(sizes, a) if r == q) for q in range(3)]
     assert max(load) - min(load) <= 100
+
+
+@pytest.mark.slow
+@pytest.mark.parametrize("optimizer", ["adamw", "muon"])
+@pytest.mark.parametrize("nproc", [2, 3])
+def test_parameter_sharded_steps_match_single_process(optimizer, nproc, tmp_path):
+    out = _torchrun("sharded_params_equivalence.py", nproc, optimizer, str(tmp_path))
+    assert out.returncode == 0, out.stdout[-3000:] + out.stderr[-3000:]
+    line = next(x for x in out.stdout.splitlines() if x.startswith("MAXERR"))
+    assert float(line.split()[1]) < 1e-10
+    line = next(x for x in out.stdout.splitlines() if x.startswith("RESUMEERR"))
+    assert float(line.split()[1]) == 0.0
