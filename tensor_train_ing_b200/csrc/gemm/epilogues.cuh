@@ -184,8 +184,15 @@ struct EpiBilinear {
 //   dl = dH * r            dr = dH * l          (mode 0)
 //   dl = dH * r * silu'(l) dr = dH * silu(l)    (mode 1)
 // l, r are the bf16 factors saved by the forward; dl/dr written bf16.
+//
+// With K = d_model the main loop of a tile is short and this epilogue moves 8 bytes per output
+// element (l, r in; dl, dr out), so it must keep many loads in flight: each thread stages the
+// factors of its row two 32-column chunks ahead with cp.async into its own 256 bytes of shared
+// memory (two buffers of l|r, 16-byte pieces XOR-swizzled by thread so a warp's reads hit distinct
+// banks), instead of holding them in registers.
 template <int NB>
 struct EpiBilinearGrad {
+  static constexpr int kSmemPerThread = 256;
   const __nv_bfloat16* Lin;
   const __nv_bfloat16* Rin;
   __nv_bfloat16* dL;
@@ -195,37 +202,41 @@ struct EpiBilinearGrad {
   int mode;
   int M, N;
 
-  // Loads the saved bf16 factors of 32 columns as packed pairs (zero outside the matrix).
-  __device__ __forceinline__ void load_pairs(long long off, bool full, int nv, uint32_t (&lp)[16],
-                                             uint32_t (&rp)[16]) const {
-    if (full) {
-#pragma unroll
-      for (int q = 0; q < 4; ++q) {
-        const uint4 u = *reinterpret_cast<const uint4*>(Lin + off + q * 8);
-        const uint4 v = *reinterpret_cast<const uint4*>(Rin + off + q * 8);
-        lp[q * 4 + 0] = u.x; lp[q * 4 + 1] = u.y; lp[q * 4 + 2] = u.z; lp[q * 4 + 3] = u.w;
-        rp[q * 4 + 0] = v.x; rp[q * 4 + 1] = v.y; rp[q * 4 + 2] = v.z; rp[q * 4 + 3] = v.w;
-      }
-    } else {
-#pragma unroll
-      for (int j = 0; j < 16; ++j) {
-        const float l0 = 2 * j < nv ? __bfloat162float(Lin[off + 2 * j]) : 0.f;
-        const float l1 = 2 * j + 1 < nv ? __bfloat162float(Lin[off + 2 * j + 1]) : 0.f;
-        const float r0 = 2 * j < nv ? __bfloat162float(Rin[off + 2 * j]) : 0.f;
-        const float r1 = 2 * j + 1 < nv ? __bfloat162float(Rin[off + 2 * j + 1]) : 0.f;
-        lp[j] = pack_bf16(l0, l1);
-        rp[j] = pack_bf16(r0, r1);
-      }
-    }
+  // piece p (0..7: l then r, 16 bytes each) of buffer b in this thread's area
+  __device__ __forceinline__ static uint32_t piece(int b, int p) {
+    return static_cast<uint32_t>(((b * 8 + p) ^ static_cast<int>(threadIdx.x & 7)) << 4);
   }
 
-  // The saved factors of chunk c+1 are loaded while chunk c is computed and stored, so the
-  // global-load latency overlaps useful work instead of stalling every 32-column chunk.
-  __device__ __forceinline__ void operator()(uint32_t taddr, int row, int n0, int, int) const {
+  // Queue the factors of one chunk into buffer b (ragged chunks: zero-padded ordinary stores), and
+  // close one cp.async group either way so that group k always belongs to chunk k.
+  __device__ __forceinline__ void stage(uint8_t* sm, int b, long long off, bool full, int nv, bool active) const {
+    if (active) {
+      if (full) {
+        const uint32_t base = smem_u32(sm);
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          cp_async16(base + piece(b, q), Lin + off + q * 8);
+          cp_async16(base + piece(b, 4 + q), Rin + off + q * 8);
+        }
+      } else {
+#pragma unroll
+        for (int j = 0; j < 16; ++j) {
+          const float l0 = 2 * j < nv ? __bfloat162float(Lin[off + 2 * j]) : 0.f;
+          const float l1 = 2 * j + 1 < nv ? __bfloat162float(Lin[off + 2 * j + 1]) : 0.f;
+          const float r0 = 2 * j < nv ? __bfloat162float(Rin[off + 2 * j]) : 0.f;
+          const float r1 = 2 * j + 1 < nv ? __bfloat162float(Rin[off + 2 * j + 1]) : 0.f;
+          *reinterpret_cast<uint32_t*>(sm + piece(b, j / 4) + (j % 4) * 4) = pack_bf16(l0, l1);
+          *reinterpret_cast<uint32_t*>(sm + piece(b, 4 + j / 4) + (j % 4) * 4) = pack_bf16(r0, r1);
+        }
+      }
+    }
+    cp_async_commit();
+  }
+
+  __device__ __forceinline__ void operator()(uint32_t taddr, int row, int n0, int, int, uint8_t* sm) const {
     constexpr int kChunks = NB / 32;
     const bool vec_ok = (ld % 8 == 0) && (ldo % 8 == 0);
     const bool row_ok = row < M;
-    uint32_t lp[16], rp[16];
     auto chunk_meta = [&](int c, long long& off, bool& full, int& nv) {
       const int col0 = n0 + c * 32;
       nv = max(0, min(32, N - col0));
@@ -233,12 +244,13 @@ struct EpiBilinearGrad {
       off = static_cast<long long>(row) * ld + col0;
     };
     const long long out_base = static_cast<long long>(row) * ldo + n0;
-    {
+#pragma unroll
+    for (int c = 0; c < 2; ++c) {
       long long off;
       bool full;
       int nv;
-      chunk_meta(0, off, full, nv);
-      if (row_ok && nv > 0) load_pairs(off, full, nv, lp, rp);
+      chunk_meta(c, off, full, nv);
+      stage(sm, c, off, full, nv, c < kChunks && row_ok && nv > 0);
     }
 #pragma unroll 1
     for (int c = 0; c < kChunks; ++c) {
@@ -248,16 +260,18 @@ struct EpiBilinearGrad {
       bool full;
       int nv;
       chunk_meta(c, off, full, nv);
-      uint32_t ln[16], rn[16];
-      if (c + 1 < kChunks) {
-        long long off2;
-        bool full2;
-        int nv2;
-        chunk_meta(c + 1, off2, full2, nv2);
-        if (row_ok && nv2 > 0) load_pairs(off2, full2, nv2, ln, rn);
-      }
+      cp_async_wait<1>();  // chunk c has landed; chunk c + 1 may still be in flight
       tmem_ld_wait();
+      const int b = c & 1;
       if (row_ok && nv > 0) {
+        uint32_t lp[16], rp[16];
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          const uint4 u = *reinterpret_cast<const uint4*>(sm + piece(b, q));
+          const uint4 v = *reinterpret_cast<const uint4*>(sm + piece(b, 4 + q));
+          lp[q * 4 + 0] = u.x; lp[q * 4 + 1] = u.y; lp[q * 4 + 2] = u.z; lp[q * 4 + 3] = u.w;
+          rp[q * 4 + 0] = v.x; rp[q * 4 + 1] = v.y; rp[q * 4 + 2] = v.z; rp[q * 4 + 3] = v.w;
+        }
         float dl[32], dr[32];
 #pragma unroll
         for (int j = 0; j < 32; ++j) {
@@ -278,14 +292,14 @@ struct EpiBilinearGrad {
         store_row32_bf16(dL + out_base + c * 32, full, nv, dl);
         store_row32_bf16(dR + out_base + c * 32, full, nv, dr);
       }
-      if (c + 1 < kChunks) {
-#pragma unroll
-        for (int j = 0; j < 16; ++j) {
-          lp[j] = ln[j];
-          rp[j] = rn[j];
-        }
-      }
+      // refill the buffer just read with chunk c + 2 (an empty group past the last chunk)
+      long long off2 = 0;
+      bool full2 = false;
+      int nv2 = 0;
+      if (c + 2 < kChunks) chunk_meta(c + 2, off2, full2, nv2);
+      stage(sm, b, off2, full2, nv2, c + 2 < kChunks && row_ok && nv2 > 0);
     }
+    cp_async_wait<0>();
   }
 };
 

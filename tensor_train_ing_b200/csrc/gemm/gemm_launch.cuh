@@ -15,16 +15,18 @@ template <int BN, int STAGES, bool DUAL, class Epi, bool A_MN, bool B_MN>
 inline void launch_impl(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& tb2, Shape s, const Epi& epi,
                         cudaStream_t stream) {
   using L = Layout<BN, STAGES, DUAL>;
+  constexpr int kSmem = with_epi_smem<Epi>(L::kSmemBytes, L::kBarOffset, STAGES);
+  static_assert(kSmem <= 232448, "GEMM shared memory exceeds 227 KB");
   auto kern = gemm_kernel<BN, STAGES, A_MN, B_MN, DUAL, Epi>;
   static bool configured = false;
   if (!configured) {
-    TTB_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kSmemBytes));
+    TTB_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem));
     configured = true;
   }
   constexpr int NB = L::kBNMma;
   const int tiles = ((s.M + BM - 1) / BM) * ((s.N + NB - 1) / NB);
   const int grid = tiles < num_sms() ? tiles : num_sms();
-  kern<<<grid, kThreads, L::kSmemBytes, stream>>>(ta, tb, tb2, s, epi);
+  kern<<<grid, kThreads, kSmem, stream>>>(ta, tb, tb2, s, epi);
   TTB_CUDA_CHECK(cudaGetLastError());
 }
 
@@ -43,16 +45,18 @@ template <class Epi, bool A_MN, bool B_MN, bool DUAL>
 inline void launch_pair(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& tb2, Shape s, const Epi& epi,
                         cudaStream_t stream) {
   using L = PairLayout<kPairStages, DUAL>;
+  constexpr int kSmem = with_epi_smem<Epi>(L::kSmemBytes, L::kBarOffset, kPairStages);
+  static_assert(kSmem <= 232448, "GEMM shared memory exceeds 227 KB");
   auto kern = gemm_pair_kernel<kPairStages, A_MN, B_MN, DUAL, Epi>;
   static bool configured = false;
   if (!configured) {
-    TTB_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kSmemBytes));
+    TTB_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem));
     configured = true;
   }
   const int tiles = ((s.M + kPairBM - 1) / kPairBM) * ((s.N + L::kTileN - 1) / L::kTileN);
   const int pairs = num_sms() / 2;
   const int grid = 2 * (tiles < pairs ? tiles : pairs);
-  kern<<<grid, kThreads, L::kSmemBytes, stream>>>(ta, tb, tb2, s, epi);
+  kern<<<grid, kThreads, kSmem, stream>>>(ta, tb, tb2, s, epi);
   TTB_CUDA_CHECK(cudaGetLastError());
 }
 

@@ -14,13 +14,46 @@
 //
 // The epilogue is a functor with
 //   __device__ void operator()(uint32_t taddr, int row, int n0, int tile_m, int tile_n) const
-// where taddr addresses this thread's TMEM lane at column 0 of the tile's accumulator.
+// where taddr addresses this thread's TMEM lane at column 0 of the tile's accumulator.  A functor
+// that declares ``static constexpr int kSmemPerThread`` gets that many bytes of shared memory per
+// epilogue thread (after the pipeline's barriers) as a sixth argument, a uint8_t* of its own.
 #pragma once
+
+#include <type_traits>
 
 #include "../common/sm100.cuh"
 
 namespace ttb {
 namespace gemm {
+
+template <class E, class = void>
+struct EpiSmem {
+  static constexpr int kPerThread = 0;
+};
+template <class E>
+struct EpiSmem<E, std::void_t<decltype(E::kSmemPerThread)>> {
+  static constexpr int kPerThread = E::kSmemPerThread;
+};
+
+constexpr int kEpiThreads = 128;  // four epilogue warps per CTA
+
+// Shared-memory offset of the epilogue's private area (after the barriers; 128-byte aligned) and
+// the dynamic shared memory a launch needs with it.
+__host__ __device__ constexpr int epi_smem_offset(int bar_offset, int stages) { return (bar_offset + (2 * stages + 5) * 8 + 16 + 127) / 128 * 128; }
+template <class Epi>
+__host__ __device__ constexpr int with_epi_smem(int smem_bytes, int bar_offset, int stages) {
+  return EpiSmem<Epi>::kPerThread == 0 ? smem_bytes
+                                       : epi_smem_offset(bar_offset, stages) + kEpiThreads * EpiSmem<Epi>::kPerThread + 1024;
+}
+
+template <class Epi>
+__device__ __forceinline__ void run_epilogue(const Epi& epi, uint32_t taddr, int row, int n0, int tm, int tn,
+                                             uint8_t* epi_smem) {
+  if constexpr (EpiSmem<Epi>::kPerThread > 0)
+    epi(taddr, row, n0, tm, tn, epi_smem);
+  else
+    epi(taddr, row, n0, tm, tn);
+}
 
 constexpr int BM = 128;
 constexpr int BK = 64;            // one 128-byte swizzle row of bf16
@@ -245,7 +278,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       tc_fence_after();
       const uint32_t taddr = tmem_base + (static_cast<uint32_t>(sub * 32) << 16) + acc * L::kAccCols;
       const int row = tm * BM + sub * 32 + lane;
-      epi(taddr, row, tn * NB, tm, tn);
+      run_epilogue(epi, taddr, row, tn * NB, tm, tn,
+                   smem + epi_smem_offset(L::kBarOffset, STAGES) + (threadIdx.x - 64) * EpiSmem<Epi>::kPerThread);
       tc_fence_before();
       mbar_arrive(&tempty[acc]);
       if (++acc == 2) {
@@ -461,7 +495,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
       tc_fence_after();
       const uint32_t taddr = tmem_base + (static_cast<uint32_t>(sub * 32) << 16) + acc * L::kAccCols;
       const int row = tm * kPairBM + static_cast<int>(rank) * kPairHalf + sub * 32 + lane;
-      epi(taddr, row, tn * TN, tm, tn);
+      run_epilogue(epi, taddr, row, tn * TN, tm, tn,
+                   smem + epi_smem_offset(L::kBarOffset, STAGES) + (threadIdx.x - 64) * EpiSmem<Epi>::kPerThread);
       tc_fence_before();
       mbar_arrive_cluster(mapa_shared(smem_u32(&tempty[acc]), 0));
       if (++acc == 2) {

@@ -19,6 +19,22 @@ it onto the owning rank.
 from __future__ import annotations
 
 import torch
+from torch.optim.optimizer import register_optimizer_step_post_hook
+
+# Optimizer steps seen so far (every torch optimizer, through a global step post-hook).  Part of the
+# cache key: fused optimizer kernels (torch's fused AdamW among them) update parameters in place
+# without bumping their version counters, so a version-only key would keep serving the bf16 copy
+# of the weights from before the step.
+_STEPS = [0]
+
+
+def weights_updated():
+    """Invalidate every bf16 weight cache (called after each optimizer step; call it after any other
+    in-place parameter update that bypasses autograd's version counters)."""
+    _STEPS[0] += 1
+
+
+register_optimizer_step_post_hook(lambda optimizer, args, kwargs: weights_updated())
 
 
 class WeightGroup:
@@ -36,7 +52,7 @@ class WeightGroup:
 
     # ------------------------------------------------------------------ forward operand
     def _version_key(self):
-        return tuple((p.data_ptr(), p._version) for p in self.params)
+        return (_STEPS[0],) + tuple((p.data_ptr(), p._version) for p in self.params)
 
     def bf16(self) -> torch.Tensor:
         if self._shard is not None and self._cache is not None:

@@ -113,3 +113,26 @@ def test_bilinear_grad_strided_outputs():
     assert _rel(dlr[:, :N], dh * ro.float()) < 2e-2 and _rel(dlr[:, N:], dh * lo.float()) < 2e-2
     torch.cuda.synchronize()
     assert _C().status() == 0
+
+
+@pytest.mark.parametrize("M,N,D", [(300, 200, 136), (256, 520, 64)])
+@pytest.mark.parametrize("mode", [0, 1])
+def test_bilinear_grad_ragged_edges(M, N, D, mode):
+    """Column counts that end inside a 32-column chunk and rows that end inside a tile."""
+    torch.manual_seed(5)
+    lo = torch.randn(M, N, device="cuda").bfloat16()
+    ro = torch.randn(M, N, device="cuda").bfloat16()
+    wd = (torch.randn(D, N, device="cuda") / N ** 0.5).bfloat16()
+    dy = torch.randn(M, D, device="cuda").bfloat16()
+    dl, dr = torch.empty_like(lo), torch.empty_like(lo)
+    _C().bilinear_grad(dy, wd, lo, ro, dl, dr, mode)
+    dh = (dy.float() @ wd.float()).bfloat16().float()
+    l, r = lo.float(), ro.float()
+    if mode == 0:
+        want_l, want_r = dh * r, dh * l
+    else:
+        sg = torch.sigmoid(l)
+        want_l, want_r = dh * r * sg * (1 + l * (1 - sg)), dh * l * sg
+    assert _rel(dl, want_l) < 2e-2 and _rel(dr, want_r) < 2e-2
+    torch.cuda.synchronize()
+    assert _C().status() == 0

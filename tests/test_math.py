@@ -215,3 +215,21 @@ def test_analysis_modes_cannot_leak_into_training():
     norm.eval()
     norm(torch.randn(2, 4))
     assert norm.denom_saved is not None
+
+
+def test_weight_cache_follows_fused_optimizer_steps():
+    """torch's fused AdamW updates parameters without bumping their version counters; the bf16
+    operand cache of a weight group must still be rebuilt after the step."""
+    import torch
+    from tensor_train_ing_b200.ops.weights import WeightGroup
+    w = torch.nn.Parameter(torch.randn(16, 8))
+    grp = WeightGroup([w])
+    before = grp.bf16().clone()
+    assert torch.equal(before, w.detach().bfloat16())
+    w.grad = torch.randn(16, 8)
+    opt = torch.optim.AdamW([w], lr=0.1, fused=True)
+    v = w._version
+    opt.step()
+    assert w._version == v  # the case this guards against
+    assert torch.equal(grp.bf16(), w.detach().bfloat16())
+    assert not torch.equal(grp.bf16(), before)
