@@ -186,13 +186,16 @@ struct EpiBilinear {
 // l, r are the bf16 factors saved by the forward; dl/dr written bf16.
 //
 // With K = d_model the main loop of a tile is short and this epilogue moves 8 bytes per output
-// element (l, r in; dl, dr out), so it must keep many loads in flight: each thread stages the
-// factors of its row two 32-column chunks ahead with cp.async into its own 256 bytes of shared
-// memory (two buffers of l|r, 16-byte pieces XOR-swizzled by thread so a warp's reads hit distinct
-// banks), instead of holding them in registers.
+// element (l, r in; dl, dr out).  A thread owns one row of the accumulator, but global memory is
+// accessed warp-cooperatively through shared memory: each warp stages the 32 x 32 chunks of l and r
+// for its 32 rows with cp.async, 8 rows of 64 bytes per instruction (coalesced), two chunks ahead;
+// every thread then reads its own row, writes its dl / dr row back into the same buffer, and the
+// warp stores the chunk to global memory 8 rows per instruction.  Rows are 64-byte swizzled
+// (16-byte piece q of row R at q ^ ((R >> 1) & 3)) so both access patterns are bank-conflict free.
+// Requires N, ld and ldo to be multiples of 8 (16-byte pieces), which the launcher checks.
 template <int NB>
 struct EpiBilinearGrad {
-  static constexpr int kSmemPerThread = 256;
+  static constexpr int kSmemPerThread = 256;  // per warp: 2 buffers x (l 2 KB | r 2 KB)
   const __nv_bfloat16* Lin;
   const __nv_bfloat16* Rin;
   __nv_bfloat16* dL;
@@ -202,102 +205,112 @@ struct EpiBilinearGrad {
   int mode;
   int M, N;
 
-  // piece p (0..7: l then r, 16 bytes each) of buffer b in this thread's area
-  __device__ __forceinline__ static uint32_t piece(int b, int p) {
-    return static_cast<uint32_t>(((b * 8 + p) ^ static_cast<int>(threadIdx.x & 7)) << 4);
+  // byte offset of 16-byte piece q of row R in one 2 KB (32 rows x 64 bytes) area
+  __device__ __forceinline__ static uint32_t at(int R, int q) {
+    return static_cast<uint32_t>(R * 64 + ((q ^ ((R >> 1) & 3)) << 4));
   }
 
-  // Queue the factors of one chunk into buffer b (ragged chunks: zero-padded ordinary stores), and
-  // close one cp.async group either way so that group k always belongs to chunk k.
-  __device__ __forceinline__ void stage(uint8_t* sm, int b, long long off, bool full, int nv, bool active) const {
-    if (active) {
-      if (full) {
-        const uint32_t base = smem_u32(sm);
+  // Queue chunk c of the warp's 32 rows (first row row0) into buffer area buf (l at +0, r at +2 KB).
+  // Lane l copies pieces (row 8i + l/4, piece l%4), i = 0..3, of both factors; pieces outside the
+  // matrix are skipped (their rows / columns are never stored).  One cp.async group per call.
+  __device__ __forceinline__ void stage(uint8_t* buf, int row0, int col0, int lane) const {
+    const uint32_t base = smem_u32(buf);
+    const int q = lane & 3;
+    const int col = col0 + q * 8;
 #pragma unroll
-        for (int q = 0; q < 4; ++q) {
-          cp_async16(base + piece(b, q), Lin + off + q * 8);
-          cp_async16(base + piece(b, 4 + q), Rin + off + q * 8);
-        }
-      } else {
-#pragma unroll
-        for (int j = 0; j < 16; ++j) {
-          const float l0 = 2 * j < nv ? __bfloat162float(Lin[off + 2 * j]) : 0.f;
-          const float l1 = 2 * j + 1 < nv ? __bfloat162float(Lin[off + 2 * j + 1]) : 0.f;
-          const float r0 = 2 * j < nv ? __bfloat162float(Rin[off + 2 * j]) : 0.f;
-          const float r1 = 2 * j + 1 < nv ? __bfloat162float(Rin[off + 2 * j + 1]) : 0.f;
-          *reinterpret_cast<uint32_t*>(sm + piece(b, j / 4) + (j % 4) * 4) = pack_bf16(l0, l1);
-          *reinterpret_cast<uint32_t*>(sm + piece(b, 4 + j / 4) + (j % 4) * 4) = pack_bf16(r0, r1);
-        }
+    for (int i = 0; i < 4; ++i) {
+      const int R = i * 8 + (lane >> 2);
+      const int row = row0 + R;
+      if (row < M && col < N) {
+        const long long off = static_cast<long long>(row) * ld + col;
+        cp_async16(base + at(R, q), Lin + off);
+        cp_async16(base + 2048 + at(R, q), Rin + off);
       }
     }
     cp_async_commit();
   }
 
+  // smem: this warp's 8 KB area (the kernel hands each thread a 256-byte slice, 32 consecutive
+  // slices per warp)
   __device__ __forceinline__ void operator()(uint32_t taddr, int row, int n0, int, int, uint8_t* sm) const {
     constexpr int kChunks = NB / 32;
-    const bool vec_ok = (ld % 8 == 0) && (ldo % 8 == 0);
+    const int lane = static_cast<int>(threadIdx.x & 31);
+    uint8_t* area = sm - lane * kSmemPerThread;  // the warp's first slice
+    const int row0 = row - lane;                 // this warp's first row
+    const int R = lane;                          // this thread's row inside the chunk
     const bool row_ok = row < M;
-    auto chunk_meta = [&](int c, long long& off, bool& full, int& nv) {
-      const int col0 = n0 + c * 32;
-      nv = max(0, min(32, N - col0));
-      full = nv == 32 && vec_ok;
-      off = static_cast<long long>(row) * ld + col0;
-    };
-    const long long out_base = static_cast<long long>(row) * ldo + n0;
-#pragma unroll
-    for (int c = 0; c < 2; ++c) {
-      long long off;
-      bool full;
-      int nv;
-      chunk_meta(c, off, full, nv);
-      stage(sm, c, off, full, nv, c < kChunks && row_ok && nv > 0);
-    }
+    stage(area, row0, n0, lane);
+    stage(area + 4096, row0, n0 + 32, lane);
 #pragma unroll 1
     for (int c = 0; c < kChunks; ++c) {
+      uint8_t* buf = area + (c & 1) * 4096;
+      const int col0 = n0 + c * 32;
       uint32_t a[32];
       tmem_ld32(taddr + c * 32, a);
-      long long off;
-      bool full;
-      int nv;
-      chunk_meta(c, off, full, nv);
-      cp_async_wait<1>();  // chunk c has landed; chunk c + 1 may still be in flight
+      cp_async_wait<1>();  // this lane's copies of chunk c have landed ...
+      __syncwarp();        // ... and so have the other lanes'
       tmem_ld_wait();
-      const int b = c & 1;
+      const int nv = max(0, min(32, N - col0));
       if (row_ok && nv > 0) {
         uint32_t lp[16], rp[16];
 #pragma unroll
         for (int q = 0; q < 4; ++q) {
-          const uint4 u = *reinterpret_cast<const uint4*>(sm + piece(b, q));
-          const uint4 v = *reinterpret_cast<const uint4*>(sm + piece(b, 4 + q));
+          const uint4 u = *reinterpret_cast<const uint4*>(buf + at(R, q));
+          const uint4 v = *reinterpret_cast<const uint4*>(buf + 2048 + at(R, q));
           lp[q * 4 + 0] = u.x; lp[q * 4 + 1] = u.y; lp[q * 4 + 2] = u.z; lp[q * 4 + 3] = u.w;
           rp[q * 4 + 0] = v.x; rp[q * 4 + 1] = v.y; rp[q * 4 + 2] = v.z; rp[q * 4 + 3] = v.w;
         }
-        float dl[32], dr[32];
+        uint32_t ol[16], orr[16];
 #pragma unroll
-        for (int j = 0; j < 32; ++j) {
-          const float l = (j & 1) ? bf16_hi(lp[j / 2]) : bf16_lo(lp[j / 2]);
-          const float r = (j & 1) ? bf16_hi(rp[j / 2]) : bf16_lo(rp[j / 2]);
-          // the reference's autograd sees dH rounded to bf16 (output grad of a bf16 product)
-          const float dh = __bfloat162float(__float2bfloat16_rn(__uint_as_float(a[j])));
-          if (mode == 1) {
-            const float sg = 1.f / (1.f + __expf(-l));
-            const float silu = l * sg;
-            dr[j] = dh * silu;
-            dl[j] = dh * r * (sg * (1.f + l * (1.f - sg)));
-          } else {
-            dl[j] = dh * r;
-            dr[j] = dh * l;
+        for (int j = 0; j < 32; j += 2) {
+          float dl[2], dr[2];
+#pragma unroll
+          for (int e = 0; e < 2; ++e) {
+            const int jj = j + e;
+            const float l = (jj & 1) ? bf16_hi(lp[jj / 2]) : bf16_lo(lp[jj / 2]);
+            const float r = (jj & 1) ? bf16_hi(rp[jj / 2]) : bf16_lo(rp[jj / 2]);
+            // the reference's autograd sees dH rounded to bf16 (output grad of a bf16 product)
+            const float dh = __bfloat162float(__float2bfloat16_rn(__uint_as_float(a[jj])));
+            if (mode == 1) {
+              const float sg = 1.f / (1.f + __expf(-l));
+              dr[e] = dh * (l * sg);
+              dl[e] = dh * r * (sg * (1.f + l * (1.f - sg)));
+            } else {
+              dl[e] = dh * r;
+              dr[e] = dh * l;
+            }
+          }
+          ol[j / 2] = pack_bf16(dl[0], dl[1]);
+          orr[j / 2] = pack_bf16(dr[0], dr[1]);
+        }
+        // this thread's row of the buffer now holds its outputs (only this thread reads that row)
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          *reinterpret_cast<uint4*>(buf + at(R, q)) = make_uint4(ol[q * 4], ol[q * 4 + 1], ol[q * 4 + 2], ol[q * 4 + 3]);
+          *reinterpret_cast<uint4*>(buf + 2048 + at(R, q)) =
+              make_uint4(orr[q * 4], orr[q * 4 + 1], orr[q * 4 + 2], orr[q * 4 + 3]);
+        }
+      }
+      __syncwarp();
+      {  // the warp stores the chunk, 8 rows of 64 bytes per instruction
+        const int q = lane & 3;
+        const int col = col0 + q * 8;
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const int Rs = i * 8 + (lane >> 2);
+          const int rw = row0 + Rs;
+          if (rw < M && col < N) {
+            const long long off = static_cast<long long>(rw) * ldo + col;
+            *reinterpret_cast<uint4*>(dL + off) = *reinterpret_cast<const uint4*>(buf + at(Rs, q));
+            *reinterpret_cast<uint4*>(dR + off) = *reinterpret_cast<const uint4*>(buf + 2048 + at(Rs, q));
           }
         }
-        store_row32_bf16(dL + out_base + c * 32, full, nv, dl);
-        store_row32_bf16(dR + out_base + c * 32, full, nv, dr);
       }
-      // refill the buffer just read with chunk c + 2 (an empty group past the last chunk)
-      long long off2 = 0;
-      bool full2 = false;
-      int nv2 = 0;
-      if (c + 2 < kChunks) chunk_meta(c + 2, off2, full2, nv2);
-      stage(sm, b, off2, full2, nv2, c + 2 < kChunks && row_ok && nv2 > 0);
+      __syncwarp();  // every lane is done with the buffer before it is refilled
+      if (c + 2 < kChunks)
+        stage(buf, row0, n0 + (c + 2) * 32, lane);
+      else
+        cp_async_commit();  // keep one group per chunk
     }
     cp_async_wait<0>();
   }

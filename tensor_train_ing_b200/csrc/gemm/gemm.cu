@@ -34,6 +34,8 @@ void gemm_bilinear(const Operand& x, const Operand& wl, const Operand& wr, int M
 void gemm_bilinear_grad(const Operand& dy, const Operand& wd, int M, int N, int K, const void* Lin, const void* Rin,
                         void* dL, void* dR, long long ld, long long ldo, int mode, cudaStream_t stream) {
   TTB_CHECK(M > 0 && N > 0 && K > 0, "empty GEMM");
+  TTB_CHECK(N % 8 == 0 && ld % 8 == 0 && ldo % 8 == 0,
+            "bilinear backward: width and row strides must be multiples of 8 elements");
   gemm::EpiBilinearGrad<256> epi{static_cast<const __nv_bfloat16*>(Lin), static_cast<const __nv_bfloat16*>(Rin),
                                  static_cast<__nv_bfloat16*>(dL), static_cast<__nv_bfloat16*>(dR), ld, ldo, mode,
                                  M, N};
