@@ -71,6 +71,85 @@ __device__ __forceinline__ void store_row32_f32(float* p, bool full, int n_valid
   }
 }
 
+// ---------------------------------------------------------------- warp-coalesced chunk I/O
+// An epilogue thread owns one accumulator row, so row-per-thread global accesses touch 32
+// different 128-byte lines per warp instruction and keep L1 busy on the short-K GEMMs.  These
+// helpers move a warp's 32 x 32 chunk through the warp's shared area instead: every thread writes
+// (or reads) its own row there, and global memory is written / read 8 bf16 rows (64 bytes each) or
+// 4 fp32 rows (128 bytes each) per instruction.  Rows are XOR-swizzled in 16-byte pieces, so
+// both the row-wise and the coalesced accesses are free of bank conflicts.  Pieces outside the
+// matrix (rows >= M, columns >= N) are skipped; N and the row strides must be multiples of 8
+// (bf16) or 4 (fp32) elements and the base pointers 16-byte aligned.
+__device__ __forceinline__ uint32_t sw_at16(int R, int q) {  // bf16: 4 pieces per 64-byte row
+  return static_cast<uint32_t>(R * 64 + ((q ^ ((R >> 1) & 3)) << 4));
+}
+__device__ __forceinline__ uint32_t sw_at32(int R, int q) {  // fp32: 8 pieces per 128-byte row
+  return static_cast<uint32_t>(R * 128 + ((q ^ (R & 7)) << 4));
+}
+
+__device__ __forceinline__ void warp_store_bf16(uint8_t* buf, const float (&v)[32], int lane, __nv_bfloat16* D,
+                                                long long ldd, int row0, int col0, int M, int N) {
+#pragma unroll
+  for (int q = 0; q < 4; ++q)
+    *reinterpret_cast<uint4*>(buf + sw_at16(lane, q)) =
+        make_uint4(pack_bf16(v[q * 8 + 0], v[q * 8 + 1]), pack_bf16(v[q * 8 + 2], v[q * 8 + 3]),
+                   pack_bf16(v[q * 8 + 4], v[q * 8 + 5]), pack_bf16(v[q * 8 + 6], v[q * 8 + 7]));
+  __syncwarp();
+  const int q = lane & 3;
+  const int col = col0 + q * 8;
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const int R = i * 8 + (lane >> 2);
+    if (row0 + R < M && col < N)
+      *reinterpret_cast<uint4*>(D + static_cast<long long>(row0 + R) * ldd + col) =
+          *reinterpret_cast<const uint4*>(buf + sw_at16(R, q));
+  }
+  __syncwarp();
+}
+
+__device__ __forceinline__ void warp_store_f32(uint8_t* buf, const float (&v)[32], int lane, float* D, long long ldd,
+                                               int row0, int col0, int M, int N) {
+#pragma unroll
+  for (int q = 0; q < 8; ++q)
+    *reinterpret_cast<float4*>(buf + sw_at32(lane, q)) = make_float4(v[q * 4], v[q * 4 + 1], v[q * 4 + 2], v[q * 4 + 3]);
+  __syncwarp();
+  const int q = lane & 7;
+  const int col = col0 + q * 4;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const int R = i * 4 + (lane >> 3);
+    if (row0 + R < M && col < N)
+      *reinterpret_cast<float4*>(D + static_cast<long long>(row0 + R) * ldd + col) =
+          *reinterpret_cast<const float4*>(buf + sw_at32(R, q));
+  }
+  __syncwarp();
+}
+
+// Queue the fp32 chunk C[row0 .., col0 ..] into buf with cp.async, 4 rows per instruction; closes
+// one cp.async group.
+__device__ __forceinline__ void warp_load_f32_async(uint8_t* buf, const float* C, long long ldc, int row0, int col0,
+                                                    int M, int N, int lane) {
+  const uint32_t base = smem_u32(buf);
+  const int q = lane & 7;
+  const int col = col0 + q * 4;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const int R = i * 4 + (lane >> 3);
+    if (row0 + R < M && col < N) cp_async16(base + sw_at32(R, q), C + static_cast<long long>(row0 + R) * ldc + col);
+  }
+  cp_async_commit();
+}
+
+__device__ __forceinline__ void read_row_f32(const uint8_t* buf, int lane, float (&v)[32]) {
+#pragma unroll
+  for (int q = 0; q < 8; ++q) {
+    const float4 u = *reinterpret_cast<const float4*>(buf + sw_at32(lane, q));
+    v[q * 4] = u.x; v[q * 4 + 1] = u.y; v[q * 4 + 2] = u.z; v[q * 4 + 3] = u.w;
+  }
+}
+
+__device__ __forceinline__ bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
+
 // D = alpha * acc + beta * C   (C optional, may alias D; D and C bf16 or fp32).
 // Optionally also adds a per-column bias (fp32) before scaling by alpha.
 template <int NB>
@@ -85,7 +164,68 @@ struct EpiLinear {
   const float* bias;
   int M, N;
 
-  __device__ __forceinline__ void operator()(uint32_t taddr, int row, int n0, int, int) const {
+  static constexpr int kSmemPerThread = 256;  // per warp: two 4 KB chunk buffers
+
+  // Warp-coalesced path: D fp32 or bf16, C absent or fp32 (prefetched two chunks ahead).
+  __device__ __forceinline__ void operator()(uint32_t taddr, int row, int n0, int tm, int tn, uint8_t* sm) const {
+    constexpr int kChunks = NB / 32;
+    const bool has_c = C != nullptr && beta != 0.f;
+    const bool fast = aligned16(D) && (d_f32 ? (ldd % 4 == 0 && N % 4 == 0) : (ldd % 8 == 0 && N % 8 == 0)) &&
+                      (!has_c || (c_f32 && aligned16(C) && ldc % 4 == 0));
+    if (!fast) return rowwise(taddr, row, n0);
+    const int lane = static_cast<int>(threadIdx.x & 31);
+    uint8_t* area = sm - lane * kSmemPerThread;
+    const int row0 = row - lane;
+    const float* Cf = static_cast<const float*>(C);
+    if (has_c) {
+      warp_load_f32_async(area, Cf, ldc, row0, n0, M, N, lane);
+      warp_load_f32_async(area + 4096, Cf, ldc, row0, n0 + 32, M, N, lane);
+    }
+#pragma unroll 1
+    for (int c = 0; c < kChunks; ++c) {
+      uint8_t* buf = area + (c & 1) * 4096;
+      const int col0 = n0 + c * 32;
+      uint32_t r[32];
+      tmem_ld32(taddr + c * 32, r);
+      if (has_c) {
+        cp_async_wait<1>();  // this lane's part of chunk c has landed ...
+        __syncwarp();        // ... and every other lane's
+      }
+      tmem_ld_wait();
+      float v[32];
+#pragma unroll
+      for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
+      if (bias != nullptr) {
+#pragma unroll
+        for (int j = 0; j < 32; ++j) v[j] += (col0 + j < N) ? bias[col0 + j] : 0.f;
+      }
+#pragma unroll
+      for (int j = 0; j < 32; ++j) v[j] *= alpha;
+      if (has_c) {
+        float cv[32];
+        read_row_f32(buf, lane, cv);
+#pragma unroll
+        for (int j = 0; j < 32; ++j) v[j] += beta * cv[j];
+        __syncwarp();  // every lane has read its C row before the buffer takes the outputs
+      }
+      if (col0 < N) {
+        if (d_f32)
+          warp_store_f32(buf, v, lane, static_cast<float*>(D), ldd, row0, col0, M, N);
+        else
+          warp_store_bf16(buf, v, lane, static_cast<__nv_bfloat16*>(D), ldd, row0, col0, M, N);
+      }
+      if (has_c) {
+        if (c + 2 < kChunks)
+          warp_load_f32_async(buf, Cf, ldc, row0, n0 + (c + 2) * 32, M, N, lane);
+        else
+          cp_async_commit();  // one group per chunk
+      }
+    }
+    if (has_c) cp_async_wait<0>();
+  }
+
+  // Row-per-thread path for strides or widths the 16-byte pieces cannot cover.
+  __device__ __forceinline__ void rowwise(uint32_t taddr, int row, int n0) const {
 #pragma unroll 1
     for (int c = 0; c < NB / 32; ++c) {
       uint32_t r[32];
@@ -138,8 +278,59 @@ struct EpiBilinear {
   const float* bias_r;
   int mode;
   int M, N;
+  static constexpr int kSmemPerThread = 256;  // per warp: three 2 KB chunk buffers (H, l, r)
 
-  __device__ __forceinline__ void operator()(uint32_t taddr, int row, int n0, int, int) const {
+  // l, r and h of one row chunk from the two accumulators (bias, bf16 rounding of the factors)
+  __device__ __forceinline__ void factors(const uint32_t (&a)[32], const uint32_t (&b)[32], int col0, float (&l)[32],
+                                          float (&r)[32], float (&h)[32]) const {
+#pragma unroll
+    for (int j = 0; j < 32; ++j) {
+      l[j] = __uint_as_float(a[j]);
+      r[j] = __uint_as_float(b[j]);
+    }
+    if (bias_l != nullptr) {
+#pragma unroll
+      for (int j = 0; j < 32; ++j) {
+        l[j] += (col0 + j < N) ? bias_l[col0 + j] : 0.f;
+        r[j] += (col0 + j < N) ? bias_r[col0 + j] : 0.f;
+      }
+    }
+    // The reference rounds l and r to bf16 before multiplying; do the same so that the
+    // saved factors and the product agree exactly with what backward sees.
+#pragma unroll
+    for (int j = 0; j < 32; ++j) {
+      l[j] = __bfloat162float(__float2bfloat16_rn(l[j]));
+      r[j] = __bfloat162float(__float2bfloat16_rn(r[j]));
+      const float g = mode == 1 ? l[j] / (1.f + __expf(-l[j])) : l[j];
+      h[j] = g * r[j];
+    }
+  }
+
+  // Warp-coalesced path (see warp_store_bf16).
+  __device__ __forceinline__ void operator()(uint32_t taddr, int row, int n0, int, int, uint8_t* sm) const {
+    const bool fast = ld % 8 == 0 && N % 8 == 0 && aligned16(H) && (Lo == nullptr || aligned16(Lo)) &&
+                      (Ro == nullptr || aligned16(Ro));
+    if (!fast) return rowwise(taddr, row, n0);
+    const int lane = static_cast<int>(threadIdx.x & 31);
+    uint8_t* area = sm - lane * kSmemPerThread;
+    const int row0 = row - lane;
+#pragma unroll 1
+    for (int c = 0; c < NB / 32; ++c) {
+      uint32_t a[32], b[32];
+      tmem_ld32(taddr + c * 32, a);
+      tmem_ld32(taddr + NB + c * 32, b);
+      tmem_ld_wait();
+      const int col0 = n0 + c * 32;
+      if (col0 >= N) continue;  // the same for the whole warp
+      float l[32], r[32], h[32];
+      factors(a, b, col0, l, r, h);
+      warp_store_bf16(area, h, lane, H, ld, row0, col0, M, N);
+      if (Lo != nullptr) warp_store_bf16(area + 2048, l, lane, Lo, ld, row0, col0, M, N);
+      if (Ro != nullptr) warp_store_bf16(area + 4096, r, lane, Ro, ld, row0, col0, M, N);
+    }
+  }
+
+  __device__ __forceinline__ void rowwise(uint32_t taddr, int row, int n0) const {
 #pragma unroll 1
     for (int c = 0; c < NB / 32; ++c) {
       uint32_t a[32], b[32];
@@ -329,8 +520,53 @@ struct EpiRope {
   const float* cos_t;
   const float* sin_t;
   int M, N;
+  static constexpr int kSmemPerThread = 256;  // per warp: two 2 KB chunk buffers
 
-  __device__ __forceinline__ void operator()(uint32_t taddr, int row, int n0, int, int) const {
+  // Warp-coalesced path (see warp_store_bf16).
+  __device__ __forceinline__ void operator()(uint32_t taddr, int row, int n0, int, int, uint8_t* sm) const {
+    if (!(ldd % 8 == 0 && N % 8 == 0 && aligned16(D))) return rowwise(taddr, row, n0);
+    const int lane = static_cast<int>(threadIdx.x & 31);
+    uint8_t* area = sm - lane * kSmemPerThread;
+    const int row0 = row - lane;
+    const int half = dk / 2;
+    const int p = row < M ? pos[row] : 0;
+#pragma unroll 1
+    for (int c = 0; c < NB / 32; ++c) {
+      const int col0 = n0 + c * 32;
+      if (col0 < rope_cols) {
+        const int o = col0 % dk;  // offset inside the head
+        if (o >= half) continue;  // second half: stored together with its first-half partner
+        const int cb = c + half / 32;
+        uint32_t ra[32], rb[32];
+        tmem_ld32(taddr + c * 32, ra);
+        tmem_ld32(taddr + cb * 32, rb);
+        tmem_ld_wait();
+        if (col0 >= N) continue;
+        float cs[32], sn[32], a[32], b[32];
+        load_row32_f32(cos_t + static_cast<long long>(p) * half + o, (half % 4 == 0), 32, cs);
+        load_row32_f32(sin_t + static_cast<long long>(p) * half + o, (half % 4 == 0), 32, sn);
+#pragma unroll
+        for (int j = 0; j < 32; ++j) {
+          const float x1 = __uint_as_float(ra[j]), x2 = __uint_as_float(rb[j]);
+          a[j] = x1 * cs[j] - x2 * sn[j];
+          b[j] = x1 * sn[j] + x2 * cs[j];
+        }
+        warp_store_bf16(area, a, lane, D, ldd, row0, col0, M, N);
+        warp_store_bf16(area + 2048, b, lane, D, ldd, row0, col0 + half, M, N);
+      } else {
+        uint32_t r[32];
+        tmem_ld32(taddr + c * 32, r);
+        tmem_ld_wait();
+        if (col0 >= N) continue;
+        float v[32];
+#pragma unroll
+        for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
+        warp_store_bf16(area, v, lane, D, ldd, row0, col0, M, N);
+      }
+    }
+  }
+
+  __device__ __forceinline__ void rowwise(uint32_t taddr, int row, int n0) const {
     const bool vec = (ldd % 8 == 0);
     const int half = dk / 2;
     const int p = row < M ? pos[row] : 0;
