@@ -69,8 +69,41 @@ struct EpiCEBwd {
   const float* grad;  // device scalar: upstream gradient of the summed loss
   float alpha;
   int M, N, V;
+  static constexpr int kSmemPerThread = 256;  // per warp: one 2 KB chunk buffer (warp-coalesced stores)
 
-  __device__ __forceinline__ void operator()(uint32_t taddr, int row, int n0, int, int) const {
+  __device__ __forceinline__ void operator()(uint32_t taddr, int row, int n0, int tm, int tn, uint8_t* sm) const {
+    if (!(ldd % 8 == 0 && N % 8 == 0 && (reinterpret_cast<uintptr_t>(dlogits) & 15) == 0))
+      return rowwise(taddr, row, n0);
+    const int lane = static_cast<int>(threadIdx.x & 31);
+    uint8_t* area = sm - lane * kSmemPerThread;
+    const int row0 = row - lane;
+    long long tgt = -1;
+    float l = 0.f, coef = 0.f;
+    if (row < M) {
+      tgt = targets[row];
+      l = lse[row];
+      coef = tgt >= 0 ? grad[0] * alpha : 0.f;
+    }
+#pragma unroll 1
+    for (int c = 0; c < NB / 32; ++c) {
+      uint32_t r[32];
+      tmem_ld32(taddr + c * 32, r);
+      tmem_ld_wait();
+      const int col0 = n0 + c * 32;
+      if (col0 >= N) continue;  // the same for the whole warp
+      float v[32];
+#pragma unroll
+      for (int j = 0; j < 32; ++j) {
+        const int col = col0 + j;
+        float p = col < V ? expf(alpha * __uint_as_float(r[j]) - l) : 0.f;
+        if (col == tgt) p -= 1.f;
+        v[j] = p * coef;
+      }
+      gemm::warp_store_bf16(area, v, lane, dlogits, ldd, row0, col0, M, N);
+    }
+  }
+
+  __device__ __forceinline__ void rowwise(uint32_t taddr, int row, int n0) const {
     long long tgt = -1;
     float l = 0.f, coef = 0.f;
     if (row < M) {
