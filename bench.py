@@ -54,6 +54,8 @@ def parse():
     p.add_argument("--micro-batch", type=int, default=None)
     p.add_argument("--optimizer", default="muon", choices=["muon", "adamw"])
     p.add_argument("--no-e2e", action="store_true")
+    p.add_argument("--global-batch", type=int, default=None,
+                   help="override the preset's global batch (functional runs; the JSON line reports it)")
     p.add_argument("--shard-params", default="auto", choices=["auto", "on", "off"],
                    help="fp32 weights/grads/optimizer state only on owner ranks (auto: when replicated does not fit)")
     return p.parse_args()
@@ -186,6 +188,9 @@ def build_reference(args, device, world):
     ref = os.path.join(ROOT, "baseline", "_ref")
     if not os.path.isdir(os.path.join(ref, "tnlm")):
         raise RuntimeError("reference not installed in baseline/_ref")
+    if args.config == "32b":
+        raise RuntimeError("the reference's stock bench path builds the full fp32 32B model on every rank's CPU "
+                           "(133 GB per rank, over 1 TB for 8 ranks)")
     sys.path.insert(0, ref)
     from tnlm.config import ModelConfig, TrainConfig
     from tnlm.model import TensorLM
@@ -242,6 +247,10 @@ def main():
     try:
         builder = build_ours if args.impl == "ours" else build_reference
         step, cfg, T, gb, n_params, eng = builder(args, device, world)
+        if args.global_batch is not None:
+            if args.global_batch % world:
+                raise SystemExit("--global-batch must be a multiple of the GPU count")
+            gb = args.global_batch
     except Exception as e:  # the reference may not build/run on this stack; say so in one line
         if args.impl == "reference":
             if rank == 0:
