@@ -162,16 +162,26 @@ class ShardedDataParallel:
         load = [0] * self.world
         for i, n in enumerate(sizes):
             load[self.owner[i]] += _aligned(n)
-        self.shard = _aligned(max(load) if load else 0)
+        self.shard = max(_aligned(max(load) if load else 0), ALIGN)
         self.peer = (self.world > 1 and self.backend == "nccl" and device.type == "cuda" and fused
                      and dtype == torch.float32 and os.environ.get("TTB_PEER_COLLECTIVES", "1") != "0")
+        # rank regions of the replicated flat buffers: equal (padded to the largest) for NCCL's
+        # reduce-scatter / all-gather, packed back to back for the peer kernels
+        if self.peer:
+            self._rlen = [_aligned(x) for x in load]
+            self._rstart = [sum(self._rlen[:r]) for r in range(self.world)]
+            self._flat_len = max(sum(self._rlen), ALIGN)
+        else:
+            self._rlen = [self.shard] * self.world
+            self._rstart = [r * self.shard for r in range(self.world)]
+            self._flat_len = self.world * self.shard
         self._cache_mode = self.shard_params and fused  # non-owned weights exist only as bf16 caches
         self._build_sharded_layout(sspec, s_owner)
         if self.peer:
             self._init_symmetric(device, dtype)
         else:
-            self.grad_flat = torch.zeros(self.world * self.shard, device=device, dtype=dtype)
-            self.param_flat = torch.zeros(self.world * self.shard, device=device, dtype=dtype)
+            self.grad_flat = torch.zeros(self._flat_len, device=device, dtype=dtype)
+            self.param_flat = torch.zeros(self._flat_len, device=device, dtype=dtype)
             self.sp_param = torch.zeros(self.s_shard, device=device, dtype=dtype)
             self.stage = (torch.zeros(2 * self.max_bucket, device=device, dtype=torch.float32)
                           if self._cache_mode else None)
@@ -179,7 +189,7 @@ class ShardedDataParallel:
 
         # ---------------------------------------------------------------- storage and values
         dest = {}  # parameter name -> tensor its initial value is copied into (None: placeholder)
-        cursor = [r * self.shard for r in range(self.world)]
+        cursor = list(self._rstart)
         self.units = []
         for (kind, obj, params), n, r in zip(units, sizes, self.owner):
             off = cursor[r]
@@ -255,6 +265,20 @@ class ShardedDataParallel:
             self.max_bucket = max(self.max_bucket, off)
         self.s_shard = max(_aligned(max(gcur) if gcur else 0), ALIGN)
         self.max_bucket = max(self.max_bucket, ALIGN)
+        # Peer transport: every rank reduces an equal slice of every bucket (whole-matrix ownership
+        # would leave one rank pulling two 151M-parameter matrices of a block while the others idle),
+        # into its rd_grad; owners gather their units' pieces from the slice holders once per step.
+        self._rd_len = 0
+        for b in self.buckets:
+            b.cut = [min(b.numel, (b.numel * r // self.world) // ALIGN * ALIGN) for r in range(self.world)]
+            b.cut.append(b.numel)
+            b.rd_off = []  # per rank: offset of its slice of this bucket in that rank's rd_grad
+        rcur = [0] * self.world
+        for b in self.buckets:
+            for r in range(self.world):
+                b.rd_off.append(rcur[r])
+                rcur[r] += b.cut[r + 1] - b.cut[r]
+        self._rd_len = max(max(rcur) if rcur else 0, ALIGN)
         self._owned_units = [su for su in self.sunits if su.owner == self.rank]
 
     @torch.no_grad()
@@ -309,7 +333,7 @@ class ShardedDataParallel:
         enable = getattr(symm_mem, "enable_symm_mem_for_group", None)
         if enable is not None:
             enable(group.group_name)
-        n = self.world * self.shard
+        n = self._flat_len
         self.grad_flat = symm_mem.empty(n, dtype=dtype, device=device)
         self.param_flat = symm_mem.empty(n, dtype=dtype, device=device)
         self.grad_flat.zero_()
@@ -332,6 +356,12 @@ class ShardedDataParallel:
             self.stage.zero_()
             ht = symm_mem.rendezvous(self.stage, group)
             self._stptrs = [int(x) for x in ht.buffer_ptrs]
+            # this rank's reduction slices of every block, accumulated over the micro-batches
+            self.rd_grad = symm_mem.empty(self._rd_len, dtype=torch.float32, device=device)
+            self.rd_grad.zero_()
+            hr = symm_mem.rendezvous(self.rd_grad, group)
+            self._rdptrs = [int(x) for x in hr.buffer_ptrs]
+            handles.append(hr)
             # the per-block reductions run on their own stream, beside the next block's backward,
             # with their own barrier pads and epochs (independent of the compute-stream barriers)
             self._stpads = [int(x) for x in ht.signal_pad_ptrs]
@@ -370,6 +400,22 @@ class ShardedDataParallel:
         self._segs = torch.tensor(rows, dtype=torch.int64).to(self.param_flat.device) if rows else None
         self._seg_max = max_n
         self._lib = lib
+        # owned units' gradients from the reduction slices: piece [x0, x1) of a unit's staging range
+        # held by rank q sits at rd_off(q) + x0 - cut(q) of q's rd_grad
+        segs, seg_max = [], 0
+        if self.shard_params:
+            sp = self.sp_grad.data_ptr()
+            for su in self._owned_units:
+                b = self.buckets[su.bucket]
+                u0, u1 = su.stage_off, su.stage_off + _aligned(su.n)
+                for q in range(self.world):
+                    x0, x1 = max(u0, b.cut[q]), min(u1, b.cut[q + 1])
+                    if x1 > x0:
+                        segs.append((self._rdptrs[q] + 4 * (b.rd_off[q] + x0 - b.cut[q]),
+                                     sp + 4 * (su.goff + x0 - u0), 0, x1 - x0))
+                        seg_max = max(seg_max, x1 - x0)
+        self._rd_segs = torch.tensor(segs, dtype=torch.int64).to(self.param_flat.device) if segs else None
+        self._rd_seg_max = seg_max
 
     def _stage_barrier(self):
         self._st_epoch += 1
@@ -394,7 +440,8 @@ class ShardedDataParallel:
         return {id(p) for p in self.owned_params()}
 
     def region(self, flat: torch.Tensor) -> torch.Tensor:
-        return flat[self.rank * self.shard:(self.rank + 1) * self.shard]
+        start = self._rstart[self.rank]
+        return flat[start:start + self._rlen[self.rank]]
 
     def sharded_names(self) -> set[str]:
         """Parameters held only by their owner (parameter-sharded mode)."""
@@ -449,11 +496,13 @@ class ShardedDataParallel:
                 # has read it); the compute stream waits for that before it writes the slot again
                 written = torch.cuda.Event()
                 written.record()
+                lo_r, hi_r = b.cut[self.rank], b.cut[self.rank + 1]
+                rd = b.rd_off[self.rank]
                 with torch.cuda.stream(self._comm):
                     self._comm.wait_event(written)
                     self._stage_barrier()
-                    if n:
-                        self._lib().rs_accumulate(self._stptrs, slot + lo, self.sp_grad[goff:goff + n],
+                    if hi_r > lo_r:
+                        self._lib().rs_accumulate(self._stptrs, slot + lo_r, self.rd_grad[rd:rd + hi_r - lo_r],
                                                   PULL_BLOCKS)
                     self._stage_barrier()
                     free = torch.cuda.Event()
@@ -504,6 +553,8 @@ class ShardedDataParallel:
                 pos += p.numel()
         if self.shard_params:
             self.sp_grad.zero_()
+            if self.peer:
+                self.rd_grad.zero_()
             for su in self.sunits:
                 for p in su.params:
                     p.grad = None
@@ -515,8 +566,14 @@ class ShardedDataParallel:
         """Sum gradients over ranks; afterwards this rank's region holds its owned units' sums
         (sharded units were reduced layer by layer during backward)."""
         if self.shard_params:
-            if self.peer:  # the per-block reductions have landed in sp_grad
+            if self.peer:
+                # the per-block reductions have landed in every rank's rd_grad: owners gather the
+                # pieces of their units from the slice holders, then no rank zeroes rd_grad early
                 torch.cuda.current_stream().wait_stream(self._comm)
+                self._stage_barrier()
+                if self._rd_segs is not None:
+                    self._lib().ag_pull_cast(self._rd_segs, self._rd_seg_max)
+                self._stage_barrier()
             for su in self._owned_units:
                 pos = su.goff
                 for p in su.params:
@@ -527,8 +584,11 @@ class ShardedDataParallel:
         self._sq = None
         if self.peer:
             self._barrier()  # every rank's backward has finished writing its buffer
-            partial = self._lib().rs_reduce_sq(self._gptrs, self.rank * self.shard, self.region(self.grad_flat))
-            self._sq = partial.sum()
+            mine = self.region(self.grad_flat)
+            if mine.numel():
+                self._sq = self._lib().rs_reduce_sq(self._gptrs, self._rstart[self.rank], mine).sum()
+            else:
+                self._sq = torch.zeros((), device=self.device, dtype=torch.float64)
         elif self.backend == "nccl":
             dist.reduce_scatter_tensor(self.region(self.grad_flat), self.grad_flat, group=self.group)
         else:
