@@ -231,7 +231,8 @@ void embed_bwd(const Tensor& idx, const Tensor& dx, Tensor& dW) {
 
 // ------------------------------------------------------------------ fused linear + CE
 // returns (loss_rows [M] fp32, lse [M] fp32)
-std::vector<Tensor> ce_fwd(const Tensor& x, const Tensor& w, int64_t V, double alpha, const Tensor& targets) {
+std::vector<Tensor> ce_fwd(const Tensor& x, const Tensor& w, int64_t V, double alpha, const Tensor& targets,
+                           const c10::optional<Tensor>& zout) {
   const c10::cuda::CUDAGuard guard(x.device());
   const auto X = a_operand(x);
   const auto W = b_operand(w.t());
@@ -245,10 +246,39 @@ std::vector<Tensor> ce_fwd(const Tensor& x, const Tensor& w, int64_t V, double a
   auto tlogit = torch::zeros({M}, opts);
   auto lse = torch::empty({M}, opts);
   auto loss = torch::empty({M}, opts);
+  float* zp = nullptr;
+  long long ldz = 0;
+  int Npad = 0;
+  if (zout.has_value()) {
+    TORCH_CHECK(zout->scalar_type() == torch::kFloat32 && zout->dim() == 2 && zout->size(0) == M &&
+                    zout->stride(1) == 1 && zout->size(1) >= V,
+                "zout: fp32 [M, >=V] with unit column stride");
+    zp = zout->data_ptr<float>();
+    ldz = zout->stride(0);
+    Npad = static_cast<int>(zout->size(1));
+  }
   ttb::ce_forward(X, W, M, V, K, static_cast<float>(alpha), reinterpret_cast<const long long*>(targets.data_ptr<int64_t>()), pmax.data_ptr<float>(),
                   psum.data_ptr<float>(), tlogit.data_ptr<float>(), lse.data_ptr<float>(), loss.data_ptr<float>(),
-                  cur_stream());
+                  cur_stream(), zp, ldz, Npad);
   return {loss, lse};
+}
+
+void ce_bwd_from_logits(const Tensor& z, double alpha, const Tensor& targets, const Tensor& lse, const Tensor& grad,
+                        Tensor& dlogits) {
+  const c10::cuda::CUDAGuard guard(z.device());
+  TORCH_CHECK(z.scalar_type() == torch::kFloat32 && z.dim() == 2 && z.stride(1) == 1, "z: fp32 [M, Npad]");
+  check_bf16(dlogits, "dlogits");
+  const int M = z.size(0), Npad = z.size(1);
+  TORCH_CHECK(dlogits.dim() == 2 && dlogits.size(0) == M && dlogits.size(1) == Npad && dlogits.stride(1) == 1,
+              "dlogits: bf16 [M, Npad]");
+  TORCH_CHECK(targets.scalar_type() == torch::kInt64 && targets.is_contiguous() && targets.numel() == M, "targets");
+  TORCH_CHECK(lse.scalar_type() == torch::kFloat32 && lse.is_contiguous() && lse.numel() == M, "lse");
+  TORCH_CHECK(grad.scalar_type() == torch::kFloat32 && grad.numel() == 1, "grad: fp32 scalar");
+  TORCH_CHECK(reinterpret_cast<uintptr_t>(z.data_ptr()) % 16 == 0 && reinterpret_cast<uintptr_t>(dlogits.data_ptr()) % 8 == 0,
+              "alignment");
+  ttb::ce_backward_from_logits(z.data_ptr<float>(), z.stride(0), M, Npad, static_cast<float>(alpha),
+                               reinterpret_cast<const long long*>(targets.data_ptr<int64_t>()), lse.data_ptr<float>(),
+                               grad.data_ptr<float>(), dlogits.data_ptr(), dlogits.stride(0), cur_stream());
 }
 
 void ce_bwd_logits(const Tensor& x, const Tensor& w, int64_t V, double alpha, const Tensor& targets, const Tensor& lse,
@@ -399,7 +429,9 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("rope_", &rope_, "in-place rotary embedding (or its inverse) on a bf16 [N, ld] buffer");
   m.def("embed_fwd", &embed_fwd, "fp32 embedding gather");
   m.def("embed_bwd", &embed_bwd, "deterministic embedding backward (accumulates into dW)");
-  m.def("ce_fwd", &ce_fwd, "fused linear + cross-entropy forward: per-row loss and lse");
+  m.def("ce_fwd", &ce_fwd, "fused linear + cross-entropy forward: per-row loss and lse", py::arg("x"), py::arg("w"),
+        py::arg("V"), py::arg("alpha"), py::arg("targets"), py::arg("zout") = py::none());
+  m.def("ce_bwd_from_logits", &ce_bwd_from_logits, "softmax-grad dlogits from the logits the forward kept");
   m.def("ce_bwd_logits", &ce_bwd_logits, "fused logits recompute + softmax-grad epilogue");
   m.def("poly_fwd", &poly_fwd, "tcgen05 polynomial attention forward");
   m.def("poly_bwd", &poly_bwd, "tcgen05 polynomial attention backward (dq and dkv kernels)", py::arg("kind"),

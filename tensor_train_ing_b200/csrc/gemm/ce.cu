@@ -26,8 +26,14 @@ struct EpiCEFwd {
   const long long* targets;
   float alpha;
   int M, V;
+  float* zout;     // optional: the scaled logits [M, Npad] (fp32, -inf past V), kept for the backward
+  long long ldz;
+  int Npad;
+  static constexpr int kSmemPerThread = 256;  // per warp: one 4 KB chunk buffer for the logit stores
 
-  __device__ __forceinline__ void operator()(uint32_t taddr, int row, int n0, int, int tn) const {
+  __device__ __forceinline__ void operator()(uint32_t taddr, int row, int n0, int, int tn, uint8_t* sm) const {
+    const int lane = static_cast<int>(threadIdx.x & 31);
+    uint8_t* area = sm - lane * kSmemPerThread;
     const long long tgt = row < M ? targets[row] : -1;
     float m = -CUDART_INF_F, s = 0.f, tz = 0.f;
 #pragma unroll 1
@@ -44,6 +50,7 @@ struct EpiCEFwd {
         cmax = fmaxf(cmax, z[j]);
         if (col0 + j == tgt) tz = z[j];
       }
+      if (zout != nullptr && col0 < Npad) gemm::warp_store_f32(area, z, lane, zout, ldz, row - lane, col0, M, Npad);
       const float nm = fmaxf(m, cmax);
       if (nm == -CUDART_INF_F) continue;
       float cs = 0.f;
@@ -132,6 +139,32 @@ struct EpiCEBwd {
   }
 };
 
+// dlogits from the logits the forward kept: one block per row, float4 in, four bf16 out.
+__global__ void __launch_bounds__(256) ce_grad_from_logits_kernel(const float* __restrict__ z, long long ldz,
+                                                                  const float* __restrict__ lse,
+                                                                  const long long* __restrict__ targets,
+                                                                  const float* __restrict__ grad, float alpha, int M,
+                                                                  int Npad, __nv_bfloat16* __restrict__ dlog,
+                                                                  long long ldd) {
+  const int row = blockIdx.x;
+  if (row >= M) return;
+  const float l = lse[row];
+  const long long t = targets[row];
+  const float coef = t >= 0 ? grad[0] * alpha : 0.f;
+  const float4* zr = reinterpret_cast<const float4*>(z + static_cast<long long>(row) * ldz);
+  uint2* dr = reinterpret_cast<uint2*>(dlog + static_cast<long long>(row) * ldd);
+  for (int i = threadIdx.x; i < Npad / 4; i += blockDim.x) {
+    const float4 v = __ldcs(zr + i);  // read once: stream past L2
+    float p[4] = {expf(v.x - l), expf(v.y - l), expf(v.z - l), expf(v.w - l)};
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      if (4LL * i + k == t) p[k] -= 1.f;
+      p[k] *= coef;
+    }
+    dr[i] = make_uint2(pack_bf16(p[0], p[1]), pack_bf16(p[2], p[3]));
+  }
+}
+
 __global__ void ce_combine_kernel(const float* __restrict__ pmax, const float* __restrict__ psum, long long ldp,
                                   int tiles, const float* __restrict__ tlogit, const long long* __restrict__ targets,
                                   float* __restrict__ lse, float* __restrict__ loss_row, int M) {
@@ -162,13 +195,24 @@ __global__ void ce_combine_kernel(const float* __restrict__ pmax, const float* _
 int ce_num_tiles(int V) { return (V + 255) / 256; }
 
 void ce_forward(const Operand& x, const Operand& w, int M, int V, int K, float alpha, const long long* targets,
-                float* pmax, float* psum, float* tlogit, float* lse, float* loss_row, cudaStream_t stream) {
+                float* pmax, float* psum, float* tlogit, float* lse, float* loss_row, cudaStream_t stream, float* zout,
+                long long ldz, int Npad) {
   TTB_CHECK(M > 0 && V > 0 && K > 0, "empty CE");
+  TTB_CHECK(zout == nullptr || (Npad >= V && Npad % 4 == 0 && ldz % 4 == 0 && (reinterpret_cast<uintptr_t>(zout) & 15) == 0),
+            "CE logits buffer: width and stride multiples of 4, 16-byte aligned");
   const int tiles = ce_num_tiles(V);
-  gemm::EpiCEFwd<256> epi{pmax, psum, tiles, tlogit, targets, alpha, M, V};
+  gemm::EpiCEFwd<256> epi{pmax, psum, tiles, tlogit, targets, alpha, M, V, zout, ldz, Npad};
   gemm::dispatch<256, 4, false>(x, w, nullptr, gemm::Shape{M, V, K, status_ptr()}, epi, stream);
   const int grid = (M + 7) / 8 < 4 * num_sms() ? (M + 7) / 8 : 4 * num_sms();
   gemm::ce_combine_kernel<<<grid, 256, 0, stream>>>(pmax, psum, tiles, tiles, tlogit, targets, lse, loss_row, M);
+  TTB_CUDA_CHECK(cudaGetLastError());
+}
+
+void ce_backward_from_logits(const float* z, long long ldz, int M, int Npad, float alpha, const long long* targets,
+                             const float* lse, const float* grad, void* dlogits, long long ldd, cudaStream_t stream) {
+  TTB_CHECK(M > 0 && Npad % 4 == 0 && ldz % 4 == 0 && ldd % 4 == 0, "CE backward from logits: widths and strides");
+  gemm::ce_grad_from_logits_kernel<<<M, 256, 0, stream>>>(z, ldz, lse, targets, grad, alpha, M, Npad,
+                                                          static_cast<__nv_bfloat16*>(dlogits), ldd);
   TTB_CUDA_CHECK(cudaGetLastError());
 }
 

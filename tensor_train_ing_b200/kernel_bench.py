@@ -5,7 +5,7 @@
 
 Cases (shapes of one 1B micro-batch, 8 x 2048 tokens, unless noted): gemm_qkv, gemm_dx, gemm_dw,
 bilinear, bilinear_grad, attn_fwd, attn_bwd, attn_case (B=2 for profiling), rmsnorm_fwd,
-rmsnorm_bwd, ce_fwd, ce_bwd.  Every input is larger than the 126 MB L2 or is flushed: ``time``
+rmsnorm_bwd, ce_fwd, ce_bwd, ce_bwd_kept.  Every input is larger than the 126 MB L2 or is flushed: ``time``
 writes a 256 MB buffer between timed launches.  ``TTB_GEMM_PAIR=0`` selects the one-CTA GEMM.
 The attention timings are the measurements the reference's kernel tuner makes for its Triton
 configurations (reference tnlm/kernels/tune.py:20-62); the tile shapes here are fixed per kernel.
@@ -98,6 +98,15 @@ def build(name: str) -> _Case:
         dres = torch.zeros_like(x)
         g16 = torch.empty(N, D, device="cuda", dtype=torch.bfloat16)
         return _Case(lambda: C.rmsnorm_bwd(y, x, w, rstd, dres, True, 1, g16, 1.0), 0, N * D * (4 + 2 + 8 + 2))
+    if name == "ce_bwd_kept":  # the elementwise backward from logits the forward kept
+        x = torch.randn(N // 2, D, device="cuda").bfloat16()
+        w = (torch.randn(V, D, device="cuda") * 0.02).bfloat16()
+        t = torch.randint(0, 50257, (N // 2,), device="cuda")
+        z = torch.empty(N // 2, V, device="cuda")
+        _, lse = C.ce_fwd(x, w, 50257, 1.0, t, z)
+        g = torch.ones(1, device="cuda")
+        dl = torch.empty(N // 2, V, device="cuda", dtype=torch.bfloat16)
+        return _Case(lambda: C.ce_bwd_from_logits(z, 1.0, t, lse, g, dl), 0, (N // 2) * V * (4 + 2))
     if name in ("ce_fwd", "ce_bwd"):
         x = torch.randn(N // 2, D, device="cuda").bfloat16()
         w = (torch.randn(V, D, device="cuda") * 0.02).bfloat16()
@@ -113,7 +122,7 @@ def build(name: str) -> _Case:
 
 
 CASES = ["gemm_qkv", "gemm_dx", "gemm_dw", "bilinear", "bilinear_grad", "attn_fwd", "attn_bwd", "rmsnorm_fwd",
-         "rmsnorm_bwd", "ce_fwd", "ce_bwd"]
+         "rmsnorm_bwd", "ce_fwd", "ce_bwd", "ce_bwd_kept"]
 
 
 def time_case(name: str, reps: int = 10) -> dict:

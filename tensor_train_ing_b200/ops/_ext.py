@@ -16,7 +16,7 @@ _PROXY = None
 KERNELS_PER_CALL = {"mm": 1, "bilinear": 1, "bilinear_grad": 1, "rmsnorm_fwd": 1, "rmsnorm_bwd": 2, "rope_": 1,
                     "embed_fwd": 1, "embed_bwd": 1, "ce_fwd": 2, "ce_bwd_logits": 1, "poly_fwd": 1,
                     "poly_bwd": 2, "qkv_rope": 1, "peer_barrier": 1, "rs_reduce_sq": 1, "ag_pull_cast": 1,
-                    "rs_accumulate": 1}
+                    "rs_accumulate": 1, "ce_bwd_from_logits": 1}
 
 
 class _Counting:

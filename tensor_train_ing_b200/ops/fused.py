@@ -309,28 +309,38 @@ def embedding(idx, group):
 class LinearCEFn(torch.autograd.Function):
     """Summed cross-entropy of (alpha * x W[:V]^T) against targets (-100 ignored), chunked over rows.
 
-    Forward keeps only the per-row log-sum-exp; backward recomputes each chunk's logits in the
-    GEMM and writes bf16 dlogits (padded to W's rows), then dx = dlogits W, dW += dlogits^T x."""
+    Forward keeps the per-row log-sum-exp and, while they fit in ``KEEP_LOGITS_BYTES``, the fp32
+    logits its GEMM epilogue already holds (written warp-coalesced beside the online LSE): the
+    backward then forms bf16 dlogits in one elementwise pass instead of recomputing every chunk's
+    logits with a second GEMM.  Otherwise the backward recomputes them in the GEMM.  Either way
+    dx = dlogits W and dW += dlogits^T x follow."""
+
+    KEEP_LOGITS_BYTES = 8 << 30
 
     @staticmethod
     def forward(ctx, x, targets, group, V, alpha, chunk, weight):
         w16 = group.bf16()
         N = x.shape[0]
+        Vp = w16.shape[0]
         lse = torch.empty(N, device=x.device, dtype=torch.float32)
         total = torch.zeros((), device=x.device, dtype=torch.float32)
+        keep = N * Vp * 4 <= LinearCEFn.KEEP_LOGITS_BYTES and Vp % 4 == 0 and any(ctx.needs_input_grad)
+        z = torch.empty(N, Vp, device=x.device, dtype=torch.float32) if keep else None
         for s in range(0, N, chunk):
             e = min(N, s + chunk)
-            loss_rows, l = lib().ce_fwd(x[s:e], w16, int(V), float(alpha), targets[s:e])
+            loss_rows, l = lib().ce_fwd(x[s:e], w16, int(V), float(alpha), targets[s:e],
+                                        z[s:e] if keep else None)
             lse[s:e] = l
             total += loss_rows.sum()
         ctx.save_for_backward(x, targets, lse)
-        ctx.group, ctx.V, ctx.alpha, ctx.chunk = group, V, alpha, chunk
+        ctx.group, ctx.V, ctx.alpha, ctx.chunk, ctx.z = group, V, alpha, chunk, z
         return total
 
     @staticmethod
     def backward(ctx, g):
         x, targets, lse = ctx.saved_tensors
-        group, V, alpha, chunk = ctx.group, ctx.V, ctx.alpha, ctx.chunk
+        group, V, alpha, chunk, z = ctx.group, ctx.V, ctx.alpha, ctx.chunk, ctx.z
+        ctx.z = None
         w16 = group.bf16()
         Vp = w16.shape[0]
         g32 = g.detach().float().reshape(1).contiguous()
@@ -344,7 +354,10 @@ class LinearCEFn(torch.autograd.Function):
             for s in range(0, N, chunk):
                 e = min(N, s + chunk)
                 d = dlog[: e - s]
-                lib().ce_bwd_logits(x[s:e], w16, int(V), float(alpha), targets[s:e], lse[s:e], g32, d)
+                if z is not None:
+                    lib().ce_bwd_from_logits(z[s:e], float(alpha), targets[s:e], lse[s:e], g32, d)
+                else:
+                    lib().ce_bwd_logits(x[s:e], w16, int(V), float(alpha), targets[s:e], lse[s:e], g32, d)
                 _mm(d, w16, dx[s:e])
                 _mm(d.t(), x[s:e], out, c=out, beta=beta if s == 0 else 1.0)
 

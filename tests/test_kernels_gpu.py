@@ -198,3 +198,40 @@ def test_embedding_deterministic_backward():
     W.grad = None
     fused.embedding(idx, grp).backward(g)
     assert torch.equal(W.grad, first)  # bitwise run-to-run determinism
+
+
+def test_ce_backward_from_kept_logits_equals_recompute():
+    """dlogits from the logits the forward kept == dlogits recomputed by the backward GEMM, and the
+    two autograd paths give the same gradients."""
+    torch.manual_seed(4)
+    from tensor_train_ing_b200.ops._ext import lib
+    from tensor_train_ing_b200.ops.weights import WeightGroup
+    N, d, V, Vp = 300, 256, 1000, 1024
+    x = torch.randn(N, d, device="cuda").bfloat16()
+    w16 = (torch.randn(Vp, d, device="cuda") * 0.05).bfloat16()
+    tgt = torch.randint(0, V, (N,), device="cuda")
+    tgt[::5] = -100
+    z = torch.full((N, Vp), float("nan"), device="cuda")
+    _, lse = lib().ce_fwd(x, w16, V, 0.5, tgt, z)
+    assert torch.isinf(z[:, V:]).all() and torch.isfinite(z[:, :V]).all()
+    g = torch.full((1,), 0.25, device="cuda")
+    d1 = torch.empty(N, Vp, device="cuda", dtype=torch.bfloat16)
+    d2 = torch.empty_like(d1)
+    lib().ce_bwd_logits(x, w16, V, 0.5, tgt, lse, g, d1)
+    lib().ce_bwd_from_logits(z, 0.5, tgt, lse, g, d2)
+    assert (d1.float() - d2.float()).abs().max().item() <= 1e-6
+    grads = []
+    for keep in (8 << 30, 0):
+        fused.LinearCEFn.KEEP_LOGITS_BYTES = keep
+        try:
+            w = torch.nn.Parameter(w16.float())
+            xg = x.clone().requires_grad_()
+            loss = fused.linear_cross_entropy(xg, tgt, WeightGroup([w]), V, alpha=0.5, chunk=128)
+            loss.backward()
+            grads.append((loss.detach(), xg.grad, w.grad))
+        finally:
+            fused.LinearCEFn.KEEP_LOGITS_BYTES = 8 << 30
+    for a, b in zip(grads[0], grads[1]):
+        assert (a.float() - b.float()).abs().max().item() <= 1e-5 * max(1.0, b.float().abs().max().item())
+    torch.cuda.synchronize()
+    assert lib().status() == 0
