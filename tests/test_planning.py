@@ -1,0 +1,199 @@
+"""Schedules, checkpoint planning / disk admission, optimizer exposure bookkeeping and the throughput
+canary (CPU)."""
+import errno
+import json
+import math
+from collections import namedtuple
+
+import pytest
+import torch
+
+from helpers import TINY_MODEL
+from tensor_train_ing_b200 import checkpoint_storage
+from tensor_train_ing_b200.checkpoint_plan import (checkpoint_retention_policy, checkpoint_storage_plan,
+                                                   milestone_policy, pending_milestone_tokens)
+from tensor_train_ing_b200.checkpoint_storage import (RESERVE_BYTES, checkpoint_space_estimate,
+                                                      require_checkpoint_space)
+from tensor_train_ing_b200.config import Config, ModelConfig, TrainConfig
+from tensor_train_ing_b200.models.model import TensorLM
+from tensor_train_ing_b200.optim import make_optimizer
+from tensor_train_ing_b200.optimizer_exposure import update_optimizer_exposure
+from tensor_train_ing_b200.schedules import (COSINE, CONSTANT, lr_multiplier, schedule_multiplier, schedule_steps,
+                                             validate_schedule)
+from tensor_train_ing_b200.throughput_canary import ThroughputCanary
+
+
+# ------------------------------------------------------------------------------------- schedules
+def test_warmup_is_max_of_100_and_one_percent():
+    assert validate_schedule(CONSTANT, 50) == 100
+    assert validate_schedule(CONSTANT, 10_000) == 100
+    assert validate_schedule(CONSTANT, 10_001) == 101
+    assert validate_schedule(COSINE, 30_000) == 300
+    assert schedule_steps(1000, 7) == 143
+
+
+def test_constant_schedule_ramps_then_holds():
+    total = 1000
+    assert schedule_multiplier(0, total) == pytest.approx(1 / 100)
+    assert schedule_multiplier(49, total) == pytest.approx(0.5)
+    assert schedule_multiplier(99, total) == 1.0
+    assert schedule_multiplier(999, total) == 1.0
+    assert lr_multiplier(99, total) == 1.0  # the same warm-up rule without a cooldown
+
+
+def test_cosine_reaches_zero_at_the_last_update_and_is_monotone_after_warmup():
+    total = 400
+    vals = [schedule_multiplier(s, total, schedule=COSINE) for s in range(total)]
+    assert vals[99] == 1.0 and vals[-1] == 0.0
+    assert all(a >= b for a, b in zip(vals[100:], vals[101:]))
+    mid = 100 + (total - 100) // 2 - 1
+    assert vals[mid] == pytest.approx(0.5 * (1 + math.cos(math.pi * (mid + 1 - 100) / 300)))
+    with pytest.raises(ValueError):
+        schedule_multiplier(total, total, schedule=COSINE)
+    with pytest.raises(ValueError):
+        validate_schedule(COSINE, 100)  # no room after warm-up
+    with pytest.raises(ValueError):
+        validate_schedule(COSINE, 400, cooldown_steps=10)
+
+
+def test_cooldown_decays_linearly_to_zero():
+    assert lr_multiplier(0, 1000, cooldown_steps=10) == 1.0
+    assert lr_multiplier(5, 1000, cooldown_steps=10) == 0.5
+    assert lr_multiplier(10, 1000, cooldown_steps=10) == 0.0
+    assert lr_multiplier(20, 1000, cooldown_steps=10) == 0.0
+    with pytest.raises(ValueError):
+        lr_multiplier(0, 1000, cooldown_steps=0)
+
+
+@pytest.mark.parametrize("bad", [0, -1, 1.5, True])
+def test_schedule_rejects_non_positive_integer_horizons(bad):
+    with pytest.raises(ValueError):
+        schedule_steps(bad, 7)
+
+
+# ------------------------------------------------------------------------ checkpoint planning
+def _cfg(project=None, **train):
+    return Config(model=ModelConfig(**TINY_MODEL),
+                  train=TrainConfig(global_prediction_tokens_per_update=1_000_000, rung_total_tokens=250_000_000,
+                                    **train),
+                  raw={"project": project or {}})
+
+
+def test_default_milestones_double_then_every_100m():
+    got = list(pending_milestone_tokens(_cfg(), start_tokens=0, token_limit=250_000_000))
+    assert got == [1_000_000, 2_000_000, 4_000_000, 8_000_000, 16_000_000, 32_000_000, 100_000_000, 200_000_000]
+    resumed = list(pending_milestone_tokens(_cfg(), start_tokens=8_000_000, token_limit=150_000_000))
+    assert resumed == [16_000_000, 32_000_000, 100_000_000]
+    branch = list(pending_milestone_tokens(_cfg(), start_tokens=0, token_limit=250_000_000, include_branch=True))
+    assert 225_000_000 in branch and branch == sorted(set(branch))
+
+
+def test_explicit_milestones_and_retention_policy_validation():
+    cfg = _cfg({"milestone_tokens": [5, 3, 3, 9], "keep_recovery_checkpoints": 4, "save_initial_checkpoint": False})
+    assert milestone_policy(cfg) == {"mode": "explicit", "tokens": [3, 5, 9]}
+    assert list(pending_milestone_tokens(cfg, start_tokens=3, token_limit=100)) == [5, 9]
+    assert checkpoint_retention_policy(cfg) == {"keep_recovery_checkpoints": 4, "save_initial_checkpoint": False}
+    with pytest.raises(ValueError):
+        milestone_policy(_cfg({"milestone_tokens": [0]}))
+    with pytest.raises(ValueError):
+        checkpoint_retention_policy(_cfg({"save_initial_checkpoint": "yes"}))
+
+
+def test_storage_plan_counts_parameters_moments_and_checkpoints():
+    cfg = _cfg(optimizer="adamw")
+    plan = checkpoint_storage_plan(cfg)
+    model = TensorLM(cfg.model)
+    params = sum(p.numel() * p.element_size() for p in model.parameters())
+    br = plan["tensor_bytes_breakdown"]
+    assert br["parameters"] == params
+    assert br["optimizer_moments"] == 2 * params  # AdamW: two fp32 moments per parameter
+    assert plan["checkpoint_count"] == sum(plan["count_breakdown"].values())
+    assert plan["required_additional_bytes"] >= plan["per_checkpoint_estimate_bytes"] * plan["checkpoint_count"]
+    muon = checkpoint_storage_plan(_cfg(optimizer="muon"))
+    assert muon["tensor_bytes_breakdown"]["optimizer_moments"] < br["optimizer_moments"]  # one moment on matrices
+    dist_plan = checkpoint_storage_plan(cfg, distributed=True, distributed_world_size=4)
+    assert dist_plan["tensor_bytes_breakdown"]["distributed_shard_padding_allowance"] > 0
+    with pytest.raises(ValueError):
+        checkpoint_storage_plan(cfg, distributed_world_size=2)  # serial plan with a world size
+
+
+def test_space_estimate_counts_shared_storage_once():
+    a = torch.zeros(1000)
+    once = checkpoint_space_estimate({"x": a})
+    twice = checkpoint_space_estimate({"x": a, "view": a[10:20], "alias": a})
+    assert twice - once < 1000  # only pickle metadata grows
+    bigger = checkpoint_space_estimate({"x": a, "y": torch.zeros(1000)})
+    assert bigger - once >= 4000
+    with pytest.raises(ValueError):
+        checkpoint_space_estimate({"m": torch.empty(3, device="meta")})
+
+
+def test_disk_admission_keeps_a_reserve(tmp_path, monkeypatch):
+    usage = namedtuple("usage", "total used free")
+    monkeypatch.setattr(checkpoint_storage.shutil, "disk_usage", lambda p: usage(10 ** 12, 0, RESERVE_BYTES + 100))
+    info = require_checkpoint_space(tmp_path / "not" / "yet" / "there", 100)
+    assert info["free_bytes"] == RESERVE_BYTES + 100
+    with pytest.raises(OSError) as exc:
+        require_checkpoint_space(tmp_path, 101)
+    assert exc.value.errno == errno.ENOSPC
+    with pytest.raises(ValueError):
+        require_checkpoint_space(tmp_path, -1)
+
+
+# ------------------------------------------------------------------------- optimizer exposure
+def test_exposure_accumulates_lr_and_decay_shrinkage():
+    torch.manual_seed(0)
+    model = TensorLM(ModelConfig(**TINY_MODEL))
+    opt = make_optimizer(model, TrainConfig(optimizer="adamw", lr=0.01, weight_decay_hidden=0.1))
+    progress = {"steps": 0, "tokens": 0}
+    for step in range(3):
+        for g in opt.param_groups:
+            g["lr"] = 0.01 * (step + 1)
+        update_optimizer_exposure(progress, opt)
+        progress["steps"] += 1
+    exp = progress["optimizer_exposure"]
+    assert exp["observed_steps"] == 3 and exp["complete_history"]
+    hidden = exp["groups"][0]
+    assert hidden["sum_lr"] == pytest.approx(0.06)
+    assert hidden["sum_lr_weight_decay"] == pytest.approx(0.006)
+    want = sum(math.log1p(-0.01 * k * 0.1) for k in (1, 2, 3))
+    assert hidden["shrinkage_log_abs"] == pytest.approx(want)
+    json.dumps(exp, allow_nan=False)
+    progress["steps"] += 5  # a gap in the observed history is refused
+    with pytest.raises(ValueError):
+        update_optimizer_exposure(progress, opt)
+
+
+def test_exposure_covers_both_muon_and_adamw_children():
+    model = TensorLM(ModelConfig(**TINY_MODEL))
+    opt = make_optimizer(model, TrainConfig(optimizer="muon", lr=0.02, aux_adamw_lr=0.003))
+    exp = update_optimizer_exposure({"steps": 0, "tokens": 0}, opt)
+    kinds = [g["identity"]["optimizer_kind"] for g in exp["groups"]]
+    assert kinds[0] == "muon" and "adamw" in kinds
+
+
+# --------------------------------------------------------------------------- throughput canary
+def test_canary_passes_on_fast_updates_and_publishes(tmp_path):
+    out = tmp_path / "canary.json"
+    c = ThroughputCanary(2, 100.0, 1, output_path=out)
+    c.observe({"step": 1, "prediction_tokens": 10, "seconds": 100.0})  # warm-up: ignored
+    c.observe({"step": 2, "prediction_tokens": 1000, "seconds": 1.0})
+    c.observe({"step": 3, "prediction_tokens": 1000, "seconds": 1.0})
+    assert c.status == "passed" and c.require_complete()["tokens_per_second"] == 1000.0
+    assert json.loads(out.read_text())["status"] == "passed"
+
+
+def test_canary_fails_loudly_when_slow_or_incomplete(tmp_path):
+    c = ThroughputCanary(1, 1e9, 0)
+    with pytest.raises(RuntimeError):
+        c.observe({"step": 1, "prediction_tokens": 10, "seconds": 1.0})
+    assert c.status == "below_threshold"
+    short = ThroughputCanary(3, 1.0, 0, output_path=tmp_path / "short.json")
+    short.observe({"step": 1, "prediction_tokens": 10, "seconds": 1.0})
+    with pytest.raises(RuntimeError):
+        short.require_complete()
+    assert json.loads((tmp_path / "short.json").read_text())["status"] == "insufficient"
+    with pytest.raises(ValueError):
+        ThroughputCanary(1, 1.0, 0).observe({"step": 0, "prediction_tokens": 1, "seconds": 1.0})
+    with pytest.raises(FileExistsError):
+        ThroughputCanary(1, 1.0, 0, output_path=tmp_path / "short.json")
