@@ -1,0 +1,88 @@
+"""Sampler index (derived, verified, rebuilt when stale) and the synthetic mechanism tasks (exact labels,
+held-out compositions, checksums) on CPU."""
+import json
+from pathlib import Path
+
+import pytest
+
+from helpers import FixtureTokenizer
+from tensor_train_ing_b200.data import prepare_data
+from tensor_train_ing_b200.sampler_index import INDEX_DIR, RECORD, index_digest, load_sampler_index
+from tensor_train_ing_b200.tasks import load_mechanism_tasks, prepare_mechanism_tasks
+
+
+@pytest.fixture
+def dataset(tmp_path):
+    source = tmp_path / "source.jsonl"
+    texts = ["doc number %d %s" % (i, "x" * i) for i in range(12)]
+    source.write_text("".join(json.dumps({"id": str(i), "text": t}) + "\n" for i, t in enumerate(texts)))
+    manifest = prepare_data(tmp_path / "data", source_jsonl=source, revision="offline-v1", tokenizer=FixtureTokenizer(),
+                            split_fractions={"train": .75, "val": .25, "test": 0., "calibration": 0.})
+    return Path(manifest).parent, json.loads(Path(manifest).read_text())
+
+
+def test_index_rows_match_document_metadata(dataset):
+    root, manifest = dataset
+    docs = [json.loads(l) for l in (root / "documents.jsonl").read_text().splitlines()]
+    for split in ("train", "val"):
+        idx = load_sampler_index(root, manifest, split)
+        want = [d for d in docs if d["split"] == split]
+        assert len(idx) == len(want)
+        for i, d in enumerate(want):
+            assert idx.start(i) == d["token_start"] and idx.length(i) == d["token_end"] - d["token_start"]
+            assert idx.numeric_id(i) == d["numeric_id"]
+            assert idx[i]["id"] == d["id"]  # the full metadata line, read by offset
+    assert (root / INDEX_DIR / "train.index.bin").stat().st_size == len(load_sampler_index(root, manifest, "train")) \
+        * RECORD.itemsize
+
+
+def test_stale_or_corrupt_index_is_rebuilt(dataset):
+    root, manifest = dataset
+    load_sampler_index(root, manifest, "train")
+    good = index_digest(root)
+    (root / INDEX_DIR / "train.index.bin").write_bytes(b"\0" * 7)  # truncated / corrupt
+    idx = load_sampler_index(root, manifest, "train")
+    assert index_digest(root) == good and len(idx) > 0
+    ident = root / INDEX_DIR / "identity.json"
+    meta = json.loads(ident.read_text())
+    meta["identity"]["documents_sha256"] = "0" * 64  # built for other metadata
+    ident.write_text(json.dumps(meta))
+    load_sampler_index(root, manifest, "train")
+    assert json.loads(ident.read_text())["identity"]["documents_sha256"] == manifest["artifacts"]["documents.jsonl"]
+    with pytest.raises(ValueError):
+        load_sampler_index(root, manifest, "holdout")
+
+
+def test_mechanism_tasks_exact_labels_and_held_out_compositions(tmp_path):
+    manifest = prepare_mechanism_tasks(tmp_path / "mech", seed=3, train_examples=8, validation_examples=8)
+    meta, val = load_mechanism_tasks(manifest, "val")
+    _, train = load_mechanism_tasks(manifest, "train")
+    assert len(val) == 16 and len(train) == 16  # counts are per task (two tasks)
+    for r in val:
+        if r["task"] == "boolean_hierarchy":
+            b, ops = r["bits"], r["operators"]
+            f = lambda op, x, y: x ^ y if op == "xor" else x & y  # noqa: E731
+            assert r["answer"] == f" {f(ops[2], f(ops[0], b[0], b[1]), f(ops[1], b[2], b[3]))}"
+        else:
+            assert r["answer"] == f" {dict(r['key_values'])[r['query']]}"
+        assert r["text"] == r["prompt"] + r["answer"]
+    for task in ("boolean_hierarchy", "associative_retrieval"):
+        tr = {r["composition_id"] for r in train if r["task"] == task}
+        va = {r["composition_id"] for r in val if r["task"] == task}
+        assert tr and va and not tr & va  # compositions held out
+    assert sum(r["answer"] == " 1" for r in val if r["task"] == "boolean_hierarchy") == 4  # balanced labels
+
+
+def test_mechanism_tasks_reject_tampering_and_bad_sizes(tmp_path):
+    manifest = prepare_mechanism_tasks(tmp_path / "mech", seed=0, train_examples=8, validation_examples=8)
+    val = Path(manifest).with_name("val.jsonl")
+    rows = val.read_text().splitlines()
+    r = json.loads(rows[0])
+    r["answer"] = " 9"
+    val.write_text("\n".join([json.dumps(r, sort_keys=True)] + rows[1:]) + "\n")
+    with pytest.raises(ValueError):
+        load_mechanism_tasks(manifest, "val")
+    with pytest.raises(ValueError):
+        prepare_mechanism_tasks(tmp_path / "odd", train_examples=9)
+    with pytest.raises(ValueError):
+        prepare_mechanism_tasks(tmp_path / "big", validation_examples=44)
