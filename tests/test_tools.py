@@ -1,0 +1,42 @@
+"""Coordinate check and the per-update profiler on CPU (their GPU use is the same code with CUDA
+activity enabled)."""
+import json
+
+import pytest
+import torch
+
+from tensor_train_ing_b200.coordcheck import run, run_depth
+from tensor_train_ing_b200.profiling import KernelProfile
+
+
+def test_width_coordinate_check_reports_every_probe_and_slopes():
+    out = run(widths=(32, 64), layers=2, head_dim=16, steps=2, batch=2, context=16, vocab=64, device="cpu")
+    assert out["widths"] == [32, 64] and set(out["rows"]) == {32, 64}
+    keys = set(out["rows"][32])
+    assert {"logits", "resid0", "resid1", "attn1", "mlp1"} <= keys
+    for row in out["rows"].values():
+        for stats in row.values():
+            assert all(v >= 0 and v == v for v in stats.values())  # finite, nonnegative RMS values
+    assert set(out["loglog_slopes"]) == {f"{k}.{f}" for k in keys for f in ("init", "delta")}
+
+
+def test_depth_coordinate_check():
+    out = run_depth(depths=(1, 2), width=32, head_dim=16, steps=1, batch=2, context=16, vocab=64, device="cpu")
+    assert out["depths"] == [1, 2] and "resid_last.delta" in out["loglog_slopes"]
+
+
+def test_kernel_profile_captures_after_warmup_and_writes_a_trace(tmp_path):
+    prof = KernelProfile(warmup_steps=1, trace_dir=tmp_path / "trace", trace_steps=2, cuda=False)
+    x = torch.randn(64, 64)
+    for step in range(4):
+        prof.start_step(step)
+        with prof.region("matmul"):
+            y = x @ x
+        prof.finish_step()
+    prof.close()
+    assert prof.steps == [1, 2]  # step 0 was warm-up; two steps captured
+    rep = prof.report()
+    assert rep["captured_steps"] == [1, 2] and "kernels" in rep
+    traces = list((tmp_path / "trace").glob("trace-steps-1-2.json"))
+    assert len(traces) == 1 and json.loads(traces[0].read_text())
+    assert y.shape == (64, 64)
