@@ -1,14 +1,17 @@
 """Training-throughput benchmark: tokens/s of full training steps (fwd + bwd + Muon/AdamW update).
 
-    python bench.py [--gpus N] [--steps K] [--warmup W] [--config 1b|7b|100m|tiny] [--impl ours|reference]
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--config 1b|7b|32b|100m|tiny] [--impl ours|reference]
+                    [--shard-params auto|on|off] [--global-batch B] [--micro-batch M] [--no-e2e]
     torchrun --nproc-per-node N --master-addr 127.0.0.1 ... bench.py --gpus N ...
 
-Workload (BASELINE.json "~1B pilot"): d_model 2048, 24 layers, 16 heads x 128, signed-product
+Default workload (the "~1B pilot" configuration): d_model 2048, 24 layers, 16 heads x 128, signed-product
 polynomial attention, bilinear MLP 8192, pre-RMSNorm, vocab 50257 (padded 50304), T = 2048,
 global batch 512 sequences (1,048,576 tokens) per optimizer step, chunked linear-CE with
 8192-token chunks, Muon on hidden matrices + AdamW elsewhere, bf16 compute / fp32 master weights
 and optimizer state.  Data: iid uniform token ids from a seed, next-token targets; random init.
-The global batch is fixed, so runs at different N are strong scaling.
+The global batch is fixed, so runs at different N are strong scaling.  ``--config 7b`` / ``32b``
+select the larger configurations (activation checkpointing; 32B needs parameter sharding over 8
+GPUs, chosen automatically).
 
 Timing: W untimed warm-up steps, then K steps bracketed by a barrier and a device synchronise on
 both sides and timed with CUDA events on the launching stream; the reported time is the max over
