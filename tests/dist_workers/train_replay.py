@@ -1,7 +1,8 @@
 """Worker: distributed trainer on gloo.  Checks that a resumed run replays an uninterrupted one
 bitwise and writes the final parameters for comparison with the serial trainer.
 
-argv: <shared tmp dir>.  Prints ``REPLAY_OK`` on rank 0."""
+argv: <shared tmp dir> [shard].  With ``shard`` the fp32 parameters are sharded over the ranks
+(owners only) and the comparisons use the exported full weights.  Prints ``REPLAY_OK`` on rank 0."""
 import json
 import os
 import sys
@@ -30,6 +31,8 @@ def config(tmp):
 
 def main():
     tmp = Path(sys.argv[1])
+    shard = len(sys.argv) > 2 and sys.argv[2] == "shard"
+    os.environ["TTB_SHARD_PARAMS"] = "1" if shard else "0"
     dist.init_process_group("gloo")
     rank = dist.get_rank()
     torch.set_num_threads(1)
@@ -41,16 +44,22 @@ def main():
                      split_fractions={"train": 1., "val": 0., "test": 0., "calibration": 0.})
     dist.barrier()
     cfg = config(tmp)
-    full = distributed_train_run(cfg, tmp / "full", max_steps=4, max_seconds=300, device="cpu")
+    export = 10 ** 9
+    full = distributed_train_run(cfg, tmp / "full", max_steps=4, max_seconds=300, device="cpu",
+                                 export_max_state_bytes=export)
     first = distributed_train_run(cfg, tmp / "a", max_steps=2, max_seconds=300, device="cpu")
-    second = distributed_train_run(cfg, tmp / "b", max_steps=2, max_seconds=300, device="cpu", resume=first["checkpoint"])
+    second = distributed_train_run(cfg, tmp / "b", max_steps=2, max_seconds=300, device="cpu", resume=first["checkpoint"],
+                                   export_max_state_bytes=export)
     assert full["progress"]["steps"] == second["progress"]["steps"] == 4
     assert full["progress"]["tokens"] == second["progress"]["tokens"] == 48
     if rank == 0:
-        a = torch.load(tmp / "full" / "final" / "model.pt", weights_only=False)["model"]
-        b = torch.load(tmp / "b" / "final" / "model.pt", weights_only=False)["model"]
+        a = torch.load(tmp / "full" / "final-weights" / "state.pt", weights_only=False)["model"]
+        b = torch.load(tmp / "b" / "final-weights" / "state.pt", weights_only=False)["model"]
         for k in a:
             assert torch.equal(a[k], b[k]), k
+        if shard:  # the recovery checkpoint's model.pt holds only what every rank replicates
+            m = torch.load(tmp / "full" / "final" / "model.pt", weights_only=False)["model"]
+            assert "blocks.0.mlp.l.weight" not in m and "embed.weight" in m
         losses = [json.loads(x)["loss"] for x in (tmp / "full" / "metrics.jsonl").read_text().splitlines()]
         (tmp / "distributed_losses.json").write_text(json.dumps(losses))
         print("REPLAY_OK", flush=True)

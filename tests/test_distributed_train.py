@@ -18,8 +18,9 @@ def _torchrun(worker, nproc, *args, timeout=600):
 
 
 @pytest.mark.slow
-def test_two_rank_training_replays_and_matches_serial(tmp_path):
-    out = _torchrun("train_replay.py", 2, str(tmp_path))
+@pytest.mark.parametrize("mode", ["replicated", "shard"])
+def test_two_rank_training_replays_and_matches_serial(tmp_path, mode):
+    out = _torchrun("train_replay.py", 2, str(tmp_path), mode)
     assert out.returncode == 0, out.stdout[-3000:] + out.stderr[-4000:]
     assert "REPLAY_OK" in out.stdout
     sys.path.insert(0, os.path.join(HERE, "dist_workers"))
@@ -35,6 +36,6 @@ def test_two_rank_training_replays_and_matches_serial(tmp_path):
     assert serial["progress"]["tokens"] == 48
     assert serial_losses == pytest.approx(dist_losses, rel=1e-5)
     s = torch.load(tmp_path / "serial" / "final" / "state.pt", weights_only=False)["model"]
-    d = torch.load(tmp_path / "full" / "final" / "model.pt", weights_only=False)["model"]
+    d = torch.load(tmp_path / "full" / "final-weights" / "state.pt", weights_only=False)["model"]
     for k in s:
         torch.testing.assert_close(s[k], d[k], rtol=1e-4, atol=1e-5)
