@@ -91,3 +91,24 @@ def test_spend_ledger_reservations_and_reconcile(tmp_path):
     assert data["runs"]["a"]["spent_usd"] == pytest.approx(0.01)
     with pytest.raises(ValueError):
         led.begin("b", 3600.0, 3600.0, None)  # $3600 exceeds the budget left
+
+
+def test_lagged_training_calibrates_before_the_first_update_and_replays(config, tmp_path):
+    """The lagged package: site-by-site calibration on the calibration split before step 1, one
+    committed statistic per update, and an exact resume across an interruption."""
+    cfg = copy.deepcopy(config)
+    cfg.model.normalization = "lagged"
+    cfg.model.final_normalization = "lagged"
+    full = train_run(cfg, tmp_path / "full", max_steps=3, max_seconds=120, device="cpu")
+    cal = full["progress"]["calibration"]
+    assert cal and cal.get("tokens", 0) > 0
+    state = torch.load(tmp_path / "full" / "final" / "state.pt", weights_only=False)["model"]
+    flags = [v for k, v in state.items() if k.endswith(".calibrated")]
+    assert flags and all(bool(v) for v in flags)
+    first = train_run(cfg, tmp_path / "a", max_steps=1, max_seconds=120, device="cpu")
+    resumed = train_run(cfg, tmp_path / "b", max_steps=2, max_seconds=120, device="cpu", resume=first["checkpoint"])
+    a = torch.load(tmp_path / "full" / "final" / "state.pt", weights_only=False)["model"]
+    b = torch.load(tmp_path / "b" / "final" / "state.pt", weights_only=False)["model"]
+    for k in a:
+        assert torch.equal(a[k], b[k]), k
+    assert resumed["progress"]["steps"] == full["progress"]["steps"] == 3
