@@ -1,5 +1,6 @@
 """Serial trainer integration on CPU (tiny model, fixture dataset)."""
 import copy
+import math
 import json
 
 import pytest
@@ -112,3 +113,32 @@ def test_lagged_training_calibrates_before_the_first_update_and_replays(config, 
     for k in a:
         assert torch.equal(a[k], b[k]), k
     assert resumed["progress"]["steps"] == full["progress"]["steps"] == 3
+
+
+@pytest.mark.parametrize("package", ["branch_rms", "sandwich_rms", "group_rms", "spectral_rms", "taper"])
+def test_every_normalization_package_trains_and_reloads(config, tmp_path, package):
+    cfg = copy.deepcopy(config)
+    cfg.model.normalization = package
+    if package == "taper":
+        cfg.model.final_normalization = "taper"
+        cfg.train.taper_end_fraction = 1.0
+        cfg.train.rung_total_tokens = 300 * cfg.train.global_prediction_tokens_per_update  # gate ends after warm-up
+    r = train_run(cfg, tmp_path / "run", max_steps=2, max_seconds=120, device="cpu")
+    rows = [json.loads(x) for x in (tmp_path / "run" / "metrics.jsonl").read_text().splitlines()]
+    assert len(rows) == 2 and all(math.isfinite(x["loss"]) for x in rows)
+    model = TensorLM(cfg.model)
+    load_checkpoint(r["checkpoint"], model, restore_rng=False, map_location="cpu")
+
+
+@pytest.mark.parametrize("source", ["probe", "batch_bound"])
+def test_qk_clip_during_training_records_its_report(config, tmp_path, source):
+    cfg = copy.deepcopy(config)
+    cfg.train.qk_clip_tau = 1e-3  # far below any score: every head is clipped
+    cfg.train.qk_clip_every_steps = 1
+    cfg.train.qk_clip_source = source
+    train_run(cfg, tmp_path / "run", max_steps=2, max_seconds=120, device="cpu")
+    rows = [json.loads(x) for x in (tmp_path / "run" / "metrics.jsonl").read_text().splitlines()]
+    clips = [x["qk_clip"] for x in rows if "qk_clip" in x]
+    assert clips and all(c["clipped_heads"] > 0 for c in clips)
+    if source == "batch_bound":
+        assert all(x.get("score_bound_max", 0) > 0 for x in rows)
