@@ -21,17 +21,25 @@ from tensor_train_ing_b200.data import prepare_data  # noqa: E402
 from tensor_train_ing_b200.distributed_train import distributed_train_run  # noqa: E402
 
 
-def config(tmp):
-    return Config(model=ModelConfig(layers=1, d_model=8, heads=1, d_key=4, d_value=4, d_mlp=12, padded_vocab=50257),
-                  train=TrainConfig(compile=False, bf16_compute=False, global_prediction_tokens_per_update=12,
-                                    rung_total_tokens=200, lr=.01),
-                  raw={"data": {"manifest": str(tmp / "data" / "manifest.json"), "context": 8, "micro_batch_size": 1},
-                       "project": {"dry_run": False, "gpu_hourly_rate_usd": 0, "spend_ledger": str(tmp / "spend.json")}})
+def config(tmp, mode="replicated"):
+    model = dict(layers=1, d_model=8, heads=1, d_key=4, d_value=4, d_mlp=12, padded_vocab=50257)
+    if mode in ("lagged", "taper"):
+        model.update(normalization=mode, final_normalization=mode)
+    cfg = Config(model=ModelConfig(**model),
+                 train=TrainConfig(compile=False, bf16_compute=False, global_prediction_tokens_per_update=12,
+                                   rung_total_tokens=200, lr=.01),
+                 raw={"data": {"manifest": str(tmp / "data" / "manifest.json"), "context": 8, "micro_batch_size": 1,
+                               "calibration_tokens": 16},
+                      "project": {"dry_run": False, "gpu_hourly_rate_usd": 0, "spend_ledger": str(tmp / "spend.json")}})
+    if mode == "taper":
+        cfg.train.rung_total_tokens = 12 * 300  # the gate must end after the 100-update warm-up
+    return cfg
 
 
 def main():
     tmp = Path(sys.argv[1])
-    shard = len(sys.argv) > 2 and sys.argv[2] == "shard"
+    mode = sys.argv[2] if len(sys.argv) > 2 else "replicated"
+    shard = mode == "shard"
     os.environ["TTB_SHARD_PARAMS"] = "1" if shard else "0"
     dist.init_process_group("gloo")
     rank = dist.get_rank()
@@ -41,9 +49,9 @@ def main():
         src.write_text("".join(json.dumps({"id": str(i), "text": "abcdefghijklm" * (1 + i % 3)}) + "\n"
                                for i in range(30)))
         prepare_data(tmp / "data", source_jsonl=src, revision="offline-v1", tokenizer=FixtureTokenizer(),
-                     split_fractions={"train": 1., "val": 0., "test": 0., "calibration": 0.})
+                     split_fractions={"train": .8, "val": 0., "test": 0., "calibration": .2})
     dist.barrier()
-    cfg = config(tmp)
+    cfg = config(tmp, mode)
     export = 10 ** 9
     full = distributed_train_run(cfg, tmp / "full", max_steps=4, max_seconds=300, device="cpu",
                                  export_max_state_bytes=export)

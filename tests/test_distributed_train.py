@@ -18,7 +18,7 @@ def _torchrun(worker, nproc, *args, timeout=600):
 
 
 @pytest.mark.slow
-@pytest.mark.parametrize("mode", ["replicated", "shard"])
+@pytest.mark.parametrize("mode", ["replicated", "shard", "lagged", "taper"])
 def test_two_rank_training_replays_and_matches_serial(tmp_path, mode):
     out = _torchrun("train_replay.py", 2, str(tmp_path), mode)
     assert out.returncode == 0, out.stdout[-3000:] + out.stderr[-4000:]
@@ -28,12 +28,14 @@ def test_two_rank_training_replays_and_matches_serial(tmp_path, mode):
 
     from tensor_train_ing_b200.train import train_run
     torch.set_num_threads(1)
-    cfg = config(tmp_path)
+    cfg = config(tmp_path, mode)
     cfg.raw["project"]["spend_ledger"] = str(tmp_path / "serial-spend.json")
     serial = train_run(cfg, tmp_path / "serial", max_steps=4, max_seconds=300, device="cpu")
     serial_losses = [json.loads(x)["loss"] for x in (tmp_path / "serial" / "metrics.jsonl").read_text().splitlines()]
     dist_losses = json.loads((tmp_path / "distributed_losses.json").read_text())
     assert serial["progress"]["tokens"] == 48
+    if mode == "lagged":  # collective calibration reproduces the serial statistics
+        assert serial["progress"]["calibration"]["tokens"] > 0
     assert serial_losses == pytest.approx(dist_losses, rel=1e-5)
     s = torch.load(tmp_path / "serial" / "final" / "state.pt", weights_only=False)["model"]
     d = torch.load(tmp_path / "full" / "final-weights" / "state.pt", weights_only=False)["model"]
