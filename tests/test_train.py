@@ -142,3 +142,44 @@ def test_qk_clip_during_training_records_its_report(config, tmp_path, source):
     assert clips and all(c["clipped_heads"] > 0 for c in clips)
     if source == "batch_bound":
         assert all(x.get("score_bound_max", 0) > 0 for x in rows)
+
+
+def test_context_fork_extends_the_context_and_records_history(config, tmp_path):
+    parent = train_run(config, tmp_path / "p", max_steps=2, max_seconds=120, device="cpu")
+    child_cfg = copy.deepcopy(config)
+    child_cfg.raw["data"]["context"] = 6
+    with pytest.raises(ValueError):  # a context change needs the explicit fork
+        train_run(child_cfg, tmp_path / "x", max_steps=1, max_seconds=120, device="cpu", resume=parent["checkpoint"])
+    child = train_run(child_cfg, tmp_path / "c", max_steps=2, max_seconds=120, device="cpu",
+                      resume=parent["checkpoint"], context_fork=True)
+    hist = child["progress"]["context_history"]
+    assert [h["context"] for h in hist] == [4, 6]
+    assert child["progress"]["steps"] == 4
+
+
+def test_batch_branch_after_warmup_scales_rates_and_quota(config, tmp_path):
+    cfg = copy.deepcopy(config)
+    cfg.train.rung_total_tokens = 7 * 400
+    parent = train_run(cfg, tmp_path / "p", max_steps=101, max_seconds=600, device="cpu")
+    early = train_run(cfg, tmp_path / "e", max_steps=1, max_seconds=120, device="cpu")
+    with pytest.raises(ValueError):  # the parent must be past its warm-up
+        train_run(cfg, tmp_path / "x", max_steps=1, max_seconds=120, device="cpu", resume=early["checkpoint"],
+                  batch_tokens=14, lr_scale=2.0)
+    child = train_run(cfg, tmp_path / "c", max_steps=2, max_seconds=120, device="cpu", resume=parent["checkpoint"],
+                      batch_tokens=14, lr_scale=2.0)
+    last = child["progress"]["batch_history"][-1]
+    assert last["source"] == "batch_branch" and last["batch_tokens"] == 14 and last["lr_scale"] == 2.0
+    rows = [json.loads(x) for x in (tmp_path / "c" / "metrics.jsonl").read_text().splitlines()]
+    assert all(r["prediction_tokens"] == 14 for r in rows)
+    assert rows[0]["lr"] == pytest.approx(2 * cfg.train.lr)
+
+
+def test_cosine_schedule_follows_its_multiplier(config, tmp_path):
+    from tensor_train_ing_b200.schedules import schedule_multiplier
+    cfg = copy.deepcopy(config)
+    cfg.train.schedule = "cosine"
+    cfg.train.rung_total_tokens = 7 * 150
+    train_run(cfg, tmp_path / "run", max_steps=3, max_seconds=120, device="cpu")
+    rows = [json.loads(x) for x in (tmp_path / "run" / "metrics.jsonl").read_text().splitlines()]
+    for k, r in enumerate(rows):
+        assert r["lr"] == pytest.approx(cfg.train.lr * schedule_multiplier(k, 150, schedule="cosine"))
