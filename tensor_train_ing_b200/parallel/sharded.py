@@ -107,6 +107,8 @@ class _Bucket:
         self.own_off: list[int] = []   # per rank: first staging offset of the rank's units
         self.own_n: list[int] = []     # per rank: aligned size of the rank's units (contiguous)
         self.own_goff: list[int] = []  # per rank: matching offset in that rank's sp buffers
+        self.cut: list[int] = []       # reduction slices (peer transport): rank r reduces [cut[r], cut[r+1])
+        self.rd_off: list[int] = []    # per rank: offset of its slice of this bucket in that rank's rd_grad
         self.ready = 0
 
 
@@ -268,11 +270,9 @@ class ShardedDataParallel:
         # Peer transport: every rank reduces an equal slice of every bucket (whole-matrix ownership
         # would leave one rank pulling two 151M-parameter matrices of a block while the others idle),
         # into its rd_grad; owners gather their units' pieces from the slice holders once per step.
-        self._rd_len = 0
         for b in self.buckets:
             b.cut = [min(b.numel, (b.numel * r // self.world) // ALIGN * ALIGN) for r in range(self.world)]
             b.cut.append(b.numel)
-            b.rd_off = []  # per rank: offset of its slice of this bucket in that rank's rd_grad
         rcur = [0] * self.world
         for b in self.buckets:
             for r in range(self.world):
@@ -293,6 +293,7 @@ class ShardedDataParallel:
             source = [(n, p.detach()) for n, p in model.named_parameters() if n in dest]
         modules = dict(model.named_modules())
         filled = set()
+
         def place(p, t):
             if p.is_meta:  # a meta tensor cannot take storage through .data: swap the tensor in place
                 torch.utils.swap_tensors(p, torch.nn.Parameter(t, requires_grad=p.requires_grad))
