@@ -1,19 +1,21 @@
 // Polynomial attention forward on the 5th-generation tensor cores (sm_100a).
 //
 // One CTA per (batch, head, block of 128 queries).  Warp roles:
-//   warp 0    TMA producer for Q1/Q2 (once) and the K1/K2 ring (3 stages of 64 keys)
-//   warp 1    tcgen05.mma issuer: S1 = Q1 K1^T, S2 = Q2 K2^T into double-buffered TMEM, then
-//             O += P V with P read straight from TMEM (A operand in tensor memory)
-//   warp 2    TMA producer for the V ring (3 stages)
-//   warps 3-10 "poly" warps: warp w owns TMEM lane quadrant w%4 (32 query rows) and one half
-//             (32 keys) of the key block; it tcgen05.ld's its S1/S2 slice, forms
-//             P = visible * row_scale * A(S1, S2) in fp32 (no per-element mask when the slice is
-//             fully visible), rounds to bf16 and tcgen05.st's it into the P buffer in TMEM;
-//             finally the eight warps drain O from TMEM to global memory.
-// K and V have separate rings: a K stage is released as soon as its S MMAs complete and a V
-// stage when its P V completes, so the loads of later blocks are in flight long before they are
-// needed.  S of key block j+1 is computed while the poly warps work on block j.  Key blocks before
-// the start of the first query's document are skipped (documents are contiguous).
+//   warp 0     TMA producer for Q1/Q2 (once) and the K1/K2 ring (3 stages of 64 keys)
+//   warp 1     tcgen05.mma issuer: S1 = Q1 K1^T, S2 = Q2 K2^T into a 3-deep ring of TMEM score
+//              buffers, issued two key blocks ahead, then O += P V with P read straight from TMEM
+//              (A operand in tensor memory)
+//   warp 2     TMA producer for the V ring (3 stages)
+//   warps 3-18 two groups of eight "poly" warps that take alternate key blocks.  Warp w owns TMEM
+//              lane quadrant w%4 (32 query rows) and one half (32 keys) of its block; it tcgen05.ld's
+//              its S1/S2 slice, forms P = visible * row_scale * A(S1, S2) in fp32 (no per-element mask
+//              when the slice is fully visible), rounds to bf16 and tcgen05.st's it over the S1
+//              columns it has just read; finally all sixteen warps drain O to global memory.
+// The elementwise step is the latency the MMAs must hide: with two groups, two key blocks are in
+// the poly stage at once while the tensor pipe runs the next scores and the previous P V.  A score
+// buffer is free again once the P V that read its P has completed.  K and V have separate rings,
+// and key blocks before the start of the first query's document are skipped (documents are
+// contiguous).
 // Reference: tnlm/kernels/poly_attn.py:38-74.
 #include "../common/host.h"
 #include "attn_api.h"
@@ -26,8 +28,9 @@ constexpr int BMQ = 128;  // queries per CTA
 constexpr int BNK = 64;   // keys per block
 constexpr int kKStages = 3;
 constexpr int kVStages = 3;
-constexpr int kThreads = 352;   // 3 control warps + 8 poly warps
-constexpr int kPolyThreads = 256;
+constexpr int kSBufs = 3;       // TMEM score buffers (S1 and S2 each), P written over S1
+constexpr int kThreads = 608;   // 3 control warps + 2 groups of 8 poly warps
+constexpr int kGroupThreads = 256;
 constexpr int kFirstPoly = 3;
 
 template <int DK, int DV>
@@ -58,12 +61,11 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* k_empty = bar + 4;    // [3]
   uint64_t* v_full = bar + 7;     // [3]
   uint64_t* v_empty = bar + 10;   // [3]
-  uint64_t* s_full = bar + 13;    // [2]
-  uint64_t* s_empty = bar + 15;   // [2]
-  uint64_t* p_full = bar + 17;    // [2]
-  uint64_t* p_empty = bar + 19;   // [2]
-  uint64_t* o_full = bar + 21;
-  uint64_t* mma_done = bar + 22;
+  uint64_t* s_full = bar + 13;    // [3] scores of the buffer's block are in TMEM
+  uint64_t* s_free = bar + 16;    // [3] the P V that read the buffer's P has completed
+  uint64_t* p_full = bar + 19;    // [3] P of the buffer's block is in TMEM
+  uint64_t* o_full = bar + 22;
+  uint64_t* mma_done = bar + 23;
   uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(bar + 24);
 
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
@@ -88,11 +90,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&v_full[i], 1);
       mbar_init(&v_empty[i], 1);
     }
-    for (int i = 0; i < 2; ++i) {
+    for (int i = 0; i < kSBufs; ++i) {
       mbar_init(&s_full[i], 1);
-      mbar_init(&s_empty[i], kPolyThreads);
-      mbar_init(&p_full[i], kPolyThreads);
-      mbar_init(&p_empty[i], 1);
+      mbar_init(&s_free[i], 1);
+      mbar_init(&p_full[i], kGroupThreads);
     }
     mbar_init(o_full, 1);
     mbar_init(mma_done, 1);
@@ -106,8 +107,10 @@ __global__ void __launch_bounds__(kThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_holder;
-  // TMEM columns: S1[2] at 0/64, S2[2] at 128/192, P[2] (bf16 pairs) at 256/288, O at 320
-  const uint32_t tS1 = tmem, tS2 = tmem + 128, tP = tmem + 256, tO = tmem + 320;
+  // TMEM columns: S1[3] at 0/64/128, S2[3] at 192/256/320, O at 384.  P of a block (bf16 pairs)
+  // overwrites the first 16 columns of each 32-key half of that block's S1.
+  const uint32_t tS1 = tmem, tS2 = tmem + kSBufs * BNK, tO = tmem + 2 * kSBufs * BNK;
+  static_assert(2 * kSBufs * BNK + DV <= 512, "TMEM budget");
 
   if (warp == 0) {
     if (elect_one()) {
@@ -159,46 +162,56 @@ __global__ void __launch_bounds__(kThreads, 1)
       constexpr uint32_t idPV = idesc_bf16_f32(128, DV, 0, 1);
       const uint32_t sQ1 = smem_u32(smem + S::kOffQ1), sQ2 = smem_u32(smem + S::kOffQ2);
       bool ok = mbar_wait(q_full, 0, p.status, kErrTimeoutMma);
-      auto issue_pv = [&](int i) -> bool {
-        const int pb = i & 1, vs = i % kVStages;
-        if (!mbar_wait(&p_full[pb], (i >> 1) & 1, p.status, kErrTimeoutMma)) return false;
-        if (!mbar_wait(&v_full[vs], (i / kVStages) & 1, p.status, kErrTimeoutMma)) return false;
-        tc_fence_after();
-        const uint32_t sV = smem_u32(smem + S::kOffV + vs * S::kV);
-#pragma unroll
-        for (int k = 0; k < BNK / 16; ++k)
-          umma_ts(tO, tP + pb * (BNK / 2) + k * 8, mnmajor_desc(sV, BNK, k), idPV, (i > 0 || k > 0) ? 1u : 0u);
-        umma_commit(&p_empty[pb]);
-        umma_commit(&v_empty[vs]);
-        return true;
-      };
-      for (int j = 0; j < nkb && ok; ++j) {
-        const int st = j & 1, ks = j % kKStages;
-        if (!mbar_wait(&k_full[ks], (j / kKStages) & 1, p.status, kErrTimeoutMma)) { ok = false; break; }
-        if (!mbar_wait(&s_empty[st], ((j >> 1) & 1) ^ 1, p.status, kErrTimeoutMma)) { ok = false; break; }
+      auto issue_s = [&](int j) -> bool {
+        const int b = j % kSBufs, ks = j % kKStages;
+        if (!mbar_wait(&k_full[ks], (j / kKStages) & 1, p.status, kErrTimeoutMma)) return false;
+        // the buffer's previous block (j - 3) must have finished its P V
+        if (!mbar_wait(&s_free[b], ((j / kSBufs) & 1) ^ 1, p.status, kErrTimeoutMma)) return false;
         tc_fence_after();
         const uint32_t sK1 = smem_u32(smem + S::kOffK + ks * S::kKStage);
         const uint32_t sK2 = sK1 + S::kK;
 #pragma unroll
         for (int k = 0; k < DK / 16; ++k)
-          umma_ss(tS1 + st * BNK, kmajor_desc(sQ1, BMQ, k), kmajor_desc(sK1, BNK, k), idS, k > 0 ? 1u : 0u);
+          umma_ss(tS1 + b * BNK, kmajor_desc(sQ1, BMQ, k), kmajor_desc(sK1, BNK, k), idS, k > 0 ? 1u : 0u);
         if (kTwo) {
 #pragma unroll
           for (int k = 0; k < DK / 16; ++k)
-            umma_ss(tS2 + st * BNK, kmajor_desc(sQ2, BMQ, k), kmajor_desc(sK2, BNK, k), idS, k > 0 ? 1u : 0u);
+            umma_ss(tS2 + b * BNK, kmajor_desc(sQ2, BMQ, k), kmajor_desc(sK2, BNK, k), idS, k > 0 ? 1u : 0u);
         }
-        umma_commit(&s_full[st]);
+        umma_commit(&s_full[b]);
         umma_commit(&k_empty[ks]);
-        if (j > 0 && !issue_pv(j - 1)) { ok = false; break; }
+        return true;
+      };
+      auto issue_pv = [&](int j) -> bool {
+        const int b = j % kSBufs, vs = j % kVStages;
+        if (!mbar_wait(&p_full[b], (j / kSBufs) & 1, p.status, kErrTimeoutMma)) return false;
+        if (!mbar_wait(&v_full[vs], (j / kVStages) & 1, p.status, kErrTimeoutMma)) return false;
+        tc_fence_after();
+        const uint32_t sV = smem_u32(smem + S::kOffV + vs * S::kV);
+        // P columns: keys 0..31 at +0..15, keys 32..63 at +32..47 of the block's S1 buffer
+#pragma unroll
+        for (int k = 0; k < BNK / 16; ++k)
+          umma_ts(tO, tS1 + b * BNK + (k >> 1) * 32 + (k & 1) * 8, mnmajor_desc(sV, BNK, k), idPV,
+                  (j > 0 || k > 0) ? 1u : 0u);
+        umma_commit(&s_free[b]);
+        umma_commit(&v_empty[vs]);
+        return true;
+      };
+      for (int j = 0; j < 2 && j < nkb && ok; ++j) ok = issue_s(j);
+      for (int j = 0; j < nkb && ok; ++j) {
+        if (j + 2 < nkb && !issue_s(j + 2)) { ok = false; break; }  // two blocks ahead
+        if (!issue_pv(j)) { ok = false; break; }
       }
-      if (ok && issue_pv(nkb - 1)) umma_commit(o_full);
+      if (ok) umma_commit(o_full);
       umma_commit(mma_done);
       mbar_wait(mma_done, 0, p.status, kErrTimeoutMma);
     }
   } else {
-    // ------------------------------------------------------------- poly warps (3..10)
-    const int sub = warp & 3;
-    const int half = (warp - kFirstPoly) >> 2;  // which 32 keys of the 64-key block
+    // ------------------------------------------------------------- poly warps (3..18)
+    const int pw = warp - kFirstPoly;
+    const int group = pw >> 3;                  // which alternate key blocks
+    const int half = (pw >> 2) & 1;             // which 32 keys of the 64-key block
+    const int sub = warp & 3;                   // TMEM lane quadrant this warp may access
     const int r = sub * 32 + lane;              // query row inside the block == TMEM lane
     const int t = q0 + r;
     const bool valid = t < p.T;
@@ -213,18 +226,15 @@ __global__ void __launch_bounds__(kThreads, 1)
     const float k0scale = p.sm * p.sm * rs;
     const uint32_t lane_off = static_cast<uint32_t>(sub * 32) << 16;
     bool ok = true;
-    for (int j = 0; j < nkb && ok; ++j) {
-      const int st = j & 1;
-      const uint32_t ph = (j >> 1) & 1;
-      if (!mbar_wait(&s_full[st], ph, p.status, kErrTimeoutEpilogue)) { ok = false; break; }
+    for (int j = group; j < nkb && ok; j += 2) {
+      const int b = j % kSBufs;
+      if (!mbar_wait(&s_full[b], (j / kSBufs) & 1, p.status, kErrTimeoutEpilogue)) { ok = false; break; }
       tc_fence_after();
       uint32_t a[32], bb[32];
-      const uint32_t col = st * BNK + half * 32;
+      const uint32_t col = b * BNK + half * 32;
       tmem_ld32(tS1 + lane_off + col, a);
       if (kTwo) tmem_ld32(tS2 + lane_off + col, bb);
       tmem_ld_wait();
-      tc_fence_before();
-      mbar_arrive(&s_empty[st]);
       const int kb0 = kstart + j * BNK + half * 32;
       const bool full_vis = rs != 0.f && kb0 >= dstart && kb0 + 31 <= t;
       uint32_t pk[16];
@@ -248,17 +258,17 @@ __global__ void __launch_bounds__(kThreads, 1)
           pk[jj / 2] = pack_bf16(v[0], v[1]);
         }
       }
-      // P buffer st is free once P V of block j-2 has completed
-      if (!mbar_wait(&p_empty[st], ph ^ 1, p.status, kErrTimeoutEpilogue)) { ok = false; break; }
-      tmem_st16(tP + lane_off + st * (BNK / 2) + half * 16, pk);
+      // P over the first 16 columns of the S1 slice this warp has just read (nobody else reads them)
+      tmem_st16(tS1 + lane_off + col, pk);
       tmem_st_wait();
       tc_fence_before();
-      mbar_arrive(&p_full[st]);
+      mbar_arrive(&p_full[b]);
     }
     if (ok && mbar_wait(o_full, 0, p.status, kErrTimeoutEpilogue)) {
       tc_fence_after();
+      const int part = group * 2 + half;  // four warps per lane quadrant share O's columns
 #pragma unroll 1
-      for (int cc = half * (DV / 64); cc < (half + 1) * (DV / 64); ++cc) {
+      for (int cc = part; cc < DV / 32; cc += 4) {
         uint32_t a[32];
         tmem_ld32(tO + lane_off + cc * 32, a);
         tmem_ld_wait();
