@@ -15,5 +15,11 @@ void poly_attention_fwd(int kind, int dk, int dv, const void* qkv, long long ld,
 void poly_attention_bwd(int kind, int dk, int dv, const void* qkv, long long ld, const void* dout, long long ldo,
                         const int* doc_end, attn::Params p, cudaStream_t stream);
 int poly_attention_dpar_blocks(int T);
+// The persistent attention kernels launch min(tiles, SMs, limit) CTAs; limit 0 means no limit.
+// Tests set a small limit so that every CTA works through many tiles.
+void poly_attention_set_grid_limit(int limit);
+namespace attn {
+int persistent_grid(int tiles);
+}
 
 }  // namespace ttb

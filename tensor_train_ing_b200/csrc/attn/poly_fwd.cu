@@ -1,7 +1,9 @@
 // Polynomial attention forward on the 5th-generation tensor cores (sm_100a).
 //
-// One CTA per (batch, head, block of 128 queries).  Warp roles:
-//   warp 0     TMA producer for Q1/Q2 (once) and the K1/K2 ring (3 stages of 64 keys)
+// Persistent: one CTA per SM takes (batch, head, block of 128 queries) tiles from a dynamic
+// scheduler in grid order (a head's query tiles in a row, so its K and V stay in L2).  Warp roles:
+//   warp 0     tile fetch; TMA producer for Q1/Q2 (once per tile, as soon as the previous tile's
+//              last score MMAs are done) and the K1/K2 ring (3 stages of 64 keys)
 //   warp 1     tcgen05.mma issuer: S1 = Q1 K1^T, S2 = Q2 K2^T into a 3-deep ring of TMEM score
 //              buffers, issued two key blocks ahead, then O += P V with P read straight from TMEM
 //              (A operand in tensor memory)
@@ -10,7 +12,8 @@
 //              lane quadrant w%4 (32 query rows) and one half (32 keys) of its block; it tcgen05.ld's
 //              its S1/S2 slice, forms P = visible * row_scale * A(S1, S2) in fp32 (no per-element mask
 //              when the slice is fully visible), rounds to bf16 and tcgen05.st's it over the S1
-//              columns it has just read; finally all sixteen warps drain O to global memory.
+//              columns it has just read; at the end of a tile all sixteen warps drain O to global
+//              memory while the tensor pipe already runs the next tile's first score blocks.
 // The elementwise step is the latency the MMAs must hide: with two groups, two key blocks are in
 // the poly stage at once while the tensor pipe runs the next scores and the previous P V.  A score
 // buffer is free again once the P V that read its P has completed.  K and V have separate rings,
@@ -48,6 +51,30 @@ struct FwdSmem {
   static constexpr int kBytes = (kOffBar + 256 + 1024) > 120 * 1024 ? (kOffBar + 256 + 1024) : 120 * 1024;
 };
 
+// Scheduler counters of the forward kernel (next tile, finished CTAs); zero between launches.
+__device__ unsigned int g_fwd_sched[2];
+
+struct FwdTile {
+  int q0, h, kstart, nkb;
+  long long row0;
+};
+
+// Tile t in grid order: head-major, heaviest (last) query block of a head first.
+__device__ __forceinline__ FwdTile fwd_tile(int t, int nqb, const Params& p) {
+  FwdTile d;
+  const int bh = t / nqb;
+  const int qb = nqb - 1 - (t - bh * nqb);
+  const int b = bh / p.H;
+  d.h = bh - b * p.H;
+  d.q0 = qb * BMQ;
+  d.row0 = static_cast<long long>(b) * p.T;
+  const int lo = d.q0 - p.pos[d.row0 + d.q0];  // start of the first query's document
+  d.kstart = (lo / BNK) * BNK;
+  const int kend = min(d.q0 + BMQ, p.T);
+  d.nkb = (kend - d.kstart + BNK - 1) / BNK;
+  return d;
+}
+
 template <int DK, int DV, int KIND>
 __global__ void __launch_bounds__(kThreads, 1)
     poly_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmKV, Params p) {
@@ -64,21 +91,20 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* s_full = bar + 13;    // [3] scores of the buffer's block are in TMEM
   uint64_t* s_free = bar + 16;    // [3] the P V that read the buffer's P has completed
   uint64_t* p_full = bar + 19;    // [3] P of the buffer's block is in TMEM
-  uint64_t* o_full = bar + 22;
+  uint64_t* o_full = bar + 22;    // O of the tile is complete in TMEM
   uint64_t* mma_done = bar + 23;
-  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(bar + 24);
+  uint64_t* acc_empty = bar + 24; // the poly warps have read O out of TMEM
+  uint64_t* q_empty = bar + 25;   // the tile's score MMAs no longer read Q
+  uint64_t* tile_full = bar + 26; // [2]
+  uint64_t* tile_empty = bar + 28;// [2]
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(bar + 30);
+  int* tile_ids = reinterpret_cast<int*>(bar + 31);  // [2]
+  constexpr int kPolyThreads = 2 * kGroupThreads;
+  constexpr int kTileReaders = 1 + 1 + kPolyThreads / 32;  // V producer, MMA issuer, poly warps
 
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
   const int nqb = (p.T + BMQ - 1) / BMQ;
-  const int qb = nqb - 1 - static_cast<int>(blockIdx.x);  // heaviest blocks first
-  const int bh = blockIdx.y;
-  const int b = bh / p.H, h = bh % p.H;
-  const int q0 = qb * BMQ;
-  const long long row0 = static_cast<long long>(b) * p.T;
-  const int lo = q0 - p.pos[row0 + q0];  // start of the first query's document
-  const int kstart = (lo / BNK) * BNK;
-  const int kend = min(q0 + BMQ, p.T);
-  const int nkb = (kend - kstart + BNK - 1) / BNK;
+  const int ntiles = nqb * p.B * p.H;
 
   if (threadIdx.x == 0) {
     mbar_init(q_full, 1);
@@ -97,6 +123,12 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     mbar_init(o_full, 1);
     mbar_init(mma_done, 1);
+    mbar_init(acc_empty, kPolyThreads);
+    mbar_init(q_empty, 1);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&tile_full[i], 1);
+      mbar_init(&tile_empty[i], kTileReaders);
+    }
     fence_mbar_init();
   }
   if (warp == 1) {
@@ -112,61 +144,92 @@ __global__ void __launch_bounds__(kThreads, 1)
   const uint32_t tS1 = tmem, tS2 = tmem + kSBufs * BNK, tO = tmem + 2 * kSBufs * BNK;
   static_assert(2 * kSBufs * BNK + DV <= 512, "TMEM budget");
 
+  auto read_tile = [&](int n, uint32_t code) -> int {
+    if (!mbar_wait(&tile_full[n & 1], (n >> 1) & 1, p.status, code)) return -1;
+    return *reinterpret_cast<volatile int*>(&tile_ids[n & 1]);
+  };
+
   if (warp == 0) {
     if (elect_one()) {
       prefetch_tmap(&tmQ);
       prefetch_tmap(&tmKV);
-      const int qrow = static_cast<int>(row0 + q0);
-      mbar_arrive_expect_tx(q_full, (kTwo ? 2 : 1) * S::kQ);
-      for (int i = 0; i < DK / 64; ++i) {
-        tma_load_2d(smem + S::kOffQ1 + i * BMQ * 128, &tmQ, q_full, p.cq1 + h * DK + 64 * i, qrow);
-        if (kTwo) tma_load_2d(smem + S::kOffQ2 + i * BMQ * 128, &tmQ, q_full, p.cq2 + h * DK + 64 * i, qrow);
-      }
-      int issued = 0;
-      for (int j = 0; j < nkb; ++j) {
-        const int st = j % kKStages;
-        if (!mbar_wait(&k_empty[st], ((j / kKStages) & 1) ^ 1, p.status, kErrTimeoutProducer)) break;
-        uint8_t* sk = smem + S::kOffK + st * S::kKStage;
-        const int krow = static_cast<int>(row0 + kstart + j * BNK);
-        mbar_arrive_expect_tx(&k_full[st], (kTwo ? 2 : 1) * S::kK);
+      uint32_t gj = 0;  // key blocks issued over all tiles
+      int nq = 0;       // Q loads issued
+      for (int n = 0;; ++n) {
+        if (!mbar_wait(&tile_empty[n & 1], ((n >> 1) & 1) ^ 1, p.status, kErrTimeoutProducer)) break;
+        const int t = static_cast<int>(atomicAdd(&g_fwd_sched[0], 1u));
+        tile_ids[n & 1] = t;
+        mbar_arrive(&tile_full[n & 1]);
+        if (t >= ntiles) break;
+        const FwdTile d = fwd_tile(t, nqb, p);
+        if (!mbar_wait(q_empty, (n & 1) ^ 1, p.status, kErrTimeoutProducer)) break;
+        const int qrow = static_cast<int>(d.row0 + d.q0);
+        mbar_arrive_expect_tx(q_full, (kTwo ? 2 : 1) * S::kQ);
         for (int i = 0; i < DK / 64; ++i) {
-          tma_load_2d(sk + i * BNK * 128, &tmKV, &k_full[st], p.ck1 + h * DK + 64 * i, krow);
-          if (kTwo) tma_load_2d(sk + S::kK + i * BNK * 128, &tmKV, &k_full[st], p.ck2 + h * DK + 64 * i, krow);
+          tma_load_2d(smem + S::kOffQ1 + i * BMQ * 128, &tmQ, q_full, p.cq1 + d.h * DK + 64 * i, qrow);
+          if (kTwo) tma_load_2d(smem + S::kOffQ2 + i * BMQ * 128, &tmQ, q_full, p.cq2 + d.h * DK + 64 * i, qrow);
         }
-        issued = j + 1;
+        ++nq;
+        bool ok = true;
+        for (int j = 0; j < d.nkb; ++j, ++gj) {
+          const int st = gj % kKStages;
+          if (!mbar_wait(&k_empty[st], ((gj / kKStages) & 1) ^ 1, p.status, kErrTimeoutProducer)) {
+            ok = false;
+            break;
+          }
+          uint8_t* sk = smem + S::kOffK + st * S::kKStage;
+          const int krow = static_cast<int>(d.row0 + d.kstart + j * BNK);
+          mbar_arrive_expect_tx(&k_full[st], (kTwo ? 2 : 1) * S::kK);
+          for (int i = 0; i < DK / 64; ++i) {
+            tma_load_2d(sk + i * BNK * 128, &tmKV, &k_full[st], p.ck1 + d.h * DK + 64 * i, krow);
+            if (kTwo) tma_load_2d(sk + S::kK + i * BNK * 128, &tmKV, &k_full[st], p.ck2 + d.h * DK + 64 * i, krow);
+          }
+        }
+        if (!ok) break;
       }
       // let in-flight copies land before exit (bounded)
-      mbar_wait(q_full, 0, p.status, kErrTimeoutProducer);
-      for (int j = max(0, issued - kKStages); j < issued; ++j)
-        mbar_wait(&k_full[j % kKStages], (j / kKStages) & 1, p.status, kErrTimeoutProducer);
+      if (nq > 0) mbar_wait(q_full, (nq - 1) & 1, p.status, kErrTimeoutProducer);
+      for (uint32_t g = gj > kKStages ? gj - kKStages : 0; g < gj; ++g)
+        mbar_wait(&k_full[g % kKStages], (g / kKStages) & 1, p.status, kErrTimeoutProducer);
     }
   } else if (warp == 2) {
     if (elect_one()) {
-      int issued = 0;
-      for (int j = 0; j < nkb; ++j) {
-        const int st = j % kVStages;
-        if (!mbar_wait(&v_empty[st], ((j / kVStages) & 1) ^ 1, p.status, kErrTimeoutProducer)) break;
-        uint8_t* sv = smem + S::kOffV + st * S::kV;
-        const int krow = static_cast<int>(row0 + kstart + j * BNK);
-        mbar_arrive_expect_tx(&v_full[st], S::kV);
-        for (int i = 0; i < DV / 64; ++i)
-          tma_load_2d(sv + i * BNK * 128, &tmKV, &v_full[st], p.cv + h * DV + 64 * i, krow);
-        issued = j + 1;
+      uint32_t gj = 0;
+      for (int n = 0;; ++n) {
+        const int t = read_tile(n, kErrTimeoutProducer);
+        if (t < 0) break;
+        mbar_arrive(&tile_empty[n & 1]);
+        if (t >= ntiles) break;
+        const FwdTile d = fwd_tile(t, nqb, p);
+        bool ok = true;
+        for (int j = 0; j < d.nkb; ++j, ++gj) {
+          const int st = gj % kVStages;
+          if (!mbar_wait(&v_empty[st], ((gj / kVStages) & 1) ^ 1, p.status, kErrTimeoutProducer)) {
+            ok = false;
+            break;
+          }
+          uint8_t* sv = smem + S::kOffV + st * S::kV;
+          const int krow = static_cast<int>(d.row0 + d.kstart + j * BNK);
+          mbar_arrive_expect_tx(&v_full[st], S::kV);
+          for (int i = 0; i < DV / 64; ++i)
+            tma_load_2d(sv + i * BNK * 128, &tmKV, &v_full[st], p.cv + d.h * DV + 64 * i, krow);
+        }
+        if (!ok) break;
       }
-      for (int j = max(0, issued - kVStages); j < issued; ++j)
-        mbar_wait(&v_full[j % kVStages], (j / kVStages) & 1, p.status, kErrTimeoutProducer);
+      for (uint32_t g = gj > kVStages ? gj - kVStages : 0; g < gj; ++g)
+        mbar_wait(&v_full[g % kVStages], (g / kVStages) & 1, p.status, kErrTimeoutProducer);
     }
   } else if (warp == 1) {
     if (elect_one()) {
       constexpr uint32_t idS = idesc_bf16_f32(128, BNK, 0, 0);
       constexpr uint32_t idPV = idesc_bf16_f32(128, DV, 0, 1);
       const uint32_t sQ1 = smem_u32(smem + S::kOffQ1), sQ2 = smem_u32(smem + S::kOffQ2);
-      bool ok = mbar_wait(q_full, 0, p.status, kErrTimeoutMma);
-      auto issue_s = [&](int j) -> bool {
-        const int b = j % kSBufs, ks = j % kKStages;
-        if (!mbar_wait(&k_full[ks], (j / kKStages) & 1, p.status, kErrTimeoutMma)) return false;
-        // the buffer's previous block (j - 3) must have finished its P V
-        if (!mbar_wait(&s_free[b], ((j / kSBufs) & 1) ^ 1, p.status, kErrTimeoutMma)) return false;
+      // S1, S2 of global key block g into score buffer g % 3
+      auto issue_s = [&](uint32_t g) -> bool {
+        const int b = g % kSBufs, ks = g % kKStages;
+        if (!mbar_wait(&k_full[ks], (g / kKStages) & 1, p.status, kErrTimeoutMma)) return false;
+        // the buffer's previous block (g - 3) must have finished its P V
+        if (!mbar_wait(&s_free[b], ((g / kSBufs) & 1) ^ 1, p.status, kErrTimeoutMma)) return false;
         tc_fence_after();
         const uint32_t sK1 = smem_u32(smem + S::kOffK + ks * S::kKStage);
         const uint32_t sK2 = sK1 + S::kK;
@@ -182,89 +245,123 @@ __global__ void __launch_bounds__(kThreads, 1)
         umma_commit(&k_empty[ks]);
         return true;
       };
-      auto issue_pv = [&](int j) -> bool {
-        const int b = j % kSBufs, vs = j % kVStages;
-        if (!mbar_wait(&p_full[b], (j / kSBufs) & 1, p.status, kErrTimeoutMma)) return false;
-        if (!mbar_wait(&v_full[vs], (j / kVStages) & 1, p.status, kErrTimeoutMma)) return false;
+      // O += P V of global key block g; the first block of tile n overwrites O once the poly warps
+      // have drained tile n-1's
+      auto issue_pv = [&](uint32_t g, bool first, int n) -> bool {
+        const int b = g % kSBufs, vs = g % kVStages;
+        if (!mbar_wait(&p_full[b], (g / kSBufs) & 1, p.status, kErrTimeoutMma)) return false;
+        if (!mbar_wait(&v_full[vs], (g / kVStages) & 1, p.status, kErrTimeoutMma)) return false;
+        if (first && !mbar_wait(acc_empty, (n & 1) ^ 1, p.status, kErrTimeoutMma)) return false;
         tc_fence_after();
         const uint32_t sV = smem_u32(smem + S::kOffV + vs * S::kV);
         // P columns: keys 0..31 at +0..15, keys 32..63 at +32..47 of the block's S1 buffer
 #pragma unroll
         for (int k = 0; k < BNK / 16; ++k)
           umma_ts(tO, tS1 + b * BNK + (k >> 1) * 32 + (k & 1) * 8, mnmajor_desc(sV, BNK, k), idPV,
-                  (j > 0 || k > 0) ? 1u : 0u);
+                  (!first || k > 0) ? 1u : 0u);
         umma_commit(&s_free[b]);
         umma_commit(&v_empty[vs]);
         return true;
       };
-      for (int j = 0; j < 2 && j < nkb && ok; ++j) ok = issue_s(j);
-      for (int j = 0; j < nkb && ok; ++j) {
-        if (j + 2 < nkb && !issue_s(j + 2)) { ok = false; break; }  // two blocks ahead
-        if (!issue_pv(j)) { ok = false; break; }
+      uint32_t gj = 0;
+      for (int n = 0;; ++n) {
+        const int t = read_tile(n, kErrTimeoutMma);
+        if (t < 0) break;
+        mbar_arrive(&tile_empty[n & 1]);
+        if (t >= ntiles) break;
+        const FwdTile d = fwd_tile(t, nqb, p);
+        if (!mbar_wait(q_full, n & 1, p.status, kErrTimeoutMma)) break;
+        bool ok = true;
+        // scores run two blocks ahead of P V; Q is free once the tile's last scores are done
+        for (int j = 0; j < 2 && j < d.nkb && ok; ++j) {
+          ok = issue_s(gj + j);
+          if (ok && j == d.nkb - 1) umma_commit(q_empty);
+        }
+        for (int j = 0; j < d.nkb && ok; ++j) {
+          if (j + 2 < d.nkb) {
+            if (!issue_s(gj + j + 2)) { ok = false; break; }
+            if (j + 2 == d.nkb - 1) umma_commit(q_empty);
+          }
+          if (!issue_pv(gj + j, j == 0, n)) { ok = false; break; }
+        }
+        if (!ok) break;
+        gj += d.nkb;
+        umma_commit(o_full);
       }
-      if (ok) umma_commit(o_full);
       umma_commit(mma_done);
       mbar_wait(mma_done, 0, p.status, kErrTimeoutMma);
     }
   } else {
     // ------------------------------------------------------------- poly warps (3..18)
     const int pw = warp - kFirstPoly;
-    const int group = pw >> 3;                  // which alternate key blocks
+    const int group = pw >> 3;                  // which alternate key blocks (by global block index)
     const int half = (pw >> 2) & 1;             // which 32 keys of the 64-key block
     const int sub = warp & 3;                   // TMEM lane quadrant this warp may access
     const int r = sub * 32 + lane;              // query row inside the block == TMEM lane
-    const int t = q0 + r;
-    const bool valid = t < p.T;
-    const long long grow = row0 + (valid ? t : q0);
-    const int dq = valid ? p.doc[grow] : -1;
-    const int dstart = valid ? t - p.pos[grow] : 0;  // documents are contiguous: keys [dstart, t]
-    const float rs = (valid && dq >= 0) ? p.row_scale[grow] : 0.f;
-    float c[4];
-#pragma unroll
-    for (int i = 0; i < 4; ++i) c[i] = p.par[h * 4 + i];
-    // signed_product fast path: P = (s1 sm)(s2 sm) rs = s1 s2 (sm^2 rs)
-    const float k0scale = p.sm * p.sm * rs;
     const uint32_t lane_off = static_cast<uint32_t>(sub * 32) << 16;
+    uint32_t gj = 0;
     bool ok = true;
-    for (int j = group; j < nkb && ok; j += 2) {
-      const int b = j % kSBufs;
-      if (!mbar_wait(&s_full[b], (j / kSBufs) & 1, p.status, kErrTimeoutEpilogue)) { ok = false; break; }
-      tc_fence_after();
-      uint32_t a[32], bb[32];
-      const uint32_t col = b * BNK + half * 32;
-      tmem_ld32(tS1 + lane_off + col, a);
-      if (kTwo) tmem_ld32(tS2 + lane_off + col, bb);
-      tmem_ld_wait();
-      const int kb0 = kstart + j * BNK + half * 32;
-      const bool full_vis = rs != 0.f && kb0 >= dstart && kb0 + 31 <= t;
-      uint32_t pk[16];
-      if (full_vis && KIND == 0) {
+    for (int n = 0; ok; ++n) {
+      const int tile = read_tile(n, kErrTimeoutEpilogue);
+      __syncwarp();
+      if (tile < 0) break;
+      if (lane == 0) mbar_arrive(&tile_empty[n & 1]);
+      if (tile >= ntiles) break;
+      const FwdTile d = fwd_tile(tile, nqb, p);
+      const int t = d.q0 + r;
+      const bool valid = t < p.T;
+      const long long grow = d.row0 + (valid ? t : d.q0);
+      const int dq = valid ? p.doc[grow] : -1;
+      const int dstart = valid ? t - p.pos[grow] : 0;  // documents are contiguous: keys [dstart, t]
+      const float rs = (valid && dq >= 0) ? p.row_scale[grow] : 0.f;
+      float c[4];
 #pragma unroll
-        for (int jj = 0; jj < 32; jj += 2)
-          pk[jj / 2] = pack_bf16(__uint_as_float(a[jj]) * __uint_as_float(bb[jj]) * k0scale,
-                                 __uint_as_float(a[jj + 1]) * __uint_as_float(bb[jj + 1]) * k0scale);
-      } else {
+      for (int i = 0; i < 4; ++i) c[i] = p.par[d.h * 4 + i];
+      // signed_product fast path: P = (s1 sm)(s2 sm) rs = s1 s2 (sm^2 rs)
+      const float k0scale = p.sm * p.sm * rs;
+      for (int j = static_cast<int>((gj & 1u) ^ static_cast<uint32_t>(group)); j < d.nkb; j += 2) {
+        const uint32_t g = gj + j;
+        const int b = g % kSBufs;
+        if (!mbar_wait(&s_full[b], (g / kSBufs) & 1, p.status, kErrTimeoutEpilogue)) { ok = false; break; }
+        tc_fence_after();
+        uint32_t a[32], bb[32];
+        const uint32_t col = b * BNK + half * 32;
+        tmem_ld32(tS1 + lane_off + col, a);
+        if (kTwo) tmem_ld32(tS2 + lane_off + col, bb);
+        tmem_ld_wait();
+        const int kb0 = d.kstart + j * BNK + half * 32;
+        const bool full_vis = rs != 0.f && kb0 >= dstart && kb0 + 31 <= t;
+        uint32_t pk[16];
+        if (full_vis && KIND == 0) {
 #pragma unroll
-        for (int jj = 0; jj < 32; jj += 2) {
-          float v[2];
+          for (int jj = 0; jj < 32; jj += 2)
+            pk[jj / 2] = pack_bf16(__uint_as_float(a[jj]) * __uint_as_float(bb[jj]) * k0scale,
+                                   __uint_as_float(a[jj + 1]) * __uint_as_float(bb[jj + 1]) * k0scale);
+        } else {
 #pragma unroll
-          for (int e = 0; e < 2; ++e) {
-            const int kt = kb0 + jj + e;
-            const float s1 = __uint_as_float(a[jj + e]) * p.sm;
-            const float s2 = kTwo ? __uint_as_float(bb[jj + e]) * p.sm : s1;
-            const bool vis = full_vis || (kt <= t && kt >= dstart);
-            v[e] = vis ? poly<KIND>(s1, s2, c) * rs : 0.f;
+          for (int jj = 0; jj < 32; jj += 2) {
+            float v[2];
+#pragma unroll
+            for (int e = 0; e < 2; ++e) {
+              const int kt = kb0 + jj + e;
+              const float s1 = __uint_as_float(a[jj + e]) * p.sm;
+              const float s2 = kTwo ? __uint_as_float(bb[jj + e]) * p.sm : s1;
+              const bool vis = full_vis || (kt <= t && kt >= dstart);
+              v[e] = vis ? poly<KIND>(s1, s2, c) * rs : 0.f;
+            }
+            pk[jj / 2] = pack_bf16(v[0], v[1]);
           }
-          pk[jj / 2] = pack_bf16(v[0], v[1]);
         }
+        // P over the first 16 columns of the S1 slice this warp has just read (nobody else reads them)
+        tmem_st16(tS1 + lane_off + col, pk);
+        tmem_st_wait();
+        tc_fence_before();
+        mbar_arrive(&p_full[b]);
       }
-      // P over the first 16 columns of the S1 slice this warp has just read (nobody else reads them)
-      tmem_st16(tS1 + lane_off + col, pk);
-      tmem_st_wait();
-      tc_fence_before();
-      mbar_arrive(&p_full[b]);
-    }
-    if (ok && mbar_wait(o_full, 0, p.status, kErrTimeoutEpilogue)) {
+      if (!ok) break;
+      gj += d.nkb;
+      // drain O (the tensor pipe meanwhile runs the next tile's first score blocks)
+      if (!mbar_wait(o_full, n & 1, p.status, kErrTimeoutEpilogue)) break;
       tc_fence_after();
       const int part = group * 2 + half;  // four warps per lane quadrant share O's columns
 #pragma unroll 1
@@ -276,9 +373,11 @@ __global__ void __launch_bounds__(kThreads, 1)
           float v[32];
 #pragma unroll
           for (int q = 0; q < 32; ++q) v[q] = __uint_as_float(a[q]);
-          store32_scaled(p.y + grow * p.ldy + h * DV + cc * 32, v);
+          store32_scaled(p.y + grow * p.ldy + d.h * DV + cc * 32, v);
         }
       }
+      tc_fence_before();
+      mbar_arrive(acc_empty);
     }
   }
   __syncwarp();
@@ -288,6 +387,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     tc_fence_after();
     tmem_dealloc(tmem, 512);
   }
+  if (threadIdx.x == 0) sched_finish(g_fwd_sched);
 }
 
 template <int DK, int DV, int KIND>
@@ -301,8 +401,8 @@ void launch_fwd(const void* qkv, long long ld, long long rows, const Params& p, 
     TTB_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, S::kBytes));
     configured = true;
   }
-  dim3 grid((p.T + BMQ - 1) / BMQ, p.B * p.H);
-  kern<<<grid, kThreads, S::kBytes, stream>>>(tq, tkv, p);
+  const int tiles = (p.T + BMQ - 1) / BMQ * p.B * p.H;
+  kern<<<persistent_grid(tiles), kThreads, S::kBytes, stream>>>(tq, tkv, p);
   TTB_CUDA_CHECK(cudaGetLastError());
 }
 

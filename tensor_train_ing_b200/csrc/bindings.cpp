@@ -434,6 +434,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("ce_bwd_from_logits", &ce_bwd_from_logits, "softmax-grad dlogits from the logits the forward kept");
   m.def("ce_bwd_logits", &ce_bwd_logits, "fused logits recompute + softmax-grad epilogue");
   m.def("poly_fwd", &poly_fwd, "tcgen05 polynomial attention forward");
+  m.def("attn_grid_limit", [](int64_t limit) { ttb::poly_attention_set_grid_limit(static_cast<int>(limit)); },
+        "cap the CTA count of the persistent attention kernels (0 = one per SM)");
   m.def("poly_bwd", &poly_bwd, "tcgen05 polynomial attention backward (dq and dkv kernels)", py::arg("kind"),
         py::arg("dk"), py::arg("dv"), py::arg("qkv"), py::arg("cols"), py::arg("dout"), py::arg("pos"), py::arg("doc"),
         py::arg("doc_end"), py::arg("row_scale"), py::arg("par"), py::arg("B"), py::arg("T"), py::arg("H"),

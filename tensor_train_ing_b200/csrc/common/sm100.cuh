@@ -91,6 +91,17 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, uint32
   }
 }
 
+// Register reallocation between warpgroups (all four warps of a warpgroup execute it).  The sum
+// over warpgroups must stay within threads x registers-per-thread at launch.
+template <uint32_t N>
+__device__ __forceinline__ void reg_alloc() {
+  asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(N));
+}
+template <uint32_t N>
+__device__ __forceinline__ void reg_dealloc() {
+  asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(N));
+}
+
 // ----------------------------------------------------------------------------------------
 // Per-thread asynchronous global -> shared copies (16 bytes, through L2 only)
 // ----------------------------------------------------------------------------------------

@@ -48,8 +48,28 @@ def dense_attention(kind, qkv, cols, B, T, H, dk, dv, docs, power, kpar):
 @pytest.mark.parametrize("dk", [64, 128])
 @pytest.mark.parametrize("B,T", [(2, 200), (1, 77), (1, 384)])
 def test_poly_attention_fwd_bwd(kind, dk, B, T):
+    check_poly_attention(kind, dk, B, T, H=2)
+
+
+@pytest.mark.parametrize("kind", ["signed_product", "offset_square", "lower_degree_mix"])
+@pytest.mark.parametrize("limit", [1, 3])
+def test_poly_attention_persistent_ctas_work_through_many_tiles(kind, limit):
+    """The persistent kernels with 1 or 3 CTAs: each CTA takes tiles of different lengths (causal,
+    document starts) one after another through the same rings and accumulators."""
+    lib().attn_grid_limit(limit)
+    try:
+        check_poly_attention(kind, 128, 2, 520, H=3)
+    finally:
+        lib().attn_grid_limit(0)
+
+
+def test_poly_attention_more_tiles_than_sms():
+    check_poly_attention("signed_product", 128, 3, 1100, H=6)  # 3 * 6 * 9 = 162 query tiles
+
+
+def check_poly_attention(kind, dk, B, T, H):
     torch.manual_seed(0)
-    H, dv = 2, dk
+    dv = dk
     dev = "cuda"
     nqk = 4 if kind != "offset_square" else 2
     cols = [0, H * dk, 2 * H * dk, 3 * H * dk, 4 * H * dk] if nqk == 4 else [0, H * dk, 0, H * dk, 2 * H * dk]
