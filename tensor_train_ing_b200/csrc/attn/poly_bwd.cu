@@ -396,10 +396,24 @@ __global__ void __launch_bounds__(kDqThreads, 1)
       const long long qp = valid ? p.pos[grow] : 0;
       const float* ct = p.rope_cos ? p.rope_cos + qp * (DK / 2) : nullptr;
       const float* st = p.rope_sin ? p.rope_sin + qp * (DK / 2) : nullptr;
+      float cs[16], sn[16];
+      if (ct != nullptr) rope_fetch16(ct, st, 0, cs, sn);  // in flight while dQ completes
       if (!mbar_wait(acc_full, n & 1, p.status, kErrTimeoutEpilogue)) break;
       tc_fence_after();
-      store_row_lean<DK>(tDQ1 + lane_off, p.dq + grow * p.ldd + p.cq1 + d.h * DK, valid, p.sm, ct, st);
-      if (kTwo) store_row_lean<DK>(tDQ2 + lane_off, p.dq + grow * p.ldd + p.cq2 + d.h * DK, valid, p.sm, ct, st);
+      __nv_bfloat16* dst1 = p.dq + grow * p.ldd + p.cq1 + d.h * DK;
+      __nv_bfloat16* dst2 = p.dq + grow * p.ldd + p.cq2 + d.h * DK;
+      if (ct != nullptr && kTwo) {
+        const uint32_t acc[2] = {tDQ1 + lane_off, tDQ2 + lane_off};
+        __nv_bfloat16* const out[2] = {dst1, dst2};
+        store_rows_rope<DK, 2>(acc, out, valid, p.sm, ct, st, cs, sn);
+      } else if (ct != nullptr) {
+        const uint32_t acc[1] = {tDQ1 + lane_off};
+        __nv_bfloat16* const out[1] = {dst1};
+        store_rows_rope<DK, 1>(acc, out, valid, p.sm, ct, st, cs, sn);
+      } else {
+        store_row_lean<DK>(tDQ1 + lane_off, dst1, valid, p.sm, nullptr, nullptr);
+        if (kTwo) store_row_lean<DK>(tDQ2 + lane_off, dst2, valid, p.sm, nullptr, nullptr);
+      }
       tc_fence_before();
       mbar_arrive(acc_empty);
     }
@@ -811,12 +825,24 @@ __global__ void __launch_bounds__(kKvThreads, 1)
       const long long kp = kvalid ? p.pos[krow] : 0;
       const float* ct = p.rope_cos ? p.rope_cos + kp * (DK / 2) : nullptr;
       const float* st = p.rope_sin ? p.rope_sin + kp * (DK / 2) : nullptr;
+      float cs[16], sn[16];
+      if (ct != nullptr) rope_fetch16(ct, st, 0, cs, sn);  // in flight while the accumulators complete
       if (!mbar_wait(acc_full, n & 1, p.status, kErrTimeoutEpilogue)) break;
       tc_fence_after();
       __nv_bfloat16* row = p.dq + krow * p.ldd;
       store_row_lean<DV>(tDV + lane_off, row + p.cv + d.h * DV, kvalid, 1.f, nullptr, nullptr);
-      store_row_lean<DK>(tDK1 + lane_off, row + p.ck1 + d.h * DK, kvalid, p.sm, ct, st);
-      if (kTwo) store_row_lean<DK>(tDK2 + lane_off, row + p.ck2 + d.h * DK, kvalid, p.sm, ct, st);
+      if (ct != nullptr && kTwo) {
+        const uint32_t acc[2] = {tDK1 + lane_off, tDK2 + lane_off};
+        __nv_bfloat16* const out[2] = {row + p.ck1 + d.h * DK, row + p.ck2 + d.h * DK};
+        store_rows_rope<DK, 2>(acc, out, kvalid, p.sm, ct, st, cs, sn);
+      } else if (ct != nullptr) {
+        const uint32_t acc[1] = {tDK1 + lane_off};
+        __nv_bfloat16* const out[1] = {row + p.ck1 + d.h * DK};
+        store_rows_rope<DK, 1>(acc, out, kvalid, p.sm, ct, st, cs, sn);
+      } else {
+        store_row_lean<DK>(tDK1 + lane_off, row + p.ck1 + d.h * DK, kvalid, p.sm, nullptr, nullptr);
+        if (kTwo) store_row_lean<DK>(tDK2 + lane_off, row + p.ck2 + d.h * DK, kvalid, p.sm, nullptr, nullptr);
+      }
       tc_fence_before();
       mbar_arrive(acc_empty);
     }

@@ -162,5 +162,61 @@ __device__ __forceinline__ void store_row_lean(uint32_t tacc, __nv_bfloat16* dst
   }
 }
 
+// Rotary tables of one row, 16 pairs (chunk cc) at a time.
+__device__ __forceinline__ void rope_fetch16(const float* ct, const float* st, int cc, float (&cs)[16],
+                                             float (&sn)[16]) {
+#pragma unroll
+  for (int q = 0; q < 4; ++q) {
+    const float4 c4 = __ldg(reinterpret_cast<const float4*>(ct + cc * 16) + q);
+    const float4 s4 = __ldg(reinterpret_cast<const float4*>(st + cc * 16) + q);
+    cs[q * 4 + 0] = c4.x; cs[q * 4 + 1] = c4.y; cs[q * 4 + 2] = c4.z; cs[q * 4 + 3] = c4.w;
+    sn[q * 4 + 0] = s4.x; sn[q * 4 + 1] = s4.y; sn[q * 4 + 2] = s4.z; sn[q * 4 + 3] = s4.w;
+  }
+}
+
+// Drain N accumulator rows of width W that share one position (dQ1/dQ2, or dK1/dK2), rotating the
+// pairs (i, i + W/2) back: g1 = a cos + b sin, g2 = -a sin + b cos.  On entry cs/sn hold chunk 0 of
+// the row's tables (fetched before the accumulators were ready); each step fetches the next chunk
+// before draining the current one, so the table latency overlaps TMEM loads and stores.
+template <int W, int N>
+__device__ __forceinline__ void store_rows_rope(const uint32_t (&tacc)[N], __nv_bfloat16* const (&dst)[N], bool valid,
+                                                float scale, const float* ct, const float* st, float (&cs)[16],
+                                                float (&sn)[16]) {
+#pragma unroll 1
+  for (int cc = 0; cc < W / 32; ++cc) {
+    float ncs[16], nsn[16];
+    if (cc + 1 < W / 32) rope_fetch16(ct, st, cc + 1, ncs, nsn);
+#pragma unroll
+    for (int n = 0; n < N; ++n) {
+      uint32_t a[16], b[16];
+      tmem_ld16(tacc[n] + cc * 16, a);
+      tmem_ld16(tacc[n] + W / 2 + cc * 16, b);
+      tmem_ld_wait();
+      if (valid) {
+        uint32_t g1[8], g2[8];
+#pragma unroll
+        for (int e = 0; e < 16; e += 2) {
+          const float x1 = __uint_as_float(a[e]) * scale, x2 = __uint_as_float(b[e]) * scale;
+          const float y1 = __uint_as_float(a[e + 1]) * scale, y2 = __uint_as_float(b[e + 1]) * scale;
+          g1[e / 2] = pack_bf16(x1 * cs[e] + x2 * sn[e], y1 * cs[e + 1] + y2 * sn[e + 1]);
+          g2[e / 2] = pack_bf16(x2 * cs[e] - x1 * sn[e], y2 * cs[e + 1] - y1 * sn[e + 1]);
+        }
+        __nv_bfloat16* d = dst[n];
+        *reinterpret_cast<uint4*>(d + cc * 16) = make_uint4(g1[0], g1[1], g1[2], g1[3]);
+        *reinterpret_cast<uint4*>(d + cc * 16 + 8) = make_uint4(g1[4], g1[5], g1[6], g1[7]);
+        *reinterpret_cast<uint4*>(d + W / 2 + cc * 16) = make_uint4(g2[0], g2[1], g2[2], g2[3]);
+        *reinterpret_cast<uint4*>(d + W / 2 + cc * 16 + 8) = make_uint4(g2[4], g2[5], g2[6], g2[7]);
+      }
+    }
+    if (cc + 1 < W / 32) {
+#pragma unroll
+      for (int e = 0; e < 16; ++e) {
+        cs[e] = ncs[e];
+        sn[e] = nsn[e];
+      }
+    }
+  }
+}
+
 }  // namespace attn
 }  // namespace ttb
