@@ -361,6 +361,90 @@ __global__ void __launch_bounds__(256) rmsnorm_bwd_warp_kernel(const TDY* __rest
   for (int j = threadIdx.x; j < d; j += blockDim.x) dw_part[static_cast<long long>(blockIdx.x) * d + j] = acc[j];
 }
 
+// Single-pass RMSNorm backward for one group (G == 1) and d = 256 * 4 * C: dx, the bf16 copy and the
+// weight-gradient partials from ONE read of x and dy.  Thread t owns the float4 chunks t, t + 256,
+// ... (every load and store coalesced) and keeps its columns of w and of the partial dw in registers.
+// CTA b walks rows b, b + gridDim.x, ... R at a time with all loads of those rows issued before any is
+// used; the row sums go through a double-buffered shared array, one barrier per step.  The partial
+// row b of dw_part is this CTA's sum over its rows in row order: deterministic.
+template <int C, int R, typename TDY>
+__global__ void __launch_bounds__(256) rmsnorm_bwd_fused_kernel(const TDY* __restrict__ dy, const float* __restrict__ x,
+                                                               const float* __restrict__ w,
+                                                               const float* __restrict__ rstd, float* __restrict__ dres,
+                                                               int accumulate, float* __restrict__ dw_part, int N,
+                                                               __nv_bfloat16* __restrict__ out16, float scale16) {
+  constexpr int d = 256 * 4 * C;
+  __shared__ float red[2][R][8];
+  const int tid = threadIdx.x, lane = tid & 31, wid = tid >> 5;
+  float wv[C][4], dwl[C][4];
+#pragma unroll
+  for (int c = 0; c < C; ++c) {
+    load4(w + (c * 256 + tid) * 4, wv[c]);
+#pragma unroll
+    for (int k = 0; k < 4; ++k) dwl[c][k] = 0.f;
+  }
+  int it = 0;
+  for (int row0 = blockIdx.x; row0 < N; row0 += R * gridDim.x, ++it) {
+    float xv[R][C][4], dv[R][C][4], pv[R][C][4], r[R];
+#pragma unroll
+    for (int i = 0; i < R; ++i) {
+      const int row = row0 + i * gridDim.x;
+      const bool live = row < N;
+      const long long base = static_cast<long long>(live ? row : row0) * d;
+      r[i] = live ? rstd[live ? row : row0] : 0.f;
+#pragma unroll
+      for (int c = 0; c < C; ++c) {
+        const long long off = base + (c * 256 + tid) * 4;
+        load4(x + off, xv[i][c]);
+        load4(dy + off, dv[i][c]);
+        if (accumulate) load4(dres + off, pv[i][c]);
+      }
+    }
+    float s[R];
+#pragma unroll
+    for (int i = 0; i < R; ++i) {
+      s[i] = 0.f;
+#pragma unroll
+      for (int c = 0; c < C; ++c)
+#pragma unroll
+        for (int k = 0; k < 4; ++k) s[i] += dv[i][c][k] * wv[c][k] * xv[i][c][k];
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) s[i] += __shfl_xor_sync(0xffffffffu, s[i], o);
+      if (lane == 0) red[it & 1][i][wid] = s[i];
+    }
+    __syncthreads();
+#pragma unroll
+    for (int i = 0; i < R; ++i) {
+      const int row = row0 + i * gridDim.x;
+      if (row >= N) break;
+      float t = 0.f;
+#pragma unroll
+      for (int q = 0; q < 8; ++q) t += red[it & 1][i][q];
+      const float m = t * r[i] / d;  // mean over the row of (dy w) xhat
+      const long long base = static_cast<long long>(row) * d;
+#pragma unroll
+      for (int c = 0; c < C; ++c) {
+        const long long off = base + (c * 256 + tid) * 4;
+        float o[4];
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          const float xh = xv[i][c][k] * r[i];
+          o[k] = r[i] * (dv[i][c][k] * wv[c][k] - xh * m) + (accumulate ? pv[i][c][k] : 0.f);
+          dwl[c][k] += dv[i][c][k] * xh;
+        }
+        *reinterpret_cast<float4*>(dres + off) = make_float4(o[0], o[1], o[2], o[3]);
+        if (out16 != nullptr)
+          *reinterpret_cast<uint2*>(out16 + off) =
+              make_uint2(pack_bf16(o[0] * scale16, o[1] * scale16), pack_bf16(o[2] * scale16, o[3] * scale16));
+      }
+    }
+  }
+#pragma unroll
+  for (int c = 0; c < C; ++c)
+    *reinterpret_cast<float4*>(dw_part + static_cast<long long>(blockIdx.x) * d + (c * 256 + tid) * 4) =
+        make_float4(dwl[c][0], dwl[c][1], dwl[c][2], dwl[c][3]);
+}
+
 // out[j] (+)= sum_p part[p][j].  Block = 32 columns x 8 row groups: warp g sums rows p = g, g+8, ...
 // in order, then warp 0 adds the 8 group sums in order (a fixed tree: deterministic).
 __global__ void __launch_bounds__(256) colsum_kernel(const float* __restrict__ part, int P, int d,
@@ -529,6 +613,27 @@ void rmsnorm_bwd_ex(const void* dy, bool dy_f32, const float* x, const float* w,
   __nv_bfloat16* out16 = static_cast<__nv_bfloat16*>(out16_);
   TTB_CHECK(d % 4 == 0 && d <= kRowThreads * kVec * kMaxChunks, "rmsnorm: d must be a multiple of 4 and <= 8192");
   const int grid = rmsnorm_bwd_partials(N);
+  if (G == 1 && (d == 1024 || d == 2048 || d == 4096)) {
+    auto fused = [&](auto c, auto r) {
+      constexpr int C = decltype(c)::value, R = decltype(r)::value;
+      if (dy_f32)
+        rmsnorm_bwd_fused_kernel<C, R, float><<<grid, 256, 0, stream>>>(
+            static_cast<const float*>(dy), x, w, rstd, dres, accumulate, dw_part, N, out16, scale16);
+      else
+        rmsnorm_bwd_fused_kernel<C, R, __nv_bfloat16><<<grid, 256, 0, stream>>>(
+            static_cast<const __nv_bfloat16*>(dy), x, w, rstd, dres, accumulate, dw_part, N, out16, scale16);
+    };
+    if (d == 1024)
+      fused(std::integral_constant<int, 1>{}, std::integral_constant<int, 2>{});
+    else if (d == 2048)
+      fused(std::integral_constant<int, 2>{}, std::integral_constant<int, 2>{});
+    else
+      fused(std::integral_constant<int, 4>{}, std::integral_constant<int, 1>{});
+    TTB_CUDA_CHECK(cudaGetLastError());
+    colsum_kernel<<<(d + 31) / 32, 256, 0, stream>>>(dw_part, grid, d, dw, dw_accumulate);
+    TTB_CUDA_CHECK(cudaGetLastError());
+    return;
+  }
   const bool done = with_chunks(d, 32, [&](auto ch) {
     constexpr int CH = decltype(ch)::value;
     const size_t smem = static_cast<size_t>(d) * sizeof(float);

@@ -2,6 +2,8 @@
 
     python -m tensor_train_ing_b200.kernel_bench time [CASE ...]      CUDA-event timings, TFLOP/s, GB/s
     python -m tensor_train_ing_b200.kernel_bench profile CASE         three launches of one case (for ncu -k/-c)
+    python -m tensor_train_ing_b200.kernel_bench attn_scale [norope]  attention at four (B, T) with B*T fixed:
+                                                                       fixed cost vs cost per key block
 
 Cases (shapes of one 1B micro-batch, 8 x 2048 tokens, unless noted): gemm_qkv, gemm_dx, gemm_dw,
 bilinear, bilinear_grad, attn_fwd, attn_bwd, attn_case (B=2 for profiling), rmsnorm_fwd,
@@ -31,7 +33,7 @@ class _Case:
         self.fn, self.flops, self.bytes = fn, flops, bytes_
 
 
-def _attn_inputs(b=B):
+def _attn_inputs(b=B, T=T):
     from .ops import fused
     from .ops.block import rope_context
     n = b * T
@@ -151,6 +153,55 @@ def time_case(name: str, reps: int = 10) -> dict:
     return out
 
 
+def _event_time(fn, reps: int = 10) -> float:
+    """Mean microseconds of fn over reps launches, each after a 256 MB write that flushes L2."""
+    flush = torch.empty(64 << 20, device="cuda")
+    for _ in range(3):
+        fn()
+    torch.cuda.synchronize()
+    total = 0.0
+    for _ in range(reps):
+        flush.zero_()
+        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s.record()
+        fn()
+        e.record()
+        torch.cuda.synchronize()
+        total += s.elapsed_time(e)
+    return total / reps * 1e3
+
+
+def attn_scaling(rope: bool = True, shapes=((16, 1024), (8, 2048), (4, 4096), (2, 8192))) -> dict:
+    """Attention forward and backward at shapes with the same B*T: the CTA-tile count of the
+    one-tile-per-CTA layout and the tokens stay fixed while the causal key blocks grow with T, so a
+    straight-line fit separates a fixed cost (operand loads, pipeline fill, accumulator drains) from
+    the cost per 64-key x 128-query block."""
+    C = _lib()
+    rows = []
+    for b, t in shapes:
+        tables, rs, qkv, par, cols, dout, rp = _attn_inputs(b, t)
+        cs, sn = (rp["cos"], rp["sin"]) if rope else (None, None)
+        fwd = lambda: C.poly_fwd(0, DK, DK, qkv, cols, tables["pos32"], tables["doc32"], rs, par, b, t, H)
+        bwd = lambda: C.poly_bwd(0, DK, DK, qkv, cols, dout, tables["pos32"], tables["doc32"], tables["doc_end32"],
+                                 rs, par, b, t, H, cs, sn)
+        nq = t // 128
+        blocks = b * H * sum(2 * (q + 1) for q in range(nq))
+        rows.append({"B": b, "T": t, "key_blocks": blocks, "fwd_us": round(_event_time(fwd), 1),
+                     "bwd_us": round(_event_time(bwd), 1)})
+        print(json.dumps(rows[-1]), flush=True)
+    from .ops._ext import check_status
+    check_status()
+    fit = {}
+    for k in ("fwd_us", "bwd_us"):
+        lo, hi = rows[0], rows[-1]
+        slope = (hi[k] - lo[k]) / (hi["key_blocks"] - lo["key_blocks"])
+        fit[k.split("_")[0]] = {"fixed_us": round(lo[k] - slope * lo["key_blocks"], 1),
+                                "ns_per_block": round(slope * 1e3, 2)}
+    out = {"rope": rope, "fit": fit}
+    print(json.dumps(out), flush=True)
+    return out
+
+
 def profile_case(name: str):
     case = build(name)
     for _ in range(3):
@@ -168,6 +219,9 @@ def main(argv=None):
     if mode == "profile":
         for n in names:
             profile_case(n)
+        return
+    if mode == "attn_scale":
+        attn_scaling(rope="norope" not in argv[1:])
         return
     for n in names:
         print(json.dumps(time_case(n)), flush=True)

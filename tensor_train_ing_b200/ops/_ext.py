@@ -12,8 +12,14 @@ _C = None
 _ERR: Exception | None = None
 _PROXY = None
 
-# kernels launched by one call of each binding (used by the launch counter)
-KERNELS_PER_CALL = {"mm": 1, "bilinear": 1, "bilinear_grad": 1, "rmsnorm_fwd": 1, "rmsnorm_bwd": 2, "rope_": 1,
+def _rmsnorm_bwd_kernels(dy, x, w, rstd, dres, accumulate, groups, *rest, **kw):
+    """One fused pass + the column sum for one group at d in {1024, 2048, 4096}; otherwise the dx
+    pass, the weight-gradient pass and the column sum (csrc/misc/rowops.cu, rmsnorm_bwd_ex)."""
+    return 2 if int(groups) == 1 and x.shape[-1] in (1024, 2048, 4096) else 3
+
+
+# Kernels each binding launches per call, for the launch counter (a callable gets the call's arguments).
+KERNELS_PER_CALL = {"mm": 1, "bilinear": 1, "bilinear_grad": 1, "rmsnorm_fwd": 1, "rmsnorm_bwd": _rmsnorm_bwd_kernels, "rope_": 1,
                     "embed_fwd": 1, "embed_bwd": 1, "ce_fwd": 2, "ce_bwd_logits": 1, "poly_fwd": 1,
                     "poly_bwd": 2, "qkv_rope": 1, "peer_barrier": 1, "rs_reduce_sq": 1, "ag_pull_cast": 1,
                     "rs_accumulate": 1, "ce_bwd_from_logits": 1}
@@ -36,8 +42,9 @@ class _Counting:
 
         def wrapped(*args, **kwargs):
             if self.enabled:
-                self.count += k
-                self.by_name[name] = self.by_name.get(name, 0) + k
+                n = k(*args, **kwargs) if callable(k) else k
+                self.count += n
+                self.by_name[name] = self.by_name.get(name, 0) + n
             return fn(*args, **kwargs)
 
         object.__setattr__(self, name, wrapped)

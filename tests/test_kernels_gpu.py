@@ -102,11 +102,13 @@ def check_poly_attention(kind, dk, B, T, H):
 
 def test_rmsnorm_fwd_bwd_groups():
     torch.manual_seed(1)
-    for groups, d in ((1, 512), (4, 2048), (1, 6144)):
-        x = torch.randn(300, d, device="cuda", requires_grad=True)
+    # one group at d = 1024 / 2048 / 4096 takes the single-pass kernel (two rows per step: odd counts)
+    for groups, d, n in ((1, 512, 300), (4, 2048, 300), (1, 6144, 300), (1, 1024, 1301), (1, 2048, 777),
+                         (1, 4096, 300)):
+        x = torch.randn(n, d, device="cuda", requires_grad=True)
         w = (1 + 0.1 * torch.randn(d, device="cuda")).requires_grad_()
         y = fused.rms_norm(x, w, groups, 1e-6)
-        gy = torch.randn(300, d, device="cuda").bfloat16()
+        gy = torch.randn(n, d, device="cuda").bfloat16()
         y.backward(gy)
         xr, wr = x.detach().double().requires_grad_(), w.detach().double().requires_grad_()
         xg = xr.unflatten(-1, (groups, -1))
@@ -120,12 +122,12 @@ def test_rmsnorm_fwd_bwd_groups():
 
 def test_residual_norm_folds_dx_into_residual_grad_and_emits_bf16_copy():
     torch.manual_seed(2)
-    for groups, d in ((1, 512), (4, 2048), (1, 6144)):
-        x = torch.randn(200, d, device="cuda", requires_grad=True)
+    for groups, d, n in ((1, 512, 200), (4, 2048, 200), (1, 6144, 200), (1, 2048, 1999), (1, 4096, 201)):
+        x = torch.randn(n, d, device="cuda", requires_grad=True)
         w = (1 + 0.1 * torch.randn(d, device="cuda")).requires_grad_()
         xr, h = fused.residual_norm(x, w, groups, 1e-6, up_alpha=0.5)
-        gres = torch.randn(200, d, device="cuda")
-        gh = torch.randn(200, d, device="cuda").bfloat16()
+        gres = torch.randn(n, d, device="cuda")
+        gh = torch.randn(n, d, device="cuda").bfloat16()
         captured = {}
 
         def hook(g):

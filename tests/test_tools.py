@@ -40,3 +40,11 @@ def test_kernel_profile_captures_after_warmup_and_writes_a_trace(tmp_path):
     traces = list((tmp_path / "trace").glob("trace-steps-1-2.json"))
     assert len(traces) == 1 and json.loads(traces[0].read_text())
     assert y.shape == (64, 64)
+
+
+def test_launch_count_of_the_rmsnorm_backward_follows_its_kernel_path():
+    from tensor_train_ing_b200.ops._ext import KERNELS_PER_CALL
+    count = KERNELS_PER_CALL["rmsnorm_bwd"]
+    for d, groups, kernels in ((2048, 1, 2), (1024, 1, 2), (4096, 1, 2), (6144, 1, 3), (2048, 4, 3), (512, 1, 3)):
+        x = torch.empty(3, d)
+        assert count(x, x, None, None, x, True, groups) == kernels
