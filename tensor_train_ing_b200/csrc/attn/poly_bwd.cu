@@ -411,8 +411,8 @@ __global__ void __launch_bounds__(kDqThreads, 1)
         __nv_bfloat16* const out[1] = {dst1};
         store_rows_rope<DK, 1>(acc, out, valid, p.sm, ct, st, cs, sn);
       } else {
-        store_row_lean<DK>(tDQ1 + lane_off, dst1, valid, p.sm, nullptr, nullptr);
-        if (kTwo) store_row_lean<DK>(tDQ2 + lane_off, dst2, valid, p.sm, nullptr, nullptr);
+        store_row_lean<DK>(tDQ1 + lane_off, dst1, valid, p.sm);
+        if (kTwo) store_row_lean<DK>(tDQ2 + lane_off, dst2, valid, p.sm);
       }
       tc_fence_before();
       mbar_arrive(acc_empty);
@@ -830,7 +830,7 @@ __global__ void __launch_bounds__(kKvThreads, 1)
       if (!mbar_wait(acc_full, n & 1, p.status, kErrTimeoutEpilogue)) break;
       tc_fence_after();
       __nv_bfloat16* row = p.dq + krow * p.ldd;
-      store_row_lean<DV>(tDV + lane_off, row + p.cv + d.h * DV, kvalid, 1.f, nullptr, nullptr);
+      store_row_lean<DV>(tDV + lane_off, row + p.cv + d.h * DV, kvalid, 1.f);
       if (ct != nullptr && kTwo) {
         const uint32_t acc[2] = {tDK1 + lane_off, tDK2 + lane_off};
         __nv_bfloat16* const out[2] = {row + p.ck1 + d.h * DK, row + p.ck2 + d.h * DK};
@@ -840,8 +840,8 @@ __global__ void __launch_bounds__(kKvThreads, 1)
         __nv_bfloat16* const out[1] = {row + p.ck1 + d.h * DK};
         store_rows_rope<DK, 1>(acc, out, kvalid, p.sm, ct, st, cs, sn);
       } else {
-        store_row_lean<DK>(tDK1 + lane_off, row + p.ck1 + d.h * DK, kvalid, p.sm, nullptr, nullptr);
-        if (kTwo) store_row_lean<DK>(tDK2 + lane_off, row + p.ck2 + d.h * DK, kvalid, p.sm, nullptr, nullptr);
+        store_row_lean<DK>(tDK1 + lane_off, row + p.ck1 + d.h * DK, kvalid, p.sm);
+        if (kTwo) store_row_lean<DK>(tDK2 + lane_off, row + p.ck2 + d.h * DK, kvalid, p.sm);
       }
       tc_fence_before();
       mbar_arrive(acc_empty);

@@ -59,105 +59,22 @@ __device__ __forceinline__ void store32_scaled(__nv_bfloat16* dst, const float (
 }
 
 // Drain one accumulator row of width W from TMEM (columns tacc..tacc+W) to global bf16 memory,
-// scaled by `scale`.  With rotary tables (ct/st = the row's table entries, W/2 each) the pairs
-// (i, i + W/2) are rotated back: g1 = a cos + b sin, g2 = -a sin + b cos.
+// scaled by `scale`, 16 columns at a time (few live registers: the epilogue warps run at the launch
+// register count while the tensor pipe works on the next tile).
 template <int W>
-__device__ __forceinline__ void store_row(uint32_t tacc, __nv_bfloat16* dst, bool valid, float scale,
-                                          const float* ct, const float* st) {
-  if (ct == nullptr) {
+__device__ __forceinline__ void store_row_lean(uint32_t tacc, __nv_bfloat16* dst, bool valid, float scale) {
 #pragma unroll 1
-    for (int cc = 0; cc < W / 32; ++cc) {
-      uint32_t a[32];
-      tmem_ld32(tacc + cc * 32, a);
-      tmem_ld_wait();
-      if (valid) {
-        float v[32];
-#pragma unroll
-        for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(a[j]) * scale;
-        store32_scaled(dst + cc * 32, v);
-      }
-    }
-    return;
-  }
-#pragma unroll 1
-  for (int cc = 0; cc < W / 64; ++cc) {
-    uint32_t a[32], b[32];
-    tmem_ld32(tacc + cc * 32, a);
-    tmem_ld32(tacc + W / 2 + cc * 32, b);
-    tmem_ld_wait();
-    if (valid) {
-      float g1[32], g2[32], cs[32], sn[32];
-#pragma unroll
-      for (int q = 0; q < 8; ++q) {
-        const float4 c4 = *reinterpret_cast<const float4*>(ct + cc * 32 + q * 4);
-        const float4 s4 = *reinterpret_cast<const float4*>(st + cc * 32 + q * 4);
-        cs[q * 4 + 0] = c4.x; cs[q * 4 + 1] = c4.y; cs[q * 4 + 2] = c4.z; cs[q * 4 + 3] = c4.w;
-        sn[q * 4 + 0] = s4.x; sn[q * 4 + 1] = s4.y; sn[q * 4 + 2] = s4.z; sn[q * 4 + 3] = s4.w;
-      }
-#pragma unroll
-      for (int j = 0; j < 32; ++j) {
-        const float c = cs[j], s = sn[j];
-        const float x1 = __uint_as_float(a[j]) * scale, x2 = __uint_as_float(b[j]) * scale;
-        g1[j] = x1 * c + x2 * s;
-        g2[j] = x2 * c - x1 * s;
-      }
-      store32_scaled(dst + cc * 32, g1);
-      store32_scaled(dst + W / 2 + cc * 32, g2);
-    }
-  }
-}
-
-// store_row in 16-column steps: fewer live registers, for epilogue warps that run at the launch
-// register count while the tensor pipe works on the next tile.
-template <int W>
-__device__ __forceinline__ void store_row_lean(uint32_t tacc, __nv_bfloat16* dst, bool valid, float scale,
-                                               const float* ct, const float* st) {
-  if (ct == nullptr) {
-#pragma unroll 1
-    for (int cc = 0; cc < W / 16; ++cc) {
-      uint32_t a[16];
-      tmem_ld16(tacc + cc * 16, a);
-      tmem_ld_wait();
-      if (valid) {
-        uint32_t u[8];
-#pragma unroll
-        for (int q = 0; q < 8; ++q)
-          u[q] = pack_bf16(__uint_as_float(a[2 * q]) * scale, __uint_as_float(a[2 * q + 1]) * scale);
-        *reinterpret_cast<uint4*>(dst + cc * 16) = make_uint4(u[0], u[1], u[2], u[3]);
-        *reinterpret_cast<uint4*>(dst + cc * 16 + 8) = make_uint4(u[4], u[5], u[6], u[7]);
-      }
-    }
-    return;
-  }
-#pragma unroll 1
-  for (int cc = 0; cc < W / 32; ++cc) {
-    uint32_t a[16], b[16];
+  for (int cc = 0; cc < W / 16; ++cc) {
+    uint32_t a[16];
     tmem_ld16(tacc + cc * 16, a);
-    tmem_ld16(tacc + W / 2 + cc * 16, b);
     tmem_ld_wait();
     if (valid) {
-      uint32_t g1[8], g2[8];
+      uint32_t u[8];
 #pragma unroll
-      for (int q = 0; q < 4; ++q) {
-        const float4 c4 = *reinterpret_cast<const float4*>(ct + cc * 16 + q * 4);
-        const float4 s4 = *reinterpret_cast<const float4*>(st + cc * 16 + q * 4);
-        const float cs[4] = {c4.x, c4.y, c4.z, c4.w}, sn[4] = {s4.x, s4.y, s4.z, s4.w};
-        float o1[4], o2[4];
-#pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          const float x1 = __uint_as_float(a[q * 4 + e]) * scale, x2 = __uint_as_float(b[q * 4 + e]) * scale;
-          o1[e] = x1 * cs[e] + x2 * sn[e];
-          o2[e] = x2 * cs[e] - x1 * sn[e];
-        }
-        g1[q * 2] = pack_bf16(o1[0], o1[1]);
-        g1[q * 2 + 1] = pack_bf16(o1[2], o1[3]);
-        g2[q * 2] = pack_bf16(o2[0], o2[1]);
-        g2[q * 2 + 1] = pack_bf16(o2[2], o2[3]);
-      }
-      *reinterpret_cast<uint4*>(dst + cc * 16) = make_uint4(g1[0], g1[1], g1[2], g1[3]);
-      *reinterpret_cast<uint4*>(dst + cc * 16 + 8) = make_uint4(g1[4], g1[5], g1[6], g1[7]);
-      *reinterpret_cast<uint4*>(dst + W / 2 + cc * 16) = make_uint4(g2[0], g2[1], g2[2], g2[3]);
-      *reinterpret_cast<uint4*>(dst + W / 2 + cc * 16 + 8) = make_uint4(g2[4], g2[5], g2[6], g2[7]);
+      for (int q = 0; q < 8; ++q)
+        u[q] = pack_bf16(__uint_as_float(a[2 * q]) * scale, __uint_as_float(a[2 * q + 1]) * scale);
+      *reinterpret_cast<uint4*>(dst + cc * 16) = make_uint4(u[0], u[1], u[2], u[3]);
+      *reinterpret_cast<uint4*>(dst + cc * 16 + 8) = make_uint4(u[4], u[5], u[6], u[7]);
     }
   }
 }
