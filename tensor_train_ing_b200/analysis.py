@@ -300,8 +300,8 @@ def normalizer_sensitivity(model, inputs, denoms, doc, max_tokens: int = 512) ->
         m.denom_mode = None
         _, auto = torch.func.jvp(lambda t: upcast(m(t)), (xs,), (delta,))
         m.denom_mode = prev
-        ana = direct + radial
-        ratio = radial.norm(dim=-1) / direct.norm(dim=-1).clamp_min(1e-30)
+        ana, auto = (direct + radial).detach(), auto.detach()
+        ratio = radial.detach().norm(dim=-1) / direct.detach().norm(dim=-1).clamp_min(1e-30)
         sites[name] = {"scope": norm_scope(m), "denominator": _quantiles(rv[valid]), "median_by_doc_position": by_pos,
                        "jvp_rel_err_analytic_vs_autograd": float((ana - auto).norm() / auto.norm().clamp_min(1e-30)),
                        "radial_over_direct_random_delta": _quantiles(ratio)}
