@@ -90,3 +90,32 @@ def test_prepare_mechanisms(tmp_path, capsys):
     r = _run(capsys, "prepare_mechanisms", "--out", tmp_path / "tasks", "--seed", 3, "--train-examples", 8,
              "--validation-examples", 8)
     assert r["manifest"]
+
+
+def test_profile_command_reports_post_warmup_steps_and_writes_a_trace(setup, capsys):
+    cfg, tmp = setup
+    r = _run(capsys, "profile", "--config", cfg, "--run-dir", tmp / "prof", "--steps", 3, "--warmup-steps", 1,
+             "--trace-steps", 1, "--max-seconds", 120, "--device", "cpu")
+    assert (r["completed_timed_steps"], r["warmup_steps"], r["completed_total_steps"]) == (3, 1, 4)
+    assert r["timed_prediction_tokens"] == 3 * 20  # three timed updates of 20 scored tokens each
+    assert r["stop_reason"] == "max_steps" and r["prediction_tokens_per_second"] > 0
+    assert (tmp / "prof" / "profile.json").exists() and (tmp / "prof" / "metrics.jsonl").exists()
+
+
+def test_branch_refuses_a_parent_still_in_warmup(setup, capsys):
+    cfg, tmp = setup
+    r = _run(capsys, "train", "--config", cfg, "--run-dir", tmp / "run", "--max-steps", 2, "--max-seconds", 120,
+             "--device", "cpu")
+    with pytest.raises(ValueError):
+        main(["branch", "--config", str(cfg), "--run-dir", str(tmp / "b"), "--max-steps", "1", "--max-seconds", "60",
+              "--device", "cpu", "--resume", r["checkpoint"], "--batch-tokens", "40", "--lr-scale", "2.0"])
+    assert not (tmp / "b" / "result.json").exists()
+
+
+def test_compare_seed_pairs_command_validates_before_writing(setup, capsys):
+    cfg, tmp = setup
+    pairs = tmp / "pairs.json"
+    pairs.write_text(json.dumps([{"seed": 1, "left": "a.json", "right": "b.json"}]))
+    with pytest.raises(ValueError, match="two"):
+        main(["compare_seed_pairs", "--pairs", str(pairs), "--out", str(tmp / "rep")])
+    assert not (tmp / "rep").exists()
