@@ -48,3 +48,36 @@ def test_launch_count_of_the_rmsnorm_backward_follows_its_kernel_path():
     for d, groups, kernels in ((2048, 1, 2), (1024, 1, 2), (4096, 1, 2), (6144, 1, 3), (2048, 4, 3), (512, 1, 3)):
         x = torch.empty(3, d)
         assert count(x, x, None, None, x, True, groups) == kernels
+
+
+def test_attention_scaling_fit_recovers_fixed_and_per_block_costs(monkeypatch):
+    """kernel_bench attn_scale: with timings exactly fixed + per_block * blocks, the fit returns them."""
+    from tensor_train_ing_b200 import kernel_bench as kb
+
+    class FakeLib:
+        def poly_fwd(self, *a):
+            return ("fwd", a[9], a[10])
+
+        def poly_bwd(self, *a):
+            return ("bwd", a[11], a[12])
+
+    blocks = {}
+
+    def fake_inputs(b, t):
+        nq = t // 128
+        blocks[(b, t)] = b * kb.H * sum(2 * (q + 1) for q in range(nq))
+        return {"pos32": 0, "doc32": 0, "doc_end32": 0}, 0, 0, 0, 0, 0, {"cos": 0, "sin": 0}
+
+    def fake_time(fn, reps=10):
+        kind, b, t = fn()
+        fixed, per = (60.0, 0.006) if kind == "fwd" else (240.0, 0.024)
+        return fixed + per * blocks[(b, t)]
+
+    monkeypatch.setattr(kb, "_lib", lambda: FakeLib())
+    monkeypatch.setattr(kb, "_attn_inputs", fake_inputs)
+    monkeypatch.setattr(kb, "_event_time", fake_time)
+    import tensor_train_ing_b200.ops._ext as ext
+    monkeypatch.setattr(ext, "check_status", lambda: None)
+    out = kb.attn_scaling(rope=True)
+    assert out["fit"]["fwd"] == {"fixed_us": pytest.approx(60.0, abs=0.2), "ns_per_block": pytest.approx(6.0, abs=0.01)}
+    assert out["fit"]["bwd"] == {"fixed_us": pytest.approx(240.0, abs=0.2), "ns_per_block": pytest.approx(24.0, abs=0.01)}
