@@ -125,6 +125,8 @@ def _require(cond: bool, msg: str):
 
 
 def _from_section(cls, section: dict[str, Any] | None):
+    if section is not None and not isinstance(section, dict):
+        raise ValueError(f"the {cls.__name__} section must be a mapping, not {type(section).__name__}")
     values = dict(section or {})
     known = {f.name for f in fields(cls)}
     extra = sorted(set(values) - known)
@@ -141,6 +143,9 @@ class Config:
 
     @classmethod
     def from_dict(cls, raw: dict) -> "Config":
+        if raw is not None and not isinstance(raw, dict):
+            # e.g. a sweep candidate list: dict() would read each two-key entry as a key/value pair
+            raise ValueError(f"a configuration must be a mapping of sections, not {type(raw).__name__}")
         raw = dict(raw or {})
         return cls(model=_from_section(ModelConfig, raw.get("model")),
                    train=_from_section(TrainConfig, raw.get("train")), raw=raw)
