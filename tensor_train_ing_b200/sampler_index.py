@@ -3,8 +3,11 @@
 ``<dataset>/.sampler-index-v1/<split>.index.bin`` holds one 40-byte record per document of the split
 (int64 token_start, token_end, numeric_id, byte offset and length of its ``documents.jsonl`` line),
 so samplers over large corpora touch only the rows they pack instead of parsing all metadata.
-The index is derived data: it is verified against the manifest's documents.jsonl checksum and
-rebuilt when missing or stale; several ranks may share it read-only.
+``index.json`` beside them records the source identity (sha256 of the canonical manifest and of
+documents.jsonl), the row layout and each split's count, size and sha256.  Directory, files, rows
+and header are the reference platform's, so either framework reads an index the other built.  The
+index is derived data: it is verified on load and rebuilt when missing or stale (the reference
+instead asks for an explicit rebuild); builds take the dataset's ``.sampler-index-v1.lock``.
 """
 from __future__ import annotations
 
@@ -21,12 +24,34 @@ import numpy as np
 from .token_format import SPLIT_ORDER
 
 INDEX_DIR = ".sampler-index-v1"
-RECORD = np.dtype([("token_start", "<i8"), ("token_end", "<i8"), ("numeric_id", "<i8"), ("offset", "<i8"),
-                   ("length", "<i8")])
+RECORD = np.dtype([("token_start", "<i8"), ("token_end", "<i8"), ("numeric_id", "<i8"),
+                   ("metadata_offset", "<i8"), ("metadata_length", "<i8")])
+INDEX_VERSION = 1
 
 
 def _identity(manifest) -> dict:
-    return {"version": 1, "documents_sha256": manifest["artifacts"]["documents.jsonl"]}
+    """The manifest's canonical text is what ``manifest.json`` holds once published (and what
+    ``manifest.sha256`` covers), so the identity is the same before and after publication."""
+    canonical = json.dumps(manifest, sort_keys=True, indent=2) + "\n"
+    return {"manifest_sha256": hashlib.sha256(canonical.encode("utf-8")).hexdigest(),
+            "documents_sha256": manifest["artifacts"]["documents.jsonl"]}
+
+
+def _file_sha256(path: Path) -> str:
+    h = hashlib.sha256()
+    with path.open("rb") as fh:
+        for block in iter(lambda: fh.read(1 << 20), b""):
+            h.update(block)
+    return h.hexdigest()
+
+
+def _write_atomic(path: Path, data: bytes):
+    fd, tmp = tempfile.mkstemp(dir=path.parent, prefix=f".{path.name}-")
+    with os.fdopen(fd, "wb") as out:
+        out.write(data)
+        out.flush()
+        os.fsync(out.fileno())
+    os.replace(tmp, path)
 
 
 def _build(root: Path, manifest, cache: Path):
@@ -38,39 +63,40 @@ def _build(root: Path, manifest, cache: Path):
             per_split[doc["split"]].append((doc["token_start"], doc["token_end"], doc["numeric_id"], offset, len(raw)))
             offset += len(raw)
     cache.mkdir(exist_ok=True)
+    splits = {}
     for split, rows in per_split.items():
         arr = np.array(rows, dtype=RECORD) if rows else np.empty(0, dtype=RECORD)
-        fd, tmp = tempfile.mkstemp(dir=cache, prefix=f".{split}-")
-        with os.fdopen(fd, "wb") as out:
-            out.write(arr.tobytes())
-            out.flush()
-            os.fsync(out.fileno())
-        os.replace(tmp, cache / f"{split}.index.bin")
-    meta = {"identity": _identity(manifest), "counts": {s: len(r) for s, r in per_split.items()}}
-    fd, tmp = tempfile.mkstemp(dir=cache, prefix=".identity-")
-    with os.fdopen(fd, "w") as out:
-        json.dump(meta, out, sort_keys=True)
-        out.flush()
-        os.fsync(out.fileno())
-    os.replace(tmp, cache / "identity.json")
+        _write_atomic(cache / f"{split}.index.bin", arr.tobytes())
+        splits[split] = {"count": len(rows), "bytes": arr.nbytes, "sha256": _file_sha256(cache / f"{split}.index.bin")}
+    header = {"index_version": INDEX_VERSION, "identity": _identity(manifest), "row_bytes": RECORD.itemsize,
+              "fields": list(RECORD.names), "splits": splits}
+    _write_atomic(cache / "index.json", (json.dumps(header, sort_keys=True, indent=2) + "\n").encode("utf-8"))
+    (cache / "identity.json").unlink(missing_ok=True)  # header of an earlier layout
+
+
+def _valid(cache: Path, manifest) -> bool:
+    try:
+        header = json.loads((cache / "index.json").read_text())
+        if (header["index_version"] != INDEX_VERSION or header["identity"] != _identity(manifest)
+                or header["row_bytes"] != RECORD.itemsize or header["fields"] != list(RECORD.names)
+                or set(header["splits"]) != set(SPLIT_ORDER)):
+            return False
+        for split in SPLIT_ORDER:
+            info, path = header["splits"][split], cache / f"{split}.index.bin"
+            if (info["bytes"] != info["count"] * RECORD.itemsize or path.stat().st_size != info["bytes"]
+                    or _file_sha256(path) != info["sha256"]):
+                return False
+        return True
+    except (OSError, ValueError, KeyError, TypeError):
+        return False
 
 
 def ensure_sampler_index(root, manifest, *, rebuild: bool = False) -> Path:
     root = Path(root)
     cache = root / INDEX_DIR
-    cache.mkdir(exist_ok=True)
-    with (cache / "build.lock").open("a") as lock:
+    with (root / f"{INDEX_DIR}.lock").open("a+b") as lock:
         fcntl.flock(lock, fcntl.LOCK_EX)
-        ok = False
-        if not rebuild:
-            try:
-                meta = json.loads((cache / "identity.json").read_text())
-                ok = meta["identity"] == _identity(manifest) and all(
-                    (cache / f"{s}.index.bin").stat().st_size == meta["counts"][s] * RECORD.itemsize
-                    for s in SPLIT_ORDER)
-            except (OSError, ValueError, KeyError):
-                ok = False
-        if not ok:
+        if rebuild or not _valid(cache, manifest):
             _build(root, manifest, cache)
     return cache
 
@@ -120,8 +146,8 @@ class IndexedDocuments(Sequence):
     def full_document(self, i):
         r = self.rows[i]
         with self._meta.open("rb") as fh:
-            fh.seek(int(r["offset"]))
-            return json.loads(fh.read(int(r["length"])))
+            fh.seek(int(r["metadata_offset"]))
+            return json.loads(fh.read(int(r["metadata_length"])))
 
     def __len__(self):
         return len(self.rows)

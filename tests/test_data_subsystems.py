@@ -43,12 +43,14 @@ def test_stale_or_corrupt_index_is_rebuilt(dataset):
     (root / INDEX_DIR / "train.index.bin").write_bytes(b"\0" * 7)  # truncated / corrupt
     idx = load_sampler_index(root, manifest, "train")
     assert index_digest(root) == good and len(idx) > 0
-    ident = root / INDEX_DIR / "identity.json"
-    meta = json.loads(ident.read_text())
+    header = root / INDEX_DIR / "index.json"
+    meta = json.loads(header.read_text())
     meta["identity"]["documents_sha256"] = "0" * 64  # built for other metadata
-    ident.write_text(json.dumps(meta))
+    header.write_text(json.dumps(meta))
     load_sampler_index(root, manifest, "train")
-    assert json.loads(ident.read_text())["identity"]["documents_sha256"] == manifest["artifacts"]["documents.jsonl"]
+    assert json.loads(header.read_text())["identity"]["documents_sha256"] == manifest["artifacts"]["documents.jsonl"]
+    assert json.loads(header.read_text())["identity"]["manifest_sha256"] == \
+        (root / "manifest.sha256").read_text().strip()
     with pytest.raises(ValueError):
         load_sampler_index(root, manifest, "holdout")
 

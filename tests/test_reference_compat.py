@@ -73,3 +73,50 @@ def test_same_seed_same_initialisation(tnlm):
     assert rs.keys() == os_.keys()
     for k in rs:
         assert torch.equal(rs[k], os_[k]), k
+
+
+def _dataset(tmp_path, n=120):
+    import json
+    import random
+
+    from helpers import FixtureTokenizer
+    from tensor_train_ing_b200.data import prepare_data
+    rnd = random.Random(0)
+    src = tmp_path / "src.jsonl"
+    src.write_text("".join(json.dumps({"id": f"d{i}", "text": "".join(rnd.choice("abcdefgh ")
+                                                                         for _ in range(rnd.randint(3, 90)))}) + "\n"
+                           for i in range(n)))
+    return prepare_data(tmp_path / "data", source_jsonl=src, revision="offline-v1", tokenizer=FixtureTokenizer(),
+                        split_fractions={"train": .8, "val": .1, "test": 0., "calibration": .1})
+
+
+def test_datasets_sampler_index_and_batches_are_shared_with_the_reference(tnlm, tmp_path):
+    """A dataset prepared here, with the sampler index built here, is accepted by the reference's
+    verifier, and both frameworks' packed samplers (and rank samplers) yield identical batches."""
+    import shutil
+
+    import tnlm.data as ref_data
+
+    from tensor_train_ing_b200.data import PackedSampler, RankPackedSampler
+    from tensor_train_ing_b200.sampler_index import INDEX_DIR
+    manifest = _dataset(tmp_path)
+    for split in ("train", "val", "calibration"):
+        for ctx, rows, seed in ((16, 4, 0), (33, 3, 7)):
+            ours = PackedSampler(manifest, split=split, batch_size=rows, context=ctx, seed=seed)
+            theirs = ref_data.PackedSampler(manifest, split=split, batch_size=rows, context=ctx, seed=seed)
+            for _ in range(25):
+                for a, b in zip(ours.next_batch(), theirs.next_batch()):
+                    assert torch.equal(a, b)
+    for r in range(3):
+        ours = RankPackedSampler(manifest, rank=r, world_size=3, batch_size=2, context=16, seed=5)
+        theirs = ref_data.RankPackedSampler(manifest, rank=r, world_size=3, batch_size=2, context=16, seed=5)
+        for _ in range(10):
+            for a, b in zip(ours.next_batch(), theirs.next_batch()):
+                assert torch.equal(a, b)
+    # an index the reference built is accepted here without a rebuild
+    root = manifest.parent
+    shutil.rmtree(root / INDEX_DIR)
+    ref_data.PackedSampler(manifest, split="train", batch_size=1, context=16, seed=0)
+    built = {p.name: p.stat().st_mtime_ns for p in (root / INDEX_DIR).iterdir()}
+    PackedSampler(manifest, split="train", batch_size=1, context=16, seed=0)
+    assert {p.name: p.stat().st_mtime_ns for p in (root / INDEX_DIR).iterdir()} == built
