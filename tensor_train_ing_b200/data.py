@@ -274,7 +274,14 @@ def _prepare(out, source_jsonl, revision, max_tokens, max_documents, tokenizer, 
                                  "split": "UTF8(stable document ID)"},
                 "bounded_selection": "smallest domain-separated selection SHA256 ranks across entire declared "
                                      "source; canonical rank order then token cap",
-                "token_offset_semantics": "source_token_* include the synthetic EOS; processed_token_* exclude it",
+                # The two descriptive strings below are the reference's wording, byte for byte: the
+                # manifest's sha256 is the dataset identity that checkpoints and resumes compare, so
+                # the same source must give the same manifest in both frameworks.
+                "token_offset_semantics": ("source_token_* are legacy processed document stream offsets including "
+                                           "synthetic EOS; processed_token_* exclude EOS; no original "
+                                           "character/byte alignment"),
+                "preparation_cost": ("full declared source scan and HF raw-shard download/hash; output "
+                                     "token/document bounds do not bound scan cost"),
                 "boundary_loss_policy": "ignore cross-document transitions and padding", "artifacts": artifacts}
     if heldout is not None:
         manifest["heldout_exclusion"] = {"excluded_unique_documents": excluded,

@@ -120,3 +120,28 @@ def test_datasets_sampler_index_and_batches_are_shared_with_the_reference(tnlm, 
     built = {p.name: p.stat().st_mtime_ns for p in (root / INDEX_DIR).iterdir()}
     PackedSampler(manifest, split="train", batch_size=1, context=16, seed=0)
     assert {p.name: p.stat().st_mtime_ns for p in (root / INDEX_DIR).iterdir()} == built
+
+
+def test_the_same_source_prepares_byte_identical_datasets(tnlm, tmp_path):
+    """Dataset preparation here and in the reference give the same bytes for every artifact, so the
+    manifest sha256 (the dataset identity that checkpoints and resumes compare) is shared."""
+    import json
+    import random
+
+    import tnlm.data as ref_data
+
+    from helpers import FixtureTokenizer
+    from tensor_train_ing_b200.data import prepare_data
+    rnd = random.Random(3)
+    src = tmp_path / "src.jsonl"
+    src.write_text("".join(json.dumps({"id": f"d{i}", "text": "".join(rnd.choice("abc\r\n xyz")
+                                                                         for _ in range(rnd.randint(1, 80)))}) + "\n"
+                           for i in range(90)))
+    kw = dict(source_jsonl=src, revision="offline-v1", max_documents=70,
+              split_fractions={"train": .7, "val": .1, "test": .1, "calibration": .1})
+    prepare_data(tmp_path / "ours", tokenizer=FixtureTokenizer(), **kw)
+    ref_data.prepare_data(tmp_path / "ref", tokenizer=FixtureTokenizer(), **kw)
+    names = sorted(p.name for p in (tmp_path / "ours").iterdir() if p.is_file())
+    assert "manifest.json" in names and "documents.jsonl" in names
+    for name in names:
+        assert (tmp_path / "ours" / name).read_bytes() == (tmp_path / "ref" / name).read_bytes(), name
