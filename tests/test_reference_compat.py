@@ -145,3 +145,36 @@ def test_the_same_source_prepares_byte_identical_datasets(tnlm, tmp_path):
     assert "manifest.json" in names and "documents.jsonl" in names
     for name in names:
         assert (tmp_path / "ours" / name).read_bytes() == (tmp_path / "ref" / name).read_bytes(), name
+
+
+def test_schedules_and_optimizer_updates_match_the_reference(tnlm):
+    import tnlm.schedules as ref_sched
+
+    from tensor_train_ing_b200 import schedules
+    from tensor_train_ing_b200.config import ModelConfig, TrainConfig
+    from tensor_train_ing_b200.models.model import TensorLM
+    from tensor_train_ing_b200.optim import make_optimizer
+    for total in (1, 7, 150, 1000, 12345):
+        for kind in ("constant_with_separate_cooldown", "cosine"):
+            for step in sorted({0, 1, 2, total // 3, max(0, total - 2), total - 1, total, total + 5}):
+                assert schedules.schedule_multiplier(step, total, schedule=kind) == \
+                    ref_sched.schedule_multiplier(step, total, schedule=kind), (total, kind, step)
+    mk = dict(layers=2, d_model=16, heads=2, d_key=8, d_value=8, d_mlp=24, vocab_size=40, padded_vocab=64)
+    for opt in ("adamw", "muon"):
+        tk = dict(optimizer=opt, lr=1e-2, aux_adamw_lr=3e-3, compile=False, bf16_compute=False)
+        torch.manual_seed(0)
+        ours = TensorLM(ModelConfig(**mk))
+        ref = tnlm.model.TensorLM(tnlm.config.ModelConfig(**mk))
+        ref.load_state_dict(ours.state_dict())
+        o_ours, o_ref = make_optimizer(ours, TrainConfig(**tk)), tnlm.optim.make_optimizer(ref, tnlm.config.TrainConfig(**tk))
+        for step in range(3):
+            g = torch.Generator().manual_seed(step)
+            grads = {k: torch.randn(p.shape, generator=g) * 0.01 for k, p in ours.named_parameters()}
+            for model in (ours, ref):
+                for k, p in model.named_parameters():
+                    p.grad = grads[k].clone()
+            o_ours.step()
+            o_ref.step()
+        ref_params = dict(ref.named_parameters())
+        for k, p in ours.named_parameters():
+            assert torch.equal(p, ref_params[k]), (opt, k)  # bit-identical updates
