@@ -154,11 +154,17 @@ def test_schedules_and_optimizer_updates_match_the_reference(tnlm):
     from tensor_train_ing_b200.config import ModelConfig, TrainConfig
     from tensor_train_ing_b200.models.model import TensorLM
     from tensor_train_ing_b200.optim import make_optimizer
+    def outcome(fn, *args, **kwargs):  # the value, or the exception type (short cosine horizons are refused)
+        try:
+            return fn(*args, **kwargs)
+        except Exception as e:  # noqa: BLE001
+            return type(e).__name__
+
     for total in (1, 7, 150, 1000, 12345):
         for kind in ("constant_with_separate_cooldown", "cosine"):
             for step in sorted({0, 1, 2, total // 3, max(0, total - 2), total - 1, total, total + 5}):
-                assert schedules.schedule_multiplier(step, total, schedule=kind) == \
-                    ref_sched.schedule_multiplier(step, total, schedule=kind), (total, kind, step)
+                assert outcome(schedules.schedule_multiplier, step, total, schedule=kind) == \
+                    outcome(ref_sched.schedule_multiplier, step, total, schedule=kind), (total, kind, step)
     mk = dict(layers=2, d_model=16, heads=2, d_key=8, d_value=8, d_mlp=24, vocab_size=40, padded_vocab=64)
     for opt in ("adamw", "muon"):
         tk = dict(optimizer=opt, lr=1e-2, aux_adamw_lr=3e-3, compile=False, bf16_compute=False)
