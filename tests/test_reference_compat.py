@@ -29,7 +29,6 @@ def tnlm():
 @pytest.mark.parametrize("normalization", ["pre_rms", "group_rms", "sandwich_rms", "spectral_rms"])
 @pytest.mark.parametrize("attention", ["signed_product", "offset_square", "lower_degree_mix"])
 def test_reference_checkpoint_loads_with_identical_logits(tnlm, tmp_path, normalization, attention):
-    from tensor_train_ing_b200.checkpoint import load_checkpoint
     from tensor_train_ing_b200.config import ModelConfig
     from tensor_train_ing_b200.models.model import TensorLM
     kw = dict(TINY_MODEL, normalization=normalization, attention=attention)
@@ -184,3 +183,47 @@ def test_schedules_and_optimizer_updates_match_the_reference(tnlm):
         ref_params = dict(ref.named_parameters())
         for k, p in ours.named_parameters():
             assert torch.equal(p, ref_params[k]), (opt, k)  # bit-identical updates
+
+
+@pytest.mark.parametrize("optimizer,normalization", [("adamw", "pre_rms"), ("muon", "pre_rms"),
+                                                     ("muon", "group_rms"), ("adamw", "lagged")])
+def test_serial_training_trajectories_match_the_reference(tnlm, tmp_path, optimizer, normalization):
+    """Both frameworks' serial trainers on one YAML config and dataset (CPU): identical per-step losses
+    and identical final weights (lagged norms include the calibration before the first update)."""
+    import json
+
+    import tnlm.train as ref_train
+    import yaml
+
+    from helpers import FixtureTokenizer
+    from tensor_train_ing_b200.config import Config
+    from tensor_train_ing_b200.data import prepare_data
+    from tensor_train_ing_b200.train import train_run
+    torch.set_num_threads(1)
+    src = tmp_path / "src.jsonl"
+    src.write_text("".join(json.dumps({"id": f"doc-{i}", "text": f"text number {i} " * 3}) + "\n" for i in range(60)))
+    manifest = prepare_data(tmp_path / "data", source_jsonl=src, revision="offline-v1", tokenizer=FixtureTokenizer(),
+                            split_fractions={"train": .6, "val": .3, "test": 0., "calibration": .1})
+    model = {"layers": 2, "d_model": 8, "heads": 1, "d_key": 4, "d_value": 4, "d_mlp": 12, "padded_vocab": 50257,
+             "normalization": normalization}
+    if normalization == "lagged":
+        model["final_normalization"] = "lagged"
+    runs = {}
+    for who, run in (("ours", train_run), ("reference", ref_train.train_run)):
+        doc = {"model": model,
+               "train": {"compile": False, "bf16_compute": False, "global_prediction_tokens_per_update": 20,
+                         "rung_total_tokens": 200, "lr": 0.01, "optimizer": optimizer, "aux_adamw_lr": 0.003},
+               "data": {"manifest": str(manifest), "context": 16, "micro_batch_size": 2, "calibration_tokens": 8},
+               "project": {"dry_run": False, "gpu_hourly_rate_usd": 0, "spend_ledger": str(tmp_path / f"{who}.json")}}
+        path = tmp_path / f"{who}.yaml"
+        path.write_text(yaml.safe_dump(doc))
+        cfg = Config.from_yaml(str(path)) if who == "ours" else tnlm.config.Config.from_yaml(str(path))
+        result = run(cfg, tmp_path / who, max_steps=5, max_seconds=120, device="cpu")
+        losses = [json.loads(l)["loss"] for l in (tmp_path / who / "metrics.jsonl").read_text().splitlines()]
+        runs[who] = (losses, result["checkpoint"])
+    assert len(runs["ours"][0]) == 5 and runs["ours"][0] == runs["reference"][0]
+    ours = torch.load(f"{runs['ours'][1]}/state.pt", weights_only=False)["model"]
+    theirs = torch.load(f"{runs['reference'][1]}/state.pt", weights_only=False)["model"]
+    assert ours.keys() == theirs.keys()
+    for k in ours:
+        assert torch.equal(ours[k], theirs[k]), k
