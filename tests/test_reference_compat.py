@@ -227,3 +227,43 @@ def test_serial_training_trajectories_match_the_reference(tnlm, tmp_path, optimi
     assert ours.keys() == theirs.keys()
     for k in ours:
         assert torch.equal(ours[k], theirs[k]), k
+
+
+def test_evaluation_reports_agree_and_cross_compare_with_the_reference(tnlm, tmp_path):
+    """One checkpoint evaluated by both frameworks: identical held-out CE and per-document losses, and
+    each framework's paired comparator accepts the other's report (provenance fields differ)."""
+    import json
+
+    import tnlm.evaluate as ref_eval
+    import yaml
+
+    from helpers import FixtureTokenizer
+    from tensor_train_ing_b200.config import Config
+    from tensor_train_ing_b200.data import prepare_data
+    from tensor_train_ing_b200.evaluate import compare_evaluations, evaluate_checkpoint
+    from tensor_train_ing_b200.train import train_run
+    torch.set_num_threads(1)
+    src = tmp_path / "src.jsonl"
+    src.write_text("".join(json.dumps({"id": f"doc-{i}", "text": f"text number {i} " * 3}) + "\n" for i in range(60)))
+    manifest = prepare_data(tmp_path / "data", source_jsonl=src, revision="offline-v1", tokenizer=FixtureTokenizer(),
+                            split_fractions={"train": .6, "val": .3, "test": 0., "calibration": .1})
+    doc = {"model": {"layers": 2, "d_model": 8, "heads": 1, "d_key": 4, "d_value": 4, "d_mlp": 12,
+                     "padded_vocab": 50257},
+           "train": {"compile": False, "bf16_compute": False, "global_prediction_tokens_per_update": 20,
+                     "rung_total_tokens": 200, "lr": 0.01},
+           "data": {"manifest": str(manifest), "context": 16, "micro_batch_size": 2},
+           "project": {"dry_run": False, "gpu_hourly_rate_usd": 0, "spend_ledger": str(tmp_path / "spend.json")}}
+    path = tmp_path / "run.yaml"
+    path.write_text(yaml.safe_dump(doc))
+    ckpt = train_run(Config.from_yaml(str(path)), tmp_path / "run", max_steps=3, max_seconds=120,
+                     device="cpu")["checkpoint"]
+    ours = evaluate_checkpoint(Config.from_yaml(str(path)), ckpt, tmp_path / "ours", max_seconds=120,
+                               bootstrap_samples=20)
+    theirs = ref_eval.evaluate_checkpoint(tnlm.config.Config.from_yaml(str(path)), ckpt, tmp_path / "ref",
+                                          max_seconds=120, bootstrap_samples=20)
+    assert ours["ce"] == theirs["ce"] and ours["prediction_tokens"] == theirs["prediction_tokens"]
+    assert ours["per_document"] == theirs["per_document"]
+    a, b = tmp_path / "ours" / "evaluation.json", tmp_path / "ref" / "evaluation.json"
+    for compare in (compare_evaluations, ref_eval.compare_evaluations):
+        for left, right in ((a, b), (b, a)):
+            assert compare(left, right, None, bootstrap_samples=10)["delta_ce_right_minus_left"] == 0.0
