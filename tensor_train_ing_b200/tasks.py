@@ -116,7 +116,18 @@ def prepare_mechanism_tasks(output_dir, seed=0, train_examples=32, validation_ex
                                   "balanced_boolean_max_per_split": {"train": 36, "val": 42}},
                 "composition_splits": {t: {s: sorted({r["composition_id"] for r in rows[s] if r["task"] == t})
                                            for s in rows} for t in _MECHANISM_TASKS},
-                "tokenizer": {"name": "gpt2", "answer_contract": "leading-space digit 0..3; evaluator verifies one token"},
+                # descriptive fields in the reference's wording: the manifest's sha256 identifies the
+                # task set, so both frameworks must write the same bytes for the same seed and sizes
+                "composition_definition": {
+                    "associative_retrieval": ("full A/B/C/D to 0/1/2/3 mapping, values may repeat; seeded permutation "
+                                              "of256 maps, first192 train, last64 val"),
+                    "boolean_hierarchy": ("operator triple [left,right,root]; even AND count train, odd val; all four "
+                                          "bits enumerated")},
+                "label_definition": {
+                    "associative_retrieval": "value for exact query key",
+                    "boolean_hierarchy": "root(left(bit0,bit1),right(bit2,bit3)); xor is exclusive-or, and is conjunction"},
+                "tokenizer": {"name": "gpt2",
+                              "answer_contract": "leading-space digit 0..3; evaluator verifies exactly one token"},
                 "scope": "exact-label synthetic mechanism probes with held-out compositions; no final-test or LM-quality claim"}
     out = Path(output_dir)
     out.mkdir(parents=True, exist_ok=False)

@@ -267,3 +267,17 @@ def test_evaluation_reports_agree_and_cross_compare_with_the_reference(tnlm, tmp
     for compare in (compare_evaluations, ref_eval.compare_evaluations):
         for left, right in ((a, b), (b, a)):
             assert compare(left, right, None, bootstrap_samples=10)["delta_ce_right_minus_left"] == 0.0
+
+
+def test_mechanism_task_sets_are_byte_identical_to_the_reference(tnlm, tmp_path):
+    import tnlm.tasks as ref_tasks
+
+    from tensor_train_ing_b200.tasks import prepare_mechanism_tasks
+    for seed, train, val in ((0, 8, 8), (7, 32, 16)):
+        prepare_mechanism_tasks(tmp_path / f"ours{seed}", seed=seed, train_examples=train, validation_examples=val)
+        ref_tasks.prepare_mechanism_tasks(tmp_path / f"ref{seed}", seed=seed, train_examples=train,
+                                          validation_examples=val)
+        names = sorted(p.name for p in (tmp_path / f"ours{seed}").iterdir() if p.is_file())
+        assert names == sorted(p.name for p in (tmp_path / f"ref{seed}").iterdir() if p.is_file())
+        for name in names:
+            assert (tmp_path / f"ours{seed}" / name).read_bytes() == (tmp_path / f"ref{seed}" / name).read_bytes()
