@@ -29,6 +29,7 @@ def tnlm():
 @pytest.mark.parametrize("normalization", ["pre_rms", "group_rms", "sandwich_rms", "spectral_rms"])
 @pytest.mark.parametrize("attention", ["signed_product", "offset_square", "lower_degree_mix"])
 def test_reference_checkpoint_loads_with_identical_logits(tnlm, tmp_path, normalization, attention):
+    from tensor_train_ing_b200.checkpoint import load_checkpoint
     from tensor_train_ing_b200.config import ModelConfig
     from tensor_train_ing_b200.models.model import TensorLM
     kw = dict(TINY_MODEL, normalization=normalization, attention=attention)
