@@ -282,3 +282,41 @@ def test_mechanism_task_sets_are_byte_identical_to_the_reference(tnlm, tmp_path)
         assert names == sorted(p.name for p in (tmp_path / f"ref{seed}").iterdir() if p.is_file())
         for name in names:
             assert (tmp_path / f"ours{seed}" / name).read_bytes() == (tmp_path / f"ref{seed}" / name).read_bytes()
+
+
+def test_run_summaries_read_reference_run_directories(tnlm, tmp_path):
+    """`summarize` over one run of each framework (same config and data): the reference's result.json,
+    metrics and ledger are read like ours, and every non-timing field of the two rows agrees."""
+    import json
+
+    import tnlm.train as ref_train
+    import yaml
+
+    from helpers import FixtureTokenizer
+    from tensor_train_ing_b200.config import Config
+    from tensor_train_ing_b200.data import prepare_data
+    from tensor_train_ing_b200.reporting import summarize_runs
+    from tensor_train_ing_b200.train import train_run
+    torch.set_num_threads(1)
+    src = tmp_path / "src.jsonl"
+    src.write_text("".join(json.dumps({"id": f"doc-{i}", "text": f"text number {i} " * 3}) + "\n" for i in range(60)))
+    manifest = prepare_data(tmp_path / "data", source_jsonl=src, revision="offline-v1", tokenizer=FixtureTokenizer(),
+                            split_fractions={"train": .6, "val": .3, "test": 0., "calibration": .1})
+    doc = {"model": {"layers": 2, "d_model": 8, "heads": 1, "d_key": 4, "d_value": 4, "d_mlp": 12,
+                     "padded_vocab": 50257},
+           "train": {"compile": False, "bf16_compute": False, "global_prediction_tokens_per_update": 20,
+                     "rung_total_tokens": 200, "lr": 0.01},
+           "data": {"manifest": str(manifest), "context": 16, "micro_batch_size": 2},
+           "project": {"dry_run": False, "gpu_hourly_rate_usd": 0, "spend_ledger": str(tmp_path / "spend.json")}}
+    path = tmp_path / "run.yaml"
+    path.write_text(yaml.safe_dump(doc))
+    train_run(Config.from_yaml(str(path)), tmp_path / "ours", max_steps=3, max_seconds=120, device="cpu")
+    ref_train.train_run(tnlm.config.Config.from_yaml(str(path)), tmp_path / "ref", max_steps=3, max_seconds=120,
+                        device="cpu")
+    out = summarize_runs([tmp_path / "ours", tmp_path / "ref"], tmp_path / "summary")
+    assert out["runs"] == 2
+    rows = json.loads((tmp_path / "summary" / "comparison.json").read_text())["runs"]
+    timing = {"run", "run_elapsed_seconds", "run_billed_usd", "step_average_prediction_tokens_per_second",
+              "cuda_peak_allocated_bytes", "cuda_peak_reserved_bytes"}
+    assert {k: v for k, v in rows[0].items() if k not in timing} == {k: v for k, v in rows[1].items()
+                                                                    if k not in timing}
