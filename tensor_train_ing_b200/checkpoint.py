@@ -166,7 +166,8 @@ def save_checkpoint(path, model, optimizer, sampler, *, config, progress, manife
     payload = {
         "format_version": FORMAT_VERSION, "model": model.state_dict(),
         "model_class": f"{type(model).__module__}.{type(model).__qualname__}",
-        "optimizer_class": f"{type(optimizer).__module__}.{type(optimizer).__qualname__}" if optimizer else None,
+        "optimizer_class": (getattr(optimizer, "checkpoint_class", None)
+                            or f"{type(optimizer).__module__}.{type(optimizer).__qualname__}") if optimizer else None,
         "optimizer": optimizer.state_dict() if optimizer is not None else None,
         "sampler": sampler.state_dict() if sampler is not None else None,
         "scheduler": scheduler.state_dict() if scheduler is not None else None,

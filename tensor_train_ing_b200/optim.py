@@ -143,6 +143,11 @@ class Muon(torch.optim.Optimizer):
 class MuonAdamW(torch.optim.Optimizer):
     """Muon on hidden matrices plus AdamW on the rest, presented as one optimizer."""
 
+    # Identity written into checkpoints: the reference platform's class of the same optimizer (same
+    # updates and state layout), whose loader requires that exact name, so either framework resumes
+    # the other's Muon runs.  This framework's loader accepts both names.
+    checkpoint_class = "tnlm.optim.MuonAdamW"
+
     def __init__(self, model, *, lr, aux_lr, weight_decay, betas, momentum=0.95, nesterov=True,
                  adjust_lr_fn="match_rms_adamw", vocab_weight_decay=0.0, only=None):
         hidden, vocab, small = param_split(model, only)

@@ -359,3 +359,41 @@ def test_a_reference_run_resumed_here_continues_exactly(tnlm, tmp_path, optimize
     a = torch.load(f"{full['checkpoint']}/state.pt", weights_only=False)["model"]
     b = torch.load(f"{rest['checkpoint']}/state.pt", weights_only=False)["model"]
     assert a.keys() == b.keys() and all(torch.equal(a[k], b[k]) for k in a)
+
+
+@pytest.mark.parametrize("optimizer", ["adamw", "muon"])
+def test_a_run_from_here_resumed_by_the_reference_continues_exactly(tnlm, tmp_path, optimizer):
+    """The reverse direction: 3 steps here, 2 more in the reference trainer from our checkpoint, equal
+    to an uninterrupted 5-step run here (our Muon checkpoints carry the reference's optimizer identity,
+    which its loader requires)."""
+    import json
+
+    import tnlm.train as ref_train
+    import yaml
+
+    from helpers import FixtureTokenizer
+    from tensor_train_ing_b200.config import Config
+    from tensor_train_ing_b200.data import prepare_data
+    from tensor_train_ing_b200.train import train_run
+    torch.set_num_threads(1)
+    src = tmp_path / "src.jsonl"
+    src.write_text("".join(json.dumps({"id": f"doc-{i}", "text": f"text number {i} " * 3}) + "\n" for i in range(60)))
+    manifest = prepare_data(tmp_path / "data", source_jsonl=src, revision="offline-v1", tokenizer=FixtureTokenizer(),
+                            split_fractions={"train": .6, "val": .3, "test": 0., "calibration": .1})
+    doc = {"model": {"layers": 2, "d_model": 8, "heads": 1, "d_key": 4, "d_value": 4, "d_mlp": 12,
+                     "padded_vocab": 50257},
+           "train": {"compile": False, "bf16_compute": False, "global_prediction_tokens_per_update": 20,
+                     "rung_total_tokens": 200, "lr": 0.01, "optimizer": optimizer, "aux_adamw_lr": 0.003},
+           "data": {"manifest": str(manifest), "context": 16, "micro_batch_size": 2},
+           "project": {"dry_run": False, "gpu_hourly_rate_usd": 0, "spend_ledger": str(tmp_path / "spend.json")}}
+    path = tmp_path / "run.yaml"
+    path.write_text(yaml.safe_dump(doc))
+    full = train_run(Config.from_yaml(str(path)), tmp_path / "full", max_steps=5, max_seconds=120, device="cpu")
+    first = train_run(Config.from_yaml(str(path)), tmp_path / "first", max_steps=3, max_seconds=120, device="cpu")
+    rest = ref_train.train_run(tnlm.config.Config.from_yaml(str(path)), tmp_path / "rest", max_steps=2,
+                               max_seconds=120, device="cpu", resume=first["checkpoint"])
+    losses = lambda d: [json.loads(l)["loss"] for l in (tmp_path / d / "metrics.jsonl").read_text().splitlines()]  # noqa: E731
+    assert losses("full") == losses("first") + losses("rest")
+    a = torch.load(f"{full['checkpoint']}/state.pt", weights_only=False)["model"]
+    b = torch.load(f"{rest['checkpoint']}/state.pt", weights_only=False)["model"]
+    assert a.keys() == b.keys() and all(torch.equal(a[k], b[k]) for k in a)
