@@ -397,3 +397,21 @@ def test_a_run_from_here_resumed_by_the_reference_continues_exactly(tnlm, tmp_pa
     a = torch.load(f"{full['checkpoint']}/state.pt", weights_only=False)["model"]
     b = torch.load(f"{rest['checkpoint']}/state.pt", weights_only=False)["model"]
     assert a.keys() == b.keys() and all(torch.equal(a[k], b[k]) for k in a)
+
+
+def test_checkpoint_storage_plans_match_the_reference(tnlm):
+    """Milestones, retention and the disk forecast agree field for field (the reference adds a descriptive
+    `assumptions` list, partly about its DCP layout, which this plan does not carry)."""
+    import tnlm.checkpoint_plan as ref_plan
+
+    from tensor_train_ing_b200 import checkpoint_plan
+    from tensor_train_ing_b200.config import Config, ModelConfig, TrainConfig
+    mk = dict(layers=4, d_model=256, heads=4, d_key=64, d_value=64, d_mlp=768)
+    for optimizer in ("adamw", "muon"):
+        for rung, batch in ((10_000_000, 8192), (2_000_000_000, 524288)):
+            tk = dict(optimizer=optimizer, rung_total_tokens=rung, global_prediction_tokens_per_update=batch)
+            ours = checkpoint_plan.checkpoint_storage_plan(Config(model=ModelConfig(**mk), train=TrainConfig(**tk)))
+            theirs = ref_plan.checkpoint_storage_plan(tnlm.config.Config(model=tnlm.config.ModelConfig(**mk),
+                                                                         train=tnlm.config.TrainConfig(**tk)))
+            assert set(theirs) - set(ours) == {"assumptions"} and not set(ours) - set(theirs)
+            assert all(ours[k] == theirs[k] for k in ours), (optimizer, rung)
