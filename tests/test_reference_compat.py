@@ -415,3 +415,36 @@ def test_checkpoint_storage_plans_match_the_reference(tnlm):
                                                                          train=tnlm.config.TrainConfig(**tk)))
             assert set(theirs) - set(ours) == {"assumptions"} and not set(ours) - set(theirs)
             assert all(ours[k] == theirs[k] for k in ours), (optimizer, rung)
+
+
+def test_both_trainers_share_one_spend_ledger(tnlm, tmp_path):
+    """Runs of either framework reserve, bill and complete entries in the same locked ledger file."""
+    import json
+
+    import tnlm.train as ref_train
+    import yaml
+
+    from helpers import FixtureTokenizer
+    from tensor_train_ing_b200.config import Config
+    from tensor_train_ing_b200.data import prepare_data
+    from tensor_train_ing_b200.train import train_run
+    torch.set_num_threads(1)
+    src = tmp_path / "src.jsonl"
+    src.write_text("".join(json.dumps({"id": f"doc-{i}", "text": f"text number {i} " * 3}) + "\n" for i in range(60)))
+    manifest = prepare_data(tmp_path / "data", source_jsonl=src, revision="offline-v1", tokenizer=FixtureTokenizer(),
+                            split_fractions={"train": .6, "val": .3, "test": 0., "calibration": .1})
+    ledger = tmp_path / "shared-ledger.json"
+    doc = {"model": {"layers": 1, "d_model": 8, "heads": 1, "d_key": 4, "d_value": 4, "d_mlp": 12,
+                     "padded_vocab": 50257},
+           "train": {"compile": False, "bf16_compute": False, "global_prediction_tokens_per_update": 20,
+                     "rung_total_tokens": 200, "lr": 0.01},
+           "data": {"manifest": str(manifest), "context": 16, "micro_batch_size": 2},
+           "project": {"dry_run": False, "gpu_hourly_rate_usd": 0, "spend_ledger": str(ledger)}}
+    path = tmp_path / "run.yaml"
+    path.write_text(yaml.safe_dump(doc))
+    train_run(Config.from_yaml(str(path)), tmp_path / "a", max_steps=2, max_seconds=60, device="cpu")
+    ref_train.train_run(tnlm.config.Config.from_yaml(str(path)), tmp_path / "b", max_steps=2, max_seconds=60,
+                        device="cpu")
+    train_run(Config.from_yaml(str(path)), tmp_path / "c", max_steps=2, max_seconds=60, device="cpu")
+    runs = json.loads(ledger.read_text())["runs"]
+    assert len(runs) == 3 and all(r["status"] == "complete" for r in runs.values())
