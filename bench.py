@@ -154,6 +154,32 @@ class ClockSampler:
                 "reasons": sorted(reasons), "samples": len(mhz)}
 
 
+def repo_libraries_loaded() -> list[str]:
+    """Shared objects under this repository that the current process has mapped (/proc/self/maps)."""
+    found = set()
+    try:
+        with open("/proc/self/maps") as fh:
+            for line in fh:
+                path = line.split()[-1] if len(line.split()) >= 6 else ""
+                if path.startswith(ROOT) and ".so" in os.path.basename(path):
+                    found.add(os.path.relpath(path, ROOT))
+    except OSError:
+        pass
+    return sorted(found)
+
+
+class _NoCounter:
+    """The reference arm counts no kernels: this repository's library must stay out of its process."""
+    count = None
+    by_name = None
+
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *exc):
+        return False
+
+
 def max_over_ranks(x, world, device):
     t = torch.tensor([x], device=device, dtype=torch.float64)
     if world > 1:
@@ -187,10 +213,59 @@ def build_ours(args, device, world):
 
 
 # ------------------------------------------------------------------------------------------ reference
+REF_DIR = os.path.join(ROOT, "baseline", "_ref")
+
+
+def install_reference() -> str:
+    """Install the unmodified reference package into baseline/_ref if it is not there yet.
+
+    The reference pins a torch release the offline wheelhouse does not carry, so dependency
+    resolution fails; with ``--no-deps`` the package installs and runs on the image's torch.  The
+    source directory comes from ``TTB_REFERENCE_SRC`` or BASELINE.json's ``reference_path``; it is
+    copied to a temporary directory first because the build writes into its source tree.
+    """
+    if os.path.isdir(os.path.join(REF_DIR, "tnlm")):
+        return REF_DIR
+    src = os.environ.get("TTB_REFERENCE_SRC")
+    if not src:
+        try:
+            with open(os.path.join(ROOT, "BASELINE.json")) as fh:
+                src = json.load(fh).get("reference_path")
+        except (OSError, ValueError):
+            src = None
+    if not src or not os.path.isdir(src):
+        raise RuntimeError(f"reference not installed in {os.path.relpath(REF_DIR, ROOT)} and its source "
+                           f"({src or 'no reference_path'}) is not on this machine")
+    import shutil
+    import tempfile
+    wheels = os.environ.get("TTB_WHEELHOUSE", "/opt/wheelhouse")
+    with tempfile.TemporaryDirectory() as tmp:
+        copy = os.path.join(tmp, "src")
+        shutil.copytree(src, copy, ignore=shutil.ignore_patterns(".git", "__pycache__"))
+        cmd = [sys.executable, "-m", "pip", "install", "--no-index", "--no-build-isolation", "--no-deps",
+               "--find-links", wheels, "--target", REF_DIR, copy]
+        proc = subprocess.run(cmd, capture_output=True, text=True, timeout=900)
+    if proc.returncode != 0 or not os.path.isdir(os.path.join(REF_DIR, "tnlm")):
+        tail = (proc.stderr or proc.stdout).strip().splitlines()[-1:] or ["no output"]
+        raise RuntimeError(f"pip install --no-deps of the reference failed: {tail[0]}")
+    return REF_DIR
+
+
 def build_reference(args, device, world):
-    ref = os.path.join(ROOT, "baseline", "_ref")
-    if not os.path.isdir(os.path.join(ref, "tnlm")):
-        raise RuntimeError("reference not installed in baseline/_ref")
+    error = None
+    rank = dist.get_rank() if world > 1 else 0
+    if rank == 0:
+        try:
+            install_reference()
+        except Exception as e:  # reported by every rank below, after the others learn of it
+            error = f"{type(e).__name__}: {e}"
+    if world > 1:
+        box = [error]
+        dist.broadcast_object_list(box, src=0)
+        error = box[0]
+    if error:
+        raise RuntimeError(error)
+    ref = REF_DIR
     if args.config == "32b":
         raise RuntimeError("the reference's stock bench path builds the full fp32 32B model on every rank's CPU "
                            "(133 GB per rank, over 1 TB for 8 ranks)")
@@ -273,7 +348,11 @@ def main():
         if world > 1:
             dist.barrier()
         # ------------------------------------------------------------ device-timed region
-        from tensor_train_ing_b200.ops._ext import launch_counter
+        if args.impl == "ours":
+            from tensor_train_ing_b200.ops._ext import launch_counter
+            eng.phase_events = []
+        else:
+            launch_counter = _NoCounter
         sampler = ClockSampler()
         if rank == 0:
             sampler.start()
@@ -294,7 +373,12 @@ def main():
             dist.barrier()
         torch.cuda.synchronize()
         ms = start.elapsed_time(stop)
+        phases = eng.phase_times_ms() if eng is not None else {}
+        if eng is not None:
+            eng.phase_events = None
         ms = max_over_ranks(ms, world, device)
+        # per-phase device time, max over ranks (the phases run back to back on the compute stream)
+        phases = {k: round(max_over_ranks(v, world, device), 2) for k, v in sorted(phases.items())}
         clocks = sampler.stop(set(range(world))) if rank == 0 else None
         loss_vals = [float(l) / tokens_per_step for l in losses]
         ms_per_step = ms / args.steps
@@ -355,6 +439,8 @@ def main():
         else:
             out["gpu_launches"] = counter.count
             out["gpu_launches_by_binding"] = counter.by_name
+            out["phase_ms_per_step"] = phases
+        out["native_so_loaded"] = repo_libraries_loaded()
         print(json.dumps(out), flush=True)
     if world > 1:
         dist.barrier()

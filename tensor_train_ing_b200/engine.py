@@ -56,6 +56,15 @@ class TrainEngine:
             optimizer = make_optimizer(self.model, cfg.train, only=only)
         self.optimizer = optimizer
         self.last_grad_norm = None
+        # optional per-phase device timing: a list that receives, per step, the (phase, CUDA event) pairs
+        # recorded at the end of each phase
+        self.phase_events: list | None = None
+
+    def _mark(self, marks, name):
+        if marks is not None:
+            ev = torch.cuda.Event(enable_timing=True)
+            ev.record()
+            marks.append((name, ev))
 
     def _to_device(self, t):
         if t.device == self.device:
@@ -87,6 +96,8 @@ class TrainEngine:
         if lr_multiplier is not None:
             for g in self.optimizer.param_groups:
                 g["lr"] = g.get("base_lr", g["lr"]) * lr_multiplier
+        marks = [] if self.phase_events is not None and self.device.type == "cuda" else None
+        self._mark(marks, "start")
         self.zero_grad()
         # valid-target count: counted on the host side of the copy, summed over ranks on the device
         local = (targets != -100).sum()
@@ -95,17 +106,34 @@ class TrainEngine:
             dist.all_reduce(count, group=self.group)
         inv = 1.0 / count.clamp_min(1).to(torch.float32)
         loss_sum = self.forward_backward(idx, doc_ids, targets, inv)
+        self._mark(marks, "forward_backward")
         if self.dp is not None:
             self.dp.reduce_gradients()
         if self.world > 1:
             dist.all_reduce(loss_sum, group=self.group)
+        self._mark(marks, "reduce_gradients")
         if self.grad_clip and self.grad_clip > 0:
             if self.dp is not None:
                 self.last_grad_norm = self.dp.clip_(self.grad_clip)
             else:
                 params = [p for p in self.model.parameters() if p.grad is not None]
                 self.last_grad_norm = torch.nn.utils.clip_grad_norm_(params, self.grad_clip, foreach=True)
+        self._mark(marks, "clip")
         self.optimizer.step()
+        self._mark(marks, "optimizer")
         if self.dp is not None:
             self.dp.gather_params()
+        self._mark(marks, "gather_params")
+        if marks is not None:
+            self.phase_events.append(marks)
         return loss_sum, count
+
+    def phase_times_ms(self) -> dict:
+        """Mean device milliseconds per step of each phase recorded in ``phase_events`` (call after a
+        device synchronise); the phases are consecutive intervals on the compute stream."""
+        out: dict[str, float] = {}
+        steps = self.phase_events or []
+        for marks in steps:
+            for (_, a), (name, b) in zip(marks, marks[1:]):
+                out[name] = out.get(name, 0.0) + a.elapsed_time(b)
+        return {k: round(v / len(steps), 3) for k, v in out.items()} if steps else {}
