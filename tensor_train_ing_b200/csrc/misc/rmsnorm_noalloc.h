@@ -16,9 +16,16 @@
 //  * Scratch limit: the call needs rmsnorm_bwd_noalloc_scratch_floats(N, d) floats of scratch
 //    and the array holds TTB_RMSNORM_NOALLOC_MAX_SCRATCH_FLOATS (8 MiB of fp32). A call that
 //    needs more is rejected with TTB_NOALLOC_TOO_LARGE before anything is launched.
+//    The need is min(ceil(N / 8), 4 * SMs) * d floats (one partial row per CTA). On a 148-SM
+//    B200 that is at most 592 * d, so every N fits for d <= 3540; at d = 4096 calls fit up to
+//    N = 4096 rows, at d = 8192 up to N = 2048 rows.
 //  * Nothing has to start at zero: every launch writes each scratch element it later reads.
 //  * The first call on each device (with that device current) looks up the scratch address
 //    with cudaGetSymbolAddress. Make that first call before any CUDA stream capture begins.
+//    The address is then cached per device index for the life of the process: it belongs to
+//    the CUDA runtime's primary context of that device. Callers that make another context
+//    current through the driver API, or that call cudaDeviceReset, must not use this entry
+//    point afterwards in the same process.
 //  * All calls on one device share the one scratch array. Calls that may overlap in time (two
 //    streams without ordering between them, or two host threads) race on it; order them on one
 //    stream or synchronise between them.

@@ -1,42 +1,56 @@
-"""Export one recorded sweep candidate's exact configuration as YAML (reference tnlm/sweep_config.py)."""
+"""Export one sweep candidate's recorded configuration as YAML that ``tnlm train`` accepts.
+
+The sweep journal (``sweep.json``, written by sweep.py) freezes an identity record and stores its
+canonical sha256 beside it; every trajectory inside carries its configuration and that
+configuration's canonical sha256.  The export re-derives both digests, so a journal edited after
+it was written is refused, and writes the saved values verbatim: defaults of the current schema are
+not filled in.  Behaviour as the reference's exporter (tnlm/sweep_config.py:14-44).
+"""
 from __future__ import annotations
 
-import hashlib
 import json
 from pathlib import Path
 
 import yaml
 
+from .hashing import canonical_sha256, file_sha256
 
-def _digest(value) -> str:
-    return hashlib.sha256(json.dumps(value, sort_keys=True, separators=(",", ":"), allow_nan=False).encode()).hexdigest()
+_JOURNAL = "sweep.json"
+
+
+def _identity(journal: dict) -> dict:
+    identity = journal.get("identity")
+    if not isinstance(identity, dict) or identity.get("version") != 1:
+        raise ValueError("the sweep journal has no identity record of a supported version")
+    if canonical_sha256(identity) != journal.get("identity_sha256"):
+        raise ValueError("the sweep identity does not match its recorded sha256")
+    rows = identity.get("trajectories")
+    if not isinstance(rows, list) or any(not isinstance(r, dict) for r in rows):
+        raise ValueError("the sweep identity's trajectory list is malformed")
+    return identity
+
+
+def _trajectory(identity: dict, name: str) -> dict:
+    hits = [r for r in identity["trajectories"] if r.get("name") == name]
+    if len(hits) != 1:
+        raise ValueError(f"{len(hits)} recorded trajectories are named {name!r}; exactly one is needed")
+    row = hits[0]
+    config = row.get("config")
+    if not (isinstance(config, dict) and isinstance(config.get("model"), dict) and isinstance(config.get("train"), dict)):
+        raise ValueError(f"trajectory {name!r} has no model and train configuration")
+    if canonical_sha256(config) != row.get("config_sha256"):
+        raise ValueError(f"trajectory {name!r}'s configuration does not match its recorded sha256")
+    return row
 
 
 def export_sweep_config(sweep, candidate) -> str:
-    """YAML of the candidate's saved configuration (no current defaults injected), with a provenance
-    comment binding it to the sweep journal's bytes and identity checksum."""
-    path = Path(sweep) / "sweep.json"
-    raw = path.read_bytes()
-    journal = json.loads(raw)
-    identity = journal.get("identity")
-    if not isinstance(identity, dict) or identity.get("version") != 1:
-        raise ValueError("unsupported or missing sweep identity")
-    if _digest(identity) != journal.get("identity_sha256"):
-        raise ValueError("sweep identity checksum mismatch")
-    rows = identity.get("trajectories")
-    if not isinstance(rows, list) or not all(isinstance(r, dict) for r in rows):
-        raise ValueError("invalid sweep trajectories")
-    chosen = [r for r in rows if r.get("name") == candidate]
-    if len(chosen) != 1:
-        raise ValueError("candidate must match exactly one recorded trajectory")
-    config = chosen[0].get("config")
-    if not isinstance(config, dict) or not all(isinstance(config.get(k), dict) for k in ("model", "train")):
-        raise ValueError("invalid recorded candidate configuration")
-    if _digest(config) != chosen[0].get("config_sha256"):
-        raise ValueError("candidate config checksum mismatch")
-    provenance = {"source": str(path.resolve()), "source_sha256": hashlib.sha256(raw).hexdigest(),
-                  "candidate": candidate, "identity_sha256": journal["identity_sha256"],
-                  "config_sha256": chosen[0]["config_sha256"]}
-    return ("# Exact recorded sweep config; current schema defaults are not injected.\n"
-            "# This export does not certify checkpoint completion.\n"
-            "# provenance: " + json.dumps(provenance, sort_keys=True) + "\n" + yaml.safe_dump(config, sort_keys=False))
+    path = Path(sweep) / _JOURNAL
+    journal = json.loads(path.read_bytes())
+    identity = _identity(journal)
+    row = _trajectory(identity, candidate)
+    provenance = {"source": str(path.resolve()), "source_sha256": file_sha256(path), "candidate": candidate,
+                  "identity_sha256": journal["identity_sha256"], "config_sha256": row["config_sha256"]}
+    header = ["# Configuration exactly as the sweep recorded it (no schema defaults added).",
+              "# Exporting it says nothing about whether the candidate's checkpoints completed.",
+              "# provenance: " + json.dumps(provenance, sort_keys=True)]
+    return "\n".join(header) + "\n" + yaml.safe_dump(row["config"], sort_keys=False)

@@ -27,7 +27,7 @@ from pathlib import Path
 
 import torch
 
-from .batch_branch import apply_branch, branch_config, history_entry, validate_parent
+from .batch_branch import BatchBranch, segment
 from .budget import SpendLedger
 from .calibration import _check_lagged_divisor, calibrate_lagged
 from .checkpoint_plan import checkpoint_retention_policy, checkpoint_storage_plan, pending_milestone_tokens
@@ -167,8 +167,11 @@ def train_run(cfg, run_dir, *, max_steps, max_seconds, device="cuda", resume=Non
     if isinstance(cfg, (str, Path)):
         cfg = Config.from_yaml(str(cfg))
     parent_cfg = cfg
-    cfg, batch_change = branch_config(cfg, batch_tokens=batch_tokens, lr_scale=lr_scale, resume=resume,
-                                      context_fork=context_fork, cooldown_steps=cooldown_steps)
+    branch = BatchBranch.request(cfg, batch_tokens=batch_tokens, lr_scale=lr_scale, resume=resume,
+                                 context_fork=context_fork, cooldown_steps=cooldown_steps)
+    if branch is not None:
+        cfg = branch.child_config(cfg)
+    batch_change = branch.record() if branch is not None else None
     parent_validator = resume_validator(parent_cfg, context_fork=context_fork)
     retention = checkpoint_retention_policy(cfg)
     stability_every = stability_interval(cfg)
@@ -227,8 +230,8 @@ def train_run(cfg, run_dir, *, max_steps, max_seconds, device="cuda", resume=Non
     if resume is not None:
         saved = torch.load(verified_state_path(resume), map_location="cpu", weights_only=False, mmap=True)
         parent_validator(saved["config"])
-        if batch_change is not None:
-            validate_parent(saved, cfg)
+        if branch is not None:
+            branch.check_parent(saved, cfg)
         old_context = saved["config"].get("data", {}).get("context", 512)
         del saved
     ledger = SpendLedger(project.get("spend_ledger", "runs/spend.json"), project.get("total_budget_usd", 1000),
@@ -268,9 +271,9 @@ def train_run(cfg, run_dir, *, max_steps, max_seconds, device="cuda", resume=Non
                     {"checkpoint": str(Path(resume).resolve()), **payload["config_compatibility"]})
             parent = {"path": str(Path(resume).resolve()),
                       "manifest_sha256": hashlib.sha256((Path(resume) / "manifest.json").read_bytes()).hexdigest()}
-            if batch_change is not None:
-                validate_parent(payload, cfg)
-                apply_branch(optimizer, sampler, progress, parent_cfg, cfg, parent, batch_change)
+            if branch is not None:
+                branch.check_parent(payload, cfg)
+                branch.apply(optimizer, sampler, progress, parent_cfg, cfg, parent)
                 import yaml
                 (run_dir / "branch-config.yaml").write_text(yaml.safe_dump(full_config(cfg), sort_keys=False))
             if context_fork:
@@ -284,7 +287,7 @@ def train_run(cfg, run_dir, *, max_steps, max_seconds, device="cuda", resume=Non
             resume_extra = payload.get("extra", {}) or {}
             del payload
         else:
-            progress["batch_history"] = [history_entry(cfg, tokens=0, steps=0, source="fresh")]
+            progress["batch_history"] = [segment(cfg, tokens=0, steps=0, source="fresh")]
             progress["context_history"] = [{"context": data.get("context", 512), "start_tokens": 0, "start_step": 0,
                                             "source": "fresh"}]
         branch_base_lr = [g["lr"] for g in optimizer.param_groups]

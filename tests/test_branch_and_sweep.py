@@ -10,11 +10,12 @@ import torch
 import yaml
 
 from helpers import TINY_MODEL
-from tensor_train_ing_b200.batch_branch import apply_branch, branch_config, validate_parent
+from tensor_train_ing_b200.batch_branch import BatchBranch
 from tensor_train_ing_b200.config import Config, ModelConfig, TrainConfig
 from tensor_train_ing_b200.models.model import TensorLM
 from tensor_train_ing_b200.optim import make_optimizer
-from tensor_train_ing_b200.sweep_config import _digest, export_sweep_config
+from tensor_train_ing_b200.hashing import canonical_sha256 as _digest
+from tensor_train_ing_b200.sweep_config import export_sweep_config
 from tensor_train_ing_b200.sweep_retention import (intermediate_payload, reject_symlink_chain, retention_forecast,
                                                    unlink_payload)
 
@@ -28,31 +29,32 @@ def _cfg(**train):
 # --------------------------------------------------------------------------------- batch branch
 def test_branch_config_scales_rates_and_sets_the_new_quota():
     cfg = _cfg()
-    child, spec = branch_config(cfg, batch_tokens=128, lr_scale=2.0, resume="parent", context_fork=False,
-                                cooldown_steps=None)
+    branch = BatchBranch.request(cfg, batch_tokens=128, lr_scale=2.0, resume="parent", context_fork=False,
+                                 cooldown_steps=None)
+    child = branch.child_config(cfg)
     assert child.train.global_prediction_tokens_per_update == 128
     assert child.train.lr == pytest.approx(0.02) and child.train.aux_adamw_lr == pytest.approx(0.004)
     assert cfg.train.lr == 0.01  # the parent config is untouched
-    assert spec == {"old_batch_tokens": 64, "new_batch_tokens": 128, "lr_scale": 2.0}
-    assert branch_config(cfg, batch_tokens=None, lr_scale=None, resume=None, context_fork=False,
-                         cooldown_steps=None) == (cfg, None)
+    assert branch.record() == {"old_batch_tokens": 64, "new_batch_tokens": 128, "lr_scale": 2.0}
+    assert BatchBranch.request(cfg, batch_tokens=None, lr_scale=None, resume=None, context_fork=False,
+                               cooldown_steps=None) is None
     for bad in (dict(batch_tokens=64, lr_scale=2.0), dict(batch_tokens=128, lr_scale=0.0),
-                dict(batch_tokens=128, lr_scale=float("inf"))):
+                dict(batch_tokens=128, lr_scale=float("inf")), dict(batch_tokens=128, lr_scale=None)):
         with pytest.raises(ValueError):
-            branch_config(cfg, resume="parent", context_fork=False, cooldown_steps=None, **bad)
+            BatchBranch.request(cfg, resume="parent", context_fork=False, cooldown_steps=None, **bad)
     with pytest.raises(ValueError):  # only from a constant schedule without a cooldown
-        branch_config(cfg, batch_tokens=128, lr_scale=2.0, resume="p", context_fork=False, cooldown_steps=10)
+        BatchBranch.request(cfg, batch_tokens=128, lr_scale=2.0, resume="p", context_fork=False, cooldown_steps=10)
 
 
 def test_parent_must_be_past_warmup_and_before_its_horizon():
     child = _cfg()
     ok = {"progress": {"warmup_steps": 100, "scheduler_step": 150, "tokens": 5000, "steps": 150}}
-    validate_parent(ok, child)
+    BatchBranch.check_parent(ok, child)
     for change in ({"scheduler_step": 50}, {"tokens": 10_000}, {"cooldown_start_tokens": 1}):
         bad = copy.deepcopy(ok)
         bad["progress"].update(change)
         with pytest.raises(ValueError):
-            validate_parent(bad, child)
+            BatchBranch.check_parent(bad, child)
 
 
 def test_apply_branch_scales_every_group_and_records_history():
@@ -61,15 +63,16 @@ def test_apply_branch_scales_every_group_and_records_history():
     cfg = _cfg(optimizer="muon")
     opt = make_optimizer(model, cfg.train)
     before = [(g["lr"], g.get("base_lr")) for g in opt.param_groups]
-    child, spec = branch_config(cfg, batch_tokens=32, lr_scale=0.5, resume="p", context_fork=False,
-                                cooldown_steps=None)
+    branch = BatchBranch.request(cfg, batch_tokens=32, lr_scale=0.5, resume="p", context_fork=False,
+                                 cooldown_steps=None)
+    child = branch.child_config(cfg)
 
     class Sampler:
         def state_dict(self):
             return {"cursor": 7}
 
     progress = {"tokens": 640, "steps": 10}
-    apply_branch(opt, Sampler(), progress, cfg, child, {"path": "p"}, spec)
+    branch.apply(opt, Sampler(), progress, cfg, child, {"path": "p"})
     for (lr, base), g in zip(before, opt.param_groups):
         assert g["lr"] == pytest.approx(0.5 * lr)
         assert g["base_lr"] == pytest.approx(0.5 * (base if base is not None else lr))
