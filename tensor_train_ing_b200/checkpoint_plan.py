@@ -1,154 +1,241 @@
-"""Checkpoint retention policy, milestone schedule and a meta-device storage forecast
-(reference tnlm/checkpoint_plan.py:24-213).  Nothing is allocated, written or deleted."""
+"""Checkpoint retention, the milestone schedule and a disk forecast for a planned run.
+
+The forecast is computed from the model's shapes on the meta device: nothing is allocated,
+initialised, drawn from an RNG, written, reserved or deleted.  Policies and numbers are the
+reference planner's (tnlm/checkpoint_plan.py:24-213), field for field, because sweep journals and
+run directories record these plans and the two frameworks' tools read each other's:
+
+* retention: ``project.keep_recovery_checkpoints`` (default 2; 0 turns recovery saves off) and
+  ``project.save_initial_checkpoint`` (default true); final, milestone and branch checkpoints stay;
+* milestones: by default 1M, 2M, 4M, ... 32M tokens, then every 100M; an explicit
+  ``project.milestone_tokens`` list replaces the whole default; the serial trainer also saves at the
+  90 % branch point of a non-cosine schedule, the distributed trainer keeps it as its own checkpoint;
+* one full-state checkpoint = parameters + optimizer moments (one per Muon matrix, two per AdamW
+  tensor) + an 8-byte step per AdamW tensor per rank + persistent buffers, plus under sharding an
+  allowance for uneven first-dimension splits, plus 1 MiB of metadata per rank file; then a 10 %
+  serialisation margin and 1 MiB per rank file.
+"""
 from __future__ import annotations
 
 import bisect
 import heapq
 import math
+from dataclasses import dataclass
+from typing import Iterator
 
 import torch
 
 from .optim import hidden_matrix
 
-_METADATA_ALLOWANCE = 1 << 20
-_SERIALIZATION_OVERHEAD = 1 << 20
-_EARLY = (1_000_000, 2_000_000, 4_000_000, 8_000_000, 16_000_000, 32_000_000)
+MIB = 1 << 20
+METADATA_ALLOWANCE = MIB      # per rank checkpoint file
+SERIALIZATION_OVERHEAD = MIB  # per rank checkpoint file, after the 10 % margin
+STEP_SCALAR_BYTES = 8         # AdamW's step counter per tensor (at least; the default dtype if wider)
 
 
-def _integer(value, name, minimum=0):
+def _count(value, what: str, minimum: int = 0) -> int:
     if isinstance(value, bool) or not isinstance(value, int) or value < minimum:
-        raise ValueError(f"{name} must be an integer >= {minimum}")
+        raise ValueError(f"{what} must be an integer >= {minimum}")
+    return value
+
+
+def _flag(value, what: str) -> bool:
+    if not isinstance(value, bool):
+        raise ValueError(f"{what} must be bool")
     return value
 
 
 def checkpoint_retention_policy(cfg) -> dict:
     project = cfg.raw.get("project", {})
-    keep = _integer(project.get("keep_recovery_checkpoints", 2), "project.keep_recovery_checkpoints")
-    initial = project.get("save_initial_checkpoint", True)
-    if not isinstance(initial, bool):
-        raise ValueError("project.save_initial_checkpoint must be bool")
-    return {"keep_recovery_checkpoints": keep, "save_initial_checkpoint": initial}
+    return {"keep_recovery_checkpoints": _count(project.get("keep_recovery_checkpoints", 2),
+                                                "project.keep_recovery_checkpoints"),
+            "save_initial_checkpoint": _flag(project.get("save_initial_checkpoint", True),
+                                             "project.save_initial_checkpoint")}
+
+
+class MilestoneSchedule:
+    """Token counts at which a milestone checkpoint is saved."""
+
+    DOUBLING = (1_000_000, 2_000_000, 4_000_000, 8_000_000, 16_000_000, 32_000_000)
+    STRIDE = 100_000_000
+
+    def __init__(self, explicit: list[int] | None = None):
+        self.explicit = explicit  # sorted unique values, or None for the default schedule
+
+    @classmethod
+    def from_config(cls, cfg) -> "MilestoneSchedule":
+        project = cfg.raw.get("project", {})
+        if "milestone_tokens" not in project:
+            return cls()
+        values = project["milestone_tokens"]
+        if not isinstance(values, list):
+            raise ValueError("project.milestone_tokens must be a list of positive integers")
+        return cls(sorted({_count(v, "each project.milestone_tokens entry", 1) for v in values}))
+
+    def policy(self) -> dict:
+        return ({"mode": "default", "tokens": None} if self.explicit is None
+                else {"mode": "explicit", "tokens": list(self.explicit)})
+
+    def between(self, start: int, end: int) -> Iterator[int]:
+        """Thresholds t with start < t <= end, ascending, produced lazily."""
+        if self.explicit is not None:
+            lo, hi = bisect.bisect_right(self.explicit, start), bisect.bisect_right(self.explicit, end)
+            yield from self.explicit[lo:hi]
+            return
+        early = [t for t in self.DOUBLING if start < t <= end]
+        strided = range((start // self.STRIDE + 1) * self.STRIDE, end + 1, self.STRIDE)
+        yield from heapq.merge(early, strided)
+
+    def count(self, start: int, end: int) -> int:
+        if self.explicit is not None:
+            return max(0, bisect.bisect_right(self.explicit, end) - bisect.bisect_right(self.explicit, start))
+        early = sum(start < t <= end for t in self.DOUBLING)
+        return early + max(0, end // self.STRIDE - start // self.STRIDE)
+
+    def __contains__(self, tokens: int) -> bool:
+        if self.explicit is not None:
+            return tokens in self.explicit
+        return tokens in self.DOUBLING or (tokens > 0 and tokens % self.STRIDE == 0)
 
 
 def milestone_policy(cfg) -> dict:
-    project = cfg.raw.get("project", {})
-    if "milestone_tokens" not in project:
-        return {"mode": "default", "tokens": None}
-    values = project["milestone_tokens"]
-    if not isinstance(values, list):
-        raise ValueError("project.milestone_tokens must be a list of positive integers")
-    for v in values:
-        _integer(v, "project.milestone_tokens entry", 1)
-    return {"mode": "explicit", "tokens": sorted(set(values))}
+    return MilestoneSchedule.from_config(cfg).policy()
+
+
+def branch_point(limit: int) -> int:
+    """The 90 % point of a token horizon, where sweeps branch their cooldowns."""
+    return (9 * limit) // 10
 
 
 def pending_milestone_tokens(cfg, *, start_tokens, token_limit, reachable_tokens=None, include_branch=False):
-    """Lazy, sorted, unique milestone thresholds in (start, min(limit, reachable)]; the default is
-    1M..32M doubling then every 100M; ``include_branch`` adds the 90% branch point."""
-    start = _integer(start_tokens, "start_tokens")
-    limit = _integer(token_limit, "token_limit")
-    end = limit if reachable_tokens is None else min(limit, _integer(reachable_tokens, "reachable_tokens"))
-    if not isinstance(include_branch, bool):
-        raise ValueError("include_branch must be bool")
-    policy = milestone_policy(cfg)
-    if policy["mode"] == "explicit":
-        vals = policy["tokens"]
-        sources = [iter(vals[bisect.bisect_right(vals, start):bisect.bisect_right(vals, end)])]
-    else:
-        sources = [(v for v in _EARLY if start < v <= end),
-                   range((start // 100_000_000 + 1) * 100_000_000, end + 1, 100_000_000)]
-    branch = (9 * limit) // 10
-    if include_branch and cfg.train.schedule != "cosine" and start < branch <= end:
-        sources.append((branch,))
+    """Unique thresholds in (start, min(limit, reachable)], ascending; with ``include_branch`` the 90 %
+    branch point of a non-cosine schedule joins them.  Arguments are checked at the call, the values
+    are produced lazily (the default schedule can span many 100M strides)."""
+    start = _count(start_tokens, "start_tokens")
+    limit = _count(token_limit, "token_limit")
+    end = limit if reachable_tokens is None else min(limit, _count(reachable_tokens, "reachable_tokens"))
+    _flag(include_branch, "include_branch")
+    sources = [MilestoneSchedule.from_config(cfg).between(start, end)]
+    bp = branch_point(limit)
+    if include_branch and cfg.train.schedule != "cosine" and start < bp <= end:
+        sources.append(iter((bp,)))
 
-    def unique():
-        prev = None
-        for v in heapq.merge(*sources):
-            if v != prev:
-                yield v
-                prev = v
-    return unique()
+    def deduplicated():
+        last = None
+        for t in heapq.merge(*sources):
+            if t != last:
+                last = t
+                yield t
+    return deduplicated()
+
+
+@dataclass
+class _Inventory:
+    """Tensor bytes of one full-state checkpoint of the model (all ranks together when sharded)."""
+    parameters: int = 0            # unique storages; every FQN when sharded (DCP addresses by name)
+    portable_parameters: int = 0   # unique storages (a torch.save export)
+    moments: int = 0
+    step_scalars: int = 0
+    padding: int = 0               # uneven Shard(0) split allowance, model and moments
+    buffers: int = 0               # persistent buffers, once per rank when sharded
+    unique_buffers: int = 0
+
+    def tensor_bytes(self) -> int:
+        return self.parameters + self.moments + self.step_scalars + self.padding + self.buffers
+
+
+def _inventory(cfg, world: int, sharded: bool) -> _Inventory:
+    with torch.device("meta"):
+        from .models.model import TensorLM
+        model = TensorLM(cfg.model)
+    inv = _Inventory()
+    step_bytes = max(STEP_SCALAR_BYTES, torch.empty((), device="meta").element_size())
+    storages = set()
+    for name, p in model.named_parameters():
+        key = p.untyped_storage()._cdata
+        if key not in storages:
+            storages.add(key)
+            inv.portable_parameters += p.untyped_storage().nbytes()
+        if not p.requires_grad:
+            continue
+        copies = 1 if cfg.train.optimizer == "muon" and hidden_matrix(name, p) else 2
+        inv.moments += copies * p.numel() * p.element_size()
+        if copies == 2:
+            inv.step_scalars += step_bytes * world
+        if sharded:
+            # one first-dimension row per extra rank (whole tensor for a scalar), model and moments
+            row = (math.prod(p.shape[1:]) if p.ndim else p.numel()) * p.element_size()
+            inv.padding += (world - 1) * row * (1 + copies)
+    inv.parameters = inv.portable_parameters
+    if sharded:
+        seen, inv.parameters = set(), 0
+        for _, p in model.named_parameters(remove_duplicate=False):
+            inv.parameters += p.numel() * p.element_size()
+            if id(p) in seen:  # a tied parameter is saved (and padded) under each name
+                inv.padding += (world - 1) * (math.prod(p.shape[1:]) if p.ndim else 1) * p.element_size()
+            seen.add(id(p))
+    param_keys = {p.untyped_storage()._cdata for p in model.parameters()}
+    buffer_sizes = {}
+    for t in model.state_dict().values():
+        key = t.untyped_storage()._cdata
+        if key not in param_keys:
+            buffer_sizes[key] = t.untyped_storage().nbytes()
+    inv.unique_buffers = sum(buffer_sizes.values())
+    inv.buffers = inv.unique_buffers * (world if sharded else 1)
+    return inv
+
+
+def _on_disk(tensor_bytes: int, files: int) -> int:
+    base = tensor_bytes + METADATA_ALLOWANCE * files
+    return base + (base + 9) // 10 + SERIALIZATION_OVERHEAD * files
 
 
 def checkpoint_storage_plan(cfg, *, start_tokens=0, token_limit=None, max_steps=None, distributed_world_size=1,
                             distributed=False, export_weights=False, cooldown=False) -> dict:
-    """Advisory bytes for all checkpoints the run will retain, from a meta-device model."""
-    from .models.model import TensorLM
-    start = _integer(start_tokens, "start_tokens")
-    limit = _integer(cfg.train.rung_total_tokens if token_limit is None else token_limit, "token_limit")
-    world = _integer(distributed_world_size, "distributed_world_size", 1)
+    """Advisory bytes of every checkpoint the run keeps at its peak (not a guaranteed bound:
+    existing artifacts, concurrent runs and filesystem allocation are outside it)."""
+    start = _count(start_tokens, "start_tokens")
+    limit = _count(cfg.train.rung_total_tokens if token_limit is None else token_limit, "token_limit")
+    world = _count(distributed_world_size, "distributed_world_size", 1)
+    for value, what in ((distributed, "distributed"), (export_weights, "export_weights"), (cooldown, "cooldown")):
+        _flag(value, what)
     if not distributed and world != 1:
-        raise ValueError("distributed_world_size must be 1 for a serial plan")
-    for name, v in (("distributed", distributed), ("export_weights", export_weights), ("cooldown", cooldown)):
-        if not isinstance(v, bool):
-            raise ValueError(f"{name} must be bool")
-    batch = _integer(cfg.train.global_prediction_tokens_per_update, "global_prediction_tokens_per_update", 1)
-    retention = checkpoint_retention_policy(cfg)
-    keep = retention["keep_recovery_checkpoints"]
-    updates = (max(0, limit - start) + batch - 1) // batch
-    if max_steps is not None:
-        updates = min(updates, _integer(max_steps, "max_steps"))
-    reachable = min(limit, start + updates * batch) if start < limit else start
-    policy = milestone_policy(cfg)
-    end = min(limit, reachable)
-    if policy["mode"] == "default":
-        milestones = sum(start < v <= end for v in _EARLY) + max(0, end // 100_000_000 - start // 100_000_000)
-    else:
-        vals = policy["tokens"]
-        milestones = max(0, bisect.bisect_right(vals, end) - bisect.bisect_right(vals, start))
-    branch = (9 * limit) // 10
-    branch_reachable = not cooldown and cfg.train.schedule != "cosine" and start < branch <= end
-    branch_is_milestone = (branch in policy["tokens"] if policy["mode"] == "explicit"
-                           else branch in _EARLY or (branch > 0 and branch % 100_000_000 == 0))
-    separate_branch = int(branch_reachable and distributed)
-    if branch_reachable and not distributed and not branch_is_milestone:
-        milestones += 1
-    rolling = min(updates, keep + 1) if keep else 0
-
-    class _Meta(TensorLM):
-        def reset_parameters(self):
-            pass
-
-    with torch.device("meta"):
-        model = _Meta(cfg.model)
+        raise ValueError("a serial plan has distributed_world_size 1")
+    batch = _count(cfg.train.global_prediction_tokens_per_update, "global_prediction_tokens_per_update", 1)
     if cfg.train.optimizer not in ("adamw", "muon"):
-        raise ValueError("checkpoint plan supports adamw or muon")
-    seen, param_bytes, opt_bytes, padding, step_scalars = set(), 0, 0, 0, 0
-    for name, p in model.named_parameters():
-        key = id(p)
-        if key not in seen:
-            seen.add(key)
-            param_bytes += p.numel() * p.element_size()
-        if not p.requires_grad:
-            continue
-        moments = 1 if cfg.train.optimizer == "muon" and hidden_matrix(name, p) else 2
-        opt_bytes += moments * p.numel() * p.element_size()
-        if moments == 2:
-            step_scalars += 8 * world
-        if distributed:
-            row = (math.prod(p.shape[1:]) if p.ndim else p.numel()) * p.element_size()
-            padding += (world - 1) * row * (1 + moments)
-    portable = param_bytes
-    buffers = sum(t.numel() * t.element_size() for n, t in model.state_dict().items()
-                  if n not in dict(model.named_parameters())) * (world if distributed else 1)
-    tensor_bytes = param_bytes + opt_bytes + step_scalars + padding + buffers
+        raise ValueError("checkpoint plans cover the adamw and muon optimizers")
+    retention = checkpoint_retention_policy(cfg)
+    schedule = MilestoneSchedule.from_config(cfg)
 
-    def estimate(tensors, copies):
-        base = tensors + _METADATA_ALLOWANCE * copies
-        return base + (base + 9) // 10 + _SERIALIZATION_OVERHEAD * copies
-
-    full = estimate(tensor_bytes, world if distributed else 1)
-    export = estimate(portable + buffers // (world if distributed else 1), 1) if export_weights else 0
+    updates = -(-max(0, limit - start) // batch)
+    if max_steps is not None:
+        updates = min(updates, _count(max_steps, "max_steps"))
+    reachable = min(limit, start + updates * batch) if start < limit else start
+    end = min(limit, reachable)
+    milestones = schedule.count(start, end)
+    bp = branch_point(limit)
+    branch_due = not cooldown and cfg.train.schedule != "cosine" and start < bp <= end
+    if branch_due and not distributed and bp not in schedule:
+        milestones += 1  # the serial trainer saves the branch point as a milestone
+    keep = retention["keep_recovery_checkpoints"]
     counts = {"initial": int(retention["save_initial_checkpoint"]), "final": 1, "milestones": milestones,
-              "separate_90_percent_branch": separate_branch, "rolling_recovery_including_staging": rolling}
-    count = sum(counts.values())
-    return {"kind": "checkpoint_storage_projection", "required_additional_bytes": full * count + export,
-            "per_checkpoint_estimate_bytes": full, "export_weights_estimate_bytes": export, "checkpoint_count": count,
-            "count_breakdown": counts, "milestone_policy": policy, "checkpoint_retention_policy": retention,
-            "start_tokens": start, "token_limit": limit, "reachable_tokens": reachable, "reachable_updates": updates,
-            "distributed": distributed, "world_size": world, "dtype": str(torch.get_default_dtype()),
-            "tensor_bytes_breakdown": {"parameters": param_bytes, "optimizer_moments": opt_bytes,
-                                       "optimizer_step_scalars": step_scalars, "persistent_buffers": buffers,
-                                       "distributed_shard_padding_allowance": padding},
-            "metadata_allowance_bytes_per_rank_checkpoint": _METADATA_ALLOWANCE,
+              "separate_90_percent_branch": int(branch_due and distributed),
+              # a new recovery checkpoint is staged before the oldest is pruned
+              "rolling_recovery_including_staging": min(updates, keep + 1) if keep else 0}
+
+    inv = _inventory(cfg, world, distributed)
+    each = _on_disk(inv.tensor_bytes(), world if distributed else 1)
+    export = _on_disk(inv.portable_parameters + inv.unique_buffers, 1) if export_weights else 0
+    total_count = sum(counts.values())
+    return {"kind": "checkpoint_storage_projection", "required_additional_bytes": each * total_count + export,
+            "per_checkpoint_estimate_bytes": each, "export_weights_estimate_bytes": export,
+            "checkpoint_count": total_count, "count_breakdown": counts, "milestone_policy": schedule.policy(),
+            "checkpoint_retention_policy": retention, "start_tokens": start, "token_limit": limit,
+            "reachable_tokens": reachable, "reachable_updates": updates, "distributed": distributed,
+            "world_size": world, "dtype": str(torch.get_default_dtype()),
+            "tensor_bytes_breakdown": {"parameters": inv.parameters, "optimizer_moments": inv.moments,
+                                       "optimizer_step_scalars": inv.step_scalars,
+                                       "persistent_buffers": inv.buffers,
+                                       "distributed_shard_padding_allowance": inv.padding},
+            "metadata_allowance_bytes_per_rank_checkpoint": METADATA_ALLOWANCE,
             "scope": "advisory projection, not guaranteed upper bound; no reservation or deletion"}

@@ -42,7 +42,7 @@ from .parallel.sharded import ShardedDataParallel
 from .runtime import determinism_metadata, full_config, resume_validator, seed_all
 from .schedules import lr_multiplier, schedule_multiplier, schedule_steps, validate_schedule
 from .train import _mask_to_count, _validate_batch
-from .training_stability import BatchScoreBounds, qk_clip_policy, qk_clip_source, stability_interval
+from .training_stability import BatchScoreBounds, StabilityPolicy
 from .training_taper import TaperTraining, validate_taper_config
 
 
@@ -82,9 +82,9 @@ def distributed_train_run(cfg, run_dir, *, max_steps, max_seconds, device="cuda"
         if validate_taper_config(cfg):
             if round(cfg.train.taper_end_fraction * planned_total) <= validate_schedule(cfg.train.schedule, planned_total):
                 raise ValueError("TaperNorm endpoint must be strictly after positive warmup_steps")
-        if qk_clip_policy(cfg)[0] > 0 and qk_clip_source(cfg) != "batch_bound":
+        if StabilityPolicy.from_config(cfg).clipping and StabilityPolicy.from_config(cfg).clip_source != "batch_bound":
             raise ValueError("distributed QK-clip supports qk_clip_source='batch_bound' only")
-        if stability_interval(cfg):
+        if StabilityPolicy.from_config(cfg).stability_every:
             raise ValueError("periodic stability logging supports serial training only")
         if export_max_state_bytes is not None and (type(export_max_state_bytes) is not int or export_max_state_bytes <= 0):
             raise ValueError("export_max_state_bytes must be a positive integer or None")
@@ -216,7 +216,8 @@ def distributed_train_run(cfg, run_dir, *, max_steps, max_seconds, device="cuda"
         taper.before_step(progress["steps"])
         taper.set_valid_mask(None)
         bounds = BatchScoreBounds(model, cfg)
-        clip_tau, clip_every = qk_clip_policy(cfg)
+        policy = StabilityPolicy.from_config(cfg)
+        clip_tau, clip_every = policy.clip_tau, policy.clip_every
         token_limit = (progress["cooldown_start_tokens"] + cooldown_steps * cfg.train.global_prediction_tokens_per_update
                        if cooldown_steps is not None else cfg.train.rung_total_tokens)
         if cooldown_end_tokens is not None:

@@ -37,10 +37,10 @@ def full_config(cfg) -> dict:
     project["spend_ledger"] = str(Path(project.get("spend_ledger", "runs/spend.json")).resolve())
     out["project"] = project
     out["train"]["deterministic"] = deterministic_requested(cfg)
-    from .training_stability import qk_clip_policy, qk_clip_source, stability_interval
-    out["train"]["stability_every_steps"] = stability_interval(cfg)
-    tau, every = qk_clip_policy(cfg)
-    out["train"].update(qk_clip_tau=tau, qk_clip_every_steps=every, qk_clip_source=qk_clip_source(cfg))
+    from .training_stability import StabilityPolicy
+    policy = StabilityPolicy.from_config(cfg)
+    out["train"].update(stability_every_steps=policy.stability_every, qk_clip_tau=policy.clip_tau,
+                        qk_clip_every_steps=policy.clip_every, qk_clip_source=policy.clip_source)
     return out
 
 

@@ -39,8 +39,7 @@ from .optim import hidden_matrix
 from .optimizer_exposure import update_optimizer_exposure
 from .runtime import determinism_metadata, full_config, resume_validator, seed_all, training_execution
 from .schedules import lr_multiplier, schedule_multiplier, schedule_steps, validate_schedule
-from .training_stability import (BatchScoreBounds, TrainingStabilityProbe, qk_clip_policy, qk_clip_source,
-                                 stability_interval)
+from .training_stability import BatchScoreBounds, StabilityPolicy, TrainingStabilityProbe
 from .training_taper import TaperTraining, validate_taper_config
 
 
@@ -174,9 +173,9 @@ def train_run(cfg, run_dir, *, max_steps, max_seconds, device="cuda", resume=Non
     batch_change = branch.record() if branch is not None else None
     parent_validator = resume_validator(parent_cfg, context_fork=context_fork)
     retention = checkpoint_retention_policy(cfg)
-    stability_every = stability_interval(cfg)
-    clip_tau, clip_every = qk_clip_policy(cfg)
-    clip_source = qk_clip_source(cfg)
+    policy = StabilityPolicy.from_config(cfg)
+    stability_every, clip_tau, clip_every, clip_source = (policy.stability_every, policy.clip_tau,
+                                                          policy.clip_every, policy.clip_source)
     planned_total = schedule_steps(cfg.train.rung_total_tokens, cfg.train.global_prediction_tokens_per_update)
     if validate_taper_config(cfg):
         if round(cfg.train.taper_end_fraction * planned_total) <= validate_schedule(cfg.train.schedule, planned_total):

@@ -1,185 +1,217 @@
-"""Training-time stability instrumentation: config policy checks, per-batch score bounds used by
-QK-clip, and a fixed probe row from an independent train sampler (reference
-tnlm/training_stability.py:15-196)."""
+"""Stability instrumentation of a training run: its policy, the per-batch score bounds that feed
+QK-clip, and a fixed probe row for diagnostics.
+
+* ``StabilityPolicy`` reads and checks the four ``train`` fields involved: how often to record
+  stability statistics, the QK-clip threshold and cadence, and where clip maxima come from
+  ("probe" or "batch_bound").
+* ``BatchScoreBounds`` collects, over the micro-batches of one update, the score bounds each
+  polynomial attention layer records in its forward; the update's maximum goes to metrics and the
+  last micro-batch's per-head bounds drive a ``batch_bound`` clip.  The maximum covers padding and
+  unscored positions and bounds the scores before the update, not after it.
+* ``TrainingStabilityProbe`` holds the first row (at most 512 tokens) of an independent train-split
+  sampler, so it never consumes the training stream, and runs statistics or a probe clip on it
+  between updates with module modes, norm statistics collection, score-bound recording and every
+  RNG restored afterwards.
+
+Behaviour as the reference's (tnlm/training_stability.py:15-196).
+"""
 from __future__ import annotations
 
 import math
 import random
 import time
+from contextlib import contextmanager
+from dataclasses import dataclass
 
 import numpy as np
 import torch
 
 from .models.normalization import lagged_modules, taper_modules
 
-
-def stability_interval(cfg) -> int:
-    value = getattr(cfg.train, "stability_every_steps", 0)
-    if isinstance(value, bool) or not isinstance(value, int) or value < 0:
-        raise ValueError("train.stability_every_steps must be an integer >= 0")
-    return value
+OPTIMIZER_STATE_POLICY = "moments and step counters unchanged"
+PROBE_MAX_CONTEXT = 512
 
 
-def qk_clip_source(cfg) -> str:
-    source = getattr(cfg.train, "qk_clip_source", "probe")
-    if type(source) is not str or source not in ("probe", "batch_bound"):
-        raise ValueError("train.qk_clip_source must be probe or batch_bound")
-    if source == "batch_bound" and cfg.model.attention == "softmax":
-        raise ValueError("batch_bound recording requires polynomial attention")
-    return source
+@dataclass(frozen=True)
+class StabilityPolicy:
+    stability_every: int
+    clip_tau: float
+    clip_every: int
+    clip_source: str
+
+    @classmethod
+    def from_config(cls, cfg) -> "StabilityPolicy":
+        t = cfg.train
+        every = getattr(t, "stability_every_steps", 0)
+        if isinstance(every, bool) or not isinstance(every, int) or every < 0:
+            raise ValueError("train.stability_every_steps must be an integer >= 0")
+        source = getattr(t, "qk_clip_source", "probe")
+        if type(source) is not str or source not in ("probe", "batch_bound"):
+            raise ValueError("train.qk_clip_source must be 'probe' or 'batch_bound'")
+        if source == "batch_bound" and cfg.model.attention == "softmax":
+            raise ValueError("batch_bound score recording needs polynomial attention")
+        tau = getattr(t, "qk_clip_tau", 0.0)
+        if type(tau) not in (int, float) or not math.isfinite(tau) or tau < 0:
+            raise ValueError("train.qk_clip_tau must be finite and nonnegative")
+        cadence = getattr(t, "qk_clip_every_steps", 0)
+        if type(cadence) is not int or cadence < 0 or (tau > 0 and cadence == 0):
+            raise ValueError("train.qk_clip_every_steps must be a nonnegative integer, positive when clipping is on")
+        if tau > 0 and cfg.model.normalization == "spectral_rms":
+            raise ValueError("QK-clip does not support spectral_rms models")
+        return cls(every, float(tau), cadence, source)
+
+    @property
+    def clipping(self) -> bool:
+        return self.clip_tau > 0
+
+    def needs_probe(self) -> bool:
+        return bool(self.stability_every) or (self.clipping and self.clip_source == "probe")
 
 
-def qk_clip_policy(cfg):
-    qk_clip_source(cfg)
-    tau = getattr(cfg.train, "qk_clip_tau", 0.0)
-    every = getattr(cfg.train, "qk_clip_every_steps", 0)
-    if type(tau) not in (int, float) or not math.isfinite(tau) or tau < 0:
-        raise ValueError("train.qk_clip_tau must be finite and nonnegative")
-    if type(every) is not int or every < 0 or (tau > 0 and every == 0):
-        raise ValueError("train.qk_clip_every_steps must be a nonnegative integer, positive when clipping is enabled")
-    if tau > 0 and cfg.model.normalization == "spectral_rms":
-        raise ValueError("QK clipping does not support spectral models")
-    return float(tau), every
+def sanitize_finite(value, root: str) -> tuple:
+    """(copy of ``value`` with non-finite floats replaced by None, the paths that were replaced)."""
+    bad: list[str] = []
 
-
-def finite_json(value, path, nonfinite):
-    if isinstance(value, dict):
-        return {k: finite_json(v, f"{path}.{k}", nonfinite) for k, v in value.items()}
-    if isinstance(value, (list, tuple)):
-        return [finite_json(v, f"{path}[{i}]", nonfinite) for i, v in enumerate(value)]
-    if isinstance(value, (float, np.floating)):
-        if not math.isfinite(value):
-            nonfinite.append(path)
+    def walk(v, path):
+        if isinstance(v, dict):
+            return {k: walk(x, f"{path}.{k}") for k, x in v.items()}
+        if isinstance(v, (list, tuple)):
+            return [walk(x, f"{path}[{i}]") for i, x in enumerate(v)]
+        if isinstance(v, (float, np.floating)):
+            if math.isfinite(v):
+                return float(v)
+            bad.append(path)
             return None
-        return float(value)
-    return value
+        return v
+    return walk(value, root), bad
+
+
+def _require_finite_clip(stats: dict) -> None:
+    _, bad = sanitize_finite(stats, "qk_clip")
+    if bad:
+        raise FloatingPointError("QK-clip produced non-finite values at " + ", ".join(bad))
 
 
 class BatchScoreBounds:
-    """Per-update maximum of the recorded per-batch score bounds (over micro-batches, layers and
-    factors), and clipping from the last micro-batch's bounds."""
-
     def __init__(self, model, cfg):
         from .qk_clip import set_score_bound_recording
         self.model = model
-        self.enabled = qk_clip_source(cfg) == "batch_bound"
-        self.maximum = None
-        self.last = None
+        self.enabled = StabilityPolicy.from_config(cfg).clip_source == "batch_bound"
+        self.maximum: torch.Tensor | None = None  # device scalar over the update so far
+        self.last: list[dict] | None = None       # per layer {factor: (H,)} of the last micro-batch
         if self.enabled:
             set_score_bound_recording(model, True)
 
-    def begin_update(self):
+    def begin_update(self) -> None:
         self.maximum = self.last = None
 
-    def observe(self):
+    def _recorded(self) -> list[tuple[int, str, torch.Tensor]]:
+        from .qk_clip import score_bounds
+        heads, found = self.model.cfg.heads, []
+        for layer, (blk, bounds) in enumerate(zip(self.model.blocks, score_bounds(self.model))):
+            if set(bounds) != ({"S1", "S2"} if hasattr(blk.attn, "q2") else {"S1"}):
+                raise ValueError(f"layer {layer} recorded no or unexpected score-bound factors")
+            for factor, b in bounds.items():
+                if not torch.is_tensor(b) or b.shape != (heads,):
+                    raise ValueError(f"layer {layer} {factor}: a score bound must be a ({heads},) tensor")
+                found.append((layer, factor, b.detach()))
+        if not found:
+            raise ValueError("no polynomial attention layer recorded score bounds")
+        return found
+
+    def observe(self) -> None:
+        """Fold the bounds of the micro-batch just run into the update's maximum (device-side)."""
         if not self.enabled:
             return
-        from .qk_clip import score_bounds
-        snapshot = score_bounds(self.model)
-        entries = []
-        for layer, (blk, bounds) in enumerate(zip(self.model.blocks, snapshot)):
-            expected = {"S1", "S2"} if hasattr(blk.attn, "q2") else {"S1"}
-            if set(bounds) != expected:
-                raise ValueError("missing or invalid polynomial score bounds")
-            for name, bound in bounds.items():
-                if not torch.is_tensor(bound) or bound.shape != (self.model.cfg.heads,):
-                    raise ValueError("invalid score bound shape")
-                entries.append((layer, name, bound.detach()))
-        if not entries:
-            raise ValueError("no polynomial score bounds were recorded")
-        values = torch.cat([b for _, _, b in entries])
-        mx = values.amax()
-        mx = torch.where((values < 0).any(), mx.new_full((), float("nan")), mx)
-        self.maximum = mx if self.maximum is None else torch.maximum(self.maximum, mx)
+        found = self._recorded()
+        # one contiguous copy: safe against reused output buffers, one reduction for all factors
+        flat = torch.cat([b for _, _, b in found])
+        top = flat.amax()
+        top = torch.where((flat < 0).any(), torch.full_like(top, float("nan")), top)
+        self.maximum = top if self.maximum is None else torch.maximum(self.maximum, top)
         heads = self.model.cfg.heads
-        self.last = [{} for _ in snapshot]
-        for k, (layer, name, _) in enumerate(entries):
-            self.last[layer][name] = values[k * heads:(k + 1) * heads]
+        self.last = [{} for _ in self.model.blocks]
+        for k, (layer, factor, _) in enumerate(found):
+            self.last[layer][factor] = flat[k * heads:(k + 1) * heads]
 
     def finish_update(self) -> float:
         if not self.enabled:
             return 0.0
         if self.maximum is None:
-            raise ValueError("no score bounds recorded for this update")
-        mx = float(self.maximum)
-        if not math.isfinite(mx) or mx < 0:
-            raise FloatingPointError("nonfinite or negative score bound; update aborted")
-        return mx
+            raise ValueError("this update recorded no score bounds")
+        top = float(self.maximum)
+        if not math.isfinite(top) or top < 0:
+            raise FloatingPointError("a score bound was non-finite or negative; the update is aborted")
+        return top
 
-    def clip(self, tau):
+    def clip(self, tau) -> dict:
         from .qk_clip import qk_clip_from_bounds_
         self.finish_update()
         if self.last is None:
-            raise ValueError("no last-microbatch score bounds for clipping")
+            raise ValueError("no last-micro-batch score bounds to clip from")
         for blk, bounds in zip(self.model.blocks, self.last):
             blk.attn.last_score_bound = bounds
         t0 = time.monotonic()
         stats = qk_clip_from_bounds_(self.model, tau)
-        bad = []
-        finite_json(stats, "qk_clip", bad)
-        if bad:
-            raise FloatingPointError("nonfinite QK clipping result: " + ", ".join(bad))
-        return {**stats, "seconds": time.monotonic() - t0, "optimizer_state_policy": "moments and step counters unchanged"}
+        _require_finite_clip(stats)
+        return {**stats, "seconds": time.monotonic() - t0, "optimizer_state_policy": OPTIMIZER_STATE_POLICY}
 
 
 class TrainingStabilityProbe:
-    """First row (<= 512 tokens) of an independent train-split sampler, used between optimizer
-    steps for stability statistics and probe-based QK-clip; RNG, module modes and norm collection
-    state are restored afterwards."""
-
     def __init__(self, cfg, device):
         from .data import PackedSampler, batch_hash
         self.device = torch.device(device)
         data = cfg.raw["data"]
-        context = min(data.get("context", 512), 512)
+        context = min(data.get("context", 512), PROBE_MAX_CONTEXT)
         sampler = PackedSampler(data["manifest"], split="train", batch_size=1, context=context, seed=cfg.train.seed)
         batch = sampler.next_batch()
-        self.identity = {"batch_sha256": batch_hash(batch), "manifest_sha256": sampler.manifest_hash, "split": "train",
-                         "seed": cfg.train.seed, "context": context, "batch_size": 1}
+        self.identity = {"batch_sha256": batch_hash(batch), "manifest_sha256": sampler.manifest_hash,
+                         "split": "train", "seed": cfg.train.seed, "context": context, "batch_size": 1}
         self.idx, self.doc = (t.to(self.device) for t in batch[:2])
 
-    def _run(self, model, operation):
-        t0 = time.monotonic()
+    @contextmanager
+    def _isolated(self, model):
+        """Eval mode, no norm statistics, no score recording, forked RNGs; all restored on exit."""
         modes = [(m, m.training) for m in model.modules()]
         norms = [(m, m.collecting, m._valid) for m in lagged_modules(model) + taper_modules(model)]
-        bounds = [(b.attn, b.attn.record_score_bound, b.attn.last_score_bound) for b in model.blocks]
-        py_rng, np_rng = random.getstate(), np.random.get_state()
-        devices = ([self.device.index if self.device.index is not None else torch.cuda.current_device()]
-                   if self.device.type == "cuda" else [])
+        recorders = [(b.attn, b.attn.record_score_bound, b.attn.last_score_bound) for b in model.blocks]
+        host_rngs = (random.getstate(), np.random.get_state())
+        cuda = ([self.device.index if self.device.index is not None else torch.cuda.current_device()]
+                if self.device.type == "cuda" else [])
         try:
-            with torch.random.fork_rng(devices=devices), torch.no_grad():
+            with torch.random.fork_rng(devices=cuda), torch.no_grad():
                 model.eval()
-                for attn, _, _ in bounds:
+                for attn, _, _ in recorders:
                     attn.record_score_bound = False
                 for m, _, _ in norms:
                     m.collecting = False
-                stats = operation(model, self.idx, self.doc)
+                yield
                 if self.device.type == "cuda":
-                    torch.cuda.synchronize(self.device)
+                    torch.cuda.synchronize(self.device)  # the probe's time includes finishing it
         finally:
-            for attn, rec, last in bounds:
-                attn.record_score_bound, attn.last_score_bound = rec, last
+            for attn, on, last in recorders:
+                attn.record_score_bound, attn.last_score_bound = on, last
             for m, training in modes:
                 m.training = training
-            for m, coll, valid in norms:
-                m.collecting, m._valid = coll, valid
-            random.setstate(py_rng)
-            np.random.set_state(np_rng)
-        return stats, time.monotonic() - t0
+            for m, collecting, valid in norms:
+                m.collecting, m._valid = collecting, valid
+            random.setstate(host_rngs[0])
+            np.random.set_state(host_rngs[1])
 
     def sample(self, model) -> dict:
         from .analysis import stability_stats
-        stats, seconds = self._run(model, stability_stats)
-        bad = []
-        clean = finite_json(stats, "stats", bad)
-        return {"stats": clean, "probe": dict(self.identity), "seconds": seconds, "nonfinite_paths": bad}
+        t0 = time.monotonic()
+        with self._isolated(model):
+            stats = stability_stats(model, self.idx, self.doc)
+        clean, bad = sanitize_finite(stats, "stats")
+        return {"stats": clean, "probe": dict(self.identity), "seconds": time.monotonic() - t0,
+                "nonfinite_paths": bad}
 
     def clip(self, model, tau) -> dict:
         from .qk_clip import qk_clip_
-        stats, seconds = self._run(model, lambda m, idx, doc: qk_clip_(m, idx, doc, tau))
-        bad = []
-        finite_json(stats, "qk_clip", bad)
-        if bad:
-            raise FloatingPointError("nonfinite QK clipping result: " + ", ".join(bad))
-        return {**stats, "probe": dict(self.identity), "seconds": seconds,
-                "optimizer_state_policy": "moments and step counters unchanged"}
+        t0 = time.monotonic()
+        with self._isolated(model):
+            stats = qk_clip_(model, self.idx, self.doc, tau)
+        _require_finite_clip(stats)
+        return {**stats, "probe": dict(self.identity), "seconds": time.monotonic() - t0,
+                "optimizer_state_policy": OPTIMIZER_STATE_POLICY}

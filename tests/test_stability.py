@@ -10,7 +10,7 @@ from tensor_train_ing_b200.config import Config, ModelConfig, TrainConfig
 from tensor_train_ing_b200.models.model import TensorLM
 from tensor_train_ing_b200.qk_clip import head_score_max, qk_clip_, qk_clip_from_bounds_, score_bounds, \
     set_score_bound_recording
-from tensor_train_ing_b200.training_stability import BatchScoreBounds, qk_clip_policy, qk_clip_source
+from tensor_train_ing_b200.training_stability import BatchScoreBounds, StabilityPolicy
 from tensor_train_ing_b200.training_taper import TaperTraining, validate_taper_config
 
 
@@ -82,7 +82,8 @@ def test_score_bound_tracker_lifecycle(fp64):
     cfg = types.SimpleNamespace(train=types.SimpleNamespace(qk_clip_source="batch_bound", qk_clip_tau=1.0,
                                                             qk_clip_every_steps=2),
                                 model=types.SimpleNamespace(attention="signed_product", normalization="pre_rms"))
-    assert qk_clip_source(cfg) == "batch_bound" and qk_clip_policy(cfg) == (1.0, 2)
+    policy = StabilityPolicy.from_config(cfg)
+    assert (policy.clip_source, policy.clip_tau, policy.clip_every, policy.stability_every) == ("batch_bound", 1.0, 2, 0)
     tracker = BatchScoreBounds(model, cfg)
     tracker.begin_update()
     with pytest.raises(ValueError):
@@ -97,7 +98,7 @@ def test_score_bound_tracker_lifecycle(fp64):
     bad = types.SimpleNamespace(train=types.SimpleNamespace(qk_clip_source="batch_bound", qk_clip_tau=1.0,
                                                             qk_clip_every_steps=0), model=cfg.model)
     with pytest.raises(ValueError):
-        qk_clip_policy(bad)  # clipping enabled with no interval
+        StabilityPolicy.from_config(bad)  # clipping enabled with no interval
 
 
 def test_taper_lifecycle_warmup_freeze_and_gate():
