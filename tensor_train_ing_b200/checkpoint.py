@@ -249,7 +249,7 @@ def _validate_optimizer_layout(optimizer, saved):
 def _optimizer_identity_ok(saved_class, optimizer) -> bool:
     """The optimizer class must match; reference and framework classes of the same optimizer
     (e.g. ``tnlm.optim.MuonAdamW`` / ``tensor_train_ing_b200.optim.MuonAdamW``) are equivalent."""
-    if saved_class is None:
+    if saved_class is None or saved_class == getattr(optimizer, "checkpoint_class", None):
         return True
     ours = f"{type(optimizer).__module__}.{type(optimizer).__qualname__}"
     if saved_class == ours:

@@ -13,6 +13,7 @@
 #include "gemm/ce_api.h"
 #include "misc/rowops.h"
 #include "comm/peer.h"
+#include "optim/optim_api.h"
 
 namespace {
 
@@ -406,6 +407,84 @@ void ag_pull_cast(const Tensor& segs, int64_t max_n) {
 
 int64_t status() { return static_cast<int64_t>(ttb::status_read_and_reset()); }
 
+// ------------------------------------------------------------------------------------ optimizer
+const float* scale_ptr(const c10::optional<Tensor>& grad_scale) {
+  if (!grad_scale.has_value()) return nullptr;
+  TORCH_CHECK(grad_scale->is_cuda() && grad_scale->scalar_type() == torch::kFloat32 && grad_scale->numel() == 1,
+              "grad_scale: one fp32 element on the device");
+  return grad_scale->data_ptr<float>();
+}
+
+void check_matrix_f32(const Tensor& t, const char* name) {
+  check_cuda(t, name);
+  TORCH_CHECK(t.scalar_type() == torch::kFloat32 && t.dim() == 2 && t.is_contiguous(), name,
+              " must be a contiguous 2-D fp32 tensor");
+}
+
+// table: int64 [count, 8] device rows (p, g, exp_avg, exp_avg_sq, step, cache, n, first_chunk).
+void adamw_update(const Tensor& table, int64_t total_chunks, double lr, double beta1, double beta2, double eps,
+                  double weight_decay, const c10::optional<Tensor>& grad_scale) {
+  check_cuda(table, "table");
+  TORCH_CHECK(table.scalar_type() == torch::kInt64 && table.dim() == 2 && table.size(1) == 8 && table.is_contiguous(),
+              "table: contiguous int64 [count, 8]");
+  const c10::cuda::CUDAGuard guard(table.device());
+  ttb::adamw_update(reinterpret_cast<const ttb::AdamwTensor*>(table.data_ptr()), static_cast<int>(table.size(0)),
+                    total_chunks, static_cast<float>(lr), static_cast<float>(beta1), static_cast<float>(beta2),
+                    static_cast<float>(eps), static_cast<float>(weight_decay), scale_ptr(grad_scale), cur_stream());
+}
+
+// Returns the number of partial sums written into `partial`.
+int64_t muon_prepare(const Tensor& g, Tensor& buf, Tensor& x, Tensor& partial, double w_buf, double w_nesterov,
+                     bool nesterov, bool transpose, const c10::optional<Tensor>& grad_scale) {
+  check_matrix_f32(g, "g");
+  check_matrix_f32(buf, "buf");
+  check_bf16(x, "x");
+  TORCH_CHECK(buf.sizes() == g.sizes(), "buf must match g");
+  const int rows = g.size(0), cols = g.size(1);
+  TORCH_CHECK(x.is_contiguous() && x.dim() == 2 && x.size(0) == (transpose ? cols : rows) &&
+                  x.size(1) == (transpose ? rows : cols), "x: contiguous, g's shape (transposed if asked)");
+  TORCH_CHECK(partial.is_cuda() && partial.scalar_type() == torch::kFloat32 && partial.numel() >= ttb::kMuonMaxPartials,
+              "partial: fp32 with room for the partial sums");
+  const c10::cuda::CUDAGuard guard(g.device());
+  return ttb::muon_prepare(g.data_ptr<float>(), buf.data_ptr<float>(),
+                           reinterpret_cast<__nv_bfloat16*>(x.data_ptr()), partial.data_ptr<float>(), rows, cols,
+                           static_cast<float>(w_buf), static_cast<float>(w_nesterov), nesterov, transpose,
+                           scale_ptr(grad_scale), cur_stream());
+}
+
+void muon_normalize(Tensor& x, const Tensor& partial, int64_t n_partial, double eps) {
+  check_bf16(x, "x");
+  TORCH_CHECK(x.is_contiguous(), "x must be contiguous");
+  TORCH_CHECK(partial.is_cuda() && partial.scalar_type() == torch::kFloat32 && partial.numel() >= n_partial,
+              "partial: fp32 holding n_partial sums");
+  const c10::cuda::CUDAGuard guard(x.device());
+  ttb::muon_normalize(reinterpret_cast<__nv_bfloat16*>(x.data_ptr()), x.numel(), partial.data_ptr<float>(),
+                      static_cast<int>(n_partial), static_cast<float>(eps), cur_stream());
+}
+
+// p = p * decay + alpha * o (o: p's shape, or transposed); cache (optional bf16 [rows, cols] view with
+// unit column stride) receives bf16(p).
+void muon_apply(Tensor& p, const Tensor& o, bool transposed, double decay, double alpha,
+                const c10::optional<Tensor>& cache) {
+  check_matrix_f32(p, "p");
+  check_bf16(o, "o");
+  const int rows = p.size(0), cols = p.size(1);
+  TORCH_CHECK(o.is_contiguous() && o.dim() == 2 && o.size(0) == (transposed ? cols : rows) &&
+                  o.size(1) == (transposed ? rows : cols), "o: contiguous, p's shape (transposed if so flagged)");
+  __nv_bfloat16* c = nullptr;
+  int64_t ld = 0;
+  if (cache.has_value()) {
+    check_bf16(*cache, "cache");
+    TORCH_CHECK(cache->dim() == 2 && cache->size(0) == rows && cache->size(1) == cols && cache->stride(1) == 1,
+                "cache: bf16 [rows, cols] with unit column stride");
+    c = reinterpret_cast<__nv_bfloat16*>(cache->data_ptr());
+    ld = cache->stride(0);
+  }
+  const c10::cuda::CUDAGuard guard(p.device());
+  ttb::muon_apply(p.data_ptr<float>(), reinterpret_cast<const __nv_bfloat16*>(o.data_ptr()), rows, cols, transposed,
+                  static_cast<float>(decay), static_cast<float>(alpha), c, ld, cur_stream());
+}
+
 }  // namespace
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
@@ -440,5 +519,14 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("dk"), py::arg("dv"), py::arg("qkv"), py::arg("cols"), py::arg("dout"), py::arg("pos"), py::arg("doc"),
         py::arg("doc_end"), py::arg("row_scale"), py::arg("par"), py::arg("B"), py::arg("T"), py::arg("H"),
         py::arg("rope_cos") = py::none(), py::arg("rope_sin") = py::none());
+  m.def("adamw_update", &adamw_update, "multi-tensor AdamW step (step counters, clip scale, bf16 copies)",
+        py::arg("table"), py::arg("total_chunks"), py::arg("lr"), py::arg("beta1"), py::arg("beta2"), py::arg("eps"),
+        py::arg("weight_decay"), py::arg("grad_scale") = py::none());
+  m.def("muon_prepare", &muon_prepare, "Muon momentum + Nesterov + bf16 operand + sum of squares",
+        py::arg("g"), py::arg("buf"), py::arg("x"), py::arg("partial"), py::arg("w_buf"), py::arg("w_nesterov"),
+        py::arg("nesterov"), py::arg("transpose"), py::arg("grad_scale") = py::none());
+  m.def("muon_normalize", &muon_normalize, "divide the Newton-Schulz operand by its bf16 Frobenius norm");
+  m.def("muon_apply", &muon_apply, "Muon decay + update + bf16 weight copy", py::arg("p"), py::arg("o"),
+        py::arg("transposed"), py::arg("decay"), py::arg("alpha"), py::arg("cache") = py::none());
   m.def("qkv_rope", &qkv_rope, "QKV projection GEMM with the rotary embedding in its epilogue");
 }

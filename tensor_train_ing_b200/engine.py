@@ -112,14 +112,21 @@ class TrainEngine:
         if self.world > 1:
             dist.all_reduce(loss_sum, group=self.group)
         self._mark(marks, "reduce_gradients")
+        scale = None
         if self.grad_clip and self.grad_clip > 0:
-            if self.dp is not None:
+            if self.dp is not None and getattr(self.optimizer, "accepts_grad_scale", False):
+                # the optimizer kernels multiply each gradient by the coefficient as they read it
+                self.last_grad_norm, scale = self.dp.clip_coefficient(self.grad_clip)
+            elif self.dp is not None:
                 self.last_grad_norm = self.dp.clip_(self.grad_clip)
             else:
                 params = [p for p in self.model.parameters() if p.grad is not None]
                 self.last_grad_norm = torch.nn.utils.clip_grad_norm_(params, self.grad_clip, foreach=True)
         self._mark(marks, "clip")
-        self.optimizer.step()
+        if scale is not None:
+            self.optimizer.step(grad_scale=scale)
+        else:
+            self.optimizer.step()
         self._mark(marks, "optimizer")
         if self.dp is not None:
             self.dp.gather_params()

@@ -131,3 +131,30 @@ def group_for(owner, name: str, params: list[torch.Tensor]):
         grp = WeightGroup(params)
         object.__setattr__(owner, attr, grp)
     return grp
+
+
+def cache_views(model):
+    """Rows of the bf16 operand caches an optimizer can write the updated weights into.
+
+    Returns ({id(param): bf16 [rows, d_in] view into its group's cache}, [groups]) over the weight
+    groups whose cache already exists and is managed here (not by a parameter-sharding layer)."""
+    from .block import model_weight_groups
+    views, groups = {}, []
+    for owner, name, lins in model_weight_groups(model):
+        grp = getattr(owner, f"_ttb_group_{name}", None)
+        if (grp is None or grp._cache is None or grp._shard is not None
+                or any(p is not l.weight for p, l in zip(grp.params, lins))):
+            continue
+        row = 0
+        for p, n in zip(grp.params, grp.rows):
+            views[id(p)] = grp._cache[row:row + n]
+            row += n
+        groups.append(grp)
+    return views, groups
+
+
+def mark_current(groups, written: set) -> None:
+    """Declare the caches of groups whose every parameter's rows were just rewritten up to date."""
+    for grp in groups:
+        if all(id(p) in written for p in grp.params):
+            grp._key = grp._version_key()

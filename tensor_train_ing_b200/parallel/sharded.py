@@ -608,6 +608,13 @@ class ShardedDataParallel:
             dist.all_reduce(sq, group=self.group)
         return sq
 
+    def clip_coefficient(self, max_norm: float) -> tuple[torch.Tensor, torch.Tensor]:
+        """(pre-clip global norm, clip coefficient) as device fp32 scalars; the gradients are left
+        as they are for an optimizer that applies the coefficient while it reads them."""
+        norm = self.grad_norm_sq().sqrt()
+        coef = (max_norm / (norm + 1e-6)).clamp(max=1.0).to(torch.float32).reshape(1)
+        return norm.float(), coef
+
     def clip_(self, max_norm: float) -> torch.Tensor:
         """Scale the owned gradients so the global norm is at most ``max_norm`` (the rule of
         torch.nn.utils.clip_grad_norm_); returns the pre-clip global norm (fp32, on the device)."""

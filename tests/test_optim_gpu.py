@@ -1,0 +1,100 @@
+"""The optimizer kernels against torch's optimizers on the same gradients (B200).
+
+* FusedAdamW (one multi-tensor kernel per group, clip coefficient read on the device) against
+  torch.optim.AdamW, three steps, with and without a gradient scale: parameters and both moments
+  within rtol 1e-5 / atol 1e-6 (the same fp32 formulas; only operation order differs).
+* Muon's fused path (prepare, normalize, tcgen05 Newton-Schulz, apply) against torch.optim.Muon,
+  three steps on wide, tall and square matrices: momentum buffers within rtol 1e-6 (identical fp32
+  lerps); parameters within 2 % of the accumulated update's norm (the Newton-Schulz GEMMs round
+  bf16 products in another order than cuBLAS).
+* MuonAdamW writes the updated bf16 operand caches, which then equal a fresh conversion of the
+  fp32 weights bit for bit.
+"""
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+
+def _grads(shapes, steps, seed):
+    g = torch.Generator(device="cuda").manual_seed(seed)
+    return [[torch.randn(s, device="cuda", generator=g) for s in shapes] for _ in range(steps)]
+
+
+@pytest.mark.parametrize("scaled", [False, True])
+def test_fused_adamw_matches_torch_adamw(scaled):
+    from tensor_train_ing_b200.optim import FusedAdamW
+    shapes = [(257, 129), (4096,), (3,), (64, 64)]
+    torch.manual_seed(0)
+    base = [torch.randn(s, device="cuda") for s in shapes]
+    ours = [b.clone().requires_grad_(True) for b in base]
+    ref = [b.clone().requires_grad_(True) for b in base]
+    groups = lambda ps: [{"params": ps[:2], "weight_decay": 0.1}, {"params": ps[2:], "weight_decay": 0.0}]
+    opt = FusedAdamW(groups(ours), lr=3e-3, betas=(0.9, 0.95))
+    topt = torch.optim.AdamW(groups(ref), lr=3e-3, betas=(0.9, 0.95), foreach=False)
+    scale = torch.tensor([0.37], device="cuda") if scaled else None
+    for grads in _grads(shapes, 3, seed=1):
+        for p, q, g in zip(ours, ref, grads):
+            p.grad = g.clone()
+            q.grad = g * 0.37 if scaled else g.clone()
+        opt.step(grad_scale=scale)
+        topt.step()
+    torch.cuda.synchronize()
+    for p, q in zip(ours, ref):
+        torch.testing.assert_close(p, q, rtol=1e-5, atol=1e-6)
+        for key in ("exp_avg", "exp_avg_sq"):
+            torch.testing.assert_close(opt.state[p][key], topt.state[q][key], rtol=1e-5, atol=1e-7)
+        assert float(opt.state[p]["step"]) == float(topt.state[q]["step"]) == 3.0
+    # the state dict is torch AdamW's: it loads into a torch optimizer unchanged
+    torch.optim.AdamW(groups([q.detach().clone().requires_grad_(True) for q in ref]), lr=3e-3).load_state_dict(
+        opt.state_dict())
+
+
+@pytest.mark.parametrize("shape", [(256, 1024), (1024, 256), (512, 512)])
+def test_fused_muon_matches_torch_muon(shape):
+    from tensor_train_ing_b200.optim import Muon
+    torch.manual_seed(0)
+    p0 = torch.randn(shape, device="cuda") * 0.02
+    ours = p0.clone().requires_grad_(True)
+    ref = p0.clone().requires_grad_(True)
+    kw = dict(lr=0.02, weight_decay=0.1, momentum=0.95, nesterov=True, adjust_lr_fn="match_rms_adamw")
+    opt = Muon([ours], **kw)
+    topt = torch.optim.Muon([ref], **kw)
+    scale = torch.tensor([0.5], device="cuda")
+    for (g,) in _grads([shape], 3, seed=2):
+        ours.grad = g.clone()
+        ref.grad = g * 0.5
+        opt.step(grad_scale=scale)
+        topt.step()
+    torch.cuda.synchronize()
+    torch.testing.assert_close(opt.state[ours]["momentum_buffer"], topt.state[ref]["momentum_buffer"],
+                               rtol=1e-6, atol=1e-7)
+    moved = (ref.detach() - p0).norm()
+    assert float((ours.detach() - ref.detach()).norm() / moved) < 2e-2
+
+
+def test_muon_adamw_writes_current_bf16_caches():
+    from tensor_train_ing_b200.config import Config
+    from tensor_train_ing_b200.engine import TrainEngine
+    from tensor_train_ing_b200.ops.weights import cache_views
+    cfg = Config.from_dict({"model": dict(vocab_size=512, padded_vocab=512, d_model=256, layers=2, heads=4, d_key=64,
+                                          d_value=64, d_mlp=512, attention="signed_product", mlp="bilinear",
+                                          loss_chunk_tokens=128),
+                            "train": dict(optimizer="muon", lr=0.02, aux_adamw_lr=3e-3, grad_clip=1.0)})
+    torch.manual_seed(0)
+    eng = TrainEngine(cfg, device="cuda", micro_batch=2)
+    assert eng.optimizer.accepts_grad_scale
+    idx = torch.randint(0, 512, (4, 128))
+    for _ in range(2):
+        eng.step(idx, torch.zeros_like(idx), torch.roll(idx, -1, 1))
+    torch.cuda.synchronize()
+    views, groups = cache_views(eng.model)
+    assert groups, "the forward built bf16 operand caches"
+    named = dict(eng.model.named_parameters())
+    checked = 0
+    for name, p in named.items():
+        view = views.get(id(p))
+        if view is not None:
+            assert torch.equal(view, p.detach().to(torch.bfloat16)), name
+            checked += 1
+    assert checked >= 2 * 9
