@@ -14,6 +14,8 @@
 #include "misc/rowops.h"
 #include "comm/peer.h"
 #include "optim/optim_api.h"
+#include "misc/norm_variants.h"
+#include "misc/spectral.h"
 
 namespace {
 
@@ -485,6 +487,170 @@ void muon_apply(Tensor& p, const Tensor& o, bool transposed, double decay, doubl
                   static_cast<float>(decay), static_cast<float>(alpha), c, ld, cur_stream());
 }
 
+// ------------------------------------------------------------------------------------ norm variants
+ttb::NormVariantArgs nv_args(const Tensor& x, const Tensor& w, const c10::optional<Tensor>& w2, int64_t mode,
+                             double g, double b, const c10::optional<Tensor>& a_dev, double eps) {
+  check_matrix_f32(x, "x");
+  TORCH_CHECK(w.is_cuda() && w.scalar_type() == torch::kFloat32 && w.is_contiguous() && w.numel() == x.size(1),
+              "w: contiguous fp32 [d]");
+  ttb::NormVariantArgs a{};
+  a.mode = static_cast<int>(mode);
+  a.N = x.size(0);
+  a.d = x.size(1);
+  a.eps = static_cast<float>(eps);
+  a.g = static_cast<float>(g);
+  a.b = static_cast<float>(b);
+  a.w = w.data_ptr<float>();
+  if (w2.has_value()) {
+    TORCH_CHECK(w2->is_cuda() && w2->scalar_type() == torch::kFloat32 && w2->is_contiguous() &&
+                    w2->numel() == x.size(1), "w2: contiguous fp32 [d]");
+    a.w2 = w2->data_ptr<float>();
+  }
+  if (a_dev.has_value()) {
+    TORCH_CHECK(a_dev->is_cuda() && a_dev->scalar_type() == torch::kFloat32 && a_dev->numel() == 1,
+                "scale: one fp32 element on the device");
+    a.a_dev = a_dev->data_ptr<float>();
+  }
+  TORCH_CHECK(reinterpret_cast<uintptr_t>(x.data_ptr()) % 16 == 0 && reinterpret_cast<uintptr_t>(a.w) % 16 == 0 &&
+                  (a.w2 == nullptr || reinterpret_cast<uintptr_t>(a.w2) % 16 == 0), "x, w, w2: 16-byte aligned");
+  return a;
+}
+
+// Returns [y16, y32, r, msq]; an output not asked for is an empty tensor.
+std::vector<Tensor> norm_variant_fwd(const Tensor& x, const Tensor& w, const c10::optional<Tensor>& w2, int64_t mode,
+                                     double g, double b, const c10::optional<Tensor>& a_dev, double eps, bool want16,
+                                     bool want32, const c10::optional<Tensor>& resid, double alpha, bool want_r,
+                                     bool want_msq) {
+  const auto a = nv_args(x, w, w2, mode, g, b, a_dev, eps);
+  const c10::cuda::CUDAGuard guard(x.device());
+  Tensor y16, y32, r, msq;
+  if (want16) y16 = torch::empty({a.N, a.d}, x.options().dtype(torch::kBFloat16));
+  if (want32) y32 = torch::empty({a.N, a.d}, x.options());
+  if (want_r) r = torch::empty({a.N}, x.options());
+  if (want_msq) msq = torch::empty({a.N}, x.options());
+  const float* res = nullptr;
+  if (resid.has_value()) {
+    TORCH_CHECK(want32, "a residual needs the fp32 result");
+    check_matrix_f32(*resid, "resid");
+    TORCH_CHECK(resid->sizes() == x.sizes(), "resid must match x");
+    res = resid->data_ptr<float>();
+  }
+  ttb::norm_variant_fwd(a, x.data_ptr<float>(), res, static_cast<float>(alpha), want16 ? y16.data_ptr() : nullptr,
+                        want32 ? y32.data_ptr<float>() : nullptr, want_r ? r.data_ptr<float>() : nullptr,
+                        want_msq ? msq.data_ptr<float>() : nullptr, cur_stream());
+  return {y16, y32, r, msq};
+}
+
+// Returns [dx, dw, dw2]; dx is `dx_out` (added to when accumulate) or a new tensor.
+std::vector<Tensor> norm_variant_bwd(const Tensor& dy, const Tensor& x, const Tensor& w,
+                                     const c10::optional<Tensor>& w2, int64_t mode, double g, double b,
+                                     const c10::optional<Tensor>& a_dev, double eps, double dy_scale,
+                                     const c10::optional<Tensor>& r, const c10::optional<Tensor>& dr,
+                                     const c10::optional<Tensor>& dx_out, bool accumulate, bool want_dw,
+                                     bool want_dw2) {
+  const auto a = nv_args(x, w, w2, mode, g, b, a_dev, eps);
+  check_cuda(dy, "dy");
+  TORCH_CHECK(dy.is_contiguous() && dy.sizes() == x.sizes() &&
+                  (dy.scalar_type() == torch::kFloat32 || dy.scalar_type() == torch::kBFloat16),
+              "dy: contiguous fp32 or bf16 of x's shape");
+  const float* rp = nullptr;
+  const float* drp = nullptr;
+  if (r.has_value()) {
+    TORCH_CHECK(r->is_cuda() && r->scalar_type() == torch::kFloat32 && r->numel() == a.N, "r: fp32 [N]");
+    rp = r->data_ptr<float>();
+  }
+  if (dr.has_value()) {
+    TORCH_CHECK(dr->is_cuda() && dr->scalar_type() == torch::kFloat32 && dr->numel() == a.N &&
+                    dr->is_contiguous(), "dr: contiguous fp32 [N]");
+    drp = dr->data_ptr<float>();
+  }
+  const c10::cuda::CUDAGuard guard(x.device());
+  Tensor dx;
+  if (dx_out.has_value()) {
+    check_matrix_f32(*dx_out, "dx");
+    TORCH_CHECK(dx_out->sizes() == x.sizes(), "dx must match x");
+    dx = *dx_out;
+  } else {
+    TORCH_CHECK(!accumulate, "accumulating needs a dx buffer");
+    dx = torch::empty_like(x);
+  }
+  Tensor dw, dw2, part;
+  if (want_dw) dw = torch::empty({a.d}, x.options());
+  if (want_dw2) dw2 = torch::empty({a.d}, x.options());
+  if (want_dw || want_dw2)
+    part = torch::empty({(want_dw2 ? 2 : 1) * static_cast<int64_t>(ttb::norm_variant_partials(a.N)) * a.d}, x.options());
+  ttb::norm_variant_bwd(a, dy.data_ptr(), dy.scalar_type() == torch::kFloat32, static_cast<float>(dy_scale),
+                        x.data_ptr<float>(), rp, drp, dx.data_ptr<float>(), accumulate,
+                        want_dw ? dw.data_ptr<float>() : nullptr, want_dw2 ? dw2.data_ptr<float>() : nullptr,
+                        part.defined() ? part.data_ptr<float>() : nullptr, cur_stream());
+  return {dx, dw, dw2};
+}
+
+// ------------------------------------------------------------------------------------ spectral linear
+void check_vec_f32(const Tensor& t, int64_t n, const char* name) {
+  check_cuda(t, name);
+  TORCH_CHECK(t.scalar_type() == torch::kFloat32 && t.is_contiguous() && t.numel() == n, name,
+              ": contiguous fp32 with the expected length");
+}
+
+Tensor spectral_scratch(const Tensor& w) {
+  return torch::empty({ttb::spectral_scratch_floats(w.size(0), w.size(1))}, w.options());
+}
+
+// Writes bf16(gamma W / max(|sigma|, floor)) into out (bf16 [rows, cols], unit column stride);
+// returns sigma = u^T W v (fp32 [1]).
+Tensor spectral_cast(const Tensor& w, const Tensor& gamma, const Tensor& u, const Tensor& v, double floor_,
+                     Tensor& out) {
+  check_matrix_f32(w, "weight");
+  const int rows = w.size(0), cols = w.size(1);
+  check_vec_f32(gamma, 1, "gamma");
+  check_vec_f32(u, rows, "u");
+  check_vec_f32(v, cols, "v");
+  check_bf16(out, "out");
+  TORCH_CHECK(out.dim() == 2 && out.size(0) == rows && out.size(1) == cols && out.stride(1) == 1 &&
+                  out.stride(0) % 4 == 0, "out: bf16 [rows, cols], unit column stride, row stride a multiple of 4");
+  const c10::cuda::CUDAGuard guard(w.device());
+  auto sigma = torch::empty({1}, w.options());
+  auto scratch = spectral_scratch(w);
+  ttb::spectral_cast(w.data_ptr<float>(), rows, cols, gamma.data_ptr<float>(), u.data_ptr<float>(),
+                     v.data_ptr<float>(), static_cast<float>(floor_), sigma.data_ptr<float>(),
+                     scratch.data_ptr<float>(), reinterpret_cast<__nv_bfloat16*>(out.data_ptr()), out.stride(0),
+                     cur_stream());
+  return sigma;
+}
+
+// Returns [dW, dgamma] from dW_eff (fp32 [rows, cols], unit column stride).
+std::vector<Tensor> spectral_grad(const Tensor& dwe, const Tensor& w, const Tensor& gamma, const Tensor& u,
+                                  const Tensor& v, const Tensor& sigma, double floor_) {
+  check_matrix_f32(w, "weight");
+  const int rows = w.size(0), cols = w.size(1);
+  check_cuda(dwe, "dW_eff");
+  TORCH_CHECK(dwe.scalar_type() == torch::kFloat32 && dwe.dim() == 2 && dwe.size(0) == rows && dwe.size(1) == cols &&
+                  dwe.stride(1) == 1, "dW_eff: fp32 [rows, cols] with unit column stride");
+  check_vec_f32(gamma, 1, "gamma");
+  check_vec_f32(u, rows, "u");
+  check_vec_f32(v, cols, "v");
+  check_vec_f32(sigma, 1, "sigma");
+  const c10::cuda::CUDAGuard guard(w.device());
+  auto dw = torch::empty_like(w);
+  auto dgamma = torch::empty({1}, w.options());
+  auto scratch = spectral_scratch(w);
+  ttb::spectral_grad(dwe.data_ptr<float>(), dwe.stride(0), w.data_ptr<float>(), rows, cols, gamma.data_ptr<float>(),
+                     u.data_ptr<float>(), v.data_ptr<float>(), sigma.data_ptr<float>(), static_cast<float>(floor_),
+                     scratch.data_ptr<float>(), dw.data_ptr<float>(), dgamma.data_ptr<float>(), cur_stream());
+  return {dw, dgamma};
+}
+
+void spectral_power_step(const Tensor& w, Tensor& u, Tensor& v, double floor_) {
+  check_matrix_f32(w, "weight");
+  check_vec_f32(u, w.size(0), "u");
+  check_vec_f32(v, w.size(1), "v");
+  const c10::cuda::CUDAGuard guard(w.device());
+  auto scratch = spectral_scratch(w);
+  ttb::spectral_power_step(w.data_ptr<float>(), w.size(0), w.size(1), u.data_ptr<float>(), v.data_ptr<float>(),
+                           static_cast<float>(floor_), scratch.data_ptr<float>(), cur_stream());
+}
+
 }  // namespace
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
@@ -528,5 +694,16 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("muon_normalize", &muon_normalize, "divide the Newton-Schulz operand by its bf16 Frobenius norm");
   m.def("muon_apply", &muon_apply, "Muon decay + update + bf16 weight copy", py::arg("p"), py::arg("o"),
         py::arg("transposed"), py::arg("decay"), py::arg("alpha"), py::arg("cache") = py::none());
+  m.def("norm_variant_fwd", &norm_variant_fwd, "lagged / taper / fp32-output RMS row normalisation",
+        py::arg("x"), py::arg("w"), py::arg("w2"), py::arg("mode"), py::arg("g"), py::arg("b"), py::arg("scale"),
+        py::arg("eps"), py::arg("want16"), py::arg("want32"), py::arg("resid"), py::arg("alpha"), py::arg("want_r"),
+        py::arg("want_msq"));
+  m.def("norm_variant_bwd", &norm_variant_bwd, "backward of norm_variant_fwd (dx, dw, dw2)", py::arg("dy"),
+        py::arg("x"), py::arg("w"), py::arg("w2"), py::arg("mode"), py::arg("g"), py::arg("b"), py::arg("scale"),
+        py::arg("eps"), py::arg("dy_scale"), py::arg("r"), py::arg("dr"), py::arg("dx"), py::arg("accumulate"),
+        py::arg("want_dw"), py::arg("want_dw2"));
+  m.def("spectral_cast", &spectral_cast, "sigma = u^T W v and the bf16 effective weight");
+  m.def("spectral_grad", &spectral_grad, "dW and dgamma of the spectral effective weight");
+  m.def("spectral_power_step", &spectral_power_step, "one power-iteration step on u and v");
   m.def("qkv_rope", &qkv_rope, "QKV projection GEMM with the rotary embedding in its epilogue");
 }

@@ -18,11 +18,22 @@ def _rmsnorm_bwd_kernels(dy, x, w, rstd, dres, accumulate, groups, *rest, **kw):
     return 2 if int(groups) == 1 and x.shape[-1] in (1024, 2048, 4096) else 3
 
 
+def _norm_variant_bwd_kernels(dy, x, w, w2, mode, g, b, scale, eps, dy_scale, r, dr, dx, accumulate, want_dw,
+                              want_dw2, **kw):
+    """The dx pass, the weight-gradient column pass when any weight gradient is asked for, and one
+    column sum per weight gradient (csrc/misc/norm_variants.cu)."""
+    wants = int(bool(want_dw)) + int(bool(want_dw2))
+    return 1 + (1 + wants if wants else 0)
+
+
 # Kernels each binding launches per call, for the launch counter (a callable gets the call's arguments).
 KERNELS_PER_CALL = {"mm": 1, "bilinear": 1, "bilinear_grad": 1, "rmsnorm_fwd": 1, "rmsnorm_bwd": _rmsnorm_bwd_kernels, "rope_": 1,
                     "embed_fwd": 1, "embed_bwd": 1, "ce_fwd": 2, "ce_bwd_logits": 1, "poly_fwd": 1,
                     "poly_bwd": 2, "qkv_rope": 1, "peer_barrier": 1, "rs_reduce_sq": 1, "ag_pull_cast": 1,
-                    "rs_accumulate": 1, "ce_bwd_from_logits": 1}
+                    "rs_accumulate": 1, "ce_bwd_from_logits": 1, "adamw_update": 2, "muon_prepare": 1,
+                    "muon_normalize": 1, "muon_apply": 1, "norm_variant_fwd": 1,
+                    "norm_variant_bwd": _norm_variant_bwd_kernels, "spectral_cast": 2, "spectral_grad": 2,
+                    "spectral_power_step": 4}
 
 
 class _Counting:

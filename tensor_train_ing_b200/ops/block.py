@@ -1,13 +1,14 @@
 """Fused (sm_100a) execution of ``TensorLM``: context tables, block forward and model forward.
 
 Per block (reference tnlm/model.py:137-144, 67-101):
-  h   = norm_in(x)                       RMSNorm / GroupRMSNorm kernel -> bf16 (other norms: module math)
+  h   = norm_in(x)                       RMSNorm / GroupRMSNorm / lagged / taper kernel -> bf16
   qkv = h [q1|k1|q2|k2|v]^T              one tcgen05 GEMM over the concatenated bf16 weights, RoPE in place
   y   = PolyAttention(qkv)               tcgen05 attention kernels
   x   = x + alpha * o(y)                 GEMM with the residual add in its epilogue (fp32 stream)
   x   = x + alpha * D(L h' * R h')       dual-B bilinear GEMM, then the down GEMM with fused residual
-With an output norm (branch_rms / sandwich_rms) the branch stays bf16 and the norm module and the
-residual add run as in the reference.  Spectral layers use their effective weights every step.
+With an output norm (branch_rms / sandwich_rms) the bf16 branch output goes through one kernel that
+forms x + alpha * RMSNorm(branch) in fp32.  Spectral layers feed the GEMMs bf16(gamma W / sigma) from one
+kernel pass per layer and turn dW_eff into dW and dgamma with another.
 """
 from __future__ import annotations
 
@@ -15,14 +16,16 @@ import torch
 import torch.nn as nn
 
 from ..models.attention import rope_inv_freq, row_scale_vector
-from ..models.normalization import GroupRMSNorm, RMSNorm, SpectralLinear
-from . import fused
-from .weights import ComputedWeights, group_for
+from ..models.normalization import GroupRMSNorm, LaggedRMS, RMSNorm, SpectralLinear, TaperRMS
+from . import fused, norms
+from .weights import group_for, spectral_group_for
 
 
 def _weights(owner, name, linears):
     if any(isinstance(l, SpectralLinear) for l in linears):
-        return ComputedWeights([l.effective_weight() for l in linears])
+        if not all(isinstance(l, SpectralLinear) and l.weight.shape[1] % 4 == 0 for l in linears):
+            raise ValueError("a fused weight group mixes spectral and plain layers")
+        return spectral_group_for(owner, name, linears)
     return group_for(owner, name, [l.weight for l in linears])
 
 
@@ -64,7 +67,18 @@ def norm_to_bf16(norm: nn.Module, x: torch.Tensor) -> torch.Tensor:
     if isinstance(norm, (RMSNorm, GroupRMSNorm)) and norm.denom_mode is None:
         groups = norm.groups if isinstance(norm, GroupRMSNorm) else 1
         return fused.rms_norm(x, norm.weight, groups, norm.eps)
+    if isinstance(norm, LaggedRMS) and x.shape[-1] % 4 == 0:
+        return norms.lagged_to_bf16(norm, x)
+    if isinstance(norm, TaperRMS) and x.shape[-1] % 4 == 0:
+        return norms.taper_to_bf16(norm, x)
     return norm(x).to(torch.bfloat16)
+
+
+def _add_branch(x, out_norm, branch, alpha):
+    """x + alpha * out_norm(branch) for a branch-output norm (fp32 stream)."""
+    if type(out_norm) is RMSNorm and out_norm.denom_mode is None and branch.shape[-1] % 4 == 0:
+        return norms.output_rms(x, branch.float(), out_norm, alpha)
+    return x + alpha * out_norm(branch)
 
 
 def _record_bound(attn, qkv, cols, N):
@@ -140,7 +154,7 @@ def block_forward(blk, x, ctx):
             x = fused.linear(y, og, residual=x, alpha=blk.alpha, bias=a.o.bias)
             up = blk.alpha
         else:
-            x = x + blk.alpha * blk.attn_out(fused.linear(y, og, bias=a.o.bias))
+            x = _add_branch(x, blk.attn_out, fused.linear(y, og, bias=a.o.bias), blk.alpha)
             up = None
     if "mlp" not in blk.ablate:
         x, h = _norm_and_residual(blk.mlp_in, x, up)
@@ -151,7 +165,7 @@ def block_forward(blk, x, ctx):
                                    bl=m.l.bias, br=m.r.bias, bd=m.d.bias)
         else:
             branch = fused.bilinear_mlp(h, gl, gr, gd, mode=mode, bl=m.l.bias, br=m.r.bias, bd=m.d.bias)
-            x = x + blk.alpha * blk.mlp_out(branch)
+            x = _add_branch(x, blk.mlp_out, branch, blk.alpha)
     return x
 
 

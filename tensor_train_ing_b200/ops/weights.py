@@ -105,22 +105,68 @@ class WeightGroup:
         return [g.to(p.dtype) for g, p in zip(self._views(out), self.params)]
 
 
-class ComputedWeights:
-    """Same interface for weights that are computed every forward (e.g. spectral effective
-    weights): no caching, gradients always go back through autograd."""
+class SpectralWeights:
+    """The weight group of SpectralLinear layers on the fused path.
 
-    def __init__(self, tensors: list[torch.Tensor]):
-        self.params = list(tensors)
-        self.rows = [t.shape[0] for t in self.params]
-        self.d_in = self.params[0].shape[-1]
+    ``bf16()`` writes bf16(gamma W / sigma) of every layer with one kernel pass each (sigma = u^T W v
+    reduced on the device), cached until a weight, gamma, u or v changes or an optimizer steps;
+    ``sink_grad`` turns the weight-gradient GEMM's dW_eff into dW and dgamma with the spectral
+    backward kernel (the gradient through sigma included).  ``params`` lists each layer's weight and
+    gamma, in that order."""
+
+    def __init__(self, linears):
+        self.linears = list(linears)
+        self.params = [t for lin in self.linears for t in (lin.weight, lin.gamma)]
+        self.rows = [lin.weight.shape[0] for lin in self.linears]
+        self.d_in = self.linears[0].weight.shape[1]
+        self._cache = None
+        self._key = None
+        self._sigmas: list[torch.Tensor] = []
+
+    def _version_key(self):
+        return (_STEPS[0],) + tuple((t.data_ptr(), t._version) for lin in self.linears
+                                    for t in (lin.weight, lin.gamma, lin.u, lin.v))
 
     def bf16(self) -> torch.Tensor:
-        return torch.cat([t.detach() for t in self.params], dim=0).to(torch.bfloat16)
+        from ..models.normalization import SIGMA_FLOOR
+        from ._ext import lib
+        key = self._version_key()
+        if self._cache is None or key != self._key:
+            dev = self.linears[0].weight.device
+            if self._cache is None or self._cache.device != dev:
+                self._cache = torch.empty(sum(self.rows), self.d_in, device=dev, dtype=torch.bfloat16)
+            self._sigmas, row = [], 0
+            with torch.no_grad():
+                for lin, n in zip(self.linears, self.rows):
+                    self._sigmas.append(lib().spectral_cast(lin.weight.detach(), lin.gamma.detach(), lin.u, lin.v,
+                                                            SIGMA_FLOOR, self._cache[row:row + n]))
+                    row += n
+            self._key = key
+        return self._cache
 
     def sink_grad(self, compute):
-        out = torch.empty(sum(self.rows), self.d_in, device=self.params[0].device, dtype=torch.float32)
-        compute(out, 0.0)
-        return [g.to(t.dtype) for g, t in zip(out.split(self.rows, dim=0), self.params)]
+        from ..models.normalization import SIGMA_FLOOR
+        from ._ext import lib
+        eff = torch.empty(sum(self.rows), self.d_in, device=self.linears[0].weight.device, dtype=torch.float32)
+        compute(eff, 0.0)
+        self.bf16()  # the sigmas of the weights this backward differentiates
+        grads, row = [], 0
+        for lin, n, sigma in zip(self.linears, self.rows, self._sigmas):
+            dw, dgamma = lib().spectral_grad(eff[row:row + n], lin.weight.detach(), lin.gamma.detach(), lin.u,
+                                             lin.v, sigma, SIGMA_FLOOR)
+            grads += [dw, dgamma]
+            row += n
+        return grads
+
+
+def spectral_group_for(owner, name: str, linears):
+    """Cached SpectralWeights stored on ``owner`` (rebuilt if the layer objects changed)."""
+    attr = f"_ttb_spectral_{name}"
+    grp = getattr(owner, attr, None)
+    if grp is None or len(grp.linears) != len(linears) or any(a is not b for a, b in zip(grp.linears, linears)):
+        grp = SpectralWeights(linears)
+        object.__setattr__(owner, attr, grp)
+    return grp
 
 
 def group_for(owner, name: str, params: list[torch.Tensor]):

@@ -84,3 +84,87 @@ def test_training_steps_follow_reference_path(optimizer):
     assert r[-1] < 0.9 * r[0], r  # the test only means something if training moves the loss
     for a, b in zip(f, r):
         assert abs(a - b) < 3e-2 * abs(b), (f, r)
+
+
+def _norm_modules(model, cls):
+    return [m for m in model.modules() if isinstance(m, cls)]
+
+
+@pytest.mark.parametrize("case", ["branch_rms", "lagged", "taper_warmup", "taper_frozen"])
+def test_norm_variant_packages_match_reference(case):
+    """The lagged, taper and branch-output norms on their fused kernels against the module path:
+    loss, every gradient (as close to fp64 as the bf16 reference path), lagged and TaperNorm
+    statistics, and the TaperNorm anchor term with its gradient."""
+    from tensor_train_ing_b200.models.normalization import LaggedRMS, TaperRMS, taper_anchor_loss
+    torch.manual_seed(0)
+    norm = {"taper_warmup": "taper", "taper_frozen": "taper"}.get(case, case)
+    cfg = ModelConfig(layers=2, d_model=256, heads=2, d_key=64, d_value=64, d_mlp=512, vocab_size=1000,
+                      padded_vocab=1024, attention="signed_product", normalization=norm, loss_chunk_tokens=256,
+                      qk_init_scale=0.5)
+    B, T = 2, 160
+    idx = torch.randint(0, 1000, (B, T), device="cuda")
+    docs = torch.zeros(B, T, dtype=torch.long, device="cuda")
+    docs[:, 90:] = 1
+    tgt = torch.roll(idx, -1, 1)
+    tgt[:, -1] = -100
+    valid = (tgt != -100).to(torch.float32)
+
+    def prepare(model):
+        with torch.no_grad():
+            for i, m in enumerate(_norm_modules(model, LaggedRMS)):
+                m.mean_sq.fill_(2.5 + i)
+                m.calibrated.fill_(True)
+                m.collecting = True
+                m.set_valid_mask(valid)
+            for i, m in enumerate(_norm_modules(model, TaperRMS)):
+                m.set_valid_mask(valid)
+                if case == "taper_warmup":
+                    m.collecting = True
+                else:
+                    m.frozen.fill_(True)
+                    m.gate.fill_(0.4)
+                    m.c.fill_(0.8 + 0.05 * i)
+                    m.s_tgt.fill_(1.3)
+                    m.weight_tilde.mul_(1.1)
+        return model
+
+    def run(model, autocast):
+        model.train()
+        with torch.autocast("cuda", dtype=torch.bfloat16, enabled=autocast):
+            _, loss, _ = model(idx, docs, tgt, reduction="sum")
+        anchor = taper_anchor_loss(model)
+        total = loss + (50.0 * anchor if anchor is not None else 0.0)
+        total.backward()
+        return loss.detach(), (anchor.detach() if anchor is not None else None)
+
+    model = prepare(TensorLM(cfg).cuda())
+    state = model.state_dict()
+    loss, anchor = run(model, False)
+    grads = {k: p.grad.detach().clone() for k, p in model.named_parameters() if p.grad is not None}
+    ref_cfg = ModelConfig(**{**cfg.__dict__, "attention_backend": "reference"})
+    ref = TensorLM(ref_cfg).cuda()
+    ref.load_state_dict(state)
+    prepare(ref)
+    _, anchor_r = run(ref, True)
+    exact = TensorLM(ref_cfg).cuda().double()
+    exact.load_state_dict(state)
+    prepare(exact)
+    loss_x, anchor_x = run(exact, False)
+    assert abs(loss.item() - loss_x.item()) / abs(loss_x.item()) < 1e-2
+    if anchor_x is not None:
+        assert abs(anchor.item() - anchor_x.item()) / abs(anchor_x.item()) < 1e-3
+    ref_grads = dict(ref.named_parameters())
+    for k, p in exact.named_parameters():
+        if p.grad is None:
+            continue
+        assert k in grads, k
+        err_fused = rel(grads[k], p.grad)
+        err_ref = rel(ref_grads[k].grad, p.grad)
+        assert err_fused < max(2.0 * err_ref, 3e-2), (k, err_fused, err_ref)
+    for fm, xm in zip(_norm_modules(model, LaggedRMS), _norm_modules(exact, LaggedRMS)):
+        assert float(fm.acc_count) == float(xm.acc_count) > 0
+        assert abs(float(fm.acc_sum) - float(xm.acc_sum)) <= 1e-5 * abs(float(xm.acc_sum))
+    for fm, xm in zip(_norm_modules(model, TaperRMS), _norm_modules(exact, TaperRMS)):
+        for name in ("acc_num", "acc_den", "acc_r", "acc_count"):
+            a, b = float(getattr(fm, name)), float(getattr(xm, name))
+            assert abs(a - b) <= 1e-5 * max(abs(b), 1e-12), (name, a, b)
