@@ -43,7 +43,7 @@ from .runtime import determinism_metadata, full_config, resume_validator, seed_a
 from .schedules import lr_multiplier, schedule_multiplier, schedule_steps, validate_schedule
 from .train import _mask_to_count, _validate_batch
 from .training_stability import BatchScoreBounds, StabilityPolicy
-from .training_taper import TaperTraining, validate_taper_config
+from .training_taper import TaperLifecycle, validate_taper_config
 
 
 def _digest_words(hexdigest: str) -> list[int]:
@@ -211,7 +211,7 @@ def distributed_train_run(cfg, run_dir, *, max_steps, max_seconds, device="cuda"
             progress["calibration"] = _agree("calibration report", calibration)
         for norm in norms:
             _phase("lagged divisor validation", lambda norm=norm: _check_lagged_divisor(norm))
-        taper = TaperTraining(model, cfg, total_steps=planned_total, warmup_steps=progress["warmup_steps"],
+        taper = TaperLifecycle(model, cfg, total_steps=planned_total, warmup_steps=progress["warmup_steps"],
                               distributed=True)
         taper.before_step(progress["steps"])
         taper.set_valid_mask(None)

@@ -7,7 +7,8 @@
 
 Cases (shapes of one 1B micro-batch, 8 x 2048 tokens, unless noted): gemm_qkv, gemm_dx, gemm_dw,
 bilinear, bilinear_grad, attn_fwd, attn_bwd, attn_case (B=2 for profiling), rmsnorm_fwd,
-rmsnorm_bwd, ce_fwd, ce_bwd, ce_bwd_kept.  Every input is larger than the 126 MB L2 or is flushed: ``time``
+rmsnorm_bwd, ce_fwd, ce_bwd, ce_bwd_kept, embed_fwd, embed_bwd, adamw (both vocabulary matrices),
+muon_prepare / muon_apply (one 8192 x 2048 matrix), norm_lagged_fwd / _bwd, spectral_cast.  Every input is larger than the 126 MB L2 or is flushed: ``time``
 writes a 256 MB buffer between timed launches.  ``TTB_GEMM_PAIR=0`` selects the one-CTA GEMM.
 The attention timings are the measurements the reference's kernel tuner makes for its Triton
 configurations (reference tnlm/kernels/tune.py:20-62); the tile shapes here are fixed per kernel.
@@ -120,11 +121,58 @@ def build(name: str) -> _Case:
         g = torch.ones(1, device="cuda")
         dl = torch.empty(N // 2, V, device="cuda", dtype=torch.bfloat16)
         return _Case(lambda: C.ce_bwd_logits(x, w, 50257, 1.0, t, lse, g, dl), fl)
+    if name in ("embed_fwd", "embed_bwd"):
+        W = torch.randn(V, D, device="cuda")
+        idx = torch.randint(0, 50257, (N,), device="cuda")
+        if name == "embed_fwd":
+            return _Case(lambda: C.embed_fwd(idx, W), 0, N * D * 4 * 2)
+        g = torch.randn(N, D, device="cuda")
+        out = torch.zeros_like(W)
+        return _Case(lambda: C.embed_bwd(idx, g, out), 0, N * D * 4 + V * D * 4 * 2)
+    if name == "adamw":  # both vocabulary matrices of the 1B model in one group
+        from .optim import FusedAdamW
+        ps = [torch.nn.Parameter(torch.randn(V, D, device="cuda") * 0.02) for _ in range(2)]
+        for p in ps:
+            p.grad = torch.randn_like(p)
+        opt = FusedAdamW([{"params": ps}], lr=1e-3, betas=(0.9, 0.95))
+        opt.step()
+        scale = torch.ones(1, device="cuda")
+        return _Case(lambda: opt.step(grad_scale=scale), 0, 2 * V * D * 4 * 7)
+    if name in ("muon_prepare", "muon_apply"):  # one 8192 x 2048 MLP matrix (tall: transposed operand)
+        g = torch.randn(DMLP, D, device="cuda")
+        buf = torch.randn_like(g)
+        x = torch.empty(D, DMLP, device="cuda", dtype=torch.bfloat16)
+        part = torch.empty(1024, device="cuda")
+        if name == "muon_prepare":
+            return _Case(lambda: C.muon_prepare(g, buf, x, part, 0.05, 0.95, True, True, None), 0,
+                         DMLP * D * (4 * 3 + 2))
+        o = torch.randn(D, DMLP, device="cuda").bfloat16()
+        cache = torch.empty(DMLP, D, device="cuda", dtype=torch.bfloat16)
+        return _Case(lambda: C.muon_apply(g, o, True, 0.999, -0.01, cache), 0, DMLP * D * (4 * 2 + 2 + 2))
+    if name in ("norm_lagged_fwd", "norm_lagged_bwd"):
+        x = torch.randn(N, D, device="cuda")
+        w = torch.ones(D, device="cuda")
+        s = torch.full((1,), 0.7, device="cuda")
+        if name == "norm_lagged_fwd":
+            return _Case(lambda: C.norm_variant_fwd(x, w, None, 0, 0.0, 0.0, s, 1e-6, True, False, None, 1.0, False,
+                                                    False), 0, N * D * (4 + 2))
+        dy = torch.randn(N, D, device="cuda").bfloat16()
+        dx = torch.zeros_like(x)
+        return _Case(lambda: C.norm_variant_bwd(dy, x, w, None, 0, 0.0, 0.0, s, 1e-6, 1.0, None, None, dx, True, True,
+                                                False), 0, N * D * (2 + 4 + 8) + N * D * (2 + 4))
+    if name == "spectral_cast":
+        W = torch.randn(DMLP, D, device="cuda") * 0.02
+        gamma = torch.ones(1, device="cuda")
+        u = torch.nn.functional.normalize(torch.randn(DMLP, device="cuda"), dim=0)
+        v = torch.nn.functional.normalize(torch.randn(D, device="cuda"), dim=0)
+        out = torch.empty(DMLP, D, device="cuda", dtype=torch.bfloat16)
+        return _Case(lambda: C.spectral_cast(W, gamma, u, v, 1e-12, out), 0, DMLP * D * (4 + 4 + 2))
     raise KeyError(name)
 
 
 CASES = ["gemm_qkv", "gemm_dx", "gemm_dw", "bilinear", "bilinear_grad", "attn_fwd", "attn_bwd", "rmsnorm_fwd",
-         "rmsnorm_bwd", "ce_fwd", "ce_bwd", "ce_bwd_kept"]
+         "rmsnorm_bwd", "ce_fwd", "ce_bwd", "ce_bwd_kept", "embed_fwd", "embed_bwd", "adamw", "muon_prepare",
+         "muon_apply", "norm_lagged_fwd", "norm_lagged_bwd", "spectral_cast"]
 
 
 def time_case(name: str, reps: int = 10) -> dict:

@@ -40,7 +40,7 @@ from .optimizer_exposure import update_optimizer_exposure
 from .runtime import determinism_metadata, full_config, resume_validator, seed_all, training_execution
 from .schedules import lr_multiplier, schedule_multiplier, schedule_steps, validate_schedule
 from .training_stability import BatchScoreBounds, StabilityPolicy, TrainingStabilityProbe
-from .training_taper import TaperTraining, validate_taper_config
+from .training_taper import TaperLifecycle, validate_taper_config
 
 
 def _assert_no_analysis_state(model):
@@ -324,7 +324,7 @@ def train_run(cfg, run_dir, *, max_steps, max_seconds, device="cuda", resume=Non
         admission = require_checkpoint_space(run_dir, storage_plan["required_additional_bytes"])
         (run_dir / "checkpoint_storage_plan.json").write_text(
             json.dumps({"plan": storage_plan, "admission": admission}, indent=2, allow_nan=False) + "\n")
-        taper = TaperTraining(model, cfg, total_steps=total_steps, warmup_steps=progress["warmup_steps"])
+        taper = TaperLifecycle(model, cfg, total_steps=total_steps, warmup_steps=progress["warmup_steps"])
         taper.before_step(progress["steps"])
         taper.set_valid_mask(None)
 

@@ -11,7 +11,7 @@ from tensor_train_ing_b200.models.model import TensorLM
 from tensor_train_ing_b200.qk_clip import head_score_max, qk_clip_, qk_clip_from_bounds_, score_bounds, \
     set_score_bound_recording
 from tensor_train_ing_b200.training_stability import BatchScoreBounds, StabilityPolicy
-from tensor_train_ing_b200.training_taper import TaperTraining, validate_taper_config
+from tensor_train_ing_b200.training_taper import TaperLifecycle, validate_taper_config
 
 
 @pytest.fixture
@@ -107,7 +107,7 @@ def test_taper_lifecycle_warmup_freeze_and_gate():
     assert validate_taper_config(cfg)
     torch.manual_seed(0)
     model = TensorLM(mcfg)
-    taper = TaperTraining(model, cfg, total_steps=40, warmup_steps=4)
+    taper = TaperLifecycle(model, cfg, total_steps=40, warmup_steps=4)
     assert taper.enabled and taper.norms and taper.end_step == 20
     idx, doc = _batch()
     gates = []
