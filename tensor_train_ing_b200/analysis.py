@@ -489,7 +489,7 @@ def probe_attention_scores(model, idx, doc, max_tokens: int = 512):
         a, x = blk.attn, upcast(attn_in[i])
         row = {}
         if a.kind != "softmax":
-            heads = lambda lin: upcast(apply_rope(a._heads(x, lin, cfg.d_key), cos, sin))[0]  # noqa: E731
+            heads = lambda lin: upcast(apply_rope(a._split_heads(x, lin, cfg.d_key), cos, sin))[0]  # noqa: E731
             row["S1"] = heads(a.q1) @ heads(a.k1).transpose(-1, -2) / cfg.d_key ** 0.5
             if hasattr(a, "q2"):
                 row["S2"] = heads(a.q2) @ heads(a.k2).transpose(-1, -2) / cfg.d_key ** 0.5

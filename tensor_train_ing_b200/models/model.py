@@ -1,19 +1,21 @@
 """Tensor-network language model: bilinear MLP + polynomial (softmax-free) attention, and the
 SwiGLU + softmax control.
 
-The module tree and state-dict names are the reference's (tnlm/model.py:16-259):
-``embed``, ``blocks.{i}.attn.{q1,k1,q2,k2,v,o}``, ``blocks.{i}.{attn_in,attn_out,mlp_in,mlp_out}``,
-``blocks.{i}.mlp.{l,r,d}``, ``final_norm``, ``unembed`` -- so reference checkpoints load as is.
+Fixed by compatibility with the reference (tnlm/model.py:16-259), and tested bit for bit on CPU:
+the module tree and state-dict names (``embed``, ``blocks.{i}.attn.{q1,k1,q2,k2,v,o}``,
+``blocks.{i}.{attn_in,attn_out,mlp_in,mlp_out}``, ``blocks.{i}.mlp.{l,r,d}``, ``final_norm``,
+``unembed``), the order in which modules are built and weights drawn (so a seed gives the same
+weights), and the order of the forward's operations (so gradients sum in the same order).
 
 Two execution paths share the parameters:
-  * the *reference* path: plain PyTorch math (``models.attention``) -- the oracle, and the CPU path;
-  * the *fused* path (CUDA tensors, ``attention_backend`` in auto/cuda/triton): every hot op runs on
-    the hand-written sm_100a kernels of ``tensor_train_ing_b200.ops`` -- RMSNorm producing bf16,
-    one QKV GEMM with a RoPE epilogue, tcgen05 polynomial attention, output GEMM with a fused
-    residual add, dual-B bilinear GEMM, down GEMM with fused residual, fused chunked linear-CE.
-    The residual stream stays fp32 as under the reference's bf16 autocast with fp32 parameters.
+  * the module path (plain PyTorch math of ``models.attention``): the oracle and the CPU path;
+  * the fused path (CUDA tensors, ``attention_backend`` auto/cuda/triton): every hot op runs on the
+    sm_100a kernels of ``tensor_train_ing_b200.ops`` (``ops/block.py`` drives it).  The residual
+    stream stays fp32 as under the reference's bf16 autocast with fp32 parameters.
 """
 from __future__ import annotations
+
+import warnings
 
 import torch
 import torch.nn as nn
@@ -21,8 +23,8 @@ import torch.nn.functional as F
 
 from ..config import ModelConfig
 from .attention import (apply_rope, doc_positions, polynomial_attention, rope_tables, row_scale_mask,
-                        row_scale_vector, softmax_attention, softmax_attention_flex, visible_mask)
-from .normalization import GroupRMSNorm, LaggedRMS, RMSNorm, SpectralLinear, TaperRMS, make_norm
+                        softmax_attention, softmax_attention_flex, visible_mask)
+from .normalization import SpectralLinear, make_norm
 
 # normalization package -> (input norm kind, output norm kind, spectral linears)
 PACKAGES = {
@@ -34,8 +36,11 @@ PACKAGES = {
     "lagged": ("lagged", None, False),
     "taper": ("taper", None, False),
 }
+# operator classes from least to most general: polynomial, normalised, general (softmax / SiLU)
 CLASS_ORDER = {"P": 0, "N": 1, "G": 2}
 ATTN_KIND_ID = {"signed_product": 0, "offset_square": 1, "lower_degree_mix": 2}
+# attention kind -> number of (query, key) pairs: S = S1 (one pair) or a polynomial of S1 and S2
+QK_PAIRS = {"softmax": 1, "offset_square": 1, "signed_product": 2, "lower_degree_mix": 2}
 
 
 def _linear(d_in, d_out, spectral, bias=False):
@@ -49,11 +54,10 @@ def linear_weight(lin: nn.Module) -> torch.Tensor:
 
 @torch.no_grad()
 def score_bound(q: torch.Tensor, k: torch.Tensor, d_key: int) -> torch.Tensor:
-    """Per-head Cauchy-Schwarz bound max|q| * max|k| / sqrt(dk) on |S| over a batch (never below
-    the true masked maximum; RoPE preserves norms).  q, k: (B, H, T, dk)."""
-    qn = q.detach().float().norm(dim=-1).amax(dim=(0, 2))
-    kn = k.detach().float().norm(dim=-1).amax(dim=(0, 2))
-    return qn * kn / d_key ** 0.5
+    """Per head, max_i |q_i| * max_j |k_j| / sqrt(dk): by Cauchy-Schwarz never below the largest
+    |S_ij| of the batch, whatever the mask (RoPE keeps norms).  q, k: (B, H, T, dk) -> (H,)."""
+    top = lambda t: t.detach().float().norm(dim=-1).amax(dim=(0, 2))  # noqa: E731
+    return top(q) * top(k) / d_key ** 0.5
 
 
 class Attention(nn.Module):
@@ -62,16 +66,16 @@ class Attention(nn.Module):
         self.cfg, self.kind = cfg, cfg.attention
         self.record_score_bound, self.last_score_bound = False, None
         H, dk, dv, d = cfg.heads, cfg.d_key, cfg.d_value, cfg.d_model
-        self.q1 = _linear(d, H * dk, spectral)
-        self.k1 = _linear(d, H * dk, spectral)
-        if self.kind in ("signed_product", "lower_degree_mix"):
-            self.q2 = _linear(d, H * dk, spectral)
-            self.k2 = _linear(d, H * dk, spectral)
+        pairs = QK_PAIRS[self.kind]
+        # built (and their spectral vectors drawn) in this order: q1, k1, [q2, k2], v, o
+        for i in range(1, pairs + 1):
+            setattr(self, f"q{i}", _linear(d, H * dk, spectral))
+            setattr(self, f"k{i}", _linear(d, H * dk, spectral))
         self.v = _linear(d, H * dv, spectral)
         self.o = _linear(H * dv, d, spectral)
         if self.kind == "offset_square":
             self.b = nn.Parameter(torch.full((H,), cfg.offset_square_b))
-        if self.kind == "lower_degree_mix":
+        elif self.kind == "lower_degree_mix":  # (c0, c1, c2, c12): starts as the signed product S1 S2
             self.coef = nn.Parameter(torch.tensor([[0.0, 0.0, 0.0, 1.0]]).repeat(H, 1))
         default_power = 1.0 if self.kind == "offset_square" else 0.5
         self.row_power = default_power if cfg.attn_row_power is None else cfg.attn_row_power
@@ -80,48 +84,50 @@ class Attention(nn.Module):
     def op_class(self):
         return "G" if self.kind == "softmax" else "P"
 
+    def qk_pairs(self) -> list[tuple[nn.Module, nn.Module]]:
+        return [(getattr(self, f"q{i}"), getattr(self, f"k{i}")) for i in range(1, QK_PAIRS[self.kind] + 1)]
+
     def projections(self):
         """Linear layers whose outputs form the fused QKV buffer, in buffer order."""
-        names = ["q1", "k1"] + (["q2", "k2"] if hasattr(self, "q2") else []) + ["v"]
-        return [getattr(self, n) for n in names]
+        return [lin for pair in self.qk_pairs() for lin in pair] + [self.v]
 
-    def _heads(self, x, lin, dh):
+    def _split_heads(self, x, lin, dh):
         B, T, _ = x.shape
         return lin(x).view(B, T, self.cfg.heads, dh).transpose(1, 2)
 
+    def _mix_polynomial(self, x, ctx, q1, k1, q2, k2, v):
+        cfg = self.cfg
+        if self.record_score_bound:
+            self.last_score_bound = {name: score_bound(q, k, cfg.d_key)
+                                     for name, q, k in (("S1", q1, k1), ("S2", q2, k2)) if q is not None}
+        if cfg.fp32_scores:  # at least fp32 (an fp64 oracle stays fp64)
+            widen = lambda t: None if t is None else t.to(torch.promote_types(t.dtype, torch.float32))  # noqa: E731
+            q1, k1, q2, k2, v = (widen(t) for t in (q1, k1, q2, k2, v))
+        with torch.autocast(x.device.type, enabled=False):
+            y = polynomial_attention(self.kind, q1, k1, q2, k2, v, ctx["C"][self.row_power],
+                                     coef=getattr(self, "coef", None), b=getattr(self, "b", None))
+        return y.to(x.dtype)
+
     def forward(self, x, ctx):
-        """Reference path (dense oracle math, or FlexAttention for the softmax control)."""
+        """Module path: dense polynomial attention, or SDPA / FlexAttention for the softmax control."""
         cfg = self.cfg
         cos, sin = ctx["rope"]
-        q1 = apply_rope(self._heads(x, self.q1, cfg.d_key), cos, sin)
-        k1 = apply_rope(self._heads(x, self.k1, cfg.d_key), cos, sin)
-        v = self._heads(x, self.v, cfg.d_value)
+        rotated = lambda lin: apply_rope(self._split_heads(x, lin, cfg.d_key), cos, sin)  # noqa: E731
+        q1, k1 = rotated(self.q1), rotated(self.k1)
+        v = self._split_heads(x, self.v, cfg.d_value)
         if self.kind == "softmax":
-            if ctx["backend"] == "flex":
-                y = softmax_attention_flex(q1, k1, v, ctx["doc_ids"])
-            else:
-                y = softmax_attention(q1, k1, v, ctx["visible"])
+            y = (softmax_attention_flex(q1, k1, v, ctx["doc_ids"]) if ctx["backend"] == "flex"
+                 else softmax_attention(q1, k1, v, ctx["visible"]))
         else:
-            q2 = k2 = None
-            if hasattr(self, "q2"):
-                q2 = apply_rope(self._heads(x, self.q2, cfg.d_key), cos, sin)
-                k2 = apply_rope(self._heads(x, self.k2, cfg.d_key), cos, sin)
-            if self.record_score_bound:
-                self.last_score_bound = {name: score_bound(q, k, cfg.d_key)
-                                         for name, q, k in (("S1", q1, k1), ("S2", q2, k2)) if q is not None}
-            if cfg.fp32_scores:
-                up = lambda t: None if t is None else t.to(torch.promote_types(t.dtype, torch.float32))
-                q1, k1, q2, k2, v = map(up, (q1, k1, q2, k2, v))
-            C = ctx["C"][self.row_power]
-            with torch.autocast(x.device.type, enabled=False):
-                y = polynomial_attention(self.kind, q1, k1, q2, k2, v, C,
-                                         coef=getattr(self, "coef", None), b=getattr(self, "b", None))
-            y = y.to(x.dtype)
+            q2, k2 = (rotated(self.q2), rotated(self.k2)) if QK_PAIRS[self.kind] == 2 else (None, None)
+            y = self._mix_polynomial(x, ctx, q1, k1, q2, k2, v)
         B, H, T, dv = y.shape
         return self.o(y.transpose(1, 2).reshape(B, T, H * dv))
 
 
 class MLP(nn.Module):
+    """``d(l(x) * r(x))``: bilinear (optionally with biases) or, for the control, SwiGLU."""
+
     def __init__(self, cfg: ModelConfig, spectral: bool):
         super().__init__()
         self.kind = cfg.mlp
@@ -135,12 +141,16 @@ class MLP(nn.Module):
         return "G" if self.kind == "swiglu" else "P"
 
     def forward(self, x):
+        gate = self.l(x)
         if self.kind == "swiglu":
-            return self.d(F.silu(self.l(x)) * self.r(x))
-        return self.d(self.l(x) * self.r(x))
+            gate = F.silu(gate)
+        return self.d(gate * self.r(x))
 
 
 class Block(nn.Module):
+    """Two residual branches, ``x + alpha * out_norm(branch(in_norm(x)))``, for attention then MLP;
+    ``ablate`` (analysis only) removes whole branches."""
+
     def __init__(self, cfg: ModelConfig):
         super().__init__()
         nin, nout, spectral = PACKAGES[cfg.normalization]
@@ -148,10 +158,13 @@ class Block(nn.Module):
         if cfg.depth_residual_base:
             self.alpha *= (cfg.depth_residual_base / cfg.layers) ** cfg.depth_residual_exponent
         self.attn, self.mlp = Attention(cfg, spectral), MLP(cfg, spectral)
-        mk = lambda kind: make_norm(kind, cfg.d_model, cfg) if kind else nn.Identity()
-        self.attn_in, self.attn_out = mk(nin), mk(nout)
-        self.mlp_in, self.mlp_out = mk(nin), mk(nout)
+        norm = lambda kind: make_norm(kind, cfg.d_model, cfg) if kind else nn.Identity()  # noqa: E731
+        self.attn_in, self.attn_out = norm(nin), norm(nout)
+        self.mlp_in, self.mlp_out = norm(nin), norm(nout)
         self.ablate: frozenset = frozenset()
+
+    def _residual(self, x, norm_in, branch, norm_out):
+        return x + self.alpha * norm_out(branch(norm_in(x)))
 
     def forward(self, x, ctx):
         if self.ablate and self.training:
@@ -160,15 +173,15 @@ class Block(nn.Module):
             from ..ops.block import block_forward
             return block_forward(self, x, ctx)
         if "attn" not in self.ablate:
-            x = x + self.alpha * self.attn_out(self.attn(self.attn_in(x), ctx))
+            x = self._residual(x, self.attn_in, lambda h: self.attn(h, ctx), self.attn_out)
         if "mlp" not in self.ablate:
-            x = x + self.alpha * self.mlp_out(self.mlp(self.mlp_in(x)))
+            x = self._residual(x, self.mlp_in, self.mlp, self.mlp_out)
         return x
 
 
-# Initialisation of each top-level component, in the order TensorLM.reset_parameters draws them
-# (reference tnlm/model.py reset_parameters).  Kept per component so that a sharded model can stream
-# the serial initialisation one component at a time (models/init_stream.py).
+# Initialisation, one top-level component at a time in the draw order of the whole model (embedding,
+# blocks in order, unembedding), so that a parameter-sharded model can stream the serial
+# initialisation component by component (models/init_stream.py).
 @torch.no_grad()
 def init_embedding(embed: nn.Module):
     nn.init.normal_(embed.weight, std=1.0)
@@ -176,11 +189,14 @@ def init_embedding(embed: nn.Module):
 
 @torch.no_grad()
 def init_block(blk: nn.Module, cfg: ModelConfig):
+    """Inputs maps (Q, K, V, L, R): std fan_in^-1/2, queries and keys then times ``qk_init_scale``;
+    output maps (O, D): std (2 depth fan_in)^-1/2; biases 0; spectral gains = sigma(W)."""
     a, m = blk.attn, blk.mlp
-    for lin in [a.q1, a.k1, a.v, m.l, m.r] + ([a.q2, a.k2] if hasattr(a, "q2") else []):
+    extra_qk = [a.q2, a.k2] if QK_PAIRS[a.kind] == 2 else []
+    for lin in [a.q1, a.k1, a.v, m.l, m.r] + extra_qk:  # the draw order
         nn.init.normal_(lin.weight, std=lin.weight.shape[1] ** -0.5)
-    if cfg.qk_init_scale != 1.0:
-        for lin in [a.q1, a.k1] + ([a.q2, a.k2] if hasattr(a, "q2") else []):
+    if cfg.qk_init_scale != 1.0:  # scores scale by s^2 per factor
+        for lin in [a.q1, a.k1] + extra_qk:
             lin.weight.mul_(cfg.qk_init_scale)
     depth = cfg.depth_residual_base or cfg.layers
     for lin in (a.o, m.d):
@@ -197,6 +213,16 @@ def init_unembedding(unembed: nn.Module):
     nn.init.normal_(unembed.weight, std=0.02)
 
 
+def operator_classes(model: nn.Module) -> dict:
+    """Every module that declares an operator class, by name (the root is "<root>")."""
+    out = {}
+    for name, mod in model.named_modules():
+        cls = getattr(mod, "op_class", None)
+        if isinstance(cls, str):
+            out[name or "<root>"] = cls
+    return out
+
+
 class TensorLM(nn.Module):
     def __init__(self, cfg: ModelConfig):
         super().__init__()
@@ -211,9 +237,6 @@ class TensorLM(nn.Module):
 
     @torch.no_grad()
     def reset_parameters(self):
-        """Fan-in init: embed N(0,1); Q/K/V/L/R std fan_in^-1/2 (Q/K times qk_init_scale);
-        O/D std (2*depth*fan_in)^-1/2; unembed 0.02; biases 0; spectral gamma = sigma(W).
-        The draw order matches the reference so a seed gives identical weights."""
         init_embedding(self.embed)
         for blk in self.blocks:
             init_block(blk, self.cfg)
@@ -227,25 +250,28 @@ class TensorLM(nn.Module):
 
     # ---------------------------------------------------------------- structure reports
     def operator_audit(self) -> dict:
-        classes = {}
-        for name, mod in self.named_modules():
-            c = getattr(mod, "op_class", None)
-            if isinstance(c, str):
-                classes[name or "<root>"] = c
-        overall = max(classes.values(), key=CLASS_ORDER.get) if classes else "P"
-        return {"class": overall, "nodes": classes}
+        """The model's operator class is its most general node's ("P" < "N" < "G")."""
+        nodes = operator_classes(self)
+        worst = max(nodes.values(), key=lambda c: CLASS_ORDER[c], default="P")
+        return {"class": worst, "nodes": nodes}
 
     def param_counts(self) -> dict:
-        matrices = sum(p.numel() for _, p in self.named_parameters() if p.dim() >= 2)
-        total = sum(p.numel() for p in self.parameters())
-        emb = self.embed.weight.numel() + (0 if self.cfg.tie_embeddings else self.unembed.weight.numel())
-        return {"total": total, "matrices": matrices, "non_embedding_matrices": matrices - emb,
-                "small": total - matrices}
+        sizes = {"total": 0, "matrices": 0}
+        for p in self.parameters():  # tied weights once
+            sizes["total"] += p.numel()
+        for _, p in self.named_parameters():
+            if p.dim() >= 2:
+                sizes["matrices"] += p.numel()
+        vocab = self.embed.weight.numel() + (0 if self.cfg.tie_embeddings else self.unembed.weight.numel())
+        return {**sizes, "non_embedding_matrices": sizes["matrices"] - vocab,
+                "small": sizes["total"] - sizes["matrices"]}
 
-    # ---------------------------------------------------------------- forward
+    # ---------------------------------------------------------------- execution path
     def _row_powers(self) -> tuple:
-        extra = {self.cfg.attn_row_power} if self.cfg.attn_row_power is not None else set()
-        return tuple(sorted({0.5, 1.0} | extra))
+        powers = {0.5, 1.0}
+        if self.cfg.attn_row_power is not None:
+            powers.add(self.cfg.attn_row_power)
+        return tuple(sorted(powers))
 
     def fused_path_supported(self) -> tuple[bool, str]:
         """Shapes the sm_100a kernels cover: head dims 64/128, TMA-aligned widths, d_model <= 8192."""
@@ -260,25 +286,24 @@ class TensorLM(nn.Module):
 
     def uses_fused_path(self, idx: torch.Tensor) -> bool:
         backend = self.cfg.attention_backend
-        if getattr(self, "_force_reference", False):  # analysis hooks need the module-level path
+        if getattr(self, "_force_reference", False):  # module hooks (analysis, calibration) need the module path
             return False
         if not (idx.is_cuda and backend in ("auto", "cuda", "triton")):
             return False
         ok, why = self.fused_path_supported()
-        if not ok:
-            if backend != "auto":
-                raise ValueError(f"attention_backend={backend!r} needs the fused kernels, which do not cover: {why}")
-            if not getattr(self, "_warned_fused", False):
-                import warnings
-                warnings.warn(f"TensorLM: using the PyTorch reference path ({why})")
-                self._warned_fused = True
-            return False
-        return True
+        if ok:
+            return True
+        if backend != "auto":
+            raise ValueError(f"attention_backend={backend!r} needs the fused kernels, which do not cover: {why}")
+        if not getattr(self, "_warned_fused", False):
+            warnings.warn(f"TensorLM: using the PyTorch module path ({why})")
+            self._warned_fused = True
+        return False
 
     def make_ctx(self, idx, doc_ids):
-        B, T = idx.shape
+        """Per-batch tables: document positions, RoPE, and the backend's masks or row scales."""
         if doc_ids is None:
-            doc_ids = torch.zeros(B, T, dtype=torch.long, device=idx.device)
+            doc_ids = torch.zeros(idx.shape, dtype=torch.long, device=idx.device)
         pos = doc_positions(doc_ids)
         ctx = {"doc_ids": doc_ids}
         if self.uses_fused_path(idx):
@@ -292,44 +317,51 @@ class TensorLM(nn.Module):
         if self.cfg.attention == "softmax":
             backend = "flex" if backend in ("triton", "cuda") else "softmax"
         ctx["backend"] = backend
-        if backend != "flex":
-            vis = visible_mask(doc_ids)
-            ctx["visible"] = vis
+        if backend != "flex":  # the dense paths; FlexAttention builds its own block mask
+            ctx["visible"] = visible_mask(doc_ids)
             if self.cfg.attention != "softmax":
-                ctx["C"] = {p: row_scale_mask(vis, p) for p in self._row_powers()}
+                ctx["C"] = {p: row_scale_mask(ctx["visible"], p) for p in self._row_powers()}
         return ctx
 
+    # ---------------------------------------------------------------- forward (module path)
+    def _trunk(self, idx, ctx):
+        x = self.embed(idx)
+        recompute = self.cfg.activation_checkpointing and self.training and torch.is_grad_enabled()
+        for blk in self.blocks:
+            x = torch.utils.checkpoint.checkpoint(blk, x, ctx, use_reentrant=False) if recompute else blk(x, ctx)
+        return self.final_norm(x)
+
+    def _loss(self, x, targets):
+        """(logits or None, summed cross-entropy) over the real vocabulary (padded rows never score)."""
+        V = self.cfg.vocab_size
+        scaled = self.cfg.width_scaling_base
+        if self.cfg.loss_chunk_tokens > 0:
+            from ..ops.linear_ce import chunked_linear_cross_entropy_reference
+            w = self.unembed.weight[:V]
+            if scaled:
+                w = w * self.logit_multiplier
+            return None, chunked_linear_cross_entropy_reference(x.flatten(0, 1), w, targets.flatten(),
+                                                                self.cfg.loss_chunk_tokens)
+        logits = self.unembed(x)[..., :V]
+        if scaled:
+            logits = logits * self.logit_multiplier
+        wide = logits.to(torch.promote_types(logits.dtype, torch.float32))
+        return logits, F.cross_entropy(wide.flatten(0, 1), targets.flatten(), ignore_index=-100, reduction="sum")
+
     def forward(self, idx, doc_ids=None, targets=None, reduction="mean"):
+        """Logits (no targets), else (logits or None, loss sum, valid targets) for ``reduction="sum"``
+        or (logits or None, mean loss)."""
         ctx = self.make_ctx(idx, doc_ids)
         if ctx.get("fused"):
             from ..ops.block import model_forward
             return model_forward(self, idx, ctx, targets, reduction)
         if getattr(self, "_ttb_weights_remote", False):
             raise RuntimeError("this parameter-sharded model holds non-owned weights only as the fused path's bf16 "
-                               "caches; the PyTorch reference path cannot run it")
-        x = self.embed(idx)
-        ckpt = self.cfg.activation_checkpointing and self.training and torch.is_grad_enabled()
-        for blk in self.blocks:
-            x = torch.utils.checkpoint.checkpoint(blk, x, ctx, use_reentrant=False) if ckpt else blk(x, ctx)
-        x = self.final_norm(x)
-        V = self.cfg.vocab_size
-        if targets is not None and self.cfg.loss_chunk_tokens > 0:
-            from ..ops.linear_ce import chunked_linear_cross_entropy_reference
-            w = self.unembed.weight[:V]
-            if self.cfg.width_scaling_base:
-                w = w * self.logit_multiplier
-            loss = chunked_linear_cross_entropy_reference(x.flatten(0, 1), w, targets.flatten(),
-                                                          self.cfg.loss_chunk_tokens)
-            logits = None
-        else:
-            logits = self.unembed(x)[..., :V]
-            if self.cfg.width_scaling_base:
-                logits = logits * self.logit_multiplier
-            if targets is None:
-                return logits
-            loss = F.cross_entropy(logits.to(torch.promote_types(logits.dtype, torch.float32)).flatten(0, 1),
-                                   targets.flatten(), ignore_index=-100, reduction="sum")
+                               "caches; the module path cannot run it")
+        x = self._trunk(idx, ctx)
+        if targets is None:
+            logits = self.unembed(x)[..., :self.cfg.vocab_size]
+            return logits * self.logit_multiplier if self.cfg.width_scaling_base else logits
+        logits, loss = self._loss(x, targets)
         n = (targets != -100).sum()
-        if reduction == "sum":
-            return logits, loss, n
-        return logits, loss / n.clamp_min(1)
+        return (logits, loss, n) if reduction == "sum" else (logits, loss / n.clamp_min(1))
