@@ -7,6 +7,12 @@ loss-normalization contract (every rank back-propagates ``local_sum / global_val
 sums gradients across ranks (one reduce-scatter onto the owning ranks), clips the global norm,
 steps the optimizer on the owned parameters and all-gathers the updated parameters.  It returns
 the step's summed loss and valid-target count as device tensors (no host synchronisation).
+
+``step`` is built on three primitives that trainers with their own batching use directly:
+``begin_update`` (zero the gradients), ``forward_loss`` / ``backward`` per micro-batch, and
+``finish_update``, which can divide the accumulated gradients by the update's target count
+afterwards (the serial trainer's contract: sum the micro-batch losses, then divide) instead of
+scaling each micro-batch's loss beforehand.
 """
 from __future__ import annotations
 
@@ -54,6 +60,8 @@ class TrainEngine:
         if optimizer is None:
             only = self.dp.owned_ids() if self.dp is not None and (self.world > 1 or self.shard_params) else None
             optimizer = make_optimizer(self.model, cfg.train, only=only)
+        elif callable(optimizer) and not isinstance(optimizer, torch.optim.Optimizer):
+            optimizer = optimizer(self.model)  # built after the parameters moved into the flat buffers
         self.optimizer = optimizer
         self.last_grad_norm = None
         # optional per-phase device timing: a list that receives, per step, the (phase, CUDA event) pairs
@@ -77,17 +85,67 @@ class TrainEngine:
         else:
             self.optimizer.zero_grad(set_to_none=True)
 
+    # ------------------------------------------------------------------ primitives
+    def begin_update(self):
+        self.zero_grad()
+
+    def forward_loss(self, idx, doc_ids, targets):
+        """One micro-batch's forward: (summed loss, valid-target count) on the device."""
+        i, d, t = (self._to_device(x) for x in (idx, doc_ids, targets))
+        _, loss, n = self.model(i, d, t, reduction="sum")
+        return loss, n
+
+    def backward(self, objective):
+        objective.backward()
+        if self.dp is not None:
+            self.dp.after_backward()
+
+    def _clip(self, error_if_nonfinite: bool):
+        """Clip norm and, for optimizers that apply it while reading gradients, the coefficient."""
+        if not (self.grad_clip and self.grad_clip > 0):
+            return None, None
+        if self.dp is not None and getattr(self.optimizer, "accepts_grad_scale", False):
+            norm, scale = self.dp.clip_coefficient(self.grad_clip)
+        elif self.dp is not None:
+            norm, scale = self.dp.clip_(self.grad_clip), None
+        else:
+            params = (self.model.parameters() if error_if_nonfinite
+                      else [p for p in self.model.parameters() if p.grad is not None])
+            return torch.nn.utils.clip_grad_norm_(params, self.grad_clip, error_if_nonfinite=error_if_nonfinite,
+                                                  foreach=None if error_if_nonfinite else True), None
+        if error_if_nonfinite and not bool(torch.isfinite(norm)):
+            raise RuntimeError(f"The total norm of gradients is non-finite ({float(norm)}), so it cannot be clipped")
+        return norm, scale
+
+    def finish_update(self, *, divide_by: float | None = None, error_if_nonfinite: bool = False, marks=None):
+        """Sum gradients across ranks, divide them by ``divide_by`` if given, clip, step the optimizer
+        and bring every rank the updated parameters.  Returns the pre-clip gradient norm."""
+        if self.dp is not None:
+            self.dp.reduce_gradients()
+        self._mark(marks, "reduce_gradients")
+        if divide_by is not None:
+            grads = [p.grad for p in self.model.parameters() if p.grad is not None]
+            torch._foreach_div_(grads, float(divide_by))
+        self.last_grad_norm, scale = self._clip(error_if_nonfinite)
+        self._mark(marks, "clip")
+        if scale is not None:
+            self.optimizer.step(grad_scale=scale)
+        else:
+            self.optimizer.step()
+        self._mark(marks, "optimizer")
+        if self.dp is not None:
+            self.dp.gather_params()
+        self._mark(marks, "gather_params")
+        return self.last_grad_norm
+
     def forward_backward(self, idx, doc_ids, targets, inv_count):
         """Accumulate gradients of sum(loss) * inv_count over micro-batches; returns the loss sum."""
         loss_total = torch.zeros((), device=self.device, dtype=torch.float32)
         rows = idx.shape[0]
         for s in range(0, rows, self.micro_batch):
             e = min(rows, s + self.micro_batch)
-            i, d, t = (self._to_device(x[s:e]) for x in (idx, doc_ids, targets))
-            _, loss, _ = self.model(i, d, t, reduction="sum")
-            (loss * inv_count).backward()
-            if self.dp is not None:
-                self.dp.after_backward()
+            loss, _ = self.forward_loss(idx[s:e], doc_ids[s:e], targets[s:e])
+            self.backward(loss * inv_count)
             loss_total += loss.detach().float()
         return loss_total
 
@@ -98,7 +156,7 @@ class TrainEngine:
                 g["lr"] = g.get("base_lr", g["lr"]) * lr_multiplier
         marks = [] if self.phase_events is not None and self.device.type == "cuda" else None
         self._mark(marks, "start")
-        self.zero_grad()
+        self.begin_update()
         # valid-target count: counted on the host side of the copy, summed over ranks on the device
         local = (targets != -100).sum()
         count = local.to(self.device, non_blocking=True).to(torch.int64)
@@ -107,30 +165,9 @@ class TrainEngine:
         inv = 1.0 / count.clamp_min(1).to(torch.float32)
         loss_sum = self.forward_backward(idx, doc_ids, targets, inv)
         self._mark(marks, "forward_backward")
-        if self.dp is not None:
-            self.dp.reduce_gradients()
         if self.world > 1:
             dist.all_reduce(loss_sum, group=self.group)
-        self._mark(marks, "reduce_gradients")
-        scale = None
-        if self.grad_clip and self.grad_clip > 0:
-            if self.dp is not None and getattr(self.optimizer, "accepts_grad_scale", False):
-                # the optimizer kernels multiply each gradient by the coefficient as they read it
-                self.last_grad_norm, scale = self.dp.clip_coefficient(self.grad_clip)
-            elif self.dp is not None:
-                self.last_grad_norm = self.dp.clip_(self.grad_clip)
-            else:
-                params = [p for p in self.model.parameters() if p.grad is not None]
-                self.last_grad_norm = torch.nn.utils.clip_grad_norm_(params, self.grad_clip, foreach=True)
-        self._mark(marks, "clip")
-        if scale is not None:
-            self.optimizer.step(grad_scale=scale)
-        else:
-            self.optimizer.step()
-        self._mark(marks, "optimizer")
-        if self.dp is not None:
-            self.dp.gather_params()
-        self._mark(marks, "gather_params")
+        self.finish_update(marks=marks)
         if marks is not None:
             self.phase_events.append(marks)
         return loss_sum, count
