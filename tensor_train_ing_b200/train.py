@@ -430,6 +430,15 @@ def train_run(cfg, run_dir, *, max_steps, max_seconds, device="cuda", resume=Non
             ledger.finish(run_id, time.monotonic() - started, status)
 
 
+def _check_tokenizer(tokenizer: dict, named, dev):
+    """The manifest's tokenizer must be the configured one (by name or fingerprint); test-only
+    tokenizers (fixtures without a fingerprint) train on the CPU only."""
+    if tokenizer.get("test_only") and dev.type != "cpu":
+        raise ValueError("test-only tokenizer manifests are restricted to CPU fixtures")
+    if named is not None and named not in (tokenizer["name"], tokenizer.get("fingerprint_sha256")):
+        raise ValueError("configured tokenizer does not match immutable manifest")
+
+
 def _assert_no_analysis_state(model):
     for name, module in model.named_modules():
         if getattr(module, "ablate", frozenset()):
@@ -470,11 +479,7 @@ class _Run:
                                      seed=self.cfg.train.seed)
         self.manifest_hash = manifest_hash(self.data["manifest"])
         self.tokenizer = self.sampler.manifest["tokenizer"]
-        if self.tokenizer.get("test_only") and self.dev.type != "cpu":
-            raise ValueError("test-only tokenizer manifests are restricted to CPU fixtures")
-        named = self.data.get("tokenizer")
-        if named is not None and named not in (self.tokenizer["name"], self.tokenizer.get("fingerprint_sha256")):
-            raise ValueError("configured tokenizer does not match immutable manifest")
+        _check_tokenizer(self.tokenizer, self.data.get("tokenizer"), self.dev)
 
     def _build_model(self):
         seed_all(self.cfg.train.seed)
