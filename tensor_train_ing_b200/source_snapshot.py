@@ -1,13 +1,18 @@
-"""Freeze the package (Python sources, CUDA sources and the built kernel library) plus run inputs
-into a read-only snapshot, and run CLI commands from it in an isolated interpreter (reference
-tnlm/source_snapshot.py:38-256).
+"""Frozen source snapshots: a read-only, checksummed copy of the package (Python sources, CUDA
+sources and the built kernel library) plus the run's input files, and a runner that executes CLI
+commands from that copy in an isolated interpreter.  A long sweep started from a snapshot is not
+affected by later edits of the working tree or of its config files.  Same capabilities and
+manifest format as the reference (tnlm/source_snapshot.py:38-256).
 
-``create_snapshot`` copies every regular file of ``tensor_train_ing_b200/`` (``__pycache__``
-excluded; symbolic links refused) and the given input files, re-checks the sources after copying,
-writes ``manifest.json`` (sha256 and size of every file) last as the completion marker and makes
-the tree read-only.  ``run_snapshot`` verifies the inventory, rewrites ``--config`` /
-``--candidates`` to the captured copies and runs ``python -I -B`` on the snapshot's package in its
-own process group, forwarding SIGINT/SIGTERM.
+A snapshot is assembled in a staging directory beside its destination: every regular file of the
+package (``__pycache__`` skipped, symbolic links refused) and each input under
+``inputs/<i>-<name>``; the sources are read a second time to catch edits made meanwhile;
+``manifest.json`` (sha256 and size of every file, the input mapping, source root and working
+directory) goes in last; the tree is made read-only and renamed into place, so a snapshot either
+exists complete or not at all.  Running one re-verifies the inventory, points ``--config`` and
+``--candidates`` at the captured copies (other values are refused) and supervises ``python -I -B``
+on the snapshot's package in its own process group, forwarding SIGINT/SIGTERM and killing the group
+if it outlives a grace period.
 
     python -m tensor_train_ing_b200.source_snapshot create --source REPO --out DIR [--input FILE ...]
     python -m tensor_train_ing_b200.source_snapshot verify DIR
@@ -23,228 +28,262 @@ import shutil
 import signal
 import subprocess
 import sys
+import tempfile
 import threading
 import time
 from pathlib import Path
 
+from .durable import fsync_dir, publish_dir
+
 PACKAGE = "tensor_train_ing_b200"
-_REQUIRED = {f"{PACKAGE}/__init__.py", f"{PACKAGE}/cli.py"}
+MANIFEST = "manifest.json"
+_REQUIRED = frozenset({f"{PACKAGE}/__init__.py", f"{PACKAGE}/cli.py"})
+_PINNED_FLAGS = ("--config", "--candidates")
 
 
-def _record(payload: bytes) -> dict:
-    return {"sha256": hashlib.sha256(payload).hexdigest(), "bytes": len(payload)}
+def _entry(blob: bytes) -> dict:
+    return {"sha256": hashlib.sha256(blob).hexdigest(), "bytes": len(blob)}
 
 
-def _source_files(root: Path) -> dict:
+# ====================================================================================== capture
+def _package_files(root: Path) -> dict[str, bytes]:
+    """Relative path -> contents of every regular file in the package (no caches, no links)."""
     pkg = root / PACKAGE
     if pkg.is_symlink() or not pkg.is_dir():
         raise ValueError(f"source must contain a regular {PACKAGE} directory")
-    out = {}
+    files = {}
     for path in sorted(pkg.rglob("*")):
         if path.is_symlink():
             raise ValueError(f"source symlink forbidden: {path}")
-        if "__pycache__" in path.parts or path.suffix == ".pyc":
-            continue
-        if path.is_file():
-            out[path.relative_to(root).as_posix()] = path.read_bytes()
-    if not _REQUIRED <= out.keys():
+        if path.is_file() and "__pycache__" not in path.parts and path.suffix != ".pyc":
+            files[path.relative_to(root).as_posix()] = path.read_bytes()
+    if not _REQUIRED <= files.keys():
         raise ValueError(f"source requires {sorted(_REQUIRED)}")
-    return out
+    return files
 
 
-def _fsync_dir(path):
-    fd = os.open(path, os.O_RDONLY)
-    try:
-        os.fsync(fd)
-    finally:
-        os.close(fd)
+def _input_files(root: Path, inputs) -> tuple[dict[str, str], dict[str, bytes]]:
+    """(absolute path -> snapshot-relative name, absolute path -> contents) of the run inputs."""
+    names, blobs = {}, {}
+    for i, given in enumerate(inputs):
+        path = Path(given) if Path(given).is_absolute() else root / given
+        if path.is_symlink() or not path.is_file():
+            raise ValueError(f"input must be a regular file: {path}")
+        key = str(path.resolve())
+        if key in names:
+            raise ValueError(f"duplicate input: {key}")
+        names[key] = f"inputs/{i}-{Path(key).name}"
+        blobs[key] = Path(key).read_bytes()
+    return names, blobs
+
+
+def _set_tree_mode(top: Path, *, writable: bool):
+    for path in sorted(top.rglob("*"), reverse=True):
+        if path.is_symlink():
+            continue
+        if path.is_dir():
+            path.chmod(0o755 if writable else 0o555)
+        else:
+            path.chmod(0o644 if writable else (0o555 if path.suffix == ".so" else 0o444))
+    top.chmod(0o755 if writable else 0o555)
 
 
 def create_snapshot(source_root, destination, inputs=(), *, workdir=None) -> dict:
+    """Capture the package under ``source_root`` and ``inputs`` into ``destination`` (which must
+    not exist); returns the manifest."""
     root = Path(source_root).resolve()
     dest = Path(destination).absolute()
     if dest.exists() or dest.is_symlink():
         raise FileExistsError(dest)
     if dest.resolve().is_relative_to(root / PACKAGE):
         raise ValueError("snapshot cannot be inside the source package")
-    wd = Path(workdir).resolve() if workdir is not None else root
-    if not wd.is_dir() or wd.is_relative_to(dest.resolve()):
+    cwd = Path(workdir).resolve() if workdir is not None else root
+    if not cwd.is_dir() or cwd.is_relative_to(dest.resolve()):
         raise ValueError("working directory must exist outside the snapshot")
-    payloads = _source_files(root)
-    input_paths, input_payloads = {}, {}
-    for i, value in enumerate(inputs):
-        p = Path(value)
-        if not p.is_absolute():
-            p = root / p
-        if p.is_symlink() or not p.is_file():
-            raise ValueError(f"input must be a regular file: {p}")
-        p = p.resolve()
-        if str(p) in input_paths:
-            raise ValueError(f"duplicate input: {p}")
-        rel = f"inputs/{i}-{p.name}"
-        input_paths[str(p)] = rel
-        input_payloads[str(p)] = payloads[rel] = p.read_bytes()
-    manifest = {"version": 1, "package": PACKAGE, "source_root": str(root), "working_directory": str(wd),
-                "input_paths": input_paths, "files": {n: _record(b) for n, b in payloads.items()}}
+    package = _package_files(root)
+    names, blobs = _input_files(root, inputs)
+    contents = {**package, **{names[k]: blob for k, blob in blobs.items()}}
+    manifest = {"version": 1, "package": PACKAGE, "source_root": str(root), "working_directory": str(cwd),
+                "input_paths": names, "files": {name: _entry(blob) for name, blob in contents.items()}}
     dest.parent.mkdir(parents=True, exist_ok=True)
-    dest.mkdir()
+    staging = Path(tempfile.mkdtemp(prefix=f".{dest.name}.staging-", dir=dest.parent))
     try:
-        for name, payload in payloads.items():
-            p = dest / name
-            p.parent.mkdir(parents=True, exist_ok=True)
-            with p.open("xb") as fh:
-                fh.write(payload)
+        for name, blob in contents.items():
+            target = staging / name
+            target.parent.mkdir(parents=True, exist_ok=True)
+            with target.open("xb") as fh:
+                fh.write(blob)
                 fh.flush()
                 os.fsync(fh.fileno())
-        if _source_files(root) != {k: v for k, v in payloads.items() if k.startswith(PACKAGE + "/")}:
+        if _package_files(root) != package:
             raise RuntimeError("source changed while creating snapshot")
-        if any(Path(n).is_symlink() or Path(n).read_bytes() != b for n, b in input_payloads.items()):
-            raise RuntimeError("input changed while creating snapshot")
-        tmp = dest / ".manifest.json.tmp"
-        with tmp.open("x") as fh:
-            json.dump(manifest, fh, sort_keys=True, indent=2)
-            fh.write("\n")
+        for key, blob in blobs.items():
+            if Path(key).is_symlink() or Path(key).read_bytes() != blob:
+                raise RuntimeError("input changed while creating snapshot")
+        with (staging / MANIFEST).open("x") as fh:
+            fh.write(json.dumps(manifest, sort_keys=True, indent=2) + "\n")
             fh.flush()
             os.fsync(fh.fileno())
-        tmp.rename(dest / "manifest.json")
-        for p in sorted(dest.rglob("*"), reverse=True):
-            p.chmod(0o555 if p.is_dir() else (0o555 if p.suffix == ".so" else 0o444))
-        dest.chmod(0o555)
-        for d in [p for p in dest.rglob("*") if p.is_dir()] + [dest, dest.parent]:
-            _fsync_dir(d)
-        verify_snapshot(dest)
+        for d in [p for p in staging.rglob("*") if p.is_dir()] + [staging]:
+            fsync_dir(d)
+        _set_tree_mode(staging, writable=False)
+        publish_dir(staging, dest)
     except BaseException:
-        dest.chmod(0o755)
-        for p in dest.rglob("*"):
-            if p.is_dir() and not p.is_symlink():
-                p.chmod(0o755)
-        shutil.rmtree(dest)
+        if staging.exists():
+            _set_tree_mode(staging, writable=True)
+            shutil.rmtree(staging)
         raise
+    verify_snapshot(dest)
     return manifest
 
 
+# ====================================================================================== verification
 def verify_snapshot(snapshot) -> dict:
-    root = Path(snapshot)
-    if root.is_symlink() or (root / "manifest.json").is_symlink():
+    """The snapshot's manifest, after checking every file against it; ValueError on any change."""
+    top = Path(snapshot)
+    if top.is_symlink() or (top / MANIFEST).is_symlink():
         raise ValueError("snapshot root and manifest must not be symlinks")
-    root = root.resolve()
-    manifest = json.loads((root / "manifest.json").read_text())
-    if (manifest.get("version") != 1 or manifest.get("package") != PACKAGE or not isinstance(manifest.get("files"), dict)
-            or not isinstance(manifest.get("input_paths"), dict) or not isinstance(manifest.get("source_root"), str)):
+    top = top.resolve()
+    manifest = json.loads((top / MANIFEST).read_text())
+    shape_ok = (manifest.get("version") == 1 and manifest.get("package") == PACKAGE
+                and isinstance(manifest.get("files"), dict) and isinstance(manifest.get("input_paths"), dict)
+                and isinstance(manifest.get("source_root"), str))
+    if not shape_ok:
         raise ValueError("invalid snapshot manifest")
     if not Path(manifest.get("working_directory", "/")).is_absolute():
         raise ValueError("snapshot working directory must be an absolute path")
-    actual = {}
-    for p in root.rglob("*"):
-        if p.is_symlink():
+    found = {}
+    for path in top.rglob("*"):
+        if path.is_symlink():
             raise ValueError("snapshot symlink forbidden")
-        if p.is_file() and p != root / "manifest.json":
-            actual[p.relative_to(root).as_posix()] = _record(p.read_bytes())
-    if actual != manifest["files"] or not _REQUIRED <= actual.keys():
+        if path.is_file() and path != top / MANIFEST:
+            found[path.relative_to(top).as_posix()] = _entry(path.read_bytes())
+    if found != manifest["files"] or not _REQUIRED <= found.keys():
         raise ValueError("snapshot file inventory or checksum mismatch")
-    for original, rel in manifest["input_paths"].items():
-        if not Path(original).is_absolute() or rel not in actual or not rel.startswith("inputs/"):
+    for original, name in manifest["input_paths"].items():
+        if not Path(original).is_absolute() or not name.startswith("inputs/") or name not in found:
             raise ValueError("invalid snapshot input mapping")
     return manifest
 
 
-def _run_child(command, *, cwd, shutdown_seconds=10.0) -> int:
-    """Run the child in its own process group until it exits; forward SIGINT/SIGTERM, escalating to
-    SIGKILL of that group after ``shutdown_seconds``."""
-    if threading.current_thread() is not threading.main_thread():
-        raise RuntimeError("snapshot subprocess supervision requires the main thread")
-    child, received, deadline = None, None, None
+# ====================================================================================== running
+def _pin_inputs(argv: list[str], top: Path, manifest: dict, cwd: Path) -> list[str]:
+    """``argv`` with every --config / --candidates value replaced by its captured copy."""
+    captured = manifest["input_paths"]
+    copies = {str(top / name) for name in captured.values()}
 
-    def send(signum):
-        if child is not None:
+    def captured_copy(value: str) -> str:
+        path = Path(value)
+        path = (path if path.is_absolute() else cwd / path).resolve()
+        if str(path) in captured:
+            return str(top / captured[str(path)])
+        if str(path) in copies:
+            return str(path)
+        raise ValueError(f"config/candidates input was not captured: {value}")
+
+    out, expect_value = [], None
+    for arg in argv:
+        if expect_value is not None:
+            out.append(captured_copy(arg))
+            expect_value = None
+            continue
+        flag, eq, value = arg.partition("=")
+        if flag.startswith("--") and flag not in _PINNED_FLAGS and any(f.startswith(flag) for f in _PINNED_FLAGS):
+            raise ValueError("spell --config and --candidates in full to pin their inputs")
+        if flag in _PINNED_FLAGS and eq:
+            out.append(f"{flag}={captured_copy(value)}")
+        else:
+            out.append(arg)
+            if flag in _PINNED_FLAGS:
+                expect_value = flag
+    if expect_value is not None:
+        raise ValueError(f"missing value for {expect_value}")
+    return out
+
+
+class _GroupSupervisor:
+    """Runs a command in its own process group; SIGINT/SIGTERM received meanwhile are forwarded to
+    the group, which is killed if it is still alive ``grace`` seconds after the first signal."""
+
+    def __init__(self, grace: float = 10.0):
+        self.grace = grace
+        self.child = None
+        self.signal = None
+        self.kill_at = None
+
+    def _to_group(self, signum):
+        if self.child is not None:
             try:
-                os.killpg(child.pid, signum)
+                os.killpg(self.child.pid, signum)
             except ProcessLookupError:
                 pass
 
-    def cancel(signum, frame):
-        nonlocal received, deadline
-        if received is None:
-            received, deadline = signum, time.monotonic() + shutdown_seconds
-        send(signum)
-    previous = {s: signal.getsignal(s) for s in (signal.SIGTERM, signal.SIGINT)}
-    try:
-        for s in previous:
-            signal.signal(s, cancel)
-        child = subprocess.Popen(command, cwd=cwd, start_new_session=True)
-        if received is not None:
-            send(received)
+    def _on_signal(self, signum, _frame):
+        if self.signal is None:
+            self.signal, self.kill_at = signum, time.monotonic() + self.grace
+        self._to_group(signum)
+
+    def _wait(self) -> int:
         while True:
             try:
-                rc = child.wait(timeout=0.1)
-                return 128 + received if received is not None else rc
+                code = self.child.wait(timeout=0.1)
+                return code if self.signal is None else 128 + self.signal
             except subprocess.TimeoutExpired:
-                if deadline is not None and time.monotonic() >= deadline:
-                    send(signal.SIGKILL)
-                    child.wait()
-                    return 128 + received
-    finally:
-        if child is not None and (received is not None or child.poll() is None):
-            send(signal.SIGKILL)
-            child.wait()
-        for s, h in previous.items():
-            signal.signal(s, h)
+                if self.kill_at is not None and time.monotonic() >= self.kill_at:
+                    self._to_group(signal.SIGKILL)
+                    self.child.wait()
+                    return 128 + self.signal
+
+    def run(self, command, *, cwd) -> int:
+        if threading.current_thread() is not threading.main_thread():
+            raise RuntimeError("snapshot subprocess supervision requires the main thread")
+        handled = (signal.SIGTERM, signal.SIGINT)
+        before = {s: signal.getsignal(s) for s in handled}
+        try:
+            for s in handled:
+                signal.signal(s, self._on_signal)
+            self.child = subprocess.Popen(command, cwd=cwd, start_new_session=True)
+            if self.signal is not None:  # arrived between installing the handler and the start
+                self._to_group(self.signal)
+            return self._wait()
+        finally:
+            if self.child is not None and (self.signal is not None or self.child.poll() is None):
+                self._to_group(signal.SIGKILL)
+                self.child.wait()
+            for s, handler in before.items():
+                signal.signal(s, handler)
 
 
 def run_snapshot(snapshot, args, *, workdir=None) -> int:
+    """Run one CLI command from the snapshot's package; returns the exit status (128 + signal
+    number when interrupted)."""
     manifest = verify_snapshot(snapshot)
-    root = Path(snapshot).resolve()
+    top = Path(snapshot).resolve()
     cwd = Path(workdir if workdir is not None else manifest.get("working_directory", manifest["source_root"])).resolve()
-    if cwd.is_relative_to(root):
+    if cwd.is_relative_to(top):
         raise ValueError("working directory must be outside the read-only snapshot")
-    argv = list(args)
-    if not argv:
+    if not args:
         raise ValueError("supply a CLI command")
-    captured = manifest["input_paths"]
-    inside = {str(root / n) for n in captured.values()}
-
-    def pinned(value):
-        p = Path(value)
-        p = (cwd / p).resolve() if not p.is_absolute() else p.resolve()
-        if str(p) in captured:
-            return str(root / captured[str(p)])
-        if str(p) in inside:
-            return str(p)
-        raise ValueError(f"config/candidates input was not captured: {value}")
-    i = 0
-    while i < len(argv):
-        flag, eq, value = argv[i].partition("=")
-        if (flag.startswith("--") and flag not in ("--config", "--candidates")
-                and any(n.startswith(flag) for n in ("--config", "--candidates"))):
-            raise ValueError("spell --config and --candidates in full to pin their inputs")
-        if flag in ("--config", "--candidates"):
-            if eq:
-                argv[i] = f"{flag}={pinned(value)}"
-            else:
-                if i + 1 == len(argv):
-                    raise ValueError(f"missing value for {flag}")
-                i += 1
-                argv[i] = pinned(argv[i])
-        i += 1
-    boot = ("import runpy,sys; sys.path.insert(0,sys.argv.pop(1)); "
-            f"sys.argv[0]='tnlm'; runpy.run_module('{PACKAGE}.cli',run_name='__main__')")
-    return _run_child([sys.executable, "-I", "-B", "-c", boot, str(root), *argv], cwd=cwd)
+    argv = _pin_inputs(list(args), top, manifest, cwd)
+    launcher = ("import runpy, sys; sys.path.insert(0, sys.argv.pop(1)); sys.argv[0] = 'tnlm'; "
+                f"runpy.run_module('{PACKAGE}.cli', run_name='__main__')")
+    return _GroupSupervisor().run([sys.executable, "-I", "-B", "-c", launcher, str(top), *argv], cwd=cwd)
 
 
 def main():
     parser = argparse.ArgumentParser(description=__doc__.split("\n")[0])
-    cmds = parser.add_subparsers(dest="command", required=True)
-    c = cmds.add_parser("create")
-    c.add_argument("--source", required=True)
-    c.add_argument("--out", required=True)
-    c.add_argument("--input", action="append", default=[])
-    c.add_argument("--workdir")
-    v = cmds.add_parser("verify")
-    v.add_argument("snapshot")
-    r = cmds.add_parser("run")
-    r.add_argument("--snapshot", required=True)
-    r.add_argument("--workdir")
-    r.add_argument("args", nargs=argparse.REMAINDER)
+    commands = parser.add_subparsers(dest="command", required=True)
+    create = commands.add_parser("create")
+    create.add_argument("--source", required=True)
+    create.add_argument("--out", required=True)
+    create.add_argument("--input", action="append", default=[])
+    create.add_argument("--workdir")
+    verify = commands.add_parser("verify")
+    verify.add_argument("snapshot")
+    run = commands.add_parser("run")
+    run.add_argument("--snapshot", required=True)
+    run.add_argument("--workdir")
+    run.add_argument("args", nargs=argparse.REMAINDER)
     a = parser.parse_args()
     if a.command == "create":
         print(json.dumps(create_snapshot(a.source, a.out, a.input, workdir=a.workdir), indent=2))

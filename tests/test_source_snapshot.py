@@ -64,3 +64,24 @@ def test_run_uses_the_captured_config_not_the_live_file(source, tmp_path, capfd)
         run_snapshot(out, ["train", "--config", str(tmp_path / "not-captured.yaml")], workdir=source)
     with pytest.raises(ValueError):
         run_snapshot(out, ["train", "--conf", "run.yaml"], workdir=source)  # abbreviations are refused
+
+
+def test_snapshot_appears_whole_or_not_at_all(source, tmp_path, monkeypatch):
+    import tensor_train_ing_b200.source_snapshot as snapshots
+    out = tmp_path / "snap"
+    real = snapshots._package_files
+    calls = []
+
+    def edited_meanwhile(root):  # the second read (after copying) sees a changed file
+        calls.append(root)
+        files = real(root)
+        if len(calls) == 2:
+            files[f"{PACKAGE}/cli.py"] += b"# edited\n"
+        return files
+    monkeypatch.setattr(snapshots, "_package_files", edited_meanwhile)
+    with pytest.raises(RuntimeError, match="source changed"):
+        create_snapshot(source, out, ["run.yaml"])
+    assert not out.exists() and sorted(p.name for p in tmp_path.iterdir()) == ["src"]
+    monkeypatch.setattr(snapshots, "_package_files", real)
+    create_snapshot(source, out, ["run.yaml"])
+    assert sorted(p.name for p in tmp_path.iterdir()) == ["snap", "src"]
