@@ -29,8 +29,9 @@ from pathlib import Path
 import torch
 import torch.distributed as dist
 
-from .checkpoint import (_code_identity, _digest, _plain, _publish, _require_finite, _restore_rng, _rng_state,
-                         _sync_directory, _validate_rng)
+from .checkpoint import assert_finite, code_identity, rng_capture, rng_check, rng_restore, to_plain
+from .durable import fsync_dir, publish_dir
+from .hashing import file_sha256
 from .checkpoint_storage import checkpoint_space_estimate, require_checkpoint_space
 
 FORMAT = "ttb-sharded-v1"
@@ -117,20 +118,20 @@ def save_distributed_checkpoint(path, model, optimizer, sampler, dp, *, config, 
     path = Path(path).resolve()
 
     def preflight():
-        _require_finite(model.state_dict(), "model")
-        _require_finite(optimizer.state_dict(), "optimizer")
+        assert_finite(model.state_dict(), "model")
+        assert_finite(optimizer.state_dict(), "optimizer")
         _check_boundary(model)
         if path.exists():
             raise FileExistsError(f"checkpoint already exists: {path}")
         return {"path": str(path), "world_size": world, "layout": _layout(dp, optimizer), "runtime": _runtime(),
-                "config": _plain(config), "progress": _plain(progress), "manifest_hash": manifest_hash,
-                "parent": _plain(parent), "extra": _plain(extra)}
+                "config": to_plain(config), "progress": to_plain(progress), "manifest_hash": manifest_hash,
+                "parent": to_plain(parent), "extra": to_plain(extra)}
     shared = _agree("checkpoint request", _phase("checkpoint preflight", preflight))
     digest = _agree("replicated state", _phase("replicated digest", lambda: _replicated_digest(model, dp)))
     sharded = bool(getattr(dp, "shard_params", False))
     local = {"rank": rank, "world_size": world, "optimizer": optimizer.state_dict(),
              "optimizer_layout": _local_layout(optimizer),
-             "sampler": sampler.state_dict() if sampler is not None else None, "rng": _rng_state(),
+             "sampler": sampler.state_dict() if sampler is not None else None, "rng": rng_capture(),
              "owned_params": ({k: v.cpu() for k, v in dp.owned_sharded_state().items()} if sharded else None)}
     replicated = _replicated_state(model, dp)
 
@@ -152,13 +153,13 @@ def save_distributed_checkpoint(path, model, optimizer, sampler, dp, *, config, 
                 torch.save(local, fh)
                 fh.flush()
                 os.fsync(fh.fileno())
-            out[name] = {"sha256": _digest(stage / name), "bytes": (stage / name).stat().st_size}
+            out[name] = {"sha256": file_sha256(stage / name), "bytes": (stage / name).stat().st_size}
             if rank == 0:
                 with (stage / "model.pt").open("wb") as fh:
                     torch.save({"model": replicated}, fh)
                     fh.flush()
                     os.fsync(fh.fileno())
-                out["model.pt"] = {"sha256": _digest(stage / "model.pt"), "bytes": (stage / "model.pt").stat().st_size}
+                out["model.pt"] = {"sha256": file_sha256(stage / "model.pt"), "bytes": (stage / "model.pt").stat().st_size}
             return out
         files = _phase("rank file write", write)
         gathered = [None] * world
@@ -168,7 +169,7 @@ def save_distributed_checkpoint(path, model, optimizer, sampler, dp, *, config, 
             if rank != 0:
                 return None
             manifest = {"format": FORMAT, "created_utc": datetime.now(timezone.utc).isoformat(), **shared,
-                        "replicated_state_sha256": digest, "code": _code_identity(),
+                        "replicated_state_sha256": digest, "code": code_identity(),
                         "files": {k: v for part in gathered for k, v in part.items()},
                         "replay_scope": "same world size, layout and torch version; rank-local RNG and data cursors"}
             with (stage / "manifest.json").open("w") as fh:
@@ -176,9 +177,8 @@ def save_distributed_checkpoint(path, model, optimizer, sampler, dp, *, config, 
                 fh.write("\n")
                 fh.flush()
                 os.fsync(fh.fileno())
-            _sync_directory(stage)
-            _publish(stage, path)
-            _sync_directory(path.parent)
+            fsync_dir(stage)
+            publish_dir(stage, path)
             return manifest
         box = [_phase("atomic publication", publish)]
         dist.broadcast_object_list(box, src=0)
@@ -224,7 +224,7 @@ def load_distributed_checkpoint(path, model, optimizer, sampler, dp, *, expected
             raise ValueError("checkpoint file set differs from manifest")
         for name in ("model.pt", f"rank-{rank:05d}.pt"):
             info = manifest["files"][name]
-            if (path / name).stat().st_size != info["bytes"] or _digest(path / name) != info["sha256"]:
+            if (path / name).stat().st_size != info["bytes"] or file_sha256(path / name) != info["sha256"]:
                 raise ValueError(f"checkpoint checksum mismatch: {name}")
         compat = config_validator(manifest["config"]) if config_validator is not None else None
         return manifest, compat
@@ -238,10 +238,10 @@ def load_distributed_checkpoint(path, model, optimizer, sampler, dp, *, expected
             raise ValueError("rank file identity mismatch")
         if local["optimizer_layout"] != _local_layout(optimizer):
             raise ValueError("this rank's optimizer parameter layout differs from the checkpoint")
-        _require_finite(state, "model")
-        _require_finite(local["optimizer"], "optimizer")
+        assert_finite(state, "model")
+        assert_finite(local["optimizer"], "optimizer")
         if restore_rng:
-            _validate_rng(local["rng"])
+            rng_check(local["rng"])
         current = _replicated_state(model, dp)
         if current.keys() != state.keys() or any(current[k].shape != state[k].shape for k in current):
             raise ValueError("checkpoint model keys or shapes differ")
@@ -250,7 +250,7 @@ def load_distributed_checkpoint(path, model, optimizer, sampler, dp, *, expected
             mine = local.get("owned_params") or {}
             if mine.keys() != owned.keys() or any(mine[k].shape != owned[k].shape for k in owned):
                 raise ValueError("this rank's sharded parameters differ from the checkpoint")
-            _require_finite(mine, "sharded parameters")
+            assert_finite(mine, "sharded parameters")
         if sampler is not None and local["sampler"] is None:
             raise ValueError("checkpoint has no sampler state")
         return state, local
@@ -267,7 +267,7 @@ def load_distributed_checkpoint(path, model, optimizer, sampler, dp, *, expected
         if sampler is not None:
             sampler.load_state_dict(local["sampler"])
         if restore_rng:
-            _restore_rng(local["rng"])
+            rng_restore(local["rng"])
     _phase("checkpoint install", install)
     if getattr(dp, "shard_params", False):
         dp.gather_params()  # bf16 caches / compute copies from the restored masters
@@ -295,7 +295,7 @@ def export_distributed_weights(path, model, *, config, progress, manifest_hash, 
             raise ValueError("positive integer export state-byte limit required")
         _check_boundary(model)
         state = model.state_dict()
-        _require_finite(_replicated_state(model, dp), "model")
+        assert_finite(_replicated_state(model, dp), "model")
         size = sum(v.numel() * v.element_size() for v in state.values())
         if size > max_state_bytes:
             raise ValueError(f"full export needs {size} tensor bytes, exceeds {max_state_bytes}")
@@ -314,7 +314,7 @@ def export_distributed_weights(path, model, *, config, progress, manifest_hash, 
             with torch.device("meta"):
                 source = type(model)(model.cfg)
             source.load_state_dict(full, assign=True)
-            _require_finite(full, "model")
+            assert_finite(full, "model")
         return save_checkpoint(request["path"], source, None, None, config=config, progress=progress,
                                manifest_hash=manifest_hash, parent=parent,
                                extra={"artifact_kind": "distributed_evaluation_weights", "training_recovery": False,
