@@ -29,6 +29,7 @@ from .calibration import _check_lagged_divisor
 from .config import Config
 from .models.model import TensorLM
 from .models.normalization import lagged_modules
+from .hashing import canonical_sha256
 from .runtime import evaluation_validator
 
 
@@ -233,6 +234,7 @@ def _training_comparison(left, right) -> dict:
 
 
 def _tensor_hash(items) -> str:
+    """sha256 over (name, dtype, shape, raw bytes) of named tensors, in name order."""
     h = hashlib.sha256()
     for name, value in sorted(items):
         value = value.detach().cpu().contiguous()
@@ -255,9 +257,150 @@ def _ledger(project):
                        project.get("reserve_usd", 150), stage_budgets=project.get("stage_budgets"))
 
 
+def ratio_bootstrap(numerators, denominators, *, samples: int, seed: int):
+    """95 % percentile interval of sum(numerators) / sum(denominators) under resampling of the
+    units (documents) with replacement: ``samples`` resamples drawn one after another from
+    ``numpy.random.default_rng(seed)``.  None with fewer than two units or no resamples."""
+    num = np.asarray(numerators, dtype=np.float64)
+    den = np.asarray(denominators, dtype=np.int64)
+    units = len(num)
+    if units < 2 or not samples:
+        return None
+    rng = np.random.default_rng(seed)
+    ratios = np.empty(samples)
+    for k in range(samples):
+        pick = rng.integers(0, units, size=units)
+        ratios[k] = num[pick].sum() / den[pick].sum()
+    return np.quantile(ratios, [.025, .975]).tolist()
+
+
+class TargetPlan:
+    """The targets a held-out evaluation scores, independent of the probe context: for each
+    validation document in the manifest's order, source target offsets 1 .. length-1 (every token
+    that has a predecessor), until ``cap`` targets are planned.  The plan's canonical JSON digest
+    is its identity: two evaluations are comparable only on the same plan."""
+
+    def __init__(self, sampler, cap: int):
+        self.ranges, left = [], cap
+        for i in range(len(sampler.docs)):
+            count = min(max(0, sampler.docs.length(i) - 1), left)
+            if count:
+                self.ranges.append({"document_id": sampler.docs[i]["id"], "target_start": 1,
+                                    "target_end": count + 1, "count": count})
+                left -= count
+            if not left:
+                break
+        if not self.ranges:
+            raise ValueError("validation split has no prediction targets")
+        self.by_document = {r["document_id"]: r for r in self.ranges}
+        self.record = {"version": 1, "validation_manifest_sha256": sampler.manifest_hash, "split": "val",
+                       "ordering": "immutable documents.jsonl order",
+                       "offset_semantics": "processed document stream; includes synthetic EOS if present",
+                       "ranges": self.ranges}
+        self.sha256 = canonical_sha256(self.record)
+
+    def select(self, mappings, original, context):
+        """Targets of one packed row restricted to the plan, and the chosen positions as
+        (column, document id, available prefix length, source offset)."""
+        targets = torch.full_like(original, -100)
+        chosen = []
+        for m in mappings:
+            planned = self.by_document.get(m["document_id"])
+            if planned is None:
+                continue
+            first, end = m["packed_token_start"], m["packed_token_end"]
+            for col in range(first, min(end - 1, context)):
+                offset = m["source_token_start"] + col - first + 1
+                if not planned["target_start"] <= offset < planned["target_end"]:
+                    continue
+                if original[0, col] == -100:
+                    raise ValueError("selected validation target was masked by sampler")
+                targets[0, col] = original[0, col]
+                chosen.append((col, m["document_id"], col - first + 1, offset))
+        return targets, chosen
+
+
+class _PlanScore:
+    """Per-document loss sums of a target plan, checked to visit every planned offset exactly once
+    and in order, with the histogram and digest of the prefixes the model saw."""
+
+    def __init__(self, plan: TargetPlan):
+        self.plan = plan
+        self.totals = {r["document_id"]: {"loss_sum": 0.0, "tokens": 0} for r in plan.ranges}
+        self.prefixes: dict[int, int] = {}
+        self.prefix_digest = hashlib.sha256()
+        self.forward_tokens = self.forward_batches = 0
+
+    def add(self, losses, chosen, input_tokens):
+        for col, doc, prefix, offset in chosen:
+            total = self.totals[doc]
+            if offset != self.plan.by_document[doc]["target_start"] + total["tokens"]:
+                raise ValueError("duplicate or missing source target offset in evaluation")
+            total["loss_sum"] += float(losses[col])
+            total["tokens"] += 1
+            self.prefixes[prefix] = self.prefixes.get(prefix, 0) + 1
+            self.prefix_digest.update(json.dumps([doc, offset, prefix], separators=(",", ":")).encode() + b"\n")
+        self.forward_batches += 1
+        self.forward_tokens += input_tokens
+
+    def finish(self):
+        for r in self.plan.ranges:
+            if self.totals[r["document_id"]]["tokens"] != r["count"]:
+                raise ValueError("validation target plan was not evaluated exactly once")
+        counts = [t["tokens"] for t in self.totals.values()]
+        sums = [t["loss_sum"] for t in self.totals.values()]
+        return counts, sums
+
+
+def _frozen_state(model) -> tuple[str, str]:
+    return _tensor_hash(model.state_dict().items()), _tensor_hash(model.named_buffers())
+
+
+def _source_provenance(checkpoint_code) -> dict:
+    pkg = Path(__file__).parent
+    runtime_sources = {f"{pkg.name}/{p.relative_to(pkg).as_posix()}": _file_hash(p) for p in sorted(pkg.rglob("*.py"))}
+    saved = checkpoint_code.get("source_sha256", {})
+    critical = ("models/model.py", "models/attention.py", "models/normalization.py", "config.py")
+    matches = {n: runtime_sources.get(f"{pkg.name}/{n}") == saved.get(f"{pkg.name}/{n}") for n in critical}
+    return {"checkpoint_code": checkpoint_code, "runtime_source_sha256": runtime_sources,
+            "critical_model_sources_match_checkpoint": all(matches.values()), "critical_model_source_matches": matches}
+
+
+def _check_eval_bounds(context, max_prediction_tokens, bootstrap_samples, max_seconds):
+    if (type(context) is not int or context <= 0 or type(max_prediction_tokens) is not int
+            or max_prediction_tokens <= 0 or type(bootstrap_samples) is not int
+            or not 0 <= bootstrap_samples <= 100_000 or not math.isfinite(max_seconds) or max_seconds <= 0):
+        raise ValueError("positive evaluation bounds and bootstrap_samples in [0, 100000] required")
+
+
+def _checked_rate(project, dev):
+    if dev.type == "cuda" and not torch.cuda.is_available():
+        raise RuntimeError("CUDA requested but unavailable")
+    rate = project.get("gpu_hourly_rate_usd")
+    if rate is None or (dev.type == "cuda" and rate <= 0):
+        raise ValueError("declare actual gpu_hourly_rate_usd (explicit 0 allowed for CPU)")
+    return rate
+
+
+def _load_frozen_model(cfg, checkpoint, train_hash, dev):
+    """The checkpoint's model in eval mode with its lagged statistics frozen; (model, payload)."""
+    from .checkpoint import load_checkpoint
+    model = TensorLM(cfg.model)
+    payload = load_checkpoint(checkpoint, model, config_validator=evaluation_validator(cfg),
+                              expected_manifest_hash=train_hash, restore_rng=False, map_location="cpu")
+    model.to(dev).eval()
+    for norm in lagged_modules(model):
+        norm.collecting = False
+        norm.set_valid_mask(None)
+        _check_lagged_divisor(norm)
+    return model, payload
+
+
 def evaluate_checkpoint(cfg, checkpoint, out_dir, *, context=None, max_prediction_tokens=1_000_000, max_seconds,
                         device="cpu", bootstrap_samples=1000, run_budget_usd=None) -> dict:
-    from .checkpoint import load_checkpoint
+    """Held-out CE of ``checkpoint`` on the validation target plan (see ``TargetPlan``), with a
+    document-bootstrap interval, proof that evaluation left the model unchanged and an exact-document
+    overlap audit against the training data; writes ``evaluation.json`` into ``out_dir``."""
     from .data import PackedSampler, audit_validation_overlap, manifest_hash, validate_tokenizer_compatibility
     if isinstance(cfg, (str, Path)):
         cfg = Config.from_yaml(str(cfg))
@@ -267,16 +410,9 @@ def evaluate_checkpoint(cfg, checkpoint, out_dir, *, context=None, max_predictio
         return {"dry_run": True, "command": "evaluate", "checkpoint": str(checkpoint), "context": probe_context,
                 "max_prediction_tokens": max_prediction_tokens, "split": "val",
                 "target_policy": "canonical document order; source target offsets 1..L-1"}
-    if (type(probe_context) is not int or probe_context <= 0 or type(max_prediction_tokens) is not int
-            or max_prediction_tokens <= 0 or type(bootstrap_samples) is not int or not 0 <= bootstrap_samples <= 100_000
-            or not math.isfinite(max_seconds) or max_seconds <= 0):
-        raise ValueError("positive evaluation bounds and bootstrap_samples in [0, 100000] required")
+    _check_eval_bounds(probe_context, max_prediction_tokens, bootstrap_samples, max_seconds)
     dev = torch.device(device)
-    if dev.type == "cuda" and not torch.cuda.is_available():
-        raise RuntimeError("CUDA requested but unavailable")
-    rate = project.get("gpu_hourly_rate_usd")
-    if rate is None or (dev.type == "cuda" and rate <= 0):
-        raise ValueError("declare actual gpu_hourly_rate_usd (explicit 0 allowed for CPU)")
+    rate = _checked_rate(project, dev)
     out_dir = Path(out_dir)
     if out_dir.exists():
         raise FileExistsError(f"evaluation directory already exists: {out_dir}")
@@ -293,113 +429,53 @@ def evaluate_checkpoint(cfg, checkpoint, out_dir, *, context=None, max_predictio
     try:
         out_dir.mkdir(parents=True, exist_ok=False)
         train_hash = manifest_hash(data["manifest"])
-        val_path = cfg.raw.get("evaluation", {}).get("validation_manifest", data["manifest"])
+        evaluation = cfg.raw.get("evaluation", {})
+        val_path = evaluation.get("validation_manifest", data["manifest"])
         tok_compat = validate_tokenizer_compatibility(data["manifest"], val_path, allow_test_only=dev.type == "cpu")
-        eval_seed = int(cfg.raw.get("evaluation", {}).get("seed", 0))
+        eval_seed = int(evaluation.get("seed", 0))
         sampler = PackedSampler(val_path, split="val", batch_size=1, context=probe_context, seed=eval_seed)
-        ranges, remaining = [], max_prediction_tokens
-        for i in range(len(sampler.docs)):
-            doc = sampler.docs[i]
-            count = min(max(0, sampler.docs.length(i) - 1), remaining)
-            if count:
-                ranges.append({"document_id": doc["id"], "target_start": 1, "target_end": count + 1, "count": count})
-                remaining -= count
-            if not remaining:
-                break
-        if not ranges:
-            raise ValueError("validation split has no prediction targets")
-        audit = audit_validation_overlap(data["manifest"], val_path, document_ids=[r["document_id"] for r in ranges])
+        plan = TargetPlan(sampler, max_prediction_tokens)
+        audit = audit_validation_overlap(data["manifest"], val_path, document_ids=[r["document_id"] for r in plan.ranges])
         (out_dir / "data-overlap-audit.json").write_text(json.dumps(audit, indent=2) + "\n")
         if audit["has_overlap"]:
             raise ValueError("held-out validation has exact whole-document content overlap; see data-overlap-audit.json")
-        model = TensorLM(cfg.model)
-        payload = load_checkpoint(checkpoint, model, config_validator=evaluation_validator(cfg),
-                                  expected_manifest_hash=train_hash, restore_rng=False, map_location="cpu")
-        model.to(dev).eval()
-        ckpt_progress, ckpt_code = payload["progress"], payload["code"]
-        descriptor = _training_descriptor(payload)
+        model, payload = _load_frozen_model(cfg, checkpoint, train_hash, dev)
+        ckpt_progress, ckpt_code, descriptor = payload["progress"], payload["code"], _training_descriptor(payload)
         del payload
-        for norm in lagged_modules(model):
-            norm.collecting = False
-            norm.set_valid_mask(None)
-            _check_lagged_divisor(norm)
-        before_model, before_buffers = _tensor_hash(model.state_dict().items()), _tensor_hash(model.named_buffers())
-        plan = {"version": 1, "validation_manifest_sha256": sampler.manifest_hash, "split": "val",
-                "ordering": "immutable documents.jsonl order",
-                "offset_semantics": "processed document stream; includes synthetic EOS if present", "ranges": ranges}
-        plan_hash = hashlib.sha256(json.dumps(plan, sort_keys=True, separators=(",", ":")).encode()).hexdigest()
-        selected = {r["document_id"]: r for r in ranges}
-        totals = {r["document_id"]: {"loss_sum": 0.0, "tokens": 0} for r in ranges}
-        prefixes, fwd_tokens, fwd_batches = {}, 0, 0
-        prefix_digest = hashlib.sha256()
+        before_model, before_buffers = _frozen_state(model)
+        score = _PlanScore(plan)
         initial = sampler.state_dict()
         with torch.inference_mode():
             for _ in range(sampler.epoch_row_count):
                 deadline()
-                idx, docs, orig = sampler.next_batch()
-                targets = torch.full_like(orig, -100)
-                positions = []
-                for m in sampler.batch_mappings()[0]["ranges"]:
-                    row = selected.get(m["document_id"])
-                    if row is None:
-                        continue
-                    s, e = m["packed_token_start"], m["packed_token_end"]
-                    for j in range(s, min(e - 1, probe_context)):
-                        off = m["source_token_start"] + j - s + 1
-                        if row["target_start"] <= off < row["target_end"]:
-                            if orig[0, j] == -100:
-                                raise ValueError("selected validation target was masked by sampler")
-                            targets[0, j] = orig[0, j]
-                            positions.append((j, m["document_id"], j - s + 1, off))
-                if not positions:
+                idx, docs, original = sampler.next_batch()
+                targets, chosen = plan.select(sampler.batch_mappings()[0]["ranges"], original, probe_context)
+                if not chosen:
                     continue
                 logits = model(idx.to(dev), doc_ids=docs.to(dev))
                 losses = F.cross_entropy(logits.float().flatten(0, 1), targets.to(dev).flatten(), reduction="none",
                                          ignore_index=-100).cpu()
                 if not torch.isfinite(losses).all():
                     raise FloatingPointError("nonfinite validation loss")
-                for j, doc_id, prefix, off in positions:
-                    if off != selected[doc_id]["target_start"] + totals[doc_id]["tokens"]:
-                        raise ValueError("duplicate or missing source target offset in evaluation")
-                    totals[doc_id]["loss_sum"] += float(losses[j])
-                    totals[doc_id]["tokens"] += 1
-                    prefixes[prefix] = prefixes.get(prefix, 0) + 1
-                    prefix_digest.update(json.dumps([doc_id, off, prefix], separators=(",", ":")).encode() + b"\n")
-                fwd_batches += 1
-                fwd_tokens += int((docs >= 0).sum())
-        for r in ranges:
-            if totals[r["document_id"]]["tokens"] != r["count"]:
-                raise ValueError("validation target plan was not evaluated exactly once")
-        after_model, after_buffers = _tensor_hash(model.state_dict().items()), _tensor_hash(model.named_buffers())
-        if before_model != after_model or before_buffers != after_buffers:
+                score.add(losses, chosen, int((docs >= 0).sum()))
+        counts, sums = score.finish()
+        after_model, after_buffers = _frozen_state(model)
+        if (before_model, before_buffers) != (after_model, after_buffers):
             raise RuntimeError("evaluation changed checkpoint model or normalization buffers")
-        counts = np.asarray([r["tokens"] for r in totals.values()], dtype=np.int64)
-        sums = np.asarray([r["loss_sum"] for r in totals.values()], dtype=np.float64)
-        tokens, loss_sum = int(counts.sum()), float(sums.sum())
-        ci = None
-        if len(counts) >= 2 and bootstrap_samples:
-            rng = np.random.default_rng(eval_seed)
-            est = np.empty(bootstrap_samples)
-            for i in range(bootstrap_samples):
-                draw = rng.integers(0, len(counts), size=len(counts))
-                est[i] = sums[draw].sum() / counts[draw].sum()
-            ci = np.quantile(est, [.025, .975]).tolist()
-        pkg = Path(__file__).parent
-        runtime_sources = {f"{pkg.name}/{p.relative_to(pkg).as_posix()}": _file_hash(p) for p in sorted(pkg.rglob("*.py"))}
-        critical = ("models/model.py", "models/attention.py", "models/normalization.py", "config.py")
-        matches = {n: runtime_sources.get(f"{pkg.name}/{n}") == ckpt_code.get("source_sha256", {}).get(f"{pkg.name}/{n}")
-                   for n in critical}
+        tokens, loss_sum = int(np.sum(counts, dtype=np.int64)), float(np.sum(sums, dtype=np.float64))
+        ci = ratio_bootstrap(sums, counts, samples=bootstrap_samples, seed=eval_seed)
         ckpt = Path(checkpoint)
         result = {"kind": "held_out_validation", "evaluation_protocol_version": 2, "data_overlap_audit": audit,
                   "tokenizer_compatibility": tok_compat, "split": "val", "context": probe_context,
                   "prediction_tokens": tokens, "loss_sum": loss_sum, "ce": loss_sum / tokens,
                   "validation_below_one_million_targets": tokens < 1_000_000,
-                  "uncertainty": {"unit": "documents, not training seeds", "method": "token-weighted ratio document bootstrap",
-                                  "samples": bootstrap_samples, "seed": eval_seed, "ce_95_ci": ci, "documents": len(totals)},
-                  "target_plan": plan, "target_plan_sha256": plan_hash,
-                  "per_document": [{"document_id": k, **v} for k, v in totals.items()],
-                  "available_prefix_length_histogram": {str(k): v for k, v in sorted(prefixes.items())},
-                  "available_prefix_plan_sha256": prefix_digest.hexdigest(), "evaluation_seed": eval_seed,
+                  "uncertainty": {"unit": "documents, not training seeds",
+                                  "method": "token-weighted ratio document bootstrap", "samples": bootstrap_samples,
+                                  "seed": eval_seed, "ce_95_ci": ci, "documents": len(score.totals)},
+                  "target_plan": plan.record, "target_plan_sha256": plan.sha256,
+                  "per_document": [{"document_id": k, **v} for k, v in score.totals.items()],
+                  "available_prefix_length_histogram": {str(k): v for k, v in sorted(score.prefixes.items())},
+                  "available_prefix_plan_sha256": score.prefix_digest.hexdigest(), "evaluation_seed": eval_seed,
                   "training_manifest_sha256": train_hash, "validation_manifest_sha256": sampler.manifest_hash,
                   "checkpoint": str(ckpt.resolve()), "checkpoint_manifest_sha256": _file_hash(ckpt / "manifest.json"),
                   "checkpoint_state_sha256": _file_hash(ckpt / "state.pt"), "checkpoint_progress": ckpt_progress,
@@ -408,15 +484,13 @@ def evaluate_checkpoint(cfg, checkpoint, out_dir, *, context=None, max_predictio
                   "frozen_state": {"model_before": before_model, "model_after": after_model,
                                    "buffers_before": before_buffers, "buffers_after": after_buffers, "unchanged": True},
                   "sampler": {"initial": initial, "final": sampler.state_dict(), "rows_scanned": sampler.epoch_row_count,
-                              "forwarded_batches": fwd_batches},
+                              "forwarded_batches": score.forward_batches},
                   "probe": {"context_override": context, "batch_size": 1, "device": str(dev),
                             "dtype": str(next(model.parameters()).dtype), "autocast": False,
-                            "checkpoint_code": ckpt_code, "runtime_source_sha256": runtime_sources,
-                            "critical_model_sources_match_checkpoint": all(matches.values()),
-                            "critical_model_source_matches": matches, "torch_version": str(torch.__version__),
+                            **_source_provenance(ckpt_code), "torch_version": str(torch.__version__),
                             "deterministic_algorithms": torch.are_deterministic_algorithms_enabled()},
-                  "exposure": {"split": "val", "unique_prediction_tokens": tokens, "forward_input_tokens": fwd_tokens,
-                               "final_test_exposed": False}}
+                  "exposure": {"split": "val", "unique_prediction_tokens": tokens,
+                               "forward_input_tokens": score.forward_tokens, "final_test_exposed": False}}
         status = "complete"
     finally:
         ledger.finish(run_id, time.monotonic() - started, status)
@@ -425,59 +499,89 @@ def evaluate_checkpoint(cfg, checkpoint, out_dir, *, context=None, max_predictio
     return result
 
 
-def _validated_report(value):
-    report = json.loads(Path(value).read_text()) if isinstance(value, (str, Path)) else value
-    if not isinstance(report, dict) or report.get("kind") != "held_out_validation" or report.get("split") != "val":
-        raise ValueError("comparison requires held_out_validation reports")
+# ====================================================================================== paired comparison
+def _require(condition, message):
+    if not condition:
+        raise ValueError(message)
+
+
+def _check_frozen_proof(report):
     frozen = report.get("frozen_state", {})
-    if (frozen.get("unchanged") is not True or not frozen.get("model_before")
-            or frozen.get("model_before") != frozen.get("model_after")
-            or frozen.get("model_before") != report.get("model_sha256")
-            or not frozen.get("buffers_before") or frozen.get("buffers_before") != frozen.get("buffers_after")):
-        raise ValueError("evaluation lacks consistent frozen-state proof")
+    model_before = frozen.get("model_before")
+    _require(frozen.get("unchanged") is True and model_before and model_before == frozen.get("model_after")
+             and model_before == report.get("model_sha256") and frozen.get("buffers_before")
+             and frozen.get("buffers_before") == frozen.get("buffers_after"),
+             "evaluation lacks consistent frozen-state proof")
+
+
+def _planned_counts(report) -> dict:
+    """document id -> planned target count, after checking the plan's identity and shape."""
     plan = report.get("target_plan")
-    if not isinstance(plan, dict) or plan.get("split") != "val":
-        raise ValueError("invalid validation target plan")
-    if hashlib.sha256(json.dumps(plan, sort_keys=True, separators=(",", ":")).encode()).hexdigest() != report.get("target_plan_sha256"):
-        raise ValueError("target-plan SHA256 mismatch")
-    if not plan.get("validation_manifest_sha256") or plan["validation_manifest_sha256"] != report.get("validation_manifest_sha256"):
-        raise ValueError("validation manifest identity mismatch")
-    ctx, ph = report.get("context"), report.get("available_prefix_plan_sha256")
-    if type(ctx) is not int or ctx <= 0 or not isinstance(ph, str) or len(ph) != 64:
-        raise ValueError("invalid context or prefix provenance")
-    audit = report.get("data_overlap_audit", {})
-    if (report.get("evaluation_protocol_version") != 2 or audit.get("has_overlap") is not False
-            or audit.get("training_manifest_hash") != report.get("training_manifest_sha256")
-            or audit.get("validation_manifest_hash") != report.get("validation_manifest_sha256")):
-        raise ValueError("evaluation lacks certified exact-document separation audit")
+    _require(isinstance(plan, dict) and plan.get("split") == "val", "invalid validation target plan")
+    _require(canonical_sha256(plan) == report.get("target_plan_sha256"), "target-plan SHA256 mismatch")
+    _require(plan.get("validation_manifest_sha256")
+             and plan["validation_manifest_sha256"] == report.get("validation_manifest_sha256"),
+             "validation manifest identity mismatch")
+    context, prefix_hash = report.get("context"), report.get("available_prefix_plan_sha256")
+    _require(type(context) is int and context > 0 and isinstance(prefix_hash, str) and len(prefix_hash) == 64,
+             "invalid context or prefix provenance")
     planned = {}
     for r in plan.get("ranges") or []:
-        name, s, e, c = (r.get(k) for k in ("document_id", "target_start", "target_end", "count"))
-        if not isinstance(name, str) or name in planned or any(type(x) is not int for x in (s, e, c)) \
-                or s < 1 or e <= s or c != e - s:
-            raise ValueError("invalid or duplicate target range/count")
-        planned[name] = c
-    if not planned:
-        raise ValueError("empty target plan")
+        doc, start, end, count = (r.get(k) for k in ("document_id", "target_start", "target_end", "count"))
+        _require(isinstance(doc, str) and doc not in planned and all(type(x) is int for x in (start, end, count))
+                 and start >= 1 and end > start and count == end - start, "invalid or duplicate target range/count")
+        planned[doc] = count
+    _require(planned, "empty target plan")
+    return planned
+
+
+def _check_separation_audit(report, planned):
+    audit = report.get("data_overlap_audit", {})
+    _require(report.get("evaluation_protocol_version") == 2 and audit.get("has_overlap") is False
+             and audit.get("training_manifest_hash") == report.get("training_manifest_sha256")
+             and audit.get("validation_manifest_hash") == report.get("validation_manifest_sha256"),
+             "evaluation lacks certified exact-document separation audit")
     ids = hashlib.sha256(json.dumps(sorted(planned), separators=(",", ":"), ensure_ascii=True).encode()).hexdigest()
-    if audit.get("selected_validation_documents") != len(planned) or audit.get("selected_validation_ids_sha256") != ids:
-        raise ValueError("document separation audit differs from target plan")
-    by_doc = {}
+    _require(audit.get("selected_validation_documents") == len(planned)
+             and audit.get("selected_validation_ids_sha256") == ids, "document separation audit differs from target plan")
+
+
+def _finite_loss(value) -> bool:
+    return not isinstance(value, bool) and isinstance(value, (int, float)) and math.isfinite(value) and value >= 0
+
+
+def _per_document(report, planned) -> dict:
+    """document id -> (targets, loss sum), checked against the plan and the report's aggregates."""
+    rows = {}
     for r in report.get("per_document") or []:
-        name, n, loss = r.get("document_id"), r.get("tokens"), r.get("loss_sum")
-        if (not isinstance(name, str) or name in by_doc or type(n) is not int or n <= 0
-                or isinstance(loss, bool) or not isinstance(loss, (int, float)) or not math.isfinite(loss) or loss < 0
-                or planned.get(name) != n):
-            raise ValueError("invalid per-document ID/count/loss")
-        by_doc[name] = (n, float(loss))
-    if set(by_doc) != set(planned):
-        raise ValueError("per-document IDs differ from target plan")
-    tt = sum(v[0] for v in by_doc.values())
-    tl = sum(v[1] for v in by_doc.values())
-    if (report.get("prediction_tokens") != tt or not math.isclose(report.get("loss_sum", -1), tl, rel_tol=1e-12, abs_tol=1e-10)
-            or not math.isclose(report.get("ce", -1), tl / tt, rel_tol=1e-12, abs_tol=1e-10)):
-        raise ValueError("aggregate losses/counts disagree with per-document state")
-    return report, by_doc
+        doc, n, loss = r.get("document_id"), r.get("tokens"), r.get("loss_sum")
+        _require(isinstance(doc, str) and doc not in rows and type(n) is int and n > 0 and _finite_loss(loss)
+                 and planned.get(doc) == n, "invalid per-document ID/count/loss")
+        rows[doc] = (n, float(loss))
+    _require(set(rows) == set(planned), "per-document IDs differ from target plan")
+    targets = sum(n for n, _ in rows.values())
+    loss = sum(s for _, s in rows.values())
+    close = lambda a, b: math.isclose(a, b, rel_tol=1e-12, abs_tol=1e-10)  # noqa: E731
+    _require(report.get("prediction_tokens") == targets and close(report.get("loss_sum", -1), loss)
+             and close(report.get("ce", -1), loss / targets), "aggregate losses/counts disagree with per-document state")
+    return rows
+
+
+def _validated_report(value):
+    """A held-out evaluation report (or its path), checked for internal consistency; returns
+    (report, per-document rows)."""
+    report = json.loads(Path(value).read_text()) if isinstance(value, (str, Path)) else value
+    _require(isinstance(report, dict) and report.get("kind") == "held_out_validation" and report.get("split") == "val",
+             "comparison requires held_out_validation reports")
+    _check_frozen_proof(report)
+    planned = _planned_counts(report)
+    _check_separation_audit(report, planned)
+    return report, _per_document(report, planned)
+
+
+_REPORT_IDENTITY = ("checkpoint", "checkpoint_manifest_sha256", "checkpoint_state_sha256", "checkpoint_progress",
+                    "training_descriptor", "model_sha256", "operator_audit", "probe", "context", "evaluation_seed",
+                    "available_prefix_plan_sha256", "available_prefix_length_histogram", "ce")
 
 
 def compare_evaluations(left, right, out_dir, *, bootstrap_samples=1000, seed=0) -> dict:
@@ -486,39 +590,30 @@ def compare_evaluations(left, right, out_dir, *, bootstrap_samples=1000, seed=0)
         raise ValueError("bootstrap_samples must be in [0, 100000]")
     if type(seed) is not int or seed < 0:
         raise ValueError("seed must be a nonnegative integer")
-    left, ld = _validated_report(left)
-    right, rd = _validated_report(right)
-    if left["target_plan"] != right["target_plan"] or left["validation_manifest_sha256"] != right["validation_manifest_sha256"]:
+    left, left_docs = _validated_report(left)
+    right, right_docs = _validated_report(right)
+    if (left["target_plan"] != right["target_plan"]
+            or left["validation_manifest_sha256"] != right["validation_manifest_sha256"]):
         raise ValueError("evaluations have different target plans or validation manifests")
-    if set(ld) != set(rd) or any(ld[k][0] != rd[k][0] for k in ld):
+    if set(left_docs) != set(right_docs) or any(left_docs[k][0] != right_docs[k][0] for k in left_docs):
         raise ValueError("evaluations have different per-document targets/counts")
-    prefix_match = left["available_prefix_plan_sha256"] == right["available_prefix_plan_sha256"]
-    if left["context"] == right["context"] and not prefix_match:
+    same_prefixes = left["available_prefix_plan_sha256"] == right["available_prefix_plan_sha256"]
+    if left["context"] == right["context"] and not same_prefixes:
         raise ValueError("same-context evaluations have different available prefix plans")
-    names = sorted(ld)
-    counts = np.asarray([ld[k][0] for k in names], dtype=np.int64)
-    diffs = np.asarray([rd[k][1] - ld[k][1] for k in names], dtype=np.float64)
-    tokens = int(counts.sum())
-    ci = None
-    if len(names) >= 2 and bootstrap_samples:
-        rng = np.random.default_rng(seed)
-        est = np.empty(bootstrap_samples)
-        for i in range(bootstrap_samples):
-            draw = rng.integers(0, len(names), size=len(names))
-            est[i] = diffs[draw].sum() / counts[draw].sum()
-        ci = np.quantile(est, [.025, .975]).tolist()
-    ident = lambda r: {k: r.get(k) for k in (  # noqa: E731
-        "checkpoint", "checkpoint_manifest_sha256", "checkpoint_state_sha256", "checkpoint_progress",
-        "training_descriptor", "model_sha256", "operator_audit", "probe", "context", "evaluation_seed",
-        "available_prefix_plan_sha256", "available_prefix_length_histogram", "ce")}
-    result = {"kind": "matched_validation_comparison", "left": ident(left), "right": ident(right),
+    names = sorted(left_docs)
+    counts = [left_docs[k][0] for k in names]
+    deltas = [right_docs[k][1] - left_docs[k][1] for k in names]
+    tokens = int(np.sum(counts, dtype=np.int64))
+    ci = ratio_bootstrap(deltas, counts, samples=bootstrap_samples, seed=seed)
+    result = {"kind": "matched_validation_comparison", "left": {k: left.get(k) for k in _REPORT_IDENTITY},
+              "right": {k: right.get(k) for k in _REPORT_IDENTITY},
               "validation_manifest_sha256": left["validation_manifest_sha256"],
               "target_plan_sha256": left["target_plan_sha256"], "prediction_tokens": tokens, "documents": len(names),
-              "contexts_match": left["context"] == right["context"], "available_prefix_plans_match": prefix_match,
+              "contexts_match": left["context"] == right["context"], "available_prefix_plans_match": same_prefixes,
               "training_comparison": _training_comparison(left, right), "automatic_ranking_eligible": False,
-              "prefix_comparison": ("identical available prefixes" if prefix_match
+              "prefix_comparison": ("identical available prefixes" if same_prefixes
                                     else "different available prefixes across contexts"),
-              "delta_ce_right_minus_left": float(diffs.sum() / tokens),
+              "delta_ce_right_minus_left": float(np.sum(deltas, dtype=np.float64) / tokens),
               "uncertainty": {"method": "paired document bootstrap of token-weighted CE difference",
                               "unit": "nominal document uncertainty; not training seeds or HPO correction",
                               "bootstrap_samples": bootstrap_samples, "seed": seed, "delta_ce_95_ci": ci},
