@@ -22,7 +22,7 @@ from typing import NamedTuple
 
 import torch
 
-from .optim import Muon, MuonAdamW
+from .optim import FusedAdamW, Muon, MuonAdamW
 
 SCOPE = ("scheduled group exposure; mathematical shrinkage product before floating-point rounding, for a "
          "parameter participating in every observed update")
@@ -47,11 +47,16 @@ def _nonnegative(value, what: str) -> float:
     return value
 
 
+def _is_adamw(optimizer) -> bool:
+    """torch AdamW or its fused-kernel subclass (same hyper-parameters and update rule)."""
+    return type(optimizer) in (torch.optim.AdamW, FusedAdamW)
+
+
 def _parts(optimizer) -> list[tuple[str, torch.optim.Optimizer]]:
-    if type(optimizer) is torch.optim.AdamW:
+    if _is_adamw(optimizer):
         return [("adamw", optimizer)]
     if (type(optimizer) is MuonAdamW and isinstance(optimizer.muon, (Muon, torch.optim.Muon))
-            and type(optimizer.adamw) is torch.optim.AdamW):
+            and _is_adamw(optimizer.adamw)):
         return [("muon", optimizer.muon), ("adamw", optimizer.adamw)]
     raise ValueError("optimizer exposure is defined for AdamW and MuonAdamW only")
 

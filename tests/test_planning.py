@@ -197,3 +197,15 @@ def test_canary_fails_loudly_when_slow_or_incomplete(tmp_path):
         ThroughputCanary(1, 1.0, 0).observe({"step": 0, "prediction_tokens": 1, "seconds": 1.0})
     with pytest.raises(FileExistsError):
         ThroughputCanary(1, 1.0, 0, output_path=tmp_path / "short.json")
+
+
+def test_exposure_accepts_the_fused_adamw_kernel_optimizer():
+    """The CUDA trainer's AdamW (the fused multi-tensor kernel subclass) has the same exposure
+    record as torch's AdamW over the same groups."""
+    from tensor_train_ing_b200.optim import FusedAdamW
+    from tensor_train_ing_b200.train import optimizer_groups
+    model = TensorLM(ModelConfig(**TINY_MODEL))
+    plain = torch.optim.AdamW(optimizer_groups(model, 0.1), lr=0.01)
+    fused = FusedAdamW(optimizer_groups(model, 0.1), lr=0.01)
+    assert (update_optimizer_exposure({"steps": 0, "tokens": 0}, fused)
+            == update_optimizer_exposure({"steps": 0, "tokens": 0}, plain))
