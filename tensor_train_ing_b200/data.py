@@ -303,237 +303,224 @@ def _prepare(out, source_jsonl, revision, max_tokens, max_documents, tokenizer, 
 
 
 # ------------------------------------------------------------------------------------------ sampler
+class _RowArithmetic:
+    """Where the rows of a packed stream begin and end, computed without materialising them.
+
+    Rows hold ``width = context + 1`` tokens.  Documents are laid down in epoch order; a document
+    that reaches the end of a row with tokens left continues in the next row, whose first token
+    repeats the row's last one.  A document of ``length`` tokens entering a row that already holds
+    ``fill`` tokens either stays open (``length < width - fill``) or closes that row after
+    ``width - fill`` of its tokens and then one continuation row per further ``context`` tokens;
+    a remainder ``r > 0`` leaves an open row holding ``r + 1`` tokens (the repeated one included),
+    a zero remainder leaves no open row."""
+
+    def __init__(self, context: int, length_of):
+        self.context, self.width, self.length_of = context, context + 1, length_of
+
+    def after(self, length: int, rows: int, fill: int) -> tuple[int, int]:
+        """(completed rows, fill of the open row) after appending ``length`` tokens of one document."""
+        room = self.width - fill
+        if length < room:
+            return rows, fill + length
+        continuation, left = divmod(length - room, self.context)
+        return rows + 1 + continuation, (left + 1 if left else 0)
+
+    def after_documents(self, order, count=None) -> tuple[int, int]:
+        rows = fill = 0
+        for i in (order if count is None else order[:count]):
+            rows, fill = self.after(self.length_of(int(i)), rows, fill)
+        return rows, fill
+
+    def rows_in_epoch(self, order) -> int:
+        rows, fill = self.after_documents(order)
+        return rows + bool(fill)
+
+    def row_start(self, order, row: int) -> tuple[int, int]:
+        """(document position, token offset) at which row ``row`` begins; (len(order), 0) once the
+        epoch's rows are used up."""
+        rows = fill = 0
+        for d in range(len(order)):
+            if rows == row and fill == 0:
+                return d, 0
+            length = self.length_of(int(order[d]))
+            done, next_fill = self.after(length, rows, fill)
+            if rows < row <= done:  # an earlier row closes inside this document
+                consumed = (self.width - fill) + (row - rows - 1) * self.context
+                return (d, consumed - 1) if consumed < length else (d + 1, 0)
+            rows, fill = done, next_fill
+        if row == rows + bool(fill):
+            return len(order), 0
+        raise ValueError("invalid canonical row seek")
+
+    def row_holding(self, order, document: int, token: int) -> int:
+        """Index of the row in which token ``token`` of the document at position ``document`` first
+        appears (it may close that row and repeat at the start of the next)."""
+        rows, fill = self.after_documents(order, document)
+        return self.after(token + 1, rows, fill)[0]
+
+
 class PackedSampler:
-    """Deterministic epoch permutations, row packing and a resumable next-batch order."""
+    """Deterministic epoch permutations, row packing and a resumable next-batch order.
+
+    The stream position is (epoch, row cursor, document position, token offset); the last two are
+    where the next row begins and are always ``_RowArithmetic.row_start`` of the row cursor, which
+    ``load_state_dict`` checks.  A context fork restarts the stream at the new context's row holding
+    the old stream's next token; targets at or before that watermark are masked in the first row."""
 
     _STATE_KEYS = ("packing_version", "manifest_hash", "split", "batch_size", "context", "seed", "epoch", "cursor",
                    "document_cursor", "token_cursor")
+    _IDENTITY_KEYS = ("packing_version", "manifest_hash", "split", "batch_size", "context", "seed")
 
     def __init__(self, manifest, split="train", batch_size=1, context=512, seed=0):
         self.path = _manifest_path(manifest)
         self.manifest_hash = manifest_hash(self.path)
         self.manifest = json.loads(self.path.read_text())
-        root = self.path.parent
-        for name, expected in self.manifest["artifacts"].items():
-            if Path(name).name != name or _sha(root / name) != expected:
-                raise ValueError(f"artifact checksum mismatch: {name}")
-        if split not in self.manifest["tokens"] or batch_size <= 0 or context <= 0:
-            raise ValueError("invalid split or batch shape")
-        required = {"documents.jsonl", *(f"{s}.tokens.bin" for s in SPLIT_ORDER)}
-        if not required.issubset(self.manifest["artifacts"]):
-            raise ValueError("dataset manifest lacks required metadata/token artifacts")
-        if self.manifest.get("format_version") != 1:
-            raise ValueError("unsupported dataset format")
-        counts = self.manifest["tokens"]
-        if set(counts) != set(SPLIT_ORDER) or any(type(n) is not int or n < 0 for n in counts.values()):
-            raise ValueError("invalid dataset token counts")
-        for name, n in counts.items():
-            if (root / f"{name}.tokens.bin").stat().st_size != n * np.dtype(TOKEN_DTYPE).itemsize:
-                raise ValueError(f"token payload size mismatch: {name}")
+        self._check_dataset(split, batch_size, context)
         self.split, self.batch_size, self.context, self.seed = split, batch_size, context, seed
         from .sampler_index import load_sampler_index
+        root = self.path.parent
         self.docs = load_sampler_index(root, self.manifest, split)
         if len(self.docs) == 0:
             raise ValueError(f"empty split: {split}")
         self.tokens = read_split_tokens(root, split)
         self.packing_version = PACKING_VERSION
+        self._orders: dict[int, np.ndarray] = {}
         self.epoch = self.cursor = 0
-        self._order_epoch = None
-        self._new_epoch_order()
+        self._start_epoch()
         self._batch_mappings = []
-        self._context_transition = None
 
-    # ---------------------------------------------------------------- packing arithmetic
-    def _permutation(self, epoch):
-        if self._order_epoch == epoch:
-            return self.order
-        order = np.arange(len(self.docs), dtype=np.int64)
-        random.Random(f"{self.seed}:{epoch}").shuffle(order)
-        order.flags.writeable = False
+    def _check_dataset(self, split, batch_size, context):
+        root, manifest = self.path.parent, self.manifest
+        for name, expected in manifest["artifacts"].items():
+            if Path(name).name != name or _sha(root / name) != expected:
+                raise ValueError(f"artifact checksum mismatch: {name}")
+        if split not in manifest["tokens"] or batch_size <= 0 or context <= 0:
+            raise ValueError("invalid split or batch shape")
+        if not {"documents.jsonl", *(f"{s}.tokens.bin" for s in SPLIT_ORDER)} <= manifest["artifacts"].keys():
+            raise ValueError("dataset manifest lacks required metadata/token artifacts")
+        if manifest.get("format_version") != 1:
+            raise ValueError("unsupported dataset format")
+        counts = manifest["tokens"]
+        if set(counts) != set(SPLIT_ORDER) or any(type(n) is not int or n < 0 for n in counts.values()):
+            raise ValueError("invalid dataset token counts")
+        for name, n in counts.items():
+            if (root / f"{name}.tokens.bin").stat().st_size != n * np.dtype(TOKEN_DTYPE).itemsize:
+                raise ValueError(f"token payload size mismatch: {name}")
+
+    # ---------------------------------------------------------------- epochs and rows
+    @property
+    def _rows(self) -> _RowArithmetic:
+        return _RowArithmetic(self.context, self.docs.length)
+
+    def _order_of(self, epoch: int) -> np.ndarray:
+        """The epoch's document order: ``random.Random(f"{seed}:{epoch}")`` shuffles positions."""
+        order = self._orders.get(epoch)
+        if order is None:
+            order = np.arange(len(self.docs), dtype=np.int64)
+            random.Random(f"{self.seed}:{epoch}").shuffle(order)
+            order.flags.writeable = False
+            self._orders = {epoch: order}  # one epoch is live at a time
         return order
 
-    def _length(self, i):
-        return self.docs.length(i)
-
-    def _count_lengths(self, lengths, *, rows=0, fill=0):
-        """Rows completed (and the fill of the open row) after packing these document lengths."""
-        width = self.context + 1
-        for remaining in lengths:
-            capacity = width - fill
-            if remaining < capacity:
-                fill += remaining
-                continue
-            rows += 1
-            remaining -= capacity
-            fill = 0
-            if remaining:
-                remaining += 1  # the overlap token starts the next row
-                complete = (remaining - 1) // self.context
-                rows += complete
-                fill = remaining - complete * self.context
-                if complete and fill == 1:
-                    fill = 0
-        return rows, fill
-
-    def _epoch_rows(self, order):
-        rows, fill = self._count_lengths(self._length(i) for i in order)
-        return rows + bool(fill)
-
-    def _new_epoch_order(self):
+    def _start_epoch(self):
         self._context_transition = None
-        self.order = self._permutation(self.epoch)
-        self._order_epoch = self.epoch
-        self.epoch_row_count = self._epoch_rows(self.order)
+        self.order = self._order_of(self.epoch)
+        self.epoch_row_count = self._rows.rows_in_epoch(self.order)
         self.document_cursor = self.token_cursor = 0
 
-    def _prefix_count(self, order, document_cursor):
-        return self._count_lengths(self._length(i) for i in order[:document_cursor])
-
-    def _seek_row(self, order, cursor):
-        """(document, token) position at which canonical row ``cursor`` starts."""
-        d = t = 0
-        rows = fill = 0
-        remaining_rows = cursor
-        width = self.context + 1
-        while remaining_rows:
-            if d == len(order):
-                if fill and remaining_rows == 1:
-                    return d, 0
-                raise ValueError("invalid canonical row seek")
-            length = self._length(order[d])
-            remaining = length - t
-            if fill == 0 and remaining >= width:
-                count = min(remaining_rows, (remaining - 1) // self.context)
-                t += count * self.context
-                remaining_rows -= count
-                if t == length - 1:
-                    d, t = d + 1, 0
-                continue
-            capacity = width - fill
-            if remaining < capacity:
-                fill += remaining
-                d, t = d + 1, 0
-            else:
-                if remaining == capacity:
-                    d, t = d + 1, 0
-                else:
-                    t += capacity - 1
-                remaining_rows -= 1
-                fill = 0
-        return d, t
-
-    def _fork_position(self, source):
-        epoch, d, t = source["epoch"], source["document_cursor"], source["token_cursor"]
-        order = self._permutation(epoch)
-        if d == len(order):
-            epoch, d, t = epoch + 1, 0, 0
-            order = self._permutation(epoch)
-        rows, fill = self._prefix_count(order, d)
-        cursor, _ = self._count_lengths((t + 1,), rows=rows, fill=fill)
-        dc, tc = self._seek_row(order, cursor)
-        return epoch, cursor, dc, tc, d, t
-
-    def fork_context(self, context):
-        """New stream at a larger (or equal) context that continues after the consumed targets:
-        earlier inputs may replay as prefix but their targets are masked once."""
-        if type(context) is not int or context <= 0:
-            raise ValueError("context must be a positive integer")
-        original = PackedSampler.state_dict(self)
-        check = copy.copy(self)
-        PackedSampler.load_state_dict(check, original)
-        if context == self.context:
-            return check
-        transition = original.get("context_transition")
-        source = copy.deepcopy(transition["source_state"] if transition else original)
-        fork = copy.copy(self)
-        fork.context = context
-        fork._order_epoch = None
-        epoch, cursor, d, t, _, _ = fork._fork_position(source)
-        target = {**source, "context": context, "epoch": epoch, "cursor": cursor, "document_cursor": d,
-                  "token_cursor": t, "context_transition": {"version": 1, "source_context": source["context"],
-                                                            "source_state": source}}
-        PackedSampler.load_state_dict(fork, target)
-        return fork
-
-    # ---------------------------------------------------------------- batches
-    def _next_row(self):
-        row, fill = [], 0
-        width = self.context + 1
+    def _take_row(self) -> list[tuple[int, int, int]]:
+        """The next row's pieces (document index, first token in the split file, token count);
+        moves the document/token position to the next row's start."""
+        pieces, fill, width = [], 0, self.context + 1
         while self.document_cursor < len(self.order) and fill < width:
-            i = int(self.order[self.document_cursor])
-            length = self._length(i)
+            doc = int(self.order[self.document_cursor])
+            length = self.docs.length(doc)
             count = min(width - fill, length - self.token_cursor)
-            row.append((i, self.docs.start(i) + self.token_cursor, count))
+            pieces.append((doc, self.docs.start(doc) + self.token_cursor, count))
             fill += count
             self.token_cursor += count
             if self.token_cursor == length:
-                self.document_cursor += 1
-                self.token_cursor = 0
+                self.document_cursor, self.token_cursor = self.document_cursor + 1, 0
             elif fill == width:
-                self.token_cursor -= 1
-        return row
+                self.token_cursor -= 1  # repeated as the next row's first token
+        return pieces
+
+    def _advance(self):
+        """Take one row (rolling over to the next epoch first if needed); returns (pieces, pending
+        context transition, document position where the row began)."""
+        if self.cursor >= self.epoch_row_count:
+            self.epoch, self.cursor = self.epoch + 1, 0
+            self._start_epoch()
+        transition, first_document = self._context_transition, self.document_cursor
+        pieces = self._take_row()
+        self._context_transition = None
+        self.cursor += 1
+        return pieces, transition, first_document
+
+    # ---------------------------------------------------------------- batches
+    def _row_contents(self, pieces):
+        """(token list, document id list, per-piece mapping records) of one row."""
+        tokens, doc_ids, mappings = [], [], []
+        for doc, start, count in pieces:
+            rec = self.docs[doc]
+            packed = len(tokens)
+            offset = start - rec["token_start"]
+            mappings.append({"document_id": rec["id"], "numeric_id": rec["numeric_id"],
+                             "content_sha256": rec["content_sha256"], "processed_sha256": rec["processed_sha256"],
+                             "source_offset": rec["source_offset"],
+                             "synthetic_eos_token_offset": rec["synthetic_eos_token_offset"],
+                             "processed_document_token_count": rec["processed_token_end"],
+                             "packed_token_start": packed, "packed_token_end": packed + count,
+                             "source_token_start": offset, "source_token_end": offset + count})
+            tokens.extend(self.tokens[start:start + count].tolist())
+            doc_ids.extend([self.docs.numeric_id(doc)] * count)
+        return tokens, doc_ids, mappings
 
     def next_batch(self):
-        idx = torch.full((self.batch_size, self.context), EOS, dtype=torch.long)
-        ids = torch.full_like(idx, -1)
-        targets = torch.full_like(idx, -100)
+        """(inputs, document ids, targets), each [batch_size, context]; padding uses EOS inputs,
+        distinct negative document ids and -100 targets; targets never cross documents."""
+        shape = (self.batch_size, self.context)
+        idx = torch.full(shape, EOS, dtype=torch.long)
+        ids = torch.full(shape, -1, dtype=torch.long)
+        targets = torch.full(shape, -100, dtype=torch.long)
         self._batch_mappings = []
         for b in range(self.batch_size):
-            if self.cursor >= self.epoch_row_count:
-                self.epoch += 1
-                self.cursor = 0
-                self._new_epoch_order()
-            transition = self._context_transition
-            row_start_document = self.document_cursor
-            row = self._next_row()
-            self._context_transition = None
-            self.cursor += 1
-            tok, docids, mappings = [], [], []
-            for i, start, count in row:
-                doc = self.docs[i]
-                packed_start = len(tok)
-                mappings.append({"document_id": doc["id"], "numeric_id": doc["numeric_id"],
-                                 "content_sha256": doc["content_sha256"], "processed_sha256": doc["processed_sha256"],
-                                 "source_offset": doc["source_offset"],
-                                 "synthetic_eos_token_offset": doc["synthetic_eos_token_offset"],
-                                 "processed_document_token_count": doc["processed_token_end"],
-                                 "packed_token_start": packed_start, "packed_token_end": packed_start + count,
-                                 "source_token_start": start - doc["token_start"],
-                                 "source_token_end": start - doc["token_start"] + count})
-                tok.extend(self.tokens[start:start + count].tolist())
-                docids.extend([self.docs.numeric_id(i)] * count)
-            self._batch_mappings.append({"epoch": self.epoch, "row_cursor": self.cursor - 1,
-                                         "input_length": min(self.context, len(tok)), "ranges": mappings})
-            n = min(self.context, len(tok))
-            token_row = torch.tensor(tok, dtype=torch.long)
-            doc_row = torch.tensor(docids, dtype=torch.long)
-            idx[b, :n] = token_row[:n]
-            ids[b, :n] = doc_row[:n]
-            pairs = min(self.context, len(tok) - 1)
-            if pairs > 0:
-                same = doc_row[:pairs] == doc_row[1:pairs + 1]
-                targets[b, :pairs] = torch.where(same, token_row[1:pairs + 1], -100)
+            pieces, transition, first_document = self._advance()
+            tokens, doc_ids, mappings = self._row_contents(pieces)
+            n = min(self.context, len(tokens))
+            self._batch_mappings.append({"epoch": self.epoch, "row_cursor": self.cursor - 1, "input_length": n,
+                                         "ranges": mappings})
+            row_tokens = torch.tensor(tokens, dtype=torch.long)
+            row_docs = torch.tensor(doc_ids, dtype=torch.long)
+            idx[b, :n], ids[b, :n] = row_tokens[:n], row_docs[:n]
+            scored = min(self.context, len(tokens) - 1)
+            if scored > 0:
+                same = row_docs[:scored] == row_docs[1:scored + 1]
+                targets[b, :scored] = torch.where(same, row_tokens[1:scored + 1], -100)
             if transition is not None:
-                self._mask_replayed(b, n, targets, mappings, row_start_document, transition)
+                self._mask_replayed(b, n, targets, mappings, first_document, transition)
             if n < self.context:
                 ids[b, n:] = -torch.arange(1, self.context - n + 1)
         return idx, ids, targets
 
-    def _mask_replayed(self, b, n, targets, mappings, row_start_document, transition):
-        _, _, _, _, frontier_doc, frontier_tok = self._fork_position(transition["source_state"])
-        exposure = {"prefix_tokens_at_or_before_watermark": 0, "masked_prediction_targets": 0}
+    def _mask_replayed(self, b, n, targets, mappings, first_document, transition):
+        """First row after a context fork: mask targets at or before the old stream's watermark and
+        count the replayed inputs and masked targets."""
+        *_, mark_document, mark_token = self._fork_position(transition["source_state"])
+
+        def seen(position, offset):
+            return position < mark_document or (position == mark_document and offset <= mark_token)
+        replayed = masked = 0
         for k, m in enumerate(mappings):
-            position = row_start_document + k
-            for packed in range(m["packed_token_start"], min(n, m["packed_token_end"])):
-                off = m["source_token_start"] + packed - m["packed_token_start"]
-                if position < frontier_doc or (position == frontier_doc and off <= frontier_tok):
-                    exposure["prefix_tokens_at_or_before_watermark"] += 1
-            for packed in range(m["packed_token_start"], min(self.context, m["packed_token_end"] - 1)):
-                toff = m["source_token_start"] + packed - m["packed_token_start"] + 1
-                if position < frontier_doc or (position == frontier_doc and toff <= frontier_tok):
-                    exposure["masked_prediction_targets"] += int(targets[b, packed] != -100)
-                    targets[b, packed] = -100
-        self._batch_mappings[-1]["context_fork_exposure"] = exposure
+            position, first = first_document + k, m["packed_token_start"]
+            base = m["source_token_start"] - first
+            replayed += sum(seen(position, base + col) for col in range(first, min(n, m["packed_token_end"])))
+            for col in range(first, min(self.context, m["packed_token_end"] - 1)):
+                if seen(position, base + col + 1):
+                    masked += int(targets[b, col] != -100)
+                    targets[b, col] = -100
+        self._batch_mappings[-1]["context_fork_exposure"] = {"prefix_tokens_at_or_before_watermark": replayed,
+                                                             "masked_prediction_targets": masked}
 
     def batch_mappings(self):
         return copy.deepcopy(self._batch_mappings)
@@ -547,6 +534,41 @@ class PackedSampler:
     def __iter__(self):
         return self
 
+    # ---------------------------------------------------------------- context forks
+    def _fork_position(self, source):
+        """(epoch, row cursor, row start document, row start token, watermark document, watermark
+        token) of this sampler's context resuming after ``source``'s consumed targets."""
+        epoch, mark_document, mark_token = source["epoch"], source["document_cursor"], source["token_cursor"]
+        order = self._order_of(epoch)
+        if mark_document == len(order):  # the source had finished its epoch
+            epoch, mark_document, mark_token = epoch + 1, 0, 0
+            order = self._order_of(epoch)
+        rows = self._rows
+        cursor = rows.row_holding(order, mark_document, mark_token)
+        start_document, start_token = rows.row_start(order, cursor)
+        return epoch, cursor, start_document, start_token, mark_document, mark_token
+
+    def fork_context(self, context):
+        """A stream at a larger (or equal) context that continues after the consumed targets:
+        earlier inputs may replay as prefix, but their targets are masked once."""
+        if type(context) is not int or context <= 0:
+            raise ValueError("context must be a positive integer")
+        current = PackedSampler.state_dict(self)
+        same = copy.copy(self)
+        PackedSampler.load_state_dict(same, current)
+        if context == self.context:
+            return same
+        pending = current.get("context_transition")
+        source = copy.deepcopy(pending["source_state"] if pending else current)
+        fork = copy.copy(self)
+        fork.context = context
+        epoch, cursor, document, token, _, _ = fork._fork_position(source)
+        PackedSampler.load_state_dict(fork, {
+            **source, "context": context, "epoch": epoch, "cursor": cursor, "document_cursor": document,
+            "token_cursor": token,
+            "context_transition": {"version": 1, "source_context": source["context"], "source_state": source}})
+        return fork
+
     # ---------------------------------------------------------------- state
     def state_dict(self):
         state = {k: getattr(self, k) for k in self._STATE_KEYS}
@@ -554,55 +576,42 @@ class PackedSampler:
             state["context_transition"] = copy.deepcopy(self._context_transition)
         return state
 
+    def _check_transition(self, transition, position):
+        if (not isinstance(transition, dict) or set(transition) != {"version", "source_context", "source_state"}
+                or transition["version"] != 1):
+            raise ValueError("invalid context transition schema")
+        source, source_context = transition["source_state"], transition["source_context"]
+        if (type(source_context) is not int or source_context <= 0 or not isinstance(source, dict)
+                or source.get("context") != source_context or set(source) != set(self._STATE_KEYS)):
+            raise ValueError("invalid context transition source")
+        at_source = copy.copy(self)
+        at_source.context, at_source._context_transition = source_context, None
+        PackedSampler.load_state_dict(at_source, source)
+        if position != self._fork_position(source)[:4]:
+            raise ValueError("context transition cursor mismatch")
+
     def load_state_dict(self, state):
-        for k in ("packing_version", "manifest_hash", "split", "batch_size", "context", "seed"):
+        for k in self._IDENTITY_KEYS:
             if state.get(k) != getattr(self, k):
                 raise ValueError(f"sampler state mismatch: {k}")
-        epoch, cursor = state["epoch"], state["cursor"]
-        dcur, tcur = state["document_cursor"], state["token_cursor"]
-        if any(type(v) is not int or v < 0 for v in (epoch, cursor, dcur, tcur)):
+        position = tuple(state[k] for k in ("epoch", "cursor", "document_cursor", "token_cursor"))
+        if any(type(v) is not int or v < 0 for v in position):
             raise ValueError("invalid sampler cursor")
-        self_order_epoch = self._order_epoch
-        self._order_epoch = None
-        order = self._permutation(epoch)
-        self._order_epoch = self_order_epoch
-        rows_total = self._epoch_rows(order)
-        if cursor > rows_total or dcur > len(order):
+        epoch, cursor, document, token = position
+        order = self._order_of(epoch)
+        rows = self._rows
+        total = rows.rows_in_epoch(order)
+        if cursor > total or document > len(order):
             raise ValueError("invalid sampler cursor")
-        if dcur == len(order):
-            if tcur != 0 or cursor != rows_total:
-                raise ValueError("inconsistent completed epoch cursor")
-        else:
-            length = self._length(order[dcur])
-            if tcur >= length or cursor == rows_total:
-                raise ValueError("invalid document token cursor")
-            rows, fill = self._prefix_count(order, dcur)
-            at_start = tcur == 0 and fill == 0 and rows == cursor
-            if not at_start:
-                rows, fill = self._count_lengths((tcur + 1,), rows=rows, fill=fill)
-                if tcur >= length - 1 or fill != 0 or rows != cursor:
-                    raise ValueError("inconsistent row/document/token cursors")
+        if document < len(order) and token >= self.docs.length(int(order[document])):
+            raise ValueError("invalid document token cursor")
+        if rows.row_start(order, cursor) != (document, token):
+            raise ValueError("inconsistent row/document/token cursors")
         transition = copy.deepcopy(state.get("context_transition"))
         if transition is not None:
-            if (not isinstance(transition, dict) or set(transition) != {"version", "source_context", "source_state"}
-                    or transition["version"] != 1):
-                raise ValueError("invalid context transition schema")
-            source, sctx = transition["source_state"], transition["source_context"]
-            if (type(sctx) is not int or sctx <= 0 or not isinstance(source, dict)
-                    or source.get("context") != sctx or set(source) != set(self._STATE_KEYS)):
-                raise ValueError("invalid context transition source")
-            checker = copy.copy(self)
-            checker.context = sctx
-            checker._context_transition = None
-            checker._order_epoch = None
-            PackedSampler.load_state_dict(checker, source)
-            probe = copy.copy(self)
-            probe._order_epoch = None
-            if (epoch, cursor, dcur, tcur) != probe._fork_position(source)[:4]:
-                raise ValueError("context transition cursor mismatch")
-        self.epoch, self.order, self.epoch_row_count = epoch, order, rows_total
-        self._order_epoch = epoch
-        self.cursor, self.document_cursor, self.token_cursor = cursor, dcur, tcur
+            self._check_transition(transition, position)
+        self.epoch, self.order, self.epoch_row_count = epoch, self._order_of(epoch), total
+        self.cursor, self.document_cursor, self.token_cursor = cursor, document, token
         self._context_transition = transition
         self._batch_mappings = []
 
@@ -619,20 +628,14 @@ class RankPackedSampler(PackedSampler):
         self.rank, self.world_size = rank, world_size
         super().__init__(manifest, split=split, batch_size=batch_size, context=context, seed=seed)
 
-    def _skip_rows(self, count):
-        for _ in range(count):
-            if self.cursor >= self.epoch_row_count:
-                self.epoch += 1
-                self.cursor = 0
-                self._new_epoch_order()
-            self._next_row()
-            self._context_transition = None
-            self.cursor += 1
+    def _skip(self, rows: int):
+        for _ in range(rows):
+            self._advance()
 
     def next_batch(self):
-        self._skip_rows(self.rank * self.batch_size)
+        self._skip(self.rank * self.batch_size)
         batch = super().next_batch()
-        self._skip_rows((self.world_size - self.rank - 1) * self.batch_size)
+        self._skip((self.world_size - self.rank - 1) * self.batch_size)
         return batch
 
     __next__ = next_batch

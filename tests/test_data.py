@@ -108,3 +108,23 @@ def test_parallel_tokenization_is_byte_identical(tmp_path):
         root = m.parent if m.is_file() else m
         outs.append({p.name: p.read_bytes() for p in root.iterdir() if p.is_file() and p.name != "manifest.json"})
     assert outs[0] == outs[1]
+
+
+@pytest.mark.parametrize("context", [1, 2, 3, 5, 8, 13])
+def test_row_arithmetic_matches_the_materialised_stream(dataset, context):
+    """Row counts and row starts computed in closed form agree with the rows actually taken, and
+    every token of every document appears as a fresh (non-repeated) input exactly once per epoch."""
+    s = PackedSampler(dataset, batch_size=1, context=context, seed=5)
+    rows = s._rows
+    fresh = {}
+    for row in range(s.epoch_row_count):
+        assert (s.document_cursor, s.token_cursor) == rows.row_start(s.order, row) and s.cursor == row
+        s.next_batch()
+        for m in s.batch_mappings()[0]["ranges"]:
+            first = m["source_token_start"] + (1 if fresh.get(m["document_id"], 0) > m["source_token_start"] else 0)
+            for off in range(first, m["source_token_end"]):
+                assert fresh.get(m["document_id"], 0) == off
+                fresh[m["document_id"]] = off + 1
+    assert (s.document_cursor, s.token_cursor) == (len(s.order), 0)
+    assert rows.row_start(s.order, s.epoch_row_count) == (len(s.order), 0)
+    assert all(fresh[s.docs[int(i)]["id"]] == s.docs.length(int(i)) for i in s.order)
