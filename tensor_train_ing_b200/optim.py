@@ -216,11 +216,26 @@ class FusedAdamW(torch.optim.AdamW):
         super().__init__(params, lr=lr, betas=betas, eps=eps, weight_decay=weight_decay, fused=True)
         self._tables: dict[int, tuple] = {}
 
+    def load_state_dict(self, state_dict):
+        """torch's load, then this optimizer's own layout: fused groups and every state tensor
+        (the ``step`` counters included, which torch keeps on the host for a state saved by a
+        non-fused AdamW) on its parameter's device, where the kernel reads them."""
+        super().load_state_dict(state_dict)
+        for group in self.param_groups:
+            group.update(fused=True, foreach=None, capturable=False)
+            for p in group["params"]:
+                st = self.state.get(p)
+                if st and "step" in st:
+                    st["step"] = st["step"].to(device=p.device, dtype=torch.float32)
+        self._tables = {}
+
     def _table(self, index, params, caches):
         rows, chunk = [], 16384
         first = 0
         for p in params:
             st = self.state[p]
+            if any(st[k].device != p.device for k in ("step", "exp_avg", "exp_avg_sq")):
+                raise ValueError("FusedAdamW state must live on its parameter's device")
             cache = caches.get(id(p)) if caches else None
             rows.append([p.data_ptr(), p.grad.data_ptr(), st["exp_avg"].data_ptr(), st["exp_avg_sq"].data_ptr(),
                          st["step"].data_ptr(), cache.data_ptr() if cache is not None else 0, p.numel(), first])

@@ -7,6 +7,8 @@
   three steps on wide, tall and square matrices: momentum buffers within rtol 1e-6 (identical fp32
   lerps); parameters within 2 % of the accumulated update's norm (the Newton-Schulz GEMMs round
   bf16 products in another order than cuBLAS).
+* FusedAdamW resumes a state saved by torch's non-fused AdamW (host step counters) and then
+  matches torch's AdamW resumed from the same state.
 * MuonAdamW writes the updated bf16 operand caches, which then equal a fresh conversion of the
   fp32 weights bit for bit.
 """
@@ -48,6 +50,40 @@ def test_fused_adamw_matches_torch_adamw(scaled):
     # the state dict is torch AdamW's: it loads into a torch optimizer unchanged
     torch.optim.AdamW(groups([q.detach().clone().requires_grad_(True) for q in ref]), lr=3e-3).load_state_dict(
         opt.state_dict())
+
+
+def test_fused_adamw_resumes_a_host_counter_adamw_state():
+    """A state saved by torch's default (non-fused) AdamW keeps its step counters on the host; loaded
+    into FusedAdamW they move to the device, and the next steps match torch's AdamW resumed from the
+    same state."""
+    from tensor_train_ing_b200.optim import FusedAdamW
+    shapes = [(300, 70), (512,)]
+    torch.manual_seed(3)
+    base = [torch.randn(s, device="cuda") for s in shapes]
+    first = [b.clone().requires_grad_(True) for b in base]
+    donor = torch.optim.AdamW([{"params": first, "weight_decay": 0.1}], lr=2e-3, foreach=False)
+    grads = _grads(shapes, 4, seed=7)
+    for p, g in zip(first, grads[0]):
+        p.grad = g.clone()
+    donor.step()
+    saved = donor.state_dict()
+    assert all(st["step"].device.type == "cpu" for st in saved["state"].values())
+    ours = [p.detach().clone().requires_grad_(True) for p in first]
+    ref = [p.detach().clone().requires_grad_(True) for p in first]
+    opt = FusedAdamW([{"params": ours, "weight_decay": 0.1}], lr=2e-3)
+    opt.load_state_dict(saved)
+    topt = torch.optim.AdamW([{"params": ref, "weight_decay": 0.1}], lr=2e-3, foreach=False)
+    topt.load_state_dict(saved)
+    assert all(opt.state[p]["step"].is_cuda for p in ours) and opt.param_groups[0]["fused"] is True
+    for step_grads in grads[1:]:
+        for p, q, g in zip(ours, ref, step_grads):
+            p.grad, q.grad = g.clone(), g.clone()
+        opt.step()
+        topt.step()
+    torch.cuda.synchronize()
+    for p, q in zip(ours, ref):
+        torch.testing.assert_close(p, q, rtol=1e-5, atol=1e-6)
+        assert float(opt.state[p]["step"]) == float(topt.state[q]["step"]) == 4.0
 
 
 @pytest.mark.parametrize("shape", [(256, 1024), (1024, 256), (512, 512)])
