@@ -141,7 +141,8 @@ def _distributed_run(cfg, args):
                                            cooldown_steps=getattr(args, "cooldown_steps", None),
                                            cooldown_end_tokens=getattr(args, "cooldown_end_tokens", None),
                                            run_budget_usd=args.run_budget_usd,
-                                           export_max_state_bytes=args.export_max_state_bytes)
+                                           export_max_state_bytes=args.export_max_state_bytes,
+                                           checkpoint_format=args.checkpoint_format)
         return result if dist.get_rank() == 0 else None
     finally:
         if owned:
@@ -248,6 +249,8 @@ def _parser():
         p.add_argument("--context-fork", action="store_true")
         p.add_argument("--distributed", action="store_true", help="one process per GPU under torchrun")
         p.add_argument("--export-max-state-bytes", type=int)
+        p.add_argument("--checkpoint-format", default="ttb-sharded-v1", choices=["ttb-sharded-v1", "tnlm-dcp-v1"],
+                       help="format of --distributed recovery checkpoints (tnlm-dcp-v1: the reference's)")
         p.add_argument("--collective-timeout-seconds", type=float, default=120.0)
         if name == "branch":
             p.add_argument("--batch-tokens", type=int, required=True)
@@ -492,6 +495,8 @@ def main(argv=None):
         else:
             if args.export_max_state_bytes is not None:
                 raise ValueError("--export-max-state-bytes is for --distributed; full-state checkpoints already evaluate")
+            if args.checkpoint_format != "ttb-sharded-v1":
+                raise ValueError("--checkpoint-format selects --distributed checkpoints; serial runs write full-state ones")
             result = train_run(cfg, args.run_dir, max_steps=args.max_steps, max_seconds=args.max_seconds,
                                device=args.device, resume=args.resume, run_budget_usd=args.run_budget_usd,
                                context_fork=args.context_fork, cooldown_steps=getattr(args, "cooldown_steps", None),

@@ -21,6 +21,7 @@ import hashlib
 import json
 import shutil
 import time
+from functools import partial
 from pathlib import Path
 
 import torch
@@ -36,12 +37,13 @@ from .distributed_checkpoint import (_agree, _phase, export_distributed_weights,
 from .models.model import TensorLM
 from .models.shapes import needs_parameter_sharding
 from .models.normalization import lagged_modules, spectral_step
-from .optim import make_optimizer
 from .optimizer_exposure import update_optimizer_exposure
 from .parallel.sharded import ShardedDataParallel
+from .reference_dcp import (is_reference_checkpoint, load_reference_checkpoint, read_reference_manifest,
+                            save_reference_checkpoint)
 from .runtime import determinism_metadata, full_config, resume_validator, seed_all
 from .schedules import lr_multiplier, schedule_multiplier, schedule_steps, validate_schedule
-from .train import _mask_to_count, _validate_batch
+from .train import _mask_to_count, _validate_batch, make_optimizer
 from .training_stability import BatchScoreBounds, StabilityPolicy
 from .training_taper import TaperLifecycle, validate_taper_config
 
@@ -55,10 +57,17 @@ def _words_digest(words) -> str:
     return b"".join(int(w).to_bytes(8, "little", signed=True) for w in words).hex()
 
 
+CHECKPOINT_FORMATS = ("ttb-sharded-v1", "tnlm-dcp-v1")
+
+
 def distributed_train_run(cfg, run_dir, *, max_steps, max_seconds, device="cuda", resume=None, cooldown_steps=None,
                           cooldown_end_tokens=None, run_budget_usd=None, export_max_state_bytes=None,
-                          context_fork=False):
-    """Train up to ``max_steps`` new updates on every rank of the initialised process group."""
+                          context_fork=False, checkpoint_format="ttb-sharded-v1"):
+    """Train up to ``max_steps`` new updates on every rank of the initialised process group.
+
+    ``resume`` may name a checkpoint of either sharded format; ``checkpoint_format`` chooses the
+    format of the checkpoints this run writes (``tnlm-dcp-v1`` is the reference's, which its own
+    distributed trainer resumes)."""
     from .data import RankPackedSampler, batch_hash, manifest_hash as hash_manifest
     if not dist.is_initialized():
         raise ValueError("distributed_train_run requires an initialized process group")
@@ -95,8 +104,10 @@ def distributed_train_run(cfg, run_dir, *, max_steps, max_seconds, device="cuda"
         if cooldown_end_tokens is not None and (type(cooldown_end_tokens) is not int or cooldown_end_tokens <= 0
                                                 or cooldown_steps is None):
             raise ValueError("cooldown_end_tokens requires a positive integer and cooldown_steps")
-        if resume is not None and not is_distributed_checkpoint(resume):
+        if resume is not None and not (is_distributed_checkpoint(resume) or is_reference_checkpoint(resume)):
             raise ValueError("distributed resume needs a sharded checkpoint of the same world size")
+        if checkpoint_format not in CHECKPOINT_FORMATS:
+            raise ValueError(f"checkpoint_format must be one of {CHECKPOINT_FORMATS}")
         dev = torch.device(device)
         if dev.type == "cuda" and not torch.cuda.is_available():
             raise RuntimeError("CUDA requested but unavailable")
@@ -113,7 +124,9 @@ def distributed_train_run(cfg, run_dir, *, max_steps, max_seconds, device="cuda"
     parent_manifest = None
     old_context = data.get("context", 512)
     if resume is not None:
-        parent_manifest = _phase("parent manifest", lambda: read_distributed_manifest(resume))
+        parent_manifest = _phase("parent manifest", lambda: (read_reference_manifest(resume)
+                                                             if is_reference_checkpoint(resume)
+                                                             else read_distributed_manifest(resume)))
         _phase("parent config validation", lambda: resume_validator(cfg, context_fork=context_fork)(parent_manifest["config"]))
         old_context = parent_manifest["config"].get("data", {}).get("context", 512)
     ledger = SpendLedger(project.get("spend_ledger", "runs/spend.json"), project.get("total_budget_usd", 1000),
@@ -176,10 +189,14 @@ def distributed_train_run(cfg, run_dir, *, max_steps, max_seconds, device="cuda"
         parent = None
         previous = {}
         if resume is not None:
-            loaded = load_distributed_checkpoint(resume, model, optimizer, sampler, dp,
-                                                 expected_manifest_hash=manifest_hash,
-                                                 config_validator=resume_validator(cfg, context_fork=context_fork))
+            loader = (partial(load_reference_checkpoint, logical=logical) if is_reference_checkpoint(resume)
+                      else load_distributed_checkpoint)
+            loaded = loader(resume, model, optimizer, sampler, dp, expected_manifest_hash=manifest_hash,
+                            config_validator=resume_validator(cfg, context_fork=context_fork))
             progress.update(loaded["progress"])
+            if loaded.get("config_compatibility", {}).get("defaulted_fields"):
+                progress.setdefault("config_compatibility_history", []).append(
+                    {"checkpoint": str(Path(resume).resolve()), **loaded["config_compatibility"]})
             progress["world_size"] = world
             previous = progress.get("distributed_schedule", {}) or {}
             parent = {"path": str(Path(resume).resolve()),
@@ -229,6 +246,10 @@ def distributed_train_run(cfg, run_dir, *, max_steps, max_seconds, device="cuda"
         every = int(project.get("checkpoint_every_steps", 0))
 
         def save(name):
+            if checkpoint_format == "tnlm-dcp-v1":
+                return save_reference_checkpoint(run_dir / name, model, optimizer, sampler, dp, logical=logical,
+                                                 config=full_config(cfg), progress=progress,
+                                                 manifest_hash=manifest_hash, parent=parent)
             return save_distributed_checkpoint(run_dir / name, model, optimizer, sampler, dp,
                                                config=full_config(cfg), progress=progress, manifest_hash=manifest_hash,
                                                parent=parent,

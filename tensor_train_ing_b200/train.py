@@ -53,27 +53,30 @@ MAX_EMPTY_BATCHES = 100
 
 
 # ====================================================================================== optimizer
-def optimizer_groups(model, weight_decay):
+def optimizer_groups(model, weight_decay, only: set[int] | None = None):
     """The reference's plain AdamW grouping: decay on block matrices, none on the vocabulary
-    matrices and small parameters (the checkpointed optimizer layout depends on it)."""
+    matrices and small parameters, each group in parameter order (the checkpointed optimizer layout
+    depends on it).  ``only``: keep these parameter ids (a rank's owned parameters); both groups
+    are kept even when empty."""
     vocab = {id(model.embed.weight), id(model.unembed.weight)}
     decay, plain = [], []
     for name, p in model.named_parameters():
-        if p.requires_grad:
+        if p.requires_grad and (only is None or id(p) in only):
             (decay if hidden_matrix(name, p) and id(p) not in vocab else plain).append(p)
     return [{"params": decay, "weight_decay": weight_decay}, {"params": plain, "weight_decay": 0.0}]
 
 
-def make_optimizer(model, cfg):
-    """The trainer's optimizer: plain AdamW grouping (the fused multi-tensor kernel on CUDA), or
-    the width-scaling / Muon builder."""
+def make_optimizer(model, cfg, only: set[int] | None = None):
+    """The trainers' optimizer: plain AdamW grouping (the fused multi-tensor kernel on CUDA), or
+    the width-scaling / Muon builder.  ``only``: over a rank's owned parameters, with the same groups."""
     if cfg.optimizer == "muon" or getattr(getattr(model, "cfg", None), "width_scaling_base", None) is not None:
         from .optim import make_optimizer as scaling_optimizer
-        return scaling_optimizer(model, cfg)
+        return scaling_optimizer(model, cfg, only=only)
     if cfg.optimizer != "adamw":
         raise ValueError("optimizer must be adamw or muon")
-    groups = optimizer_groups(model, cfg.weight_decay_hidden)
-    if all(p.is_cuda for p in model.parameters()):
+    groups = optimizer_groups(model, cfg.weight_decay_hidden, only)
+    params = [p for g in groups for p in g["params"]]
+    if params and all(p.is_cuda for p in params):
         return FusedAdamW(groups, lr=cfg.lr, betas=(cfg.beta1, cfg.beta2))
     return torch.optim.AdamW(groups, lr=cfg.lr, betas=(cfg.beta1, cfg.beta2))
 
