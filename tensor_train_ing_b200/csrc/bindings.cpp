@@ -53,7 +53,7 @@ ttb::Operand b_operand(const Tensor& b) {
 // out = alpha * (a @ b + bias) + beta * c     (out/c: bf16 or fp32, row-major rows)
 // With b2: out = alpha * (a @ cat(b, b2) + bias) + beta * c, the contraction concatenated in one pass.
 void mm(const Tensor& a, const Tensor& b, Tensor& out, const c10::optional<Tensor>& c, double alpha, double beta,
-        const c10::optional<Tensor>& bias, const c10::optional<Tensor>& b2) {
+        const c10::optional<Tensor>& bias, const c10::optional<Tensor>& b2, int64_t tile_n) {
   const c10::cuda::CUDAGuard guard(a.device());
   const auto A = a_operand(a);
   const auto B = b_operand(b);
@@ -89,7 +89,7 @@ void mm(const Tensor& a, const Tensor& b, Tensor& out, const c10::optional<Tenso
   }
   ttb::gemm_linear(A, B, M, N, K, out.data_ptr(), out.stride(0), out.scalar_type() == torch::kFloat32, cp, ldc,
                    c_f32, static_cast<float>(alpha), static_cast<float>(beta), bp, cur_stream(),
-                   b2.has_value() ? &B2 : nullptr, k_split);
+                   b2.has_value() ? &B2 : nullptr, k_split, static_cast<int>(tile_n));
 }
 
 // qkv = x w^T with the rotary embedding applied to the first rope_cols columns
@@ -657,7 +657,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.doc() = "tensor_train_ing_b200 sm_100a kernels (tcgen05 / TMEM / TMA)";
   m.def("mm", &mm, "out = alpha*(a@b + bias) + beta*c on the tcgen05 GEMM", py::arg("a"), py::arg("b"),
         py::arg("out"), py::arg("c") = py::none(), py::arg("alpha") = 1.0, py::arg("beta") = 0.0,
-        py::arg("bias") = py::none(), py::arg("b2") = py::none());
+        py::arg("bias") = py::none(), py::arg("b2") = py::none(), py::arg("tile_n") = 0);
   m.def("bilinear", &bilinear, "dual-B GEMM forming the bilinear hidden layer");
   m.def("bilinear_grad", &bilinear_grad, "dH GEMM fused with the bilinear backward");
   m.def("status", &status, "read and clear the device error word (bounded-wait timeouts)");

@@ -17,10 +17,12 @@ struct Operand {
 
 // D[M,N] = alpha * (A B^T + bias) + beta * C.  With b2 the contraction is concatenated: B rows
 // [0, k_split) come from b and [k_split, K) from b2 (k_split a multiple of 64), so
-// A[:, :k_split] b^T + A[:, k_split:] b2^T accumulates in one pass.
+// A[:, :k_split] b^T + A[:, k_split:] b2^T accumulates in one pass.  tile_n picks the output tile
+// width (128: six K stages; 256: four); 0 takes 128 for N <= 128 and 256 otherwise.  Each output
+// element accumulates its K blocks in the same order either way.
 void gemm_linear(const Operand& a, const Operand& b, int M, int N, int K, void* D, long long ldd, bool d_f32,
                  const void* C, long long ldc, bool c_f32, float alpha, float beta, const float* bias,
-                 cudaStream_t stream, const Operand* b2 = nullptr, int k_split = 0);
+                 cudaStream_t stream, const Operand* b2 = nullptr, int k_split = 0, int tile_n = 0);
 
 // l = x Wl^T (+bl), r = x Wr^T (+br), H = l*r (mode 0) or silu(l)*r (mode 1); all [M, N] bf16 with row stride ld.
 void gemm_bilinear(const Operand& x, const Operand& wl, const Operand& wr, int M, int N, int K, void* H, void* Lo,

@@ -11,10 +11,11 @@ namespace ttb {
 
 void gemm_linear(const Operand& a, const Operand& b, int M, int N, int K, void* D, long long ldd, bool d_f32,
                  const void* C, long long ldc, bool c_f32, float alpha, float beta, const float* bias,
-                 cudaStream_t stream, const Operand* b2, int k_split) {
+                 cudaStream_t stream, const Operand* b2, int k_split, int tile_n) {
   TTB_CHECK(M > 0 && N > 0 && K > 0, "empty GEMM");
+  TTB_CHECK(tile_n == 0 || tile_n == 128 || tile_n == 256, "GEMM tile width must be 0 (automatic), 128 or 256");
   const gemm::Shape shape{M, N, K, status_ptr(), b2 != nullptr ? k_split : 0};
-  if (N <= 128) {
+  if (tile_n == 128 || (tile_n == 0 && N <= 128)) {
     gemm::EpiLinear<128> epi{D, ldd, d_f32, C, ldc, c_f32, alpha, beta, bias, M, N};
     gemm::dispatch<128, 6, false>(a, b, b2, shape, epi, stream);
   } else {

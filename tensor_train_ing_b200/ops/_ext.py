@@ -7,6 +7,7 @@ every fused op of this package runs only on these kernels.
 from __future__ import annotations
 
 import importlib
+import os
 
 _C = None
 _ERR: Exception | None = None
@@ -92,6 +93,10 @@ def lib():
             "tensor_train_ing_b200._C (the sm_100a kernel library) is not built or failed to load: "
             f"{e!r}. Build it with `python setup.py build_ext --inplace`.") from e
     _PROXY = _Counting(_C)
+    tuning = os.environ.get("TTB_TUNING")
+    if tuning:  # a table written by ``python -m tensor_train_ing_b200.tune ... --write``
+        from ..tune import apply
+        apply(tuning)
     return _PROXY
 
 

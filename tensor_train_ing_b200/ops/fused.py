@@ -12,9 +12,15 @@ import torch
 from ._ext import lib
 
 
+# (M, N, K) -> output tile width (128 or 256) chosen by ``tensor_train_ing_b200.tune``; absent shapes
+# take the kernel's own choice (128 for N <= 128, else the 256-wide CTA-pair tile)
+GEMM_TILES: dict[tuple[int, int, int], int] = {}
+
+
 def _mm(a, b, out, c=None, alpha=1.0, beta=0.0, bias=None, b2=None):
     """out = alpha * (a @ b + bias) + beta * c; with ``b2``, a @ cat(b, b2) in one pass."""
-    lib().mm(a, b, out, c, float(alpha), float(beta), bias, b2)
+    tile = GEMM_TILES.get((out.shape[0], out.shape[1], a.shape[1]), 0) if GEMM_TILES else 0
+    lib().mm(a, b, out, c, float(alpha), float(beta), bias, b2, tile)
     return out
 
 
