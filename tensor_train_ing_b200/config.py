@@ -7,7 +7,9 @@ section (``project``, ``data``, ``evaluation``, ``b200`` ...) is kept verbatim i
 
 Additions of this framework:
   * ``attention_backend`` also accepts ``"cuda"``; ``"triton"`` (the reference's name for its
-    tiled kernel) selects the same hand-written sm_100a kernels here.
+    tiled kernel) selects the same hand-written sm_100a kernels here;
+  * ``attention_backend="recurrent"`` runs polynomial attention in its chunked linear-state form
+    (``models/long_context.py``): no T x T matrix, for very long contexts.
 """
 from __future__ import annotations
 
@@ -20,7 +22,7 @@ MLP_KINDS = ("bilinear", "affine_bilinear", "swiglu")
 ATTN_KINDS = ("signed_product", "offset_square", "lower_degree_mix", "softmax")
 NORM_PACKAGES = ("pre_rms", "branch_rms", "sandwich_rms", "group_rms", "spectral_rms", "lagged", "taper")
 FINAL_NORMS = ("rms", "lagged", "taper")
-ATTN_BACKENDS = ("reference", "triton", "cuda", "auto")
+ATTN_BACKENDS = ("reference", "triton", "cuda", "auto", "recurrent")
 
 
 @dataclass
@@ -76,6 +78,8 @@ class ModelConfig:
         _require(self.padded_vocab >= self.vocab_size, "padded_vocab must be >= vocab_size")
         _require(self.dropout == 0.0, "dropout is not part of this model family")
         _require(self.attention_backend in ATTN_BACKENDS, f"attention_backend {self.attention_backend!r}")
+        _require(not (self.attention_backend == "recurrent" and self.attention == "softmax"),
+                 "the recurrent attention backend is a polynomial-attention form (no softmax)")
         if self.normalization == "lagged" and self.final_normalization != "lagged":
             raise ValueError("lagged package requires final_normalization: lagged (else label it N)")
         if self.normalization == "taper" and self.final_normalization != "taper":

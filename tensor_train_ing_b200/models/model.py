@@ -104,8 +104,14 @@ class Attention(nn.Module):
             widen = lambda t: None if t is None else t.to(torch.promote_types(t.dtype, torch.float32))  # noqa: E731
             q1, k1, q2, k2, v = (widen(t) for t in (q1, k1, q2, k2, v))
         with torch.autocast(x.device.type, enabled=False):
-            y = polynomial_attention(self.kind, q1, k1, q2, k2, v, ctx["C"][self.row_power],
-                                     coef=getattr(self, "coef", None), b=getattr(self, "b", None))
+            if ctx["backend"] == "recurrent":
+                from .long_context import chunked_polynomial_attention
+                y, _, _ = chunked_polynomial_attention(self.kind, q1, k1, q2, k2, v, ctx["doc_ids"],
+                                                       ctx["row_scale"][self.row_power],
+                                                       coef=getattr(self, "coef", None), b=getattr(self, "b", None))
+            else:
+                y = polynomial_attention(self.kind, q1, k1, q2, k2, v, ctx["C"][self.row_power],
+                                         coef=getattr(self, "coef", None), b=getattr(self, "b", None))
         return y.to(x.dtype)
 
     def forward(self, x, ctx):
@@ -317,6 +323,12 @@ class TensorLM(nn.Module):
         if self.cfg.attention == "softmax":
             backend = "flex" if backend in ("triton", "cuda") else "softmax"
         ctx["backend"] = backend
+        if backend == "recurrent":  # the linear-state form needs row scales, never a T x T mask
+            if self.cfg.attention == "softmax":
+                raise ValueError("the recurrent attention backend has no softmax form")
+            scale = lambda p: torch.where(doc_ids >= 0, (pos + 1).to(torch.float64).pow(-p), 0.0)  # noqa: E731
+            ctx["row_scale"] = {p: scale(p) for p in self._row_powers()}
+            return ctx
         if backend != "flex":  # the dense paths; FlexAttention builds its own block mask
             ctx["visible"] = visible_mask(doc_ids)
             if self.cfg.attention != "softmax":
