@@ -94,7 +94,7 @@ void mm(const Tensor& a, const Tensor& b, Tensor& out, const c10::optional<Tenso
 
 // qkv = x w^T with the rotary embedding applied to the first rope_cols columns
 Tensor qkv_rope(const Tensor& x, const Tensor& w, int64_t rope_cols, int64_t dk, const Tensor& pos,
-                const Tensor& cos_t, const Tensor& sin_t) {
+                const Tensor& cos_t, const Tensor& sin_t, const c10::optional<Tensor>& norm_max) {
   const c10::cuda::CUDAGuard guard(x.device());
   const auto X = a_operand(x);
   const auto W = b_operand(w.t());
@@ -104,9 +104,16 @@ Tensor qkv_rope(const Tensor& x, const Tensor& w, int64_t rope_cols, int64_t dk,
   TORCH_CHECK(cos_t.scalar_type() == torch::kFloat32 && cos_t.is_contiguous() && cos_t.size(-1) == dk / 2, "cos table");
   TORCH_CHECK(sin_t.scalar_type() == torch::kFloat32 && sin_t.is_contiguous() && sin_t.sizes() == cos_t.sizes(),
               "sin table");
+  unsigned int* nm = nullptr;
+  if (norm_max.has_value()) {
+    TORCH_CHECK(norm_max->scalar_type() == torch::kFloat32 && norm_max->is_contiguous() &&
+                    norm_max->numel() == rope_cols / dk && norm_max->device() == x.device(),
+                "norm_max: zeroed fp32 [rope_cols / dk] on the input's device");
+    nm = reinterpret_cast<unsigned int*>(norm_max->data_ptr<float>());
+  }
   auto out = torch::empty({M, N}, x.options());
   ttb::gemm_qkv_rope(X, W, M, N, K, out.data_ptr(), out.stride(0), rope_cols, dk, pos.data_ptr<int>(),
-                     cos_t.data_ptr<float>(), sin_t.data_ptr<float>(), cur_stream());
+                     cos_t.data_ptr<float>(), sin_t.data_ptr<float>(), cur_stream(), nm);
   return out;
 }
 
@@ -705,5 +712,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("spectral_cast", &spectral_cast, "sigma = u^T W v and the bf16 effective weight");
   m.def("spectral_grad", &spectral_grad, "dW and dgamma of the spectral effective weight");
   m.def("spectral_power_step", &spectral_power_step, "one power-iteration step on u and v");
-  m.def("qkv_rope", &qkv_rope, "QKV projection GEMM with the rotary embedding in its epilogue");
+  m.def("qkv_rope", &qkv_rope, "QKV projection GEMM with the rotary embedding in its epilogue (optionally the "
+        "per-head maximum row norms)", py::arg("x"), py::arg("w"), py::arg("rope_cols"), py::arg("dk"), py::arg("pos"),
+        py::arg("cos_t"), py::arg("sin_t"), py::arg("norm_max") = py::none());
 }

@@ -34,8 +34,11 @@ void gemm_bilinear_grad(const Operand& dy, const Operand& wd, int M, int N, int 
                         void* dL, void* dR, long long ld, long long ldo, int mode, cudaStream_t stream);
 
 // qkv[M, N] = x W^T (bf16) with the rotary embedding applied to the first rope_cols columns
-// (heads of width dk; cos/sin tables [positions, dk/2] fp32; pos [M] int32).
+// (heads of width dk; cos/sin tables [positions, dk/2] fp32; pos [M] int32).  With norm_max
+// (rope_cols / dk zeroed words) the epilogue also records, per rotated head, the largest row norm
+// of the stored values (float bits), from which score bounds follow.
 void gemm_qkv_rope(const Operand& x, const Operand& w, int M, int N, int K, void* D, long long ldd, int rope_cols,
-                   int dk, const int* pos, const float* cos_t, const float* sin_t, cudaStream_t stream);
+                   int dk, const int* pos, const float* cos_t, const float* sin_t, cudaStream_t stream,
+                   unsigned int* norm_max = nullptr);
 
 }  // namespace ttb

@@ -520,7 +520,30 @@ struct EpiRope {
   const float* cos_t;
   const float* sin_t;
   int M, N;
+  // optional side output: per rotated head (rope_cols / dk of them, in column order) the largest
+  // row norm of the stored bf16 values, as float bits in an unsigned word (atomicMax on the bits
+  // orders non-negative floats); the caller zeroes it.  Rows past M hold zeros and add nothing.
+  unsigned int* norm_max;
   static constexpr int kSmemPerThread = 256;  // per warp: two 2 KB chunk buffers
+
+  // squares of the bf16-rounded values: the norms of exactly what the attention kernels read
+  __device__ __forceinline__ static float rounded_sq(const float* a, const float* b) {
+    float s = 0.f;
+#pragma unroll
+    for (int j = 0; j < 32; ++j) {
+      const float x = __bfloat162float(__float2bfloat16_rn(a[j]));
+      const float y = __bfloat162float(__float2bfloat16_rn(b[j]));
+      s = fmaf(x, x, fmaf(y, y, s));
+    }
+    return s;
+  }
+  // after the last first-half chunk of a head: warp max of the 32 rows' norms, one atomic per warp
+  __device__ __forceinline__ void publish_norm(float ss, int col0) const {
+    float n = sqrtf(ss);
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) n = fmaxf(n, __shfl_xor_sync(0xffffffffu, n, off));
+    if ((threadIdx.x & 31) == 0) atomicMax(norm_max + col0 / dk, __float_as_uint(n));
+  }
 
   // Warp-coalesced path (see warp_store_bf16).
   __device__ __forceinline__ void operator()(uint32_t taddr, int row, int n0, int, int, uint8_t* sm) const {
@@ -530,6 +553,7 @@ struct EpiRope {
     const int row0 = row - lane;
     const int half = dk / 2;
     const int p = row < M ? pos[row] : 0;
+    float ss = 0.f;  // running squared norm of this row's current head
 #pragma unroll 1
     for (int c = 0; c < NB / 32; ++c) {
       const int col0 = n0 + c * 32;
@@ -553,6 +577,10 @@ struct EpiRope {
         }
         warp_store_bf16(area, a, lane, D, ldd, row0, col0, M, N);
         warp_store_bf16(area + 2048, b, lane, D, ldd, row0, col0 + half, M, N);
+        if (norm_max != nullptr) {
+          ss = (o == 0 ? 0.f : ss) + rounded_sq(a, b);
+          if (o + 32 == half) publish_norm(ss, col0);
+        }
       } else {
         uint32_t r[32];
         tmem_ld32(taddr + c * 32, r);
@@ -570,6 +598,7 @@ struct EpiRope {
     const bool vec = (ldd % 8 == 0);
     const int half = dk / 2;
     const int p = row < M ? pos[row] : 0;
+    float ss = 0.f;
 #pragma unroll 1
     for (int c = 0; c < NB / 32; ++c) {
       const int col0 = n0 + c * 32;
@@ -581,16 +610,21 @@ struct EpiRope {
         tmem_ld32(taddr + c * 32, ra);
         tmem_ld32(taddr + cb * 32, rb);
         tmem_ld_wait();
-        if (row >= M || col0 >= N) continue;
+        if (col0 >= N) continue;
         float cs[32], sn[32], a[32], b[32];
         load_row32_f32(cos_t + static_cast<long long>(p) * half + o, (half % 4 == 0), 32, cs);
         load_row32_f32(sin_t + static_cast<long long>(p) * half + o, (half % 4 == 0), 32, sn);
 #pragma unroll
         for (int j = 0; j < 32; ++j) {
           const float x1 = __uint_as_float(ra[j]), x2 = __uint_as_float(rb[j]);
-          a[j] = x1 * cs[j] - x2 * sn[j];
-          b[j] = x1 * sn[j] + x2 * cs[j];
+          a[j] = row < M ? x1 * cs[j] - x2 * sn[j] : 0.f;
+          b[j] = row < M ? x1 * sn[j] + x2 * cs[j] : 0.f;
         }
+        if (norm_max != nullptr) {  // every lane reaches the warp reduction
+          ss = (o == 0 ? 0.f : ss) + rounded_sq(a, b);
+          if (o + 32 == half) publish_norm(ss, col0);
+        }
+        if (row >= M) continue;
         store_row32_bf16(D + row * ldd + col0, vec, 32, a);
         store_row32_bf16(D + row * ldd + col0 + half, vec, 32, b);
       } else {

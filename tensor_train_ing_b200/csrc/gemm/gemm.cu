@@ -44,11 +44,12 @@ void gemm_bilinear_grad(const Operand& dy, const Operand& wd, int M, int N, int 
 }
 
 void gemm_qkv_rope(const Operand& x, const Operand& w, int M, int N, int K, void* D, long long ldd, int rope_cols,
-                   int dk, const int* pos, const float* cos_t, const float* sin_t, cudaStream_t stream) {
+                   int dk, const int* pos, const float* cos_t, const float* sin_t, cudaStream_t stream,
+                   unsigned int* norm_max) {
   TTB_CHECK(M > 0 && N > 0 && K > 0, "empty GEMM");
   TTB_CHECK(dk % 64 == 0 && 256 % dk == 0 && rope_cols % dk == 0 && rope_cols <= N,
             "qkv rope epilogue: dk in {64,128,256}, rope columns a multiple of dk");
-  gemm::EpiRope<256> epi{static_cast<__nv_bfloat16*>(D), ldd, rope_cols, dk, pos, cos_t, sin_t, M, N};
+  gemm::EpiRope<256> epi{static_cast<__nv_bfloat16*>(D), ldd, rope_cols, dk, pos, cos_t, sin_t, M, N, norm_max};
   gemm::dispatch<256, 4, false>(x, w, nullptr, gemm::Shape{M, N, K, status_ptr()}, epi, stream);
 }
 

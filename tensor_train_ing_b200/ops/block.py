@@ -81,16 +81,14 @@ def _add_branch(x, out_norm, branch, alpha):
     return x + alpha * out_norm(branch)
 
 
-def _record_bound(attn, qkv, cols, N):
-    cfg = attn.cfg
-    H, dk = cfg.heads, cfg.d_key
-    bounds = {}
-    pairs = (("S1", cols[0], cols[1]),) + ((("S2", cols[2], cols[3]),) if attn.kind != "offset_square" else ())
-    with torch.no_grad():
-        for name, cq, ck in pairs:
-            qn = qkv[:, cq:cq + H * dk].float().view(N, H, dk).norm(dim=-1).amax(0)
-            kn = qkv[:, ck:ck + H * dk].float().view(N, H, dk).norm(dim=-1).amax(0)
-            bounds[name] = qn * kn / dk ** 0.5
+def _record_bound(attn, norms):
+    """Per head max |q| max |k| / sqrt(dk) from the per-head maximum row norms the QKV epilogue
+    wrote (rotated heads in buffer order: q1, k1[, q2, k2])."""
+    H, dk = attn.cfg.heads, attn.cfg.d_key
+    per = norms.view(-1, H)
+    bounds = {"S1": per[0] * per[1] / dk ** 0.5}
+    if attn.kind != "offset_square":
+        bounds["S2"] = per[2] * per[3] / dk ** 0.5
     attn.last_score_bound = bounds
 
 
@@ -102,13 +100,14 @@ def attention_branch(blk, h, ctx):
     grp = _weights(a, "qkv", projs)
     two = a.kind != "offset_square"
     n_qk = 4 if two else 2
-    qkv = fused.qkv_rope(h, grp, n_qk * H * dk, dk, ctx["rope"])
+    norms = torch.zeros(n_qk * H, device=h.device, dtype=torch.float32) if a.record_score_bound else None
+    qkv = fused.qkv_rope(h, grp, n_qk * H * dk, dk, ctx["rope"], norms)
     if two:
         cols = [0, H * dk, 2 * H * dk, 3 * H * dk, 4 * H * dk]
     else:
         cols = [0, H * dk, 0, H * dk, 2 * H * dk]
-    if a.record_score_bound:
-        _record_bound(a, qkv, cols, h.shape[0])
+    if norms is not None:
+        _record_bound(a, norms)
     kpar = getattr(a, "b", None) if a.kind == "offset_square" else getattr(a, "coef", None)
     return fused.poly_attention(qkv, kpar, a.kind, dk, dv, H, cols, ctx["tables"], ctx["row_scale"][a.row_power],
                                 ctx["rope"])

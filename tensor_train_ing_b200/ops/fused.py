@@ -140,9 +140,9 @@ class QKVRopeFn(torch.autograd.Function):
     rotated back (it writes dq/dk w.r.t. the pre-rotation projections), so only GEMMs remain."""
 
     @staticmethod
-    def forward(ctx, x, group, rope_cols, dk, rope, *weights):
+    def forward(ctx, x, group, rope_cols, dk, rope, norm_max, *weights):
         w16 = group.bf16()
-        qkv = lib().qkv_rope(x, w16, int(rope_cols), int(dk), rope["pos32"], rope["cos"], rope["sin"])
+        qkv = lib().qkv_rope(x, w16, int(rope_cols), int(dk), rope["pos32"], rope["cos"], rope["sin"], norm_max)
         ctx.save_for_backward(x)
         ctx.group = group
         return qkv
@@ -157,11 +157,13 @@ class QKVRopeFn(torch.autograd.Function):
         dx = torch.empty_like(x)  # bf16 like the input: no cast inserted by autograd
         _mm(g, w16, dx)
         grads = ctx.group.sink_grad(lambda out, beta: _mm(g.t(), x, out, c=out, beta=beta))
-        return (dx, None, None, None, None, *grads)
+        return (dx, None, None, None, None, None, *grads)
 
 
-def qkv_rope(x, group, rope_cols, dk, rope):
-    return QKVRopeFn.apply(x, group, rope_cols, dk, rope, *group.params)
+def qkv_rope(x, group, rope_cols, dk, rope, norm_max=None):
+    """``norm_max``: a zeroed fp32 [rope_cols / dk] buffer that receives, per rotated head, the
+    largest row norm of the stored bf16 values (a by-product of the epilogue)."""
+    return QKVRopeFn.apply(x, group, rope_cols, dk, rope, norm_max, *group.params)
 
 
 # ============================================================================ polynomial attention

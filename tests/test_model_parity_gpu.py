@@ -189,3 +189,33 @@ def test_norm_variant_packages_match_reference(case):
             a, b = float(getattr(fm, name)), float(getattr(xm, name))
             # activations of the later layers carry the bf16 path's rounding
             assert abs(a - b) <= 1e-3 * max(abs(b), 1e-12), (name, a, b)
+
+
+@pytest.mark.parametrize("kind", ["signed_product", "offset_square"])
+@pytest.mark.parametrize("dk", [64, 128])
+def test_score_bounds_from_the_qkv_epilogue(kind, dk):
+    """The per-head score bound max|q| max|k| / sqrt(dk) recorded by the fused path (row norms from
+    the QKV GEMM's RoPE epilogue) agrees with the bound the reference path computes from its own
+    bf16 q and k on the same weights."""
+    from tensor_train_ing_b200.qk_clip import set_score_bound_recording
+    torch.manual_seed(0)
+    cfg = ModelConfig(layers=2, d_model=256, heads=2, d_key=dk, d_value=dk, d_mlp=512, vocab_size=1000,
+                      padded_vocab=1024, attention=kind, qk_init_scale=0.5)
+    model = TensorLM(cfg).cuda().eval()
+    ref = TensorLM(ModelConfig(**{**cfg.__dict__, "attention_backend": "reference"})).cuda().eval()
+    ref.load_state_dict(model.state_dict())
+    idx = torch.randint(0, 1000, (2, 300), device="cuda")
+    docs = torch.zeros(2, 300, dtype=torch.long, device="cuda")
+    docs[:, 170:] = 1
+    for m in (model, ref):
+        set_score_bound_recording(m, True)
+    with torch.no_grad():
+        model(idx, docs)
+        with torch.autocast("cuda", dtype=torch.bfloat16):
+            ref(idx, docs)
+    for blk, rblk in zip(model.blocks, ref.blocks):
+        got, want = blk.attn.last_score_bound, rblk.attn.last_score_bound
+        assert set(got) == set(want) == ({"S1", "S2"} if kind == "signed_product" else {"S1"})
+        for name in got:
+            assert got[name].shape == (2,) and bool((got[name] > 0).all())
+            torch.testing.assert_close(got[name], want[name].float(), rtol=2e-2, atol=1e-4)
