@@ -50,10 +50,65 @@ ttb::Operand b_operand(const Tensor& b) {
   return {b.data_ptr(), b.stride(0), true};  // stored [K][N]
 }
 
+// Fused all-gather description from Python: None, or one tuple per staged B operand
+// (src_ptrs [world], cuts [world + 1], done int32 [rows / 64], target); the staging buffers are the
+// weights passed as the B operands, dense [rows, cols] bf16.
+bool make_gather(const py::object& obj, const std::vector<const Tensor*>& staging, ttb::gemm::Gather& g) {
+  if (obj.is_none()) return false;
+  const auto ops = obj.cast<std::vector<py::tuple>>();
+  TORCH_CHECK(ops.size() == staging.size(), "gather: one description per staged operand");
+  g = ttb::gemm::Gather{};
+  g.nops = static_cast<int>(ops.size());
+  g.claim = ttb::gather_claim_counter();
+  for (size_t o = 0; o < ops.size(); ++o) {
+    TORCH_CHECK(ops[o].size() == 4, "gather: (src_ptrs, cuts, done, target)");
+    const auto src = ops[o][0].cast<std::vector<int64_t>>();
+    const auto cut = ops[o][1].cast<std::vector<int64_t>>();
+    const Tensor done = ops[o][2].cast<Tensor>();
+    const int64_t target = ops[o][3].cast<int64_t>();
+    const Tensor& w = *staging[o];
+    check_bf16(w, "gather staging");
+    TORCH_CHECK(w.dim() == 2 && w.is_contiguous(), "gather staging must be a dense [rows, cols] matrix");
+    const int64_t rows = w.size(0), cols = w.size(1);
+    const int world = static_cast<int>(src.size());
+    TORCH_CHECK(world >= 1 && world <= ttb::gemm::kGatherMaxRanks && cut.size() == src.size() + 1,
+                "gather: 1..8 ranks and world + 1 cuts");
+    TORCH_CHECK(rows % ttb::gemm::kGatherSlabRows == 0 && cols % 8 == 0, "gather: rows % 64 == 0 and cols % 8 == 0");
+    TORCH_CHECK(cut[0] == 0 && cut[world] == rows, "gather: cuts must span the rows");
+    for (int r = 0; r < world; ++r) {
+      TORCH_CHECK(cut[r] <= cut[r + 1] && cut[r] % ttb::gemm::kGatherChunkRows == 0, "gather: cuts ascend in 16-row steps");
+      TORCH_CHECK(src[r] % 16 == 0, "gather: shard pointers must be 16-byte aligned");
+      g.op[o].src[r] = reinterpret_cast<const __nv_bfloat16*>(src[r]);
+      g.op[o].cut[r] = static_cast<int>(cut[r]);
+    }
+    g.op[o].cut[world] = static_cast<int>(rows);
+    TORCH_CHECK(done.is_cuda() && done.scalar_type() == torch::kInt32 && done.is_contiguous() &&
+                    done.numel() == rows / ttb::gemm::kGatherSlabRows && done.device() == w.device(),
+                "gather: done must be int32 [rows / 64] on the staging buffer's device");
+    TORCH_CHECK(reinterpret_cast<uintptr_t>(w.data_ptr()) % 16 == 0, "gather: staging must be 16-byte aligned");
+    g.op[o].world = world;
+    g.op[o].rows = static_cast<int>(rows);
+    g.op[o].cols = static_cast<int>(cols);
+    g.op[o].dst = reinterpret_cast<__nv_bfloat16*>(w.data_ptr());
+    g.op[o].done = reinterpret_cast<uint32_t*>(done.data_ptr<int>());
+    g.op[o].target = static_cast<uint32_t>(target);
+  }
+  TORCH_CHECK(g.nops == 1 || g.op[0].rows == g.op[1].rows, "gather: two staged operands need equal rows");
+  return true;
+}
+
+void gather_rows(const Tensor& w, const py::object& gather) {
+  const c10::cuda::CUDAGuard guard(w.device());
+  ttb::gemm::Gather g;
+  TORCH_CHECK(make_gather(gather, {&w}, g), "gather_rows needs a gather description");
+  ttb::gather_rows(g, cur_stream());
+}
+
 // out = alpha * (a @ b + bias) + beta * c     (out/c: bf16 or fp32, row-major rows)
 // With b2: out = alpha * (a @ cat(b, b2) + bias) + beta * c, the contraction concatenated in one pass.
+// With gather, b must be the transpose view of a dense staging buffer w [N, K] (b = w.t()).
 void mm(const Tensor& a, const Tensor& b, Tensor& out, const c10::optional<Tensor>& c, double alpha, double beta,
-        const c10::optional<Tensor>& bias, const c10::optional<Tensor>& b2, int64_t tile_n) {
+        const c10::optional<Tensor>& bias, const c10::optional<Tensor>& b2, int64_t tile_n, const py::object& gather) {
   const c10::cuda::CUDAGuard guard(a.device());
   const auto A = a_operand(a);
   const auto B = b_operand(b);
@@ -87,14 +142,19 @@ void mm(const Tensor& a, const Tensor& b, Tensor& out, const c10::optional<Tenso
     TORCH_CHECK(bias->scalar_type() == torch::kFloat32 && bias->is_contiguous() && bias->numel() == N, "bias");
     bp = bias->data_ptr<float>();
   }
+  ttb::gemm::Gather g;
+  const Tensor w = b.t();
+  const bool gathered = make_gather(gather, {&w}, g);
+  TORCH_CHECK(!gathered || (!b2.has_value() && !B.mn_major), "gather: one K-major weight operand");
   ttb::gemm_linear(A, B, M, N, K, out.data_ptr(), out.stride(0), out.scalar_type() == torch::kFloat32, cp, ldc,
                    c_f32, static_cast<float>(alpha), static_cast<float>(beta), bp, cur_stream(),
-                   b2.has_value() ? &B2 : nullptr, k_split, static_cast<int>(tile_n));
+                   b2.has_value() ? &B2 : nullptr, k_split, static_cast<int>(tile_n), gathered ? &g : nullptr);
 }
 
 // qkv = x w^T with the rotary embedding applied to the first rope_cols columns
 Tensor qkv_rope(const Tensor& x, const Tensor& w, int64_t rope_cols, int64_t dk, const Tensor& pos,
-                const Tensor& cos_t, const Tensor& sin_t, const c10::optional<Tensor>& norm_max) {
+                const Tensor& cos_t, const Tensor& sin_t, const c10::optional<Tensor>& norm_max,
+                const py::object& gather) {
   const c10::cuda::CUDAGuard guard(x.device());
   const auto X = a_operand(x);
   const auto W = b_operand(w.t());
@@ -111,16 +171,18 @@ Tensor qkv_rope(const Tensor& x, const Tensor& w, int64_t rope_cols, int64_t dk,
                 "norm_max: zeroed fp32 [rope_cols / dk] on the input's device");
     nm = reinterpret_cast<unsigned int*>(norm_max->data_ptr<float>());
   }
+  ttb::gemm::Gather g;
+  const bool gathered = make_gather(gather, {&w}, g);
   auto out = torch::empty({M, N}, x.options());
   ttb::gemm_qkv_rope(X, W, M, N, K, out.data_ptr(), out.stride(0), rope_cols, dk, pos.data_ptr<int>(),
-                     cos_t.data_ptr<float>(), sin_t.data_ptr<float>(), cur_stream(), nm);
+                     cos_t.data_ptr<float>(), sin_t.data_ptr<float>(), cur_stream(), nm, gathered ? &g : nullptr);
   return out;
 }
 
 // h = l*r (mode 0) / silu(l)*r (mode 1) with l = x wl^T (+bl), r = x wr^T (+br)
 void bilinear(const Tensor& x, const Tensor& wl, const Tensor& wr, const c10::optional<Tensor>& bl,
               const c10::optional<Tensor>& br, int64_t mode, Tensor& h, const c10::optional<Tensor>& lo,
-              const c10::optional<Tensor>& ro) {
+              const c10::optional<Tensor>& ro, const py::object& gather) {
   const c10::cuda::CUDAGuard guard(x.device());
   const auto X = a_operand(x);
   const auto WL = b_operand(wl.t());
@@ -143,8 +205,10 @@ void bilinear(const Tensor& x, const Tensor& wl, const Tensor& wr, const c10::op
   const float* blp = bl.has_value() ? bl->data_ptr<float>() : nullptr;
   const float* brp = br.has_value() ? br->data_ptr<float>() : nullptr;
   TORCH_CHECK((blp == nullptr) == (brp == nullptr), "both biases or neither");
+  ttb::gemm::Gather g;
+  const bool gathered = make_gather(gather, {&wl, &wr}, g);
   ttb::gemm_bilinear(X, WL, WR, M, N, K, h.data_ptr(), lp, rp, h.stride(0), blp, brp, static_cast<int>(mode),
-                     cur_stream());
+                     cur_stream(), gathered ? &g : nullptr);
 }
 
 // dl, dr from dH = dy @ wd (wd: [d_out, N] weight of the down projection)
@@ -664,8 +728,13 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.doc() = "tensor_train_ing_b200 sm_100a kernels (tcgen05 / TMEM / TMA)";
   m.def("mm", &mm, "out = alpha*(a@b + bias) + beta*c on the tcgen05 GEMM", py::arg("a"), py::arg("b"),
         py::arg("out"), py::arg("c") = py::none(), py::arg("alpha") = 1.0, py::arg("beta") = 0.0,
-        py::arg("bias") = py::none(), py::arg("b2") = py::none(), py::arg("tile_n") = 0);
-  m.def("bilinear", &bilinear, "dual-B GEMM forming the bilinear hidden layer");
+        py::arg("bias") = py::none(), py::arg("b2") = py::none(), py::arg("tile_n") = 0,
+        py::arg("gather") = py::none());
+  m.def("bilinear", &bilinear, "dual-B GEMM forming the bilinear hidden layer", py::arg("x"), py::arg("wl"),
+        py::arg("wr"), py::arg("bl"), py::arg("br"), py::arg("mode"), py::arg("h"), py::arg("lo"), py::arg("ro"),
+        py::arg("gather") = py::none());
+  m.def("gather_rows", &gather_rows, "copy a row-sharded weight into its staging buffer (the fused GEMM's gather "
+        "without the GEMM)", py::arg("w"), py::arg("gather"));
   m.def("bilinear_grad", &bilinear_grad, "dH GEMM fused with the bilinear backward");
   m.def("status", &status, "read and clear the device error word (bounded-wait timeouts)");
   m.def("peer_barrier", &peer_barrier, "cross-GPU barrier through symmetric signal pads (bounded wait)",
@@ -714,5 +783,5 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("spectral_power_step", &spectral_power_step, "one power-iteration step on u and v");
   m.def("qkv_rope", &qkv_rope, "QKV projection GEMM with the rotary embedding in its epilogue (optionally the "
         "per-head maximum row norms)", py::arg("x"), py::arg("w"), py::arg("rope_cols"), py::arg("dk"), py::arg("pos"),
-        py::arg("cos_t"), py::arg("sin_t"), py::arg("norm_max") = py::none());
+        py::arg("cos_t"), py::arg("sin_t"), py::arg("norm_max") = py::none(), py::arg("gather") = py::none());
 }

@@ -4,6 +4,8 @@
 #include <cuda_runtime.h>
 #include <cstdint>
 
+#include "gather.h"
+
 namespace ttb {
 
 // One bf16 matrix operand in global memory.
@@ -22,11 +24,13 @@ struct Operand {
 // element accumulates its K blocks in the same order either way.
 void gemm_linear(const Operand& a, const Operand& b, int M, int N, int K, void* D, long long ldd, bool d_f32,
                  const void* C, long long ldc, bool c_f32, float alpha, float beta, const float* bias,
-                 cudaStream_t stream, const Operand* b2 = nullptr, int k_split = 0, int tile_n = 0);
+                 cudaStream_t stream, const Operand* b2 = nullptr, int k_split = 0, int tile_n = 0,
+                 const gemm::Gather* gather = nullptr);
 
 // l = x Wl^T (+bl), r = x Wr^T (+br), H = l*r (mode 0) or silu(l)*r (mode 1); all [M, N] bf16 with row stride ld.
 void gemm_bilinear(const Operand& x, const Operand& wl, const Operand& wr, int M, int N, int K, void* H, void* Lo,
-                   void* Ro, long long ld, const float* bias_l, const float* bias_r, int mode, cudaStream_t stream);
+                   void* Ro, long long ld, const float* bias_l, const float* bias_r, int mode, cudaStream_t stream,
+                   const gemm::Gather* gather = nullptr);
 
 // dH = dY Wd (B operand = Wd^T view), fused with the bilinear backward: writes dl, dr [M, N] bf16
 // (row stride ldo; the saved factors Lin / Rin have row stride ld).
@@ -39,6 +43,15 @@ void gemm_bilinear_grad(const Operand& dy, const Operand& wd, int M, int N, int 
 // of the stored values (float bits), from which score bounds follow.
 void gemm_qkv_rope(const Operand& x, const Operand& w, int M, int N, int K, void* D, long long ldd, int rope_cols,
                    int dk, const int* pos, const float* cos_t, const float* sin_t, cudaStream_t stream,
-                   unsigned int* norm_max = nullptr);
+                   unsigned int* norm_max = nullptr, const gemm::Gather* gather = nullptr);
+
+// Fused all-gather of row-sharded weights (gemm/gather.cuh).  The gemm_* calls above take an
+// optional Gather whose operands' staging buffers are their B operands (wl and wr for the bilinear
+// form): the CTA-pair GEMM copies the rows from the ranks' shards while it runs.  gather_rows runs
+// the copy alone (the same chunks and done words), for consumers that are not CTA-pair GEMMs.
+// gather_claim_counter() is this device's chunk counter pair (zeroed once, returned to zero by
+// every launch).
+void gather_rows(const gemm::Gather& g, cudaStream_t stream);
+uint32_t* gather_claim_counter();
 
 }  // namespace ttb

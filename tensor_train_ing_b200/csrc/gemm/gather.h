@@ -1,0 +1,35 @@
+// Host- and device-visible description of a row gather fused into a GEMM (see gather.cuh).
+#pragma once
+
+#include <cuda_bf16.h>
+#include <stdint.h>
+
+namespace ttb {
+namespace gemm {
+
+constexpr int kGatherMaxRanks = 8;
+constexpr int kGatherSlabRows = 64;   // readiness granularity (rows of one done word)
+constexpr int kGatherChunkRows = 16;  // rows one warp copies per claim
+constexpr int kGatherChunksPerSlab = kGatherSlabRows / kGatherChunkRows;
+
+// One row-sharded operand.  dst is the local staging buffer [rows, cols] (row stride cols); rank r's
+// rows start at src[r] (row stride cols).  rows % 64 == 0, cut[r] % 16 == 0, cols % 8 == 0, every
+// pointer 16-byte aligned.
+struct GatherOp {
+  const __nv_bfloat16* src[kGatherMaxRanks];
+  int cut[kGatherMaxRanks + 1];
+  int world;
+  int rows, cols;
+  __nv_bfloat16* dst;
+  uint32_t* done;    // [rows / 64]
+  uint32_t target;   // value every done word reaches when this call's copy of its slab is complete
+};
+
+struct Gather {
+  GatherOp op[2];
+  int nops;         // 0: no gather; 2: two operands of equal rows, slabs interleaved (dual-B GEMM)
+  uint32_t* claim;  // {next chunk, finished CTAs}
+};
+
+}  // namespace gemm
+}  // namespace ttb

@@ -41,13 +41,13 @@ inline bool pair_enabled() {
   return on;
 }
 
-template <class Epi, bool A_MN, bool B_MN, bool DUAL>
-inline void launch_pair(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& tb2, Shape s, const Epi& epi,
-                        cudaStream_t stream) {
+template <class Epi, bool A_MN, bool B_MN, bool DUAL, bool GATHER>
+inline void launch_pair_impl(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& tb2, Shape s,
+                             const Epi& epi, const Gather& g, cudaStream_t stream) {
   using L = PairLayout<kPairStages, DUAL>;
   constexpr int kSmem = with_epi_smem<Epi>(L::kSmemBytes, L::kBarOffset, kPairStages);
   static_assert(kSmem <= 232448, "GEMM shared memory exceeds 227 KB");
-  auto kern = gemm_pair_kernel<kPairStages, A_MN, B_MN, DUAL, Epi>;
+  auto kern = gemm_pair_kernel<kPairStages, A_MN, B_MN, DUAL, Epi, GATHER>;
   static bool configured = false;
   if (!configured) {
     TTB_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem));
@@ -56,13 +56,28 @@ inline void launch_pair(const CUtensorMap& ta, const CUtensorMap& tb, const CUte
   const int tiles = ((s.M + kPairBM - 1) / kPairBM) * ((s.N + L::kTileN - 1) / L::kTileN);
   const int pairs = num_sms() / 2;
   const int grid = 2 * (tiles < pairs ? tiles : pairs);
-  kern<<<grid, kThreads, kSmem, stream>>>(ta, tb, tb2, s, epi);
+  kern<<<grid, GATHER ? kPairGatherThreads : kThreads, kSmem, stream>>>(ta, tb, tb2, s, epi, g);
   TTB_CUDA_CHECK(cudaGetLastError());
 }
 
-template <int BN, int STAGES, bool DUAL, class Epi>
+template <class Epi, bool A_MN, bool B_MN, bool DUAL, bool CAN_GATHER>
+inline void launch_pair(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& tb2, Shape s, const Epi& epi,
+                        const Gather* gather, cudaStream_t stream) {
+  if constexpr (CAN_GATHER && !A_MN && !B_MN) {
+    if (gather != nullptr) return launch_pair_impl<Epi, A_MN, B_MN, DUAL, true>(ta, tb, tb2, s, epi, *gather, stream);
+  }
+  TTB_CHECK(gather == nullptr, "the fused gather needs K-major A and B operands");
+  launch_pair_impl<Epi, A_MN, B_MN, DUAL, false>(ta, tb, tb2, s, epi, Gather{}, stream);
+}
+
+// gather (nullable): B (and b2 for DUAL) are staging buffers filled from row shards by the GEMM
+// itself (CTA-pair path) or, where the pair path does not apply, by a gather launch before it.
+// CAN_GATHER instantiates the gathering kernels (only for the epilogues of weight-consuming GEMMs).
+template <int BN, int STAGES, bool DUAL, bool CAN_GATHER = false, class Epi>
 inline void dispatch(const Operand& a, const Operand& b, const Operand* b2, Shape s, const Epi& epi,
-                     cudaStream_t stream) {
+                     cudaStream_t stream, const Gather* gather = nullptr) {
+  TTB_CHECK(gather == nullptr || (s.k_split == 0 && !b.mn_major && gather->nops == (DUAL ? 2 : 1)),
+            "the fused gather takes K-major B operands without K concatenation, one per B");
   // contraction extents of the B operands: all of K, or the two parts of a K concatenation
   TTB_CHECK(s.k_split == 0 || (!DUAL && b2 != nullptr && s.k_split % BK == 0 && s.k_split < s.K),
             "K concatenation needs a second B operand and a split on a k-block boundary");
@@ -83,13 +98,14 @@ inline void dispatch(const Operand& a, const Operand& b, const Operand* b2, Shap
       const CUtensorMap tb2 = b2 != nullptr ? bmap(*b2, k2) : tb;
       TTB_CHECK(b2 == nullptr || b2->mn_major == b.mn_major, "dual GEMM operands must share a layout");
       if (a.mn_major) {
-        if (b.mn_major) return launch_pair<Epi, true, true, DUAL>(ta, tb, tb2, s, epi, stream);
-        return launch_pair<Epi, true, false, DUAL>(ta, tb, tb2, s, epi, stream);
+        if (b.mn_major) return launch_pair<Epi, true, true, DUAL, CAN_GATHER>(ta, tb, tb2, s, epi, gather, stream);
+        return launch_pair<Epi, true, false, DUAL, CAN_GATHER>(ta, tb, tb2, s, epi, gather, stream);
       }
-      if (b.mn_major) return launch_pair<Epi, false, true, DUAL>(ta, tb, tb2, s, epi, stream);
-      return launch_pair<Epi, false, false, DUAL>(ta, tb, tb2, s, epi, stream);
+      if (b.mn_major) return launch_pair<Epi, false, true, DUAL, CAN_GATHER>(ta, tb, tb2, s, epi, gather, stream);
+      return launch_pair<Epi, false, false, DUAL, CAN_GATHER>(ta, tb, tb2, s, epi, gather, stream);
     }
   }
+  if (gather != nullptr) gather_rows(*gather, stream);
   constexpr int NB = DUAL ? BN / 2 : BN;
   // A: rows = M, contraction = K.  K-major -> [M, K] rows; MN-major -> [K, M] rows.
   const CUtensorMap ta = a.mn_major

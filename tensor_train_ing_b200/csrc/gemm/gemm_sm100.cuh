@@ -22,6 +22,7 @@
 #include <type_traits>
 
 #include "../common/sm100.cuh"
+#include "gather.cuh"
 
 namespace ttb {
 namespace gemm {
@@ -325,10 +326,15 @@ struct PairLayout {
   static constexpr int kSmemBytes = kBarOffset + (2 * STAGES + 5) * 8 + 16 + 1024;
 };
 
-template <int STAGES, bool A_MN, bool B_MN, bool DUAL, class Epi>
-__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
+// GATHER: B (and B2) are staging buffers that two extra warps per CTA (warps 6 and 7) fill from the
+// ranks' row shards while the GEMM runs (gather.cuh); the producer waits for a tile's rows first.
+constexpr int kPairGatherThreads = kThreads + 64;
+
+template <int STAGES, bool A_MN, bool B_MN, bool DUAL, class Epi, bool GATHER = false>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(GATHER ? kPairGatherThreads : kThreads, 1)
     gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
-                     const __grid_constant__ CUtensorMap tmB2, Shape s, Epi epi) {
+                     const __grid_constant__ CUtensorMap tmB2, Shape s, Epi epi, const __grid_constant__ Gather g) {
+  static_assert(!GATHER || !B_MN, "the fused gather stages K-major B operands (weights [N, K])");
   using L = PairLayout<STAGES, DUAL>;
   constexpr int TN = L::kTileN;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
@@ -389,6 +395,13 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         tile_coords(tile, m_tiles, n_tiles, tm, tn);
         const int m0 = tm * kPairBM + static_cast<int>(rank) * kPairHalf;
         const int n0 = tn * TN + static_cast<int>(rank) * L::kBCols;
+        if constexpr (GATHER) {
+          if (!gather_wait_rows(g, 0, n0, n0 + L::kBCols, s.status) ||
+              (DUAL && !gather_wait_rows(g, 1, n0, n0 + L::kBCols, s.status))) {
+            ok = false;
+            break;
+          }
+        }
         for (int kb = 0; kb < k_blocks; ++kb) {
           if (!mbar_wait(&empty[stage], phase ^ 1, s.status, kErrTimeoutProducer)) {
             ok = false;
@@ -483,7 +496,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
       umma_commit_pair(mma_done, 0x1);
       mbar_wait(mma_done, 0, s.status, kErrTimeoutMma);
     }
-  } else {
+  } else if (warp < 6) {
     // ------------------------------------------------------------------ epilogue (warps 2..5, both CTAs)
     const int sub = warp & 3;
     int acc = 0;
@@ -504,6 +517,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         acc_phase ^= 1;
       }
     }
+  } else {
+    // ------------------------------------------------------------------ gather warps (6, 7)
+    if constexpr (GATHER) gather_warp(g, lane);
   }
 
   __syncwarp();
@@ -512,6 +528,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
   if (warp == 1) {
     tc_fence_after();
     tmem_dealloc_pair(tmem_base, L::kTmemCols);
+  }
+  if constexpr (GATHER) {
+    if (threadIdx.x == 0) gather_finish(g);
   }
 }
 

@@ -17,11 +17,18 @@ from ._ext import lib
 GEMM_TILES: dict[tuple[int, int, int], int] = {}
 
 
-def _mm(a, b, out, c=None, alpha=1.0, beta=0.0, bias=None, b2=None):
-    """out = alpha * (a @ b + bias) + beta * c; with ``b2``, a @ cat(b, b2) in one pass."""
+def _mm(a, b, out, c=None, alpha=1.0, beta=0.0, bias=None, b2=None, gather=None):
+    """out = alpha * (a @ b + bias) + beta * c; with ``b2``, a @ cat(b, b2) in one pass.  ``gather``:
+    b is the transpose of a staging buffer that the GEMM fills from the ranks' row shards first."""
     tile = GEMM_TILES.get((out.shape[0], out.shape[1], a.shape[1]), 0) if GEMM_TILES else 0
-    lib().mm(a, b, out, c, float(alpha), float(beta), bias, b2, tile)
+    lib().mm(a, b, out, c, float(alpha), float(beta), bias, b2, tile, gather)
     return out
+
+
+def _gathers(*specs):
+    """Gather descriptions of a GEMM's staged operands, as the kernels take them (None: nothing to
+    gather)."""
+    return [s for s in specs] if all(s is not None for s in specs) else None
 
 
 # ============================================================================ RMSNorm
@@ -102,14 +109,14 @@ class LinearFn(torch.autograd.Function):
 
     @staticmethod
     def forward(ctx, x, residual, bias, group, alpha, *weights):
-        w16 = group.bf16()
+        w16, spec = group.operand()
         N = x.shape[0]
         if residual is not None:
             out = torch.empty(N, w16.shape[0], device=x.device, dtype=torch.float32)
-            _mm(x, w16.t(), out, c=residual, alpha=alpha, beta=1.0, bias=bias)
+            _mm(x, w16.t(), out, c=residual, alpha=alpha, beta=1.0, bias=bias, gather=_gathers(spec))
         else:
             out = torch.empty(N, w16.shape[0], device=x.device, dtype=torch.bfloat16)
-            _mm(x, w16.t(), out, alpha=alpha, bias=bias)
+            _mm(x, w16.t(), out, alpha=alpha, bias=bias, gather=_gathers(spec))
         ctx.save_for_backward(x)
         ctx.group, ctx.alpha, ctx.has_res, ctx.has_bias = group, alpha, residual is not None, bias is not None
         return out
@@ -141,8 +148,9 @@ class QKVRopeFn(torch.autograd.Function):
 
     @staticmethod
     def forward(ctx, x, group, rope_cols, dk, rope, norm_max, *weights):
-        w16 = group.bf16()
-        qkv = lib().qkv_rope(x, w16, int(rope_cols), int(dk), rope["pos32"], rope["cos"], rope["sin"], norm_max)
+        w16, spec = group.operand()
+        qkv = lib().qkv_rope(x, w16, int(rope_cols), int(dk), rope["pos32"], rope["cos"], rope["sin"], norm_max,
+                             _gathers(spec))
         ctx.save_for_backward(x)
         ctx.group = group
         return qkv
@@ -230,19 +238,22 @@ class BilinearMLPFn(torch.autograd.Function):
 
     @staticmethod
     def forward(ctx, x, residual, bl, br, bd, g_l, g_r, g_d, alpha, mode, *weights):
-        wl, wr = g_l.bf16(), g_r.bf16()
-        wd = g_d.bf16()
+        (wl, sl), (wr, sr) = g_l.operand(), g_r.operand()
+        if (sl is None) != (sr is None):  # one factor still resident: copy the other one alone
+            lib().gather_rows(wl if sl is not None else wr, [sl if sl is not None else sr])
+            sl = sr = None
         N, F_ = x.shape[0], wl.shape[0]
         h = torch.empty(N, F_, device=x.device, dtype=torch.bfloat16)
         l = torch.empty_like(h)
         r = torch.empty_like(h)
-        lib().bilinear(x, wl, wr, bl, br, int(mode), h, l, r)
+        lib().bilinear(x, wl, wr, bl, br, int(mode), h, l, r, _gathers(sl, sr) if sl is not None else None)
+        wd, sd = g_d.operand()
         if residual is not None:
             out = torch.empty(N, wd.shape[0], device=x.device, dtype=torch.float32)
-            _mm(h, wd.t(), out, c=residual, alpha=alpha, beta=1.0, bias=bd)
+            _mm(h, wd.t(), out, c=residual, alpha=alpha, beta=1.0, bias=bd, gather=_gathers(sd))
         else:
             out = torch.empty(N, wd.shape[0], device=x.device, dtype=torch.bfloat16)
-            _mm(h, wd.t(), out, alpha=alpha, bias=bd)
+            _mm(h, wd.t(), out, alpha=alpha, bias=bd, gather=_gathers(sd))
         ctx.save_for_backward(x, h, l, r)
         ctx.groups = (g_l, g_r, g_d)
         ctx.alpha, ctx.mode, ctx.has_res = alpha, mode, residual is not None

@@ -49,12 +49,22 @@ class WeightGroup:
         self._key = None
         self._grad = None
         self._shard = None  # (sharding layer, unit) under parameter-sharded data parallelism
+        self._gather = None  # parallel.gather.GatheredWeight when the bf16 rows are sharded across ranks
 
     # ------------------------------------------------------------------ forward operand
     def _version_key(self):
         return (_STEPS[0],) + tuple((p.data_ptr(), p._version) for p in self.params)
 
+    def operand(self):
+        """(bf16 weight, gather description or None) for a GEMM that can gather row-sharded weights
+        itself: with a description, the returned staging buffer is filled by that GEMM."""
+        if self._gather is not None:
+            return self._gather.operand()
+        return self.bf16(), None
+
     def bf16(self) -> torch.Tensor:
+        if self._gather is not None:
+            return self._gather.resident()
         if self._shard is not None and self._cache is not None:
             return self._cache  # written by the sharding layer's gather, once per optimizer step
         key = self._version_key()
@@ -126,6 +136,9 @@ class SpectralWeights:
     def _version_key(self):
         return (_STEPS[0],) + tuple((t.data_ptr(), t._version) for lin in self.linears
                                     for t in (lin.weight, lin.gamma, lin.u, lin.v))
+
+    def operand(self):
+        return self.bf16(), None
 
     def bf16(self) -> torch.Tensor:
         from ..models.normalization import SIGMA_FLOOR

@@ -179,6 +179,11 @@ class ShardedDataParallel:
             self._flat_len = self.world * self.shard
         self._cache_mode = self.shard_params and fused  # non-owned weights exist only as bf16 caches
         self._build_sharded_layout(sspec, s_owner)
+        # fused all-gather (parallel/gather.py): the bf16 rows of the sharded groups are split across the
+        # ranks and gathered by the GEMMs that read them, instead of a full bf16 copy on every rank
+        self.fused_gather = (self.peer and self._cache_mode and os.environ.get("TTB_FUSED_GATHER", "1") != "0"
+                             and all(sum(su.group.rows) % 64 == 0 and su.group.d_in % 8 == 0 for su in self.sunits))
+        self.window = None
         if self.peer:
             self._init_symmetric(device, dtype)
         else:
@@ -370,8 +375,34 @@ class ShardedDataParallel:
             self._comm = torch.cuda.Stream(device)
             self._slot_free = [None, None]  # event: every owner has read the slot (None: never used)
             handles += [hs, ht]
+            if self.fused_gather:
+                handles.append(self._init_row_shards(device))
         self._handles = handles
         self._epoch = 0
+
+    def _init_row_shards(self, device):
+        """Symmetric bf16 buffer of this rank's row slice of every sharded group (same offsets on every
+        rank), the staging window, and each group's gather description."""
+        import torch.distributed._symmetric_memory as symm_mem
+
+        from .gather import GatheredWeight, GatherWindow, row_cuts
+        group = self.group if self.group is not None else dist.group.WORLD
+        woff, largest = 0, 0
+        for su in self.sunits:
+            su.rows, su.cols = sum(su.group.rows), su.group.d_in
+            su.cuts = row_cuts(su.rows, self.world)
+            su.woff = woff
+            woff += _aligned(max(b - a for a, b in zip(su.cuts, su.cuts[1:])) * su.cols)
+            largest = max(largest, su.rows * su.cols)
+        self.wshard = symm_mem.empty(max(woff, ALIGN), dtype=torch.bfloat16, device=device)
+        handle = symm_mem.rendezvous(self.wshard, group)
+        self._wsptrs = [int(x) for x in handle.buffer_ptrs]
+        slots = int(os.environ.get("TTB_GATHER_SLOTS", "8"))
+        self.window = GatherWindow(device, slots, (largest + 127) // 128 * 128)
+        for su in self.sunits:
+            su.group._gather = GatheredWeight(self.window, su.rows, su.cols, su.cuts,
+                                              [base + 2 * su.woff for base in self._wsptrs])
+        return handle
 
     def _build_gather_plan(self):
         """Copy segments of the fused all-gather: every replicated unit from its owner's buffer into
@@ -394,6 +425,13 @@ class ShardedDataParallel:
             rows.append((src, dst32, dst16, n4 if dst16 == 0 else n))
             max_n = max(max_n, n4)
         for su in self.sunits:
+            if self.fused_gather:  # this rank's rows of the group, from the owner's master
+                lo, hi = su.cuts[self.rank], su.cuts[self.rank + 1]
+                if hi > lo:
+                    rows.append((self._spptrs[su.owner] + 4 * (su.goff + lo * su.cols), 0,
+                                 self.wshard.data_ptr() + 2 * su.woff, (hi - lo) * su.cols))
+                    max_n = max(max_n, (hi - lo) * su.cols)
+                continue
             cache = su.group.bf16()
             assert cache.numel() == su.n and su.n % 4 == 0
             rows.append((self._spptrs[su.owner] + 4 * su.goff, 0, cache.data_ptr(), su.n))
@@ -636,6 +674,9 @@ class ShardedDataParallel:
             for kind, obj, *_ in self.units:
                 if kind == "group":
                     obj._key = obj._version_key()  # the caches were written from the gathered values
+            if self.fused_gather:
+                self.window.invalidate()
+                self._barrier()  # every rank's row shards are written before any GEMM gathers from them
             return
         if self.world > 1:
             if self.backend == "nccl":

@@ -18,11 +18,13 @@ CFG = Config(model=ModelConfig(layers=3, d_model=256, heads=4, d_key=64, d_value
              train=TrainConfig(optimizer="muon", lr=0.01, aux_adamw_lr=0.003, grad_clip=0.5))
 
 
-def build(shard: bool, peer: bool):
+def build(shard: bool, peer: bool, gather: bool = True):
     os.environ["TTB_PEER_COLLECTIVES"] = "1" if peer else "0"
+    os.environ["TTB_FUSED_GATHER"] = "1" if gather else "0"
     torch.manual_seed(0)
     eng = TrainEngine(CFG, device="cuda", micro_batch=2, shard_params=shard)
     assert eng.dp.peer == peer and eng.dp.shard_params == shard
+    assert eng.dp.fused_gather == (shard and peer and gather)
     return eng
 
 
@@ -44,10 +46,12 @@ def main():
     dist.init_process_group("nccl")
     rank, world = dist.get_rank(), dist.get_world_size()
     torch.cuda.set_device(int(os.environ["LOCAL_RANK"]))
-    engines = {"replicated": build(False, True), "sharded_peer": build(True, True), "sharded_nccl": build(True, False)}
+    engines = {"replicated": build(False, True), "sharded_gather": build(True, True),
+               "sharded_peer": build(True, True, gather=False), "sharded_nccl": build(True, False)}
+    sharded = ("sharded_gather", "sharded_peer", "sharded_nccl")
     ref = engines["replicated"]
     ref_state = {k: v.detach().cpu() for k, v in ref.model.state_dict().items()}
-    for name in ("sharded_peer", "sharded_nccl"):
+    for name in sharded:
         eng = engines[name]
         dp = eng.dp
         assert dp.model._ttb_weights_remote
@@ -57,9 +61,17 @@ def main():
         full = dp.full_state_dict(dst=None)
         for k, v in ref_state.items():  # the streamed initialisation is the serial one, bit for bit
             assert torch.equal(full[k], v), f"{name}: initial {k} differs"
-        for su in dp.sunits:  # every rank's bf16 caches come from the owners' masters
+        for su in dp.sunits:  # every rank's bf16 operands come from the owners' masters
             want = torch.cat([ref_state[n].reshape(-1) for n in su.names]).to("cuda").bfloat16()
-            assert torch.equal(su.group._cache.reshape(-1), want), f"{name}: cache of {su.names[0]}"
+            if dp.fused_gather:
+                # no full copy on any rank: this rank's row shard, and the rows gathered from both ranks
+                assert su.group._cache is None, f"{name}: a full bf16 copy of {su.names[0]}"
+                lo, hi = su.cuts[rank], su.cuts[rank + 1]
+                mine = dp.wshard[su.woff:su.woff + (hi - lo) * su.cols]
+                assert torch.equal(mine, want[lo * su.cols:hi * su.cols]), f"{name}: row shard of {su.names[0]}"
+                assert torch.equal(su.group.bf16().reshape(-1), want), f"{name}: gathered {su.names[0]}"
+            else:
+                assert torch.equal(su.group._cache.reshape(-1), want), f"{name}: cache of {su.names[0]}"
     g = torch.Generator().manual_seed(1)
     losses = {k: [] for k in engines}
     for step in range(3):
@@ -70,7 +82,12 @@ def main():
     torch.cuda.synchronize()
     check_status()
     final = {k: v.detach().cpu() for k, v in ref.model.state_dict().items()}
-    for name in ("sharded_peer", "sharded_nccl"):
+    window = engines["sharded_gather"].dp.window
+    assert window.gathers > 0
+    if rank == 0:
+        print(f"sharded_gather: {window.gathers} gathers, window {window.nbytes / 2**20:.1f} MiB, "
+              f"row shards {engines['sharded_gather'].dp.wshard.numel() * 2 / 2**20:.1f} MiB", flush=True)
+    for name in sharded:
         for a, b in zip(losses[name], losses["replicated"]):
             assert abs(a - b) < 1e-3 * abs(b), (name, losses[name], losses["replicated"])
         full = engines[name].dp.full_state_dict(dst=None)

@@ -12,6 +12,8 @@
 * MuonAdamW writes the updated bf16 operand caches, which then equal a fresh conversion of the
   fp32 weights bit for bit.
 """
+import copy
+
 import pytest
 import torch
 
@@ -71,9 +73,11 @@ def test_fused_adamw_resumes_a_host_counter_adamw_state():
     ours = [p.detach().clone().requires_grad_(True) for p in first]
     ref = [p.detach().clone().requires_grad_(True) for p in first]
     opt = FusedAdamW([{"params": ours, "weight_decay": 0.1}], lr=2e-3)
-    opt.load_state_dict(saved)
+    # torch's loader keeps the given state tensors (no copy) where device and dtype already match, so
+    # each optimizer loads its own copy instead of both updating the donor's moment tensors
+    opt.load_state_dict(copy.deepcopy(saved))
     topt = torch.optim.AdamW([{"params": ref, "weight_decay": 0.1}], lr=2e-3, foreach=False)
-    topt.load_state_dict(saved)
+    topt.load_state_dict(copy.deepcopy(saved))
     assert all(opt.state[p]["step"].is_cuda for p in ours) and opt.param_groups[0]["fused"] is True
     for step_grads in grads[1:]:
         for p, q, g in zip(ours, ref, step_grads):

@@ -44,3 +44,28 @@ def test_parameter_sharded_steps_match_single_process(optimizer, nproc, tmp_path
     assert float(line.split()[1]) < 1e-10
     line = next(x for x in out.stdout.splitlines() if x.startswith("RESUMEERR"))
     assert float(line.split()[1]) == 0.0
+
+
+def test_row_cuts_and_gather_window_residency():
+    """Row shards of a gathered weight are 64-row aligned and cover every row; the staging window
+    hands out a resident group without a gather and evicts the least recently used slot."""
+    from tensor_train_ing_b200.parallel.gather import GatheredWeight, GatherWindow, row_cuts
+    assert row_cuts(1280, 2) == [0, 640, 1280]
+    cuts = row_cuts(768, 8)
+    assert cuts[0] == 0 and cuts[-1] == 768 and all(c % 64 == 0 for c in cuts)
+    assert all(a <= b for a, b in zip(cuts, cuts[1:]))
+    with pytest.raises(ValueError):
+        row_cuts(100, 2)
+    win = GatherWindow("cpu", 2, 64 * 8)
+    a, b, c = (GatheredWeight(win, 64, 8, [0, 64], [0]) for _ in range(3))
+    _, spec = a.operand()
+    assert spec[3] == 4  # first gather of a: done target 4
+    assert a.operand()[1] is None  # resident
+    b.operand()
+    c.operand()  # evicts a (least recently used)
+    view, spec = a.operand()
+    assert spec is not None and spec[3] == 8 and view.shape == (64, 8)
+    assert b.operand()[1] is not None  # b was evicted by a
+    win.invalidate()
+    assert a.operand()[1] is not None  # the shards changed: gather again
+    assert win.gathers == 6
