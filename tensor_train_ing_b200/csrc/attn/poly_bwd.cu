@@ -13,7 +13,7 @@
 // dq kernel:  S1, S2, dP tiles of 64 keys in TMEM, dS written back into TMEM as the A operand of
 //             dQ1 += dS1 K1 and dQ2 += dS2 K2 (TMEM accumulators).
 // dkv kernel: the transposed scores S1^T, S2^T, dP^T of 32 queries in TMEM, P^T and dS^T written
-//             to 64B-swizzled SMEM, accumulating dV, dK1, dK2 in TMEM (480 of the 512 columns at
+//             to 64B-swizzled SMEM, accumulating dV, dK1, dK2 in TMEM (384 columns; 480 of the 512 with the scores, at
 //             head dim 128).  Learned kind parameters get per-key-block partial sums reduced later
 //             in a fixed order.  Reference: tnlm/kernels/poly_attn.py:78-202.
 #include "../common/host.h"

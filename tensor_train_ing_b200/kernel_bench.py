@@ -4,6 +4,9 @@
     python -m tensor_train_ing_b200.kernel_bench profile CASE         three launches of one case (for ncu -k/-c)
     python -m tensor_train_ing_b200.kernel_bench attn_scale [norope]  attention at four (B, T) with B*T fixed:
                                                                        fixed cost vs cost per key block
+    torchrun --nproc-per-node N -m tensor_train_ing_b200.kernel_bench gather_nvlink
+                                                                       the all-gather fused into the GEMM over
+                                                                       NVLink against NCCL all-gather + GEMM
 
 Cases (shapes of one 1B micro-batch, 8 x 2048 tokens, unless noted): gemm_qkv, gemm_dx, gemm_dw,
 bilinear, bilinear_grad, attn_fwd, attn_bwd, attn_case (B=2 for profiling), rmsnorm_fwd,
@@ -167,12 +170,29 @@ def build(name: str) -> _Case:
         v = torch.nn.functional.normalize(torch.randn(D, device="cuda"), dim=0)
         out = torch.empty(DMLP, D, device="cuda", dtype=torch.bfloat16)
         return _Case(lambda: C.spectral_cast(W, gamma, u, v, 1e-12, out), 0, DMLP * D * (4 + 4 + 2))
+    if name == "gemm_qkv_gather":
+        # the QKV GEMM gathering its weight from eight row shards (local buffers standing in for the
+        # ranks): the copy's HBM traffic overlapped with the MMAs
+        from .parallel.gather import row_cuts
+        a = torch.randn(N, D, device="cuda").bfloat16()
+        w = torch.randn(5 * H * DK, D, device="cuda").bfloat16()
+        cuts = row_cuts(w.shape[0], 8)
+        shards = [w[x:y].clone() for x, y in zip(cuts, cuts[1:])]
+        staging = torch.empty_like(w)
+        done = torch.zeros(w.shape[0] // 64, dtype=torch.int32, device="cuda")
+        out = torch.empty(N, 5 * H * DK, device="cuda", dtype=torch.bfloat16)
+        uses = [0]
+
+        def run():
+            uses[0] += 1
+            C.mm(a, staging.t(), out, gather=[([t.data_ptr() for t in shards], cuts, done, 4 * uses[0])])
+        return _Case(run, 2.0 * N * D * 5 * H * DK)
     raise KeyError(name)
 
 
 CASES = ["gemm_qkv", "gemm_dx", "gemm_dw", "bilinear", "bilinear_grad", "attn_fwd", "attn_bwd", "rmsnorm_fwd",
          "rmsnorm_bwd", "ce_fwd", "ce_bwd", "ce_bwd_kept", "embed_fwd", "embed_bwd", "adamw", "muon_prepare",
-         "muon_apply", "norm_lagged_fwd", "norm_lagged_bwd", "spectral_cast"]
+         "muon_apply", "norm_lagged_fwd", "norm_lagged_bwd", "spectral_cast", "gemm_qkv_gather"]
 
 
 def time_case(name: str, reps: int = 10) -> dict:
@@ -250,6 +270,85 @@ def attn_scaling(rope: bool = True, shapes=((16, 1024), (8, 2048), (4, 4096), (2
     return out
 
 
+def gather_nvlink(shapes=((8192, 5 * 6144, 6144), (8192, 6144, 6144), (8192, 6144, 24576)), reps: int = 10):
+    """The all-gather fused into the GEMM over NVLink (run under torchrun, one GPU per rank): each rank
+    holds a row slice of a bf16 weight in symmetric memory; per shape (32B QKV, output and down
+    projections at a 2 x 4096-token micro-batch) the fused gather GEMM, NCCL's all-gather followed
+    by the same GEMM, the GEMM alone and the gather alone, CUDA-event timed, max over ranks.  The
+    roofline is the slower of the GEMM's FLOPs at the measured bf16 peak and the bytes this rank
+    pulls over NVLink at 770 GB/s per direction."""
+    import os
+
+    import torch.distributed as dist
+    import torch.distributed._symmetric_memory as symm_mem
+
+    from .ops._ext import check_status
+    from .parallel.gather import row_cuts
+    os.environ.setdefault("TORCH_SYMM_MEM_DISABLE_MULTICAST", "1")
+    dist.init_process_group("nccl")
+    rank, world = dist.get_rank(), dist.get_world_size()
+    torch.cuda.set_device(int(os.environ.get("LOCAL_RANK", rank)))
+    C = _lib()
+    peak = 1639.2e12
+    try:
+        with open(os.path.join(os.path.dirname(os.path.dirname(os.path.abspath(__file__))),
+                               "MEASURED_PEAKS.json")) as fh:
+            peak = float(json.load(fh).get("bf16_tflops", 1639.2)) * 1e12
+    except (OSError, ValueError):
+        pass
+    for M, Nw, K in shapes:
+        torch.manual_seed(0)
+        w = torch.randn(Nw, K, device="cuda").bfloat16()  # the same full weight on every rank (seeded)
+        cuts = row_cuts(Nw, world)
+        lo, hi = cuts[rank], cuts[rank + 1]
+        buf = symm_mem.empty(max(b - a for a, b in zip(cuts, cuts[1:])) * K, dtype=torch.bfloat16, device="cuda")
+        buf[:(hi - lo) * K].copy_(w[lo:hi].reshape(-1))
+        handle = symm_mem.rendezvous(buf, dist.group.WORLD)
+        ptrs = [int(p) for p in handle.buffer_ptrs]
+        dist.barrier()
+        torch.cuda.synchronize()
+        x = torch.randn(M, K, device="cuda").bfloat16()
+        staging = torch.empty_like(w)
+        done = torch.zeros(Nw // 64, dtype=torch.int32, device="cuda")
+        out = torch.empty(M, Nw, device="cuda", dtype=torch.bfloat16)
+        uses = [0]
+        even = Nw % world == 0
+        full = torch.empty_like(w)
+
+        def fused():
+            uses[0] += 1
+            C.mm(x, staging.t(), out, gather=[(ptrs, cuts, done, 4 * uses[0])])
+
+        def alone():
+            uses[0] += 1
+            C.gather_rows(staging, [(ptrs, cuts, done, 4 * uses[0])])
+
+        def nccl():
+            dist.all_gather_into_tensor(full, w[rank * Nw // world:(rank + 1) * Nw // world].contiguous())
+            C.mm(x, full.t(), out)
+
+        row = {"M": M, "N": Nw, "K": K, "world": world}
+        for name, fn in (("fused_us", fused), ("gemm_us", lambda: C.mm(x, w.t(), out)), ("gather_us", alone),
+                         ("nccl_ag_then_gemm_us", nccl if even else None)):
+            if fn is None:
+                continue
+            t = torch.tensor([_event_time(fn, reps)], device="cuda")
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            row[name] = round(float(t), 1)
+        check_status()
+        assert torch.equal(staging, w), "gathered weight differs"
+        remote = (Nw - (hi - lo)) * K * 2
+        roof_us = max(2.0 * M * Nw * K / peak, remote / 770e9) * 1e6
+        row.update(remote_MB=round(remote / 1e6, 1), roofline_us=round(roof_us, 1),
+                   fused_of_roofline=round(roof_us / row["fused_us"], 3),
+                   gather_GBps=round(remote / row["gather_us"] / 1e3, 1))
+        if rank == 0:
+            print(json.dumps(row), flush=True)
+        del handle
+        dist.barrier()
+    dist.destroy_process_group()
+
+
 def profile_case(name: str):
     case = build(name)
     for _ in range(3):
@@ -267,6 +366,9 @@ def main(argv=None):
     if mode == "profile":
         for n in names:
             profile_case(n)
+        return
+    if mode == "gather_nvlink":
+        gather_nvlink()
         return
     if mode == "attn_scale":
         attn_scaling(rope="norope" not in argv[1:])

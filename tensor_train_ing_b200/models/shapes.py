@@ -89,15 +89,26 @@ def activation_bytes_per_token_layer(cfg: ModelConfig) -> float:
     return 4 * d + 2 * 2 * d + qkv + 2 * H * cfg.d_value + 2 * 2 * cfg.d_mlp + 16
 
 
+def largest_weight_group(cfg: ModelConfig) -> int:
+    """Elements of the largest matrix group one GEMM reads (fused QKV, one bilinear factor, the down
+    projection or the unembedding): the size of a gather staging slot."""
+    d, H = cfg.d_model, cfg.heads
+    qk = 4 if cfg.attention in ("signed_product", "lower_degree_mix") else 2
+    qkv = (qk * H * cfg.d_key + H * cfg.d_value) * d
+    return max(qkv, cfg.d_mlp * d, cfg.padded_vocab * d)
+
+
 def memory_plan(cfg: ModelConfig, *, gpus: int, micro_tokens_per_gpu: int, gpu_gb: float = 180.0,
                 checkpointing: bool | None = None, workspace_gb: float = 4.0, optimizer: str = "muon",
-                shard_params: bool = False) -> dict:
+                shard_params: bool = False, fused_gather: bool = True, gather_slots: int = 8) -> dict:
     """Per-GPU bytes of the owner-computes layout plus one micro-batch of activations.
 
     Replicated layout: fp32 parameters and gradients and the bf16 GEMM caches on every rank, the
     optimizer state sharded.  ``shard_params``: the block matrices and the unembedding keep fp32
-    master, gradient accumulator and optimizer state only on their owner (1/gpus each), every rank
-    holds their bf16 caches and two per-block fp32 staging slots; embedding and vectors replicated."""
+    master, gradient accumulator and optimizer state only on their owner (1/gpus each) and two
+    per-block fp32 staging slots; their bf16 rows are split across the ranks (1/gpus each) and
+    gathered by the consuming GEMMs into ``gather_slots`` staging slots (``fused_gather``), or held
+    in full on every rank; embedding and vectors replicated."""
     ckpt = cfg.activation_checkpointing if checkpointing is None else checkpointing
     c = count_params(cfg)
     n = c["total"]
@@ -110,7 +121,8 @@ def memory_plan(cfg: ModelConfig, *, gpus: int, micro_tokens_per_gpu: int, gpu_g
     if shard_params:
         sharded = hidden + unembed
         staging = 2 * 4 * max(c["per_block"], unembed)
-        weights = 2 * sharded + 8 * sharded / gpus + 10 * (n - sharded) + staging
+        bf16 = 2 * sharded / gpus + 2 * gather_slots * largest_weight_group(cfg) if fused_gather else 2 * sharded
+        weights = bf16 + 8 * sharded / gpus + 10 * (n - sharded) + staging
     else:
         weights = (4 + 4 + 2) * n
     per_layer = activation_bytes_per_token_layer(cfg)
@@ -121,8 +133,9 @@ def memory_plan(cfg: ModelConfig, *, gpus: int, micro_tokens_per_gpu: int, gpu_g
     chunk = min(micro_tokens_per_gpu, cfg.loss_chunk_tokens or micro_tokens_per_gpu)
     loss = 2 * chunk * cfg.padded_vocab + 8 * micro_tokens_per_gpu
     total = weights + opt + act + loss + workspace_gb * 1e9
-    layout = ("owner-computes, parameter-sharded: fp32 masters/grads/optimizer state on owners, bf16 caches "
-              "replicated" if shard_params else
+    layout = ("owner-computes, parameter-sharded: fp32 masters/grads/optimizer state on owners, bf16 rows "
+              + ("split across ranks and gathered by the GEMMs" if fused_gather else "replicated")
+              if shard_params else
               "owner-computes: replicated fp32 params/grads + bf16 caches, sharded optimizer state")
     return {"params_B": round(n / 1e9, 3), "gpus": gpus, "micro_tokens_per_gpu": micro_tokens_per_gpu,
             "checkpointing": ckpt, "shard_params": shard_params, "replicated_state_GB": round(weights / 1e9, 1),
