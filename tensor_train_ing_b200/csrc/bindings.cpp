@@ -286,7 +286,7 @@ Tensor embed_fwd(const Tensor& idx, const Tensor& W) {
   auto x = torch::empty({idx.numel(), W.size(1)}, W.options());
   if (idx.numel() > 0)
     ttb::embed_fwd(reinterpret_cast<const long long*>(idx.data_ptr<int64_t>()), W.data_ptr<float>(), x.data_ptr<float>(), idx.numel(), W.size(1),
-                   cur_stream());
+                   W.size(0), cur_stream());
   return x;
 }
 
@@ -300,7 +300,7 @@ void embed_bwd(const Tensor& idx, const Tensor& dx, Tensor& dW) {
   auto ids = std::get<0>(sorted).contiguous();
   auto order = std::get<1>(sorted).contiguous();
   ttb::embed_bwd(reinterpret_cast<const long long*>(ids.data_ptr<int64_t>()), reinterpret_cast<const long long*>(order.data_ptr<int64_t>()), dx.data_ptr<float>(), dW.data_ptr<float>(),
-                 idx.numel(), dW.size(1), cur_stream());
+                 idx.numel(), dW.size(1), dW.size(0), cur_stream());
 }
 
 // ------------------------------------------------------------------ fused linear + CE

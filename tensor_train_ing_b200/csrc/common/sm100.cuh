@@ -23,6 +23,7 @@ enum : uint32_t {
   kErrTimeoutEpilogue = 3,
   kErrTimeoutPeer = 4,
   kErrBadArgument = 5,
+  kErrBadIndex = 6,  // a data-dependent index (token id, target) outside its table; the access was skipped
 };
 
 // Cycles a single wait may spin before giving up (about 1 s at 2 GHz).

@@ -89,7 +89,7 @@ struct EpiCEBwd {
     if (row < M) {
       tgt = targets[row];
       l = lse[row];
-      coef = tgt >= 0 ? grad[0] * alpha : 0.f;
+      coef = tgt >= 0 && tgt < V ? grad[0] * alpha : 0.f;  // out-of-range targets: no loss, no gradient
     }
 #pragma unroll 1
     for (int c = 0; c < NB / 32; ++c) {
@@ -116,7 +116,7 @@ struct EpiCEBwd {
     if (row < M) {
       tgt = targets[row];
       l = lse[row];
-      coef = tgt >= 0 ? grad[0] * alpha : 0.f;
+      coef = tgt >= 0 && tgt < V ? grad[0] * alpha : 0.f;  // out-of-range targets: no loss, no gradient
     }
 #pragma unroll 1
     for (int c = 0; c < NB / 32; ++c) {
@@ -150,7 +150,7 @@ __global__ void __launch_bounds__(256) ce_grad_from_logits_kernel(const float* _
   if (row >= M) return;
   const float l = lse[row];
   const long long t = targets[row];
-  const float coef = t >= 0 ? grad[0] * alpha : 0.f;
+  const float coef = t >= 0 && t < Npad ? grad[0] * alpha : 0.f;
   const float4* zr = reinterpret_cast<const float4*>(z + static_cast<long long>(row) * ldz);
   uint2* dr = reinterpret_cast<uint2*>(dlog + static_cast<long long>(row) * ldd);
   for (int i = threadIdx.x; i < Npad / 4; i += blockDim.x) {
@@ -165,9 +165,12 @@ __global__ void __launch_bounds__(256) ce_grad_from_logits_kernel(const float* _
   }
 }
 
+// A target outside [0, V) (other than the negative ignore ids) is recorded in the status word and
+// its row contributes no loss.
 __global__ void ce_combine_kernel(const float* __restrict__ pmax, const float* __restrict__ psum, long long ldp,
                                   int tiles, const float* __restrict__ tlogit, const long long* __restrict__ targets,
-                                  float* __restrict__ lse, float* __restrict__ loss_row, int M) {
+                                  float* __restrict__ lse, float* __restrict__ loss_row, int M, int V,
+                                  uint32_t* status) {
   const int warps = blockDim.x / 32;
   const int lane = threadIdx.x % 32;
   for (int row = blockIdx.x * warps + threadIdx.x / 32; row < M; row += gridDim.x * warps) {
@@ -185,7 +188,9 @@ __global__ void ce_combine_kernel(const float* __restrict__ pmax, const float* _
     if (lane == 0) {
       const float l = mx + logf(s);
       lse[row] = l;
-      loss_row[row] = targets[row] >= 0 ? l - tlogit[row] : 0.f;
+      const long long t = targets[row];
+      if (t >= V) record_error(status, kErrBadIndex);
+      loss_row[row] = t >= 0 && t < V ? l - tlogit[row] : 0.f;
     }
   }
 }
@@ -204,7 +209,8 @@ void ce_forward(const Operand& x, const Operand& w, int M, int V, int K, float a
   gemm::EpiCEFwd<256> epi{pmax, psum, tiles, tlogit, targets, alpha, M, V, zout, ldz, Npad};
   gemm::dispatch<256, 4, false>(x, w, nullptr, gemm::Shape{M, V, K, status_ptr()}, epi, stream);
   const int grid = (M + 7) / 8 < 4 * num_sms() ? (M + 7) / 8 : 4 * num_sms();
-  gemm::ce_combine_kernel<<<grid, 256, 0, stream>>>(pmax, psum, tiles, tiles, tlogit, targets, lse, loss_row, M);
+  gemm::ce_combine_kernel<<<grid, 256, 0, stream>>>(pmax, psum, tiles, tiles, tlogit, targets, lse, loss_row, M, V,
+                                                    status_ptr());
   TTB_CUDA_CHECK(cudaGetLastError());
 }
 

@@ -519,27 +519,40 @@ __global__ void rope_kernel(__nv_bfloat16* __restrict__ buf, long long ld, int N
   }
 }
 
-// x[t, :] = W[idx[t], :]   (fp32 rows; d multiple of 4)
+// x[t, :] = W[idx[t], :]   (fp32 rows; d multiple of 4).  An id outside [0, V) is recorded in the
+// status word and its row is written as zeros instead of being read from outside the table.
 __global__ void embed_fwd_kernel(const long long* __restrict__ idx, const float* __restrict__ W,
-                                 float* __restrict__ x, int N, int d) {
+                                 float* __restrict__ x, int N, int d, long long V, uint32_t* status) {
   const int warps = blockDim.x / 32;
   const int lane = threadIdx.x % 32;
   for (int t = blockIdx.x * warps + threadIdx.x / 32; t < N; t += gridDim.x * warps) {
-    const float4* src = reinterpret_cast<const float4*>(W + idx[t] * static_cast<long long>(d));
+    const long long id = idx[t];
     float4* dst = reinterpret_cast<float4*>(x + static_cast<long long>(t) * d);
+    if (id < 0 || id >= V) {
+      if (lane == 0) record_error(status, kErrBadIndex);
+      for (int j = lane; j < d / 4; j += 32) dst[j] = make_float4(0.f, 0.f, 0.f, 0.f);
+      continue;
+    }
+    const float4* src = reinterpret_cast<const float4*>(W + id * static_cast<long long>(d));
     for (int j = lane; j < d / 4; j += 32) dst[j] = src[j];
   }
 }
 
 // Deterministic embedding backward over tokens sorted by id (stable sort, so equal ids keep
 // their original order): the first position of each run sums the run's gradient rows in order.
+// Ids outside [0, V) are recorded in the status word and their gradient rows dropped.
 __global__ void embed_bwd_kernel(const long long* __restrict__ sorted_ids, const long long* __restrict__ order,
-                                 const float* __restrict__ dx, float* __restrict__ dW, int N, int d) {
+                                 const float* __restrict__ dx, float* __restrict__ dW, int N, int d, long long V,
+                                 uint32_t* status) {
   const int warps = blockDim.x / 32;
   const int lane = threadIdx.x % 32;
   for (int s = blockIdx.x * warps + threadIdx.x / 32; s < N; s += gridDim.x * warps) {
     const long long id = sorted_ids[s];
     if (s > 0 && sorted_ids[s - 1] == id) continue;
+    if (id < 0 || id >= V) {
+      if (lane == 0) record_error(status, kErrBadIndex);
+      continue;
+    }
     int e = s + 1;
     while (e < N && sorted_ids[e] == id) ++e;
     float* dst = dW + id * static_cast<long long>(d);
@@ -692,18 +705,18 @@ void rope_apply(void* buf, long long ld, int N, int rope_cols, int dk, const int
   TTB_CUDA_CHECK(cudaGetLastError());
 }
 
-void embed_fwd(const long long* idx, const float* W, float* x, int N, int d, cudaStream_t stream) {
+void embed_fwd(const long long* idx, const float* W, float* x, int N, int d, long long V, cudaStream_t stream) {
   TTB_CHECK(d % 4 == 0, "embedding: d must be a multiple of 4");
   const int grid = (N + 7) / 8 < 4 * num_sms() ? (N + 7) / 8 : 4 * num_sms();
-  embed_fwd_kernel<<<grid, 256, 0, stream>>>(idx, W, x, N, d);
+  embed_fwd_kernel<<<grid, 256, 0, stream>>>(idx, W, x, N, d, V, status_ptr());
   TTB_CUDA_CHECK(cudaGetLastError());
 }
 
 void embed_bwd(const long long* sorted_ids, const long long* order, const float* dx, float* dW, int N, int d,
-               cudaStream_t stream) {
+               long long V, cudaStream_t stream) {
   TTB_CHECK(d % 4 == 0, "embedding: d must be a multiple of 4");
   const int grid = (N + 7) / 8 < 4 * num_sms() ? (N + 7) / 8 : 4 * num_sms();
-  embed_bwd_kernel<<<grid, 256, 0, stream>>>(sorted_ids, order, dx, dW, N, d);
+  embed_bwd_kernel<<<grid, 256, 0, stream>>>(sorted_ids, order, dx, dW, N, d, V, status_ptr());
   TTB_CUDA_CHECK(cudaGetLastError());
 }
 

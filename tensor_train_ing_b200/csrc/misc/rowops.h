@@ -21,8 +21,10 @@ void rmsnorm_bwd_ex(const void* dy, bool dy_f32, const float* x, const float* w,
 // In-place rotary embedding of the first rope_cols columns (heads of width dk) of a bf16 [N, ld] buffer.
 void rope_apply(void* buf, long long ld, int N, int rope_cols, int dk, const int* pos, const float* inv_freq,
                 bool inverse, cudaStream_t stream);
-void embed_fwd(const long long* idx, const float* W, float* x, int N, int d, cudaStream_t stream);
+// Embedding rows of a V-row table; ids outside [0, V) set kErrBadIndex in the status word and are
+// skipped (zero rows forward, no gradient backward).
+void embed_fwd(const long long* idx, const float* W, float* x, int N, int d, long long V, cudaStream_t stream);
 void embed_bwd(const long long* sorted_ids, const long long* order, const float* dx, float* dW, int N, int d,
-               cudaStream_t stream);
+               long long V, cudaStream_t stream);
 
 }  // namespace ttb

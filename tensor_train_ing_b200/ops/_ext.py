@@ -34,7 +34,7 @@ KERNELS_PER_CALL = {"mm": 1, "bilinear": 1, "bilinear_grad": 1, "rmsnorm_fwd": 1
                     "rs_accumulate": 1, "ce_bwd_from_logits": 1, "adamw_update": 2, "muon_prepare": 1,
                     "muon_normalize": 1, "muon_apply": 1, "norm_variant_fwd": 1,
                     "norm_variant_bwd": _norm_variant_bwd_kernels, "spectral_cast": 2, "spectral_grad": 2,
-                    "spectral_power_step": 4}
+                    "spectral_power_step": 4, "gather_rows": 1}
 
 
 class _Counting:
@@ -113,5 +113,5 @@ def check_status():
     code = lib().status()
     if code:
         names = {1: "TMA producer wait", 2: "MMA issuer wait", 3: "epilogue wait", 4: "peer flag wait",
-                 5: "bad argument"}
+                 5: "bad argument", 6: "index out of range (token id or target); the access was skipped"}
         raise RuntimeError(f"sm_100a kernel reported error {code} ({names.get(code, 'unknown')})")

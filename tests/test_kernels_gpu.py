@@ -257,3 +257,43 @@ def test_ce_backward_from_kept_logits_equals_recompute():
         assert (a.float() - b.float()).abs().max().item() <= 1e-5 * max(1.0, b.float().abs().max().item())
     torch.cuda.synchronize()
     assert lib().status() == 0
+
+
+def test_out_of_range_ids_and_targets_are_reported_and_skipped():
+    """Token ids outside the embedding table and targets outside the vocabulary set the status word's
+    bad-index code; the embedding writes zero rows (and drops their gradients) instead of reading
+    outside the table, the loss of such a target row is zero, and later kernels run normally.  The
+    table is a view with spare rows on both sides, so even a broken check would read mapped memory."""
+    from tensor_train_ing_b200.ops._ext import check_status, lib
+    V, d = 100, 64
+    big = torch.randn(V + 2, d, device="cuda")
+    W = big[1:V + 1]
+    idx = torch.tensor([3, V, 7, -1, 5], device="cuda", dtype=torch.long)
+    x = lib().embed_fwd(idx, W)
+    torch.cuda.synchronize()
+    with pytest.raises(RuntimeError, match="index out of range"):
+        check_status()
+    assert torch.equal(x[[0, 2, 4]], W[[3, 7, 5]]) and not x[[1, 3]].any()
+    dW = torch.zeros_like(W)
+    spare = big[[0, V + 1]].clone()
+    lib().embed_bwd(idx, torch.ones(5, d, device="cuda"), dW)
+    torch.cuda.synchronize()
+    with pytest.raises(RuntimeError, match="index out of range"):
+        check_status()
+    assert torch.equal(dW[[3, 7, 5]], torch.ones(3, d, device="cuda")) and float(dW.abs().sum()) == 3 * d
+    assert torch.equal(big[[0, V + 1]], spare)
+    # a target past the vocabulary: no loss for its row, the others unchanged
+    M, K, Vp = 256, 128, 128
+    xs = torch.randn(M, K, device="cuda").bfloat16()
+    w = torch.randn(Vp, K, device="cuda").bfloat16()
+    tgt = torch.randint(0, V, (M,), device="cuda")
+    loss_ok, _ = lib().ce_fwd(xs, w, V, 1.0, tgt)
+    tgt_bad = tgt.clone()
+    tgt_bad[10] = V + 3
+    loss_bad, _ = lib().ce_fwd(xs, w, V, 1.0, tgt_bad)
+    torch.cuda.synchronize()
+    with pytest.raises(RuntimeError, match="index out of range"):
+        check_status()
+    keep = torch.arange(M, device="cuda") != 10
+    assert float(loss_bad[10]) == 0.0 and torch.equal(loss_bad[keep], loss_ok[keep])
+    check_status()  # cleared: later launches report nothing
