@@ -7,6 +7,9 @@
     torchrun --nproc-per-node N -m tensor_train_ing_b200.kernel_bench gather_nvlink
                                                                        the all-gather fused into the GEMM over
                                                                        NVLink against NCCL all-gather + GEMM
+    torchrun --nproc-per-node N -m tensor_train_ing_b200.kernel_bench peer_nvlink
+                                                                       the peer reduce-scatter / all-gather
+                                                                       kernels against NCCL, GB/s of NVLink
 
 Cases (shapes of one 1B micro-batch, 8 x 2048 tokens, unless noted): gemm_qkv, gemm_dx, gemm_dw,
 bilinear, bilinear_grad, attn_fwd, attn_bwd, attn_case (B=2 for profiling), rmsnorm_fwd,
@@ -349,6 +352,62 @@ def gather_nvlink(shapes=((8192, 5 * 6144, 6144), (8192, 6144, 6144), (8192, 614
     dist.destroy_process_group()
 
 
+def peer_nvlink(numel: int = 256 << 20, reps: int = 10):
+    """The data-parallel peer collectives over NVLink (run under torchrun, one GPU per rank): the pull
+    reduce-scatter with the fused sum of squares (``rs_reduce_sq``) and the pull all-gather with the
+    fused bf16 cache writes (``ag_pull_cast``) on a flat fp32 buffer of ``numel`` values (1 GiB by
+    default, the order of the 1B model's gradients), against NCCL's reduce-scatter and all-gather of
+    the same bytes.  CUDA-event time, max over ranks; the roofline is the bytes this rank pulls from
+    its peers at 770 GB/s per direction."""
+    import os
+
+    import torch.distributed as dist
+    import torch.distributed._symmetric_memory as symm_mem
+
+    from .ops._ext import check_status
+    os.environ.setdefault("TORCH_SYMM_MEM_DISABLE_MULTICAST", "1")
+    dist.init_process_group("nccl")
+    rank, world = dist.get_rank(), dist.get_world_size()
+    torch.cuda.set_device(int(os.environ.get("LOCAL_RANK", rank)))
+    C = _lib()
+    n = numel // (4 * world) * 4 * world
+    region = n // world
+    buf = symm_mem.empty(n, dtype=torch.float32, device="cuda")
+    buf.normal_()
+    handle = symm_mem.rendezvous(buf, dist.group.WORLD)
+    ptrs = [int(p) for p in handle.buffer_ptrs]
+    mine = torch.empty(region, device="cuda")
+    cache = torch.empty(n, device="cuda", dtype=torch.bfloat16)
+    segs = torch.tensor([(ptrs[q] + 4 * q * region, 0 if q == rank else buf.data_ptr() + 4 * q * region,
+                          cache.data_ptr() + 2 * q * region, region) for q in range(world)],
+                        dtype=torch.int64, device="cuda")
+    dist.barrier()
+    torch.cuda.synchronize()
+    plain = torch.empty(n, device="cuda")
+    shard = torch.empty(region, device="cuda")
+    cases = {
+        "rs_reduce_sq": lambda: C.rs_reduce_sq(ptrs, rank * region, mine),
+        "ag_pull_cast": lambda: C.ag_pull_cast(segs, region),
+        "nccl_reduce_scatter": lambda: dist.reduce_scatter_tensor(shard, plain),
+        "nccl_all_gather": lambda: dist.all_gather_into_tensor(plain, shard),
+    }
+    remote = (world - 1) * region * 4
+    row = {"world": world, "bytes_per_rank_GB": round(n * 4 / 1e9, 3), "pulled_GB": round(remote / 1e9, 3)}
+    for name, fn in cases.items():
+        t = torch.tensor([_event_time(fn, reps)], device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        us = float(t)
+        row[f"{name}_us"] = round(us, 1)
+        row[f"{name}_GBps"] = round(remote / us / 1e3, 1)
+        row[f"{name}_of_770"] = round(remote / us / 1e3 / 770.0, 3)
+    check_status()
+    if rank == 0:
+        print(json.dumps(row), flush=True)
+    del handle
+    dist.barrier()
+    dist.destroy_process_group()
+
+
 def profile_case(name: str):
     case = build(name)
     for _ in range(3):
@@ -366,6 +425,9 @@ def main(argv=None):
     if mode == "profile":
         for n in names:
             profile_case(n)
+        return
+    if mode == "peer_nvlink":
+        peer_nvlink()
         return
     if mode == "gather_nvlink":
         gather_nvlink()
