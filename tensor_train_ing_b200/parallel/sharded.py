@@ -181,9 +181,14 @@ class ShardedDataParallel:
         self._build_sharded_layout(sspec, s_owner)
         # fused all-gather (parallel/gather.py): the bf16 rows of the sharded groups are split across the
         # ranks and gathered by the GEMMs that read them, instead of a full bf16 copy on every rank
-        self.fused_gather = (self.peer and self._cache_mode and os.environ.get("TTB_FUSED_GATHER", "1") != "0"
+        # (default on with the peer transport; a one-rank CUDA engine takes it with TTB_FUSED_GATHER=1, which
+        # runs the whole path against its own memory)
+        want = os.environ.get("TTB_FUSED_GATHER", "1" if self.peer else "0") != "0"
+        self.fused_gather = (want and self._cache_mode and (self.peer or (self.world == 1 and device.type == "cuda"))
                              and all(sum(su.group.rows) % 64 == 0 and su.group.d_in % 8 == 0 for su in self.sunits))
         self.window = None
+        if self.fused_gather and not self.peer:
+            self._init_row_shards(device)
         if self.peer:
             self._init_symmetric(device, dtype)
         else:
@@ -383,10 +388,7 @@ class ShardedDataParallel:
     def _init_row_shards(self, device):
         """Symmetric bf16 buffer of this rank's row slice of every sharded group (same offsets on every
         rank), the staging window, and each group's gather description."""
-        import torch.distributed._symmetric_memory as symm_mem
-
         from .gather import GatheredWeight, GatherWindow, row_cuts
-        group = self.group if self.group is not None else dist.group.WORLD
         woff, largest = 0, 0
         for su in self.sunits:
             su.rows, su.cols = sum(su.group.rows), su.group.d_in
@@ -394,9 +396,16 @@ class ShardedDataParallel:
             su.woff = woff
             woff += _aligned(max(b - a for a, b in zip(su.cuts, su.cuts[1:])) * su.cols)
             largest = max(largest, su.rows * su.cols)
-        self.wshard = symm_mem.empty(max(woff, ALIGN), dtype=torch.bfloat16, device=device)
-        handle = symm_mem.rendezvous(self.wshard, group)
-        self._wsptrs = [int(x) for x in handle.buffer_ptrs]
+        handle = None
+        if self.peer:
+            import torch.distributed._symmetric_memory as symm_mem
+            group = self.group if self.group is not None else dist.group.WORLD
+            self.wshard = symm_mem.empty(max(woff, ALIGN), dtype=torch.bfloat16, device=device)
+            handle = symm_mem.rendezvous(self.wshard, group)
+            self._wsptrs = [int(x) for x in handle.buffer_ptrs]
+        else:  # one rank: its shard is every row, read from its own memory
+            self.wshard = torch.empty(max(woff, ALIGN), dtype=torch.bfloat16, device=device)
+            self._wsptrs = [self.wshard.data_ptr()]
         slots = int(os.environ.get("TTB_GATHER_SLOTS", "8"))
         self.window = GatherWindow(device, slots, (largest + 127) // 128 * 128)
         for su in self.sunits:
@@ -686,6 +695,12 @@ class ShardedDataParallel:
                     dist.broadcast(self.param_flat[r * self.shard:(r + 1) * self.shard], src=global_rank,
                                    group=self.group)
         if not self.shard_params:
+            return
+        if self.fused_gather:  # one rank: its row shard of every group is all of the group's rows
+            for su in self.sunits:
+                self.wshard[su.woff:su.woff + su.n].view(su.rows, su.cols).copy_(
+                    torch.cat([p.detach().reshape(-1, su.cols) for p in su.params]))
+            self.window.invalidate()
             return
         for su in self.sunits:
             src = self._ranks[su.owner]

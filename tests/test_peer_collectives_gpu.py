@@ -76,3 +76,42 @@ def test_parameter_sharded_single_gpu_matches_replicated():
     b = eng.dp.full_state_dict(dst=None)
     for k, v in a.items():
         assert torch.equal(b[k], v.cpu()), k
+
+
+def test_parameter_sharded_single_gpu_with_fused_gather_matches_replicated(monkeypatch):
+    """The fused all-gather path on one rank: the sharded groups' bf16 rows live only in the row-shard
+    buffer (no full cache), every forward GEMM gathers its weight into a window slot itself and the
+    other consumers find it resident or gather it alone.  The staged values equal the caches' values
+    and the kernels' arithmetic is unchanged, so training is bitwise identical to the replicated
+    engine."""
+    from tensor_train_ing_b200.config import Config, ModelConfig, TrainConfig
+    from tensor_train_ing_b200.engine import TrainEngine
+    from tensor_train_ing_b200.ops._ext import check_status
+    cfg = Config(model=ModelConfig(layers=2, d_model=256, heads=4, d_key=64, d_value=64, d_mlp=512, vocab_size=1000,
+                                   padded_vocab=1024, loss_chunk_tokens=512),
+                 train=TrainConfig(optimizer="muon", lr=0.01, aux_adamw_lr=0.003, grad_clip=1e9))
+    torch.manual_seed(0)
+    ref = TrainEngine(cfg, device="cuda", micro_batch=2, shard_params=False)
+    monkeypatch.setenv("TTB_FUSED_GATHER", "1")
+    monkeypatch.setenv("TTB_GATHER_SLOTS", "3")  # fewer slots than a block's groups: evictions and re-gathers
+    torch.manual_seed(0)
+    eng = TrainEngine(cfg, device="cuda", micro_batch=2, shard_params=True)
+    assert eng.dp.fused_gather and all(su.group._cache is None for su in eng.dp.sunits)
+    g = torch.Generator().manual_seed(1)
+    for _ in range(3):
+        idx = torch.randint(0, 1000, (4, 256), generator=g)
+        doc = torch.zeros_like(idx)
+        doc[:, 130:] = 1
+        tgt = torch.roll(idx, -1, 1)
+        tgt[:, -1] = -100
+        l1, _ = ref.step(idx, doc, tgt)
+        l2, _ = eng.step(idx, doc, tgt)
+        assert float(l1) == float(l2)
+    torch.cuda.synchronize()
+    check_status()
+    assert eng.dp.window.gathers > 3 * 2 * cfg.model.layers
+    assert all(su.group._cache is None for su in eng.dp.sunits)
+    a = ref.model.state_dict()
+    b = eng.dp.full_state_dict(dst=None)
+    for k, v in a.items():
+        assert torch.equal(b[k], v.cpu()), k
