@@ -209,3 +209,48 @@ def test_exposure_accepts_the_fused_adamw_kernel_optimizer():
     fused = FusedAdamW(optimizer_groups(model, 0.1), lr=0.01)
     assert (update_optimizer_exposure({"steps": 0, "tokens": 0}, fused)
             == update_optimizer_exposure({"steps": 0, "tokens": 0}, plain))
+
+
+def test_presets_count_the_parameters_the_benchmark_builds():
+    """The planner's parameter counts are those of the modules the benchmark instantiates (meta-device
+    blocks, never formulas): 2,018,084,864 for the 1B bench shape with its untied 50304-row vocabulary."""
+    from tensor_train_ing_b200.models.shapes import count_params, preset
+    cfg = preset("bench_1b", padded_vocab=50304, vocab_size=50257)
+    c = count_params(cfg)
+    assert c["total"] == 2018084864
+    assert c["embedding"] == 2 * 50304 * 2048
+    # per block: q1 k1 q2 k2 v o (6 d^2 at 16 x 128 = d) and L R D (3 d x 8192), plus norm vectors
+    assert c["non_embedding"] == 24 * (6 * 2048 ** 2 + 3 * 2048 * 8192)
+    assert c["total"] - c["embedding"] - c["non_embedding"] == 24 * (c["per_block"] - c["non_embedding"] // 24) + 2048
+
+
+def test_memory_plan_layouts_and_the_gathered_weights():
+    """Replicated state is 10 bytes per parameter; parameter sharding moves fp32 state to owners; the
+    fused all-gather keeps 1/N of the bf16 rows plus the staging window, so the 32B plan on 8 GPUs
+    shrinks by about 7/8 of the bf16 model."""
+    from tensor_train_ing_b200.models.shapes import count_params, largest_weight_group, memory_plan, min_gpus, preset
+    cfg = preset("bench_32b", loss_chunk_tokens=8192, activation_checkpointing=True)
+    rep = memory_plan(cfg, gpus=8, micro_tokens_per_gpu=8192)
+    shard = memory_plan(cfg, gpus=8, micro_tokens_per_gpu=8192, shard_params=True, fused_gather=False)
+    gath = memory_plan(cfg, gpus=8, micro_tokens_per_gpu=8192, shard_params=True)
+    assert not rep["fits"] and shard["fits"] and gath["fits"]
+    assert gath["total_GB"] < shard["total_GB"] < rep["total_GB"]
+    c = count_params(cfg)
+    sharded = c["non_embedding"] + cfg.padded_vocab * cfg.d_model
+    saved = 2 * sharded * 7 / 8 - 2 * 8 * largest_weight_group(cfg)
+    assert abs((shard["total_GB"] - gath["total_GB"]) - saved / 1e9) < 0.2
+    assert "gathered by the GEMMs" in gath["layout"]
+    small = min_gpus(preset("bench_1b", loss_chunk_tokens=8192), 16384)
+    assert small is not None and small["gpus"] == 1 and not small["shard_params"]
+
+
+def test_parameter_sharding_is_chosen_by_size_or_forced(monkeypatch):
+    from tensor_train_ing_b200.models.shapes import needs_parameter_sharding, preset
+    monkeypatch.delenv("TTB_SHARD_PARAMS", raising=False)
+    assert not needs_parameter_sharding(preset("bench_1b"), 8)
+    assert needs_parameter_sharding(preset("bench_32b"), 8)
+    assert not needs_parameter_sharding(preset("bench_32b"), 1)  # one rank cannot shard
+    monkeypatch.setenv("TTB_SHARD_PARAMS", "1")
+    assert needs_parameter_sharding(preset("bench_1b"), 2)
+    monkeypatch.setenv("TTB_SHARD_PARAMS", "0")
+    assert not needs_parameter_sharding(preset("bench_32b"), 8)
