@@ -64,13 +64,15 @@ __device__ __forceinline__ void gather_warp(const Gather& g, int lane) {
     uint4* d = reinterpret_cast<uint4*>(op.dst + static_cast<long long>(row) * op.cols);
     const int nvec = kGatherChunkRows * op.cols / 8;
     int i = lane;
-    for (; i + 3 * 32 < nvec; i += 4 * 32) {
-      // peer memory through L2 only (__ldcg): four loads in flight per lane before the stores
-      const uint4 v0 = __ldcg(s + i), v1 = __ldcg(s + i + 32), v2 = __ldcg(s + i + 64), v3 = __ldcg(s + i + 96);
-      d[i] = v0;
-      d[i + 32] = v1;
-      d[i + 64] = v2;
-      d[i + 96] = v3;
+    // peer memory through L2 only (__ldcg).  NVLink reads take microseconds, so the link is kept busy
+    // only with many bytes in flight: eight 16-byte loads per lane (4 KB per warp) before the stores.
+    constexpr int kUnroll = 8;
+    for (; i + (kUnroll - 1) * 32 < nvec; i += kUnroll * 32) {
+      uint4 v[kUnroll];
+#pragma unroll
+      for (int u = 0; u < kUnroll; ++u) v[u] = __ldcg(s + i + u * 32);
+#pragma unroll
+      for (int u = 0; u < kUnroll; ++u) d[i + u * 32] = v[u];
     }
     for (; i < nvec; i += 32) d[i] = __ldcg(s + i);
     __syncwarp();

@@ -104,6 +104,21 @@ __device__ __forceinline__ void tile_coords(int tile, int m_tiles, int n_tiles, 
   tn = in_group / gsize;
 }
 
+// Tile raster of a GEMM that gathers its B operand while it runs: groups of kGroupN column panels
+// sweep every row tile, so the first wave needs only kGroupN panels of the weight and the copy of
+// later panels overlaps the MMAs of earlier ones (the default raster sweeps every column panel for
+// its first rows, which would wait for the whole weight before the first group of rows finished).
+constexpr int kGroupN = 4;
+__device__ __forceinline__ void tile_coords_gather(int tile, int m_tiles, int n_tiles, int& tm, int& tn) {
+  const int per_group = kGroupN * m_tiles;
+  const int group = tile / per_group;
+  const int first_n = group * kGroupN;
+  const int gsize = min(n_tiles - first_n, kGroupN);
+  const int in_group = tile - group * per_group;
+  tn = first_n + in_group % gsize;
+  tm = in_group / gsize;
+}
+
 template <int BN, int STAGES, bool A_MN, bool B_MN, bool DUAL, class Epi>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
@@ -392,7 +407,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(GATHER ? kPairGather
       bool ok = true;
       for (int tile = pair; tile < num_tiles && ok; tile += npairs) {
         int tm, tn;
-        tile_coords(tile, m_tiles, n_tiles, tm, tn);
+        if constexpr (GATHER)
+          tile_coords_gather(tile, m_tiles, n_tiles, tm, tn);
+        else
+          tile_coords(tile, m_tiles, n_tiles, tm, tn);
         const int m0 = tm * kPairBM + static_cast<int>(rank) * kPairHalf;
         const int n0 = tn * TN + static_cast<int>(rank) * L::kBCols;
         if constexpr (GATHER) {
@@ -503,7 +521,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(GATHER ? kPairGather
     uint32_t acc_phase = 0;
     for (int tile = pair; tile < num_tiles; tile += npairs) {
       int tm, tn;
-      tile_coords(tile, m_tiles, n_tiles, tm, tn);
+      if constexpr (GATHER)
+        tile_coords_gather(tile, m_tiles, n_tiles, tm, tn);
+      else
+        tile_coords(tile, m_tiles, n_tiles, tm, tn);
       if (!mbar_wait(&tfull[acc], acc_phase, s.status, kErrTimeoutEpilogue)) break;
       tc_fence_after();
       const uint32_t taddr = tmem_base + (static_cast<uint32_t>(sub * 32) << 16) + acc * L::kAccCols;
