@@ -51,8 +51,9 @@ ttb::Operand b_operand(const Tensor& b) {
 }
 
 // Fused all-gather description from Python: None, or one tuple per staged B operand
-// (src_ptrs [world], cuts [world + 1], done int32 [rows / 64], target); the staging buffers are the
-// weights passed as the B operands, dense [rows, cols] bf16.
+// (src_ptrs [world], cuts [world + 1], done int32 [rows / 64], uses), where uses counts this gather
+// among all gathers into that done array (1 for the first); the staging buffers are the weights
+// passed as the B operands, dense [rows, cols] bf16.
 bool make_gather(const py::object& obj, const std::vector<const Tensor*>& staging, ttb::gemm::Gather& g) {
   if (obj.is_none()) return false;
   const auto ops = obj.cast<std::vector<py::tuple>>();
@@ -61,11 +62,12 @@ bool make_gather(const py::object& obj, const std::vector<const Tensor*>& stagin
   g.nops = static_cast<int>(ops.size());
   g.claim = ttb::gather_claim_counter();
   for (size_t o = 0; o < ops.size(); ++o) {
-    TORCH_CHECK(ops[o].size() == 4, "gather: (src_ptrs, cuts, done, target)");
+    TORCH_CHECK(ops[o].size() == 4, "gather: (src_ptrs, cuts, done, uses)");
     const auto src = ops[o][0].cast<std::vector<int64_t>>();
     const auto cut = ops[o][1].cast<std::vector<int64_t>>();
     const Tensor done = ops[o][2].cast<Tensor>();
-    const int64_t target = ops[o][3].cast<int64_t>();
+    const int64_t uses = ops[o][3].cast<int64_t>();
+    TORCH_CHECK(uses >= 1, "gather: uses counts from 1");
     const Tensor& w = *staging[o];
     check_bf16(w, "gather staging");
     TORCH_CHECK(w.dim() == 2 && w.is_contiguous(), "gather staging must be a dense [rows, cols] matrix");
@@ -76,7 +78,8 @@ bool make_gather(const py::object& obj, const std::vector<const Tensor*>& stagin
     TORCH_CHECK(rows % ttb::gemm::kGatherSlabRows == 0 && cols % 8 == 0, "gather: rows % 64 == 0 and cols % 8 == 0");
     TORCH_CHECK(cut[0] == 0 && cut[world] == rows, "gather: cuts must span the rows");
     for (int r = 0; r < world; ++r) {
-      TORCH_CHECK(cut[r] <= cut[r + 1] && cut[r] % ttb::gemm::kGatherChunkRows == 0, "gather: cuts ascend in 16-row steps");
+      TORCH_CHECK(cut[r] <= cut[r + 1] && cut[r] % ttb::gemm::kGatherSlabRows == 0,
+                  "gather: cuts ascend in 64-row steps");
       TORCH_CHECK(src[r] % 16 == 0, "gather: shard pointers must be 16-byte aligned");
       g.op[o].src[r] = reinterpret_cast<const __nv_bfloat16*>(src[r]);
       g.op[o].cut[r] = static_cast<int>(cut[r]);
@@ -91,9 +94,10 @@ bool make_gather(const py::object& obj, const std::vector<const Tensor*>& stagin
     g.op[o].cols = static_cast<int>(cols);
     g.op[o].dst = reinterpret_cast<__nv_bfloat16*>(w.data_ptr());
     g.op[o].done = reinterpret_cast<uint32_t*>(done.data_ptr<int>());
-    g.op[o].target = static_cast<uint32_t>(target);
+    g.op[o].target = static_cast<uint32_t>(uses * ttb::gemm::gather_chunks_per_slab(static_cast<int>(cols)));
   }
-  TORCH_CHECK(g.nops == 1 || g.op[0].rows == g.op[1].rows, "gather: two staged operands need equal rows");
+  TORCH_CHECK(g.nops == 1 || (g.op[0].rows == g.op[1].rows && g.op[0].cols == g.op[1].cols),
+              "gather: two staged operands need equal shapes");
   return true;
 }
 

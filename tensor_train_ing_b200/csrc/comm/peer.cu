@@ -95,9 +95,26 @@ __global__ void __launch_bounds__(kThreads) ag_pull_cast_kernel(const CopySeg* _
   if (j >= nseg) return;
   const CopySeg sg = segs[j];
   const long long n4 = sg.n / 4;
-  for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < n4;
-       i += static_cast<long long>(gridDim.x) * blockDim.x) {
-    const float4 v = __ldcg(reinterpret_cast<const float4*>(sg.src) + i);
+  const float4* src = reinterpret_cast<const float4*>(sg.src);
+  // four 16-byte loads in flight per thread before the stores: a peer read takes microseconds, so
+  // the link stays busy only with several MB outstanding across the grid
+  constexpr int kUnroll = 4;
+  const long long stride = static_cast<long long>(gridDim.x) * blockDim.x;
+  long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x;
+  for (; i + (kUnroll - 1) * stride < n4; i += kUnroll * stride) {
+    float4 v[kUnroll];
+#pragma unroll
+    for (int u = 0; u < kUnroll; ++u) v[u] = __ldcg(src + i + u * stride);
+#pragma unroll
+    for (int u = 0; u < kUnroll; ++u) {
+      if (sg.dst32 != nullptr) reinterpret_cast<float4*>(sg.dst32)[i + u * stride] = v[u];
+      if (sg.dst16 != nullptr)
+        reinterpret_cast<uint2*>(sg.dst16)[i + u * stride] =
+            make_uint2(pack_bf16(v[u].x, v[u].y), pack_bf16(v[u].z, v[u].w));
+    }
+  }
+  for (; i < n4; i += stride) {
+    const float4 v = __ldcg(src + i);
     if (sg.dst32 != nullptr) reinterpret_cast<float4*>(sg.dst32)[i] = v;
     if (sg.dst16 != nullptr)
       reinterpret_cast<uint2*>(sg.dst16)[i] = make_uint2(pack_bf16(v.x, v.y), pack_bf16(v.z, v.w));

@@ -4,9 +4,10 @@
 // weight matrix (rank r: rows [cut[r], cut[r+1])) in symmetric memory, mapped into every rank's
 // address space over NVLink.  A GEMM whose B operand is such a matrix takes a local staging buffer
 // [rows, cols] as B and a Gather description: besides the producer / MMA / epilogue warps, two
-// gather warps per CTA claim 16-row chunks of the matrix from a device counter (slab order, the
+// gather warps per CTA claim chunks of the matrix from a device counter (slab order, the
 // order in which the tiles consume them), copy each from the owning rank's memory into the staging
 // buffer with plain 16-byte loads and stores, and count the chunk into its 64-row slab's done word.
+// (A chunk is a 32 KB piece of a 64-row slab, so matrices of any width split into many claims.)
 // Before the TMA producer loads a B tile it waits, bounded, until the tile's slabs are complete.
 // So every weight row crosses NVLink exactly once per call, the copy of later slabs overlaps the
 // MMAs of earlier tiles, and TMA only ever reads this GPU's memory (never a peer's, never
@@ -17,8 +18,8 @@
 // reads the done word with ld.acquire.gpu and issues fence.proxy.async.global before its TMA loads,
 // so the async-proxy reads observe the generic-proxy writes.
 //
-// Done words only grow: call e of a staging buffer passes target = e * kGatherChunksPerSlab, so no
-// reset is needed between calls (zero them once when the buffer is created).  The chunk counter is
+// Done words only grow: the e-th gather into a done array passes target = e * chunks per slab, so
+// no reset is needed between calls (zero them once when the array is created).  The chunk counter is
 // a {next, finished CTAs} pair that the last CTA to finish returns to zero, so launches that share
 // one counter must be ordered on a stream.
 #pragma once
@@ -42,31 +43,38 @@ __device__ __forceinline__ uint32_t ld_acquire_gpu(const uint32_t* p) {
 }
 
 __device__ __forceinline__ uint32_t gather_chunks(const Gather& g) {
-  return static_cast<uint32_t>(g.nops) * static_cast<uint32_t>(g.op[0].rows / kGatherChunkRows);
+  return static_cast<uint32_t>(g.nops) * static_cast<uint32_t>(g.op[0].rows / kGatherSlabRows) *
+         static_cast<uint32_t>(gather_chunks_per_slab(g.op[0].cols));
 }
 
-// One warp copies chunks until every chunk of the call has been claimed.
+// One warp copies chunks until every chunk of the call has been claimed.  Chunks are claimed in slab
+// order (the two operands of a dual-B GEMM alternate slab by slab), each a 32 KB piece of a 64-row
+// slab, so a wide matrix still splits into many claims.
+template <int kUnroll>
 __device__ __forceinline__ void gather_warp(const Gather& g, int lane) {
   const uint32_t total = gather_chunks(g);
+  const uint32_t cps = static_cast<uint32_t>(gather_chunks_per_slab(g.op[0].cols));
   for (;;) {
     uint32_t c = 0;
     if (lane == 0) c = atomicAdd(g.claim, 1u);
     c = __shfl_sync(0xffffffffu, c, 0);
     if (c >= total) break;
-    const uint32_t j = c / kGatherChunksPerSlab;  // position in slab order
+    const uint32_t j = c / cps;  // position in slab order
     const int o = g.nops == 2 ? static_cast<int>(j & 1u) : 0;
     const int slab = static_cast<int>(g.nops == 2 ? (j >> 1) : j);
     const GatherOp& op = g.op[o];
-    const int row = slab * kGatherSlabRows + static_cast<int>(c % kGatherChunksPerSlab) * kGatherChunkRows;
+    const int row = slab * kGatherSlabRows;
     int r = 0;
     while (r + 1 < op.world && row >= op.cut[r + 1]) ++r;
-    const uint4* s = reinterpret_cast<const uint4*>(op.src[r] + static_cast<long long>(row - op.cut[r]) * op.cols);
-    uint4* d = reinterpret_cast<uint4*>(op.dst + static_cast<long long>(row) * op.cols);
-    const int nvec = kGatherChunkRows * op.cols / 8;
+    const long long slab_vecs = static_cast<long long>(kGatherSlabRows) * op.cols / 8;
+    const long long v0 = static_cast<long long>(c % cps) * kGatherChunkVecs;
+    const int nvec = static_cast<int>(min(static_cast<long long>(kGatherChunkVecs), slab_vecs - v0));
+    const uint4* s =
+        reinterpret_cast<const uint4*>(op.src[r] + static_cast<long long>(row - op.cut[r]) * op.cols) + v0;
+    uint4* d = reinterpret_cast<uint4*>(op.dst + static_cast<long long>(row) * op.cols) + v0;
     int i = lane;
     // peer memory through L2 only (__ldcg).  NVLink reads take microseconds, so the link is kept busy
-    // only with many bytes in flight: eight 16-byte loads per lane (4 KB per warp) before the stores.
-    constexpr int kUnroll = 8;
+    // only with many bytes in flight: kUnroll 16-byte loads per lane before the stores.
     for (; i + (kUnroll - 1) * 32 < nvec; i += kUnroll * 32) {
       uint4 v[kUnroll];
 #pragma unroll

@@ -8,13 +8,18 @@ namespace ttb {
 namespace gemm {
 
 constexpr int kGatherMaxRanks = 8;
-constexpr int kGatherSlabRows = 64;   // readiness granularity (rows of one done word)
-constexpr int kGatherChunkRows = 16;  // rows one warp copies per claim
-constexpr int kGatherChunksPerSlab = kGatherSlabRows / kGatherChunkRows;
+constexpr int kGatherSlabRows = 64;    // readiness granularity (rows of one done word)
+constexpr int kGatherChunkVecs = 2048; // 16-byte vectors one warp copies per claim (32 KB)
+
+// Chunks of one 64-row slab of a matrix with `cols` bf16 columns (a slab is 8 * cols vectors).
+__host__ __device__ constexpr int gather_chunks_per_slab(int cols) {
+  return (kGatherSlabRows * cols / 8 + kGatherChunkVecs - 1) / kGatherChunkVecs;
+}
 
 // One row-sharded operand.  dst is the local staging buffer [rows, cols] (row stride cols); rank r's
-// rows start at src[r] (row stride cols).  rows % 64 == 0, cut[r] % 16 == 0, cols % 8 == 0, every
-// pointer 16-byte aligned.
+// rows start at src[r] (row stride cols).  rows % 64 == 0, cut[r] % 64 == 0 (a slab lies in one
+// shard), cols % 8 == 0, every pointer 16-byte aligned.  A call that is the e-th gather into a done
+// array passes target = e * gather_chunks_per_slab(cols).
 struct GatherOp {
   const __nv_bfloat16* src[kGatherMaxRanks];
   int cut[kGatherMaxRanks + 1];

@@ -10,7 +10,7 @@ namespace ttb {
 namespace gemm {
 // Every warp of the launch copies gather chunks (the fused GEMM's copy without the GEMM).
 __global__ void __launch_bounds__(256) gather_rows_kernel(const __grid_constant__ Gather g) {
-  gather_warp(g, threadIdx.x % 32);
+  gather_warp<8>(g, threadIdx.x % 32);
   __syncthreads();
   if (threadIdx.x == 0) gather_finish(g);
 }
@@ -29,8 +29,9 @@ uint32_t* gather_claim_counter() {
 
 void gather_rows(const gemm::Gather& g, cudaStream_t stream) {
   TTB_CHECK(g.nops >= 1 && g.nops <= 2 && g.claim != nullptr, "gather: one or two operands and a chunk counter");
-  const int chunks = g.nops * (g.op[0].rows / gemm::kGatherChunkRows);
-  const int blocks = (chunks + 7) / 8 < num_sms() ? (chunks + 7) / 8 : num_sms();
+  const long long chunks = static_cast<long long>(g.nops) * (g.op[0].rows / gemm::kGatherSlabRows) *
+                           gemm::gather_chunks_per_slab(g.op[0].cols);
+  const int blocks = (chunks + 7) / 8 < num_sms() ? static_cast<int>((chunks + 7) / 8) : num_sms();
   gemm::gather_rows_kernel<<<blocks > 0 ? blocks : 1, 256, 0, stream>>>(g);
   TTB_CUDA_CHECK(cudaGetLastError());
 }

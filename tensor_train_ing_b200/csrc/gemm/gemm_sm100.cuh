@@ -540,7 +540,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(GATHER ? kPairGather
     }
   } else {
     // ------------------------------------------------------------------ gather warps (6, 7)
-    if constexpr (GATHER) gather_warp(g, lane);
+    if constexpr (GATHER) gather_warp<16>(g, lane);  // 8 KB in flight per warp, 296 warps per GPU
   }
 
   __syncwarp();

@@ -188,7 +188,7 @@ def build(name: str) -> _Case:
 
         def run():
             uses[0] += 1
-            C.mm(a, staging.t(), out, gather=[([t.data_ptr() for t in shards], cuts, done, 4 * uses[0])])
+            C.mm(a, staging.t(), out, gather=[([t.data_ptr() for t in shards], cuts, done, uses[0])])
         return _Case(run, 2.0 * N * D * 5 * H * DK)
     raise KeyError(name)
 
@@ -320,11 +320,11 @@ def gather_nvlink(shapes=((8192, 5 * 6144, 6144), (8192, 6144, 6144), (8192, 614
 
         def fused():
             uses[0] += 1
-            C.mm(x, staging.t(), out, gather=[(ptrs, cuts, done, 4 * uses[0])])
+            C.mm(x, staging.t(), out, gather=[(ptrs, cuts, done, uses[0])])
 
         def alone():
             uses[0] += 1
-            C.gather_rows(staging, [(ptrs, cuts, done, 4 * uses[0])])
+            C.gather_rows(staging, [(ptrs, cuts, done, uses[0])])
 
         def nccl():
             dist.all_gather_into_tensor(full, w[rank * Nw // world:(rank + 1) * Nw // world].contiguous())

@@ -16,16 +16,23 @@ Per-rank weight memory is therefore 1/N of the bf16 model plus the window (a few
 where the reference's FSDP2 all-gathers every block's fp32 parameters before each of its forward
 and backward passes (tnlm/parallel.py:23-30).
 
-Every gather of a group adds 4 to each of the group's per-slab done words (int32, zeroed once), so a
-call's target is ``4 * uses``; launches of the gather are ordered on the compute stream, which
-keeps the window slots, the done words and the kernels' chunk counter consistent.
+Every gather of a group adds its chunks per slab (one per 32 KB of a 64-row slab) to each of the
+group's per-slab done words (int32, zeroed once), so a call passes how many gathers of the group
+there have been and the kernel waits for that many times the chunk count; launches of the gather
+are ordered on the compute stream, which keeps the window slots, the done words and the kernels'
+chunk counter consistent.
 """
 from __future__ import annotations
 
 import torch
 
-SLAB = 64    # rows per done word
-CHUNK = 16   # rows one warp copies at a time; shard cuts are multiples of SLAB
+SLAB = 64        # rows per done word; shard cuts are multiples of SLAB
+CHUNK_VECS = 2048  # 16-byte vectors one warp copies per claim
+
+
+def chunks_per_slab(cols: int) -> int:
+    """Chunks of one 64-row slab of a bf16 matrix with ``cols`` columns."""
+    return -(-(SLAB * cols // 8) // CHUNK_VECS)
 
 
 def row_cuts(rows: int, world: int) -> list[int]:
@@ -49,9 +56,10 @@ class GatheredWeight:
         self.uses = 0
 
     def spec(self) -> tuple:
-        """Description for one more gather of this group (the kernels' tuple form)."""
+        """Description for one more gather of this group (the kernels' tuple form: the kernel waits for
+        done words of ``uses`` times the chunks of a slab)."""
         self.uses += 1
-        return (self.src_ptrs, self.cuts, self.done, 4 * self.uses)
+        return (self.src_ptrs, self.cuts, self.done, self.uses)
 
     def operand(self):
         """(staging [rows, cols] bf16, gather description or None when the rows are already there)."""

@@ -59,12 +59,12 @@ def test_row_cuts_and_gather_window_residency():
     win = GatherWindow("cpu", 2, 64 * 8)
     a, b, c = (GatheredWeight(win, 64, 8, [0, 64], [0]) for _ in range(3))
     _, spec = a.operand()
-    assert spec[3] == 4  # first gather of a: done target 4
+    assert spec[3] == 1  # first gather of a
     assert a.operand()[1] is None  # resident
     b.operand()
     c.operand()  # evicts a (least recently used)
     view, spec = a.operand()
-    assert spec is not None and spec[3] == 8 and view.shape == (64, 8)
+    assert spec is not None and spec[3] == 2 and view.shape == (64, 8)
     assert b.operand()[1] is not None  # b was evicted by a
     win.invalidate()
     assert a.operand()[1] is not None  # the shards changed: gather again
