@@ -117,3 +117,68 @@ def test_unfinished_stat_collection_rejected(tmp_path):
     m(torch.randint(0, 97, (1, 4)))
     with pytest.raises(ValueError):
         _save(tmp_path / "c", m)
+
+
+def test_identity_checks_refuse_another_dataset_or_config(tmp_path):
+    """A checkpoint names the dataset (manifest hash) and the config it was trained with; loading it
+    for another dataset or config is refused before any tensor is touched, and a validator may record
+    a compatibility note instead."""
+    m = _model(1)
+    save_checkpoint(tmp_path / "c", m, None, None, config={"model": {"d_model": 32}, "train": {"lr": 0.1}},
+                    progress={"steps": 3}, manifest_hash="a" * 64)
+    target = _model(2)
+    before = _clone_state(target)
+    with pytest.raises(ValueError, match="Data manifest hash mismatch"):
+        load_checkpoint(tmp_path / "c", target, expected_manifest_hash="b" * 64, restore_rng=False)
+    with pytest.raises(ValueError, match="config mismatch"):
+        load_checkpoint(tmp_path / "c", target, expected_config={"model": {"d_model": 64}, "train": {"lr": 0.1}},
+                        restore_rng=False)
+    for k, v in before.items():
+        assert torch.equal(v, target.state_dict()[k])
+    payload = load_checkpoint(tmp_path / "c", target, expected_manifest_hash="a" * 64,
+                              config_validator=lambda saved: {"accepted_lr": saved["train"]["lr"]},
+                              restore_rng=False)
+    assert payload["config_compatibility"] == {"accepted_lr": 0.1} and payload["progress"]["steps"] == 3
+
+
+def test_rng_streams_continue_after_a_restore(tmp_path):
+    """The saved python / numpy / torch generator states are restored, so random draws after a
+    resume are the draws an uninterrupted run makes."""
+    import random
+
+    import numpy as np
+    m = _model(3)
+    torch.manual_seed(123)
+    random.seed(5)
+    np.random.seed(7)
+    _save(tmp_path / "c", m)
+    want = (torch.rand(4), random.random(), np.random.rand(2))
+    torch.manual_seed(0)
+    random.seed(0)
+    np.random.seed(0)
+    load_checkpoint(tmp_path / "c", _model(4))
+    got = (torch.rand(4), random.random(), np.random.rand(2))
+    assert torch.equal(got[0], want[0]) and got[1] == want[1] and (got[2] == want[2]).all()
+
+
+def test_sampler_cursor_resumes_the_batch_stream(tmp_path, config):
+    """The data cursor travels with the checkpoint: a sampler restored from it yields the batches the
+    original would have yielded next."""
+    from tensor_train_ing_b200.data import PackedSampler
+    manifest = config.raw["data"]["manifest"]
+    s = PackedSampler(manifest, batch_size=2, context=4, seed=1)
+    for _ in range(3):
+        s.next_batch()
+    m = _model(0)
+    save_checkpoint(tmp_path / "c", m, None, s, config={"model": {}}, progress={"steps": 3},
+                    manifest_hash=s.manifest_hash)
+    expected = [s.next_batch() for _ in range(4)]
+    fresh = PackedSampler(manifest, batch_size=2, context=4, seed=1)
+    load_checkpoint(tmp_path / "c", _model(0), None, fresh, expected_manifest_hash=s.manifest_hash,
+                    restore_rng=False)
+    for want in expected:
+        got = fresh.next_batch()
+        assert all(torch.equal(a, b) for a, b in zip(got, want))
+    other_seed = PackedSampler(manifest, batch_size=2, context=4, seed=2)
+    with pytest.raises(ValueError):
+        load_checkpoint(tmp_path / "c", _model(0), None, other_seed, restore_rng=False)
