@@ -92,3 +92,58 @@ def test_training_descriptor_never_infers_missing_evidence():
     assert d["cooldown_status"] == "unknown" and d["completion_status"] == "unknown"
     cmp = _training_comparison({"training_descriptor": d}, {"training_descriptor": d})
     assert "optimizer" in cmp["unknown_dimensions"] and not cmp["matched_dimensions"]
+
+
+def test_ratio_bootstrap_interval_properties():
+    """The percentile interval is reproducible for a seed, contains the pooled ratio, is a point when
+    every unit has the same ratio, and needs at least two units and one resample."""
+    import numpy as np
+
+    from tensor_train_ing_b200.evaluate import ratio_bootstrap
+    rng = np.random.default_rng(0)
+    den = rng.integers(5, 50, size=30)
+    num = den * rng.uniform(2.0, 4.0, size=30)
+    lo, hi = ratio_bootstrap(num, den, samples=400, seed=3)
+    assert [lo, hi] == ratio_bootstrap(num, den, samples=400, seed=3)
+    assert lo < num.sum() / den.sum() < hi
+    assert ratio_bootstrap(num, den, samples=400, seed=4) != [lo, hi]
+    flat = ratio_bootstrap(3.0 * den, den, samples=50, seed=0)
+    assert flat == pytest.approx([3.0, 3.0])
+    assert ratio_bootstrap(num[:1], den[:1], samples=50, seed=0) is None
+    assert ratio_bootstrap(num, den, samples=0, seed=0) is None
+
+
+def test_target_plan_is_a_context_free_identity(setup):
+    """The plan lists, per validation document in manifest order, target offsets 1 .. length-1 up to
+    the cap; its digest does not depend on the sampler's context, and a smaller cap truncates the
+    last planned document."""
+    from tensor_train_ing_b200.data import PackedSampler
+    from tensor_train_ing_b200.evaluate import TargetPlan
+    cfg, _, _ = setup
+    manifest = cfg.raw["data"]["manifest"]
+    short = PackedSampler(manifest, split="val", context=8)
+    long_ = PackedSampler(manifest, split="val", context=64)
+    full = TargetPlan(short, cap=10 ** 9)
+    assert full.sha256 == TargetPlan(long_, cap=10 ** 9).sha256
+    total = sum(max(0, short.docs.length(i) - 1) for i in range(len(short.docs)))
+    assert sum(r["count"] for r in full.ranges) == total
+    assert [r["document_id"] for r in full.ranges] == [short.docs[i]["id"] for i in range(len(short.docs))
+                                                        if short.docs.length(i) > 1]
+    first = full.ranges[0]["count"]
+    capped = TargetPlan(short, cap=first + 3)
+    assert [r["count"] for r in capped.ranges] == [first, 3] and capped.sha256 != full.sha256
+
+
+def test_evaluation_is_reproducible_and_depends_on_the_weights(setup):
+    """Two evaluations of one checkpoint agree exactly (same plan, same per-document sums, same
+    interval for the same bootstrap seed); another checkpoint scores the same plan differently."""
+    cfg, ckpt, tmp = setup
+    a, _ = ckpt("a", 1)
+    b, _ = ckpt("b", 2)
+    r1 = evaluate_checkpoint(cfg, a, tmp / "e1", max_seconds=120, device="cpu", bootstrap_samples=30)
+    r2 = evaluate_checkpoint(cfg, a, tmp / "e2", max_seconds=120, device="cpu", bootstrap_samples=30)
+    r3 = evaluate_checkpoint(cfg, b, tmp / "e3", max_seconds=120, device="cpu", bootstrap_samples=30)
+    assert r1["per_document"] == r2["per_document"] and r1["ce"] == r2["ce"]
+    assert r1["target_plan_sha256"] == r3["target_plan_sha256"]
+    assert r1["ce"] != r3["ce"]
+    assert json.loads((tmp / "e1" / "evaluation.json").read_text())["ce"] == r1["ce"]
