@@ -378,8 +378,10 @@ def peer_nvlink(numel: int = 256 << 20, reps: int = 10):
     ptrs = [int(p) for p in handle.buffer_ptrs]
     mine = torch.empty(region, device="cuda")
     cache = torch.empty(n, device="cuda", dtype=torch.bfloat16)
+    # each rank starts at the next rank's region, as the training all-gather orders its segments
+    order = [(rank + 1 + k) % world for k in range(world)]
     segs = torch.tensor([(ptrs[q] + 4 * q * region, 0 if q == rank else buf.data_ptr() + 4 * q * region,
-                          cache.data_ptr() + 2 * q * region, region) for q in range(world)],
+                          cache.data_ptr() + 2 * q * region, region) for q in order],
                         dtype=torch.int64, device="cuda")
     dist.barrier()
     torch.cuda.synchronize()

@@ -418,7 +418,7 @@ class ShardedDataParallel:
         the local one (own units are not copied), plus the bf16 cache of every weight group
         (sharded groups: straight from the owner's master)."""
         from ..ops._ext import lib
-        rows, max_n = [], 0
+        rows, owners, max_n = [], [], 0
         local = self.param_flat.data_ptr()
         for kind, obj, params, off, n, r in self.units:
             n4 = (n + 3) // 4 * 4  # units are 64-element aligned, so the rounded tail stays in padding
@@ -432,6 +432,7 @@ class ShardedDataParallel:
             if dst32 == 0 and dst16 == 0:
                 continue
             rows.append((src, dst32, dst16, n4 if dst16 == 0 else n))
+            owners.append(r)
             max_n = max(max_n, n4)
         for su in self.sunits:
             if self.fused_gather:  # this rank's rows of the group, from the owner's master
@@ -439,12 +440,19 @@ class ShardedDataParallel:
                 if hi > lo:
                     rows.append((self._spptrs[su.owner] + 4 * (su.goff + lo * su.cols), 0,
                                  self.wshard.data_ptr() + 2 * su.woff, (hi - lo) * su.cols))
+                    owners.append(su.owner)
                     max_n = max(max_n, (hi - lo) * su.cols)
                 continue
             cache = su.group.bf16()
             assert cache.numel() == su.n and su.n % 4 == 0
             rows.append((self._spptrs[su.owner] + 4 * su.goff, 0, cache.data_ptr(), su.n))
+            owners.append(su.owner)
             max_n = max(max_n, su.n)
+        # the kernel takes segments roughly in list order; starting each rank at the next rank's units
+        # (and ending at its own) spreads the pulls over every owner at once instead of every rank
+        # reading owner 0 first
+        order = sorted(range(len(rows)), key=lambda i: ((owners[i] - self.rank - 1) % self.world, i))
+        rows = [rows[i] for i in order]
         self._segs = torch.tensor(rows, dtype=torch.int64).to(self.param_flat.device) if rows else None
         self._seg_max = max_n
         self._lib = lib
