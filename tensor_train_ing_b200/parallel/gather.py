@@ -3,8 +3,9 @@
 Under parameter sharding the fp32 master of every block matrix lives on one owner rank.  The GEMMs
 read bf16 operands; instead of a full bf16 copy of the model on every rank, each rank keeps a
 *row shard* of every sharded weight group (rank r: rows ``cut[r]:cut[r+1]``, 64-row aligned) in one
-symmetric buffer that every rank can read over NVLink.  The owner writes those shards once per
-optimizer step (the step's pull all-gather, as fp32 master -> bf16 rows).  When a forward GEMM needs
+symmetric buffer that every rank can read over NVLink.  Once per optimizer step each rank pulls its
+rows of every group from the owners' updated fp32 masters into that buffer, as bf16 (the step's pull
+all-gather), and a barrier follows before any GEMM reads a peer's rows.  When a forward GEMM needs
 a group it takes a slot of a small local staging window and passes the GEMM a gather description:
 the CTA-pair GEMM copies the rows from the ranks' shards into the slot while it computes
 (csrc/gemm/gather.cuh), so the transfer overlaps the MMAs tile by tile and every row crosses
