@@ -57,6 +57,9 @@ def parse():
     p.add_argument("--micro-batch", type=int, default=None)
     p.add_argument("--optimizer", default="muon", choices=["muon", "adamw"])
     p.add_argument("--no-e2e", action="store_true")
+    p.add_argument("--recompute-blocks", default=None,
+                   help="activation-checkpointed configs: recompute only the first N blocks, or 'auto' "
+                        "(from the capacity plan and the GPU's memory; default: all)")
     p.add_argument("--global-batch", type=int, default=None,
                    help="override the preset's global batch (functional runs; the JSON line reports it)")
     p.add_argument("--shard-params", default="auto", choices=["auto", "on", "off"],
@@ -200,7 +203,9 @@ def build_ours(args, device, world):
         shard = needs_parameter_sharding(cfg.model, world, device)
     # a sharded model is drawn on the device (the serial CPU initialisation of 33B weights takes minutes)
     eng = TrainEngine(cfg, device=device, micro_batch=args.micro_batch or mb, shard_params=shard,
-                      init="device" if shard else "serial")
+                      init="device" if shard else "serial",
+                      recompute_blocks=(args.recompute_blocks if args.recompute_blocks in (None, "auto")
+                                        else int(args.recompute_blocks)))
     if not eng.fused:
         raise SystemExit("the fused sm_100a path does not cover this configuration")
     n_params = sum(p.numel() for p in eng.model.parameters())
@@ -425,13 +430,16 @@ def main():
                                                        else ""), "tokens_per_step": tokens_per_step,
                        "optimizer": f"{args.optimizer} (hidden) + adamw", "micro_batch": args.micro_batch
                        or PRESETS[args.config][7], "params": n_params,
-                       "l2": "per-step working set >> 126 MB L2; no flush needed"},
+                       "l2": "per-step working set >> 126 MB L2; no flush needed",
+                       "recompute_blocks": (getattr(eng.model, "recompute_blocks", None) if eng is not None
+                                            else None)},
             "mfu": round(6 * n_params * value / (world * peak_tflops * 1e12), 4),
             "mfu_peak_tflops": peak_tflops,
             "mfu_of_sustained": round(6 * n_params * value / (world * sustained_tflops * 1e12), 4),
             "mfu_sustained_tflops": sustained_tflops,
             "loss_first_last": [round(loss_vals[0], 4), round(loss_vals[-1], 4)],
             "clocks": clocks, "e2e": e2e,
+            "peak_mem_gb": round(torch.cuda.max_memory_allocated(device) / 1e9, 1),
         }
         if args.impl == "reference":
             out["impl"] = "reference"

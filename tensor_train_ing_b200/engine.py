@@ -16,6 +16,8 @@ scaling each micro-batch's loss beforehand.
 """
 from __future__ import annotations
 
+import os
+
 import torch
 import torch.distributed as dist
 
@@ -28,12 +30,15 @@ from .parallel.sharded import ShardedDataParallel
 class TrainEngine:
     def __init__(self, cfg: Config, device="cuda", micro_batch: int = 8, model: TensorLM | None = None,
                  optimizer=None, group=None, grad_clip: float | None = None, shard_params: bool | None = None,
-                 init: str = "serial"):
+                 init: str = "serial", recompute_blocks: int | None = None):
         """``shard_params``: keep fp32 weights, gradients and optimizer state only on their owner
         rank (None: when ``TTB_SHARD_PARAMS=1`` or when the replicated layout would not fit the
         device; see models.shapes.needs_parameter_sharding).  A sharded engine builds its model
         itself from the streamed serial initialisation unless ``model`` is given (``init="device"``:
-        the same distributions drawn on the device, for throughput runs)."""
+        the same distributions drawn on the device, for throughput runs).  ``recompute_blocks``
+        (or ``TTB_RECOMPUTE_BLOCKS``): under activation checkpointing, recompute only the first this
+        many blocks and keep the others' activations (selective recompute where memory allows);
+        ``"auto"`` picks the count from the capacity plan and this GPU's memory."""
         self.cfg = cfg
         self.device = torch.device(device)
         self.micro_batch = int(micro_batch)
@@ -51,6 +56,12 @@ class TrainEngine:
                 model = TensorLM(cfg.model).to(self.device)
         self.model = model
         self.model.train()
+        if recompute_blocks is None and os.environ.get("TTB_RECOMPUTE_BLOCKS"):
+            recompute_blocks = os.environ["TTB_RECOMPUTE_BLOCKS"]
+        # "auto" is resolved at the first micro-batch, when the tokens per micro-batch are known
+        self._recompute_auto = recompute_blocks == "auto"
+        if recompute_blocks is not None and not self._recompute_auto:
+            self.model.recompute_blocks = int(recompute_blocks)
         self.grad_clip = cfg.train.grad_clip if grad_clip is None else grad_clip
         self.fused = self.device.type == "cuda" and self.model.fused_path_supported()[0]
         # flat gradient/parameter buffers: needed by the fused path and by every multi-rank run
@@ -67,6 +78,18 @@ class TrainEngine:
         # optional per-phase device timing: a list that receives, per step, the (phase, CUDA event) pairs
         # recorded at the end of each phase
         self.phase_events: list | None = None
+
+    def _resolve_auto_recompute(self, tokens: int):
+        """Blocks to recompute so that the capacity plan with the rest kept fits 92 % of this GPU
+        (``recompute_blocks="auto"``; resolved once, at the first micro-batch of ``tokens`` tokens)."""
+        self._recompute_auto = False
+        if self.device.type != "cuda" or not self.cfg.model.activation_checkpointing:
+            return
+        from .models.shapes import blocks_to_recompute
+        total = torch.cuda.get_device_properties(self.device).total_memory
+        self.model.recompute_blocks = blocks_to_recompute(
+            self.cfg.model, gpus=self.world, micro_tokens_per_gpu=tokens, device_bytes=total,
+            shard_params=self.shard_params, optimizer=self.cfg.train.optimizer)
 
     def _mark(self, marks, name):
         if marks is not None:
@@ -91,6 +114,8 @@ class TrainEngine:
 
     def forward_loss(self, idx, doc_ids, targets):
         """One micro-batch's forward: (summed loss, valid-target count) on the device."""
+        if self._recompute_auto:
+            self._resolve_auto_recompute(idx.numel())
         i, d, t = (self._to_device(x) for x in (idx, doc_ids, targets))
         _, loss, n = self.model(i, d, t, reduction="sum")
         return loss, n

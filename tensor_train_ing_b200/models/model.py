@@ -336,11 +336,22 @@ class TensorLM(nn.Module):
         return ctx
 
     # ---------------------------------------------------------------- forward (module path)
+    def recomputed_blocks(self) -> int:
+        """How many blocks (the first ones) a training forward recomputes in backward under
+        activation checkpointing: all of them, unless ``recompute_blocks`` (set by the training engine
+        when the device has room to keep some blocks' activations) says fewer.  Keeping the last
+        blocks' activations changes no value, only memory and time."""
+        if not (self.cfg.activation_checkpointing and self.training and torch.is_grad_enabled()):
+            return 0
+        limit = getattr(self, "recompute_blocks", None)
+        n = len(self.blocks)
+        return n if limit is None else max(0, min(n, int(limit)))
+
     def _trunk(self, idx, ctx):
         x = self.embed(idx)
-        recompute = self.cfg.activation_checkpointing and self.training and torch.is_grad_enabled()
-        for blk in self.blocks:
-            x = torch.utils.checkpoint.checkpoint(blk, x, ctx, use_reentrant=False) if recompute else blk(x, ctx)
+        recompute = self.recomputed_blocks()
+        for i, blk in enumerate(self.blocks):
+            x = torch.utils.checkpoint.checkpoint(blk, x, ctx, use_reentrant=False) if i < recompute else blk(x, ctx)
         return self.final_norm(x)
 
     def _loss(self, x, targets):

@@ -100,7 +100,8 @@ def largest_weight_group(cfg: ModelConfig) -> int:
 
 def memory_plan(cfg: ModelConfig, *, gpus: int, micro_tokens_per_gpu: int, gpu_gb: float = 180.0,
                 checkpointing: bool | None = None, workspace_gb: float = 4.0, optimizer: str = "muon",
-                shard_params: bool = False, fused_gather: bool = True, gather_slots: int = 8) -> dict:
+                shard_params: bool = False, fused_gather: bool = True, gather_slots: int = 8,
+                kept_blocks: int = 0) -> dict:
     """Per-GPU bytes of the owner-computes layout plus one micro-batch of activations.
 
     Replicated layout: fp32 parameters and gradients and the bf16 GEMM caches on every rank, the
@@ -108,7 +109,9 @@ def memory_plan(cfg: ModelConfig, *, gpus: int, micro_tokens_per_gpu: int, gpu_g
     master, gradient accumulator and optimizer state only on their owner (1/gpus each) and two
     per-block fp32 staging slots; their bf16 rows are split across the ranks (1/gpus each) and
     gathered by the consuming GEMMs into ``gather_slots`` staging slots (``fused_gather``), or held
-    in full on every rank; embedding and vectors replicated."""
+    in full on every rank; embedding and vectors replicated.  ``kept_blocks``: under checkpointing,
+    blocks whose activations are kept rather than recomputed (the engine's ``recompute_blocks`` is
+    the layer count minus this)."""
     ckpt = cfg.activation_checkpointing if checkpointing is None else checkpointing
     c = count_params(cfg)
     n = c["total"]
@@ -127,7 +130,7 @@ def memory_plan(cfg: ModelConfig, *, gpus: int, micro_tokens_per_gpu: int, gpu_g
         weights = (4 + 4 + 2) * n
     per_layer = activation_bytes_per_token_layer(cfg)
     if ckpt:
-        act = (4 * cfg.d_model * cfg.layers + per_layer) * micro_tokens_per_gpu
+        act = (4 * cfg.d_model * cfg.layers + per_layer * (1 + min(kept_blocks, cfg.layers))) * micro_tokens_per_gpu
     else:
         act = per_layer * cfg.layers * micro_tokens_per_gpu
     chunk = min(micro_tokens_per_gpu, cfg.loss_chunk_tokens or micro_tokens_per_gpu)
@@ -142,6 +145,19 @@ def memory_plan(cfg: ModelConfig, *, gpus: int, micro_tokens_per_gpu: int, gpu_g
             "optimizer_state_GB": round(opt / 1e9, 1), "activations_GB": round(act / 1e9, 1),
             "loss_GB": round(loss / 1e9, 2), "total_GB": round(total / 1e9, 1), "fits": total < 0.92 * gpu_gb * 1e9,
             "layout": layout}
+
+
+def blocks_to_recompute(cfg: ModelConfig, *, gpus: int, micro_tokens_per_gpu: int, device_bytes: float,
+                        shard_params: bool = False, fill: float = 0.92, optimizer: str = "muon") -> int:
+    """Selective recompute: how many of the first blocks to recompute under activation checkpointing so
+    that the plan with the other blocks' activations kept stays within ``fill`` of the device (all
+    of them when nothing more fits; never fewer than zero)."""
+    plan = memory_plan(cfg, gpus=gpus, micro_tokens_per_gpu=micro_tokens_per_gpu, gpu_gb=device_bytes / 1e9,
+                       checkpointing=True, shard_params=shard_params, optimizer=optimizer)
+    room = fill * device_bytes - plan["total_GB"] * 1e9
+    per_block = activation_bytes_per_token_layer(cfg) * micro_tokens_per_gpu
+    kept = max(0, min(cfg.layers, int(room // per_block)))
+    return cfg.layers - kept
 
 
 def needs_parameter_sharding(cfg: ModelConfig, world: int, device=None) -> bool:

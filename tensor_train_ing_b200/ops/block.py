@@ -176,9 +176,9 @@ def model_forward(model, idx, ctx, targets, reduction):
     for blk in model.blocks:
         object.__setattr__(blk, "_ttb_up_alpha", up)
         up = _output_alpha(blk, up)
-    ckpt = cfg.activation_checkpointing and model.training and torch.is_grad_enabled()
-    for blk in model.blocks:
-        if ckpt:
+    recompute = model.recomputed_blocks()
+    for i, blk in enumerate(model.blocks):
+        if i < recompute:
             x = torch.utils.checkpoint.checkpoint(block_forward, blk, x, ctx, use_reentrant=False)
         else:
             x = blk(x, ctx)

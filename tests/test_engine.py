@@ -79,3 +79,37 @@ def test_clipping_bounds_the_global_norm_and_lr_multiplier_scales_from_base():
     base = [g.get("base_lr", g["lr"]) for g in eng.optimizer.param_groups]
     eng.step(*_batch(seed=1), lr_multiplier=0.25)
     assert [g["lr"] for g in eng.optimizer.param_groups] == pytest.approx([0.25 * b for b in base])
+
+
+@pytest.mark.parametrize("recompute", [None, 0, 1, 2])
+def test_selective_recompute_keeps_every_gradient(recompute, monkeypatch):
+    """Under activation checkpointing, recomputing only the first ``recompute`` blocks (keeping the
+    other blocks' activations) gives bit-identical gradients to recomputing all of them; the model
+    reports how many it recomputes."""
+    cfg = _cfg()
+    cfg.model.activation_checkpointing = True
+    monkeypatch.delenv("TTB_RECOMPUTE_BLOCKS", raising=False)
+    torch.manual_seed(0)
+    ref = TrainEngine(cfg, device="cpu", micro_batch=2, model=TensorLM(cfg.model))
+    torch.manual_seed(0)
+    eng = TrainEngine(cfg, device="cpu", micro_batch=2, model=TensorLM(cfg.model), recompute_blocks=recompute)
+    assert eng.model.recomputed_blocks() == (2 if recompute is None else recompute)
+    idx, docs, tgt = _batch()
+    for e in (ref, eng):
+        e.begin_update()
+        inv = torch.tensor(1.0 / float((tgt != -100).sum()))
+        e.forward_backward(idx, docs, tgt, inv)
+    for (name, a), b in zip(ref.model.named_parameters(), eng.model.parameters()):
+        assert (a.grad is None) == (b.grad is None), name
+        if a.grad is not None:
+            assert torch.equal(a.grad, b.grad), name
+    eng.model.eval()
+    assert eng.model.recomputed_blocks() == 0  # evaluation keeps nothing to recompute
+
+
+def test_recompute_blocks_from_the_environment(monkeypatch):
+    cfg = _cfg()
+    cfg.model.activation_checkpointing = True
+    monkeypatch.setenv("TTB_RECOMPUTE_BLOCKS", "1")
+    eng = _engine(cfg, 2)
+    assert eng.model.recomputed_blocks() == 1

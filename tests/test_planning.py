@@ -254,3 +254,18 @@ def test_parameter_sharding_is_chosen_by_size_or_forced(monkeypatch):
     assert needs_parameter_sharding(preset("bench_1b"), 2)
     monkeypatch.setenv("TTB_SHARD_PARAMS", "0")
     assert not needs_parameter_sharding(preset("bench_32b"), 8)
+
+
+def test_selective_recompute_choice_fits_the_plan():
+    """The automatic choice keeps as many blocks' activations as fit 92 % of the device after the
+    checkpointed plan; a device with no room recomputes every block."""
+    from tensor_train_ing_b200.models.shapes import blocks_to_recompute, memory_plan, preset
+    cfg = preset("bench_7b", loss_chunk_tokens=8192, activation_checkpointing=True)
+    total = 191.5e9  # a B200 as torch reports it
+    n = blocks_to_recompute(cfg, gpus=1, micro_tokens_per_gpu=16384, device_bytes=total)
+    kept = cfg.layers - n
+    assert 0 < kept < cfg.layers
+    assert memory_plan(cfg, gpus=1, micro_tokens_per_gpu=16384, kept_blocks=kept)["total_GB"] * 1e9 <= 0.92 * total
+    assert memory_plan(cfg, gpus=1, micro_tokens_per_gpu=16384, kept_blocks=kept + 1)["total_GB"] * 1e9 > 0.92 * total
+    assert blocks_to_recompute(cfg, gpus=8, micro_tokens_per_gpu=16384, device_bytes=total) < n  # sharded state frees room
+    assert blocks_to_recompute(cfg, gpus=1, micro_tokens_per_gpu=16384, device_bytes=100e9) == cfg.layers
