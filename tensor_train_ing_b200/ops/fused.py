@@ -7,6 +7,8 @@ accumulated through ``WeightGroup.sink_grad`` (fp32, in the GEMM epilogue).
 """
 from __future__ import annotations
 
+import contextlib
+
 import torch
 
 from ._ext import lib
@@ -29,6 +31,21 @@ def _gathers(*specs):
     """Gather descriptions of a GEMM's staged operands, as the kernels take them (None: nothing to
     gather)."""
     return [s for s in specs] if all(s is not None for s in specs) else None
+
+
+@contextlib.contextmanager
+def _launching(*pairs):
+    """Around a launch that gathers its weights: when the launch is refused on the host, the groups'
+    window slots and done words are put back so the next request gathers from scratch."""
+    try:
+        yield
+    except Exception:
+        for group, spec in pairs:
+            gw = getattr(group, "_gather", None)
+            if spec is not None and gw is not None:
+                gw.window.release(gw)
+                gw.reset()
+        raise
 
 
 # ============================================================================ RMSNorm
@@ -111,12 +128,13 @@ class LinearFn(torch.autograd.Function):
     def forward(ctx, x, residual, bias, group, alpha, *weights):
         w16, spec = group.operand()
         N = x.shape[0]
-        if residual is not None:
-            out = torch.empty(N, w16.shape[0], device=x.device, dtype=torch.float32)
-            _mm(x, w16.t(), out, c=residual, alpha=alpha, beta=1.0, bias=bias, gather=_gathers(spec))
-        else:
-            out = torch.empty(N, w16.shape[0], device=x.device, dtype=torch.bfloat16)
-            _mm(x, w16.t(), out, alpha=alpha, bias=bias, gather=_gathers(spec))
+        with _launching((group, spec)):
+            if residual is not None:
+                out = torch.empty(N, w16.shape[0], device=x.device, dtype=torch.float32)
+                _mm(x, w16.t(), out, c=residual, alpha=alpha, beta=1.0, bias=bias, gather=_gathers(spec))
+            else:
+                out = torch.empty(N, w16.shape[0], device=x.device, dtype=torch.bfloat16)
+                _mm(x, w16.t(), out, alpha=alpha, bias=bias, gather=_gathers(spec))
         ctx.save_for_backward(x)
         ctx.group, ctx.alpha, ctx.has_res, ctx.has_bias = group, alpha, residual is not None, bias is not None
         return out
@@ -149,8 +167,9 @@ class QKVRopeFn(torch.autograd.Function):
     @staticmethod
     def forward(ctx, x, group, rope_cols, dk, rope, norm_max, *weights):
         w16, spec = group.operand()
-        qkv = lib().qkv_rope(x, w16, int(rope_cols), int(dk), rope["pos32"], rope["cos"], rope["sin"], norm_max,
-                             _gathers(spec))
+        with _launching((group, spec)):
+            qkv = lib().qkv_rope(x, w16, int(rope_cols), int(dk), rope["pos32"], rope["cos"], rope["sin"], norm_max,
+                                 _gathers(spec))
         ctx.save_for_backward(x)
         ctx.group = group
         return qkv
@@ -239,21 +258,23 @@ class BilinearMLPFn(torch.autograd.Function):
     @staticmethod
     def forward(ctx, x, residual, bl, br, bd, g_l, g_r, g_d, alpha, mode, *weights):
         (wl, sl), (wr, sr) = g_l.operand(), g_r.operand()
-        if (sl is None) != (sr is None):  # one factor still resident: copy the other one alone
-            lib().gather_rows(wl if sl is not None else wr, [sl if sl is not None else sr])
-            sl = sr = None
         N, F_ = x.shape[0], wl.shape[0]
         h = torch.empty(N, F_, device=x.device, dtype=torch.bfloat16)
         l = torch.empty_like(h)
         r = torch.empty_like(h)
-        lib().bilinear(x, wl, wr, bl, br, int(mode), h, l, r, _gathers(sl, sr) if sl is not None else None)
+        with _launching((g_l, sl), (g_r, sr)):
+            if (sl is None) != (sr is None):  # one factor still resident: copy the other one alone
+                lib().gather_rows(wl if sl is not None else wr, [sl if sl is not None else sr])
+                sl = sr = None
+            lib().bilinear(x, wl, wr, bl, br, int(mode), h, l, r, _gathers(sl, sr) if sl is not None else None)
         wd, sd = g_d.operand()
-        if residual is not None:
-            out = torch.empty(N, wd.shape[0], device=x.device, dtype=torch.float32)
-            _mm(h, wd.t(), out, c=residual, alpha=alpha, beta=1.0, bias=bd, gather=_gathers(sd))
-        else:
-            out = torch.empty(N, wd.shape[0], device=x.device, dtype=torch.bfloat16)
-            _mm(h, wd.t(), out, alpha=alpha, bias=bd, gather=_gathers(sd))
+        with _launching((g_d, sd)):
+            if residual is not None:
+                out = torch.empty(N, wd.shape[0], device=x.device, dtype=torch.float32)
+                _mm(h, wd.t(), out, c=residual, alpha=alpha, beta=1.0, bias=bd, gather=_gathers(sd))
+            else:
+                out = torch.empty(N, wd.shape[0], device=x.device, dtype=torch.bfloat16)
+                _mm(h, wd.t(), out, alpha=alpha, bias=bd, gather=_gathers(sd))
         ctx.save_for_backward(x, h, l, r)
         ctx.groups = (g_l, g_r, g_d)
         ctx.alpha, ctx.mode, ctx.has_res = alpha, mode, residual is not None

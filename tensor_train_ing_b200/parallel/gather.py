@@ -58,9 +58,16 @@ class GatheredWeight:
 
     def spec(self) -> tuple:
         """Description for one more gather of this group (the kernels' tuple form: the kernel waits for
-        done words of ``uses`` times the chunks of a slab)."""
+        done words of ``uses`` times the chunks of a slab).  The count advances here, so a description
+        must be launched; one that is dropped (a launch refused on the host) leaves the done words a
+        gather behind, and ``reset`` puts both back to zero."""
         self.uses += 1
         return (self.src_ptrs, self.cuts, self.done, self.uses)
+
+    def reset(self):
+        """Zero the done words and the use count (stream-ordered after earlier gathers)."""
+        self.done.zero_()
+        self.uses = 0
 
     def operand(self):
         """(staging [rows, cols] bf16, gather description or None when the rows are already there)."""
@@ -71,7 +78,12 @@ class GatheredWeight:
         view, spec = self.window.acquire(self)
         if spec is not None:
             from ..ops._ext import lib
-            lib().gather_rows(view, [spec])
+            try:
+                lib().gather_rows(view, [spec])
+            except Exception:
+                self.window.release(self)
+                self.reset()
+                raise
         return view
 
 
@@ -97,6 +109,13 @@ class GatherWindow:
     def invalidate(self):
         """The shards changed (an optimizer step): no slot's contents are current any more."""
         self.version += 1
+
+    def release(self, gw: GatheredWeight):
+        """Forget a slot holding ``gw`` (its gather was not launched): the next request gathers again."""
+        for s, h in enumerate(self.holder):
+            if h is not None and h[0] == id(gw):
+                self.holder[s] = None
+                self.last_use[s] = 0
 
     def acquire(self, gw: GatheredWeight):
         self.clock += 1

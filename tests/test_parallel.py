@@ -69,3 +69,17 @@ def test_row_cuts_and_gather_window_residency():
     win.invalidate()
     assert a.operand()[1] is not None  # the shards changed: gather again
     assert win.gathers == 6
+
+
+def test_a_refused_gather_launch_is_forgotten():
+    """A gather description that was never launched leaves no trace: the slot is released and the
+    done words and use count start over, so the next request gathers and waits for its own copy."""
+    from tensor_train_ing_b200.parallel.gather import GatheredWeight, GatherWindow
+    win = GatherWindow("cpu", 2, 64 * 8)
+    gw = GatheredWeight(win, 64, 8, [0, 64], [0])
+    _, spec = gw.operand()
+    assert spec[3] == 1
+    win.release(gw)
+    gw.reset()
+    view, spec = gw.operand()
+    assert spec is not None and spec[3] == 1 and gw.uses == 1 and not gw.done.any()
