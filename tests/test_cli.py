@@ -119,3 +119,25 @@ def test_compare_seed_pairs_command_validates_before_writing(setup, capsys):
     with pytest.raises(ValueError, match="two"):
         main(["compare_seed_pairs", "--pairs", str(pairs), "--out", str(tmp / "rep")])
     assert not (tmp / "rep").exists()
+
+
+def test_every_subcommand_documents_its_flags():
+    """The reference's command surface: the parser has exactly the reference's nineteen subcommands,
+    and each parses --help (exit 0)."""
+    import argparse
+    import contextlib
+    import io
+
+    from tensor_train_ing_b200.cli import _parser
+    parser = _parser()
+    actions = [a for a in parser._actions if isinstance(a, argparse._SubParsersAction)]
+    names = sorted(actions[0].choices)
+    assert names == sorted(["analyze", "branch", "check_math", "compare_evaluations", "compare_seed_pairs",
+                            "cooldown", "evaluate", "evaluate_mechanisms", "plan_search", "prepare_data",
+                            "prepare_mechanisms", "profile", "reconcile", "record_spend", "summarize", "sweep",
+                            "sweep-config", "train", "validate_config"])
+    for name in names:
+        out = io.StringIO()
+        with contextlib.redirect_stdout(out), pytest.raises(SystemExit) as exit_info:
+            parser.parse_args([name, "--help"])
+        assert exit_info.value.code == 0 and "usage:" in out.getvalue(), name
