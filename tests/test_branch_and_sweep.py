@@ -135,3 +135,38 @@ def test_export_sweep_config_round_trips_the_recorded_config(tmp_path):
     (tmp_path / "sweep.json").write_text(json.dumps({"identity": identity, "identity_sha256": _digest(identity)}))
     with pytest.raises(ValueError):
         export_sweep_config(tmp_path, "cand-a")
+
+
+def test_sweep_plan_freezes_each_candidate_and_totals_the_projections(config):
+    """Candidates are laid over the base config section by section, frozen with their digests, and
+    their projected storage is summed; nothing is run or written."""
+    from tensor_train_ing_b200.search import overlay, plan_sweep
+    cands = [{"name": "base", "overrides": {}},
+             {"name": "lr2x", "overrides": {"train": {"lr": 0.02}}},
+             {"name": "wide", "overrides": {"model": {"d_model": 16}}}]
+    plan = plan_sweep(config, cands)
+    assert plan["candidate_count"] == 3 and [r["name"] for r in plan["runs"]] == ["base", "lr2x", "wide"]
+    by = {r["name"]: r for r in plan["runs"]}
+    assert by["lr2x"]["config"]["train"]["lr"] == 0.02 and by["base"]["config"]["train"]["lr"] == config.train.lr
+    assert by["wide"]["config"]["model"]["d_model"] == 16
+    assert len({r["config_sha256"] for r in plan["runs"]}) == 3
+    assert plan["required_additional_bytes"] == sum(r["plan"]["checkpoint_storage_plan"]["required_additional_bytes"]
+                                                    for r in plan["runs"])
+    assert plan_sweep(config, cands)["runs"][1]["config_sha256"] == by["lr2x"]["config_sha256"]  # deterministic
+    assert overlay({"a": {"b": 1, "c": 2}}, {"a": {"c": 3}}) == {"a": {"b": 1, "c": 3}}
+
+
+@pytest.mark.parametrize("bad", [
+    [],
+    [{"name": "x"}],
+    [{"name": "x", "overrides": {}, "extra": 1}],
+    [{"name": "../up", "overrides": {}}],
+    [{"name": "x", "overrides": {}}, {"name": "x", "overrides": {}}],
+    [{"name": "x", "overrides": {"optimizer": {"lr": 1}}}],
+    [{"name": "x", "overrides": {"train": 3}}],
+    [{"name": "x", "overrides": {"model": {"layers": {"deep": 1}}}}],
+])
+def test_sweep_plan_refuses_malformed_candidates(config, bad):
+    from tensor_train_ing_b200.search import plan_sweep
+    with pytest.raises(ValueError):
+        plan_sweep(config, bad)
