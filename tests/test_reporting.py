@@ -171,3 +171,20 @@ def test_ordered_tokenization_is_independent_of_workers_and_batching():
     assert [len(b) for b in batches([("d", "z")] * 300, 1 << 20)] == [128, 128, 44]  # 128 documents at most
     with pytest.raises(ValueError):
         list(ordered_tokenization(rows, tokenizer=FixtureTokenizer(), workers=0, batch_bytes=10))
+
+
+def test_config_flattening_and_differences_are_type_exact():
+    """Recorded configurations compare leaf by leaf on dot paths; an int and a float of equal value
+    differ (a changed type is a changed configuration), an empty section is a leaf, and keys that
+    would break the dot paths are refused."""
+    from tensor_train_ing_b200.replication import config_differences, flatten_config
+    tree = {"model": {"d_model": 8, "extra": {}}, "train": {"lr": 0.01, "seed": 1}}
+    assert flatten_config(tree) == {"config.model.d_model": 8, "config.model.extra": {}, "config.train.lr": 0.01,
+                                    "config.train.seed": 1}
+    other = {"model": {"d_model": 8.0, "extra": {}}, "train": {"lr": 0.01, "seed": 2}}
+    assert config_differences(tree, other) == ["config.model.d_model", "config.train.seed"]
+    assert config_differences(tree, other, ignore=("config.train.seed",)) == ["config.model.d_model"]
+    with pytest.raises(ValueError):
+        config_differences(tree, {"model": {"d_model": 8}, "train": {"lr": 0.01, "seed": 1}})
+    with pytest.raises(ValueError):
+        flatten_config({"a.b": 1})
