@@ -1,8 +1,9 @@
 """Worker: distributed trainer on gloo.  Checks that a resumed run replays an uninterrupted one
 bitwise and writes the final parameters for comparison with the serial trainer.
 
-argv: <shared tmp dir> [shard].  With ``shard`` the fp32 parameters are sharded over the ranks
-(owners only) and the comparisons use the exported full weights.  Prints ``REPLAY_OK`` on rank 0."""
+argv: <shared tmp dir> [mode].  Modes: replicated, shard (the fp32 parameters are sharded over the
+ranks, owners only, and the comparisons use the exported full weights), lagged, taper, cosine (the
+fixed-horizon schedule) and muon (Muon on the hidden matrices).  Prints ``REPLAY_OK`` on rank 0."""
 import json
 import os
 import sys
@@ -31,8 +32,13 @@ def config(tmp, mode="replicated"):
                  raw={"data": {"manifest": str(tmp / "data" / "manifest.json"), "context": 8, "micro_batch_size": 1,
                                "calibration_tokens": 16},
                       "project": {"dry_run": False, "gpu_hourly_rate_usd": 0, "spend_ledger": str(tmp / "spend.json")}})
-    if mode == "taper":
-        cfg.train.rung_total_tokens = 12 * 300  # the gate must end after the 100-update warm-up
+    if mode in ("taper", "cosine"):
+        cfg.train.rung_total_tokens = 12 * 300  # the gate / the decay must end after the 100-update warm-up
+    if mode == "cosine":
+        cfg.train.schedule = "cosine"
+    if mode == "muon":
+        cfg.train.optimizer = "muon"
+        cfg.train.aux_adamw_lr = .01
     return cfg
 
 

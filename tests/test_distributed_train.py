@@ -18,7 +18,7 @@ def _torchrun(worker, nproc, *args, timeout=600):
 
 
 @pytest.mark.slow
-@pytest.mark.parametrize("mode", ["replicated", "shard", "lagged", "taper"])
+@pytest.mark.parametrize("mode", ["replicated", "shard", "lagged", "taper", "cosine", "muon"])
 def test_two_rank_training_replays_and_matches_serial(tmp_path, mode):
     out = _torchrun("train_replay.py", 2, str(tmp_path), mode)
     assert out.returncode == 0, out.stdout[-3000:] + out.stderr[-4000:]
