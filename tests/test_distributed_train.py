@@ -41,3 +41,10 @@ def test_two_rank_training_replays_and_matches_serial(tmp_path, mode):
     d = torch.load(tmp_path / "full" / "final-weights" / "state.pt", weights_only=False)["model"]
     for k in s:
         torch.testing.assert_close(s[k], d[k], rtol=1e-4, atol=1e-5)
+
+
+@pytest.mark.slow
+def test_two_rank_context_fork_is_recorded_and_deterministic(tmp_path):
+    out = _torchrun("context_fork.py", 2, str(tmp_path))
+    assert out.returncode == 0, out.stdout[-3000:] + out.stderr[-4000:]
+    assert "FORK_OK" in out.stdout
