@@ -1,5 +1,5 @@
-"""Host-side failure injection on CPU ranks: a rank-local error, a corrupted shard and a departed rank
-end as errors on every rank, never as a hang."""
+"""Host-side failure injection on CPU ranks: a rank-local error, a corrupted shard, a departed rank,
+a non-finite gradient on one rank and a full disk end as errors on every rank, never as a hang."""
 import os
 import subprocess
 import sys
@@ -18,7 +18,8 @@ def _run(scenario, tmp_path, nproc=2):
 
 
 @pytest.mark.slow
-@pytest.mark.parametrize("scenario,expected", [("phase", 2), ("corrupt", 2), ("dead_rank", 1)])
+@pytest.mark.parametrize("scenario,expected", [("phase", 2), ("corrupt", 2), ("dead_rank", 1), ("nonfinite", 2),
+                                               ("disk_full", 2)])
 def test_failures_reach_every_rank(scenario, expected, tmp_path):
     out = _run(scenario, tmp_path)
     assert out.stdout.count(f"SCENARIO_OK {scenario}") == expected, out.stdout[-2000:] + out.stderr[-3000:]
