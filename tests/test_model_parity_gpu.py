@@ -219,3 +219,32 @@ def test_score_bounds_from_the_qkv_epilogue(kind, dk):
         for name in got:
             assert got[name].shape == (2,) and bool((got[name] > 0).all())
             torch.testing.assert_close(got[name], want[name].float(), rtol=2e-2, atol=1e-4)
+
+
+def test_selective_recompute_on_the_fused_path_keeps_every_gradient():
+    """Activation checkpointing on the fused path: recomputing all, some or none of the blocks gives
+    bit-identical gradients (the recomputed forward runs the same kernels on the same inputs)."""
+    from tensor_train_ing_b200.config import ModelConfig
+    from tensor_train_ing_b200.models.model import TensorLM
+    cfg = ModelConfig(layers=3, d_model=256, heads=4, d_key=64, d_value=64, d_mlp=512, vocab_size=1000,
+                      padded_vocab=1024, loss_chunk_tokens=512, activation_checkpointing=True)
+    torch.manual_seed(0)
+    model = TensorLM(cfg).cuda()
+    g = torch.Generator().manual_seed(2)
+    idx = torch.randint(0, 1000, (2, 256), generator=g).cuda()
+    doc = torch.zeros_like(idx)
+    doc[:, 100:] = 1
+    tgt = torch.roll(idx, -1, 1)
+    grads = []
+    for recompute in (None, 2, 0):
+        model.recompute_blocks = recompute
+        model.zero_grad(set_to_none=True)
+        assert model.recomputed_blocks() == (3 if recompute is None else recompute)
+        _, loss, _ = model(idx, doc, tgt, reduction="sum")
+        loss.backward()
+        grads.append({n: p.grad.clone() for n, p in model.named_parameters() if p.grad is not None})
+    torch.cuda.synchronize()
+    for other in grads[1:]:
+        assert other.keys() == grads[0].keys()
+        for n in grads[0]:
+            assert torch.equal(grads[0][n], other[n]), n
