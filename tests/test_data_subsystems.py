@@ -88,3 +88,36 @@ def test_mechanism_tasks_reject_tampering_and_bad_sizes(tmp_path):
         prepare_mechanism_tasks(tmp_path / "odd", train_examples=9)
     with pytest.raises(ValueError):
         prepare_mechanism_tasks(tmp_path / "big", validation_examples=44)
+
+
+def test_mechanism_tasks_are_a_function_of_their_seed(tmp_path):
+    a = prepare_mechanism_tasks(tmp_path / "a", seed=5, train_examples=8, validation_examples=8)
+    b = prepare_mechanism_tasks(tmp_path / "b", seed=5, train_examples=8, validation_examples=8)
+    c = prepare_mechanism_tasks(tmp_path / "c", seed=6, train_examples=8, validation_examples=8)
+    for name in ("train.jsonl", "val.jsonl"):
+        assert Path(a).with_name(name).read_bytes() == Path(b).with_name(name).read_bytes()
+        assert Path(a).with_name(name).read_bytes() != Path(c).with_name(name).read_bytes()
+
+
+def test_mechanism_training_audit_finds_leaked_validation_examples(tmp_path):
+    """A corpus prepared from the benchmark's own train.jsonl is verified; one that also contains a
+    validation example reports that composition as overlapping."""
+    from helpers import FixtureTokenizer
+    from tensor_train_ing_b200.data import prepare_data
+    from tensor_train_ing_b200.tasks import audit_mechanism_training
+    manifest = prepare_mechanism_tasks(tmp_path / "mech", seed=1, train_examples=8, validation_examples=8)
+    train_src = Path(manifest).with_name("train.jsonl")
+    splits = {"train": 1.0, "val": 0.0, "test": 0.0, "calibration": 0.0}
+    clean = prepare_data(tmp_path / "clean", source_jsonl=train_src, revision="offline-v1",
+                         tokenizer=FixtureTokenizer(), split_fractions=splits)
+    report = audit_mechanism_training(manifest, clean)
+    assert report["verified"] and report["status"] == "verified" and not report["has_validation_overlap"]
+    assert report["coverage"]["fraction"] == 1.0
+    _, val = load_mechanism_tasks(manifest, "val")
+    leaked = tmp_path / "leaked.jsonl"
+    leaked.write_text(train_src.read_text() + json.dumps({"id": "leak", "text": val[0]["text"]}) + "\n")
+    dirty = prepare_data(tmp_path / "dirty", source_jsonl=leaked, revision="offline-v1",
+                         tokenizer=FixtureTokenizer(), split_fractions=splits)
+    report = audit_mechanism_training(manifest, dirty)
+    assert report["status"] == "overlap" and not report["verified"]
+    assert val[0]["composition_id"] in report["validation_composition_overlap"][val[0]["task"]]
