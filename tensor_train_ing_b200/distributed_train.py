@@ -133,14 +133,19 @@ def distributed_train_run(cfg, run_dir, *, max_steps, max_seconds, device="cuda"
                          project.get("reserve_usd", 150), stage_budgets=project.get("stage_budgets")) if rank == 0 else None
     run_id = str(run_dir.resolve())
 
-    def begin():
+    def fresh():
         if run_dir.exists():
             raise FileExistsError(f"run directory already exists: {run_dir}")
+
+    def begin():
         if rank == 0:
             # one reservation for the whole job: the declared rate is per GPU
             ledger.begin(run_id, rate * world, max_seconds, run_budget_usd, parent_checkpoint=resume,
                          cost_margin_fraction=project.get("cost_margin_fraction", .1), stage=project.get("stage", "A"))
             run_dir.mkdir(parents=True)
+    # every rank looks for an existing directory before rank 0 creates it (one phase each: a rank that
+    # looked after the creation would otherwise refuse the job's own directory)
+    _phase("run directory check", fresh)
     _phase("run reservation", begin)
     started = time.monotonic()
     status = "failed"
