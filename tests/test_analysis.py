@@ -74,3 +74,50 @@ def test_swiglu_layers_are_skipped_by_the_local_tensor_check(tmp_path):
     result = analyze(model, batches, tmp_path / "ana")
     assert all(row.get("skipped") for row in result["local_tensor"]["per_layer"])
     assert result["operator_class"] == "G"
+
+
+def test_analytic_norm_jvp_matches_autograd_in_fp64():
+    """The (group) RMSNorm Jacobian-vector product splits into a direct part delta/r and a radial part
+    (the divisor's response); their sum equals autograd's JVP, and the radial part vanishes for a
+    perturbation orthogonal to x within each group."""
+    import torch
+
+    from tensor_train_ing_b200.analysis import _analytic_jvp
+    from tensor_train_ing_b200.models.normalization import GroupRMSNorm, RMSNorm
+    torch.manual_seed(0)
+    for norm in (RMSNorm(16, 1e-6).double(), GroupRMSNorm(16, 4).double()):
+        with torch.no_grad():
+            norm.weight.uniform_(0.5, 1.5)
+        x = torch.randn(5, 16, dtype=torch.float64)
+        delta = torch.randn(5, 16, dtype=torch.float64)
+        direct, radial = _analytic_jvp(norm, x, delta)
+        _, ref = torch.func.jvp(norm, (x,), (delta,))
+        torch.testing.assert_close(direct + radial, ref, rtol=1e-10, atol=1e-12)
+        groups = getattr(norm, "groups", 1)
+        xs, ds = x.unflatten(-1, (groups, -1)), delta.unflatten(-1, (groups, -1))
+        ortho = (ds - xs * (xs * ds).sum(-1, keepdim=True) / xs.square().sum(-1, keepdim=True)).flatten(-2)
+        _, radial_ortho = _analytic_jvp(norm, x, ortho)
+        assert float(radial_ortho.abs().max()) < 1e-12
+
+
+def test_norm_gains_fold_lagged_and_refuse_a_mid_taper():
+    """The fixed map a norm site folds into the adjacent linear maps: gamma for RMS, gamma over the
+    frozen RMS for the lagged norm; a TaperRMS part-way through its gate has none."""
+    import torch
+
+    from tensor_train_ing_b200.analysis import gain, norm_scope
+    from tensor_train_ing_b200.models.normalization import LaggedRMS, RMSNorm, TaperRMS
+    rms = RMSNorm(8, 1e-6)
+    assert torch.equal(gain(rms, 8, "cpu"), rms.weight.detach().float())
+    assert norm_scope(rms) == "per-token RMS over all features"
+    lag = LaggedRMS(8)
+    with torch.no_grad():
+        lag.mean_sq.fill_(4.0)
+    expected = lag.weight.detach().float() / torch.sqrt(torch.tensor(4.0) + lag.eps)
+    torch.testing.assert_close(gain(lag, 8, "cpu"), expected)
+    taper = TaperRMS(8)
+    with torch.no_grad():
+        taper.gate.fill_(0.5)
+    with pytest.raises(ValueError, match="no fixed map"):
+        gain(taper, 8, "cpu")
+    assert torch.equal(gain(torch.nn.Identity(), 8, "cpu"), torch.ones(8))
