@@ -183,3 +183,22 @@ def test_cosine_schedule_follows_its_multiplier(config, tmp_path):
     rows = [json.loads(x) for x in (tmp_path / "run" / "metrics.jsonl").read_text().splitlines()]
     for k, r in enumerate(rows):
         assert r["lr"] == pytest.approx(cfg.train.lr * schedule_multiplier(k, 150, schedule="cosine"))
+
+
+def test_metrics_rows_carry_progress_rate_and_cost(config, tmp_path):
+    """Each update row records the step, the cumulative tokens (one quota per update), the loss, the
+    learning rate, the elapsed run time, the billed dollars at the configured rate and the token rate
+    since the previous row; steps and times only grow."""
+    cfg = copy.deepcopy(config)
+    cfg.raw["project"]["gpu_hourly_rate_usd"] = 3.6
+    train_run(cfg, tmp_path / "run", max_steps=4, max_seconds=120, device="cpu")
+    rows = [json.loads(x) for x in (tmp_path / "run" / "metrics.jsonl").read_text().splitlines()]
+    rows = [r for r in rows if r.get("kind", "train") == "train"]
+    assert [r["step"] for r in rows] == [1, 2, 3, 4]
+    quota = cfg.train.global_prediction_tokens_per_update
+    assert [r["tokens"] for r in rows] == [quota * (i + 1) for i in range(4)]
+    times = [r["run_elapsed_seconds"] for r in rows]
+    assert times == sorted(times) and times[0] > 0
+    for r in rows:
+        assert r["loss"] > 0 and r["lr"] >= 0 and r["tokens_per_second"] > 0
+        assert r["run_billed_usd"] == pytest.approx(r["run_elapsed_seconds"] * 3.6 / 3600)
