@@ -409,8 +409,14 @@ def main():
             e2e = {"value": tokens_per_step * e2e_steps / wall, "unit": "tokens/s",
                    "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": 4,
                    "api": "TrainEngine.step" if args.impl == "ours" else "tnlm TensorLM/make_optimizer loop"}
-    finally:
-        pass
+    except torch.OutOfMemoryError as e:
+        # the reference's stock path may not fit a configuration on one GPU (7B at micro-batch 4): say so
+        # in one line; a multi-rank run ends through torchrun, whose other ranks stop with this one
+        if args.impl != "reference" or world > 1:
+            raise
+        print(json.dumps({"impl": "reference", "unavailable": f"out of memory: {str(e).splitlines()[0]}"[:300],
+                          "config": {"model": f"tnlm-{args.config}", "micro_batch": args.micro_batch}}))
+        return
 
     peaks_path = os.path.join(ROOT, "MEASURED_PEAKS.json")
     peak_tflops, sustained_tflops = 1590.0, 1400.0
