@@ -8,12 +8,20 @@ documents.jsonl), the row layout and each split's count, size and sha256.  Direc
 and header are the reference platform's, so either framework reads an index the other built.  The
 index is derived data: it is verified on load and rebuilt when missing or stale (the reference
 instead asks for an explicit rebuild); builds take the dataset's ``.sampler-index-v1.lock``.
+
+A long run reads rows from all over the index (one epoch visits every document in shuffled order),
+so without a bound the mapping's resident pages would grow to the whole file.  ``IndexedDocuments``
+counts its row reads and, every ``RELEASE_EVERY`` of them, drops this process's resident pages of the
+mapping with ``madvise(MADV_DONTNEED)`` (reference ``tnlm/sampler_index.py:247-320`` bounds residency
+the same way).  The file is read-only and shared, so a release changes no value: later reads fault
+the pages back in from the page cache.
 """
 from __future__ import annotations
 
 import fcntl
 import hashlib
 import json
+import mmap
 import os
 import tempfile
 from collections.abc import Mapping, Sequence
@@ -124,30 +132,67 @@ class _Document(Mapping):
 
 
 class IndexedDocuments(Sequence):
-    """Documents of one split, in ``documents.jsonl`` order."""
+    """Documents of one split, in ``documents.jsonl`` order.
+
+    ``length``, ``start``, ``numeric_id`` and item access read one index row each; every
+    ``RELEASE_EVERY`` such reads the mapping's resident pages are released (``release_pages``).
+    Code that reads ``rows`` directly bypasses the count and may call ``release_pages`` itself."""
+
+    RELEASE_EVERY = 4096
 
     def __init__(self, root, cache, split):
         self.root, self.cache_dir, self.split = Path(root), Path(cache), split
         path = self.cache_dir / f"{split}.index.bin"
         n = path.stat().st_size // RECORD.itemsize
         self.rows = np.memmap(path, dtype=RECORD, mode="r", shape=(n,)) if n else np.empty(0, dtype=RECORD)
-        self._meta = self.root / "documents.jsonl"
+        self._meta = (self.root / "documents.jsonl").open("rb")
+        self.reads = 0         # row reads since the last release
+        self.releases = 0      # releases that took effect
+
+    def release_pages(self) -> bool:
+        """Drop this process's resident pages of the index mapping.  False where the platform has no
+        ``madvise``/``MADV_DONTNEED`` or the call fails (the values read are the same either way)."""
+        self.reads = 0
+        mapped = getattr(self.rows, "_mmap", None)
+        advice = getattr(mmap, "MADV_DONTNEED", None)
+        if mapped is None or advice is None or not hasattr(mapped, "madvise"):
+            return False
+        try:
+            mapped.madvise(advice)
+        except (OSError, ValueError):
+            return False
+        self.releases += 1
+        return True
+
+    def _row(self, i):
+        n = len(self.rows)
+        i = int(i)
+        if i < 0:
+            i += n
+        if not 0 <= i < n:
+            raise IndexError(f"document {i} outside a split of {n}")
+        self.reads += 1
+        if self.reads >= self.RELEASE_EVERY:
+            self.release_pages()
+        return i, self.rows[i]
 
     def length(self, i):
-        r = self.rows[i]
+        _, r = self._row(i)
         return int(r["token_end"] - r["token_start"])
 
     def start(self, i):
-        return int(self.rows[i]["token_start"])
+        return int(self._row(i)[1]["token_start"])
 
     def numeric_id(self, i):
-        return int(self.rows[i]["numeric_id"])
+        return int(self._row(i)[1]["numeric_id"])
 
     def full_document(self, i):
-        r = self.rows[i]
-        with self._meta.open("rb") as fh:
-            fh.seek(int(r["metadata_offset"]))
-            return json.loads(fh.read(int(r["metadata_length"])))
+        _, r = self._row(i)
+        raw = os.pread(self._meta.fileno(), int(r["metadata_length"]), int(r["metadata_offset"]))
+        return json.loads(raw)
+
+    def close(self):
+        self._meta.close()
 
     def __len__(self):
         return len(self.rows)
@@ -155,7 +200,7 @@ class IndexedDocuments(Sequence):
     def __getitem__(self, i):
         if isinstance(i, slice):
             return [self[j] for j in range(*i.indices(len(self)))]
-        return _Document(self, i)
+        return _Document(self, self._row(i)[0])
 
 
 def load_sampler_index(root, manifest, split, *, rebuild: bool = False) -> IndexedDocuments:

@@ -55,6 +55,79 @@ def test_stale_or_corrupt_index_is_rebuilt(dataset):
         load_sampler_index(root, manifest, "holdout")
 
 
+def test_index_is_a_bounded_sequence(dataset):
+    """Iteration stops at the end of the split, negative positions count from the end and positions
+    outside the split raise IndexError (the contract ``Sequence`` iteration relies on)."""
+    root, manifest = dataset
+    idx = load_sampler_index(root, manifest, "train")
+    ids = [d["id"] for d in idx]
+    assert len(ids) == len(idx) > 1
+    assert idx[-1]["id"] == ids[-1] and idx.start(-1) == idx.start(len(idx) - 1)
+    for bad in (len(idx), -len(idx) - 1):
+        with pytest.raises(IndexError):
+            idx[bad]
+        with pytest.raises(IndexError):
+            idx.length(bad)
+    assert [d["id"] for d in idx[1:3]] == ids[1:3]
+
+
+def test_page_release_keeps_the_sampler_stream(dataset):
+    """Releasing the mapping's resident pages (periodically or by hand) changes no value the
+    sampler reads: two samplers, one releasing after every row read, give the same batches."""
+    from tensor_train_ing_b200.data import PackedSampler
+    root, manifest = dataset
+    plain = PackedSampler(root / "manifest.json", batch_size=2, context=6, seed=4)
+    released = PackedSampler(root / "manifest.json", batch_size=2, context=6, seed=4)
+    released.docs.RELEASE_EVERY = 1
+    for _ in range(8):
+        a, b = plain.next_batch(), released.next_batch()
+        for x, y in zip(a, b):
+            assert (x == y).all()
+    assert released.docs.releases > 0 and plain.docs.releases == 0
+    assert released.docs.release_pages() is True and released.docs.reads == 0
+
+
+def test_page_release_counts_reads_and_is_safe_without_madvise(dataset, monkeypatch):
+    import mmap
+    root, manifest = dataset
+    idx = load_sampler_index(root, manifest, "train")
+    idx.RELEASE_EVERY = 5
+    calls = []
+    real = idx.release_pages
+    monkeypatch.setattr(idx, "release_pages", lambda: calls.append(idx.reads) or real())
+    for i in range(12):
+        idx.length(i % len(idx))
+    assert calls == [5, 5]  # two releases after five reads each, the count reset by each
+    monkeypatch.undo()
+    before = [idx.start(i) for i in range(len(idx))]
+    monkeypatch.delattr(mmap, "MADV_DONTNEED")
+    assert idx.release_pages() is False  # no such advice here: nothing released, nothing changed
+    assert [idx.start(i) for i in range(len(idx))] == before
+
+
+def test_concurrent_builds_publish_one_valid_index(dataset):
+    """Ranks that find no index at once serialise on the dataset's lock: one builds, the others
+    find it valid, and every one reads the same rows."""
+    import threading
+    root, manifest = dataset
+    loaded, errors = [], []
+
+    def load():
+        try:
+            loaded.append([idx.start(i) for idx in [load_sampler_index(root, manifest, "train")]
+                           for i in range(len(idx))])
+        except Exception as exc:  # pragma: no cover - reported below
+            errors.append(exc)
+    threads = [threading.Thread(target=load) for _ in range(6)]
+    for t in threads:
+        t.start()
+    for t in threads:
+        t.join()
+    assert not errors and len(loaded) == 6 and all(x == loaded[0] for x in loaded)
+    leftovers = [p.name for p in (root / INDEX_DIR).iterdir() if p.name.startswith(".")]
+    assert leftovers == []  # no temporary file of an interrupted publication
+
+
 def test_mechanism_tasks_exact_labels_and_held_out_compositions(tmp_path):
     manifest = prepare_mechanism_tasks(tmp_path / "mech", seed=3, train_examples=8, validation_examples=8)
     meta, val = load_mechanism_tasks(manifest, "val")
