@@ -417,6 +417,45 @@ def test_checkpoint_storage_plans_match_the_reference(tnlm):
             assert all(ours[k] == theirs[k] for k in ours), (optimizer, rung)
 
 
+@pytest.mark.parametrize("case", [
+    dict(plan=dict(token_limit=10_000_000, max_steps=2)),
+    dict(plan=dict(token_limit=1_000_000_000, distributed=True, distributed_world_size=2)),
+    dict(plan=dict(token_limit=10_000_000, cooldown=True)),
+    dict(plan=dict(start_tokens=2_000_000, token_limit=4_000_001, max_steps=1)),
+    dict(plan=dict(max_steps=0, export_weights=True)),
+    dict(plan=dict(token_limit=10 ** 40)),
+    dict(plan=dict(max_steps=0, export_weights=True, distributed=True, distributed_world_size=3), tie=True),
+    dict(plan=dict(token_limit=16), milestones=[7, 14, 14]),
+    dict(plan=dict(token_limit=20_000_000, distributed=True, distributed_world_size=2), milestones=[]),
+    dict(plan=dict(max_steps=0), normalization="spectral_rms", optimizer="muon"),
+    dict(plan=dict(token_limit=200_000_000, max_steps=123), retention=dict(keep_recovery_checkpoints=0,
+                                                                            save_initial_checkpoint=False)),
+])
+def test_checkpoint_storage_plan_edge_cases_match_the_reference(tnlm, case):
+    """Resumes, zero-update runs, horizons beyond any int64, tied embeddings, explicit and empty
+    milestone lists, the cooldown and distributed branch rules and the retention switches give the
+    reference's plan field for field."""
+    import tnlm.checkpoint_plan as ref_plan
+
+    from tensor_train_ing_b200 import checkpoint_plan
+    from tensor_train_ing_b200.config import Config, ModelConfig, TrainConfig
+    mk = dict(layers=1, d_model=8, heads=1, d_key=4, d_value=4, d_mlp=12, vocab_size=16, padded_vocab=16,
+              attention_backend="reference", tie_embeddings=case.get("tie", False),
+              normalization=case.get("normalization", "pre_rms"))
+    tk = dict(global_prediction_tokens_per_update=1_000_000, optimizer=case.get("optimizer", "adamw"))
+    project = {}
+    if "milestones" in case:
+        project["milestone_tokens"] = case["milestones"]
+    project.update(case.get("retention", {}))
+    ours = checkpoint_plan.checkpoint_storage_plan(
+        Config(model=ModelConfig(**mk), train=TrainConfig(**tk), raw={"project": dict(project)}), **case["plan"])
+    theirs = ref_plan.checkpoint_storage_plan(
+        tnlm.config.Config(model=tnlm.config.ModelConfig(**mk), train=tnlm.config.TrainConfig(**tk),
+                           raw={"project": dict(project)}), **case["plan"])
+    theirs.pop("assumptions")
+    assert ours == theirs
+
+
 def test_both_trainers_share_one_spend_ledger(tnlm, tmp_path):
     """Runs of either framework reserve, bill and complete entries in the same locked ledger file."""
     import json
