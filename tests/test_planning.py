@@ -117,6 +117,52 @@ def test_storage_plan_counts_parameters_moments_and_checkpoints():
         checkpoint_storage_plan(cfg, distributed_world_size=2)  # serial plan with a world size
 
 
+def test_storage_plan_builds_nothing_real_and_draws_no_random_numbers(monkeypatch):
+    """The plan sizes a model built on the meta device: no parameter memory, and the Python, NumPy
+    and torch generators are where they were (a plan before a run does not shift its initialisation)."""
+    import random
+
+    import numpy as np
+    built = []
+    original = TensorLM.__init__
+
+    def recording(self, *args, **kwargs):
+        original(self, *args, **kwargs)
+        built.append({p.device.type for p in self.parameters()})
+    monkeypatch.setattr(TensorLM, "__init__", recording)
+    py, npy, th = random.getstate(), np.random.get_state()[1].copy(), torch.get_rng_state().clone()
+    checkpoint_storage_plan(_cfg(optimizer="adamw"))
+    assert built and all(kinds == {"meta"} for kinds in built)
+    assert random.getstate() == py and (np.random.get_state()[1] == npy).all()
+    assert torch.equal(torch.get_rng_state(), th)
+
+
+def test_storage_plan_follows_the_default_dtype_and_huge_horizons_stay_json():
+    base = checkpoint_storage_plan(_cfg(optimizer="adamw"), max_steps=0)
+    old = torch.get_default_dtype()
+    try:
+        torch.set_default_dtype(torch.float64)
+        double = checkpoint_storage_plan(_cfg(optimizer="adamw"), max_steps=0)
+    finally:
+        torch.set_default_dtype(old)
+    assert double["tensor_bytes_breakdown"]["parameters"] == 2 * base["tensor_bytes_breakdown"]["parameters"]
+    assert double["dtype"] == "torch.float64"
+    huge = checkpoint_storage_plan(_cfg(optimizer="adamw"), token_limit=10 ** 40)
+    assert huge["count_breakdown"]["milestones"] > 10 ** 30  # counted in closed form, not enumerated
+    json.dumps(huge, allow_nan=False)
+    exported = checkpoint_storage_plan(_cfg(optimizer="adamw"), max_steps=0, export_weights=True)
+    assert exported["required_additional_bytes"] == (base["required_additional_bytes"]
+                                                     + exported["export_weights_estimate_bytes"])
+
+
+@pytest.mark.parametrize("bad", [{"start_tokens": -1}, {"token_limit": float("inf")}, {"max_steps": True},
+                                 {"max_steps": 2.5}, {"distributed_world_size": 0}, {"cooldown": 1},
+                                 {"distributed": "yes"}])
+def test_storage_plan_rejects_malformed_arguments(bad):
+    with pytest.raises(ValueError):
+        checkpoint_storage_plan(_cfg(optimizer="adamw"), **bad)
+
+
 def test_space_estimate_counts_shared_storage_once():
     a = torch.zeros(1000)
     once = checkpoint_space_estimate({"x": a})
