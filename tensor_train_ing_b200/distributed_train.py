@@ -10,7 +10,10 @@ tnlm/distributed_train.py:45-550).
   norm is clipped (error on non-finite), each rank updates the matrices it owns and one all-gather
   returns the replicas to bitwise agreement.
 * Lifecycle: collective lagged calibration and commits, TaperNorm, per-update score bounds (max over
-  ranks) with batch-bound QK-clip, constant / cooldown / cosine schedules, context forks, sharded
+  ranks) with batch-bound QK-clip (the reference refuses QK-clip in its distributed trainer,
+  tnlm/distributed_train.py:126-128; here every rank clips each head by the maximum over the ranks of
+  their last micro-batch's bound, so the replicated weights stay identical), constant / cooldown /
+  cosine schedules, context forks, sharded
   recovery checkpoints (``ttb-sharded-v1``) and an optional full-state weight export.
 * Control plane: validation and I/O run under ``_phase`` so a rank-local error fails every rank at
   the same step; time limits use the maximum over ranks so all ranks stop at the same update.
@@ -154,6 +157,12 @@ def distributed_train_run(cfg, run_dir, *, max_steps, max_seconds, device="cuda"
         t = torch.tensor([float(value)], dtype=torch.float64, device=dev if dist.get_backend() == "nccl" else "cpu")
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         return float(t.item())
+
+    def max_over_ranks_(t: torch.Tensor) -> None:
+        on = t.to(dev) if dist.get_backend() == "nccl" else t
+        dist.all_reduce(on, op=dist.ReduceOp.MAX)
+        if on is not t:
+            t.copy_(on.cpu())
 
     def expired() -> bool:
         return max_value(time.monotonic() - started) >= max_seconds
@@ -376,6 +385,7 @@ def distributed_train_run(cfg, run_dir, *, max_steps, max_seconds, device="cuda"
             taper.after_step(progress["steps"])
             clipping = None
             if clip_tau > 0 and progress["steps"] % clip_every == 0:
+                bounds.reduce_last(max_over_ranks_)  # one clip factor per head on every rank
                 clipping = bounds.clip(clip_tau)
                 if dp.shard_params:
                     dp.gather_params()  # owners rescaled their masters: refresh every rank's copies

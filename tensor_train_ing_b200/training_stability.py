@@ -144,6 +144,25 @@ class BatchScoreBounds:
             raise FloatingPointError("a score bound was non-finite or negative; the update is aborted")
         return top
 
+    def reduce_last(self, all_reduce_max_) -> None:
+        """Data-parallel ranks each ran their own last micro-batch, so their recorded per-head bounds
+        differ; clipping from them would rescale the replicated Q/K weights differently on each rank.
+        This replaces them with their maximum over the ranks (``all_reduce_max_`` reduces a flat fp64
+        CPU tensor in place), a bound on the scores of every rank's last micro-batch, so every rank
+        clips by the same factors.  A rank that ran no micro-batch contributes zeros (bounds are
+        nonnegative)."""
+        heads = self.model.cfg.heads
+        layout = [(layer, f) for layer, blk in enumerate(self.model.blocks)
+                  for f in (("S1", "S2") if hasattr(blk.attn, "q2") else ("S1",))]
+        flat = torch.zeros(len(layout) * heads, dtype=torch.float64)
+        if self.last is not None:
+            for k, (layer, f) in enumerate(layout):
+                flat[k * heads:(k + 1) * heads] = self.last[layer][f].detach().to("cpu", torch.float64)
+        all_reduce_max_(flat)
+        self.last = [{} for _ in self.model.blocks]
+        for k, (layer, f) in enumerate(layout):
+            self.last[layer][f] = flat[k * heads:(k + 1) * heads]
+
     def clip(self, tau) -> dict:
         from .qk_clip import qk_clip_from_bounds_
         self.finish_update()

@@ -3,7 +3,10 @@ bitwise and writes the final parameters for comparison with the serial trainer.
 
 argv: <shared tmp dir> [mode].  Modes: replicated, shard (the fp32 parameters are sharded over the
 ranks, owners only, and the comparisons use the exported full weights), lagged, taper, cosine (the
-fixed-horizon schedule) and muon (Muon on the hidden matrices).  Prints ``REPLAY_OK`` on rank 0."""
+fixed-horizon schedule), muon (Muon on the hidden matrices) and qkclip (QK-clip every update from
+the batch score bounds, with a threshold every head exceeds; qkclip-shard the same with sharded
+parameters, where only owners rescale and the gather brings the result).  Prints ``REPLAY_OK`` on
+rank 0."""
 import json
 import os
 import sys
@@ -39,13 +42,17 @@ def config(tmp, mode="replicated"):
     if mode == "muon":
         cfg.train.optimizer = "muon"
         cfg.train.aux_adamw_lr = .01
+    if mode.startswith("qkclip"):
+        cfg.train.qk_clip_tau = 1e-3
+        cfg.train.qk_clip_every_steps = 1
+        cfg.train.qk_clip_source = "batch_bound"
     return cfg
 
 
 def main():
     tmp = Path(sys.argv[1])
     mode = sys.argv[2] if len(sys.argv) > 2 else "replicated"
-    shard = mode == "shard"
+    shard = mode in ("shard", "qkclip-shard")
     os.environ["TTB_SHARD_PARAMS"] = "1" if shard else "0"
     dist.init_process_group("gloo")
     rank = dist.get_rank()
