@@ -456,6 +456,59 @@ def test_checkpoint_storage_plan_edge_cases_match_the_reference(tnlm, case):
     assert ours == theirs
 
 
+def test_training_evidence_descriptors_match_the_reference(tnlm):
+    """The training evidence an evaluation report carries (batch and context histories, cooldown and
+    completion status) is the reference's, field for field, on valid, partial, malformed and
+    inconsistent checkpoint payloads, and so are the comparisons built from it."""
+    import copy
+    import itertools
+
+    import tnlm.evaluate as ref_eval
+
+    from tensor_train_ing_b200 import evaluate as our_eval
+    base = {"config": {"train": {"global_prediction_tokens_per_update": 48, "lr": 0.03, "aux_adamw_lr": None,
+                                 "rung_total_tokens": 480, "schedule": "constant"},
+                       "model": {"d_model": 64, "layers": 2}, "data": {"context": 32}},
+            "progress": {"tokens": 160, "steps": 6, "scheduler_step": 6, "batch_history": [
+                {"batch_tokens": 16, "lr": 0.01, "aux_adamw_lr": None, "start_tokens": 0, "start_step": 0,
+                 "source": "fresh"},
+                {"batch_tokens": 48, "lr": 0.03, "aux_adamw_lr": None, "start_tokens": 64, "start_step": 4,
+                 "source": "batch_branch", "lr_scale": 3.0, "parent": {"path": "/p"}}],
+                "context_history": [{"context": 16, "start_tokens": 0, "start_step": 0, "source": "fresh"},
+                                    {"context": 32, "start_tokens": 96, "start_step": 5, "source": "context_fork"}]},
+            "extra": {"cooldown_steps": None}}
+    edits = [None, ("batch_history", 0, "source", "legacy_unknown"), ("batch_history", 1, "start_tokens", 161),
+             ("batch_history", 1, "lr_scale", 0), ("batch_history", 1, "lr", 0.05),
+             ("batch_history", 0, "batch_tokens", True), ("context_history", 1, "context", 8),
+             ("context_history", 1, "source", "fresh"), ("context_history", 0, "source", "legacy_unknown"),
+             ("context_history", 1, "start_step", 9), ("extra", None, "cooldown_steps", 4),
+             ("progress", None, "cooldown_start_tokens", 120), ("progress", None, "tokens", 480),
+             ("config", "train", "schedule", "cosine")]
+    payloads = []
+    for edit in edits:
+        p = copy.deepcopy(base)
+        if edit is not None:
+            where, i, field, value = edit
+            if where in ("batch_history", "context_history"):
+                p["progress"][where][i][field] = value
+            elif where == "config":
+                p["config"][i][field] = value
+            else:
+                p[where][field] = value
+        payloads.append(p)
+    ours = [our_eval._training_descriptor(p) for p in payloads]
+    # the reference adds two descriptive sentences about the histories' scope; the values are compared
+    theirs = [{k: v for k, v in ref_eval._training_descriptor(p).items()
+               if k not in ("batch_history_scope", "context_history_scope")} for p in payloads]
+    for o, t, edit in zip(ours, theirs, edits):
+        assert o == t, edit
+    for a, b in itertools.combinations(range(len(payloads)), 2):
+        mine = our_eval._training_comparison({"training_descriptor": ours[a]}, {"training_descriptor": ours[b]})
+        ref = ref_eval._training_comparison({"training_descriptor": theirs[a]}, {"training_descriptor": theirs[b]})
+        mine.pop("scope"), ref.pop("scope")  # descriptive sentences
+        assert mine == ref, (edits[a], edits[b])
+
+
 def test_both_trainers_share_one_spend_ledger(tnlm, tmp_path):
     """Runs of either framework reserve, bill and complete entries in the same locked ledger file."""
     import json
