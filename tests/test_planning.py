@@ -210,6 +210,75 @@ def test_exposure_accumulates_lr_and_decay_shrinkage():
         update_optimizer_exposure(progress, opt)
 
 
+def _exposure_opt(lr=0.01, wd=0.1):
+    torch.manual_seed(0)
+    model = TensorLM(ModelConfig(**TINY_MODEL))
+    return make_optimizer(model, TrainConfig(optimizer="adamw", lr=lr, weight_decay_hidden=wd))
+
+
+def test_exposure_zero_and_negative_decay_factors_stay_finite():
+    """lr * wd = 1 zeroes the shrinkage (its sign becomes 0 and the log is undefined, recorded as
+    None); lr * wd > 1 flips its sign once per such update; the record stays finite JSON; a zero
+    rate still counts as an update."""
+    opt = _exposure_opt()
+    progress = {"steps": 0, "tokens": 0}
+    hidden = lambda: progress["optimizer_exposure"]["groups"][0]  # noqa: E731
+    for lr, wd in ((0.0, 0.1), (3.0, 1.0), (4.0, 1.0)):
+        for g in opt.param_groups:
+            g["lr"] = lr
+            g["weight_decay"] = wd if g["weight_decay"] else 0.0
+        update_optimizer_exposure(progress, opt)
+        progress["steps"] += 1
+    row = hidden()
+    assert row["observed_steps"] == 3 and row["sum_lr"] == pytest.approx(7.0)
+    assert row["negative_factors"] == 2 and row["zero_factors"] == 0 and row["shrinkage_sign"] == 1
+    assert row["shrinkage_log_abs"] == pytest.approx(math.log(2.0) + math.log(3.0))
+    for g in opt.param_groups:
+        g["lr"] = 1.0
+        g["weight_decay"] = 1.0 if g["weight_decay"] else 0.0
+    update_optimizer_exposure(progress, opt)
+    assert hidden()["zero_factors"] == 1 and hidden()["shrinkage_sign"] == 0 and hidden()["shrinkage_log_abs"] is None
+    json.dumps(progress["optimizer_exposure"], allow_nan=False)
+
+
+def test_exposure_refuses_bad_input_without_touching_progress():
+    opt = _exposure_opt()
+    progress = {"steps": 0, "tokens": 0}
+    update_optimizer_exposure(progress, opt)
+    progress["steps"] += 1
+    snapshot = json.dumps(progress, sort_keys=True)
+    for g in opt.param_groups:
+        g["lr"] = float("nan")
+    with pytest.raises(ValueError):
+        update_optimizer_exposure(progress, opt)
+    for g in opt.param_groups:
+        g["lr"] = 1e308
+        g["weight_decay"] = 1e308 if g["weight_decay"] else 0.0
+    with pytest.raises(ValueError):  # lr * wd overflows
+        update_optimizer_exposure(progress, opt)
+    assert json.dumps(progress, sort_keys=True) == snapshot
+    other = _exposure_opt()
+    other.param_groups[0]["params"] = other.param_groups[0]["params"][:1]  # a different group identity
+    for g in opt.param_groups:
+        g["lr"], g["weight_decay"] = 0.01, (0.1 if g["weight_decay"] else 0.0)
+    with pytest.raises(ValueError, match="not the group"):
+        update_optimizer_exposure(progress, other)
+    assert json.dumps(progress, sort_keys=True) == snapshot
+    with pytest.raises(ValueError):
+        update_optimizer_exposure({"steps": True, "tokens": 0}, opt)
+
+
+def test_exposure_started_mid_run_is_not_a_complete_history():
+    opt = _exposure_opt()
+    progress = {"steps": 40, "tokens": 4000}  # a parent from before exposure was recorded
+    update_optimizer_exposure(progress, opt)
+    rec = progress["optimizer_exposure"]
+    assert not rec["complete_history"] and rec["known_start_steps"] == 40 and rec["known_start_tokens"] == 4000
+    progress["steps"] += 1
+    update_optimizer_exposure(progress, opt)
+    assert progress["optimizer_exposure"]["observed_steps"] == 2
+
+
 def test_exposure_covers_both_muon_and_adamw_children():
     model = TensorLM(ModelConfig(**TINY_MODEL))
     opt = make_optimizer(model, TrainConfig(optimizer="muon", lr=0.02, aux_adamw_lr=0.003))

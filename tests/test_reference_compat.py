@@ -509,6 +509,36 @@ def test_training_evidence_descriptors_match_the_reference(tnlm):
         assert mine == ref, (edits[a], edits[b])
 
 
+@pytest.mark.parametrize("optimizer", ["adamw", "muon"])
+def test_optimizer_exposure_records_match_the_reference(tnlm, optimizer):
+    """The exposure record a checkpoint carries (group identities and digests, rate and decay sums,
+    the shrinkage product with zero and negative factors) is the reference's after the same updates."""
+    import json
+
+    import tnlm.optimizer_exposure as ref_exposure
+
+    from tensor_train_ing_b200.config import ModelConfig, TrainConfig
+    from tensor_train_ing_b200.models.model import TensorLM
+    from tensor_train_ing_b200.optim import make_optimizer
+    from tensor_train_ing_b200.optimizer_exposure import update_optimizer_exposure
+    tk = dict(optimizer=optimizer, lr=0.02, aux_adamw_lr=0.003, weight_decay_hidden=0.1)
+    ours_opt = make_optimizer(TensorLM(ModelConfig(**TINY_MODEL)), TrainConfig(**tk))
+    ref_opt = tnlm.optim.make_optimizer(tnlm.model.TensorLM(tnlm.config.ModelConfig(**TINY_MODEL)),
+                                        tnlm.config.TrainConfig(**tk))
+    progress = {"ours": {"steps": 3, "tokens": 30}, "ref": {"steps": 3, "tokens": 30}}
+    for scale in (1.0, 0.0, 50.0, 60.0):  # ordinary, zero rate, lr * wd = 1 and above it
+        for opt in (ours_opt, ref_opt):
+            groups = (opt.muon.param_groups + opt.adamw.param_groups) if hasattr(opt, "muon") else opt.param_groups
+            for g in groups:
+                g["lr"] = 0.02 * scale
+        update_optimizer_exposure(progress["ours"], ours_opt)
+        ref_exposure.update_optimizer_exposure(progress["ref"], ref_opt)
+        for side in progress.values():
+            side["steps"] += 1
+    ours, ref = (json.dumps(progress[k]["optimizer_exposure"], sort_keys=True) for k in ("ours", "ref"))
+    assert ours == ref
+
+
 def test_both_trainers_share_one_spend_ledger(tnlm, tmp_path):
     """Runs of either framework reserve, bill and complete entries in the same locked ledger file."""
     import json
