@@ -107,97 +107,137 @@ def _batch_history_descriptor(progress, train):
              "lr_scale": e.get("lr_scale", 1.0)} for e in entries], status
 
 
+class _SegmentEvidence:
+    """What a checkpoint payload says about the training segment it ends: whether the segment is a
+    cooldown branch ("cooled", with its step horizon), a run on its own rung ("uncooled"), or
+    undecidable; the segment's token endpoint; and whether the checkpoint reached it.  Every
+    inconsistency leaves a note and turns the affected verdict to "unknown"; nothing missing is
+    filled in.  The verdicts and note texts are the reference's report vocabulary (evaluation
+    reports from either framework compare with each other)."""
+
+    def __init__(self, progress: dict, extra: dict, train: dict):
+        self.notes: list[str] = []
+        self.tokens = _integer(progress.get("tokens"))
+        self.rung = _integer(train.get("rung_total_tokens"), 1)
+        self.batch = _integer(train.get("global_prediction_tokens_per_update"), 1)
+        self.scheduler_step = _integer(progress.get("scheduler_step"))
+        self.start = _integer(progress.get("cooldown_start_tokens"))
+        self.status, self.steps = self._branch(progress.get("distributed_schedule"), extra)
+        self.target, explicit_end_invalid = self._endpoint(progress)
+        self.completion = self._reached(explicit_end_invalid, cosine=train.get("schedule") == "cosine")
+
+    def _unknown(self, note: str, value=None):
+        self.notes.append(note)
+        return value
+
+    def _branch(self, schedule, extra) -> tuple:
+        """(status, cooldown steps) from the horizons the payload declares in its two places."""
+        declared = set()
+        for record in (schedule, extra):
+            if isinstance(record, dict) and "cooldown_steps" in record:
+                steps = record["cooldown_steps"]
+                if steps is None or _integer(steps, 1) is not None:
+                    declared.add(steps)
+        if len(declared) > 1:
+            return self._unknown("conflicting checkpoint cooldown metadata", ("unknown", None))
+        if declared:
+            steps = declared.pop()
+            if steps is not None:
+                return "cooled", steps
+            if self.start is None:
+                return "uncooled", None
+            return self._unknown("cooldown start conflicts with explicit uncooled metadata", ("unknown", None))
+        if self.start is not None:
+            return self._unknown("cooldown branch start exists but its step horizon is missing", ("cooled", None))
+        return self._unknown("checkpoint has no explicit cooldown branch evidence", ("unknown", None))
+
+    def _endpoint(self, progress) -> tuple:
+        """(token endpoint of the segment or None, whether an explicit endpoint was refused)."""
+        horizon = None
+        if self.status == "uncooled":
+            horizon = self.rung
+        elif self.status == "cooled" and None not in (self.start, self.steps, self.batch):
+            horizon = self.start + self.steps * self.batch
+        if "cooldown_end_tokens" not in progress:
+            return horizon, False
+        end = _integer(progress["cooldown_end_tokens"], 1)
+        # an explicit endpoint lies inside the last update of the branch's horizon
+        if (self.status == "cooled" and None not in (end, self.start, self.steps, self.batch)
+                and self.start + (self.steps - 1) * self.batch < end <= self.start + self.steps * self.batch):
+            return end, False
+        return self._unknown("invalid explicit cooldown token endpoint", (None, True))
+
+    def _reached(self, explicit_end_invalid: bool, *, cosine: bool) -> str:
+        verdict = "unknown"
+        if self.target is not None and self.tokens is not None:
+            reached = self.tokens >= self.target
+            verdict = "complete" if reached else "partial"
+            if (self.status == "cooled" and self.scheduler_step is not None
+                    and reached != (self.scheduler_step >= self.steps)):
+                verdict = self._unknown("cooldown token and scheduler-step completion evidence disagree", "unknown")
+        elif (not explicit_end_invalid and self.status == "cooled" and None not in (self.steps, self.scheduler_step)):
+            verdict = "complete" if self.scheduler_step >= self.steps else "partial"
+        if cosine and not self._cosine_consistent():
+            verdict = self._unknown("cosine token and scheduler horizon evidence is missing or inconsistent",
+                                    "unknown")
+        return verdict
+
+    def _cosine_consistent(self) -> bool:
+        """A cosine run has no separate cooldown and reaches its rung exactly at its last update."""
+        if self.status != "uncooled" or None in (self.rung, self.batch, self.scheduler_step, self.tokens):
+            return False
+        updates = -(-self.rung // self.batch)
+        return (self.scheduler_step <= updates and self.tokens <= self.rung
+                and (self.tokens == self.rung) == (self.scheduler_step == updates))
+
+
 def _training_descriptor(payload) -> dict:
     """Training evidence recorded in a checkpoint payload (never evaluation overrides)."""
-    as_map = lambda v: v if isinstance(v, dict) else {}  # noqa: E731
-    config, progress, extra = (as_map(payload.get(k)) for k in ("config", "progress", "extra"))
-    train, model, data = (as_map(config.get(k)) for k in ("train", "model", "data"))
+    def section(mapping, key):
+        value = mapping.get(key) if isinstance(mapping, dict) else None
+        return value if isinstance(value, dict) else {}
+    config, progress, extra = (section(payload, k) for k in ("config", "progress", "extra"))
+    train, model, data = (section(config, k) for k in ("train", "model", "data"))
     ctx_hist, ctx_status = _context_history_descriptor(progress, data.get("context", 512))
     batch_hist, batch_status = _batch_history_descriptor(progress, train)
-    text = lambda v: v if isinstance(v, str) and v else None  # noqa: E731
-    schedule = as_map(progress.get("distributed_schedule"))
-    candidates = [(src, vals["cooldown_steps"]) for src, vals in (("progress.distributed_schedule", schedule),
-                                                                  ("extra", extra))
-                  if "cooldown_steps" in vals and (vals["cooldown_steps"] is None
-                                                   or _integer(vals["cooldown_steps"], 1) is not None)]
-    notes, cooldown_steps = [], None
-    start = _integer(progress.get("cooldown_start_tokens"))
-    if candidates and len({v for _, v in candidates}) > 1:
-        cooldown = "unknown"
-        notes.append("conflicting checkpoint cooldown metadata")
-    elif candidates:
-        cooldown_steps = candidates[0][1]
-        cooldown = "uncooled" if cooldown_steps is None else "cooled"
-        if cooldown == "uncooled" and start is not None:
-            cooldown = "unknown"
-            notes.append("cooldown start conflicts with explicit uncooled metadata")
-    elif start is not None:
-        cooldown = "cooled"
-        notes.append("cooldown branch start exists but its step horizon is missing")
-    else:
-        cooldown = "unknown"
-        notes.append("checkpoint has no explicit cooldown branch evidence")
-    tokens = _integer(progress.get("tokens"))
-    rung = _integer(train.get("rung_total_tokens"), 1)
-    batch = _integer(train.get("global_prediction_tokens_per_update"), 1)
-    sched = _integer(progress.get("scheduler_step"))
-    target = rung if cooldown == "uncooled" else None
-    if cooldown == "cooled" and None not in (start, cooldown_steps, batch):
-        target = start + cooldown_steps * batch
-    invalid_end = False
-    if "cooldown_end_tokens" in progress:
-        end = _integer(progress["cooldown_end_tokens"], 1)
-        if (cooldown != "cooled" or None in (end, start, cooldown_steps, batch)
-                or not start + (cooldown_steps - 1) * batch < end <= start + cooldown_steps * batch):
-            invalid_end, target = True, None
-            notes.append("invalid explicit cooldown token endpoint")
-        else:
-            target = end
-    completion = "unknown"
-    if target is not None and tokens is not None:
-        completion = "complete" if tokens >= target else "partial"
-        if cooldown == "cooled" and sched is not None and (tokens >= target) != (sched >= cooldown_steps):
-            completion = "unknown"
-            notes.append("cooldown token and scheduler-step completion evidence disagree")
-    elif not invalid_end and cooldown == "cooled" and cooldown_steps is not None and sched is not None:
-        completion = "complete" if sched >= cooldown_steps else "partial"
-    if train.get("schedule") == "cosine":
-        expected = (rung + batch - 1) // batch if rung is not None and batch is not None else None
-        if (cooldown != "uncooled" or None in (expected, sched, tokens) or sched > expected or tokens > rung
-                or (tokens == rung) != (sched == expected)):
-            completion = "unknown"
-            notes.append("cosine token and scheduler horizon evidence is missing or inconsistent")
-    disabled_or = lambda key: ("disabled" if key in model and model[key] is None  # noqa: E731
-                               else _integer(model.get(key), 1))
-    return {"version": 1, "source": "checkpoint_payload",
-            "config_compatibility": copy.deepcopy(payload.get("config_compatibility", {})),
-            "configuration": copy.deepcopy({k: v for k, v in config.items() if k != "project"}),
-            "optimizer": text(train.get("optimizer")), "seed": _integer(train.get("seed")),
-            "width": _integer(model.get("d_model"), 1), "depth": _integer(model.get("layers"), 1),
-            "train_context": _integer(data.get("context"), 1), "rung_total_tokens": rung,
-            "context_history": ctx_hist, "context_history_status": ctx_status,
-            "batch_history": batch_hist, "batch_history_status": batch_status,
-            "normalization": text(model.get("normalization")), "attention": text(model.get("attention")),
-            "width_scaling_base": disabled_or("width_scaling_base"),
-            "width_lr_exponent": _number(model.get("width_lr_exponent"), False),
-            "width_logit_exponent": _number(model.get("width_logit_exponent"), False),
-            "depth_scaling_base": disabled_or("depth_scaling_base"),
-            "depth_lr_exponent": _number(model.get("depth_lr_exponent"), False),
-            "depth_residual_base": disabled_or("depth_residual_base"),
-            "depth_residual_exponent": _number(model.get("depth_residual_exponent"), False),
-            "residual_alpha": _number(model.get("residual_alpha"), False),
-            "weight_decay_hidden": _number(train.get("weight_decay_hidden")),
-            "beta1": _number(train.get("beta1")), "beta2": _number(train.get("beta2")),
-            "aux_adamw_lr": ("default_to_lr" if "aux_adamw_lr" in train and train["aux_adamw_lr"] is None
-                             else _number(train.get("aux_adamw_lr"))),
-            "actual_prediction_tokens": tokens, "optimizer_steps": _integer(progress.get("steps")),
-            "global_prediction_tokens_per_update": batch, "lr": _number(train.get("lr")),
-            "schedule": text(train.get("schedule")), "scheduler_step": sched,
-            "warmup_steps": _integer(progress.get("warmup_steps"), 1), "cooldown_status": cooldown,
-            "cooldown_steps": cooldown_steps, "cooldown_start_tokens": start,
-            "segment_target_prediction_tokens": target, "completion_status": completion, "evidence_notes": notes,
-            "completion_scope": "declared training segment token/step endpoint only; no automatic experiment "
-                                "completion, fairness, or ranking claim"}
+    segment = _SegmentEvidence(progress, extra, train)
+
+    def text(v):
+        return v if isinstance(v, str) and v else None
+
+    def positive_or_disabled(key):  # an explicit null switches the scaling rule off
+        return "disabled" if key in model and model[key] is None else _integer(model.get(key), 1)
+    descriptor = {
+        "version": 1, "source": "checkpoint_payload",
+        "config_compatibility": copy.deepcopy(payload.get("config_compatibility", {})),
+        "configuration": copy.deepcopy({k: v for k, v in config.items() if k != "project"}),
+        "optimizer": text(train.get("optimizer")), "seed": _integer(train.get("seed")),
+        "width": _integer(model.get("d_model"), 1), "depth": _integer(model.get("layers"), 1),
+        "train_context": _integer(data.get("context"), 1), "rung_total_tokens": segment.rung,
+        "context_history": ctx_hist, "context_history_status": ctx_status,
+        "batch_history": batch_hist, "batch_history_status": batch_status,
+        "normalization": text(model.get("normalization")), "attention": text(model.get("attention")),
+        "width_scaling_base": positive_or_disabled("width_scaling_base"),
+        "depth_scaling_base": positive_or_disabled("depth_scaling_base"),
+        "depth_residual_base": positive_or_disabled("depth_residual_base"),
+    }
+    for key in ("width_lr_exponent", "width_logit_exponent", "depth_lr_exponent", "depth_residual_exponent",
+                "residual_alpha"):  # signed
+        descriptor[key] = _number(model.get(key), False)
+    for key in ("weight_decay_hidden", "beta1", "beta2", "lr"):
+        descriptor[key] = _number(train.get(key))
+    descriptor["aux_adamw_lr"] = ("default_to_lr" if "aux_adamw_lr" in train and train["aux_adamw_lr"] is None
+                                  else _number(train.get("aux_adamw_lr")))
+    descriptor.update({
+        "actual_prediction_tokens": segment.tokens, "optimizer_steps": _integer(progress.get("steps")),
+        "global_prediction_tokens_per_update": segment.batch, "schedule": text(train.get("schedule")),
+        "scheduler_step": segment.scheduler_step, "warmup_steps": _integer(progress.get("warmup_steps"), 1),
+        "cooldown_status": segment.status, "cooldown_steps": segment.steps,
+        "cooldown_start_tokens": segment.start, "segment_target_prediction_tokens": segment.target,
+        "completion_status": segment.completion, "evidence_notes": segment.notes,
+        "completion_scope": "declared training segment token/step endpoint only; no automatic experiment "
+                            "completion, fairness, or ranking claim"})
+    return descriptor
 
 
 _COMPARED = ("optimizer", "seed", "width", "depth", "train_context", "context_history", "batch_history",

@@ -484,17 +484,32 @@ def test_training_evidence_descriptors_match_the_reference(tnlm):
              ("context_history", 1, "start_step", 9), ("extra", None, "cooldown_steps", 4),
              ("progress", None, "cooldown_start_tokens", 120), ("progress", None, "tokens", 480),
              ("config", "train", "schedule", "cosine")]
+    # combinations that reach the cooldown endpoint and completion rules
+    cooled = [("extra", None, "cooldown_steps", 2), ("progress", None, "cooldown_start_tokens", 96)]
+    edits += [tuple(cooled),
+              tuple(cooled + [("progress", None, "cooldown_end_tokens", 190)]),   # inside the last update
+              tuple(cooled + [("progress", None, "cooldown_end_tokens", 140)]),   # before it: refused
+              tuple(cooled + [("progress", None, "tokens", 192), ("progress", None, "scheduler_step", 2)]),
+              tuple(cooled + [("progress", None, "tokens", 192), ("progress", None, "scheduler_step", 1)]),
+              tuple(cooled + [("progress", None, "distributed_schedule", {"cooldown_steps": 3})]),
+              (("extra", None, "cooldown_steps", 0),),
+              (("config", "train", "schedule", "cosine"), ("progress", None, "tokens", 480),
+               ("progress", None, "scheduler_step", 10)),
+              (("config", "train", "schedule", "cosine"), ("progress", None, "scheduler_step", 11))]
+
+    def apply(p, edit):
+        where, i, field, value = edit
+        if where in ("batch_history", "context_history"):
+            p["progress"][where][i][field] = value
+        elif where == "config":
+            p["config"][i][field] = value
+        else:
+            p[where][field] = value
     payloads = []
     for edit in edits:
         p = copy.deepcopy(base)
-        if edit is not None:
-            where, i, field, value = edit
-            if where in ("batch_history", "context_history"):
-                p["progress"][where][i][field] = value
-            elif where == "config":
-                p["config"][i][field] = value
-            else:
-                p[where][field] = value
+        for one in (() if edit is None else edit if isinstance(edit[0], tuple) else (edit,)):
+            apply(p, one)
         payloads.append(p)
     ours = [our_eval._training_descriptor(p) for p in payloads]
     # the reference adds two descriptive sentences about the histories' scope; the values are compared
