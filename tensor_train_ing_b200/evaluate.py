@@ -248,27 +248,41 @@ _COMPARED = ("optimizer", "seed", "width", "depth", "train_context", "context_hi
              "depth_residual_exponent", "residual_alpha", "weight_decay_hidden", "beta1", "beta2")
 
 
+def _comparable(report) -> dict:
+    """The report's training descriptor, or {} when it is absent or of another version/source."""
+    d = report.get("training_descriptor")
+    return d if isinstance(d, dict) and d.get("version") == 1 and d.get("source") == "checkpoint_payload" else {}
+
+
+def _dimension_value(d: dict, field: str):
+    """A descriptor's value for one compared dimension: an uncooled run's absent cooldown horizon is
+    "not_applicable" rather than missing, and a history counts only when it is complete."""
+    value = d.get(field)
+    if field == "cooldown_steps" and value is None and field in d and d.get("cooldown_status") == "uncooled":
+        return "not_applicable"
+    if field in ("context_history", "batch_history") and d.get(f"{field}_status") != "complete":
+        return None
+    return value
+
+
 def _training_comparison(left, right) -> dict:
-    def descriptor(report):
-        v = report.get("training_descriptor")
-        return v if isinstance(v, dict) and v.get("version") == 1 and v.get("source") == "checkpoint_payload" else {}
-    ds = descriptor(left), descriptor(right)
-    dims = {}
-    for f in _COMPARED:
-        vals = [d.get(f) for d in ds]
-        if f == "cooldown_steps":
-            vals = ["not_applicable" if d.get("cooldown_status") == "uncooled" and f in d and v is None else v
-                    for d, v in zip(ds, vals)]
-        known = all(v is not None and v != "unknown" for v in vals)
-        if f == "context_history":
-            known = known and all(d.get("context_history_status") == "complete" for d in ds)
-        if f == "batch_history":
-            known = known and all(d.get("batch_history_status") == "complete" for d in ds)
-        dims[f] = {"status": ("matched" if vals[0] == vals[1] else "different") if known else "unknown",
-                   "left": vals[0], "right": vals[1]}
-    return {"dimensions": dims, "matched_dimensions": [k for k, v in dims.items() if v["status"] == "matched"],
-            "different_dimensions": [k for k, v in dims.items() if v["status"] == "different"],
-            "unknown_dimensions": [k for k, v in dims.items() if v["status"] == "unknown"],
+    """Per dimension: matched, different, or unknown when either side lacks the evidence (missing
+    evidence is never taken as equal)."""
+    sides = (_comparable(left), _comparable(right))
+    dims, by_status = {}, {"matched": [], "different": [], "unknown": []}
+    for field in _COMPARED:
+        a, b = (_dimension_value(d, field) for d in sides)
+        if any(v is None or v == "unknown" for v in (a, b)):
+            status = "unknown"
+        else:
+            status = "matched" if a == b else "different"
+        # the report shows the recorded values, also for a history that is not complete
+        shown = [d.get(field) if field in ("context_history", "batch_history") else v
+                 for d, v in zip(sides, (a, b))]
+        dims[field] = {"status": status, "left": shown[0], "right": shown[1]}
+        by_status[status].append(field)
+    return {"dimensions": dims, "matched_dimensions": by_status["matched"],
+            "different_dimensions": by_status["different"], "unknown_dimensions": by_status["unknown"],
             "automatic_ranking_eligible": False,
             "scope": "training evidence summary only; equality of missing evidence is never inferred"}
 
