@@ -93,56 +93,68 @@ def _require_finite_clip(stats: dict) -> None:
 
 
 class BatchScoreBounds:
+    """Attention-score bounds of one optimizer update, taken from the training forwards themselves.
+
+    Each micro-batch's forward records, per layer and score factor (S1, and S2 for two-factor
+    attention), every head's bound max|q|*max|k|/sqrt(dk) (the QKV GEMM's epilogue emits the row
+    norms on the fused path).  The update's diagnostic is the largest bound over all its micro-batches
+    (NaN, which aborts the update, once any bound is negative); QK-clip uses the per-head bounds of
+    the update's last micro-batch, as the reference does (tnlm/training_stability.py:57-130).  The
+    bounds are snapshotted after each forward because the kernels reuse their output buffers and an
+    activation-checkpointing backward would record again."""
+
     def __init__(self, model, cfg):
         from .qk_clip import set_score_bound_recording
         self.model = model
         self.enabled = StabilityPolicy.from_config(cfg).clip_source == "batch_bound"
-        self.maximum: torch.Tensor | None = None  # device scalar over the update so far
-        self.last: list[dict] | None = None       # per layer {factor: (H,)} of the last micro-batch
+        self._factors = [("S1", "S2") if hasattr(blk.attn, "q2") else ("S1",) for blk in model.blocks]
+        self.top: torch.Tensor | None = None   # device scalar over the update so far
+        self.last: list[dict] | None = None    # per layer {factor: (H,)} of the latest micro-batch
         if self.enabled:
             set_score_bound_recording(model, True)
 
     def begin_update(self) -> None:
-        self.maximum = self.last = None
+        self.top = self.last = None
 
-    def _recorded(self) -> list[tuple[int, str, torch.Tensor]]:
+    def _snapshot(self) -> tuple[torch.Tensor, list[dict]]:
+        """One stacked copy of every recorded bound, and per-layer views into it."""
         from .qk_clip import score_bounds
-        heads, found = self.model.cfg.heads, []
-        for layer, (blk, bounds) in enumerate(zip(self.model.blocks, score_bounds(self.model))):
-            if set(bounds) != ({"S1", "S2"} if hasattr(blk.attn, "q2") else {"S1"}):
+        heads, flat, keys = self.model.cfg.heads, [], []
+        for layer, (expected, got) in enumerate(zip(self._factors, score_bounds(self.model))):
+            if set(got) != set(expected):
                 raise ValueError(f"layer {layer} recorded no or unexpected score-bound factors")
-            for factor, b in bounds.items():
+            for factor in expected:
+                b = got[factor]
                 if not torch.is_tensor(b) or b.shape != (heads,):
                     raise ValueError(f"layer {layer} {factor}: a score bound must be a ({heads},) tensor")
-                found.append((layer, factor, b.detach()))
-        if not found:
+                flat.append(b.detach())
+                keys.append((layer, factor))
+        if not flat:
             raise ValueError("no polynomial attention layer recorded score bounds")
-        return found
+        stacked = torch.stack(flat)
+        views = [{} for _ in self.model.blocks]
+        for row, (layer, factor) in zip(stacked, keys):
+            views[layer][factor] = row
+        return stacked, views
 
     def observe(self) -> None:
-        """Fold the bounds of the micro-batch just run into the update's maximum (device-side)."""
+        """Fold the micro-batch just run into the update (device-side, no host synchronisation)."""
         if not self.enabled:
             return
-        found = self._recorded()
-        # one contiguous copy: safe against reused output buffers, one reduction for all factors
-        flat = torch.cat([b for _, _, b in found])
-        top = flat.amax()
-        top = torch.where((flat < 0).any(), torch.full_like(top, float("nan")), top)
-        self.maximum = top if self.maximum is None else torch.maximum(self.maximum, top)
-        heads = self.model.cfg.heads
-        self.last = [{} for _ in self.model.blocks]
-        for k, (layer, factor, _) in enumerate(found):
-            self.last[layer][factor] = flat[k * heads:(k + 1) * heads]
+        stacked, self.last = self._snapshot()
+        worst = torch.where((stacked < 0).any(), stacked.new_tensor(float("nan")), stacked.max())
+        self.top = worst if self.top is None else torch.maximum(self.top, worst)
 
     def finish_update(self) -> float:
+        """The update's largest bound (the one host read); raises when it is missing or invalid."""
         if not self.enabled:
             return 0.0
-        if self.maximum is None:
+        if self.top is None:
             raise ValueError("this update recorded no score bounds")
-        top = float(self.maximum)
-        if not math.isfinite(top) or top < 0:
+        value = float(self.top)
+        if not (math.isfinite(value) and value >= 0):
             raise FloatingPointError("a score bound was non-finite or negative; the update is aborted")
-        return top
+        return value
 
     def reduce_last(self, all_reduce_max_) -> None:
         """Data-parallel ranks each ran their own last micro-batch, so their recorded per-head bounds
@@ -152,8 +164,7 @@ class BatchScoreBounds:
         clips by the same factors.  A rank that ran no micro-batch contributes zeros (bounds are
         nonnegative)."""
         heads = self.model.cfg.heads
-        layout = [(layer, f) for layer, blk in enumerate(self.model.blocks)
-                  for f in (("S1", "S2") if hasattr(blk.attn, "q2") else ("S1",))]
+        layout = [(layer, f) for layer, factors in enumerate(self._factors) for f in factors]
         flat = torch.zeros(len(layout) * heads, dtype=torch.float64)
         if self.last is not None:
             for k, (layer, f) in enumerate(layout):
@@ -164,6 +175,7 @@ class BatchScoreBounds:
             self.last[layer][f] = flat[k * heads:(k + 1) * heads]
 
     def clip(self, tau) -> dict:
+        """Rescale every head over ``tau`` by the last micro-batch's bounds (after checking the update's)."""
         from .qk_clip import qk_clip_from_bounds_
         self.finish_update()
         if self.last is None:
