@@ -182,3 +182,72 @@ def test_sampler_cursor_resumes_the_batch_stream(tmp_path, config):
     other_seed = PackedSampler(manifest, batch_size=2, context=4, seed=2)
     with pytest.raises(ValueError):
         load_checkpoint(tmp_path / "c", _model(0), None, other_seed, restore_rng=False)
+
+
+def _rewrite_state(path, mutate):
+    """Replace ``state.pt`` by a mutated payload and re-sign it in the manifest, so only the content
+    checks (not the checksum) can refuse it."""
+    import hashlib
+    payload = torch.load(path / "state.pt", weights_only=False)
+    mutate(payload)
+    torch.save(payload, path / "state.pt")
+    data = (path / "state.pt").read_bytes()
+    manifest = json.loads((path / "manifest.json").read_text())
+    manifest["files"]["state.pt"] = {"sha256": hashlib.sha256(data).hexdigest(), "bytes": len(data)}
+    (path / "manifest.json").write_text(json.dumps(manifest))
+
+
+def test_a_checksum_valid_nonfinite_payload_is_refused_without_mutation(tmp_path):
+    _save(tmp_path / "ck", _model(1))
+    name = next(iter(_model().state_dict()))
+    _rewrite_state(tmp_path / "ck", lambda p: p["model"][name].view(-1)[0].fill_(float("nan")))
+    target = _model(2)
+    before = _clone_state(target)
+    with pytest.raises((ValueError, FloatingPointError)):
+        load_checkpoint(tmp_path / "ck", target, restore_rng=False)
+    assert all(torch.equal(v, target.state_dict()[k]) for k, v in before.items())
+
+
+@pytest.mark.parametrize("manifest", ["not json", "[]", '{"files": {}}',
+                                      '{"files": {"state.pt": {"sha256": "xyz", "bytes": 1}}}'])
+def test_a_malformed_manifest_is_refused_cleanly(tmp_path, manifest):
+    _save(tmp_path / "ck", _model(1))
+    (tmp_path / "ck" / "manifest.json").write_text(manifest)
+    target = _model(2)
+    before = _clone_state(target)
+    with pytest.raises((ValueError, KeyError, TypeError)):
+        load_checkpoint(tmp_path / "ck", target, restore_rng=False)
+    assert all(torch.equal(v, target.state_dict()[k]) for k, v in before.items())
+
+
+def test_a_second_publisher_never_replaces_a_checkpoint(tmp_path):
+    first = _save(tmp_path / "ck", _model(1))
+    with pytest.raises(FileExistsError):
+        _save(tmp_path / "ck", _model(2))
+    assert read_manifest(tmp_path / "ck")["files"] == first["files"]
+    leftovers = [p.name for p in tmp_path.iterdir() if p.name != "ck"]
+    assert leftovers == []  # the refused save's staging directory is gone
+
+
+def test_a_composite_optimizer_mismatch_is_refused_before_the_model_changes(tmp_path):
+    model = _model(1)
+    muon = make_opt(model, TrainConfig(optimizer="muon", lr=0.02, aux_adamw_lr=0.003))
+    _save(tmp_path / "ck", model, muon)
+    target = _model(2)
+    adamw = make_opt(target, TrainConfig(optimizer="adamw", lr=0.02))
+    before = _clone_state(target)
+    with pytest.raises((ValueError, KeyError, TypeError)):
+        load_checkpoint(tmp_path / "ck", target, adamw, restore_rng=False)
+    assert all(torch.equal(v, target.state_dict()[k]) for k, v in before.items())
+
+
+def test_code_identity_covers_every_package_source(tmp_path):
+    from pathlib import Path
+
+    from tensor_train_ing_b200.checkpoint import code_identity
+    ident = code_identity()
+    text = json.dumps(ident)
+    package = Path(__file__).resolve().parents[1] / "tensor_train_ing_b200"
+    for nested in ("models/model.py", "ops/fused.py", "csrc/gemm/gemm.cu", "parallel/sharded.py"):
+        if (package / nested).exists():
+            assert Path(nested).name in text, nested
