@@ -221,6 +221,39 @@ def test_score_bounds_from_the_qkv_epilogue(kind, dk):
             torch.testing.assert_close(got[name], want[name].float(), rtol=2e-2, atol=1e-4)
 
 
+def test_batch_score_bounds_and_clip_on_the_fused_path():
+    """The trainer's batch-bound bookkeeping on CUDA: the update's maximum spans both micro-batches,
+    the clip uses the last one's per-head bounds (2 layers x 2 factors x 2 heads over tau), and after
+    the clip a re-run of that micro-batch records bounds at tau (the rescale multiplies each clipped
+    head's scores by tau / bound; bf16 operands round the re-run's norms)."""
+    from tensor_train_ing_b200.config import Config, TrainConfig
+    from tensor_train_ing_b200.training_stability import BatchScoreBounds
+    torch.manual_seed(0)
+    mcfg = ModelConfig(layers=2, d_model=256, heads=2, d_key=64, d_value=64, d_mlp=512, vocab_size=1000,
+                       padded_vocab=1024, attention="signed_product", qk_init_scale=0.5)
+    cfg = Config(model=mcfg, train=TrainConfig(qk_clip_source="batch_bound", qk_clip_tau=1e-3,
+                                               qk_clip_every_steps=1), raw={})
+    model = TensorLM(mcfg).cuda().eval()
+    bounds = BatchScoreBounds(model, cfg)
+    docs = torch.zeros(2, 256, dtype=torch.long, device="cuda")
+    batches = [torch.randint(0, 1000, (2, 256), device="cuda") for _ in range(2)]
+    bounds.begin_update()
+    seen = []
+    with torch.no_grad():
+        for idx in batches:
+            model(idx, docs)
+            bounds.observe()
+            seen.append(max(float(b.max()) for layer in bounds.last for b in layer.values()))
+    assert bounds.finish_update() == pytest.approx(max(seen), rel=1e-6)
+    report = bounds.clip(1e-3)
+    assert report["clipped_heads"] == 8 and report["max_bound_before"] == pytest.approx(seen[-1], rel=1e-6)
+    bounds.begin_update()
+    with torch.no_grad():
+        model(batches[-1], docs)
+    bounds.observe()
+    assert bounds.finish_update() <= 1e-3 * (1 + 2e-2)  # bf16 operands: the re-run's norms round
+
+
 def test_selective_recompute_on_the_fused_path_keeps_every_gradient():
     """Activation checkpointing on the fused path: recomputing all, some or none of the blocks gives
     bit-identical gradients (the recomputed forward runs the same kernels on the same inputs)."""
