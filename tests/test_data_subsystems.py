@@ -128,6 +128,23 @@ def test_concurrent_builds_publish_one_valid_index(dataset):
     assert leftovers == []  # no temporary file of an interrupted publication
 
 
+def test_the_index_is_derived_data_outside_the_manifest(dataset):
+    """Building or rebuilding the index leaves the dataset's manifest and its digest untouched and is
+    not one of its artifacts; a dataset whose metadata no longer matches its manifest is refused by
+    the sampler even when a valid-looking index exists."""
+    from tensor_train_ing_b200.data import PackedSampler
+    root, manifest = dataset
+    before = {n: (root / n).read_bytes() for n in ("manifest.json", "manifest.sha256")}
+    load_sampler_index(root, manifest, "train", rebuild=True)
+    assert {n: (root / n).read_bytes() for n in before} == before
+    assert not any(name.startswith(INDEX_DIR) for name in manifest["artifacts"])
+    PackedSampler(root / "manifest.json", batch_size=1, context=8)  # builds or reuses the index
+    docs = root / "documents.jsonl"
+    docs.write_text(docs.read_text().replace('"split"', '"split" ', 1))  # same records, other bytes
+    with pytest.raises(ValueError, match="checksum"):
+        PackedSampler(root / "manifest.json", batch_size=1, context=8)
+
+
 def test_mechanism_tasks_exact_labels_and_held_out_compositions(tmp_path):
     manifest = prepare_mechanism_tasks(tmp_path / "mech", seed=3, train_examples=8, validation_examples=8)
     meta, val = load_mechanism_tasks(manifest, "val")
