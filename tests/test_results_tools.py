@@ -145,3 +145,16 @@ def test_export_is_thinned_weight_free_and_idempotent(tmp_path):
     assert not list(out.rglob("*.pt")) and len(first["written"]) == 2
     again = results.export_results(runs, out, max_rows=100)
     assert again["written"] == [] and len(again["unchanged"]) == 2
+
+
+def test_the_command_line_prints_json_for_every_tool(tmp_path, capsys):
+    runs = tmp_path / "runs"
+    for lr in (0.001, 0.002, 0.004):
+        _report(runs, f"w64_lr{lr}", _planted(64, lr))
+    assert results.main(["lr-optimum", str(runs), "--pattern", PATTERN]) == 0
+    fit = json.loads(capsys.readouterr().out)
+    assert fit["groups"]["64"]["optimum"] == pytest.approx(0.008, rel=1e-6) and fit["power_law"] is None
+    assert results.main(["states", str(runs), "--min-age-min", "0"]) == 0
+    assert json.loads(capsys.readouterr().out) == {"states": [], "total_bytes": 0}
+    assert results.main(["export", str(runs), str(tmp_path / "out")]) == 0
+    assert len(json.loads(capsys.readouterr().out)["written"]) == 3
