@@ -128,3 +128,30 @@ def test_taper_lifecycle_warmup_freeze_and_gate():
     bad = Config(model=mcfg, train=TrainConfig(compile=False, taper_end_fraction=1.5))
     with pytest.raises(ValueError):
         validate_taper_config(bad)
+
+
+def test_reduce_last_takes_the_per_head_maximum_over_ranks(fp64):
+    """The distributed clip's agreement step: each (layer, factor, head) bound becomes the maximum of
+    the ranks' values, and a rank that ran no micro-batch contributes zeros.  The reducer here plays
+    two other ranks."""
+    model = _model()
+    cfg = Config(model=model.cfg, train=TrainConfig(qk_clip_source="batch_bound"), raw={})
+    bounds = BatchScoreBounds(model, cfg)
+    idx, doc = _batch()
+    bounds.begin_update()
+    model(idx, doc_ids=doc)
+    bounds.observe()
+    mine = torch.cat([b.double() for layer in bounds.last for b in layer.values()])
+    other = torch.rand_like(mine) * 2 * float(mine.max())
+
+    def reducer(flat):  # ranks: this one, one with other values, one with no micro-batch (zeros)
+        flat.copy_(torch.maximum(torch.maximum(flat, other), torch.zeros_like(flat)))
+    bounds.reduce_last(reducer)
+    got = torch.cat([b for layer in bounds.last for b in layer.values()])
+    assert torch.equal(got, torch.maximum(mine, other))
+    idle = BatchScoreBounds(model, cfg)  # a rank without a micro-batch this update
+    idle.begin_update()
+    seen = []
+    idle.reduce_last(lambda flat: seen.append(flat.clone()) or flat.copy_(torch.maximum(flat, other)))
+    assert torch.equal(seen[0], torch.zeros_like(other))
+    assert torch.equal(torch.cat([b for layer in idle.last for b in layer.values()]), other)
